@@ -1,0 +1,186 @@
+/*
+ * indecis_b200 — C ABI of the B200 (sm_100a) int8 ModernBERT encoder.
+ *
+ * This is the drop-in boundary for the int8 inference path of
+ * github.com/bornholm/indecis (paths relative to that module). The seam is
+ * internal/modernbert/infer.go:304 `func (m *Model) run(seqs [][]int32,
+ * done func(xn []float32, offs []int)) error`, the single place where the
+ * int8 forward runs; a build-tagged cgo file gives it a device branch (see
+ * INTEGRATION.md). Plain pointers and sizes only; no allocation is handed to
+ * the caller. All entry points are reentrant: a model is read-only after
+ * creation and every call takes its own workspace and stream.
+ *
+ * Status codes: 0 on success, otherwise an IG_ERR_* value; ig_last_error()
+ * gives the message of the calling thread's last failure.
+ */
+#ifndef INDECIS_B200_H
+#define INDECIS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define IG_API __attribute__((visibility("default")))
+#else
+#define IG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IG_OK 0
+#define IG_ERR_BAD_ARG 1      /* inconsistent sizes or pointers (the reference panics or errors) */
+#define IG_ERR_OUT_OF_VOCAB 2 /* "modernbert: id %d out of vocabulary" (infer.go:310-312) */
+#define IG_ERR_CUDA 3         /* a CUDA call failed */
+#define IG_ERR_TIMEOUT 4      /* a kernel's bounded wait ran out */
+#define IG_ERR_UNSUPPORTED 5  /* a shape this build does not handle */
+#define IG_ERR_NO_DEVICE 6    /* no usable sm_100 device */
+
+#define IG_MODE_POOLED 0 /* EncodeSeqs: [nseq][hidden], mean or first token */
+#define IG_MODE_TOKENS 1 /* EncodeTokens: [sum of lengths][hidden] */
+
+#define IG_POOL_MEAN 0
+#define IG_POOL_CLS 1
+
+/* modernbert.Config (internal/modernbert/model.go:25-49), the fields that
+ * determine the computation. Biases are not supported, as in validate()
+ * (model.go:64-80). simd_lanes is the float32 lane count whose summation
+ * order LayerNorm and ExpShift reproduce (8: the reference on AVX2). */
+typedef struct ig_config {
+  int32_t vocab, hidden, layers, heads, intermediate;
+  int32_t global_every;    /* global_attn_every_n_layers */
+  int32_t local_attention; /* total window width; half-window = local_attention / 2 */
+  int32_t pooling;         /* IG_POOL_MEAN or IG_POOL_CLS */
+  double norm_eps, global_theta, local_theta;
+  int32_t simd_lanes;
+} ig_config;
+
+/* Float32 host views in transformers layouts (FromTensors, model.go:179-234).
+ * Per-layer arrays have `layers` entries; attn_norm[0] is ignored (layer 0
+ * has no attention norm). Weights are copied; the views are not retained. */
+typedef struct ig_weights {
+  const float *tok_embeddings; /* [vocab][hidden] embeddings.tok_embeddings.weight */
+  const float *emb_norm;       /* [hidden] embeddings.norm.weight */
+  const float *final_norm;     /* [hidden] final_norm.weight */
+  const float *const *attn_norm; /* [hidden] layers.%d.attn_norm.weight */
+  const float *const *wqkv;      /* [3*hidden][hidden] layers.%d.attn.Wqkv.weight */
+  const float *const *wo;        /* [hidden][hidden] layers.%d.attn.Wo.weight */
+  const float *const *mlp_norm;  /* [hidden] layers.%d.mlp_norm.weight */
+  const float *const *wi;        /* [2*intermediate][hidden] layers.%d.mlp.Wi.weight (input, then gate) */
+  const float *const *wo_mlp;    /* [hidden][intermediate] layers.%d.mlp.Wo.weight */
+} ig_weights;
+
+/* A decision head (heads.go:19-27): `rows` logits z = W.x + b over the pooled
+ * vector, or over every token state when per_token (Spans). */
+typedef struct ig_head {
+  int32_t rows;
+  int32_t per_token;
+  const float *w; /* [rows][hidden] */
+  const float *b; /* [rows] */
+} ig_head;
+
+typedef struct ig_model ig_model;
+
+/* Replaces modernbert.FromTensors + SetInt8(true) + the first-use packing
+ * (infer.go:119-135, :184-219): validates the config, uploads the weights to
+ * `device` and quantizes each layer matrix per output channel (PackB8,
+ * linalg/int8.go:36-77) on the device. */
+IG_API int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, ig_model **out);
+
+/* Releases the model's device memory. Replaces Invalidate (infer.go:95-100)
+ * for the device copy: a changed model is destroyed and created again. */
+IG_API void ig_model_destroy(ig_model *m);
+
+/* Replaces the heads of Model (heads.go:29-48, model.go:312-341); copied. */
+IG_API int ig_model_set_heads(ig_model *m, int32_t nheads, const ig_head *heads);
+
+/* Replaces EncodeSeqs (infer.go:261, mode IG_MODE_POOLED, out [nseq][hidden])
+ * and EncodeTokens (infer.go:293, mode IG_MODE_TOKENS, out [offs[nseq]][hidden]).
+ * ids are the concatenated sequences, offs[nseq+1] their starts (offs[0] = 0).
+ * Host buffers; the call returns when out is written. An id outside
+ * [0, vocab) fails with IG_ERR_OUT_OF_VOCAB before any device work. */
+IG_API int ig_encode(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
+              size_t out_len);
+
+/* ig_encode on device buffers (d_ids [offs[nseq]], d_out) enqueued on
+ * `stream` (a cudaStream_t; NULL: the legacy default stream). offs stays a
+ * host array: it sizes the launches. Returns once the work is enqueued;
+ * an out-of-vocabulary id is reported by ig_device_error() after the stream
+ * completes (its row reads embedding row 0). */
+IG_API int ig_encode_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int32_t nseq, int32_t mode,
+                     float *d_out, void *stream);
+
+/* Replaces the logits half of DecideInputs (spans.go:369-461 then
+ * heads.go:62-74 per head): float64 logits of every pooled head for each
+ * sequence, concatenated in head order ([nseq][sum of pooled rows]), and,
+ * when token_logits is not NULL, of every per-token head for each token
+ * ([offs[nseq]][sum of per-token rows]). The answers (sigmoid, softmax,
+ * ordinal distribution, heads.go:124-187) stay with the caller. */
+IG_API int ig_logits(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, double *logits,
+              size_t logits_len, double *token_logits, size_t token_len);
+
+/* Message of the calling thread's last failure ("" if none). */
+IG_API const char *ig_last_error(void);
+
+/* First error code a kernel recorded (bounded waits, out-of-vocabulary ids
+ * in ig_encode_device); reset != 0 clears it. Synchronizes the device. */
+IG_API int32_t ig_device_error(int32_t reset);
+
+/* ---- per-operation entry points (device pointers, enqueued on stream) ---- */
+
+/* MatMul8N's integer product and dequantization (linalg/int8.go:88-155):
+ * acc = A . B^T with A uint8 [M][lda] (q + 128) and B int8 [N][ldb] (K bytes
+ * used per row; lda, ldb multiples of 16);
+ * C[i][j] (+)= ((float(acc) - zc[j]) * sb[j]) * sa[i] with row stride ldc.
+ * acc_out (optional, [M][ldc] int32) receives the accumulators instead of C. */
+IG_API int ig_gemm_u8s8(const uint8_t *A, int32_t lda, const int8_t *B, int32_t ldb, int32_t M, int32_t N, int32_t K,
+                 const float *sa, const float *sb, const float *zc, float *C, int32_t ldc, int32_t accumulate,
+                 int32_t *acc_out, void *stream);
+
+/* quantizeA (linalg/int8.go:157-191): per row s = max|x|/127,
+ * q = rne(x * (1/s)) + 128 (all 128 and s = 0 for a zero row). */
+IG_API int ig_quantize_rows(const float *x, int32_t ldx, int32_t M, int32_t K, uint8_t *q, int32_t ldq, float *sa,
+                     void *stream);
+
+/* LayerNormRow (linalg/vec_simd.go:281-327) of each row, optional f32
+ * output xn, and the quantized rows as ig_quantize_rows (q may be NULL). */
+IG_API int ig_layernorm_quant(const float *x, const float *gamma, int32_t M, int32_t H, double eps, int32_t simd_lanes,
+                       float *xn, uint8_t *q, int32_t ldq, float *sa, void *stream);
+
+/* PackB8 with transB (linalg/int8.go:36-77): w [n][k] f32 -> q int8 [n][ldq]
+ * (zero padded), scale [n], zc [n] = 128 * colsum, colsum [n] (optional). */
+IG_API int ig_pack_b8(const float *w, int32_t n, int32_t k, int8_t *q, int32_t ldq, float *scale, float *zc,
+               int32_t *colsum, void *stream);
+
+/* attention8 (infer.go:484-518; linalg/attention8.go): qkv [N][3*hidden]
+ * rows after RoPE, sequences at host offsets offs[nseq+1]; window < 0 for a
+ * global layer, else the half-window; ctx [N][hidden]. Work buffers are
+ * allocated for the call (a test entry point; ig_encode uses its workspace). */
+IG_API int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t *offs, int32_t nseq,
+                 int32_t window, int32_t simd_lanes, float *ctx, void *stream);
+
+/* Per-layer intermediates of one ig_encode call, copied to host buffers for
+ * parity checks (NULL fields are skipped). Layouts as the oracle's. */
+typedef struct ig_dump {
+  int32_t layer;
+  uint8_t *xq;  float *xq_s;  /* QKV input quantized [N][hidden], [N] */
+  float *qkv;                 /* [N][3*hidden] after RoPE */
+  float *ctx;                 /* [N][hidden] */
+  uint8_t *cq;  float *cq_s;  /* Wo input quantized */
+  float *x_attn;              /* residual after attention */
+  uint8_t *hq;  float *hq_s;  /* Wi input quantized */
+  float *g;                   /* [N][intermediate] GeGLU output */
+  uint8_t *gq;  float *gq_s;  /* WoMLP input quantized [N][intermediate] */
+  float *x_mlp;               /* residual after the MLP */
+  float *emb_ln;              /* [N][hidden] embedding after its norm */
+} ig_dump;
+
+IG_API int ig_encode_dump(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
+                   size_t out_len, ig_dump *dump);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INDECIS_B200_H */

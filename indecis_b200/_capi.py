@@ -1,0 +1,102 @@
+"""ctypes binding of libindecis_b200.so (include/indecis_b200.h).
+
+Loading fails loudly when the library has not been built: there is no
+fallback implementation of any entry point.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libindecis_b200.so")
+
+IG_OK = 0
+IG_ERR_BAD_ARG = 1
+IG_ERR_OUT_OF_VOCAB = 2
+IG_ERR_CUDA = 3
+IG_ERR_TIMEOUT = 4
+IG_ERR_UNSUPPORTED = 5
+IG_ERR_NO_DEVICE = 6
+IG_MODE_POOLED = 0
+IG_MODE_TOKENS = 1
+
+# Every symbol the header declares (tests check the library exports them all).
+SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_encode", "ig_encode_device",
+           "ig_logits", "ig_last_error", "ig_device_error", "ig_gemm_u8s8", "ig_quantize_rows",
+           "ig_layernorm_quant", "ig_pack_b8", "ig_attention", "ig_encode_dump"]
+
+
+class IgConfig(C.Structure):
+    _fields_ = [("vocab", C.c_int32), ("hidden", C.c_int32), ("layers", C.c_int32), ("heads", C.c_int32),
+                ("intermediate", C.c_int32), ("global_every", C.c_int32), ("local_attention", C.c_int32),
+                ("pooling", C.c_int32), ("norm_eps", C.c_double), ("global_theta", C.c_double),
+                ("local_theta", C.c_double), ("simd_lanes", C.c_int32)]
+
+
+class IgWeights(C.Structure):
+    _fields_ = [("tok_embeddings", C.c_void_p), ("emb_norm", C.c_void_p), ("final_norm", C.c_void_p),
+                ("attn_norm", C.POINTER(C.c_void_p)), ("wqkv", C.POINTER(C.c_void_p)),
+                ("wo", C.POINTER(C.c_void_p)), ("mlp_norm", C.POINTER(C.c_void_p)),
+                ("wi", C.POINTER(C.c_void_p)), ("wo_mlp", C.POINTER(C.c_void_p))]
+
+
+class IgHead(C.Structure):
+    _fields_ = [("rows", C.c_int32), ("per_token", C.c_int32), ("w", C.c_void_p), ("b", C.c_void_p)]
+
+
+class IgDump(C.Structure):
+    _fields_ = [("layer", C.c_int32)] + [(n, C.c_void_p) for n in (
+        "xq", "xq_s", "qkv", "ctx", "cq", "cq_s", "x_attn", "hq", "hq_s", "g", "gq", "gq_s", "x_mlp", "emb_ln")]
+
+
+_lib = None
+
+
+class LibraryMissing(RuntimeError):
+    pass
+
+
+def load() -> C.CDLL:
+    """Loads the in-tree library (built by indecis_b200.build)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise LibraryMissing(f"{LIB_PATH} is not built: run `python -m indecis_b200.build` (no CPU fallback exists)")
+    L = C.CDLL(LIB_PATH)
+    vp, i32, i64p = C.c_void_p, C.c_int32, C.POINTER(C.c_int64)
+    L.ig_model_create.argtypes = [C.POINTER(IgConfig), C.POINTER(IgWeights), i32, C.POINTER(C.c_void_p)]
+    L.ig_model_create.restype = C.c_int
+    L.ig_model_destroy.argtypes = [vp]
+    L.ig_model_destroy.restype = None
+    L.ig_model_set_heads.argtypes = [vp, i32, C.POINTER(IgHead)]
+    L.ig_encode.argtypes = [vp, vp, vp, i32, i32, vp, C.c_size_t]
+    L.ig_encode_device.argtypes = [vp, vp, vp, i32, i32, vp, vp]
+    L.ig_logits.argtypes = [vp, vp, vp, i32, vp, C.c_size_t, vp, C.c_size_t]
+    L.ig_last_error.restype = C.c_char_p
+    L.ig_device_error.argtypes = [i32]
+    L.ig_device_error.restype = i32
+    L.ig_gemm_u8s8.argtypes = [vp, i32, vp, i32, i32, i32, i32, vp, vp, vp, vp, i32, i32, vp, vp]
+    L.ig_quantize_rows.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp]
+    L.ig_layernorm_quant.argtypes = [vp, vp, i32, i32, C.c_double, i32, vp, vp, i32, vp, vp]
+    L.ig_pack_b8.argtypes = [vp, i32, i32, vp, i32, vp, vp, vp, vp]
+    L.ig_attention.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
+    L.ig_encode_dump.argtypes = [vp, vp, vp, i32, i32, vp, C.c_size_t, C.POINTER(IgDump)]
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    return load().ig_last_error().decode()
+
+
+class IgError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg or f"indecis_b200 error {code}")
+        self.code = code
+
+
+def check(rc: int):
+    if rc != IG_OK:
+        raise IgError(rc, last_error())

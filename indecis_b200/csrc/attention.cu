@@ -1,0 +1,246 @@
+// int8 attention over unpadded variable-length sequences, local (|i-j| <=
+// window) or global, restating linalg/attention8.go (Attn8.prepareAVX2 and
+// Attend) as three kernels:
+//
+//   attn_stats   per (sequence, head, dimension): the mean of K over the
+//                sequence (float32, keys in order, then times 1/float32(n):
+//                AddTo + Scale, attention8.go:224-229) and the V column
+//                scale max|v|/127 with its inverse (attention8.go:255-269).
+//   attn_quant   per (row, head), one warp: Q per row (uint8, q+128; scale
+//                times the score scale), K centred per key (int8, scale,
+//                128*sum), V per column (int8) (quant_amd64.s:17-156).
+//   attn_attend  per (sequence, head, block of queries), one warp per query:
+//                scores ((acc - kzc)*ks)*sq over the query's valid keys,
+//                ExpShift (vector body / scalar tail split by position),
+//                P = rne(e*255) as uint8 with sp = 1/float32(sum P), then
+//                O = (float(sum P*V) * vs) * sp (attention8.go:298-376).
+//
+// All products are exact integer dot products (dp4a), so the scores and
+// outputs are the reference's bits whatever the tiling.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "exactmath.cuh"
+#include "internal.h"
+
+namespace ig {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnQPerWarp = 4;
+constexpr int kAttnQBlock = kAttnWarps * kAttnQPerWarp;
+
+__global__ void attn_stats_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ offs, int H, int nh,
+                                  int D, float *__restrict__ kmean, float *__restrict__ vs,
+                                  float *__restrict__ vinv) {
+  const int s = blockIdx.x, h = blockIdx.y;
+  const int t0 = offs[s], t1 = offs[s + 1];
+  const int n = t1 - t0;
+  const size_t ld = 3 * (size_t)H;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float sum = 0.0f, mx = 0.0f;
+    const float *kc = qkv + (size_t)t0 * ld + H + h * D + d;
+    const float *vc = qkv + (size_t)t0 * ld + 2 * H + h * D + d;
+    int j = 0;
+    for (; j + 4 <= n; j += 4) {
+      const float k0 = kc[(j + 0) * ld], k1 = kc[(j + 1) * ld], k2 = kc[(j + 2) * ld], k3 = kc[(j + 3) * ld];
+      const float v0 = vc[(j + 0) * ld], v1 = vc[(j + 1) * ld], v2 = vc[(j + 2) * ld], v3 = vc[(j + 3) * ld];
+      sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, k0), k1), k2), k3);
+      mx = fmaxf(fmaxf(fmaxf(fmaxf(mx, fabsf(v0)), fabsf(v1)), fabsf(v2)), fabsf(v3));
+    }
+    for (; j < n; j++) {
+      sum = __fadd_rn(sum, kc[j * ld]);
+      mx = fmaxf(mx, fabsf(vc[j * ld]));
+    }
+    const size_t o = ((size_t)s * nh + h) * D + d;
+    kmean[o] = n > 0 ? __fmul_rn(sum, __fdiv_rn(1.0f, (float)n)) : 0.0f;
+    const float sc = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
+    vs[o] = sc;
+    vinv[o] = mx > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+  }
+}
+
+// One warp per (row, head); D <= 128 (each lane holds D/32 values).
+__global__ void attn_quant_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ row_seq, int N, int H,
+                                  int nh, int D, float scale, const float *__restrict__ kmean,
+                                  const float *__restrict__ vinv, uint8_t *__restrict__ qa, float *__restrict__ sq,
+                                  int8_t *__restrict__ kq, float *__restrict__ ks, float *__restrict__ kzc,
+                                  int8_t *__restrict__ vq) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (gw >= N * nh) return;
+  const int row = gw / nh, h = gw % nh;
+  const int s = row_seq[row];
+  const float *base = qkv + (size_t)row * 3 * H + h * D;
+  const size_t plane = (size_t)h * N + row;
+  const float *km = kmean + ((size_t)s * nh + h) * D;
+  const float *vi = vinv + ((size_t)s * nh + h) * D;
+  constexpr int kMax = 4;  // D <= 128
+  float qv[kMax], kv[kMax], vv[kMax];
+  float qmx = 0.0f, kmx = 0.0f;
+#pragma unroll
+  for (int u = 0; u < kMax; u++) {
+    const int d = lane + 32 * u;
+    qv[u] = kv[u] = vv[u] = 0.0f;
+    if (d < D) {
+      qv[u] = base[d];
+      kv[u] = __fsub_rn(base[H + d], km[d]);
+      vv[u] = base[2 * H + d];
+      qmx = fmaxf(qmx, fabsf(qv[u]));
+      kmx = fmaxf(kmx, fabsf(kv[u]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    qmx = fmaxf(qmx, __shfl_xor_sync(0xffffffffu, qmx, o));
+    kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+  }
+  // Q (attention8.go:210-220): uint8 with the 128 offset.
+  const float qs = qmx > 0.0f ? __fdiv_rn(qmx, 127.0f) : 0.0f;
+  const float qinv = qmx > 0.0f ? __fdiv_rn(1.0f, qs) : 0.0f;
+  // K (attention8.go:240-251): centred, int8, scale and 128*sum.
+  const float kss = kmx > 0.0f ? __fdiv_rn(kmx, 127.0f) : 0.0f;
+  const float kinv = kmx > 0.0f ? __fdiv_rn(1.0f, kss) : 0.0f;
+  int ksum = 0;
+#pragma unroll
+  for (int u = 0; u < kMax; u++) {
+    const int d = lane + 32 * u;
+    if (d < D) {
+      int a = qmx > 0.0f ? rne_int(__fmul_rn(qv[u], qinv)) : 0;
+      a = max(-128, min(127, a));
+      qa[plane * D + d] = (uint8_t)(a + 128);
+      int b = 0;
+      if (kmx > 0.0f) {
+        b = rne_int(__fmul_rn(kv[u], kinv));
+        ksum += b;
+        b = max(-128, min(127, b));
+      }
+      kq[plane * D + d] = (int8_t)b;
+      int c = rne_int(__fmul_rn(vv[u], vi[d]));
+      vq[plane * D + d] = (int8_t)max(-128, min(127, c));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ksum += __shfl_xor_sync(0xffffffffu, ksum, o);
+  if (lane == 0) {
+    sq[plane] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
+    ks[plane] = kss;
+    kzc[plane] = kmx > 0.0f ? __fmul_rn(128.0f, (float)ksum) : 0.0f;
+  }
+}
+
+// Block table entry: (sequence, first query).
+__global__ void __launch_bounds__(32 * kAttnWarps)
+    attn_attend_kernel(const int2 *__restrict__ blocks, const int32_t *__restrict__ offs, int N, int H, int nh,
+                       int D, int window, int V, int max_len, const uint8_t *__restrict__ qa,
+                       const float *__restrict__ sq, const int8_t *__restrict__ kq, const float *__restrict__ ks,
+                       const float *__restrict__ kzc, const int8_t *__restrict__ vq, const float *__restrict__ vs,
+                       float *__restrict__ ctx) {
+  extern __shared__ uint8_t attn_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int2 blk = blocks[blockIdx.x];
+  const int s = blk.x, h = blockIdx.y;
+  const int t0 = offs[s];
+  const int n = offs[s + 1] - t0;
+  float *s_buf = reinterpret_cast<float *>(attn_smem) + (size_t)warp * max_len;
+  uint8_t *p_buf = attn_smem + (size_t)kAttnWarps * max_len * sizeof(float) + (size_t)warp * max_len;
+  const int DW = D / 4;  // 32-bit words per row
+  const size_t hbase = (size_t)h * N;
+  const float *vsc = vs + ((size_t)s * nh + h) * D;
+
+  for (int qi = 0; qi < kAttnQPerWarp; qi++) {
+    const int i = blk.y + warp * kAttnQPerWarp + qi;
+    if (i >= n) break;
+    const size_t qrow = hbase + t0 + i;
+    int js = 0, je = n;
+    if (window >= 0) {
+      js = max(0, i - window);
+      je = min(n, i + window + 1);
+    }
+    const int len = je - js;
+    // Scores of the valid keys, and their maximum (MaxOf).
+    uint32_t qw[32];
+    const uint32_t *qsrc = reinterpret_cast<const uint32_t *>(qa + qrow * D);
+#pragma unroll
+    for (int w = 0; w < 32; w++) qw[w] = w < DW ? __ldg(qsrc + w) : 0u;
+    const float sqi = sq[qrow];
+    float mx = -INFINITY;
+    for (int j = js + lane; j < je; j += 32) {
+      const size_t krow = hbase + t0 + j;
+      const uint32_t *ksrc = reinterpret_cast<const uint32_t *>(kq + krow * D);
+      int acc = 0;
+#pragma unroll
+      for (int w = 0; w < 32; w++)
+        if (w < DW) acc = dp4a_us(qw[w], __ldg(ksrc + w), acc);
+      const float sc = dequant1(acc, kzc[krow], ks[krow], sqi);
+      s_buf[j] = sc;
+      mx = fmaxf(mx, sc);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    // exp, uint8 P and its sum (QuantizeRowU8).
+    int psum = 0;
+    for (int j = js + lane; j < je; j += 32) {
+      const float e = exp_shift_at(s_buf[j], mx, j - js, len, V);
+      const int p = rne_int(__fmul_rn(e, 255.0f));
+      p_buf[j] = (uint8_t)p;
+      psum += p;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+    const float sp = __fdiv_rn(1.0f, (float)psum);
+    __syncwarp();
+    // O = P.V over the valid keys, lane d handles dimensions d, d+32, ...
+    int acc[4] = {0, 0, 0, 0};
+    for (int j = js; j < je; j++) {
+      const int p = p_buf[j];
+      const int8_t *vr = vq + (hbase + t0 + j) * D;
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int d = lane + 32 * u;
+        if (d < D) acc[u] += p * (int)vr[d];
+      }
+    }
+    __syncwarp();
+    float *o = ctx + (size_t)(t0 + i) * H + h * D;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int d = lane + 32 * u;
+      if (d < D) o[d] = dequant1(acc[u], 0.0f, vsc[d], sp);
+    }
+  }
+}
+
+int launch_attention(const AttnArgs &a, cudaStream_t st) {
+  if (a.nseq <= 0 || a.N <= 0) return 0;
+  if (a.D > 128 || (a.D % 4) || a.max_len <= 0 || a.V < 1) return IG_ERR_BAD_ARG;
+  const int sthreads = a.D <= 128 ? 128 : 256;
+  attn_stats_kernel<<<dim3(a.nseq, a.nh), sthreads, 0, st>>>(a.qkv, a.offs, a.H, a.nh, a.D, a.kmean, a.vs, a.vinv);
+  if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+  const int warps = a.N * a.nh;
+  attn_quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(a.qkv, a.row_seq, a.N, a.H, a.nh, a.D, a.scale,
+                                                             a.kmean, a.vinv, a.qa, a.sq, a.kq, a.ks, a.kzc, a.vq);
+  if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+  return 0;
+}
+
+// Second half: the attend kernel over a host-built block table.
+int launch_attend(const AttnArgs &a, const int2 *d_blocks, int nblocks, cudaStream_t st) {
+  if (nblocks <= 0) return 0;
+  const size_t smem = (size_t)kAttnWarps * a.max_len * (sizeof(float) + 1);
+  if (smem > 200 * 1024) return IG_ERR_UNSUPPORTED;
+  static size_t smem_set = 0;
+  if (smem > 48 * 1024 && smem > smem_set) {
+    if (cudaFuncSetAttribute(attn_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return IG_ERR_CUDA;
+    smem_set = smem;
+  }
+  attn_attend_kernel<<<dim3(nblocks, a.nh), 32 * kAttnWarps, smem, st>>>(
+      d_blocks, a.offs, a.N, a.H, a.nh, a.D, a.window, a.V, a.max_len, a.qa, a.sq, a.kq, a.ks, a.kzc, a.vq, a.vs,
+      a.ctx);
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
+int attn_query_block() { return kAttnQBlock; }
+
+}  // namespace ig

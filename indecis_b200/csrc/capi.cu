@@ -1,0 +1,838 @@
+// Host runtime behind include/indecis_b200.h: model creation (upload and
+// on-device weight quantization), a per-device workspace pool, and the
+// encoder's launch sequence, which replaces internal/modernbert/infer.go:304-430
+// (run) layer for layer:
+//
+//   embed + LN(emb_norm) + quant           infer.go:361-368
+//   per layer l:
+//     [l > 0] LN(attn_norm) + quant        infer.go:384-389
+//     QKV GEMM, RoPE fused in the epilogue infer.go:390-399
+//     attention (stats, quant, attend)     infer.go:401, :484-518
+//     quant(ctx); Wo GEMM, x += fused      infer.go:403
+//     LN(mlp_norm) + quant                 infer.go:404-406
+//     Wi GEMM, GeGLU fused in the epilogue infer.go:416-419
+//     quant(g); WoMLP GEMM, x += fused     infer.go:423
+//   LN(final_norm), pooling                infer.go:427, :261-289
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace ig {
+
+
+static thread_local std::string t_last_error;
+
+static int fail(int code, const std::string &msg) {
+  t_last_error = msg;
+  return code;
+}
+
+#define IG_CU(x)                                                                         \
+  do {                                                                                   \
+    cudaError_t e_ = (x);                                                                \
+    if (e_ != cudaSuccess) return fail(IG_ERR_CUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define IG_TRY(x)                                                                \
+  do {                                                                           \
+    int r_ = (x);                                                                \
+    if (r_) {                                                                    \
+      if (t_last_error.empty()) t_last_error = std::string("failed: ") + #x;     \
+      return r_;                                                                 \
+    }                                                                            \
+  } while (0)
+
+static inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct DevMat {
+  int8_t *q = nullptr;
+  float *scale = nullptr, *zc = nullptr;
+  int n = 0, k = 0, ld = 0;
+};
+
+struct DevLayer {
+  DevMat qkv, o, wi, wom;
+  float *attn_norm = nullptr, *mlp_norm = nullptr;
+};
+
+struct DevHead {
+  int rows = 0, per_token = 0;
+  float *w = nullptr, *b = nullptr;
+};
+
+struct Plan {
+  int nseq = 0, N = 0, max_len = 0, nblocks = 0;
+  std::vector<int32_t> offs, row_seq, pos;
+  std::vector<int2> blocks;
+};
+
+// Device buffers of one encode call, sized for `rows` rows and `nseq` sequences.
+struct Workspace {
+  int device = 0;
+  size_t rows_cap = 0, seq_cap = 0, blk_cap = 0, tl_cap = 0, pl_cap = 0;
+  void *dev = nullptr;
+  void *host = nullptr;  // pinned staging
+  size_t host_bytes = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaEvent_t done = nullptr;
+  int32_t *ids, *offs, *row_seq, *pos;
+  int2 *blocks;
+  float *x, *xn, *sa, *qkv, *ctx, *g, *sq, *ks, *kzc, *kmean, *vs, *vinv, *pooled;
+  uint8_t *xq, *qa;
+  int8_t *kq, *vq;
+  double *logits, *tlogits;
+  ~Workspace() {
+    if (dev) cudaFree(dev);
+    if (host) cudaFreeHost(host);
+    if (done) cudaEventDestroy(done);
+    if (own_stream) cudaStreamDestroy(own_stream);
+  }
+};
+
+}  // namespace ig
+
+using namespace ig;
+
+struct ig_model {
+  ig_config cfg{};
+  int device = 0;
+  int H = 0, I = 0, nh = 0, D = 0, ldk = 0, NI = 0;
+  float *emb = nullptr, *emb_norm = nullptr, *final_norm = nullptr;
+  std::vector<DevLayer> layers;
+  std::mutex mu;  // rope tables, heads, workspace pool
+  int rope_npos = 0;
+  float *rope_cos[2] = {nullptr, nullptr}, *rope_sin[2] = {nullptr, nullptr};
+  std::vector<void *> retired;  // rope tables replaced by longer ones
+  std::vector<DevHead> heads;
+  std::vector<std::unique_ptr<Workspace>> pool;
+  std::vector<void *> allocs;
+  ~ig_model() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    cudaDeviceSynchronize();
+    pool.clear();
+    for (void *p : allocs) cudaFree(p);
+    for (void *p : retired) cudaFree(p);
+    for (auto &h : heads) {
+      cudaFree(h.w);
+      cudaFree(h.b);
+    }
+    cudaSetDevice(prev);
+  }
+};
+
+namespace {
+
+struct DeviceGuard {
+  int prev = 0;
+  explicit DeviceGuard(int d) {
+    cudaGetDevice(&prev);
+    if (prev != d) cudaSetDevice(d);
+  }
+  ~DeviceGuard() { cudaSetDevice(prev); }
+};
+
+template <class T>
+int dev_alloc(ig_model *m, T **p, size_t count) {
+  void *v = nullptr;
+  IG_CU(cudaMalloc(&v, std::max<size_t>(count * sizeof(T), 16)));
+  m->allocs.push_back(v);
+  *p = reinterpret_cast<T *>(v);
+  return 0;
+}
+
+int upload(ig_model *m, float **dst, const float *src, size_t count) {
+  IG_TRY(dev_alloc(m, dst, count));
+  IG_CU(cudaMemcpy(*dst, src, count * sizeof(float), cudaMemcpyHostToDevice));
+  return 0;
+}
+
+// Quantizes a float32 [n][k] host matrix into a DevMat with n_out packed
+// rows (perm chooses their source rows).
+int pack_matrix(ig_model *m, DevMat &dm, const float *w, int n, int k, const std::vector<int32_t> &perm, float *tmp,
+                int32_t *d_perm) {
+  const int n_out = perm.empty() ? n : (int)perm.size();
+  dm.n = n_out;
+  dm.k = k;
+  dm.ld = (int)align_up(k, 16);
+  IG_TRY(dev_alloc(m, &dm.q, (size_t)n_out * dm.ld));
+  IG_TRY(dev_alloc(m, &dm.scale, n_out));
+  IG_TRY(dev_alloc(m, &dm.zc, n_out));
+  IG_CU(cudaMemcpy(tmp, w, (size_t)n * k * sizeof(float), cudaMemcpyHostToDevice));
+  if (!perm.empty()) IG_CU(cudaMemcpy(d_perm, perm.data(), perm.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
+  IG_TRY(launch_pack_b8(tmp, n, k, perm.empty() ? nullptr : d_perm, n_out, dm.q, dm.ld, dm.scale, dm.zc, nullptr,
+                        0));
+  IG_CU(cudaDeviceSynchronize());
+  return 0;
+}
+
+// RoPE cos/sin of the reference's table (internal/modernbert/model.go:255-277),
+// computed on the host in float64 as there, for npos positions.
+void rope_table_host(double theta, int D, int npos, std::vector<float> &cs, std::vector<float> &sn) {
+  const int half = D / 2;
+  cs.assign((size_t)npos * half, 0.0f);
+  sn.assign((size_t)npos * half, 0.0f);
+  for (int i = 0; i < half; i++) {
+    const float inv = (float)(1.0 / std::pow(theta, (double)(2 * i) / (double)D));
+    for (int p = 0; p < npos; p++) {
+      const double f = (double)((float)p * inv);
+      cs[(size_t)p * half + i] = (float)std::cos(f);
+      sn[(size_t)p * half + i] = (float)std::sin(f);
+    }
+  }
+}
+
+int ensure_rope(ig_model *m, int npos) {
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (m->rope_npos >= npos) return 0;
+  const int n = std::max(npos, std::max(512, m->rope_npos * 2));
+  const double thetas[2] = {m->cfg.global_theta, m->cfg.local_theta};
+  for (int t = 0; t < 2; t++) {
+    std::vector<float> cs, sn;
+    rope_table_host(thetas[t], m->D, n, cs, sn);
+    float *dc = nullptr, *ds = nullptr;
+    IG_CU(cudaMalloc(&dc, cs.size() * sizeof(float)));
+    IG_CU(cudaMalloc(&ds, sn.size() * sizeof(float)));
+    IG_CU(cudaMemcpy(dc, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
+    IG_CU(cudaMemcpy(ds, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+    // The old tables may still be read by enqueued work: retire, free at destroy.
+    if (m->rope_cos[t]) m->retired.push_back(m->rope_cos[t]);
+    if (m->rope_sin[t]) m->retired.push_back(m->rope_sin[t]);
+    m->rope_cos[t] = dc;
+    m->rope_sin[t] = ds;
+  }
+  m->rope_npos = n;
+  return 0;
+}
+
+int make_plan(const int64_t *offs, int nseq, Plan &p) {
+  if (nseq < 0 || !offs) return fail(IG_ERR_BAD_ARG, "modernbert: inconsistent batch");
+  if (offs[0] != 0) return fail(IG_ERR_BAD_ARG, "modernbert: offs[0] must be 0");
+  const int64_t N = offs[nseq];
+  if (N < 0 || N > (int64_t)INT32_MAX / 4) return fail(IG_ERR_BAD_ARG, "modernbert: batch too large");
+  p.nseq = nseq;
+  p.N = (int)N;
+  p.offs.resize(nseq + 1);
+  p.row_seq.resize(N);
+  p.pos.resize(N);
+  p.blocks.clear();
+  p.max_len = 0;
+  const int qb = attn_query_block();
+  for (int s = 0; s < nseq; s++) {
+    if (offs[s + 1] < offs[s]) return fail(IG_ERR_BAD_ARG, "modernbert: decreasing offsets");
+    p.offs[s] = (int32_t)offs[s];
+    const int n = (int)(offs[s + 1] - offs[s]);
+    p.max_len = std::max(p.max_len, n);
+    for (int t = 0; t < n; t++) {
+      p.row_seq[offs[s] + t] = s;
+      p.pos[offs[s] + t] = t;
+    }
+    for (int q0 = 0; q0 < n; q0 += qb) p.blocks.push_back(make_int2(s, q0));
+  }
+  p.offs[nseq] = (int32_t)N;
+  p.nblocks = (int)p.blocks.size();
+  return 0;
+}
+
+struct Carve {
+  char *base;
+  size_t off = 0;
+  template <class T>
+  T *take(size_t count) {
+    off = align_up(off, 256);
+    T *p = reinterpret_cast<T *>(base ? base + off : nullptr);
+    off += std::max<size_t>(count * sizeof(T), 16);
+    return p;
+  }
+};
+
+void carve_ws(Workspace &w, const ig_model *m, char *base, size_t rows, size_t seqs, size_t blks, size_t tl,
+              size_t pl, size_t *total) {
+  Carve c{base};
+  const size_t H = m->H, I = m->I, nh = m->nh, D = m->D;
+  w.ids = c.take<int32_t>(rows);
+  w.offs = c.take<int32_t>(seqs + 1);
+  w.row_seq = c.take<int32_t>(rows);
+  w.pos = c.take<int32_t>(rows);
+  w.blocks = c.take<int2>(blks);
+  w.x = c.take<float>(rows * H);
+  w.xn = c.take<float>(rows * H);
+  w.sa = c.take<float>(rows);
+  w.xq = c.take<uint8_t>(rows * m->ldk);
+  w.qkv = c.take<float>(rows * 3 * H);
+  w.ctx = c.take<float>(rows * H);
+  w.g = c.take<float>(rows * I);
+  w.qa = c.take<uint8_t>(rows * nh * D);
+  w.kq = c.take<int8_t>(rows * nh * D);
+  w.vq = c.take<int8_t>(rows * nh * D);
+  w.sq = c.take<float>(rows * nh);
+  w.ks = c.take<float>(rows * nh);
+  w.kzc = c.take<float>(rows * nh);
+  w.kmean = c.take<float>(seqs * nh * D);
+  w.vs = c.take<float>(seqs * nh * D);
+  w.vinv = c.take<float>(seqs * nh * D);
+  w.pooled = c.take<float>(seqs * H);
+  w.logits = c.take<double>(seqs * pl);
+  w.tlogits = c.take<double>(rows * tl);
+  *total = c.off;
+}
+
+// Takes a workspace with room for the plan; `st` then waits for the
+// workspace's previous user.
+int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st, bool capturing, Workspace **out) {
+  std::unique_ptr<Workspace> w;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    if (!m->pool.empty()) {
+      w = std::move(m->pool.back());
+      m->pool.pop_back();
+    }
+  }
+  if (!w) {
+    w.reset(new Workspace());
+    w->device = m->device;
+    IG_CU(cudaEventCreateWithFlags(&w->done, cudaEventDisableTiming));
+  }
+  const size_t rows = std::max<size_t>(p.N, 1), seqs = std::max<size_t>(p.nseq, 1),
+               blks = std::max<size_t>(p.nblocks, 1);
+  if (rows > w->rows_cap || seqs > w->seq_cap || blks > w->blk_cap || tl > w->tl_cap || pl > w->pl_cap) {
+    if (capturing) return fail(IG_ERR_BAD_ARG, "workspace must be sized before stream capture");
+    IG_CU(cudaEventSynchronize(w->done));
+    if (w->dev) IG_CU(cudaFree(w->dev));
+    w->dev = nullptr;
+    const size_t r2 = std::max(rows, w->rows_cap), s2 = std::max(seqs, w->seq_cap), b2 = std::max(blks, w->blk_cap);
+    const size_t t2 = std::max(tl, w->tl_cap), p2 = std::max(pl, w->pl_cap);
+    size_t total = 0;
+    carve_ws(*w, m, nullptr, r2, s2, b2, t2, p2, &total);
+    IG_CU(cudaMalloc(&w->dev, total));
+    carve_ws(*w, m, reinterpret_cast<char *>(w->dev), r2, s2, b2, t2, p2, &total);
+    w->rows_cap = r2;
+    w->seq_cap = s2;
+    w->blk_cap = b2;
+    w->tl_cap = t2;
+    w->pl_cap = p2;
+  }
+  const size_t hb = sizeof(int32_t) * (p.nseq + 1 + 3 * (size_t)p.N) + sizeof(int2) * p.nblocks + 64;
+  if (hb > w->host_bytes) {
+    if (capturing) return fail(IG_ERR_BAD_ARG, "workspace must be sized before stream capture");
+    IG_CU(cudaEventSynchronize(w->done));
+    if (w->host) IG_CU(cudaFreeHost(w->host));
+    w->host = nullptr;
+    IG_CU(cudaMallocHost(&w->host, hb * 2));
+    w->host_bytes = hb * 2;
+  }
+  if (!capturing) {
+    IG_CU(cudaEventSynchronize(w->done));  // staging buffer reuse
+    IG_CU(cudaStreamWaitEvent(st, w->done, 0));
+  }
+  *out = w.release();
+  return 0;
+}
+
+void release_ws(ig_model *m, Workspace *w, cudaStream_t st, bool capturing) {
+  if (!capturing) cudaEventRecord(w->done, st);
+  std::lock_guard<std::mutex> lk(m->mu);
+  m->pool.emplace_back(w);
+}
+
+// Uploads the plan's metadata (offsets, row -> sequence, positions, query
+// blocks, and optionally the host ids) with one copy.
+int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream_t st) {
+  char *h = reinterpret_cast<char *>(w.host);
+  size_t off = 0;
+  auto put = [&](const void *src, size_t bytes) {
+    std::memcpy(h + off, src, bytes);
+    off += bytes;
+  };
+  put(p.offs.data(), sizeof(int32_t) * (p.nseq + 1));
+  put(p.row_seq.data(), sizeof(int32_t) * p.N);
+  put(p.pos.data(), sizeof(int32_t) * p.N);
+  put(p.blocks.data(), sizeof(int2) * p.nblocks);
+  if (host_ids) put(host_ids, sizeof(int32_t) * p.N);
+  // The device buffers are carved separately: issue one copy per region
+  // from the pinned staging (small, contiguous on the host).
+  size_t o = 0;
+  IG_CU(cudaMemcpyAsync(w.offs, h + o, sizeof(int32_t) * (p.nseq + 1), cudaMemcpyHostToDevice, st));
+  o += sizeof(int32_t) * (p.nseq + 1);
+  if (p.N) {
+    IG_CU(cudaMemcpyAsync(w.row_seq, h + o, sizeof(int32_t) * p.N, cudaMemcpyHostToDevice, st));
+    o += sizeof(int32_t) * p.N;
+    IG_CU(cudaMemcpyAsync(w.pos, h + o, sizeof(int32_t) * p.N, cudaMemcpyHostToDevice, st));
+    o += sizeof(int32_t) * p.N;
+  }
+  if (p.nblocks) IG_CU(cudaMemcpyAsync(w.blocks, h + o, sizeof(int2) * p.nblocks, cudaMemcpyHostToDevice, st));
+  o += sizeof(int2) * p.nblocks;
+  if (host_ids && p.N) IG_CU(cudaMemcpyAsync(w.ids, h + o, sizeof(int32_t) * p.N, cudaMemcpyHostToDevice, st));
+  return 0;
+}
+
+int copy_rows_d2h(void *dst, const void *src, size_t row_bytes, size_t src_pitch, size_t rows, cudaStream_t st) {
+  if (!dst || rows == 0) return 0;
+  IG_CU(cudaMemcpy2DAsync(dst, row_bytes, src, src_pitch, row_bytes, rows, cudaMemcpyDeviceToHost, st));
+  return 0;
+}
+
+// The layer loop. d_ids: device ids; results in w.xn (tokens) / w.pooled.
+int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, int mode, cudaStream_t st,
+                ig_dump *dump) {
+  const ig_config &c = m->cfg;
+  const int H = m->H, I = m->I, N = p.N;
+  const int V = c.simd_lanes;
+  if (N == 0) return 0;
+  IG_TRY(launch_embed_checked(d_ids, c.vocab, m->emb, m->emb_norm, N, H, c.norm_eps, V, w.x, w.xq, m->ldk, w.sa, st));
+  if (dump && dump->emb_ln) IG_TRY(copy_rows_d2h(dump->emb_ln, w.x, H * 4, H * 4, N, st));
+  AttnArgs at{};
+  at.qkv = w.qkv;
+  at.H = H;
+  at.nh = m->nh;
+  at.D = m->D;
+  at.offs = w.offs;
+  at.nseq = p.nseq;
+  at.max_len = p.max_len;
+  at.scale = (float)(1.0 / std::sqrt((double)m->D));
+  at.V = V;
+  at.qa = w.qa;
+  at.sq = w.sq;
+  at.kq = w.kq;
+  at.ks = w.ks;
+  at.kzc = w.kzc;
+  at.vq = w.vq;
+  at.kmean = w.kmean;
+  at.vs = w.vs;
+  at.vinv = w.vinv;
+  at.row_seq = w.row_seq;
+  at.N = N;
+  at.ctx = w.ctx;
+  for (int l = 0; l < c.layers; l++) {
+    const DevLayer &L = m->layers[l];
+    const bool global = l % c.global_every == 0;
+    const bool dl = dump && dump->layer == l;
+    if (l > 0)
+      IG_TRY(launch_ln_quant(w.x, L.attn_norm, N, H, c.norm_eps, V, nullptr, w.xq, m->ldk, w.sa, st));
+    if (dl) {
+      IG_TRY(copy_rows_d2h(dump->xq, w.xq, H, m->ldk, N, st));
+      IG_TRY(copy_rows_d2h(dump->xq_s, w.sa, 4, 4, N, st));
+    }
+    {
+      GemmArgs g{w.xq, L.qkv.q, N, L.qkv.n, H, m->ldk, L.qkv.ld, 256};
+      GemmEpilogue e{};
+      e.sa = w.sa;
+      e.sb = L.qkv.scale;
+      e.zc = L.qkv.zc;
+      e.C = w.qkv;
+      e.ldc = 3 * H;
+      e.pos = w.pos;
+      e.rope_cos = m->rope_cos[global ? 0 : 1];
+      e.rope_sin = m->rope_sin[global ? 0 : 1];
+      e.rope_cols = 2 * H;
+      IG_TRY(gemm_u8s8(g, e, kEpiRope, st));
+    }
+    if (dl) IG_TRY(copy_rows_d2h(dump->qkv, w.qkv, 3 * H * 4, 3 * H * 4, N, st));
+    at.window = global ? -1 : c.local_attention / 2;
+    IG_TRY(launch_attention(at, st));
+    IG_TRY(launch_attend(at, w.blocks, p.nblocks, st));
+    if (dl) IG_TRY(copy_rows_d2h(dump->ctx, w.ctx, H * 4, H * 4, N, st));
+    IG_TRY(launch_quant_rows(w.ctx, H, N, H, w.xq, m->ldk, w.sa, st));
+    if (dl) {
+      IG_TRY(copy_rows_d2h(dump->cq, w.xq, H, m->ldk, N, st));
+      IG_TRY(copy_rows_d2h(dump->cq_s, w.sa, 4, 4, N, st));
+    }
+    {
+      GemmArgs g{w.xq, L.o.q, N, L.o.n, H, m->ldk, L.o.ld, 0};
+      GemmEpilogue e{};
+      e.sa = w.sa;
+      e.sb = L.o.scale;
+      e.zc = L.o.zc;
+      e.C = w.x;
+      e.ldc = H;
+      e.accumulate = 1;
+      IG_TRY(gemm_u8s8(g, e, kEpiF32, st));
+    }
+    if (dl) IG_TRY(copy_rows_d2h(dump->x_attn, w.x, H * 4, H * 4, N, st));
+    IG_TRY(launch_ln_quant(w.x, L.mlp_norm, N, H, c.norm_eps, V, nullptr, w.xq, m->ldk, w.sa, st));
+    if (dl) {
+      IG_TRY(copy_rows_d2h(dump->hq, w.xq, H, m->ldk, N, st));
+      IG_TRY(copy_rows_d2h(dump->hq_s, w.sa, 4, 4, N, st));
+    }
+    {
+      GemmArgs g{w.xq, L.wi.q, N, L.wi.n, H, m->ldk, L.wi.ld, 256};
+      GemmEpilogue e{};
+      e.sa = w.sa;
+      e.sb = L.wi.scale;
+      e.zc = L.wi.zc;
+      e.C = w.g;
+      e.ldc = I;
+      e.geglu_n = I;
+      IG_TRY(gemm_u8s8(g, e, kEpiGeglu, st));
+    }
+    if (dl) IG_TRY(copy_rows_d2h(dump->g, w.g, I * 4, I * 4, N, st));
+    IG_TRY(launch_quant_rows(w.g, I, N, I, w.xq, m->ldk, w.sa, st));
+    if (dl) {
+      IG_TRY(copy_rows_d2h(dump->gq, w.xq, I, m->ldk, N, st));
+      IG_TRY(copy_rows_d2h(dump->gq_s, w.sa, 4, 4, N, st));
+    }
+    {
+      GemmArgs g{w.xq, L.wom.q, N, L.wom.n, I, m->ldk, L.wom.ld, 0};
+      GemmEpilogue e{};
+      e.sa = w.sa;
+      e.sb = L.wom.scale;
+      e.zc = L.wom.zc;
+      e.C = w.x;
+      e.ldc = H;
+      e.accumulate = 1;
+      IG_TRY(gemm_u8s8(g, e, kEpiF32, st));
+    }
+    if (dl) IG_TRY(copy_rows_d2h(dump->x_mlp, w.x, H * 4, H * 4, N, st));
+  }
+  IG_TRY(launch_ln_quant(w.x, m->final_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
+  if (mode == IG_MODE_POOLED)
+    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, c.pooling == IG_POOL_CLS, w.pooled, st));
+  return 0;
+}
+
+int check_ids(const ig_model *m, const int32_t *ids, int64_t N) {
+  for (int64_t t = 0; t < N; t++)
+    if (ids[t] < 0 || ids[t] >= m->cfg.vocab)
+      return fail(IG_ERR_OUT_OF_VOCAB, "modernbert: id " + std::to_string(ids[t]) + " out of vocabulary");
+  return 0;
+}
+
+int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
+                size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len) {
+  t_last_error.clear();
+  if (!m || (nseq > 0 && !offs)) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS) return fail(IG_ERR_BAD_ARG, "bad mode");
+  DeviceGuard dg(m->device);
+  Plan p;
+  IG_TRY(make_plan(offs, nseq, p));
+  if (p.N > 0 && !ids) return fail(IG_ERR_BAD_ARG, "null ids");
+  IG_TRY(check_ids(m, ids, p.N));
+  const size_t H = m->H;
+  const size_t need = mode == IG_MODE_POOLED ? (size_t)nseq * H : (size_t)p.N * H;
+  if (out && out_len < need) return fail(IG_ERR_BAD_ARG, "output too short");
+  size_t pl = 0, tl = 0;
+  if (logits || tlog) {
+    std::lock_guard<std::mutex> lk(m->mu);
+    for (auto &h : m->heads) (h.per_token ? tl : pl) += h.rows;
+  }
+  if (logits && logits_len < (size_t)nseq * pl) return fail(IG_ERR_BAD_ARG, "logits too short");
+  if (tlog && tlog_len < (size_t)p.N * tl) return fail(IG_ERR_BAD_ARG, "token logits too short");
+  IG_TRY(ensure_rope(m, p.max_len));
+  Workspace *w = nullptr;
+  cudaStream_t st = nullptr;
+  IG_TRY(acquire_ws(m, p, tl, pl, nullptr, false, &w));
+  if (!w->own_stream) IG_CU(cudaStreamCreateWithFlags(&w->own_stream, cudaStreamNonBlocking));
+  st = w->own_stream;
+  int rc = upload_plan(*w, p, ids, st);
+  const int enc_mode = (logits || tlog) ? IG_MODE_POOLED : mode;
+  if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump);
+  if (!rc && (logits || tlog)) {
+    std::vector<DevHead> hs;
+    {
+      std::lock_guard<std::mutex> lk(m->mu);
+      hs = m->heads;
+    }
+    size_t po = 0, to = 0;
+    for (auto &h : hs) {
+      if (h.per_token) {
+        if (tlog) rc = launch_head_logits(h.w, h.b, h.rows, (int)H, w->xn, p.N, w->tlogits + to, (int)tl, st);
+        to += h.rows;
+      } else {
+        if (logits) rc = launch_head_logits(h.w, h.b, h.rows, (int)H, w->pooled, nseq, w->logits + po, (int)pl, st);
+        po += h.rows;
+      }
+      if (rc) break;
+    }
+    if (!rc && logits && nseq && pl)
+      rc = cudaMemcpyAsync(logits, w->logits, sizeof(double) * nseq * pl, cudaMemcpyDeviceToHost, st) ? IG_ERR_CUDA : 0;
+    if (!rc && tlog && p.N && tl)
+      rc = cudaMemcpyAsync(tlog, w->tlogits, sizeof(double) * p.N * tl, cudaMemcpyDeviceToHost, st) ? IG_ERR_CUDA : 0;
+  }
+  if (!rc && out && need) {
+    const float *src = mode == IG_MODE_POOLED ? w->pooled : w->xn;
+    if (mode == IG_MODE_POOLED && p.N == 0) {
+      std::memset(out, 0, need * sizeof(float));
+    } else if (cudaMemcpyAsync(out, src, need * sizeof(float), cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+      rc = fail(IG_ERR_CUDA, "copy of the output");
+    }
+  }
+  cudaError_t se = cudaStreamSynchronize(st);
+  release_ws(m, w, st, false);
+  if (rc) return rc;
+  if (se != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(se));
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, ig_model **out) {
+  t_last_error.clear();
+  if (!cfg || !w || !out) return fail(IG_ERR_BAD_ARG, "null argument");
+  *out = nullptr;
+  const ig_config &c = *cfg;
+  // Config.validate (internal/modernbert/model.go:64-80).
+  if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.intermediate <= 0 || c.vocab <= 0)
+    return fail(IG_ERR_BAD_ARG, "modernbert: invalid dimensions");
+  if (c.hidden % c.heads != 0 || (c.hidden / c.heads) % 2 != 0)
+    return fail(IG_ERR_BAD_ARG, "modernbert: hidden_size " + std::to_string(c.hidden) + " incompatible with " +
+                                    std::to_string(c.heads) + " heads");
+  if (c.global_every <= 0 || c.local_attention <= 0) return fail(IG_ERR_BAD_ARG, "modernbert: invalid attention windows");
+  if (c.pooling != IG_POOL_MEAN && c.pooling != IG_POOL_CLS) return fail(IG_ERR_BAD_ARG, "modernbert: pooling not supported");
+  if (c.simd_lanes < 1 || c.simd_lanes > 32) return fail(IG_ERR_BAD_ARG, "simd_lanes must be in [1, 32]");
+  if (c.hidden / c.heads != 64) return fail(IG_ERR_UNSUPPORTED, "head dimension must be 64 in this build");
+  if (c.hidden > 4096 || c.intermediate > 8192) return fail(IG_ERR_UNSUPPORTED, "hidden/intermediate too large");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+    return fail(IG_ERR_NO_DEVICE, "no such CUDA device");
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10)
+    return fail(IG_ERR_NO_DEVICE, "device is not sm_100");
+  DeviceGuard dg(device);
+  std::unique_ptr<ig_model> m(new ig_model());
+  m->cfg = c;
+  m->device = device;
+  m->H = c.hidden;
+  m->I = c.intermediate;
+  m->nh = c.heads;
+  m->D = c.hidden / c.heads;
+  m->ldk = (int)align_up(std::max(c.hidden, c.intermediate), 16);
+  m->NI = (c.intermediate + 127) / 128 * 256;
+  const int H = m->H, I = m->I;
+  IG_TRY(upload(m.get(), &m->emb, w->tok_embeddings, (size_t)c.vocab * H));
+  IG_TRY(upload(m.get(), &m->emb_norm, w->emb_norm, H));
+  IG_TRY(upload(m.get(), &m->final_norm, w->final_norm, H));
+  float *tmp = nullptr;
+  int32_t *dperm = nullptr;
+  const size_t tmp_elems = (size_t)std::max(3 * H, 2 * I) * std::max(H, I);
+  IG_CU(cudaMalloc(&tmp, tmp_elems * sizeof(float)));
+  IG_CU(cudaMalloc(&dperm, sizeof(int32_t) * m->NI));
+  // Wi rows interleaved per 128: [input 128t.., gate 128t..] so one 256-wide
+  // tile holds matching GELU inputs and gates.
+  std::vector<int32_t> wi_perm(m->NI);
+  for (int p = 0; p < m->NI; p++) {
+    const int t = p / 256, r = p % 256;
+    const int ch = 128 * t + (r % 128);
+    wi_perm[p] = ch < I ? (r < 128 ? ch : I + ch) : -1;
+  }
+  m->layers.resize(c.layers);
+  int rc = 0;
+  for (int l = 0; l < c.layers && !rc; l++) {
+    DevLayer &L = m->layers[l];
+    if (l > 0) rc = upload(m.get(), &L.attn_norm, w->attn_norm[l], H);
+    if (!rc) rc = upload(m.get(), &L.mlp_norm, w->mlp_norm[l], H);
+    if (!rc) rc = pack_matrix(m.get(), L.qkv, w->wqkv[l], 3 * H, H, {}, tmp, dperm);
+    if (!rc) rc = pack_matrix(m.get(), L.o, w->wo[l], H, H, {}, tmp, dperm);
+    if (!rc) rc = pack_matrix(m.get(), L.wi, w->wi[l], 2 * I, H, wi_perm, tmp, dperm);
+    if (!rc) rc = pack_matrix(m.get(), L.wom, w->wo_mlp[l], H, I, {}, tmp, dperm);
+  }
+  cudaFree(tmp);
+  cudaFree(dperm);
+  if (rc) return rc;
+  IG_TRY(ensure_rope(m.get(), 512));
+  *out = m.release();
+  return 0;
+}
+
+void ig_model_destroy(ig_model *m) { delete m; }
+
+int ig_model_set_heads(ig_model *m, int32_t nheads, const ig_head *heads) {
+  t_last_error.clear();
+  if (!m || nheads < 0 || (nheads && !heads)) return fail(IG_ERR_BAD_ARG, "null argument");
+  DeviceGuard dg(m->device);
+  std::vector<DevHead> hs(nheads);
+  for (int i = 0; i < nheads; i++) {
+    if (heads[i].rows <= 0 || !heads[i].w || !heads[i].b) return fail(IG_ERR_BAD_ARG, "bad head");
+    hs[i].rows = heads[i].rows;
+    hs[i].per_token = heads[i].per_token;
+    const size_t nw = (size_t)heads[i].rows * m->H;
+    IG_CU(cudaMalloc(&hs[i].w, nw * sizeof(float)));
+    IG_CU(cudaMalloc(&hs[i].b, heads[i].rows * sizeof(float)));
+    IG_CU(cudaMemcpy(hs[i].w, heads[i].w, nw * sizeof(float), cudaMemcpyHostToDevice));
+    IG_CU(cudaMemcpy(hs[i].b, heads[i].b, heads[i].rows * sizeof(float), cudaMemcpyHostToDevice));
+  }
+  IG_CU(cudaDeviceSynchronize());
+  std::lock_guard<std::mutex> lk(m->mu);
+  for (auto &h : m->heads) {
+    cudaFree(h.w);
+    cudaFree(h.b);
+  }
+  m->heads = hs;
+  return 0;
+}
+
+int ig_encode(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
+              size_t out_len) {
+  if (!out) return fail(IG_ERR_BAD_ARG, "null output");
+  return encode_host(m, ids, offs, nseq, mode, out, out_len, nullptr, nullptr, 0, nullptr, 0);
+}
+
+int ig_encode_dump(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
+                   size_t out_len, ig_dump *dump) {
+  return encode_host(m, ids, offs, nseq, mode, out, out_len, dump, nullptr, 0, nullptr, 0);
+}
+
+int ig_logits(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, double *logits, size_t logits_len,
+              double *token_logits, size_t token_len) {
+  if (!logits && !token_logits) return fail(IG_ERR_BAD_ARG, "no output");
+  return encode_host(m, ids, offs, nseq, IG_MODE_POOLED, nullptr, 0, nullptr, logits, logits_len, token_logits,
+                     token_len);
+}
+
+int ig_encode_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int32_t nseq, int32_t mode,
+                     float *d_out, void *stream) {
+  t_last_error.clear();
+  if (!m || !offs || !d_out) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS) return fail(IG_ERR_BAD_ARG, "bad mode");
+  DeviceGuard dg(m->device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  IG_CU(cudaStreamIsCapturing(st, &cs));
+  const bool capturing = cs != cudaStreamCaptureStatusNone;
+  Plan p;
+  IG_TRY(make_plan(offs, nseq, p));
+  if (capturing && m->rope_npos < p.max_len) return fail(IG_ERR_BAD_ARG, "run once before capturing");
+  IG_TRY(ensure_rope(m, p.max_len));
+  Workspace *w = nullptr;
+  IG_TRY(acquire_ws(m, p, 0, 0, st, capturing, &w));
+  int rc = upload_plan(*w, p, nullptr, st);
+  if (!rc) rc = run_encoder(m, *w, d_ids, p, mode, st, nullptr);
+  if (!rc && p.N) {
+    const size_t H = m->H;
+    if (mode == IG_MODE_POOLED)
+      rc = cudaMemcpyAsync(d_out, w->pooled, sizeof(float) * nseq * H, cudaMemcpyDeviceToDevice, st) ? IG_ERR_CUDA : 0;
+    else
+      rc = cudaMemcpyAsync(d_out, w->xn, sizeof(float) * p.N * H, cudaMemcpyDeviceToDevice, st) ? IG_ERR_CUDA : 0;
+  } else if (!rc && mode == IG_MODE_POOLED && nseq) {
+    rc = cudaMemsetAsync(d_out, 0, sizeof(float) * nseq * m->H, st) ? IG_ERR_CUDA : 0;
+  }
+  release_ws(m, w, st, capturing);
+  return rc;
+}
+
+const char *ig_last_error(void) { return t_last_error.c_str(); }
+
+int32_t ig_device_error(int32_t reset) {
+  cudaDeviceSynchronize();
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_device_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+int ig_gemm_u8s8(const uint8_t *A, int32_t lda, const int8_t *B, int32_t ldb, int32_t M, int32_t N, int32_t K,
+                 const float *sa, const float *sb, const float *zc, float *C, int32_t ldc, int32_t accumulate,
+                 int32_t *acc_out, void *stream) {
+  t_last_error.clear();
+  if (M < 0 || N < 0 || K < 0) return fail(IG_ERR_BAD_ARG, "negative size");
+  if (!acc_out && (!sa || !sb || !zc || !C)) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (ldc < N) return fail(IG_ERR_BAD_ARG, "ldc must be >= N");
+  GemmArgs g{A, B, M, N, K, lda, ldb, 0};
+  GemmEpilogue e{};
+  e.sa = sa;
+  e.sb = sb;
+  e.zc = zc;
+  e.C = C;
+  e.ldc = ldc;
+  e.accumulate = accumulate;
+  e.acc_out = acc_out;
+  int rc = gemm_u8s8(g, e, acc_out ? kEpiI32 : kEpiF32, reinterpret_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "ig_gemm_u8s8: bad shape, stride or alignment (lda/ldb multiples of 16, >= K)");
+  return 0;
+}
+
+int ig_quantize_rows(const float *x, int32_t ldx, int32_t M, int32_t K, uint8_t *q, int32_t ldq, float *sa,
+                     void *stream) {
+  t_last_error.clear();
+  int rc = launch_quant_rows(x, ldx, M, K, q, ldq, sa, reinterpret_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "ig_quantize_rows failed") : 0;
+}
+
+int ig_layernorm_quant(const float *x, const float *gamma, int32_t M, int32_t H, double eps, int32_t simd_lanes,
+                       float *xn, uint8_t *q, int32_t ldq, float *sa, void *stream) {
+  t_last_error.clear();
+  if (!gamma) return fail(IG_ERR_BAD_ARG, "null gamma");
+  int rc = launch_ln_quant(x, gamma, M, H, eps, simd_lanes, xn, q, ldq, sa, reinterpret_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "ig_layernorm_quant failed") : 0;
+}
+
+int ig_pack_b8(const float *w, int32_t n, int32_t k, int8_t *q, int32_t ldq, float *scale, float *zc,
+               int32_t *colsum, void *stream) {
+  t_last_error.clear();
+  int rc = launch_pack_b8(w, n, k, nullptr, n, q, ldq, scale, zc, colsum, reinterpret_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "ig_pack_b8 failed") : 0;
+}
+
+int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t *offs, int32_t nseq, int32_t window,
+                 int32_t simd_lanes, float *ctx, void *stream) {
+  t_last_error.clear();
+  if (!qkv || !ctx || !offs || heads <= 0 || hidden % heads) return fail(IG_ERR_BAD_ARG, "bad argument");
+  Plan p;
+  IG_TRY(make_plan(offs, nseq, p));
+  if (p.N == 0) return 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t N = p.N, nh = heads, D = hidden / heads;
+  AttnArgs a{};
+  a.qkv = qkv;
+  a.H = hidden;
+  a.nh = heads;
+  a.D = (int)D;
+  a.nseq = nseq;
+  a.max_len = p.max_len;
+  a.window = window;
+  a.scale = (float)(1.0 / std::sqrt((double)D));
+  a.V = simd_lanes;
+  a.N = p.N;
+  a.ctx = ctx;
+  std::vector<void *> bufs;
+  auto take = [&](size_t bytes) {
+    void *v = nullptr;
+    if (cudaMalloc(&v, std::max<size_t>(bytes, 16)) != cudaSuccess) return (void *)nullptr;
+    bufs.push_back(v);
+    return v;
+  };
+  int32_t *d_offs = (int32_t *)take(4 * (nseq + 1));
+  int32_t *d_rs = (int32_t *)take(4 * N);
+  int2 *d_blk = (int2 *)take(sizeof(int2) * p.nblocks);
+  a.qa = (uint8_t *)take(N * nh * D);
+  a.kq = (int8_t *)take(N * nh * D);
+  a.vq = (int8_t *)take(N * nh * D);
+  a.sq = (float *)take(4 * N * nh);
+  a.ks = (float *)take(4 * N * nh);
+  a.kzc = (float *)take(4 * N * nh);
+  a.kmean = (float *)take(4 * nseq * nh * D);
+  a.vs = (float *)take(4 * nseq * nh * D);
+  a.vinv = (float *)take(4 * nseq * nh * D);
+  a.offs = d_offs;
+  a.row_seq = d_rs;
+  int rc = 0;
+  for (void *b : bufs)
+    if (!b) rc = fail(IG_ERR_CUDA, "cudaMalloc failed");
+  if (!rc) {
+    cudaMemcpyAsync(d_offs, p.offs.data(), 4 * (nseq + 1), cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(d_rs, p.row_seq.data(), 4 * N, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(d_blk, p.blocks.data(), sizeof(int2) * p.nblocks, cudaMemcpyHostToDevice, st);
+    rc = launch_attention(a, st);
+    if (!rc) rc = launch_attend(a, d_blk, p.nblocks, st);
+    if (rc) fail(rc, "ig_attention launch failed");
+  }
+  cudaStreamSynchronize(st);
+  for (void *b : bufs) cudaFree(b);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,108 @@
+// Float32 functions of the reference's int8 path, evaluated with explicit
+// IEEE roundings (every multiply, add and fused multiply-add is spelled out),
+// so the device produces the reference's bits, not CUDA's libm results:
+//   exp: Cephes expf as linalg/vec_simd.go:216-264 (vector body, FMA) and
+//        linalg/fastmath.go:35-51 (scalar tail, no FMA);
+//   GELU(erf) x gate: the Eigen/XLA erf rational of linalg/fastmath.go:7-26,
+//        in the FMA order of linalg/gelu_amd64.s:165-225.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ig {
+
+// Vector-body exp of v = x - m (ExpShift, vec_simd.go:235-248).
+__device__ __forceinline__ float exp_body(float v) {
+  const bool under = v < -87.3f;
+  v = fminf(fmaxf(v, -87.3f), 88.7f);
+  float n = __fsub_rn(__fmaf_rn(v, 1.44269504088896341f, 12582912.0f), 12582912.0f);
+  float r = __fmaf_rn(n, -0.693359375f, v);
+  r = __fmaf_rn(n, 2.12194440e-4f, r);
+  float p = __fmaf_rn(r, 1.9875691500e-4f, 1.3981999507e-3f);
+  p = __fmaf_rn(r, p, 8.3334519073e-3f);
+  p = __fmaf_rn(r, p, 4.1665795894e-2f);
+  p = __fmaf_rn(r, p, 1.6666665459e-1f);
+  p = __fmaf_rn(r, p, 5.0000001201e-1f);
+  float y = __fadd_rn(__fmaf_rn(__fmul_rn(p, r), r, r), 1.0f);
+  const int ni = __float2int_rn(n);
+  const float pw = __int_as_float((ni + 127) << 23);
+  return under ? 0.0f : __fmul_rn(y, pw);
+}
+
+// Scalar-tail exp (exp32, fastmath.go:35-51): separate roundings throughout.
+__device__ __forceinline__ float exp_tail(float x) {
+  if (x < -87.3f) return 0.0f;
+  x = fminf(x, 88.7f);
+  float n = __fsub_rn(__fadd_rn(__fmul_rn(x, 1.44269504088896341f), 12582912.0f), 12582912.0f);
+  float r = __fsub_rn(x, __fmul_rn(n, 0.693359375f));
+  r = __fsub_rn(r, __fmul_rn(n, -2.12194440e-4f));
+  float p = 1.9875691500e-4f;
+  p = __fadd_rn(__fmul_rn(p, r), 1.3981999507e-3f);
+  p = __fadd_rn(__fmul_rn(p, r), 8.3334519073e-3f);
+  p = __fadd_rn(__fmul_rn(p, r), 4.1665795894e-2f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.6666665459e-1f);
+  p = __fadd_rn(__fmul_rn(p, r), 5.0000001201e-1f);
+  float y = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(p, r), r), r), 1.0f);
+  const int ni = __float2int_rn(n);
+  return __fmul_rn(y, __int_as_float((ni + 127) << 23));
+}
+
+// Element t of an ExpShift over `len` values with V lanes: the vector body
+// covers t < (len / V) * V, exp32 the rest.
+__device__ __forceinline__ float exp_shift_at(float x, float m, int t, int len, int V) {
+  const float v = __fsub_rn(x, m);
+  return t < (len / V) * V ? exp_body(v) : exp_tail(v);
+}
+
+// geluMulAVX2 for one element (gelu_amd64.s:176-200).
+__device__ __forceinline__ float gelu_mul_fma(float x, float gate) {
+  float t = __fmul_rn(x, 0.7071067811865476f);
+  t = fmaxf(t, -4.0f);
+  t = fminf(t, 4.0f);
+  const float t2 = __fmul_rn(t, t);
+  float p = __fmaf_rn(t2, -2.72614225801306e-10f, 2.77068142495902e-08f);
+  p = __fmaf_rn(t2, p, -2.10102402082508e-06f);
+  p = __fmaf_rn(t2, p, -5.69250639462346e-05f);
+  p = __fmaf_rn(t2, p, -7.34990630326855e-04f);
+  p = __fmaf_rn(t2, p, -2.95459980854025e-03f);
+  p = __fmaf_rn(t2, p, -1.60960333262415e-02f);
+  p = __fmul_rn(p, t);
+  float q = __fmaf_rn(t2, -1.45660718464996e-05f, -2.13374055278905e-04f);
+  q = __fmaf_rn(t2, q, -1.68282697438203e-03f);
+  q = __fmaf_rn(t2, q, -7.37332916720468e-03f);
+  q = __fmaf_rn(t2, q, -1.42647390514189e-02f);
+  float r = __fdiv_rn(p, q);
+  r = __fadd_rn(r, 1.0f);
+  const float g = __fmul_rn(r, __fmul_rn(x, 0.5f));
+  return __fmul_rn(g, gate);
+}
+
+// geluScalar(x) * gate (fastmath.go:9-26): the tail of GeluMul when the row
+// length is not a multiple of 16.
+__device__ __forceinline__ float gelu_mul_scalar(float x, float gate) {
+  float e = __fmul_rn(x, 0.7071067811865476f);
+  e = fminf(fmaxf(e, -4.0f), 4.0f);
+  const float x2 = __fmul_rn(e, e);
+  float p = __fadd_rn(__fmul_rn(x2, -2.72614225801306e-10f), 2.77068142495902e-08f);
+  p = __fadd_rn(__fmul_rn(x2, p), -2.10102402082508e-06f);
+  p = __fadd_rn(__fmul_rn(x2, p), -5.69250639462346e-05f);
+  p = __fadd_rn(__fmul_rn(x2, p), -7.34990630326855e-04f);
+  p = __fadd_rn(__fmul_rn(x2, p), -2.95459980854025e-03f);
+  p = __fadd_rn(__fmul_rn(x2, p), -1.60960333262415e-02f);
+  p = __fmul_rn(p, e);
+  float q = __fadd_rn(__fmul_rn(x2, -1.45660718464996e-05f), -2.13374055278905e-04f);
+  q = __fadd_rn(__fmul_rn(x2, q), -1.68282697438203e-03f);
+  q = __fadd_rn(__fmul_rn(x2, q), -7.37332916720468e-03f);
+  q = __fadd_rn(__fmul_rn(x2, q), -1.42647390514189e-02f);
+  const float erf = __fdiv_rn(p, q);
+  const float g = __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erf));
+  return __fmul_rn(g, gate);
+}
+
+// GeluMul element i of a row of n values (vec_simd.go:121-160 on amd64:
+// the first n &^ 15 go through the AVX2 kernel).
+__device__ __forceinline__ float gelu_mul_at(float x, float gate, int i, int n) {
+  return i < (n & ~15) ? gelu_mul_fma(x, gate) : gelu_mul_scalar(x, gate);
+}
+
+}  // namespace ig

@@ -1,0 +1,89 @@
+// Declarations shared by the CUDA translation units of libindecis_b200.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/indecis_b200.h"
+
+namespace ig {
+
+enum Epilogue : int { kEpiF32 = 0, kEpiI32 = 1, kEpiRope = 2, kEpiGeglu = 3 };
+
+struct GemmArgs {
+  const uint8_t *A;  // [M][lda] uint8 activations (q + 128)
+  const int8_t *B;   // [N][ldb] int8 weights, output channel rows
+  int M, N, K;
+  int lda, ldb;      // row strides in bytes, multiples of 16
+  int bn;            // 128 or 256 (0: choose)
+};
+
+struct GemmEpilogue {
+  const float *sa;  // [M] row scales
+  const float *sb;  // [N] column scales
+  const float *zc;  // [N] 128 * column sums
+  float *C;         // f32 output, row stride ldc (elements)
+  int32_t *acc_out; // int32 output (kEpiI32)
+  int ldc;
+  int accumulate;   // C = dequant + C
+  // kEpiRope
+  const int32_t *pos;
+  const float *rope_cos, *rope_sin;  // [positions][32]
+  int rope_cols;
+  // kEpiGeglu
+  int geglu_n;  // GeGLU output width (intermediate size)
+};
+
+int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t st);
+
+// ---- row kernels (rows.cu) ----
+// x (f32 [M][H]) -> LayerNorm (gamma) -> optional xn out -> per-row quantized
+// uint8 q [M][ldq] + sa. gamma == nullptr: no norm, quantize x itself.
+int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps, int V, float *xn, uint8_t *q,
+                    int ldq, float *sa, cudaStream_t st);
+// Embedding gather then LayerNorm: x = LN(emb[ids]) (f32), and its quantized copy.
+int launch_embed_checked(const int32_t *ids, int vocab, const float *emb, const float *gamma, int M, int H,
+                         double eps, int V, float *x, uint8_t *q, int ldq, float *sa, cudaStream_t st);
+// Per-row quantization of f32 rows (ld elements apart).
+int launch_quant_rows(const float *x, int ldx, int M, int K, uint8_t *q, int ldq, float *sa, cudaStream_t st);
+// Mean (float64, token order) or first-token pooling.
+int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, float *out, cudaStream_t st);
+// Head logits in float64: z[t][r] = sum_i w[r][i] x[t][i] + b[r] (heads.go:62-74).
+int launch_head_logits(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z,
+                       int ldz, cudaStream_t st);
+// Weight quantization per output channel (PackB8, linalg/int8.go:36-77):
+// w f32 [n][k] -> q int8 [n][ldq], scale, zc. Rows of `perm` (optional)
+// choose the source channel of each packed row (-1: zero row).
+int launch_pack_b8(const float *w, int n, int k, const int32_t *perm, int n_out, int8_t *q, int ldq, float *scale,
+                   float *zc, int32_t *colsum, cudaStream_t st);
+
+// ---- attention (attention.cu) ----
+struct AttnArgs {
+  const float *qkv;     // [N][3H] rows after RoPE
+  int H, nh, D;
+  const int32_t *offs;  // [nseq+1] row offsets (device)
+  int nseq;
+  int max_len;          // longest sequence
+  int window;           // half window, < 0: global
+  float scale;          // 1/sqrt(D)
+  int V;                // lanes of ExpShift
+  // work buffers (device)
+  uint8_t *qa;          // [nh][N][D]
+  float *sq;            // [nh][N]
+  int8_t *kq;           // [nh][N][D]
+  float *ks, *kzc;      // [nh][N]
+  int8_t *vq;           // [nh][N][D]
+  float *kmean;         // [nseq][nh][D]
+  float *vs, *vinv;     // [nseq][nh][D]
+  const int32_t *row_seq;  // [N] sequence of each row
+  int N;
+  float *ctx;           // [N][H] output
+  // optional int32 dumps (parity): none in the hot path
+};
+int launch_attention(const AttnArgs &a, cudaStream_t st);
+int launch_attend(const AttnArgs &a, const int2 *d_blocks, int nblocks, cudaStream_t st);
+int attn_query_block();
+
+// Device error flag (kernels' bounded waits).
+int read_device_error(int reset);
+
+}  // namespace ig

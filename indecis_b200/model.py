@@ -1,0 +1,390 @@
+"""Host-side mirror of indecis' int8 ModernBERT inference API over the C ABI.
+
+Names, argument meanings and errors follow the Go reference:
+  internal/modernbert/model.go   Config, FromTensors, validate
+  internal/modernbert/infer.go   SetInt8, Encode, EncodeSeqs, EncodeTokens, run
+  heads.go                       head.logits / head.answer (noul, choice, score, spans)
+The computation runs in libindecis_b200.so on an sm_100 GPU; nothing here
+computes the encoder on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _capi
+
+
+class ModernBertError(ValueError):
+    """An error the reference returns as a Go `error` (same wording)."""
+
+
+@dataclass
+class Config:
+    """modernbert.Config (internal/modernbert/model.go:25-49)."""
+    hidden_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    intermediate_size: int
+    vocab_size: int
+    norm_eps: float = 1e-5
+    global_attn_every_n_layers: int = 3
+    local_attention: int = 128
+    global_rope_theta: float = 10000.0
+    local_rope_theta: float = 10000.0
+    pad_token_id: int = 0
+    hidden_activation: str = "gelu"
+    classifier_pooling: str = "mean"
+    attention_bias: bool = False
+    mlp_bias: bool = False
+    norm_bias: bool = False
+    simd_lanes: int = 8
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "Config":
+        """From the synthetic-shape dicts (indecis_b200.synthetic) or a config.json."""
+        if "hidden" in d:
+            return cls(hidden_size=d["hidden"], num_hidden_layers=d["layers"], num_attention_heads=d["heads"],
+                       intermediate_size=d["intermediate"], vocab_size=d["vocab"], norm_eps=d["norm_eps"],
+                       global_attn_every_n_layers=d["global_every"], local_attention=d["local_attention"],
+                       global_rope_theta=d["global_theta"], local_rope_theta=d["local_theta"],
+                       classifier_pooling=d.get("pooling", "mean"), simd_lanes=d.get("V", 8))
+        keys = {f for f in cls.__dataclass_fields__}
+        return cls(**{k: v for k, v in d.items() if k in keys})
+
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_attention_heads
+
+    def is_global(self, l: int) -> bool:
+        return l % self.global_attn_every_n_layers == 0
+
+    def window(self) -> int:
+        return self.local_attention // 2
+
+    def cls(self) -> bool:
+        return self.classifier_pooling == "cls"
+
+    def validate(self):
+        """Config.validate (model.go:64-80), same messages."""
+        if (self.hidden_size <= 0 or self.num_hidden_layers <= 0 or self.num_attention_heads <= 0
+                or self.intermediate_size <= 0 or self.vocab_size <= 0):
+            raise ModernBertError("modernbert: invalid dimensions")
+        if self.hidden_size % self.num_attention_heads != 0 or self.head_dim() % 2 != 0:
+            raise ModernBertError(f"modernbert: hidden_size {self.hidden_size} incompatible with "
+                                  f"{self.num_attention_heads} heads")
+        if self.global_attn_every_n_layers <= 0 or self.local_attention <= 0:
+            raise ModernBertError("modernbert: invalid attention windows")
+        if self.hidden_activation != "gelu":
+            raise ModernBertError(f"modernbert: activation {self.hidden_activation!r} not supported")
+        if self.attention_bias or self.mlp_bias or self.norm_bias:
+            raise ModernBertError("modernbert: biases are not supported")
+        if self.classifier_pooling not in ("", "mean", "cls"):
+            raise ModernBertError(f"modernbert: pooling {self.classifier_pooling!r} not supported")
+
+    def to_c(self) -> _capi.IgConfig:
+        return _capi.IgConfig(vocab=self.vocab_size, hidden=self.hidden_size, layers=self.num_hidden_layers,
+                              heads=self.num_attention_heads, intermediate=self.intermediate_size,
+                              global_every=self.global_attn_every_n_layers, local_attention=self.local_attention,
+                              pooling=1 if self.cls() else 0, norm_eps=self.norm_eps,
+                              global_theta=self.global_rope_theta, local_theta=self.local_rope_theta,
+                              simd_lanes=self.simd_lanes)
+
+
+@dataclass
+class Batch:
+    """modernbert.Batch (internal/modernbert/forward.go:10-15): right-padded."""
+    IDs: np.ndarray
+    Lens: list
+    T: int
+
+    def B(self) -> int:
+        return len(self.Lens)
+
+
+def new_batch(seqs, pad: int = 0) -> Batch:
+    """NewBatch (forward.go:17-30)."""
+    T = max((len(s) for s in seqs), default=0)
+    ids = np.full(len(seqs) * T, pad, np.int32)
+    for i, s in enumerate(seqs):
+        ids[i * T:i * T + len(s)] = s
+    return Batch(ids, [len(s) for s in seqs], T)
+
+
+def _concat(seqs):
+    """seqs -> (ids int32 [N], offs int64 [B+1]) as run() lays them out (infer.go:307-315)."""
+    if isinstance(seqs, tuple) and len(seqs) == 2 and isinstance(seqs[1], np.ndarray):
+        ids, offs = seqs
+        return np.ascontiguousarray(ids, np.int32), np.ascontiguousarray(offs, np.int64)
+    lens = [len(s) for s in seqs]
+    offs = np.zeros(len(seqs) + 1, np.int64)
+    offs[1:] = np.cumsum(lens)
+    ids = np.concatenate([np.asarray(s, np.int64) for s in seqs]) if seqs and offs[-1] else np.zeros(0, np.int64)
+    if ids.size and (ids.min() < -2**31 or ids.max() >= 2**31):
+        bad = int(ids[(ids < -2**31) | (ids >= 2**31)][0])
+        raise ModernBertError(f"modernbert: id {bad} out of vocabulary")
+    return np.ascontiguousarray(ids, np.int32), offs
+
+
+_TENSOR_NAMES = {
+    "emb": "embeddings.tok_embeddings.weight", "emb_norm": "embeddings.norm.weight",
+    "final_norm": "final_norm.weight",
+}
+
+
+class Model:
+    """modernbert.Model restricted to int8 inference on one GPU."""
+
+    def __init__(self, cfg: Config, handle, device: int):
+        self.Cfg = cfg
+        self._h = handle
+        self.device = device
+        self._int8 = True
+        self.heads: list[Head] = []
+
+    # ---- construction (model.go:179-234) ----
+    @classmethod
+    def FromTensors(cls, cfg: Config, tensors: dict, device: int = 0) -> "Model":
+        """Assembles a model from tensors named as in transformers (the "model."
+        prefix is accepted) and uploads it; quantization happens on the device."""
+        cfg.validate()
+        H, I, V, L = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size, cfg.num_hidden_layers
+
+        def get(name, *shape):
+            t = tensors.get(name)
+            if t is None:
+                t = tensors.get("model." + name)
+            if t is None:
+                raise ModernBertError(f"modernbert: tensor {name} missing")
+            t = np.ascontiguousarray(t, np.float32)
+            if list(t.shape) != list(shape):
+                raise ModernBertError(f"modernbert: {name}: shape {list(t.shape)}, expected {list(shape)}")
+            return t
+
+        keep = [get("embeddings.tok_embeddings.weight", V, H), get("embeddings.norm.weight", H),
+                get("final_norm.weight", H)]
+        per = {k: [] for k in ("attn_norm", "wqkv", "wo", "mlp_norm", "wi", "wo_mlp")}
+        for l in range(L):
+            p = f"layers.{l}."
+            per["attn_norm"].append(get(p + "attn_norm.weight", H) if l > 0 else None)
+            per["wqkv"].append(get(p + "attn.Wqkv.weight", 3 * H, H))
+            per["wo"].append(get(p + "attn.Wo.weight", H, H))
+            per["mlp_norm"].append(get(p + "mlp_norm.weight", H))
+            per["wi"].append(get(p + "mlp.Wi.weight", 2 * I, H))
+            per["wo_mlp"].append(get(p + "mlp.Wo.weight", H, I))
+        return cls._create(cfg, keep, per, device)
+
+    @classmethod
+    def from_arrays(cls, cfg: Config, w: dict, device: int = 0) -> "Model":
+        """From the layout of indecis_b200.synthetic.weights (same arrays, short keys)."""
+        tensors = {_TENSOR_NAMES[k]: w[k] for k in ("emb", "emb_norm", "final_norm")}
+        for l in range(cfg.num_hidden_layers):
+            p = f"layers.{l}."
+            if l > 0:
+                tensors[p + "attn_norm.weight"] = w["attn_norm"][l]
+            tensors[p + "attn.Wqkv.weight"] = w["wqkv"][l]
+            tensors[p + "attn.Wo.weight"] = w["wo"][l]
+            tensors[p + "mlp_norm.weight"] = w["mlp_norm"][l]
+            tensors[p + "mlp.Wi.weight"] = w["wi"][l]
+            tensors[p + "mlp.Wo.weight"] = w["wo_mlp"][l]
+        return cls.FromTensors(cfg, tensors, device)
+
+    @classmethod
+    def _create(cls, cfg, keep, per, device):
+        L = cfg.num_hidden_layers
+        lib = _capi.load()
+
+        def ptrs(name):
+            arr = (C.c_void_p * L)(*[0 if a is None else a.ctypes.data for a in per[name]])
+            return C.cast(arr, C.POINTER(C.c_void_p)), arr
+
+        hold = {}
+        fields = {}
+        for name in per:
+            fields[name], hold[name] = ptrs(name)
+        w = _capi.IgWeights(tok_embeddings=keep[0].ctypes.data, emb_norm=keep[1].ctypes.data,
+                            final_norm=keep[2].ctypes.data, **fields)
+        c = cfg.to_c()
+        h = C.c_void_p()
+        _capi.check(lib.ig_model_create(C.byref(c), C.byref(w), device, C.byref(h)))
+        return cls(cfg, h, device)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _capi.load().ig_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- switches (infer.go:115-135) ----
+    def SetInt8(self, on: bool):
+        if not on:
+            raise ModernBertError("modernbert: the device path computes in int8 only (SetInt8(false) is not available)")
+        self._int8 = True
+
+    # ---- inference (infer.go:237-299) ----
+    def _run(self, seqs, mode):
+        ids, offs = _concat(seqs)
+        nseq = len(offs) - 1
+        H = self.Cfg.hidden_size
+        rows = nseq if mode == _capi.IG_MODE_POOLED else int(offs[-1])
+        out = np.zeros((rows, H), np.float32)
+        rc = _capi.load().ig_encode(self._h, ids.ctypes.data, offs.ctypes.data, nseq, mode, out.ctypes.data,
+                                    out.size)
+        if rc == _capi.IG_ERR_OUT_OF_VOCAB:
+            raise ModernBertError(_capi.last_error())
+        _capi.check(rc)
+        return out
+
+    def EncodeSeqs(self, seqs) -> np.ndarray:
+        """Pooled embedding [B, H] of unpadded sequences (infer.go:255-289)."""
+        return self._run(seqs, _capi.IG_MODE_POOLED)
+
+    def EncodeTokens(self, seqs) -> np.ndarray:
+        """Final state of every token, laid end to end [sum of lengths, H] (infer.go:291-299)."""
+        return self._run(seqs, _capi.IG_MODE_TOKENS)
+
+    def Encode(self, b: Batch) -> np.ndarray:
+        """Pooled embedding of a padded batch (infer.go:237-253)."""
+        if len(b.IDs) != b.B() * b.T:
+            raise ModernBertError("modernbert: inconsistent batch")
+        return self.EncodeSeqs([b.IDs[i * b.T:i * b.T + n] for i, n in enumerate(b.Lens)])
+
+    def encode_dump(self, seqs, layer: int, mode=_capi.IG_MODE_POOLED):
+        """EncodeSeqs plus the intermediates of one layer (parity tests)."""
+        ids, offs = _concat(seqs)
+        nseq = len(offs) - 1
+        N = int(offs[-1])
+        H, I = self.Cfg.hidden_size, self.Cfg.intermediate_size
+        arr = dict(xq=np.zeros((N, H), np.uint8), xq_s=np.zeros(N, np.float32), qkv=np.zeros((N, 3 * H), np.float32),
+                   ctx=np.zeros((N, H), np.float32), cq=np.zeros((N, H), np.uint8), cq_s=np.zeros(N, np.float32),
+                   x_attn=np.zeros((N, H), np.float32), hq=np.zeros((N, H), np.uint8), hq_s=np.zeros(N, np.float32),
+                   g=np.zeros((N, I), np.float32), gq=np.zeros((N, I), np.uint8), gq_s=np.zeros(N, np.float32),
+                   x_mlp=np.zeros((N, H), np.float32), emb_ln=np.zeros((N, H), np.float32))
+        d = _capi.IgDump(layer=layer, **{k: v.ctypes.data for k, v in arr.items()})
+        rows = nseq if mode == _capi.IG_MODE_POOLED else N
+        out = np.zeros((rows, H), np.float32)
+        _capi.check(_capi.load().ig_encode_dump(self._h, ids.ctypes.data, offs.ctypes.data, nseq, mode,
+                                                out.ctypes.data, out.size, C.byref(d)))
+        return out, arr
+
+    # ---- heads (heads.go) ----
+    def SetHeads(self, heads: list["Head"]):
+        hs = (_capi.IgHead * len(heads))()
+        for i, h in enumerate(heads):
+            hs[i] = _capi.IgHead(rows=h.rows, per_token=1 if h.kind == "spans" else 0, w=h.w.ctypes.data,
+                                 b=h.b.ctypes.data)
+        _capi.check(_capi.load().ig_model_set_heads(self._h, len(heads), hs))
+        self.heads = list(heads)
+
+    def Logits(self, seqs):
+        """float64 logits of every pooled head per sequence, and of every span head per token."""
+        ids, offs = _concat(seqs)
+        nseq = len(offs) - 1
+        N = int(offs[-1])
+        pr = sum(h.rows for h in self.heads if h.kind != "spans")
+        tr = sum(h.rows for h in self.heads if h.kind == "spans")
+        z = np.zeros((nseq, pr), np.float64)
+        zt = np.zeros((N, tr), np.float64) if tr else None
+        rc = _capi.load().ig_logits(self._h, ids.ctypes.data, offs.ctypes.data, nseq, z.ctypes.data, z.size,
+                                    zt.ctypes.data if zt is not None else None, zt.size if zt is not None else 0)
+        if rc == _capi.IG_ERR_OUT_OF_VOCAB:
+            raise ModernBertError(_capi.last_error())
+        _capi.check(rc)
+        out, po, to = [], 0, 0
+        for h in self.heads:
+            if h.kind == "spans":
+                out.append(zt[:, to:to + h.rows])
+                to += h.rows
+            else:
+                out.append(z[:, po:po + h.rows])
+                po += h.rows
+        return out, offs
+
+
+# ---- decision heads: answers from logits (heads.go:124-237) ----
+
+def sigmoid(z: float) -> float:
+    if z >= 0:
+        return 1 / (1 + math.exp(-z))
+    e = math.exp(z)
+    return e / (1 + e)
+
+
+def softmax(z):
+    mx = max(z)
+    p = [math.exp(v - mx) for v in z]
+    s = 0.0
+    for v in p:
+        s += v
+    return [v / s for v in p]
+
+
+def margin(p, best):
+    if len(p) < 2:
+        return p[best]
+    others = 0.0
+    for i, v in enumerate(p):
+        if i != best:
+            others += v
+    return p[best] - others / (len(p) - 1)
+
+
+@dataclass
+class Head:
+    """A question's output layer (heads.go:19-27)."""
+    name: str
+    kind: str  # noul | choice | score | spans
+    w: np.ndarray
+    b: np.ndarray
+    options: list = field(default_factory=list)
+
+    @property
+    def rows(self) -> int:
+        return self.w.shape[0]
+
+    def answer(self, z, temperature: float = 1.0) -> dict:
+        """head.answer (heads.go:124-187)."""
+        if temperature <= 0:
+            temperature = 1
+        zt = [float(v) / temperature for v in z]
+        a = dict(question=self.name, kind=self.kind)
+        opts = self.options or [str(i) for i in range(len(zt) + (1 if self.kind == "score" else 0))]
+        if self.kind == "noul":
+            a["P"] = sigmoid(zt[0])
+            a["Confidence"] = max(a["P"], 1 - a["P"])
+        elif self.kind == "choice":
+            p = softmax(zt)
+            best = 0
+            for i, v in enumerate(p):
+                if v > p[best]:
+                    best = i
+            a["Probs"] = {opts[i]: v for i, v in enumerate(p)}
+            a["Choice"], a["Confidence"], a["Margin"] = opts[best], p[best], margin(p, best)
+        elif self.kind == "score":
+            gt = []
+            for k, v in enumerate(zt):
+                g = sigmoid(v)
+                if k > 0:
+                    g = min(g, gt[k - 1])
+                gt.append(g)
+            levels = len(opts)
+            dist = []
+            for k in range(levels):
+                above = 1.0 if k == 0 else gt[k - 1]
+                below = gt[k] if k < len(gt) else 0.0
+                dist.append(above - below)
+            best, score = 0, 0.0
+            for k, v in enumerate(dist):
+                score += k * v
+                if v > dist[best]:
+                    best = k
+            a["Probs"] = {opts[k]: v for k, v in enumerate(dist)}
+            a["Score"], a["Choice"], a["Confidence"] = score, opts[best], dist[best]
+        return a

@@ -1,0 +1,283 @@
+// CPU oracle (test infrastructure): the int8 encoder forward of
+// internal/modernbert/infer.go:304-430 (run) and its pooling (:261-289),
+// assembled from the elementary restatements in oracle.cpp. With threads > 1
+// or fast != 0 it is also the CPU baseline bench.py times: the same
+// arithmetic, rows sliced over threads as linalg/parallel.go:38-72 does and
+// the integer products on AVX-VNNI (cpu_baseline.cpp).
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "oracle.h"
+#include "oracle_internal.h"
+
+using namespace orc;
+
+struct PackedMat {
+  int k = 0, n = 0;
+  std::vector<int8_t> q;       // [n][k]
+  std::vector<int8_t> panels;  // [n/16][k/4][16][4] for the fast GEMM
+  std::vector<float> scale, zc;
+  std::vector<int32_t> colsum;
+};
+
+struct or_model {
+  or_config cfg;
+  std::vector<float> emb, emb_norm, final_norm;
+  std::vector<std::vector<float>> attn_norm, mlp_norm;
+  std::vector<PackedMat> qkv, o, wi, womlp;
+};
+
+static void pack(PackedMat &p, const float *w, int k, int n) {
+  p.k = k;
+  p.n = n;
+  p.q.resize((size_t)n * k);
+  p.scale.resize(n);
+  p.zc.resize(n);
+  p.colsum.resize(n);
+  pack_b8(w, k, n, true, p.q.data(), p.scale.data(), p.colsum.data(), p.zc.data());
+  pack_panels(p.q.data(), n, k, p.panels);
+}
+
+// linalg/parallel.go:38-72 ParallelN: about four slices per worker, each a
+// multiple of grain, taken with an atomic counter.
+template <class F>
+static void parallel_n(int workers, int n, int grain, F fn) {
+  if (n <= 0) return;
+  grain = std::max(1, grain);
+  if (workers <= 1 || n <= grain) {
+    fn(0, n);
+    return;
+  }
+  int step = ((n + 4 * workers - 1) / (4 * workers) + grain - 1) / grain * grain;
+  workers = std::min(workers, (n + step - 1) / step);
+  std::atomic<int> next(0);
+  auto run = [&]() {
+    for (;;) {
+      int lo = next.fetch_add(1) * step;
+      if (lo >= n) return;
+      fn(lo, std::min(lo + step, n));
+    }
+  };
+  std::vector<std::thread> ts;
+  for (int w = 1; w < workers; w++) ts.emplace_back(run);
+  run();
+  for (auto &t : ts) t.join();
+}
+
+// One MatMul8N call on rows [lo, hi): c (+)= dequant(quant(a) . W^T).
+struct GemmScratch {
+  std::vector<uint8_t> aq;
+  std::vector<float> sa;
+  std::vector<int32_t> acc;
+};
+
+static void matmul_rows(const PackedMat &W, const float *a, float *c, int rows, bool accumulate, bool fast,
+                        GemmScratch &s, uint8_t *aq_dump, float *sa_dump, int32_t *acc_dump) {
+  const int k = W.k, n = W.n;
+  const int kp = (k + 3) / 4 * 4;
+  const int rp = (rows + 5) / 6 * 6;
+  s.aq.assign((size_t)rp * kp, 128);
+  s.sa.assign(rp, 0.0f);
+  s.acc.resize((size_t)rows * n);
+  for (int i = 0; i < rows; i++) quantize_a_row(a + (size_t)i * k, k, s.aq.data() + (size_t)i * kp, &s.sa[i]);
+  if (fast)
+    gemm_u8s8_fast(s.aq.data(), W.panels.data(), rp, n, kp, 0, rows, s.acc.data());
+  else
+    gemm_u8s8(s.aq.data(), kp, W.q.data(), k, rows, n, k, s.acc.data());
+  dequant(s.acc.data(), rows, n, s.sa.data(), W.scale.data(), W.zc.data(), c, accumulate);
+  if (aq_dump)
+    for (int i = 0; i < rows; i++) std::memcpy(aq_dump + (size_t)i * k, s.aq.data() + (size_t)i * kp, k);
+  if (sa_dump) std::memcpy(sa_dump, s.sa.data(), sizeof(float) * rows);
+  if (acc_dump) std::memcpy(acc_dump, s.acc.data(), sizeof(int32_t) * rows * n);
+}
+
+extern "C" {
+
+or_model *or_model_create(const or_config *cfg, const or_weights *w) {
+  auto *m = new or_model();
+  m->cfg = *cfg;
+  const int H = cfg->hidden, I = cfg->intermediate, L = cfg->layers, V = cfg->vocab;
+  m->emb.assign(w->emb, w->emb + (size_t)V * H);
+  m->emb_norm.assign(w->emb_norm, w->emb_norm + H);
+  m->final_norm.assign(w->final_norm, w->final_norm + H);
+  m->attn_norm.resize(L);
+  m->mlp_norm.resize(L);
+  m->qkv.resize(L);
+  m->o.resize(L);
+  m->wi.resize(L);
+  m->womlp.resize(L);
+  for (int l = 0; l < L; l++) {
+    if (l > 0) m->attn_norm[l].assign(w->attn_norm[l], w->attn_norm[l] + H);
+    m->mlp_norm[l].assign(w->mlp_norm[l], w->mlp_norm[l] + H);
+    pack(m->qkv[l], w->wqkv[l], H, 3 * H);
+    pack(m->o[l], w->wo[l], H, H);
+    pack(m->wi[l], w->wi[l], H, 2 * I);
+    pack(m->womlp[l], w->wo_mlp[l], I, H);
+  }
+  return m;
+}
+
+void or_model_destroy(or_model *m) { delete m; }
+
+void or_model_packed(const or_model *m, int l, int which, const int8_t **q, const float **scale, const float **zc,
+                     int *k, int *n) {
+  const PackedMat *p = which == 0 ? &m->qkv[l] : which == 1 ? &m->o[l] : which == 2 ? &m->wi[l] : &m->womlp[l];
+  *q = p->q.data();
+  *scale = p->scale.data();
+  *zc = p->zc.data();
+  *k = p->k;
+  *n = p->n;
+}
+
+int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int nseq, int mode, float *out,
+              int threads, int fast, or_dump *dump, int32_t *bad_id) {
+  const or_config &cfg = m->cfg;
+  const int H = cfg.hidden, I = cfg.intermediate, nh = cfg.heads, D = H / nh, half = D / 2, VL = cfg.V;
+  const int64_t N = offs[nseq];
+  // infer.go:307-315: every id in [0, vocab).
+  for (int64_t t = 0; t < N; t++)
+    if (ids[t] < 0 || ids[t] >= cfg.vocab) {
+      if (bad_id) *bad_id = ids[t];
+      return 1;
+    }
+  if (mode == 0) std::memset(out, 0, sizeof(float) * (size_t)nseq * H);
+  if (N == 0) return 0;
+  const bool use_fast = fast != 0 || threads > 1;
+  const int workers = std::max(1, threads);
+  std::vector<float> x((size_t)N * H), xn((size_t)N * H), qkv((size_t)N * 3 * H), ctx((size_t)N * H);
+  std::vector<int32_t> pos(N);
+  int T = 0;
+  for (int i = 0; i < nseq; i++) {
+    T = std::max<int>(T, (int)(offs[i + 1] - offs[i]));
+    for (int64_t t = offs[i]; t < offs[i + 1]; t++) pos[t] = (int32_t)(t - offs[i]);
+  }
+  for (int64_t r = 0; r < N; r++) std::memcpy(&xn[r * H], &m->emb[(size_t)ids[r] * H], sizeof(float) * H);
+  for (int64_t r = 0; r < N; r++) layernorm_row(&x[r * H], &xn[r * H], m->emb_norm.data(), H, cfg.norm_eps, VL);
+  if (dump && dump->emb_ln) std::memcpy(dump->emb_ln, x.data(), sizeof(float) * N * H);
+
+  // infer.go:570-572 sliceRows.
+  const int slice = std::min(24, std::max(6, (int)((N / 8 + 3) / 6 * 6)));
+  const int npos = std::max(T, 512);
+  std::vector<float> rc((size_t)npos * half), rs((size_t)npos * half);
+  double theta_cached = -1;
+
+  for (int l = 0; l < cfg.layers; l++) {
+    const bool global = l % cfg.global_every == 0;
+    const double theta = global ? cfg.global_theta : cfg.local_theta;
+    if (theta != theta_cached) {
+      rope_table(theta, D, npos, rc.data(), rs.data());
+      theta_cached = theta;
+    }
+    const bool dl = dump && dump->layer == l;
+    // Norm, QKV projection, RoPE (infer.go:382-400).
+    parallel_n(workers, (int)N, slice, [&](int lo, int hi) {
+      GemmScratch s;
+      const float *in = &x[(size_t)lo * H];
+      if (l > 0) {
+        for (int r = lo; r < hi; r++)
+          layernorm_row(&xn[(size_t)r * H], &x[(size_t)r * H], m->attn_norm[l].data(), H, cfg.norm_eps, VL);
+        in = &xn[(size_t)lo * H];
+      }
+      matmul_rows(m->qkv[l], in, &qkv[(size_t)lo * 3 * H], hi - lo, false, use_fast, s,
+                  dl && dump->xq ? dump->xq + (size_t)lo * H : nullptr, dl && dump->xq_s ? dump->xq_s + lo : nullptr,
+                  dl && dump->qkv_acc ? dump->qkv_acc + (size_t)lo * 3 * H : nullptr);
+      for (int r = lo; r < hi; r++) {
+        const int t = pos[r];
+        float *row = &qkv[(size_t)r * 3 * H];
+        for (int h = 0; h < 2 * nh; h++) rope(row + h * D, &rc[(size_t)t * half], &rs[(size_t)t * half], half);
+      }
+    });
+    if (dl && dump->qkv) std::memcpy(dump->qkv, qkv.data(), sizeof(float) * N * 3 * H);
+
+    // attention8 (infer.go:484-518): prepare per (sequence, head), attend per
+    // block of queries.
+    const int window = global ? -1 : cfg.local_attention / 2;
+    const float scale = (float)(1.0 / std::sqrt((double)D));
+    std::vector<AttnPrep> prep((size_t)nseq * nh);
+    parallel_n(workers, nseq * nh, 1, [&](int lo, int hi) {
+      for (int task = lo; task < hi; task++) {
+        const int bi = task / nh, h = task % nh;
+        const int64_t off = offs[bi];
+        const int n = (int)(offs[bi + 1] - off);
+        if (n == 0) continue;
+        const float *rows = &qkv[(size_t)off * 3 * H];
+        attn_prepare(rows + h * D, rows + H + h * D, rows + 2 * H + h * D, 3 * H, n, D, scale, prep[task]);
+      }
+    });
+    struct Blk {
+      int task, i0;
+    };
+    std::vector<Blk> blocks;
+    const int AttnBlock = 48;
+    for (int bi = 0; bi < nseq; bi++)
+      for (int h = 0; h < nh; h++)
+        for (int i0 = 0; i0 < offs[bi + 1] - offs[bi]; i0 += AttnBlock) blocks.push_back({bi * nh + h, i0});
+    parallel_n(workers, (int)blocks.size(), 1, [&](int lo, int hi) {
+      std::vector<float> srow(T);
+      std::vector<uint8_t> prow(T);
+      for (int b = lo; b < hi; b++) {
+        const int bi = blocks[b].task / nh, h = blocks[b].task % nh;
+        const int64_t off = offs[bi];
+        const int n = (int)(offs[bi + 1] - off);
+        const AttnPrep &P = prep[blocks[b].task];
+        for (int i = blocks[b].i0; i < std::min(n, blocks[b].i0 + AttnBlock); i++)
+          attn_row(P, i, window, VL, &ctx[(size_t)(off + i) * H + h * D], srow.data(), prow.data(), nullptr, nullptr,
+                   nullptr);
+      }
+    });
+    if (dl && dump->ctx) std::memcpy(dump->ctx, ctx.data(), sizeof(float) * N * H);
+
+    // Output projection, norm, MLP (infer.go:402-425).
+    std::vector<float> xa;
+    if (dl && dump->x_attn) xa.resize((size_t)N * H);
+    parallel_n(workers, (int)N, slice, [&](int lo, int hi) {
+      GemmScratch s;
+      const int rows = hi - lo;
+      matmul_rows(m->o[l], &ctx[(size_t)lo * H], &x[(size_t)lo * H], rows, true, use_fast, s,
+                  dl && dump->cq ? dump->cq + (size_t)lo * H : nullptr, dl && dump->cq_s ? dump->cq_s + lo : nullptr,
+                  nullptr);
+      if (!xa.empty()) std::memcpy(&xa[(size_t)lo * H], &x[(size_t)lo * H], sizeof(float) * rows * H);
+      for (int r = lo; r < hi; r++)
+        layernorm_row(&xn[(size_t)r * H], &x[(size_t)r * H], m->mlp_norm[l].data(), H, cfg.norm_eps, VL);
+      std::vector<float> z((size_t)rows * 2 * I), g((size_t)rows * I);
+      matmul_rows(m->wi[l], &xn[(size_t)lo * H], z.data(), rows, false, use_fast, s,
+                  dl && dump->hq ? dump->hq + (size_t)lo * H : nullptr, dl && dump->hq_s ? dump->hq_s + lo : nullptr,
+                  nullptr);
+      if (dl && dump->z) std::memcpy(dump->z + (size_t)lo * 2 * I, z.data(), sizeof(float) * rows * 2 * I);
+      for (int r = 0; r < rows; r++) gelu_mul(&g[(size_t)r * I], &z[(size_t)r * 2 * I], &z[(size_t)r * 2 * I + I], I);
+      matmul_rows(m->womlp[l], g.data(), &x[(size_t)lo * H], rows, true, use_fast, s,
+                  dl && dump->gq ? dump->gq + (size_t)lo * I : nullptr, dl && dump->gq_s ? dump->gq_s + lo : nullptr,
+                  nullptr);
+    });
+    if (!xa.empty()) std::memcpy(dump->x_attn, xa.data(), sizeof(float) * N * H);
+    if (dl && dump->x_mlp) std::memcpy(dump->x_mlp, x.data(), sizeof(float) * N * H);
+  }
+  // Final norm (infer.go:427) then pooling (infer.go:261-289).
+  for (int64_t r = 0; r < N; r++) layernorm_row(&xn[r * H], &x[r * H], m->final_norm.data(), H, cfg.norm_eps, VL);
+  if (mode == 1) {
+    std::memcpy(out, xn.data(), sizeof(float) * N * H);
+    return 0;
+  }
+  for (int i = 0; i < nseq; i++) {
+    const int64_t n = offs[i + 1] - offs[i];
+    if (n == 0) continue;
+    if (cfg.cls) {
+      std::memcpy(out + (size_t)i * H, &xn[(size_t)offs[i] * H], sizeof(float) * H);
+      continue;
+    }
+    for (int k = 0; k < H; k++) {
+      double acc = 0.0;
+      for (int64_t t = offs[i]; t < offs[i + 1]; t++) acc += (double)xn[(size_t)t * H + k];
+      out[(size_t)i * H + k] = (float)(acc / (double)n);
+    }
+  }
+  return 0;
+}
+
+int or_cpu_features(void) { return cpu_features(); }
+
+}  // extern "C"

@@ -1,0 +1,50 @@
+// Internal declarations shared by the oracle's translation units (test
+// infrastructure; see oracle.h).
+#pragma once
+#include <stdint.h>
+
+#include <vector>
+
+namespace orc {
+
+float round_half_even(float v);
+float abs32(float v);
+float exp32(float x);
+float exp_body(float v);
+float exp_shift(float *x, int n, float m, int V);
+float erf32(float x);
+float gelu_mul_fma(float x, float gate);
+float gelu_mul_scalar(float x, float gate);
+void gelu_mul(float *o, const float *a, const float *b, int n);
+void layernorm_row(float *o, const float *x, const float *gamma, int n, double eps, int V);
+void rope(float *x, const float *c, const float *s, int half);
+void rope_table(double theta, int D, int npos, float *cs, float *sn);
+float quant_row(int8_t *dst, const float *x, const float *mean, int n, bool flip, int32_t *sum);
+void pack_b8(const float *b, int k, int n, bool transB, int8_t *q, float *scale, int32_t *colsum, float *zc);
+void quantize_a_row(const float *x, int k, uint8_t *q, float *sa);
+void gemm_u8s8(const uint8_t *A, int lda, const int8_t *B, int ldb, int M, int N, int K, int32_t *acc);
+float dequant1(int32_t acc, float zc, float sb, float sa);
+void dequant(const int32_t *acc, int M, int N, const float *sa, const float *sb, const float *zc, float *C,
+             bool accumulate);
+
+struct AttnPrep {
+  int n = 0, D = 0;
+  std::vector<uint8_t> qa;
+  std::vector<float> sq;
+  std::vector<int8_t> kq;
+  std::vector<float> ks, kzc;
+  std::vector<int8_t> vq;
+  std::vector<float> vs, kmean;
+};
+void attn_prepare(const float *q, const float *k, const float *v, int ld, int n, int D, float scale, AttnPrep &P);
+void attn_row(const AttnPrep &P, int i, int window, int V, float *o, float *s_row, uint8_t *p_row, float *sp_out,
+              int32_t *sacc_row, int32_t *oacc_row);
+
+// CPU baseline GEMM (cpu_baseline.cpp): same integers as gemm_u8s8, VNNI when
+// the host has it; rows [r0, r1) of acc.
+void gemm_u8s8_fast(const uint8_t *A, const int8_t *Bpanels, int M, int N, int K, int r0, int r1, int32_t *acc);
+// Panels of 16 output channels, 4 depths per 32-bit word (linalg/int8.go:25-34).
+void pack_panels(const int8_t *q, int N, int K, std::vector<int8_t> &out);
+int cpu_features();
+
+}  // namespace orc

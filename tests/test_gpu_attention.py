@@ -1,0 +1,74 @@
+"""int8 attention vs the oracle, bit-exact, over unpadded varlen batches,
+local and global (linalg/attention8_test.go:50 TestAttend8 shapes and
+windows, :87 TestAttn8Ranges), with NaN-prefilled outputs that must be
+fully written."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _qkv(lens, H, nh, seed):
+    rng = np.random.default_rng(seed)
+    N = int(sum(lens))
+    D = H // nh
+    q = rng.standard_normal((N, H)).astype(np.float32) * 2
+    k = rng.standard_normal((N, H)).astype(np.float32) * 2 + (np.arange(H) % D % 7).astype(np.float32)
+    v = rng.standard_normal((N, H)).astype(np.float32)
+    return np.ascontiguousarray(np.concatenate([q, k, v], 1)), np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+
+
+def _ref(oracle_lib, qkv, offs, H, nh, window):
+    D = H // nh
+    out = np.zeros((qkv.shape[0], H), np.float32)
+    for s in range(len(offs) - 1):
+        a, b = offs[s], offs[s + 1]
+        for h in range(nh):
+            o = oracle_lib.attn8(qkv[a:b, h * D:(h + 1) * D], qkv[a:b, H + h * D:H + (h + 1) * D],
+                                 qkv[a:b, 2 * H + h * D:2 * H + (h + 1) * D], window, np.float32(1 / np.sqrt(D)))
+            out[a:b, h * D:(h + 1) * D] = o
+    return out
+
+
+@pytest.mark.parametrize("window", [-1, 8, 64])
+@pytest.mark.parametrize("lens", [[1], [5], [17], [48], [100], [128], [259], [1, 5, 17, 48, 100, 259],
+                                  [128] * 8, [512, 3, 300]])
+def test_attention_bitexact(igdev, oracle_lib, lens, window):
+    from indecis_b200 import ops
+    H, nh = 256, 4
+    qkv, offs = _qkv(lens, H, nh, seed=sum(lens) + window)
+    ref = _ref(oracle_lib, qkv, offs, H, nh, window)
+    ctx = ops.attention(torch.from_numpy(qkv).cuda(), H, nh, offs, window).cpu().numpy()
+    assert not np.isnan(ctx).any()
+    assert np.array_equal(ctx.view(np.uint32), ref.view(np.uint32))
+
+
+def test_attention_long_global(igdev, oracle_lib):
+    """A 4096-token global layer (BASELINE config 3 length)."""
+    from indecis_b200 import ops
+    H, nh = 128, 2
+    qkv, offs = _qkv([4096], H, nh, seed=11)
+    ref = _ref(oracle_lib, qkv, offs, H, nh, -1)
+    ctx = ops.attention(torch.from_numpy(qkv).cuda(), H, nh, offs, -1).cpu().numpy()
+    assert np.array_equal(ctx.view(np.uint32), ref.view(np.uint32))
+
+
+def test_attention_accuracy_vs_float(igdev):
+    """TestAttend8 bounds: relative error <= 0.03, worst <= 0.25 vs float64."""
+    from indecis_b200 import ops
+    H, nh = 64, 1
+    for n in (5, 48, 259):
+        for window in (-1, 8, 64):
+            qkv, offs = _qkv([n], H, nh, seed=n * 3 + window)
+            ctx = ops.attention(torch.from_numpy(qkv).cuda(), H, nh, offs, window).cpu().numpy().astype(np.float64)
+            q, k, v = (qkv[:, i * H:(i + 1) * H].astype(np.float64) for i in range(3))
+            s = q @ k.T / np.sqrt(H)
+            idx = np.arange(n)
+            if window >= 0:
+                s[np.abs(idx[:, None] - idx[None, :]) > window] = -np.inf
+            p = np.exp(s - s.max(1, keepdims=True))
+            want = (p / p.sum(1, keepdims=True)) @ v
+            d = ctx - want
+            rel = np.sqrt((d ** 2).sum() / (want ** 2).sum())
+            assert rel <= 0.03 and np.abs(d).max() <= 0.25, (n, window, rel)

@@ -1,0 +1,135 @@
+"""Whole int8 encoder on the GPU vs the oracle: every layer's int8
+activations, scales and float states bit-exact; pooled outputs, token states
+and head logits bit-exact (the spec bound is 1e-4 absolute on logits).
+Mirrors internal/modernbert/infer_test.go (EncodeSeqs / EncodeTokens) and
+concurrency_test.go:12 (batch composition and concurrency do not change a
+sequence's result)."""
+import threading
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _models(cfg, seed=42, gamma_noise=0.1):
+    import oracle
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Config, Model
+    W = S.weights(cfg, seed=seed, gamma_noise=gamma_noise)
+    return oracle.Model(cfg, W), Model.from_arrays(Config.from_dict(cfg), W), W
+
+
+def _bits(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+@pytest.fixture(scope="module")
+def tiny(igdev, oracle_lib):
+    from indecis_b200 import synthetic as S
+    cfg = S.tiny(layers=4, hidden=256, heads=4, intermediate=384, vocab=1000)
+    return (cfg,) + _models(cfg)
+
+
+def test_layers_bitexact(tiny):
+    from indecis_b200 import synthetic as S
+    cfg, om, gm, _ = tiny
+    ids, offs = S.ids_varlen(7, 1, 300, cfg["vocab"], seed=5)
+    for layer in range(cfg["layers"]):
+        ro, do = om.encode(ids, offs, dump_layer=layer)
+        rg, dg = gm.encode_dump((ids, offs), layer)
+        if layer == 0:
+            assert np.array_equal(_bits(dg["emb_ln"]), _bits(do["emb_ln"]))
+        for k in ("xq", "cq", "hq", "gq"):
+            assert np.array_equal(dg[k], do[k]), (layer, k)
+        for k in ("xq_s", "cq_s", "hq_s", "gq_s", "qkv", "ctx", "x_attn", "x_mlp"):
+            assert np.array_equal(_bits(dg[k]), _bits(do[k])), (layer, k)
+        assert np.array_equal(_bits(rg), _bits(ro))
+
+
+def test_encode_seqs_and_tokens(tiny):
+    from indecis_b200 import synthetic as S
+    cfg, om, gm, _ = tiny
+    ids, offs = S.ids_varlen(9, 1, 200, cfg["vocab"], seed=6)
+    seqs = [ids[offs[i]:offs[i + 1]] for i in range(len(offs) - 1)]
+    assert np.array_equal(_bits(gm.EncodeSeqs(seqs)), _bits(om.encode(ids, offs, mode=0)))
+    assert np.array_equal(_bits(gm.EncodeTokens(seqs)), _bits(om.encode(ids, offs, mode=1)))
+
+
+def test_c1_batch_bitexact(igdev, oracle_lib):
+    """32 x 128 tokens, 6 layers, hidden 256."""
+    from indecis_b200 import synthetic as S
+    om, gm, _ = _models(S.C1, gamma_noise=0.0)
+    ids, offs = S.ids_fixed(32, 128, S.C1["vocab"], seed=1)
+    ref = om.encode(ids, offs, threads=8)
+    got = gm.EncodeSeqs((ids, offs))
+    assert np.array_equal(_bits(got), _bits(ref))
+
+
+def test_batch_composition_and_threads(tiny):
+    """concurrency_test.go:12: a sequence's result is the same alone, in any
+    batch, and under concurrent calls on one shared model."""
+    from indecis_b200 import synthetic as S
+    cfg, om, gm, _ = tiny
+    ids, offs = S.ids_varlen(12, 3, 150, cfg["vocab"], seed=8)
+    seqs = [ids[offs[i]:offs[i + 1]] for i in range(len(offs) - 1)]
+    full = gm.EncodeSeqs(seqs)
+    for i in (0, 5, 11):
+        alone = gm.EncodeSeqs([seqs[i]])
+        assert np.array_equal(_bits(alone[0]), _bits(full[i]))
+    results = [None] * 8
+    def work(t):
+        order = list(range(len(seqs)))[t % 3:] + list(range(len(seqs)))[:t % 3]
+        out = gm.EncodeSeqs([seqs[j] for j in order])
+        results[t] = out[np.argsort(order)]
+    ths = [threading.Thread(target=work, args=(t,)) for t in range(8)]
+    [t.start() for t in ths]
+    [t.join() for t in ths]
+    for r in results:
+        assert np.array_equal(_bits(r), _bits(full))
+
+
+def test_edge_cases(tiny):
+    from indecis_b200.model import ModernBertError
+    cfg, om, gm, _ = tiny
+    # empty batch, empty sequences (pooled rows stay zero), one-token sequence
+    assert gm.EncodeSeqs([]).shape == (0, cfg["hidden"])
+    out = gm.EncodeSeqs([[], [5], []])
+    ref = om.encode(np.array([5], np.int32), np.array([0, 0, 1, 1], np.int64))
+    assert np.array_equal(_bits(out), _bits(ref))
+    assert not out[0].any() and not out[2].any()
+    # out-of-vocabulary ids are an error with the reference's wording (infer.go:310-312)
+    with pytest.raises(ModernBertError, match="modernbert: id 1000 out of vocabulary"):
+        gm.EncodeSeqs([[1, 2, 1000]])
+    with pytest.raises(ModernBertError, match="modernbert: id -1 out of vocabulary"):
+        gm.EncodeSeqs([[-1]])
+    # the model is still usable after the error
+    assert np.array_equal(_bits(gm.EncodeSeqs([[5]])), _bits(ref[1:2]))
+
+
+def test_cls_pooling(igdev, oracle_lib):
+    from indecis_b200 import synthetic as S
+    cfg = S.tiny(layers=2, vocab=300, pooling="cls")
+    om, gm, _ = _models(cfg)
+    ids, offs = S.ids_varlen(4, 1, 70, cfg["vocab"], seed=9)
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(om.encode(ids, offs)))
+
+
+def test_head_logits(tiny):
+    """heads.go:62-74 in float64 over the pooled vector and per token."""
+    import oracle
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Head
+    cfg, om, gm, _ = tiny
+    heads = [Head(h["name"], h["kind"], h["w"], h["b"] + np.float32(0.01)) for h in S.heads(cfg["hidden"])]
+    gm.SetHeads(heads)
+    ids, offs = S.ids_varlen(6, 2, 90, cfg["vocab"], seed=10)
+    logits, _ = gm.Logits((ids, offs))
+    pooled = om.encode(ids, offs)
+    tokens = om.encode(ids, offs, mode=1)
+    for h, z in zip(heads, logits):
+        ref = oracle.head_logits(h.w, h.b, tokens if h.kind == "spans" else pooled)
+        assert np.abs(z - ref).max() <= 1e-4
+        assert np.array_equal(z, ref)
+    a = heads[2].answer(logits[2][0])
+    assert abs(sum(a["Probs"].values()) - 1) < 1e-12

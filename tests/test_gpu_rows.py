@@ -1,0 +1,66 @@
+"""Row kernels vs the oracle, bit-exact: LayerNormRow (linalg/vec_simd.go:281),
+quantizeA (linalg/int8.go:157; quant_amd64_test.go:11 TestQuantAVX2) and
+PackB8 (linalg/int8.go:36)."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("H", [1, 7, 16, 37, 256, 384, 768, 1153])
+def test_layernorm_quant_bitexact(igdev, oracle_lib, H):
+    from indecis_b200 import ops
+    rng = np.random.default_rng(H)
+    M = 67
+    x = (rng.standard_normal((M, H)) * 3 + rng.uniform(-2, 2, (M, 1))).astype(np.float32)
+    x[3] = 0.0  # a zero row: variance 0
+    gamma = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    xn_ref = oracle_lib.layernorm(x, gamma, 1e-5, 8)
+    q_ref, s_ref = oracle_lib.quantize_a(xn_ref)
+    xn, q, sa = ops.layernorm_quant(torch.from_numpy(x).cuda(), torch.from_numpy(gamma).cuda())
+    assert np.array_equal(xn.cpu().numpy().view(np.uint32), xn_ref.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(sa.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+
+
+def test_layernorm_lanes_16(igdev, oracle_lib):
+    """The lane count is a parameter (16: the reference on AVX-512 hosts)."""
+    from indecis_b200 import ops
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((33, 256)).astype(np.float32)
+    g = np.ones(256, np.float32)
+    ref = oracle_lib.layernorm(x, g, 1e-5, 16)
+    xn, _, _ = ops.layernorm_quant(torch.from_numpy(x).cuda(), torch.from_numpy(g).cuda(), simd_lanes=16)
+    assert np.array_equal(xn.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("K", [1, 32, 256, 301, 384, 4096])
+def test_quantize_rows_bitexact(igdev, oracle_lib, K):
+    from indecis_b200 import ops
+    rng = np.random.default_rng(K)
+    x = (rng.standard_normal((50, K)) * rng.uniform(0.01, 10, (50, 1))).astype(np.float32)
+    x[7] = 0.0
+    x[9, :] = 0.5  # ties: x * (127/0.5) lands on exact halves only through rounding
+    q_ref, s_ref = oracle_lib.quantize_a(x)
+    q, sa = ops.quantize_rows(torch.from_numpy(x).cuda())
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(sa.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("n,k", [(768, 256), (256, 384), (17, 301), (1, 1)])
+def test_pack_b8_bitexact(igdev, oracle_lib, n, k):
+    from indecis_b200 import ops
+    rng = np.random.default_rng(n + k)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    if n > 3:
+        w[2] = 0.0
+        w[3, :4] = [0.5, -0.5, 1.0, -1.0]  # half-away rounding cases after scaling
+    q_ref, s_ref, cs_ref, zc_ref = oracle_lib.pack_b8(w)
+    q, s, zc, cs = ops.pack_b8(torch.from_numpy(w).cuda())
+    q = q.cpu().numpy()
+    assert np.array_equal(q[:, :k], q_ref)
+    assert not q[:, k:].any()
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+    assert np.array_equal(zc.cpu().numpy().view(np.uint32), zc_ref.view(np.uint32))
+    assert np.array_equal(cs.cpu().numpy(), cs_ref)
