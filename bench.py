@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""Throughput of the int8 ModernBERT encoder + decision heads on B200.
+
+Workload: ModernBERT vocab 16384, hidden 256, 6 layers,
+4 heads of 64, GeGLU 384, local window 128 with every 3rd layer global,
+seeded random-init weights, 128-token sequences with ids uniform in
+[4, 16384), heads noul / choice(5) / score(5 levels) / spans(9 tags).
+A step is one call of the encoder + heads over `--seqs-per-step` sequences
+(a stream of 32-sequence batches laid end to end); the metric is sequences
+per second. Multi-GPU: one process per GPU, each encoding its own shard of
+sequences (weak scaling, no data-path collective); the time is the max over
+ranks.
+
+  python bench.py [--gpus N --steps K --warmup W]   # this implementation
+  python bench.py --impl reference ...               # the reference's CPU path
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "int8 encoder seq/s (128 tok)"
+SEQ_LEN = 128
+BATCH = 32
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seqs-per-step", type=int, default=2048)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target length of the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return dict(hbm=float(p["hbm_gbs"]), bf16=float(p["bf16_tflops"]), src="measured")
+    except Exception:
+        return dict(hbm=6650.0, bf16=1590.0, src="fallback")
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Clocks:
+    """nvidia-smi samples of one GPU during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except Exception:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_gpu(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local])
+        except (ValueError, IndexError):
+            pass
+    return local
+
+
+def workload(seqs: int, seed: int):
+    from indecis_b200 import synthetic as S
+    return S.ids_fixed(seqs, SEQ_LEN, S.C1["vocab"], seed=seed)
+
+
+def config_obj(args, world):
+    return {"workload": "C1 ModernBERT int8 forward + heads (vocab 16384, hidden 256, 6 layers, 4x64 heads, GeGLU 384, "
+                        "local 128 / global every 3rd), noul+choice5+score5+spans9 heads",
+            "seq_len": SEQ_LEN, "batch": BATCH, "seqs_per_step_per_gpu": args.seqs_per_step,
+            "batches_per_step_per_gpu": args.seqs_per_step // BATCH, "global_batch": args.seqs_per_step * world,
+            "parallelism": f"sequence shard x{world}, no collective",
+            "l2": "inputs and activations larger than L2 (x alone is seqs*128*1 KiB)", "weights": "random-init seed 42"}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the oracle port of the reference path; test/bench infrastructure)
+# ---------------------------------------------------------------------------
+
+def cpu_model():
+    import oracle
+    from indecis_b200 import synthetic as S
+    oracle.build()
+    model = oracle.Model(S.C1, S.weights(S.C1, seed=42))
+    model.heads = S.heads(S.C1["hidden"])
+    return model, oracle
+
+
+def cpu_sample(model, batches: int, threads: int, seed: int = 1):
+    """Encoder + heads on `batches` batches of 32x128: token states, float64
+    mean pooling in token order, then every head's float64 logits."""
+    import oracle
+    ids, offs = workload(batches * BATCH, seed)
+    t0 = time.perf_counter()
+    for b in range(batches):
+        lo, hi = b * BATCH, (b + 1) * BATCH
+        o = offs[lo:hi + 1] - offs[lo]
+        tokens = model.encode(ids[offs[lo]:offs[hi]], o, mode=1, threads=threads, fast=True)
+        pooled = np.stack([tokens[o[i]:o[i + 1]].astype(np.float64).mean(0) for i in range(BATCH)]).astype(np.float32)
+        for h in model.heads:
+            oracle.head_logits(h["w"], h["b"], tokens if h["kind"] == "spans" else pooled)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(target_s: float):
+    model, oracle = cpu_model()
+    threads = os.cpu_count() or 1
+    t1 = cpu_sample(model, 1, threads)
+    batches = int(max(1, min(200, target_s / max(t1, 1e-3))))
+    t = cpu_sample(model, batches, threads, seed=2)
+    feats = oracle.lib().or_cpu_features()
+    isa = "AVX-VNNI" if feats & 1 else ("AVX512-VNNI" if feats & 2 else "scalar int")
+    return {"value": batches * BATCH / t, "unit": "seq/s", "cores": threads, "kind": "port",
+            "sample": f"{batches} batches of 32x128 (C1), oracle C++ port of the reference int8 path, {isa} 6x16 "
+                      f"tiles, {threads} threads, {t:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU implementation of the path (the oracle port, since
+    the Go reference cannot run on this image), on all host threads."""
+    if rank != 0:
+        return
+    model, oracle = cpu_model()
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_sample(model, 1, threads)
+    ts = [cpu_sample(model, 1, threads, seed=3 + k) for k in range(args.steps)]
+    total = sum(ts)
+    v = args.steps * BATCH / total
+    feats = oracle.lib().or_cpu_features()
+    isa = "AVX-VNNI" if feats & 1 else ("AVX512-VNNI" if feats & 2 else "scalar int")
+    line = {"metric": METRIC, "value": v, "unit": "seq/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {**config_obj(args, 1), "seqs_per_step_per_gpu": BATCH, "batches_per_step_per_gpu": 1,
+                       "global_batch": BATCH, "note": "one 32x128 batch per step (bounded CPU sample)"},
+            "cpu_baseline": {"value": v, "unit": "seq/s", "cores": threads, "kind": "port",
+                             "sample": f"one 32x128 batch per step, oracle C++ port (Go reference not runnable: no Go "
+                                       f"toolchain), {isa}, {threads} threads"},
+            "e2e": {"value": v, "unit": "seq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+
+def roofline(report, pk):
+    ks = [k for k in report["kernels"] if k["records"] > 0 and k["ms"] > 0]
+    top = max(ks, key=lambda k: k["ms"])
+    total_ms = sum(k["ms"] for k in ks)
+    per_ms = top["ms"] / top["records"]
+    bytes_ = top["bytes"] / top["records"]
+    ops = top["ops"] / top["records"]
+    int8_peak = 2.0 * pk["bf16"]  # TOP/s: int8 dense = 2x bf16 dense on B200
+    t_hbm = bytes_ / (pk["hbm"] * 1e9)
+    t_ops = ops / (int8_peak * 1e12) if ops else 0.0
+    if t_ops > t_hbm:
+        ach = ops / (per_ms * 1e-3) / 1e12
+        rf = {"bound": "tensor", "achieved": ach, "peak": int8_peak, "unit": "TFLOP/s", "frac": ach / int8_peak}
+        peak_note = f"int8 dense = 2 x {pk['src']} bf16 burst {pk['bf16']} TFLOP/s (no int8 entry)"
+    else:
+        ach = bytes_ / (per_ms * 1e-3) / 1e9
+        rf = {"bound": "hbm", "achieved": ach, "peak": pk["hbm"], "unit": "GB/s", "frac": ach / pk["hbm"]}
+        peak_note = f"{pk['src']} HBM copy bandwidth"
+    rf.update({"kernel": top["name"], "share": top["ms"] / total_ms, "ms_per_launch": per_ms,
+               "algorithmic_bytes": bytes_, "algorithmic_ops": ops, "peak_source": peak_note, "traffic": None})
+    return rf
+
+
+def gemm_point(M, N, K, pk, reps=20):
+    import torch
+    from indecis_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.randint(1, 256, (M, K), dtype=torch.uint8, device="cuda", generator=g)
+    B = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g)
+    sa = torch.rand(M, device="cuda", generator=g) * 0.1 + 1e-3
+    sb = torch.rand(N, device="cuda", generator=g) * 0.1 + 1e-3
+    zc = 128.0 * B.to(torch.float32).sum(1)
+    C = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        ops.gemm_u8s8(A, B, sa=sa, sb=sb, zc=zc, C=C)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(reps):
+        ops.gemm_u8s8(A, B, sa=sa, sb=sb, zc=zc, C=C)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    tops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    byts = M * K + N * K + 4 * M + 8 * N + 4 * M * N
+    int8_peak = 2.0 * pk["bf16"]
+    bound = min(int8_peak, byts and (2.0 * M * N * K / byts) * pk["hbm"] / 1e3)
+    return {"M": M, "N": N, "K": K, "ms": ms, "tops": tops, "frac_of_int8_peak": tops / int8_peak,
+            "frac_of_roofline": tops / bound, "out": "f32"}
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    from indecis_b200 import _capi, build
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Config, Head, Model
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    build.build()
+    pk = peaks()
+    cfg = Config.from_dict(S.C1)
+    model = Model.from_arrays(cfg, S.weights(S.C1, seed=42), device=local)
+    heads = [Head(h["name"], h["kind"], h["w"], h["b"]) for h in S.heads(cfg.hidden_size)]
+    model.SetHeads(heads)
+    L = _capi.load()
+
+    nseq = args.seqs_per_step
+    ids, offs = workload(nseq, seed=1 + rank)
+    N = int(offs[-1])
+    pooled_rows = sum(h.rows for h in heads if h.kind != "spans")
+    token_rows = sum(h.rows for h in heads if h.kind == "spans")
+    d_ids = torch.from_numpy(ids).cuda()
+    d_logits = torch.empty((nseq, pooled_rows), dtype=torch.float64, device="cuda")
+    d_tlog = torch.empty((N, token_rows), dtype=torch.float64, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        _capi.check(L.ig_logits_device(model._h, d_ids.data_ptr(), offs.ctypes.data, nseq, d_logits.data_ptr(),
+                                       d_tlog.data_ptr(), stream.cuda_stream))
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: device events on the launching stream -------------
+    clocks = Clocks(physical_gpu(local))
+    _capi.profile(True)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    report = _capi.profile_report()
+    _capi.profile(False)
+    value = world * nseq * args.steps / (ms / 1e3)
+    dev_err = L.ig_device_error(1)
+    if dev_err:
+        raise RuntimeError(f"device error {dev_err}")
+
+    # ---- end to end: the host API (ids from host memory, logits back) -----
+    e2e_steps = max(3, min(args.steps, 20))
+    seqs = (ids, offs)
+    model.Logits(seqs)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        model.Logits(seqs)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    nblocks = sum((int(offs[i + 1] - offs[i]) + 15) // 16 for i in range(nseq))
+    h2d = 4 * N + 4 * (nseq + 1) + 8 * N + 8 * nblocks  # ids + offsets, row->sequence, positions, query blocks
+    d2h = 8 * nseq * pooled_rows + 8 * N * token_rows
+    e2e = {"value": world * nseq * e2e_steps / e2e_s, "unit": "seq/s", "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "api": "ig_logits (host buffers, synchronous), host clock around "
+                                                "device-synchronized calls"}
+
+    gemm = None
+    if rank == 0 and not args.no_gemm:
+        gemm = [gemm_point(65536, 2304, 768, pk), gemm_point(65536, 768, 256, pk)]
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "seq/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config_obj(args, world),
+                "e2e": e2e, "gpu_launches": report["launches"], "roofline": roofline(report, pk),
+                "kernels": {k["name"]: {"ms": round(k["ms"], 3), "launches": k["launches"]}
+                            for k in report["kernels"]},
+                "clocks": clk, "cpu_baseline": cpu, "gemm_sweep": gemm}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -120,6 +120,21 @@ IG_API int ig_encode_device(ig_model *m, const int32_t *d_ids, const int64_t *of
 IG_API int ig_logits(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, double *logits,
               size_t logits_len, double *token_logits, size_t token_len);
 
+/* ig_logits on device buffers, enqueued on `stream` like ig_encode_device:
+ * d_logits [nseq][sum of pooled rows], d_token_logits [offs[nseq]][sum of
+ * per-token rows] (either may be NULL). */
+IG_API int ig_logits_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int32_t nseq, double *d_logits,
+                            double *d_token_logits, void *stream);
+
+/* Kernel profiling. ig_profile(1) clears the records and brackets every
+ * encoder launch with CUDA events on its stream (outside stream capture);
+ * ig_profile(0) stops. ig_profile_report synchronizes the device and writes
+ * a JSON summary {"launches": total kernel launches since ig_profile(1),
+ * "kernels": [{name, launches, ms, bytes, ops}]} where bytes and ops are the
+ * launches' algorithmic memory traffic and arithmetic; returns its length. */
+IG_API int ig_profile(int32_t enable);
+IG_API int64_t ig_profile_report(char *buf, size_t len);
+
 /* Message of the calling thread's last failure ("" if none). */
 IG_API const char *ig_last_error(void);
 

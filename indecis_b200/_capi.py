@@ -24,7 +24,8 @@ IG_MODE_TOKENS = 1
 # Every symbol the header declares (tests check the library exports them all).
 SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_encode", "ig_encode_device",
            "ig_logits", "ig_last_error", "ig_device_error", "ig_gemm_u8s8", "ig_quantize_rows",
-           "ig_layernorm_quant", "ig_pack_b8", "ig_attention", "ig_encode_dump"]
+           "ig_layernorm_quant", "ig_pack_b8", "ig_attention", "ig_encode_dump", "ig_logits_device",
+           "ig_profile", "ig_profile_report"]
 
 
 class IgConfig(C.Structure):
@@ -83,6 +84,10 @@ def load() -> C.CDLL:
     L.ig_pack_b8.argtypes = [vp, i32, i32, vp, i32, vp, vp, vp, vp]
     L.ig_attention.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
     L.ig_encode_dump.argtypes = [vp, vp, vp, i32, i32, vp, C.c_size_t, C.POINTER(IgDump)]
+    L.ig_logits_device.argtypes = [vp, vp, vp, i32, vp, vp, vp]
+    L.ig_profile.argtypes = [i32]
+    L.ig_profile_report.argtypes = [C.c_char_p, C.c_size_t]
+    L.ig_profile_report.restype = C.c_int64
     _lib = L
     return L
 
@@ -95,6 +100,20 @@ class IgError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(msg or f"indecis_b200 error {code}")
         self.code = code
+
+
+def profile(enable: bool):
+    check(load().ig_profile(1 if enable else 0))
+
+
+def profile_report() -> dict:
+    """Per-kernel totals since profile(True) (synchronizes the device)."""
+    import json
+    L = load()
+    n = L.ig_profile_report(None, 0)
+    buf = C.create_string_buffer(int(n) + 1)
+    L.ig_profile_report(buf, len(buf))
+    return json.loads(buf.value.decode())
 
 
 def check(rc: int):

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -52,6 +53,58 @@ static int fail(int code, const std::string &msg) {
   } while (0)
 
 static inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---- kernel profiling (ig_profile / ig_profile_report) ----------------------
+// When enabled, every launch site of the encoder brackets its kernels with a
+// pair of CUDA events on the launching stream and records the algorithmic
+// bytes and integer/float operations of the launch (computed from its
+// shapes), so a caller can derive achieved bandwidth or throughput per kernel.
+struct ProfRec {
+  const char *name;
+  cudaEvent_t a, b;
+  double bytes, ops;
+  int launches;
+};
+
+struct Profiler {
+  std::mutex mu;
+  bool on = false;
+  std::vector<ProfRec> recs;
+  std::vector<cudaEvent_t> pool;
+  cudaEvent_t get() {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+static Profiler g_prof;
+static std::atomic<long long> g_launches{0};
+
+struct ProfScope {
+  bool on = false;
+  ProfRec r{};
+  cudaStream_t st = nullptr;
+  ProfScope(const char *name, double bytes, double ops, int launches, cudaStream_t s, bool capturing = false) {
+    g_launches += launches;
+    on = g_prof.on && !capturing;
+    if (!on) return;
+    st = s;
+    r = ProfRec{name, g_prof.get(), g_prof.get(), bytes, ops, launches};
+    cudaEventRecord(r.a, st);
+  }
+  ~ProfScope() {
+    if (!on) return;
+    cudaEventRecord(r.b, st);
+    std::lock_guard<std::mutex> lk(g_prof.mu);
+    g_prof.recs.push_back(r);
+  }
+};
 
 struct DevMat {
   int8_t *q = nullptr;
@@ -383,13 +436,38 @@ int copy_rows_d2h(void *dst, const void *src, size_t row_bytes, size_t src_pitch
 }
 
 // The layer loop. d_ids: device ids; results in w.xn (tokens) / w.pooled.
+// Algorithmic bytes of a GEMM launch: A (M x K u8), B (N x K s8), scales,
+// and out_row_bytes of output traffic per row.
+double gemm_bytes(double M, double N, double K, double out_row_bytes) {
+  return M * K + N * K + 4.0 * M + 8.0 * N + M * out_row_bytes;
+}
+
+// Valid (query, key) pairs of an attention layer over the plan's sequences.
+double attn_pairs(const Plan &p, int window) {
+  double pairs = 0;
+  for (int s = 0; s < p.nseq; s++) {
+    const double n = p.offs[s + 1] - p.offs[s];
+    if (window < 0 || n <= window + 1) {
+      pairs += n * n;
+    } else {
+      const double w = window;
+      pairs += n * (2 * w + 1) - w * (w + 1);  // rows near the ends see fewer keys
+    }
+  }
+  return pairs;
+}
+
 int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, int mode, cudaStream_t st,
-                ig_dump *dump) {
+                ig_dump *dump, bool capturing = false) {
   const ig_config &c = m->cfg;
   const int H = m->H, I = m->I, N = p.N;
   const int V = c.simd_lanes;
   if (N == 0) return 0;
-  IG_TRY(launch_embed_checked(d_ids, c.vocab, m->emb, m->emb_norm, N, H, c.norm_eps, V, w.x, w.xq, m->ldk, w.sa, st));
+  {
+    ProfScope ps("embed_ln_quant", (double)N * (8 + 9.0 * H) + 4.0 * H, 0, 1, st, capturing);
+    IG_TRY(launch_embed_checked(d_ids, c.vocab, m->emb, m->emb_norm, N, H, c.norm_eps, V, w.x, w.xq, m->ldk, w.sa,
+                                st));
+  }
   if (dump && dump->emb_ln) IG_TRY(copy_rows_d2h(dump->emb_ln, w.x, H * 4, H * 4, N, st));
   AttnArgs at{};
   at.qkv = w.qkv;
@@ -417,8 +495,10 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
     const DevLayer &L = m->layers[l];
     const bool global = l % c.global_every == 0;
     const bool dl = dump && dump->layer == l;
-    if (l > 0)
+    if (l > 0) {
+      ProfScope ps("ln_quant", (double)N * (5.0 * H + 4) + 4.0 * H, 0, 1, st, capturing);
       IG_TRY(launch_ln_quant(w.x, L.attn_norm, N, H, c.norm_eps, V, nullptr, w.xq, m->ldk, w.sa, st));
+    }
     if (dl) {
       IG_TRY(copy_rows_d2h(dump->xq, w.xq, H, m->ldk, N, st));
       IG_TRY(copy_rows_d2h(dump->xq_s, w.sa, 4, 4, N, st));
@@ -435,14 +515,26 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       e.rope_cos = m->rope_cos[global ? 0 : 1];
       e.rope_sin = m->rope_sin[global ? 0 : 1];
       e.rope_cols = 2 * H;
+      ProfScope ps("gemm_qkv_rope", gemm_bytes(N, 3 * H, H, 4.0 * 3 * H) + 8.0 * N, 2.0 * N * 3 * H * H, 1, st,
+                   capturing);
       IG_TRY(gemm_u8s8(g, e, kEpiRope, st));
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->qkv, w.qkv, 3 * H * 4, 3 * H * 4, N, st));
     at.window = global ? -1 : c.local_attention / 2;
-    IG_TRY(launch_attention(at, st));
-    IG_TRY(launch_attend(at, w.blocks, p.nblocks, st));
+    {
+      ProfScope ps("attn_prep", (double)N * H * 4 * 5 + (double)N * H * 3 + 12.0 * N * m->nh, 0, 2, st, capturing);
+      IG_TRY(launch_attention(at, st));
+    }
+    {
+      const double pairs = attn_pairs(p, at.window);
+      ProfScope ps("attn_attend", (double)N * H * 7 + 12.0 * N * m->nh, 4.0 * pairs * m->D * m->nh, 1, st, capturing);
+      IG_TRY(launch_attend(at, w.blocks, p.nblocks, st));
+    }
     if (dl) IG_TRY(copy_rows_d2h(dump->ctx, w.ctx, H * 4, H * 4, N, st));
-    IG_TRY(launch_quant_rows(w.ctx, H, N, H, w.xq, m->ldk, w.sa, st));
+    {
+      ProfScope ps("quant_rows", (double)N * (5.0 * H + 4), 0, 1, st, capturing);
+      IG_TRY(launch_quant_rows(w.ctx, H, N, H, w.xq, m->ldk, w.sa, st));
+    }
     if (dl) {
       IG_TRY(copy_rows_d2h(dump->cq, w.xq, H, m->ldk, N, st));
       IG_TRY(copy_rows_d2h(dump->cq_s, w.sa, 4, 4, N, st));
@@ -456,10 +548,14 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       e.C = w.x;
       e.ldc = H;
       e.accumulate = 1;
+      ProfScope ps("gemm_wo_residual", gemm_bytes(N, H, H, 8.0 * H), 2.0 * N * H * H, 1, st, capturing);
       IG_TRY(gemm_u8s8(g, e, kEpiF32, st));
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->x_attn, w.x, H * 4, H * 4, N, st));
-    IG_TRY(launch_ln_quant(w.x, L.mlp_norm, N, H, c.norm_eps, V, nullptr, w.xq, m->ldk, w.sa, st));
+    {
+      ProfScope ps("ln_quant", (double)N * (5.0 * H + 4) + 4.0 * H, 0, 1, st, capturing);
+      IG_TRY(launch_ln_quant(w.x, L.mlp_norm, N, H, c.norm_eps, V, nullptr, w.xq, m->ldk, w.sa, st));
+    }
     if (dl) {
       IG_TRY(copy_rows_d2h(dump->hq, w.xq, H, m->ldk, N, st));
       IG_TRY(copy_rows_d2h(dump->hq_s, w.sa, 4, 4, N, st));
@@ -473,10 +569,14 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       e.C = w.g;
       e.ldc = I;
       e.geglu_n = I;
+      ProfScope ps("gemm_wi_geglu", gemm_bytes(N, 2 * I, H, 4.0 * I), 2.0 * N * 2 * I * H, 1, st, capturing);
       IG_TRY(gemm_u8s8(g, e, kEpiGeglu, st));
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->g, w.g, I * 4, I * 4, N, st));
-    IG_TRY(launch_quant_rows(w.g, I, N, I, w.xq, m->ldk, w.sa, st));
+    {
+      ProfScope ps("quant_rows", (double)N * (5.0 * I + 4), 0, 1, st, capturing);
+      IG_TRY(launch_quant_rows(w.g, I, N, I, w.xq, m->ldk, w.sa, st));
+    }
     if (dl) {
       IG_TRY(copy_rows_d2h(dump->gq, w.xq, I, m->ldk, N, st));
       IG_TRY(copy_rows_d2h(dump->gq_s, w.sa, 4, 4, N, st));
@@ -490,13 +590,51 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       e.C = w.x;
       e.ldc = H;
       e.accumulate = 1;
+      ProfScope ps("gemm_womlp_residual", gemm_bytes(N, H, I, 8.0 * H), 2.0 * N * H * I, 1, st, capturing);
       IG_TRY(gemm_u8s8(g, e, kEpiF32, st));
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->x_mlp, w.x, H * 4, H * 4, N, st));
   }
-  IG_TRY(launch_ln_quant(w.x, m->final_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
-  if (mode == IG_MODE_POOLED)
+  {
+    ProfScope ps("ln_final", (double)N * 8.0 * H + 4.0 * H, 0, 1, st, capturing);
+    IG_TRY(launch_ln_quant(w.x, m->final_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
+  }
+  if (mode == IG_MODE_POOLED) {
+    ProfScope ps("pool", (double)N * 4.0 * H + 4.0 * p.nseq * H, 0, 1, st, capturing);
     IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, c.pooling == IG_POOL_CLS, w.pooled, st));
+  }
+  return 0;
+}
+
+// Head logits (heads.go:62-74) of the pooled vectors and, for per-token
+// heads, of every token state, into [nseq][pooled rows] / [N][token rows].
+int run_heads(ig_model *m, Workspace &w, const Plan &p, cudaStream_t st, double *d_logits, double *d_tlogits,
+              bool capturing) {
+  std::vector<DevHead> hs;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    hs = m->heads;
+  }
+  size_t pl = 0, tl = 0;
+  for (auto &h : hs) (h.per_token ? tl : pl) += h.rows;
+  size_t po = 0, to = 0;
+  const int H = m->H;
+  for (auto &h : hs) {
+    if (h.per_token) {
+      if (d_tlogits && p.N) {
+        ProfScope ps("head_logits", (double)p.N * (4.0 * H + 8.0 * h.rows), 2.0 * p.N * h.rows * H, 1, st, capturing);
+        IG_TRY(launch_head_logits(h.w, h.b, h.rows, H, w.xn, p.N, d_tlogits + to, (int)tl, st));
+      }
+      to += h.rows;
+    } else {
+      if (d_logits && p.nseq) {
+        ProfScope ps("head_logits", (double)p.nseq * (4.0 * H + 8.0 * h.rows), 2.0 * p.nseq * h.rows * H, 1, st,
+                     capturing);
+        IG_TRY(launch_head_logits(h.w, h.b, h.rows, H, w.pooled, p.nseq, d_logits + po, (int)pl, st));
+      }
+      po += h.rows;
+    }
+  }
   return 0;
 }
 
@@ -536,23 +674,9 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   int rc = upload_plan(*w, p, ids, st);
   const int enc_mode = (logits || tlog) ? IG_MODE_POOLED : mode;
   if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump);
+  if (!rc && (logits || tlog))
+    rc = run_heads(m, *w, p, st, logits ? w->logits : nullptr, tlog ? w->tlogits : nullptr, false);
   if (!rc && (logits || tlog)) {
-    std::vector<DevHead> hs;
-    {
-      std::lock_guard<std::mutex> lk(m->mu);
-      hs = m->heads;
-    }
-    size_t po = 0, to = 0;
-    for (auto &h : hs) {
-      if (h.per_token) {
-        if (tlog) rc = launch_head_logits(h.w, h.b, h.rows, (int)H, w->xn, p.N, w->tlogits + to, (int)tl, st);
-        to += h.rows;
-      } else {
-        if (logits) rc = launch_head_logits(h.w, h.b, h.rows, (int)H, w->pooled, nseq, w->logits + po, (int)pl, st);
-        po += h.rows;
-      }
-      if (rc) break;
-    }
     if (!rc && logits && nseq && pl)
       rc = cudaMemcpyAsync(logits, w->logits, sizeof(double) * nseq * pl, cudaMemcpyDeviceToHost, st) ? IG_ERR_CUDA : 0;
     if (!rc && tlog && p.N && tl)
@@ -707,7 +831,7 @@ int ig_encode_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int
   Workspace *w = nullptr;
   IG_TRY(acquire_ws(m, p, 0, 0, st, capturing, &w));
   int rc = upload_plan(*w, p, nullptr, st);
-  if (!rc) rc = run_encoder(m, *w, d_ids, p, mode, st, nullptr);
+  if (!rc) rc = run_encoder(m, *w, d_ids, p, mode, st, nullptr, capturing);
   if (!rc && p.N) {
     const size_t H = m->H;
     if (mode == IG_MODE_POOLED)
@@ -719,6 +843,89 @@ int ig_encode_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int
   }
   release_ws(m, w, st, capturing);
   return rc;
+}
+
+int ig_logits_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int32_t nseq, double *d_logits,
+                     double *d_token_logits, void *stream) {
+  t_last_error.clear();
+  if (!m || !offs || (!d_logits && !d_token_logits)) return fail(IG_ERR_BAD_ARG, "null argument");
+  DeviceGuard dg(m->device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  IG_CU(cudaStreamIsCapturing(st, &cs));
+  const bool capturing = cs != cudaStreamCaptureStatusNone;
+  Plan p;
+  IG_TRY(make_plan(offs, nseq, p));
+  if (capturing && m->rope_npos < p.max_len) return fail(IG_ERR_BAD_ARG, "run once before capturing");
+  IG_TRY(ensure_rope(m, p.max_len));
+  Workspace *w = nullptr;
+  IG_TRY(acquire_ws(m, p, 0, 0, st, capturing, &w));
+  int rc = upload_plan(*w, p, nullptr, st);
+  if (!rc) rc = run_encoder(m, *w, d_ids, p, IG_MODE_POOLED, st, nullptr, capturing);
+  if (!rc) rc = run_heads(m, *w, p, st, d_logits, d_token_logits, capturing);
+  release_ws(m, w, st, capturing);
+  return rc;
+}
+
+int ig_profile(int32_t enable) {
+  t_last_error.clear();
+  if (enable) {
+    cudaDeviceSynchronize();
+    std::lock_guard<std::mutex> lk(g_prof.mu);
+    for (auto &r : g_prof.recs) {
+      g_prof.pool.push_back(r.a);
+      g_prof.pool.push_back(r.b);
+    }
+    g_prof.recs.clear();
+    g_launches = 0;
+  }
+  g_prof.on = enable != 0;
+  return 0;
+}
+
+int64_t ig_profile_report(char *buf, size_t len) {
+  cudaDeviceSynchronize();
+  struct Agg {
+    std::string name;
+    long long launches = 0;
+    double ms = 0, bytes = 0, ops = 0;
+    long long records = 0;
+  };
+  std::vector<Agg> aggs;
+  {
+    std::lock_guard<std::mutex> lk(g_prof.mu);
+    for (auto &r : g_prof.recs) {
+      float ms = 0.0f;
+      if (cudaEventElapsedTime(&ms, r.a, r.b) != cudaSuccess) ms = 0.0f;
+      Agg *a = nullptr;
+      for (auto &x : aggs)
+        if (x.name == r.name) a = &x;
+      if (!a) {
+        aggs.push_back(Agg{r.name});
+        a = &aggs.back();
+      }
+      a->launches += r.launches;
+      a->records += 1;
+      a->ms += ms;
+      a->bytes += r.bytes;
+      a->ops += r.ops;
+    }
+  }
+  std::string js = "{\"launches\": " + std::to_string((long long)g_launches) + ", \"kernels\": [";
+  char tmp[512];
+  for (size_t i = 0; i < aggs.size(); i++) {
+    snprintf(tmp, sizeof(tmp), "%s{\"name\": \"%s\", \"launches\": %lld, \"records\": %lld, \"ms\": %.6f, "
+             "\"bytes\": %.1f, \"ops\": %.1f}", i ? ", " : "", aggs[i].name.c_str(), aggs[i].launches,
+             aggs[i].records, aggs[i].ms, aggs[i].bytes, aggs[i].ops);
+    js += tmp;
+  }
+  js += "]}";
+  if (buf && len) {
+    const size_t n = std::min(len - 1, js.size());
+    std::memcpy(buf, js.data(), n);
+    buf[n] = 0;
+  }
+  return (int64_t)js.size();
 }
 
 const char *ig_last_error(void) { return t_last_error.c_str(); }
