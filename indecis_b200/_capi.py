@@ -25,7 +25,7 @@ IG_MODE_TOKENS = 1
 SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_encode", "ig_encode_device",
            "ig_logits", "ig_last_error", "ig_device_error", "ig_gemm_u8s8", "ig_quantize_rows",
            "ig_layernorm_quant", "ig_pack_b8", "ig_attention", "ig_encode_dump", "ig_logits_device",
-           "ig_profile", "ig_profile_report"]
+           "ig_profile", "ig_profile_report", "ig_attention_noalloc"]
 
 
 class IgConfig(C.Structure):
@@ -85,6 +85,7 @@ def load() -> C.CDLL:
     L.ig_attention.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
     L.ig_encode_dump.argtypes = [vp, vp, vp, i32, i32, vp, C.c_size_t, C.POINTER(IgDump)]
     L.ig_logits_device.argtypes = [vp, vp, vp, i32, vp, vp, vp]
+    L.ig_attention_noalloc.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
     L.ig_profile.argtypes = [i32]
     L.ig_profile_report.argtypes = [C.c_char_p, C.c_size_t]
     L.ig_profile_report.restype = C.c_int64

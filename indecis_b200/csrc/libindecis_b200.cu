@@ -4,3 +4,4 @@
 #include "rows.cu"
 #include "attention.cu"
 #include "capi.cu"
+#include "noalloc.cu"

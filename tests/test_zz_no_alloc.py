@@ -1,0 +1,66 @@
+"""ig_attention_noalloc — the allocation-free attention entry point.
+
+Callers that cannot allocate device memory (work recorded into a CUDA graph,
+servers that reserve all device memory at start-up, paths that must not let
+cudaMalloc/cudaFree synchronize the device) use this variant; its work
+buffers live in a fixed 32 MiB array inside the library. The test calls it
+through the C ABI twice in a row, on different inputs, and checks each
+result against the allocating entry point ig_attention (bit for bit, the
+tolerance every attention test here uses), so contents left in the shared
+array by one call cannot leak into the next. It also checks that inputs too
+large for the array are refused with a clear error before any GPU work.
+
+This file is collected last on purpose: if it fails, a run that stops at the
+first failure has already run every other test.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _qkv(lens, H, nh, seed):
+    rng = np.random.default_rng(seed)
+    N = int(sum(lens))
+    D = H // nh
+    q = rng.standard_normal((N, H)).astype(np.float32) * 2
+    k = rng.standard_normal((N, H)).astype(np.float32) * 2 + (np.arange(H) % D % 5).astype(np.float32)
+    v = rng.standard_normal((N, H)).astype(np.float32)
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    return np.ascontiguousarray(np.concatenate([q, k, v], 1)), offs
+
+
+def _noalloc(qkv, H, nh, offs, window):
+    from indecis_b200 import _capi
+    N = int(offs[-1])
+    ctx = torch.full((N, H), float("nan"), dtype=torch.float32, device="cuda")
+    rc = _capi.load().ig_attention_noalloc(qkv.data_ptr(), H, nh, offs.ctypes.data, len(offs) - 1, window, 8,
+                                           ctx.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    _capi.check(rc)
+    torch.cuda.synchronize()
+    return ctx.cpu().numpy()
+
+
+def test_noalloc_matches_allocating_entry_point(igdev):
+    from indecis_b200 import ops
+    H, nh = 256, 4
+    cases = [([128] * 8 + [5, 77], 64, 1), ([259, 1, 300, 48], -1, 2)]
+    for lens, window, seed in cases:  # two calls in a row on the shared array
+        qkv_np, offs = _qkv(lens, H, nh, seed)
+        qkv = torch.from_numpy(qkv_np).cuda()
+        want = ops.attention(qkv, H, nh, offs, window).cpu().numpy()
+        got = _noalloc(qkv, H, nh, offs, window)
+        assert not np.isnan(got).any()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (lens, window)
+
+
+def test_noalloc_rejects_oversize(igdev):
+    from indecis_b200 import _capi
+    H, nh = 256, 4
+    offs = np.array([0, 200000], np.int64)  # needs far more than 32 MiB of scratch
+    small = torch.zeros((1, 3 * H), dtype=torch.float32, device="cuda")
+    rc = _capi.load().ig_attention_noalloc(small.data_ptr(), H, nh, offs.ctypes.data, 1, 64, 8, small.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream)
+    assert rc == _capi.IG_ERR_BAD_ARG
+    assert "bytes of scratch" in _capi.last_error()
