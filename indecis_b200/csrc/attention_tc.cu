@@ -1,0 +1,319 @@
+// int8 attention on the tensor cores: the Attend half of linalg/attention8.go
+// (:298-376) for a block of 128 queries of one (sequence, head) whose keys
+// fit in 256 columns (every local layer with a half-window up to 64, and
+// global layers up to 256 tokens). Longer key ranges go through
+// attn_attend_kernel (attention.cu), which computes the same bits.
+//
+// One CTA, 6 warps:
+//   warp 0     TMA: Q tile [128 rows][64 B], K and V tiles [128 keys][64 B]
+//              per 128 keys, all SWIZZLE_64B (no multicast).
+//   warp 1     TMEM (256 columns) and the MMAs:
+//                S = Q . K^T     M=128 queries, N=128 keys per tile, K=64
+//                                (kind::i8, Q uint8 q+128, K int8, K-major)
+//                O = P . V       M=128, N=64 dims, K=keys; P uint8 from shared
+//                                memory (K-major, SWIZZLE_128B), V int8 read
+//                                in its natural [keys][dims] layout as an
+//                                MN-major operand. O overwrites S's columns.
+//   warps 2-5  one query row per thread (TMEM lane): dequantize its scores,
+//              MaxOf over the valid keys, ExpShift (vector-body / scalar-tail
+//              split by position), P = rne(e*255), sp = 1/float32(sum P),
+//              P written to shared memory; then O = (float(acc)*vs[d])*sp.
+// Every wait is bounded (mbar_wait), so a lost arrival ends the kernel with
+// an error code instead of a hang.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "exactmath.cuh"
+#include "internal.h"
+
+namespace ig {
+
+constexpr int kAtQ = 128;       // queries per CTA
+constexpr int kAtKT = 128;      // keys per S tile
+constexpr int kAtThreads = 192;
+
+struct AttnTcSmem {
+  static constexpr int kQ = 0;                  // [128][64 B] SW64
+  static constexpr int kK = kQ + 8192;          // 2 x [128][64 B] SW64
+  static constexpr int kV = kK + 16384;         // 2 x [128][64 B] SW64 (MN-major B operand)
+  static constexpr int kP = kV + 16384;         // 2 x [128][128 B] SW128 (1024-aligned)
+  static constexpr int kKs = kP + 32768;        // 256 key scales
+  static constexpr int kKzc = kKs + 1024;       // 256 key zero corrections
+  static constexpr int kBar = kKzc + 1024;      // 4 mbarriers
+  static constexpr int kTmem = kBar + 64;
+  // Requested size: padded so that at most two CTAs share an SM (two x 256
+  // TMEM columns fill the SM's 512).
+  static constexpr int kTotal = 100 * 1024;
+};
+
+// K-major operand with 64-byte rows (SWIZZLE_64B): 8-row groups 512 B apart.
+__device__ __forceinline__ uint64_t smem_desc_k_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)4 << 61;  // SWIZZLE_64B
+  return d;
+}
+
+// MN-major operand whose MN extent is one 64-byte swizzle row (64 int8 values):
+// rows along K are 64 B apart, 8-row groups 512 B apart (SBO). The leading
+// offset (between 64-byte MN atoms) is unused at N = 64; it is set to the
+// V tile size so that it would stay inside the CTA's shared memory.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(16384 >> 4) << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)4 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Block entry: x sequence, y first query, z first key c0 (a multiple of 16),
+// w number of 128-key tiles (1 or 2).
+__global__ void __launch_bounds__(kAtThreads, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                   const __grid_constant__ CUtensorMap mv, const int4 *__restrict__ blocks,
+                   const int32_t *__restrict__ offs, int N, int H, int nh, int window, int V,
+                   const float *__restrict__ sq, const float *__restrict__ ks, const float *__restrict__ kzc,
+                   const float *__restrict__ vs, float *__restrict__ ctx) {
+  using S = AttnTcSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float *s_ks = reinterpret_cast<float *>(smem + S::kKs);
+  float *s_kzc = reinterpret_cast<float *>(smem + S::kKzc);
+  uint64_t *bar_load = reinterpret_cast<uint64_t *>(smem + S::kBar);
+  uint64_t *bar_s = bar_load + 1;
+  uint64_t *bar_p = bar_load + 2;
+  uint64_t *bar_o = bar_load + 3;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::kTmem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int4 blk = blocks[blockIdx.x];
+  const int s = blk.x, i0 = blk.y, c0 = blk.z, nkt = blk.w;
+  const int h = blockIdx.y;
+  const int t0 = offs[s];
+  const int n = offs[s + 1] - t0;
+  const int prow = h * N + t0;  // first row of this sequence in the head plane
+
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&mq);
+    prefetch_tensormap(&mk);
+    prefetch_tensormap(&mv);
+    mbar_init(bar_load, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_p, 128);
+    mbar_init(bar_o, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  if (warp >= 2) {
+    for (int c = threadIdx.x - 64; c < nkt * kAtKT; c += 128) {
+      const int j = c0 + c;
+      s_ks[c] = j < n ? ks[prow + j] : 0.0f;
+      s_kzc[c] = j < n ? kzc[prow + j] : 0.0f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar_load, 8192 + nkt * 16384);
+      tma_load_2d(&mq, smem + S::kQ, bar_load, 0, prow + i0);
+      for (int kt = 0; kt < nkt; kt++) {
+        tma_load_2d(&mk, smem + S::kK + kt * 8192, bar_load, 0, prow + c0 + kt * kAtKT);
+        tma_load_2d(&mv, smem + S::kV + kt * 8192, bar_load, 0, prow + c0 + kt * kAtKT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_u8s8(kAtQ, kAtKT);
+      constexpr uint32_t idesc_o = idesc_u8s8(kAtQ, 64) | (1u << 16);  // B (V) MN-major
+      if (mbar_wait(bar_load, 0, kDevTimeoutFull)) {
+        tc_fence_after();
+        const uint32_t q_base = smem_u32(smem + S::kQ);
+        for (int kt = 0; kt < nkt; kt++) {
+          const uint32_t k_base = smem_u32(smem + S::kK + kt * 8192);
+#pragma unroll
+          for (int kk = 0; kk < 2; kk++)
+            mma_u8s8(tmem + kt * kAtKT, smem_desc_k_sw64(q_base + kk * 32), smem_desc_k_sw64(k_base + kk * 32),
+                     idesc_s, kk);
+        }
+        mma_commit(bar_s);
+        if (mbar_wait(bar_p, 0, kDevTimeoutEmpty)) {
+          tc_fence_after();
+          const uint32_t p_base = smem_u32(smem + S::kP);
+          const uint32_t v_base = smem_u32(smem + S::kV);
+          for (int kt = 0; kt < nkt; kt++) {
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+              mma_u8s8(tmem, smem_desc_k_sw128(p_base + kt * 16384 + kk * 32),
+                       smem_desc_mn_sw64(v_base + (kt * kAtKT + kk * 32) * 64), idesc_o, (kt | kk) != 0);
+          }
+        }
+        mma_commit(bar_o);
+      } else {
+        mma_commit(bar_s);
+        mma_commit(bar_o);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int i = i0 + r;
+    const bool valid = i < n;
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    int js = 0, je = n;
+    if (window >= 0) {
+      js = max(0, i - window);
+      je = min(n, i + window + 1);
+    }
+    const int a = valid ? js - c0 : 0, b = valid ? je - c0 : 0;  // valid columns [a, b)
+    const int len = je - js;
+    const float sqi = valid ? sq[prow + i] : 0.0f;
+    const int nch = nkt * (kAtKT / 32);
+    uint8_t *prow_smem = smem + S::kP + r * 128;
+    bool ok = mbar_wait(bar_s, 0, kDevTimeoutAccum);
+    tc_fence_after();
+    float mx = -INFINITY;
+    int psum = 0;
+    if (ok) {
+      for (int ch = 0; ch < nch; ch++) {
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(tbase + ch * 32, acc);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 32; v++) {
+          const int col = ch * 32 + v;
+          if (col >= a && col < b) mx = fmaxf(mx, dequant1((int32_t)acc[v], s_kzc[col], s_ks[col], sqi));
+        }
+      }
+      for (int ch = 0; ch < nch; ch++) {
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(tbase + ch * 32, acc);
+        tmem_ld_wait();
+        uint32_t w[8];
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int v = g * 4 + u;
+            const int col = ch * 32 + v;
+            uint32_t p = 0;
+            if (col >= a && col < b) {
+              const float sc = dequant1((int32_t)acc[v], s_kzc[col], s_ks[col], sqi);
+              const float e = exp_shift_at(sc, mx, c0 + col - js, len, V);
+              p = (uint32_t)rne_int(__fmul_rn(e, 255.0f));
+              psum += (int)p;
+            }
+            word |= p << (8 * u);
+          }
+          w[g] = word;
+        }
+        // 32 keys = two 16-byte pieces of the row's 128-byte swizzle row.
+        const int kc = ch >> 2;               // 128-key chunk
+        const int piece = (ch & 3) * 2;       // 16-byte piece index in the row
+        uint8_t *base = prow_smem + kc * 16384;
+        *reinterpret_cast<uint4 *>(base + (((piece + 0) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(base + (((piece + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    }
+    tc_fence_before();
+    fence_proxy_async_smem();
+    mbar_arrive(bar_p);
+    const float sp = psum > 0 ? __fdiv_rn(1.0f, (float)psum) : 0.0f;
+    if (ok) ok = mbar_wait(bar_o, 0, kDevTimeoutAccum);
+    tc_fence_after();
+    uint32_t o0[32], o1[32];
+    tmem_ld_32x32b_x32(tbase, o0);
+    tmem_ld_32x32b_x32(tbase + 32, o1);
+    tmem_ld_wait();
+    if (ok && valid) {
+      const float *vsc = vs + ((size_t)s * nh + h) * 64;
+      float *out = ctx + (size_t)(t0 + i) * H + h * 64;
+#pragma unroll
+      for (int d = 0; d < 32; d += 4) {
+        *reinterpret_cast<float4 *>(out + d) =
+            make_float4(dequant1((int32_t)o0[d], 0.0f, __ldg(vsc + d), sp),
+                        dequant1((int32_t)o0[d + 1], 0.0f, __ldg(vsc + d + 1), sp),
+                        dequant1((int32_t)o0[d + 2], 0.0f, __ldg(vsc + d + 2), sp),
+                        dequant1((int32_t)o0[d + 3], 0.0f, __ldg(vsc + d + 3), sp));
+        *reinterpret_cast<float4 *>(out + 32 + d) =
+            make_float4(dequant1((int32_t)o1[d], 0.0f, __ldg(vsc + 32 + d), sp),
+                        dequant1((int32_t)o1[d + 1], 0.0f, __ldg(vsc + 33 + d), sp),
+                        dequant1((int32_t)o1[d + 2], 0.0f, __ldg(vsc + 34 + d), sp),
+                        dequant1((int32_t)o1[d + 3], 0.0f, __ldg(vsc + 35 + d), sp));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// A [rows][64 B] plane as TMA tiles of box_rows x 64 B, SWIZZLE_64B.
+static int make_map_rows64(CUtensorMap *map, const void *base, int rows, int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {64, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {64};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+int attn_tc_fits(int n, int i0, int window, int *c0_out, int *nkt_out) {
+  int c0 = 0, c1 = n;
+  if (window >= 0) {
+    c0 = max(0, i0 - window) & ~15;
+    c1 = min(n, i0 + kAtQ + window);
+  }
+  const int width = c1 - c0;
+  if (width > 2 * kAtKT) return 0;
+  *c0_out = c0;
+  *nkt_out = (width + kAtKT - 1) / kAtKT;
+  return 1;
+}
+
+int attn_tc_query_block() { return kAtQ; }
+
+int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaStream_t st) {
+  if (nblocks <= 0) return 0;
+  if (a.D != 64) return IG_ERR_UNSUPPORTED;
+  const int rows = a.nh * a.N;
+  CUtensorMap mq, mk, mv;
+  if (make_map_rows64(&mq, a.qa, rows, kAtQ) || make_map_rows64(&mk, a.kq, rows, kAtKT) ||
+      make_map_rows64(&mv, a.vq, rows, kAtKT))
+    return IG_ERR_CUDA;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcSmem::kTotal) !=
+        cudaSuccess)
+      return IG_ERR_CUDA;
+    attr = true;
+  }
+  attn_tc_kernel<<<dim3(nblocks, a.nh), kAtThreads, AttnTcSmem::kTotal, st>>>(
+      mq, mk, mv, d_blocks, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx);
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
+}  // namespace ig

@@ -122,10 +122,25 @@ struct DevHead {
   float *w = nullptr, *b = nullptr;
 };
 
+// Host-side plan of one call: offsets, row -> sequence, positions, and for
+// each attention kind (0 global, 1 local) the 128-query blocks the tensor-core
+// kernel takes (x seq, y first query, z first key, w key tiles) and the
+// 16-query blocks of the wider key ranges it leaves to attn_attend_kernel.
 struct Plan {
-  int nseq = 0, N = 0, max_len = 0, nblocks = 0;
+  int nseq = 0, N = 0, max_len = 0;
   std::vector<int32_t> offs, row_seq, pos;
-  std::vector<int2> blocks;
+  std::vector<int4> tc[2];
+  std::vector<int2> v1[2];
+  size_t block_bytes() const {
+    return 16 * (tc[0].size() + tc[1].size()) + 8 * (v1[0].size() + v1[1].size());
+  }
+};
+
+// Device copies of the plan's block lists (inside the workspace).
+struct PlanDev {
+  const int4 *tc[2] = {nullptr, nullptr};
+  const int2 *v1[2] = {nullptr, nullptr};
+  int ntc[2] = {0, 0}, nv1[2] = {0, 0};
 };
 
 // Device buffers of one encode call, sized for `rows` rows and `nseq` sequences.
@@ -138,7 +153,8 @@ struct Workspace {
   cudaStream_t own_stream = nullptr;
   cudaEvent_t done = nullptr;
   int32_t *ids, *offs, *row_seq, *pos;
-  int2 *blocks;
+  char *blocks;  // PlanDev lists
+  PlanDev pd;
   float *x, *xn, *sa, *qkv, *ctx, *g, *sq, *ks, *kzc, *kmean, *vs, *vinv, *pooled;
   uint8_t *xq, *qa;
   int8_t *kq, *vq;
@@ -268,7 +284,9 @@ int ensure_rope(ig_model *m, int npos) {
   return 0;
 }
 
-int make_plan(const int64_t *offs, int nseq, Plan &p) {
+// windows[k]: the half window of attention kind k (-1: global); kinds whose
+// window is < -1 are not planned.
+int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2]) {
   if (nseq < 0 || !offs) return fail(IG_ERR_BAD_ARG, "modernbert: inconsistent batch");
   if (offs[0] != 0) return fail(IG_ERR_BAD_ARG, "modernbert: offs[0] must be 0");
   const int64_t N = offs[nseq];
@@ -278,7 +296,10 @@ int make_plan(const int64_t *offs, int nseq, Plan &p) {
   p.offs.resize(nseq + 1);
   p.row_seq.resize(N);
   p.pos.resize(N);
-  p.blocks.clear();
+  for (int k = 0; k < 2; k++) {
+    p.tc[k].clear();
+    p.v1[k].clear();
+  }
   p.max_len = 0;
   const int qb = attn_query_block();
   for (int s = 0; s < nseq; s++) {
@@ -290,10 +311,19 @@ int make_plan(const int64_t *offs, int nseq, Plan &p) {
       p.row_seq[offs[s] + t] = s;
       p.pos[offs[s] + t] = t;
     }
-    for (int q0 = 0; q0 < n; q0 += qb) p.blocks.push_back(make_int2(s, q0));
+    for (int k = 0; k < 2; k++) {
+      if (windows[k] < -1) continue;
+      for (int i0 = 0; i0 < n; i0 += attn_tc_query_block()) {
+        int c0 = 0, nkt = 0;
+        if (attn_tc_fits(n, i0, windows[k], &c0, &nkt)) {
+          p.tc[k].push_back(make_int4(s, i0, c0, nkt));
+        } else {
+          for (int q0 = i0; q0 < std::min(n, i0 + attn_tc_query_block()); q0 += qb) p.v1[k].push_back(make_int2(s, q0));
+        }
+      }
+    }
   }
   p.offs[nseq] = (int32_t)N;
-  p.nblocks = (int)p.blocks.size();
   return 0;
 }
 
@@ -317,7 +347,7 @@ void carve_ws(Workspace &w, const ig_model *m, char *base, size_t rows, size_t s
   w.offs = c.take<int32_t>(seqs + 1);
   w.row_seq = c.take<int32_t>(rows);
   w.pos = c.take<int32_t>(rows);
-  w.blocks = c.take<int2>(blks);
+  w.blocks = c.take<char>(blks);
   w.x = c.take<float>(rows * H);
   w.xn = c.take<float>(rows * H);
   w.sa = c.take<float>(rows);
@@ -357,7 +387,7 @@ int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st
     IG_CU(cudaEventCreateWithFlags(&w->done, cudaEventDisableTiming));
   }
   const size_t rows = std::max<size_t>(p.N, 1), seqs = std::max<size_t>(p.nseq, 1),
-               blks = std::max<size_t>(p.nblocks, 1);
+               blks = std::max<size_t>(p.block_bytes(), 16);
   if (rows > w->rows_cap || seqs > w->seq_cap || blks > w->blk_cap || tl > w->tl_cap || pl > w->pl_cap) {
     if (capturing) return fail(IG_ERR_BAD_ARG, "workspace must be sized before stream capture");
     IG_CU(cudaEventSynchronize(w->done));
@@ -375,7 +405,7 @@ int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st
     w->tl_cap = t2;
     w->pl_cap = p2;
   }
-  const size_t hb = sizeof(int32_t) * (p.nseq + 1 + 3 * (size_t)p.N) + sizeof(int2) * p.nblocks + 64;
+  const size_t hb = sizeof(int32_t) * (p.nseq + 1 + 3 * (size_t)p.N) + p.block_bytes() + 64;
   if (hb > w->host_bytes) {
     if (capturing) return fail(IG_ERR_BAD_ARG, "workspace must be sized before stream capture");
     IG_CU(cudaEventSynchronize(w->done));
@@ -410,7 +440,8 @@ int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream
   put(p.offs.data(), sizeof(int32_t) * (p.nseq + 1));
   put(p.row_seq.data(), sizeof(int32_t) * p.N);
   put(p.pos.data(), sizeof(int32_t) * p.N);
-  put(p.blocks.data(), sizeof(int2) * p.nblocks);
+  for (int k = 0; k < 2; k++) put(p.tc[k].data(), 16 * p.tc[k].size());
+  for (int k = 0; k < 2; k++) put(p.v1[k].data(), 8 * p.v1[k].size());
   if (host_ids) put(host_ids, sizeof(int32_t) * p.N);
   // The device buffers are carved separately: issue one copy per region
   // from the pinned staging (small, contiguous on the host).
@@ -423,8 +454,20 @@ int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream
     IG_CU(cudaMemcpyAsync(w.pos, h + o, sizeof(int32_t) * p.N, cudaMemcpyHostToDevice, st));
     o += sizeof(int32_t) * p.N;
   }
-  if (p.nblocks) IG_CU(cudaMemcpyAsync(w.blocks, h + o, sizeof(int2) * p.nblocks, cudaMemcpyHostToDevice, st));
-  o += sizeof(int2) * p.nblocks;
+  const size_t bb = p.block_bytes();
+  if (bb) IG_CU(cudaMemcpyAsync(w.blocks, h + o, bb, cudaMemcpyHostToDevice, st));
+  o += bb;
+  size_t bo = 0;
+  for (int k = 0; k < 2; k++) {
+    w.pd.tc[k] = reinterpret_cast<const int4 *>(w.blocks + bo);
+    w.pd.ntc[k] = (int)p.tc[k].size();
+    bo += 16 * p.tc[k].size();
+  }
+  for (int k = 0; k < 2; k++) {
+    w.pd.v1[k] = reinterpret_cast<const int2 *>(w.blocks + bo);
+    w.pd.nv1[k] = (int)p.v1[k].size();
+    bo += 8 * p.v1[k].size();
+  }
   if (host_ids && p.N) IG_CU(cudaMemcpyAsync(w.ids, h + o, sizeof(int32_t) * p.N, cudaMemcpyHostToDevice, st));
   return 0;
 }
@@ -528,7 +571,9 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
     {
       const double pairs = attn_pairs(p, at.window);
       ProfScope ps("attn_attend", (double)N * H * 7 + 12.0 * N * m->nh, 4.0 * pairs * m->D * m->nh, 1, st, capturing);
-      IG_TRY(launch_attend(at, w.blocks, p.nblocks, st));
+      const int kind = global ? 0 : 1;
+      IG_TRY(launch_attend_tc(at, w.pd.tc[kind], w.pd.ntc[kind], st));
+      IG_TRY(launch_attend(at, w.pd.v1[kind], w.pd.nv1[kind], st));
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->ctx, w.ctx, H * 4, H * 4, N, st));
     {
@@ -652,7 +697,8 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS) return fail(IG_ERR_BAD_ARG, "bad mode");
   DeviceGuard dg(m->device);
   Plan p;
-  IG_TRY(make_plan(offs, nseq, p));
+  const int win[2] = {-1, m->cfg.local_attention / 2};
+  IG_TRY(make_plan(offs, nseq, p, win));
   if (p.N > 0 && !ids) return fail(IG_ERR_BAD_ARG, "null ids");
   IG_TRY(check_ids(m, ids, p.N));
   const size_t H = m->H;
@@ -825,7 +871,8 @@ int ig_encode_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int
   IG_CU(cudaStreamIsCapturing(st, &cs));
   const bool capturing = cs != cudaStreamCaptureStatusNone;
   Plan p;
-  IG_TRY(make_plan(offs, nseq, p));
+  const int win[2] = {-1, m->cfg.local_attention / 2};
+  IG_TRY(make_plan(offs, nseq, p, win));
   if (capturing && m->rope_npos < p.max_len) return fail(IG_ERR_BAD_ARG, "run once before capturing");
   IG_TRY(ensure_rope(m, p.max_len));
   Workspace *w = nullptr;
@@ -855,7 +902,8 @@ int ig_logits_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int
   IG_CU(cudaStreamIsCapturing(st, &cs));
   const bool capturing = cs != cudaStreamCaptureStatusNone;
   Plan p;
-  IG_TRY(make_plan(offs, nseq, p));
+  const int win[2] = {-1, m->cfg.local_attention / 2};
+  IG_TRY(make_plan(offs, nseq, p, win));
   if (capturing && m->rope_npos < p.max_len) return fail(IG_ERR_BAD_ARG, "run once before capturing");
   IG_TRY(ensure_rope(m, p.max_len));
   Workspace *w = nullptr;
@@ -989,7 +1037,8 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
   t_last_error.clear();
   if (!qkv || !ctx || !offs || heads <= 0 || hidden % heads) return fail(IG_ERR_BAD_ARG, "bad argument");
   Plan p;
-  IG_TRY(make_plan(offs, nseq, p));
+  const int win[2] = {window < 0 ? -1 : window, -2};
+  IG_TRY(make_plan(offs, nseq, p, win));
   if (p.N == 0) return 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const size_t N = p.N, nh = heads, D = hidden / heads;
@@ -1014,7 +1063,8 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
   };
   int32_t *d_offs = (int32_t *)take(4 * (nseq + 1));
   int32_t *d_rs = (int32_t *)take(4 * N);
-  int2 *d_blk = (int2 *)take(sizeof(int2) * p.nblocks);
+  int4 *d_tc = (int4 *)take(16 * p.tc[0].size());
+  int2 *d_v1 = (int2 *)take(8 * p.v1[0].size());
   a.qa = (uint8_t *)take(N * nh * D);
   a.kq = (int8_t *)take(N * nh * D);
   a.vq = (int8_t *)take(N * nh * D);
@@ -1032,9 +1082,11 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
   if (!rc) {
     cudaMemcpyAsync(d_offs, p.offs.data(), 4 * (nseq + 1), cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(d_rs, p.row_seq.data(), 4 * N, cudaMemcpyHostToDevice, st);
-    cudaMemcpyAsync(d_blk, p.blocks.data(), sizeof(int2) * p.nblocks, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(d_tc, p.tc[0].data(), 16 * p.tc[0].size(), cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(d_v1, p.v1[0].data(), 8 * p.v1[0].size(), cudaMemcpyHostToDevice, st);
     rc = launch_attention(a, st);
-    if (!rc) rc = launch_attend(a, d_blk, p.nblocks, st);
+    if (!rc) rc = launch_attend_tc(a, d_tc, (int)p.tc[0].size(), st);
+    if (!rc) rc = launch_attend(a, d_v1, (int)p.v1[0].size(), st);
     if (rc) fail(rc, "ig_attention launch failed");
   }
   cudaStreamSynchronize(st);

@@ -82,6 +82,11 @@ struct AttnArgs {
 int launch_attention(const AttnArgs &a, cudaStream_t st);
 int launch_attend(const AttnArgs &a, const int2 *d_blocks, int nblocks, cudaStream_t st);
 int attn_query_block();
+// Tensor-core attention (attention_tc.cu): 128-query blocks whose keys span
+// at most 256 columns.
+int attn_tc_fits(int n, int i0, int window, int *c0_out, int *nkt_out);
+int attn_tc_query_block();
+int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaStream_t st);
 
 // Device error flag (kernels' bounded waits).
 int read_device_error(int reset);

@@ -3,5 +3,6 @@
 #include "gemm_i8.cu"
 #include "rows.cu"
 #include "attention.cu"
+#include "attention_tc.cu"
 #include "capi.cu"
 #include "noalloc.cu"
