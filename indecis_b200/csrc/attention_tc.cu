@@ -4,7 +4,7 @@
 // global layers up to 256 tokens). Longer key ranges go through
 // attn_attend_kernel (attention.cu), which computes the same bits.
 //
-// One CTA, 6 warps:
+// One CTA, 10 warps:
 //   warp 0     TMA: Q tile [128 rows][64 B], K and V tiles [128 keys][64 B]
 //              per 128 keys, all SWIZZLE_64B (no multicast).
 //   warp 1     TMEM (256 columns) and the MMAs:
@@ -14,10 +14,12 @@
 //                                memory (K-major, SWIZZLE_128B), V int8 read
 //                                in its natural [keys][dims] layout as an
 //                                MN-major operand. O overwrites S's columns.
-//   warps 2-5  one query row per thread (TMEM lane): dequantize its scores,
-//              MaxOf over the valid keys, ExpShift (vector-body / scalar-tail
-//              split by position), P = rne(e*255), sp = 1/float32(sum P),
-//              P written to shared memory; then O = (float(acc)*vs[d])*sp.
+//   warps 2-9  two warps per query row quarter (TMEM lanes), each taking
+//              alternate 16-key chunks: dequantize the row's scores, MaxOf
+//              over the valid keys (the two halves combined through shared
+//              memory), ExpShift (vector-body / scalar-tail split by position),
+//              P = rne(e*255) into shared memory, sp = 1/float32(sum P); then
+//              O = (float(acc)*vs[d])*sp, each warp 32 of the 64 dimensions.
 // Every wait is bounded (mbar_wait), so a lost arrival ends the kernel with
 // an error code instead of a hang.
 #include <cuda.h>
@@ -32,7 +34,8 @@ namespace ig {
 
 constexpr int kAtQ = 128;       // queries per CTA
 constexpr int kAtKT = 128;      // keys per S tile
-constexpr int kAtThreads = 192;
+constexpr int kAtSoftWarps = 8;  // two per TMEM lane quarter, alternate 16-key chunks
+constexpr int kAtThreads = 64 + 32 * kAtSoftWarps;
 
 struct AttnTcSmem {
   static constexpr int kQ = 0;                  // [128][64 B] SW64
@@ -41,7 +44,8 @@ struct AttnTcSmem {
   static constexpr int kP = kV + 16384;         // 2 x [128][128 B] SW128 (1024-aligned)
   static constexpr int kKs = kP + 32768;        // 256 key scales
   static constexpr int kKzc = kKs + 1024;       // 256 key zero corrections
-  static constexpr int kBar = kKzc + 1024;      // 4 mbarriers
+  static constexpr int kRed = kKzc + 1024;      // row max / P-sum exchange: 2 groups x 128 rows x 8 B
+  static constexpr int kBar = kRed + 2048;      // 4 mbarriers
   static constexpr int kTmem = kBar + 64;
   // Requested size: padded so that at most two CTAs share an SM (two x 256
   // TMEM columns fill the SM's 512).
@@ -77,6 +81,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// The scalar-tail exp (at most V-1 keys per row) out of line, so that the
+// vector-body form alone is evaluated for the other keys.
+__device__ __noinline__ float exp_tail_call(float v) { return exp_tail(v); }
+
 // Block entry: x sequence, y first query, z first key c0 (a multiple of 16),
 // w number of 128-key tiles (1 or 2).
 __global__ void __launch_bounds__(kAtThreads, 2)
@@ -110,13 +122,13 @@ __global__ void __launch_bounds__(kAtThreads, 2)
     prefetch_tensormap(&mv);
     mbar_init(bar_load, 1);
     mbar_init(bar_s, 1);
-    mbar_init(bar_p, 128);
+    mbar_init(bar_p, 32 * kAtSoftWarps);
     mbar_init(bar_o, 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 256);
   if (warp >= 2) {
-    for (int c = threadIdx.x - 64; c < nkt * kAtKT; c += 128) {
+    for (int c = threadIdx.x - 64; c < nkt * kAtKT; c += 32 * kAtSoftWarps) {
       const int j = c0 + c;
       s_ks[c] = j < n ? ks[prow + j] : 0.0f;
       s_kzc[c] = j < n ? kzc[prow + j] : 0.0f;
@@ -169,7 +181,8 @@ __global__ void __launch_bounds__(kAtThreads, 2)
       }
     }
   } else {
-    const int q = warp & 3;
+    const int q = warp & 3;                // TMEM lane quarter: rows [32q, 32q+32)
+    const int g = (warp - 2) >> 2;         // 16-key chunks with parity g
     const int r = q * 32 + lane;
     const int i = i0 + r;
     const bool valid = i < n;
@@ -179,82 +192,84 @@ __global__ void __launch_bounds__(kAtThreads, 2)
       js = max(0, i - window);
       je = min(n, i + window + 1);
     }
-    const int a = valid ? js - c0 : 0, b = valid ? je - c0 : 0;  // valid columns [a, b)
     const int len = je - js;
+    const int body_end = js + (len / V) * V;  // ExpShift: vector body before, exp32 tail after
+    const int a = valid ? js - c0 : 1 << 30, b = valid ? je - c0 : 0;  // valid columns [a, b)
+    // Columns any row of this warp needs, in 16-key chunks [ch0, ch1).
+    const int wa = __reduce_min_sync(0xffffffffu, a), wb = __reduce_max_sync(0xffffffffu, b);
+    const int ch0 = wb > 0 ? wa / 16 : 0, ch1 = wb > 0 ? (wb + 15) / 16 : 0;
+    const int nch = nkt * (kAtKT / 16);
     const float sqi = valid ? sq[prow + i] : 0.0f;
-    const int nch = nkt * (kAtKT / 32);
+    float *red = reinterpret_cast<float *>(smem + S::kRed);  // [2][128] max, then [2][128] P sums
     uint8_t *prow_smem = smem + S::kP + r * 128;
     bool ok = mbar_wait(bar_s, 0, kDevTimeoutAccum);
     tc_fence_after();
     float mx = -INFINITY;
-    int psum = 0;
     if (ok) {
-      for (int ch = 0; ch < nch; ch++) {
-        uint32_t acc[32];
-        tmem_ld_32x32b_x32(tbase + ch * 32, acc);
+      for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2) {
+        uint32_t acc[16];
+        tmem_ld_32x32b_x16(tbase + ch * 16, acc);
         tmem_ld_wait();
 #pragma unroll
-        for (int v = 0; v < 32; v++) {
-          const int col = ch * 32 + v;
+        for (int v = 0; v < 16; v++) {
+          const int col = ch * 16 + v;
           if (col >= a && col < b) mx = fmaxf(mx, dequant1((int32_t)acc[v], s_kzc[col], s_ks[col], sqi));
         }
       }
-      for (int ch = 0; ch < nch; ch++) {
-        uint32_t acc[32];
-        tmem_ld_32x32b_x32(tbase + ch * 32, acc);
-        tmem_ld_wait();
-        uint32_t w[8];
+    }
+    red[g * 128 + r] = mx;
+    named_barrier_sync(1, 32 * kAtSoftWarps);
+    mx = fmaxf(red[r], red[128 + r]);
+    int psum = 0;
+    if (ok) {
+      for (int ch = g; ch < nch; ch += 2) {
+        uint32_t w[4] = {0, 0, 0, 0};
+        if (ch >= ch0 && ch < ch1) {
+          uint32_t acc[16];
+          tmem_ld_32x32b_x16(tbase + ch * 16, acc);
+          tmem_ld_wait();
 #pragma unroll
-        for (int g = 0; g < 8; g++) {
-          uint32_t word = 0;
-#pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const int v = g * 4 + u;
-            const int col = ch * 32 + v;
-            uint32_t p = 0;
+          for (int v = 0; v < 16; v++) {
+            const int col = ch * 16 + v;
             if (col >= a && col < b) {
               const float sc = dequant1((int32_t)acc[v], s_kzc[col], s_ks[col], sqi);
-              const float e = exp_shift_at(sc, mx, c0 + col - js, len, V);
-              p = (uint32_t)rne_int(__fmul_rn(e, 255.0f));
+              const int j = c0 + col;
+              float e = exp_body(__fsub_rn(sc, mx));
+              if (j >= body_end) e = exp_tail_call(__fsub_rn(sc, mx));
+              const uint32_t p = (uint32_t)rne_int(__fmul_rn(e, 255.0f));
               psum += (int)p;
+              w[v >> 2] |= p << (8 * (v & 3));
             }
-            word |= p << (8 * u);
           }
-          w[g] = word;
         }
-        // 32 keys = two 16-byte pieces of the row's 128-byte swizzle row.
-        const int kc = ch >> 2;               // 128-key chunk
-        const int piece = (ch & 3) * 2;       // 16-byte piece index in the row
-        uint8_t *base = prow_smem + kc * 16384;
-        *reinterpret_cast<uint4 *>(base + (((piece + 0) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4 *>(base + (((piece + 1) ^ (r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+        // 16 keys = one 16-byte piece of the row's 128-byte swizzle row.
+        const int kc = ch >> 3, piece = ch & 7;
+        *reinterpret_cast<uint4 *>(prow_smem + kc * 16384 + ((piece ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
     tc_fence_before();
     fence_proxy_async_smem();
     mbar_arrive(bar_p);
+    named_barrier_sync(1, 32 * kAtSoftWarps);  // every thread has read red[] (max)
+    reinterpret_cast<int *>(red)[g * 128 + r] = psum;
+    named_barrier_sync(1, 32 * kAtSoftWarps);
+    psum = reinterpret_cast<int *>(red)[r] + reinterpret_cast<int *>(red)[128 + r];
     const float sp = psum > 0 ? __fdiv_rn(1.0f, (float)psum) : 0.0f;
     if (ok) ok = mbar_wait(bar_o, 0, kDevTimeoutAccum);
     tc_fence_after();
-    uint32_t o0[32], o1[32];
-    tmem_ld_32x32b_x32(tbase, o0);
-    tmem_ld_32x32b_x32(tbase + 32, o1);
+    // Output dimensions [32g, 32g+32) of the row.
+    uint32_t o[32];
+    tmem_ld_32x32b_x32(tbase + 32 * g, o);
     tmem_ld_wait();
     if (ok && valid) {
-      const float *vsc = vs + ((size_t)s * nh + h) * 64;
-      float *out = ctx + (size_t)(t0 + i) * H + h * 64;
+      const float *vsc = vs + ((size_t)s * nh + h) * 64 + 32 * g;
+      float *out = ctx + (size_t)(t0 + i) * H + h * 64 + 32 * g;
 #pragma unroll
       for (int d = 0; d < 32; d += 4) {
+        const float4 sv = __ldg(reinterpret_cast<const float4 *>(vsc + d));
         *reinterpret_cast<float4 *>(out + d) =
-            make_float4(dequant1((int32_t)o0[d], 0.0f, __ldg(vsc + d), sp),
-                        dequant1((int32_t)o0[d + 1], 0.0f, __ldg(vsc + d + 1), sp),
-                        dequant1((int32_t)o0[d + 2], 0.0f, __ldg(vsc + d + 2), sp),
-                        dequant1((int32_t)o0[d + 3], 0.0f, __ldg(vsc + d + 3), sp));
-        *reinterpret_cast<float4 *>(out + 32 + d) =
-            make_float4(dequant1((int32_t)o1[d], 0.0f, __ldg(vsc + 32 + d), sp),
-                        dequant1((int32_t)o1[d + 1], 0.0f, __ldg(vsc + 33 + d), sp),
-                        dequant1((int32_t)o1[d + 2], 0.0f, __ldg(vsc + 34 + d), sp),
-                        dequant1((int32_t)o1[d + 3], 0.0f, __ldg(vsc + 35 + d), sp));
+            make_float4(dequant1((int32_t)o[d], 0.0f, sv.x, sp), dequant1((int32_t)o[d + 1], 0.0f, sv.y, sp),
+                        dequant1((int32_t)o[d + 2], 0.0f, sv.z, sp), dequant1((int32_t)o[d + 3], 0.0f, sv.w, sp));
       }
     }
   }

@@ -318,6 +318,11 @@ static cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, int M
   return cudaGetLastError();
 }
 
+// The persistent TMA-store kernel (gemm_persist.cu); -1 when the output does
+// not suit it.
+static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, int bn, const CUtensorMap &ma,
+                            const CUtensorMap &mb, cudaStream_t st);
+
 int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t st) {
   if (g.M <= 0 || g.N <= 0) return 0;
   if (g.K <= 0 || (g.lda % 16) || (g.ldb % 16) || g.lda < g.K || g.ldb < g.K) return IG_ERR_BAD_ARG;
@@ -329,6 +334,8 @@ int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t s
   CUtensorMap ma, mb;
   if (make_map_u8(&ma, g.A, g.M, g.K, g.lda, kBM) || make_map_u8(&mb, g.B, g.N, g.K, g.ldb, bn))
     return IG_ERR_CUDA;
+  const int prc = gemm_persist_try(g, ep, epi, bn, ma, mb, st);
+  if (prc != -1) return prc;
   cudaError_t e;
 #define IG_GEMM_CASE(E)                                                    \
   case E:                                                                  \

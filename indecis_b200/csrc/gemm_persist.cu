@@ -1,0 +1,435 @@
+// Persistent int8 GEMM: the same arithmetic as gemm_u8s8_kernel (gemm_i8.cu),
+// organised so that memory traffic and tensor-core work overlap:
+//
+//   * one CTA per SM walks the output tiles (tile t, t + gridDim.x, ...);
+//   * the smem ring of A/B K-blocks runs continuously across tiles;
+//   * two TMEM accumulators (2 x BN columns): the MMA warp fills one while
+//     the epilogue warps drain the other;
+//   * the epilogue writes each warp's 32 rows x 32 columns of f32 into a
+//     128-byte-swizzled staging buffer and hands it to a TMA bulk store
+//     (cp.async.bulk.tensor ... bulk_group) — or a TMA reduce-add for the
+//     residual stream x += dequant (the reference's accumulate store,
+//     linalg/kernel_vnni_amd64.s:201-234; float addition commutes, so
+//     x + v is the reference's v + x bit for bit). Double-buffered staging
+//     per warp, recycled with cp.async.bulk.wait_group.read.
+// Requirements (checked by the launcher): C 16-byte aligned with a row stride
+// that is a multiple of 4 elements.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "exactmath.cuh"
+#include "internal.h"
+
+namespace ig {
+
+// Epilogue warps: two per TMEM lane quarter, taking alternate column chunks.
+constexpr int kPEpiWarps = 8;
+constexpr int kPThreads = 64 + 32 * kPEpiWarps;
+
+template <int BN>
+struct PGemmSmem {
+  static constexpr int kStages = BN == 256 ? 3 : 4;
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = BN * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStaging = kStages * kStageBytes;  // per epilogue warp 2 x [32 rows][128 B]
+  static constexpr int kBar = kStaging + kPEpiWarps * 2 * 4096;
+  static constexpr int kTmemSlot = kBar + 8 * (2 * kStages + 4);
+  static constexpr int kTotal = kTmemSlot + 16 + 1024;
+};
+
+// Dequantized accumulators of columns j0..j0+15, the column scales read four
+// at a time (sb, zc 16-byte aligned; columns past N read column N-1 and are
+// clipped by the store).
+__device__ __forceinline__ void dequant16(const uint32_t (&r)[16], const float *__restrict__ sb,
+                                          const float *__restrict__ zc, int j0, int N, float sa, float (&o)[16]) {
+  if (j0 + 16 <= N) {
+#pragma unroll
+    for (int k = 0; k < 16; k += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(sb + j0 + k));
+      const float4 z = __ldg(reinterpret_cast<const float4 *>(zc + j0 + k));
+      o[k] = dequant1((int32_t)r[k], z.x, b.x, sa);
+      o[k + 1] = dequant1((int32_t)r[k + 1], z.y, b.y, sa);
+      o[k + 2] = dequant1((int32_t)r[k + 2], z.z, b.z, sa);
+      o[k + 3] = dequant1((int32_t)r[k + 3], z.w, b.w, sa);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const int j = min(j0 + k, N - 1);
+      o[k] = dequant1((int32_t)r[k], __ldg(zc + j), __ldg(sb + j), sa);
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *smem_src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// One warp's 32 x 32 float sub-tile: thread = row; writes the row into the
+// 128-byte-swizzled staging buffer, then lane 0 issues the bulk store.
+struct StageWriter {
+  uint8_t *bufs;  // two 4 KB buffers
+  int count = 0;
+  __device__ __forceinline__ uint8_t *begin(int lane) {
+    uint8_t *b = bufs + (count & 1) * 4096;
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    return b;
+  }
+  // Both buffers at once (all earlier stores of this warp have read theirs).
+  __device__ __forceinline__ void begin2(int lane, uint8_t **a, uint8_t **b) {
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+    *a = bufs;
+    *b = bufs + 4096;
+  }
+  // Columns [16*half, 16*half+16) of the warp's 32-column row.
+  __device__ __forceinline__ static void put_half(uint8_t *b, int lane, int half, const float (&v)[16]) {
+    uint8_t *row = b + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+      *reinterpret_cast<float4 *>(row + (((half * 4 + j) ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+  __device__ __forceinline__ static void put_row(uint8_t *b, int lane, const float (&v)[32]) {
+    uint8_t *row = b + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      *reinterpret_cast<float4 *>(row + ((j ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+  __device__ __forceinline__ void finish(const CUtensorMap *map, uint8_t *b, int lane, int col, int row0,
+                                         bool reduce_add) {
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      if (reduce_add)
+        tma_reduce_add_2d(map, b, col, row0);
+      else
+        tma_store_2d(map, b, col, row0);
+      bulk_commit();
+    }
+    count++;
+  }
+  // Stores two buffers (one bulk group each), written after begin2.
+  __device__ __forceinline__ void finish2(const CUtensorMap *map, uint8_t *a, uint8_t *b, int lane, int col_a,
+                                          bool store_b, int col_b, int row0) {
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, a, col_a, row0);
+      bulk_commit();
+      if (store_b) {
+        tma_store_2d(map, b, col_b, row0);
+        bulk_commit();
+      }
+    }
+  }
+  __device__ __forceinline__ static void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_persist_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                        const __grid_constant__ CUtensorMap mapC, int M, int N, int K, GemmEpilogue ep) {
+  using S = PGemmSmem<BN>;
+  constexpr int kStages = S::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::kBar);
+  uint64_t *empty = full + kStages;
+  uint64_t *accf = empty + kStages;
+  uint64_t *acce = accf + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::kTmemSlot);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int ntiles = ((M + kBM - 1) / kBM) * tiles_n;
+  const int num_kb = (K + kBK - 1) / kBK;
+
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&mapA);
+    prefetch_tensormap(&mapB);
+    prefetch_tensormap(&mapC);
+    for (int s = 0; s < kStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], kPEpiWarps);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int kbg = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
+        for (int kb = 0; kb < num_kb; kb++, kbg++) {
+          const int s = kbg % kStages;
+          const uint32_t ph = (kbg / kStages) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          uint8_t *a = smem + s * S::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+          tma_load_2d(&mapA, a, &full[s], kb * kBK, m0);
+          tma_load_2d(&mapB, a + S::kABytes, &full[s], kb * kBK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_u8s8(kBM, BN);
+      int kbg = 0, it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, it++) {
+        const int b = it & 1;
+        const uint32_t u = (uint32_t)(it >> 1);
+        if (!mbar_wait(&acce[b], (u & 1) ^ 1, kDevTimeoutEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * BN;
+        for (int kb = 0; kb < num_kb; kb++, kbg++) {
+          const int s = kbg % kStages;
+          const uint32_t ph = (kbg / kStages) & 1;
+          if (!mbar_wait(&full[s], ph, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + s * S::kStageBytes);
+          const uint32_t b_base = a_base + S::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; kk++)
+            mma_u8s8(d, smem_desc_k_sw128(a_base + kk * 32), smem_desc_k_sw128(b_base + kk * 32), idesc,
+                     (kb | kk) != 0);
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&accf[b]);
+      }
+    }
+  } else {
+    const int q = warp & 3;            // TMEM lane quarter
+    const int e = warp - 2;            // epilogue warp 0..7
+    const int g = e >> 2;              // which alternate column chunks
+    StageWriter sw{smem + S::kStaging + e * 8192};
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
+      const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
+      const int b = it & 1;
+      const uint32_t u = (uint32_t)(it >> 1);
+      if (!mbar_wait(&accf[b], u & 1, kDevTimeoutAccum)) break;
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < M;
+      const int row0 = m0 + q * 32;
+      const uint32_t tbase = tmem + b * BN + ((uint32_t)(q * 32) << 16);
+      const float sa = (EPI != kEpiI32 && row_ok) ? __ldg(ep.sa + row) : 0.0f;
+      if constexpr (EPI == kEpiF32 || EPI == kEpiI32) {
+#pragma unroll 1
+        for (int c = g * 32; c < BN; c += 64) {
+          if (n0 + c >= N) continue;
+          uint8_t *buf = sw.begin(lane);
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(tbase + c + 16 * h, r);
+            tmem_ld_wait();
+            float v[16];
+            if constexpr (EPI == kEpiI32) {
+#pragma unroll
+              for (int k = 0; k < 16; k++) v[k] = __int_as_float((int)r[k]);
+            } else {
+              dequant16(r, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, v);
+            }
+            StageWriter::put_half(buf, lane, h, v);
+          }
+          sw.finish(&mapC, buf, lane, n0 + c, row0, EPI == kEpiF32 && ep.accumulate);
+        }
+      } else if constexpr (EPI == kEpiRope) {
+        // Head groups of 64 columns: x1 = [c, c+32), x2 = [c+32, c+64).
+        const int pos = row_ok ? __ldg(ep.pos + row) : 0;
+#pragma unroll 1
+        for (int c = g * 64; c < BN; c += 128) {
+          const int j0 = n0 + c;
+          if (j0 >= N) continue;
+          uint8_t *ba, *bb;
+          sw.begin2(lane, &ba, &bb);
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            uint32_t r1[16], r2[16];
+            tmem_ld_32x32b_x16(tbase + c + 16 * h, r1);
+            tmem_ld_32x32b_x16(tbase + c + 32 + 16 * h, r2);
+            tmem_ld_wait();
+            float x1[16], x2[16];
+            dequant16(r1, ep.sb, ep.zc, j0 + 16 * h, N, sa, x1);
+            dequant16(r2, ep.sb, ep.zc, j0 + 32 + 16 * h, N, sa, x2);
+            if (j0 < ep.rope_cols) {
+              const float4 *cs = reinterpret_cast<const float4 *>(ep.rope_cos + (size_t)pos * 32 + 16 * h);
+              const float4 *sn = reinterpret_cast<const float4 *>(ep.rope_sin + (size_t)pos * 32 + 16 * h);
+#pragma unroll
+              for (int k4 = 0; k4 < 4; k4++) {
+                const float4 co = __ldg(cs + k4), si = __ldg(sn + k4);
+                const float cv[4] = {co.x, co.y, co.z, co.w}, sv[4] = {si.x, si.y, si.z, si.w};
+#pragma unroll
+                for (int m = 0; m < 4; m++) {
+                  const int k = 4 * k4 + m;
+                  const float a = x1[k], bv = x2[k];
+                  x1[k] = __fsub_rn(__fmul_rn(a, cv[m]), __fmul_rn(bv, sv[m]));
+                  x2[k] = __fadd_rn(__fmul_rn(bv, cv[m]), __fmul_rn(a, sv[m]));
+                }
+              }
+            }
+            StageWriter::put_half(ba, lane, h, x1);
+            StageWriter::put_half(bb, lane, h, x2);
+          }
+          sw.finish2(&mapC, ba, bb, lane, j0, j0 + 32 < N, j0 + 32, row0);
+        }
+      } else if constexpr (EPI == kEpiGeglu) {
+        // Tile columns [0, BN/2) are GELU inputs, [BN/2, BN) their gates.
+        constexpr int H2 = BN / 2;
+        const int g0 = n0 / 2;
+#pragma unroll 1
+        for (int c = g * 32; c < H2; c += 64) {
+          if (g0 + c >= ep.geglu_n) continue;
+          uint8_t *buf = sw.begin(lane);
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            uint32_t ra[16], rg[16];
+            tmem_ld_32x32b_x16(tbase + c + 16 * h, ra);
+            tmem_ld_32x32b_x16(tbase + H2 + c + 16 * h, rg);
+            tmem_ld_wait();
+            float a[16], gt[16];
+            dequant16(ra, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, a);
+            dequant16(rg, ep.sb, ep.zc, n0 + H2 + c + 16 * h, N, sa, gt);
+#pragma unroll
+            for (int k = 0; k < 16; k++) a[k] = gelu_mul_at(a[k], gt[k], g0 + c + 16 * h + k, ep.geglu_n);
+            StageWriter::put_half(buf, lane, h, a);
+          }
+          sw.finish(&mapC, buf, lane, g0 + c, row0, false);
+        }
+      }
+      // This accumulator buffer is drained: hand it back to the MMA warp.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[b]);
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
+// f32 (or int32) output [rows][cols] with row stride ld elements: TMA boxes of
+// 32 rows x 32 columns (128-byte rows, 128-byte swizzle).
+static int make_map_out32(CUtensorMap *map, const void *base, int rows, int cols, int ld, bool is_int) {
+  auto enc = get_encode_fn();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, is_int ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                   const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int EPI>
+static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc, int M, int N,
+                                  int K, const GemmEpilogue &ep, cudaStream_t st) {
+  using S = PGemmSmem<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_persist_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         S::kTotal);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int ntiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int grid = ntiles < num_sms() ? ntiles : num_sms();
+  gemm_persist_kernel<BN, EPI><<<grid, kPThreads, S::kTotal, st>>>(ma, mb, mc, M, N, K, ep);
+  return cudaGetLastError();
+}
+
+// Persistent path when the output suits TMA stores; returns -1 to ask the
+// caller for the plain kernel.
+static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, int bn, const CUtensorMap &ma,
+                            const CUtensorMap &mb, cudaStream_t st) {
+  void *out = epi == kEpiI32 ? (void *)ep.acc_out : (void *)ep.C;
+  if (!out || (reinterpret_cast<uintptr_t>(out) & 15) || (ep.ldc & 3)) return -1;
+  if (epi != kEpiI32 && ((reinterpret_cast<uintptr_t>(ep.sb) | reinterpret_cast<uintptr_t>(ep.zc)) & 15)) return -1;
+  if (epi == kEpiRope && ((reinterpret_cast<uintptr_t>(ep.rope_cos) | reinterpret_cast<uintptr_t>(ep.rope_sin)) & 15))
+    return -1;
+  const int out_cols = epi == kEpiGeglu ? ep.geglu_n : g.N;
+  CUtensorMap mc;
+  if (make_map_out32(&mc, out, g.M, out_cols, ep.ldc, epi == kEpiI32)) return IG_ERR_CUDA;
+  cudaError_t e;
+#define IG_PCASE(E)                                                                         \
+  case E:                                                                                   \
+    e = bn == 256 ? launch_persist<256, E>(ma, mb, mc, g.M, g.N, g.K, ep, st)               \
+                  : launch_persist<128, E>(ma, mb, mc, g.M, g.N, g.K, ep, st);              \
+    break;
+  switch (epi) {
+    IG_PCASE(kEpiF32)
+    IG_PCASE(kEpiI32)
+    IG_PCASE(kEpiRope)
+    case kEpiGeglu:
+      e = launch_persist<256, kEpiGeglu>(ma, mb, mc, g.M, g.N, g.K, ep, st);
+      break;
+    default:
+      return IG_ERR_BAD_ARG;
+  }
+#undef IG_PCASE
+  return e == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
+}  // namespace ig

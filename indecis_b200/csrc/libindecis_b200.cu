@@ -1,6 +1,7 @@
 // Single translation unit of libindecis_b200.so: the kernels share device
 // globals (the error flag) without relocatable device code.
 #include "gemm_i8.cu"
+#include "gemm_persist.cu"
 #include "rows.cu"
 #include "attention.cu"
 #include "attention_tc.cu"
