@@ -210,7 +210,113 @@ __global__ void __launch_bounds__(32 * kAttnWarps)
   }
 }
 
+int launch_attention_two_pass(const AttnArgs &a, cudaStream_t st);
+
+// attn_stats followed by attn_quant for one (sequence, head) in one CTA: the
+// statistics pass reads the sequence's K and V columns, the quantization pass
+// re-reads its Q, K and V rows while they are still in L2 (same results).
+__global__ void __launch_bounds__(256)
+    attn_prep_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ offs, int N, int H, int nh, int D,
+                     float scale, float *__restrict__ vs_out, uint8_t *__restrict__ qa, float *__restrict__ sq,
+                     int8_t *__restrict__ kq, float *__restrict__ ks, float *__restrict__ kzc,
+                     int8_t *__restrict__ vq) {
+  __shared__ float s_mean[128], s_vinv[128];
+  const int s = blockIdx.x, h = blockIdx.y;
+  const int t0 = offs[s], n = offs[s + 1] - t0;
+  const size_t ld = 3 * (size_t)H;
+  const int tid = threadIdx.x;
+  if (tid < 2 * D) {
+    const bool is_k = tid < D;
+    const int d = is_k ? tid : tid - D;
+    const float *col = qkv + (size_t)t0 * ld + (is_k ? H : 2 * H) + h * D + d;
+    float acc = 0.0f;
+    int j = 0;
+    if (is_k) {
+      for (; j + 4 <= n; j += 4) {
+        const float k0 = col[(j + 0) * ld], k1 = col[(j + 1) * ld], k2 = col[(j + 2) * ld], k3 = col[(j + 3) * ld];
+        acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, k0), k1), k2), k3);
+      }
+      for (; j < n; j++) acc = __fadd_rn(acc, col[j * ld]);
+      s_mean[d] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
+    } else {
+      for (; j + 4 <= n; j += 4) {
+        const float v0 = col[(j + 0) * ld], v1 = col[(j + 1) * ld], v2 = col[(j + 2) * ld], v3 = col[(j + 3) * ld];
+        acc = fmaxf(fmaxf(fmaxf(fmaxf(acc, fabsf(v0)), fabsf(v1)), fabsf(v2)), fabsf(v3));
+      }
+      for (; j < n; j++) acc = fmaxf(acc, fabsf(col[j * ld]));
+      const float sc = acc > 0.0f ? __fdiv_rn(acc, 127.0f) : 0.0f;
+      vs_out[((size_t)s * nh + h) * D + d] = sc;
+      s_vinv[d] = acc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+    }
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int j = warp; j < n; j += 8) {
+    const int row = t0 + j;
+    const float *base = qkv + (size_t)row * ld + h * D;
+    const size_t plane = (size_t)h * N + row;
+    float qv[4], kv[4], vv[4];
+    float qmx = 0.0f, kmx = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int d = lane + 32 * u;
+      qv[u] = kv[u] = vv[u] = 0.0f;
+      if (d < D) {
+        qv[u] = base[d];
+        kv[u] = __fsub_rn(base[H + d], s_mean[d]);
+        vv[u] = base[2 * H + d];
+        qmx = fmaxf(qmx, fabsf(qv[u]));
+        kmx = fmaxf(kmx, fabsf(kv[u]));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      qmx = fmaxf(qmx, __shfl_xor_sync(0xffffffffu, qmx, o));
+      kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+    }
+    const float qs = qmx > 0.0f ? __fdiv_rn(qmx, 127.0f) : 0.0f;
+    const float qinv = qmx > 0.0f ? __fdiv_rn(1.0f, qs) : 0.0f;
+    const float kss = kmx > 0.0f ? __fdiv_rn(kmx, 127.0f) : 0.0f;
+    const float kinv = kmx > 0.0f ? __fdiv_rn(1.0f, kss) : 0.0f;
+    int ksum = 0;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int d = lane + 32 * u;
+      if (d < D) {
+        int a = qmx > 0.0f ? rne_int(__fmul_rn(qv[u], qinv)) : 0;
+        a = max(-128, min(127, a));
+        qa[plane * D + d] = (uint8_t)(a + 128);
+        int b = 0;
+        if (kmx > 0.0f) {
+          b = rne_int(__fmul_rn(kv[u], kinv));
+          ksum += b;
+          b = max(-128, min(127, b));
+        }
+        kq[plane * D + d] = (int8_t)b;
+        const int c = rne_int(__fmul_rn(vv[u], s_vinv[d]));
+        vq[plane * D + d] = (int8_t)max(-128, min(127, c));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ksum += __shfl_xor_sync(0xffffffffu, ksum, o);
+    if (lane == 0) {
+      sq[plane] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
+      ks[plane] = kss;
+      kzc[plane] = kmx > 0.0f ? __fmul_rn(128.0f, (float)ksum) : 0.0f;
+    }
+  }
+}
+
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
+  if (a.nseq > 0 && a.N > 0 && a.D <= 128 && (a.D % 4) == 0 && a.V >= 1) {
+    attn_prep_kernel<<<dim3(a.nseq, a.nh), 256, 0, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.D, a.scale, a.vs, a.qa,
+                                                          a.sq, a.kq, a.ks, a.kzc, a.vq);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
+  return launch_attention_two_pass(a, st);
+}
+
+int launch_attention_two_pass(const AttnArgs &a, cudaStream_t st) {
   if (a.nseq <= 0 || a.N <= 0) return 0;
   if (a.D > 128 || (a.D % 4) || a.max_len <= 0 || a.V < 1) return IG_ERR_BAD_ARG;
   const int sthreads = a.D <= 128 ? 128 : 256;

@@ -3,6 +3,7 @@
 #include "gemm_i8.cu"
 #include "gemm_persist.cu"
 #include "rows.cu"
+#include "rows_ln.cu"
 #include "attention.cu"
 #include "attention_tc.cu"
 #include "capi.cu"

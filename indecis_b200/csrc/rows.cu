@@ -21,6 +21,11 @@ namespace ig {
 
 constexpr int kRowWarps = 8;
 
+// Several rows per warp (rows_ln.cu); -1 when it does not apply.
+template <bool EMBED>
+static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const float *emb, const float *gamma, int M,
+                           int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa, cudaStream_t st);
+
 // Per-row quantization of the n values in s_row (shared), by one warp.
 __device__ __forceinline__ void quant_row_warp(const float *s_row, int n, uint8_t *q, float *sa, int lane) {
   float mx = 0.0f;
@@ -164,6 +169,29 @@ __global__ void head_logits_kernel(const float *__restrict__ w, const float *__r
   z[(size_t)t * ldz + r] = __dadd_rn(s, (double)b[r]);
 }
 
+// Every row of a head for one token per thread: the rows' sequential float64
+// sums run side by side (heads.go:62-74, same order per row), and the token's
+// x[i] is read once for all rows.
+__global__ void head_logits_rows_kernel(const float *__restrict__ w, const float *__restrict__ b, int rows, int H,
+                                        const float *__restrict__ x, int nx, double *__restrict__ z, int ldz) {
+  constexpr int kMaxRows = 16;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= nx) return;
+  const float *xt = x + (size_t)t * H;
+  double s[kMaxRows];
+#pragma unroll
+  for (int r = 0; r < kMaxRows; r++) s[r] = 0.0;
+  for (int i = 0; i < H; i++) {
+    const double xi = (double)__ldg(xt + i);
+#pragma unroll
+    for (int r = 0; r < kMaxRows; r++)
+      if (r < rows) s[r] = __dadd_rn(s[r], __dmul_rn((double)__ldg(w + (size_t)r * H + i), xi));
+  }
+#pragma unroll
+  for (int r = 0; r < kMaxRows; r++)
+    if (r < rows) z[(size_t)t * ldz + r] = __dadd_rn(s[r], (double)b[r]);
+}
+
 // PackB8 for one packed row per warp.
 __global__ void pack_b8_kernel(const float *__restrict__ w, int n, int k, const int32_t *__restrict__ perm,
                                int n_out, int8_t *__restrict__ q, int ldq, float *__restrict__ scale,
@@ -224,6 +252,10 @@ static int set_rows_smem(const void *fn, int H) {
 int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps, int V, float *xn, uint8_t *q,
                     int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
+  if (gamma) {
+    const int rc = launch_ln_group<false>(x, nullptr, 0, nullptr, gamma, M, H, eps, V, xn, q, ldq, sa, st);
+    if (rc != -1) return rc;
+  }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;
   if (set_rows_smem((const void *)ln_quant_kernel, H)) return IG_ERR_CUDA;
   ln_quant_kernel<<<row_blocks(M), 32 * kRowWarps, H * kRowWarps * sizeof(float), st>>>(x, gamma, M, H, eps, V, xn,
@@ -234,6 +266,10 @@ int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps
 int launch_embed_checked(const int32_t *ids, int vocab, const float *emb, const float *gamma, int M, int H,
                          double eps, int V, float *x, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
+  {
+    const int rc = launch_ln_group<true>(nullptr, ids, vocab, emb, gamma, M, H, eps, V, x, q, ldq, sa, st);
+    if (rc != -1) return rc;
+  }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;
   if (set_rows_smem((const void *)embed_ln_quant_kernel, H)) return IG_ERR_CUDA;
   embed_ln_quant_kernel<<<row_blocks(M), 32 * kRowWarps, H * kRowWarps * sizeof(float), st>>>(
@@ -258,6 +294,10 @@ int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, 
 int launch_head_logits(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z, int ldz,
                        cudaStream_t st) {
   if (nx <= 0 || rows <= 0) return 0;
+  if (rows <= 16 && nx >= 1024) {
+    head_logits_rows_kernel<<<(nx + 127) / 128, 128, 0, st>>>(w, b, rows, H, x, nx, z, ldz);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
   const int total = nx * rows;
   head_logits_kernel<<<(total + 127) / 128, 128, 0, st>>>(w, b, rows, H, x, nx, z, ldz);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
