@@ -193,7 +193,7 @@ IG_API int ig_attention_noalloc(const float *qkv, int32_t hidden, int32_t heads,
 typedef struct ig_dump {
   int32_t layer;
   uint8_t *xq;  float *xq_s;  /* QKV input quantized [N][hidden], [N] */
-  float *qkv;                 /* [N][3*hidden] after RoPE */
+  float *qkv;                 /* [N][3*hidden] QKV projection (RoPE is applied in the attention) */
   float *ctx;                 /* [N][hidden] */
   uint8_t *cq;  float *cq_s;  /* Wo input quantized */
   float *x_attn;              /* residual after attention */

@@ -215,9 +215,13 @@ int launch_attention_two_pass(const AttnArgs &a, cudaStream_t st);
 // attn_stats followed by attn_quant for one (sequence, head) in one CTA: the
 // statistics pass reads the sequence's K and V columns, the quantization pass
 // re-reads its Q, K and V rows while they are still in L2 (same results).
+// With rope tables, q and k are first rotated (rotate_half, no FMA) at the
+// row's position within its sequence, as run() does after the QKV product
+// (internal/modernbert/infer.go:391-399); the K statistics use rotated keys.
 __global__ void __launch_bounds__(256)
     attn_prep_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ offs, int N, int H, int nh, int D,
-                     float scale, float *__restrict__ vs_out, uint8_t *__restrict__ qa, float *__restrict__ sq,
+                     float scale, const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
+                     float *__restrict__ vs_out, uint8_t *__restrict__ qa, float *__restrict__ sq,
                      int8_t *__restrict__ kq, float *__restrict__ ks, float *__restrict__ kzc,
                      int8_t *__restrict__ vq) {
   __shared__ float s_mean[128], s_vinv[128];
@@ -225,7 +229,44 @@ __global__ void __launch_bounds__(256)
   const int t0 = offs[s], n = offs[s + 1] - t0;
   const size_t ld = 3 * (size_t)H;
   const int tid = threadIdx.x;
-  if (tid < 2 * D) {
+  if (rope_cos) {
+    // D = 64. Chunks of 64 keys: every thread loads (and rotates) K and V
+    // values into shared memory, then thread d < 64 continues the ordered
+    // float32 sum of dimension d and thread 64 + d the max of |v[., d]|.
+    __shared__ float s_k[64][64], s_v[64][64];
+    float acc = 0.0f;
+    const float *kbase = qkv + (size_t)t0 * ld + H + h * 64;
+    for (int c0 = 0; c0 < n; c0 += 64) {
+      const int rows = min(64, n - c0);
+#pragma unroll 4
+      for (int e = tid; e < 64 * 64; e += 256) {
+        const int r = e >> 6, d = e & 63;
+        if (r < rows) {
+          const float *kr = kbase + (size_t)(c0 + r) * ld;
+          const int i = d & 31;
+          const float a = kr[d], b = kr[d ^ 32];
+          const float c = __ldg(rope_cos + (size_t)(c0 + r) * 32 + i), sn = __ldg(rope_sin + (size_t)(c0 + r) * 32 + i);
+          s_k[r][d] = d < 32 ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+          s_v[r][d] = kr[H + d];
+        }
+      }
+      __syncthreads();
+      if (tid < 64) {
+        for (int r = 0; r < rows; r++) acc = __fadd_rn(acc, s_k[r][tid]);
+      } else if (tid < 128) {
+        for (int r = 0; r < rows; r++) acc = fmaxf(acc, fabsf(s_v[r][tid - 64]));
+      }
+      __syncthreads();
+    }
+    if (tid < 64) {
+      s_mean[tid] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
+    } else if (tid < 128) {
+      const int d = tid - 64;
+      const float sc = acc > 0.0f ? __fdiv_rn(acc, 127.0f) : 0.0f;
+      vs_out[((size_t)s * nh + h) * 64 + d] = sc;
+      s_vinv[d] = acc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+    }
+  } else if (tid < 2 * D) {
     const bool is_k = tid < D;
     const int d = is_k ? tid : tid - D;
     const float *col = qkv + (size_t)t0 * ld + (is_k ? H : 2 * H) + h * D + d;
@@ -263,8 +304,24 @@ __global__ void __launch_bounds__(256)
       qv[u] = kv[u] = vv[u] = 0.0f;
       if (d < D) {
         qv[u] = base[d];
-        kv[u] = __fsub_rn(base[H + d], s_mean[d]);
+        kv[u] = base[H + d];
         vv[u] = base[2 * H + d];
+      }
+    }
+    if (rope_cos) {
+      // D = 64: lane l holds dimensions l and l + 32, a rotate_half pair.
+      const float c = __ldg(rope_cos + (size_t)j * 32 + lane), sn = __ldg(rope_sin + (size_t)j * 32 + lane);
+      const float q1 = qv[0], q2 = qv[1], k1 = kv[0], k2 = kv[1];
+      qv[0] = __fsub_rn(__fmul_rn(q1, c), __fmul_rn(q2, sn));
+      qv[1] = __fadd_rn(__fmul_rn(q2, c), __fmul_rn(q1, sn));
+      kv[0] = __fsub_rn(__fmul_rn(k1, c), __fmul_rn(k2, sn));
+      kv[1] = __fadd_rn(__fmul_rn(k2, c), __fmul_rn(k1, sn));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int d = lane + 32 * u;
+      if (d < D) {
+        kv[u] = __fsub_rn(kv[u], s_mean[d]);
         qmx = fmaxf(qmx, fabsf(qv[u]));
         kmx = fmaxf(kmx, fabsf(kv[u]));
       }
@@ -307,12 +364,128 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// attn_prep_kernel for sequences of at most kShortSeq tokens and D = 64 with
+// RoPE: the (sequence, head) slices of Q, K and V are staged once in shared
+// memory with 16-byte loads, Q and K rotated there, the ordered K sum and V
+// maxima read from there, and each row quantized from there (one warp per
+// row). Same arithmetic, one pass over qkv.
+constexpr int kShortSeq = 128;
+
+__global__ void __launch_bounds__(256)
+    attn_prep_short_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ offs, int N, int H, int nh,
+                           float scale, const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
+                           float *__restrict__ vs_out, uint8_t *__restrict__ qa, float *__restrict__ sq,
+                           int8_t *__restrict__ kq, float *__restrict__ ks, float *__restrict__ kzc,
+                           int8_t *__restrict__ vq) {
+  extern __shared__ float s_rows[];
+  float(*s_q)[64] = reinterpret_cast<float(*)[64]>(s_rows);
+  float(*s_k)[64] = reinterpret_cast<float(*)[64]>(s_rows + kShortSeq * 64);
+  float(*s_v)[64] = reinterpret_cast<float(*)[64]>(s_rows + 2 * kShortSeq * 64);
+  __shared__ float s_mean[64], s_vinv[64];
+  const int s = blockIdx.x, h = blockIdx.y;
+  const int t0 = offs[s], n = offs[s + 1] - t0;
+  const size_t ld = 3 * (size_t)H;
+  const int tid = threadIdx.x;
+  const float *base = qkv + (size_t)t0 * ld + h * 64;
+  for (int e = tid; e < n * 16; e += 256) {
+    const int r = e >> 4, c = (e & 15) * 4;
+    const float *row = base + (size_t)r * ld + c;
+    *reinterpret_cast<float4 *>(&s_q[r][c]) = __ldg(reinterpret_cast<const float4 *>(row));
+    *reinterpret_cast<float4 *>(&s_k[r][c]) = __ldg(reinterpret_cast<const float4 *>(row + H));
+    *reinterpret_cast<float4 *>(&s_v[r][c]) = __ldg(reinterpret_cast<const float4 *>(row + 2 * H));
+  }
+  __syncthreads();
+  for (int e = tid; e < n * 32; e += 256) {
+    const int r = e >> 5, i = e & 31;
+    const float c = __ldg(rope_cos + (size_t)r * 32 + i), sn = __ldg(rope_sin + (size_t)r * 32 + i);
+    const float q1 = s_q[r][i], q2 = s_q[r][i + 32], k1 = s_k[r][i], k2 = s_k[r][i + 32];
+    s_q[r][i] = __fsub_rn(__fmul_rn(q1, c), __fmul_rn(q2, sn));
+    s_q[r][i + 32] = __fadd_rn(__fmul_rn(q2, c), __fmul_rn(q1, sn));
+    s_k[r][i] = __fsub_rn(__fmul_rn(k1, c), __fmul_rn(k2, sn));
+    s_k[r][i + 32] = __fadd_rn(__fmul_rn(k2, c), __fmul_rn(k1, sn));
+  }
+  __syncthreads();
+  if (tid < 64) {
+    float acc = 0.0f;
+    for (int r = 0; r < n; r++) acc = __fadd_rn(acc, s_k[r][tid]);
+    s_mean[tid] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
+  } else if (tid < 128) {
+    const int d = tid - 64;
+    float mx = 0.0f;
+    for (int r = 0; r < n; r++) mx = fmaxf(mx, fabsf(s_v[r][d]));
+    const float sc = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
+    vs_out[((size_t)s * nh + h) * 64 + d] = sc;
+    s_vinv[d] = mx > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int j = warp; j < n; j += 8) {
+    const size_t plane = (size_t)h * N + t0 + j;
+    const float qv0 = s_q[j][lane], qv1 = s_q[j][lane + 32];
+    const float kv0 = __fsub_rn(s_k[j][lane], s_mean[lane]), kv1 = __fsub_rn(s_k[j][lane + 32], s_mean[lane + 32]);
+    const float vv0 = s_v[j][lane], vv1 = s_v[j][lane + 32];
+    float qmx = fmaxf(fabsf(qv0), fabsf(qv1)), kmx = fmaxf(fabsf(kv0), fabsf(kv1));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      qmx = fmaxf(qmx, __shfl_xor_sync(0xffffffffu, qmx, o));
+      kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+    }
+    const float qs = qmx > 0.0f ? __fdiv_rn(qmx, 127.0f) : 0.0f;
+    const float qinv = qmx > 0.0f ? __fdiv_rn(1.0f, qs) : 0.0f;
+    const float kss = kmx > 0.0f ? __fdiv_rn(kmx, 127.0f) : 0.0f;
+    const float kinv = kmx > 0.0f ? __fdiv_rn(1.0f, kss) : 0.0f;
+    int a0 = 0, a1 = 0, b0 = 0, b1 = 0, ksum = 0;
+    if (qmx > 0.0f) {
+      a0 = max(-128, min(127, rne_int(__fmul_rn(qv0, qinv))));
+      a1 = max(-128, min(127, rne_int(__fmul_rn(qv1, qinv))));
+    }
+    if (kmx > 0.0f) {
+      b0 = rne_int(__fmul_rn(kv0, kinv));
+      b1 = rne_int(__fmul_rn(kv1, kinv));
+      ksum = b0 + b1;
+      b0 = max(-128, min(127, b0));
+      b1 = max(-128, min(127, b1));
+    }
+    const int c0 = max(-128, min(127, rne_int(__fmul_rn(vv0, s_vinv[lane]))));
+    const int c1 = max(-128, min(127, rne_int(__fmul_rn(vv1, s_vinv[lane + 32]))));
+    qa[plane * 64 + lane] = (uint8_t)(a0 + 128);
+    qa[plane * 64 + lane + 32] = (uint8_t)(a1 + 128);
+    kq[plane * 64 + lane] = (int8_t)b0;
+    kq[plane * 64 + lane + 32] = (int8_t)b1;
+    vq[plane * 64 + lane] = (int8_t)c0;
+    vq[plane * 64 + lane + 32] = (int8_t)c1;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ksum += __shfl_xor_sync(0xffffffffu, ksum, o);
+    if (lane == 0) {
+      sq[plane] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
+      ks[plane] = kss;
+      kzc[plane] = kmx > 0.0f ? __fmul_rn(128.0f, (float)ksum) : 0.0f;
+    }
+  }
+}
+
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
-  if (a.nseq > 0 && a.N > 0 && a.D <= 128 && (a.D % 4) == 0 && a.V >= 1) {
-    attn_prep_kernel<<<dim3(a.nseq, a.nh), 256, 0, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.D, a.scale, a.vs, a.qa,
-                                                          a.sq, a.kq, a.ks, a.kzc, a.vq);
+  if (a.rope_cos && a.D != 64) return IG_ERR_UNSUPPORTED;
+  if (a.rope_cos && a.nseq > 0 && a.N > 0 && a.max_len <= kShortSeq && (a.H % 4) == 0) {
+    const int smem = 3 * kShortSeq * 64 * (int)sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+      if (cudaFuncSetAttribute(attn_prep_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+          cudaSuccess)
+        return IG_ERR_CUDA;
+      attr = true;
+    }
+    attn_prep_short_kernel<<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.scale,
+                                                                   a.rope_cos, a.rope_sin, a.vs, a.qa, a.sq, a.kq,
+                                                                   a.ks, a.kzc, a.vq);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
+  if (a.nseq > 0 && a.N > 0 && a.D <= 128 && (a.D % 4) == 0 && a.V >= 1) {
+    attn_prep_kernel<<<dim3(a.nseq, a.nh), 256, 0, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.D, a.scale, a.rope_cos,
+                                                          a.rope_sin, a.vs, a.qa, a.sq, a.kq, a.ks, a.kzc, a.vq);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
+  if (a.rope_cos) return IG_ERR_UNSUPPORTED;
   return launch_attention_two_pass(a, st);
 }
 

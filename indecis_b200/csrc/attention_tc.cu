@@ -211,9 +211,13 @@ __global__ void __launch_bounds__(kAtThreads, 2)
         tmem_ld_32x32b_x16(tbase + ch * 16, acc);
         tmem_ld_wait();
 #pragma unroll
-        for (int v = 0; v < 16; v++) {
+        for (int v = 0; v < 16; v += 2) {
           const int col = ch * 16 + v;
-          if (col >= a && col < b) mx = fmaxf(mx, dequant1((int32_t)acc[v], s_kzc[col], s_ks[col], sqi));
+          const float2 sc = dequant2((int32_t)acc[v], (int32_t)acc[v + 1],
+                                     *reinterpret_cast<const float2 *>(s_kzc + col),
+                                     *reinterpret_cast<const float2 *>(s_ks + col), sqi);
+          if (col >= a && col < b) mx = fmaxf(mx, sc.x);
+          if (col + 1 >= a && col + 1 < b) mx = fmaxf(mx, sc.y);
         }
       }
     }
@@ -229,17 +233,23 @@ __global__ void __launch_bounds__(kAtThreads, 2)
           tmem_ld_32x32b_x16(tbase + ch * 16, acc);
           tmem_ld_wait();
 #pragma unroll
-          for (int v = 0; v < 16; v++) {
+          for (int v = 0; v < 16; v += 2) {
             const int col = ch * 16 + v;
-            if (col >= a && col < b) {
-              const float sc = dequant1((int32_t)acc[v], s_kzc[col], s_ks[col], sqi);
-              const int j = c0 + col;
-              float e = exp_body(__fsub_rn(sc, mx));
-              if (j >= body_end) e = exp_tail_call(__fsub_rn(sc, mx));
-              const uint32_t p = (uint32_t)rne_int(__fmul_rn(e, 255.0f));
-              psum += (int)p;
-              w[v >> 2] |= p << (8 * (v & 3));
-            }
+            const float2 sc = dequant2((int32_t)acc[v], (int32_t)acc[v + 1],
+                                       *reinterpret_cast<const float2 *>(s_kzc + col),
+                                       *reinterpret_cast<const float2 *>(s_ks + col), sqi);
+            // Scalar subtraction: a packed add after the packed product above
+            // could be fused into one rounding.
+            const float2 x = make_float2(__fsub_rn(sc.x, mx), __fsub_rn(sc.y, mx));
+            float2 e = exp_body2(x);
+            const int j = c0 + col;
+            if (j >= body_end && j < je) e.x = exp_tail_call(x.x);
+            if (j + 1 >= body_end && j + 1 < je) e.y = exp_tail_call(x.y);
+            const float2 e255 = __fmul2_rn(e, f2(255.0f));
+            const uint32_t p0 = (col >= a && col < b) ? (uint32_t)rne_int(e255.x) : 0u;
+            const uint32_t p1 = (col + 1 >= a && col + 1 < b) ? (uint32_t)rne_int(e255.y) : 0u;
+            psum += (int)(p0 + p1);
+            w[v >> 2] |= (p0 | (p1 << 8)) << (8 * (v & 3));
           }
         }
         // 16 keys = one 16-byte piece of the row's 128-byte swizzle row.

@@ -554,18 +554,16 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       e.zc = L.qkv.zc;
       e.C = w.qkv;
       e.ldc = 3 * H;
-      e.pos = w.pos;
-      e.rope_cos = m->rope_cos[global ? 0 : 1];
-      e.rope_sin = m->rope_sin[global ? 0 : 1];
-      e.rope_cols = 2 * H;
-      ProfScope ps("gemm_qkv_rope", gemm_bytes(N, 3 * H, H, 4.0 * 3 * H) + 8.0 * N, 2.0 * N * 3 * H * H, 1, st,
-                   capturing);
-      IG_TRY(gemm_u8s8(g, e, kEpiRope, st));
+      ProfScope ps("gemm_qkv", gemm_bytes(N, 3 * H, H, 4.0 * 3 * H), 2.0 * N * 3 * H * H, 1, st, capturing);
+      IG_TRY(gemm_u8s8(g, e, kEpiF32, st));
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->qkv, w.qkv, 3 * H * 4, 3 * H * 4, N, st));
     at.window = global ? -1 : c.local_attention / 2;
+    at.rope_cos = m->rope_cos[global ? 0 : 1];
+    at.rope_sin = m->rope_sin[global ? 0 : 1];
     {
-      ProfScope ps("attn_prep", (double)N * H * 4 * 5 + (double)N * H * 3 + 12.0 * N * m->nh, 0, 2, st, capturing);
+      ProfScope ps("attn_prep", (double)N * H * 4 * 3 + (double)N * H * 3 + 12.0 * N * m->nh + 8.0 * N * 32, 0, 1, st,
+                   capturing);
       IG_TRY(launch_attention(at, st));
     }
     {

@@ -54,6 +54,64 @@ __device__ __forceinline__ float exp_shift_at(float x, float m, int t, int len, 
   return t < (len / V) * V ? exp_body(v) : exp_tail(v);
 }
 
+// ---- two lanes at once (f32x2: each lane rounds exactly as the scalar op) ----
+// Caution: a packed add fed directly by a packed multiply may be contracted
+// into one fused multiply-add by the compiler (the scalar __f*_rn intrinsics
+// are never contracted). The helpers below have no multiply-then-add step;
+// callers that subtract from a packed product use the scalar __fsub_rn.
+
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
+// exp_body for two values (a - b is a + (-b) in IEEE arithmetic).
+__device__ __forceinline__ float2 exp_body2(float2 v) {
+  const bool u0 = v.x < -87.3f, u1 = v.y < -87.3f;
+  v.x = fminf(fmaxf(v.x, -87.3f), 88.7f);
+  v.y = fminf(fmaxf(v.y, -87.3f), 88.7f);
+  const float2 n = __fadd2_rn(__ffma2_rn(v, f2(1.44269504088896341f), f2(12582912.0f)), f2(-12582912.0f));
+  float2 r = __ffma2_rn(n, f2(-0.693359375f), v);
+  r = __ffma2_rn(n, f2(2.12194440e-4f), r);
+  float2 p = __ffma2_rn(r, f2(1.9875691500e-4f), f2(1.3981999507e-3f));
+  p = __ffma2_rn(r, p, f2(8.3334519073e-3f));
+  p = __ffma2_rn(r, p, f2(4.1665795894e-2f));
+  p = __ffma2_rn(r, p, f2(1.6666665459e-1f));
+  p = __ffma2_rn(r, p, f2(5.0000001201e-1f));
+  const float2 y = __fadd2_rn(__ffma2_rn(__fmul2_rn(p, r), r, r), f2(1.0f));
+  const float2 pw = make_float2(__int_as_float((__float2int_rn(n.x) + 127) << 23),
+                                __int_as_float((__float2int_rn(n.y) + 127) << 23));
+  const float2 e = __fmul2_rn(y, pw);
+  return make_float2(u0 ? 0.0f : e.x, u1 ? 0.0f : e.y);
+}
+
+// ((float(acc) - zc) * sb) * sa for two columns.
+__device__ __forceinline__ float2 dequant2(int32_t a0, int32_t a1, float2 zc, float2 sb, float sa) {
+  float2 v = __fadd2_rn(make_float2(__int2float_rn(a0), __int2float_rn(a1)), make_float2(-zc.x, -zc.y));
+  v = __fmul2_rn(v, sb);
+  return __fmul2_rn(v, f2(sa));
+}
+
+// gelu_mul_fma for two elements.
+__device__ __forceinline__ float2 gelu_mul_fma2(float2 x, float2 gate) {
+  float2 t = __fmul2_rn(x, f2(0.7071067811865476f));
+  t.x = fminf(fmaxf(t.x, -4.0f), 4.0f);
+  t.y = fminf(fmaxf(t.y, -4.0f), 4.0f);
+  const float2 t2 = __fmul2_rn(t, t);
+  float2 p = __ffma2_rn(t2, f2(-2.72614225801306e-10f), f2(2.77068142495902e-08f));
+  p = __ffma2_rn(t2, p, f2(-2.10102402082508e-06f));
+  p = __ffma2_rn(t2, p, f2(-5.69250639462346e-05f));
+  p = __ffma2_rn(t2, p, f2(-7.34990630326855e-04f));
+  p = __ffma2_rn(t2, p, f2(-2.95459980854025e-03f));
+  p = __ffma2_rn(t2, p, f2(-1.60960333262415e-02f));
+  p = __fmul2_rn(p, t);
+  float2 q = __ffma2_rn(t2, f2(-1.45660718464996e-05f), f2(-2.13374055278905e-04f));
+  q = __ffma2_rn(t2, q, f2(-1.68282697438203e-03f));
+  q = __ffma2_rn(t2, q, f2(-7.37332916720468e-03f));
+  q = __ffma2_rn(t2, q, f2(-1.42647390514189e-02f));
+  float2 r = make_float2(__fdiv_rn(p.x, q.x), __fdiv_rn(p.y, q.y));
+  r = __fadd2_rn(r, f2(1.0f));
+  const float2 g = __fmul2_rn(r, __fmul2_rn(x, f2(0.5f)));
+  return __fmul2_rn(g, gate);
+}
+
 // geluMulAVX2 for one element (gelu_amd64.s:176-200).
 __device__ __forceinline__ float gelu_mul_fma(float x, float gate) {
   float t = __fmul_rn(x, 0.7071067811865476f);

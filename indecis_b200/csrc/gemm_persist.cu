@@ -50,10 +50,13 @@ __device__ __forceinline__ void dequant16(const uint32_t (&r)[16], const float *
     for (int k = 0; k < 16; k += 4) {
       const float4 b = __ldg(reinterpret_cast<const float4 *>(sb + j0 + k));
       const float4 z = __ldg(reinterpret_cast<const float4 *>(zc + j0 + k));
-      o[k] = dequant1((int32_t)r[k], z.x, b.x, sa);
-      o[k + 1] = dequant1((int32_t)r[k + 1], z.y, b.y, sa);
-      o[k + 2] = dequant1((int32_t)r[k + 2], z.z, b.z, sa);
-      o[k + 3] = dequant1((int32_t)r[k + 3], z.w, b.w, sa);
+      const float2 lo = dequant2((int32_t)r[k], (int32_t)r[k + 1], make_float2(z.x, z.y), make_float2(b.x, b.y), sa);
+      const float2 hi =
+          dequant2((int32_t)r[k + 2], (int32_t)r[k + 3], make_float2(z.z, z.w), make_float2(b.z, b.w), sa);
+      o[k] = lo.x;
+      o[k + 1] = lo.y;
+      o[k + 2] = hi.x;
+      o[k + 3] = hi.y;
     }
   } else {
 #pragma unroll
@@ -333,8 +336,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
             float a[16], gt[16];
             dequant16(ra, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, a);
             dequant16(rg, ep.sb, ep.zc, n0 + H2 + c + 16 * h, N, sa, gt);
+            const int i0 = g0 + c + 16 * h;  // GeGLU column of a[0]
+            if (i0 + 16 <= (ep.geglu_n & ~15)) {
 #pragma unroll
-            for (int k = 0; k < 16; k++) a[k] = gelu_mul_at(a[k], gt[k], g0 + c + 16 * h + k, ep.geglu_n);
+              for (int k = 0; k < 16; k += 2) {
+                const float2 o2 = gelu_mul_fma2(make_float2(a[k], a[k + 1]), make_float2(gt[k], gt[k + 1]));
+                a[k] = o2.x;
+                a[k + 1] = o2.y;
+              }
+            } else {
+#pragma unroll
+              for (int k = 0; k < 16; k++) a[k] = gelu_mul_at(a[k], gt[k], i0 + k, ep.geglu_n);
+            }
             StageWriter::put_half(buf, lane, h, a);
           }
           sw.finish(&mapC, buf, lane, g0 + c, row0, false);

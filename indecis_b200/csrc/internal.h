@@ -58,13 +58,16 @@ int launch_pack_b8(const float *w, int n, int k, const int32_t *perm, int n_out,
 
 // ---- attention (attention.cu) ----
 struct AttnArgs {
-  const float *qkv;     // [N][3H] rows after RoPE
+  const float *qkv;     // [N][3H] q, k, v rows
   int H, nh, D;
   const int32_t *offs;  // [nseq+1] row offsets (device)
   int nseq;
   int max_len;          // longest sequence
   int window;           // half window, < 0: global
   float scale;          // 1/sqrt(D)
+  // RoPE (Rope, linalg/vec_simd.go:404-425) of q and k at each row's position
+  // in its sequence, applied while preparing; null when qkv is already rotated.
+  const float *rope_cos, *rope_sin;  // [positions][D/2]
   int V;                // lanes of ExpShift
   // work buffers (device)
   uint8_t *qa;          // [nh][N][D]

@@ -185,13 +185,14 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
       matmul_rows(m->qkv[l], in, &qkv[(size_t)lo * 3 * H], hi - lo, false, use_fast, s,
                   dl && dump->xq ? dump->xq + (size_t)lo * H : nullptr, dl && dump->xq_s ? dump->xq_s + lo : nullptr,
                   dl && dump->qkv_acc ? dump->qkv_acc + (size_t)lo * 3 * H : nullptr);
+      if (dl && dump->qkv)
+        std::memcpy(dump->qkv + (size_t)lo * 3 * H, &qkv[(size_t)lo * 3 * H], sizeof(float) * (hi - lo) * 3 * H);
       for (int r = lo; r < hi; r++) {
         const int t = pos[r];
         float *row = &qkv[(size_t)r * 3 * H];
         for (int h = 0; h < 2 * nh; h++) rope(row + h * D, &rc[(size_t)t * half], &rs[(size_t)t * half], half);
       }
     });
-    if (dl && dump->qkv) std::memcpy(dump->qkv, qkv.data(), sizeof(float) * N * 3 * H);
 
     // attention8 (infer.go:484-518): prepare per (sequence, head), attend per
     // block of queries.

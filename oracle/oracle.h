@@ -119,7 +119,7 @@ typedef struct {
   int layer;
   uint8_t *xq;      float *xq_s;   /* QKV input, quantized [N][H], [N] */
   int32_t *qkv_acc;                /* [N][3H] */
-  float *qkv;                      /* [N][3H] after RoPE */
+  float *qkv;                      /* [N][3H] QKV projection, before RoPE */
   float *ctx;                      /* [N][H] attention output */
   uint8_t *cq;      float *cq_s;   /* Wo input quantized */
   float *x_attn;                   /* [N][H] residual after attention */
