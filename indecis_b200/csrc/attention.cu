@@ -406,8 +406,17 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
   if (tid < 64) {
+    // Ordered float32 sum over the keys; loads run ahead of the adds.
     float acc = 0.0f;
-    for (int r = 0; r < n; r++) acc = __fadd_rn(acc, s_k[r][tid]);
+    int r = 0;
+    for (; r + 8 <= n; r += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = s_k[r + u][tid];
+#pragma unroll
+      for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, v[u]);
+    }
+    for (; r < n; r++) acc = __fadd_rn(acc, s_k[r][tid]);
     s_mean[tid] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
   } else if (tid < 128) {
     const int d = tid - 64;
@@ -418,15 +427,29 @@ __global__ void __launch_bounds__(256)
     s_vinv[d] = mx > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
   }
   __syncthreads();
+  // Four rows per warp: lanes 8g..8g+7 take row j + g, eight dimensions each.
   const int warp = tid >> 5, lane = tid & 31;
-  for (int j = warp; j < n; j += 8) {
-    const size_t plane = (size_t)h * N + t0 + j;
-    const float qv0 = s_q[j][lane], qv1 = s_q[j][lane + 32];
-    const float kv0 = __fsub_rn(s_k[j][lane], s_mean[lane]), kv1 = __fsub_rn(s_k[j][lane + 32], s_mean[lane + 32]);
-    const float vv0 = s_v[j][lane], vv1 = s_v[j][lane + 32];
-    float qmx = fmaxf(fabsf(qv0), fabsf(qv1)), kmx = fmaxf(fabsf(kv0), fabsf(kv1));
+  const int g = lane >> 3, d0 = (lane & 7) * 8;
+  for (int j0 = warp * 4; j0 < n; j0 += 32) {
+    const int j = j0 + g;
+    const bool ok = j < n;
+    const int jr = ok ? j : 0;
+    float qv[8], kv[8], vv[8];
+    *reinterpret_cast<float4 *>(qv) = *reinterpret_cast<const float4 *>(&s_q[jr][d0]);
+    *reinterpret_cast<float4 *>(qv + 4) = *reinterpret_cast<const float4 *>(&s_q[jr][d0 + 4]);
+    *reinterpret_cast<float4 *>(kv) = *reinterpret_cast<const float4 *>(&s_k[jr][d0]);
+    *reinterpret_cast<float4 *>(kv + 4) = *reinterpret_cast<const float4 *>(&s_k[jr][d0 + 4]);
+    *reinterpret_cast<float4 *>(vv) = *reinterpret_cast<const float4 *>(&s_v[jr][d0]);
+    *reinterpret_cast<float4 *>(vv + 4) = *reinterpret_cast<const float4 *>(&s_v[jr][d0 + 4]);
+    float qmx = 0.0f, kmx = 0.0f;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
+    for (int u = 0; u < 8; u++) {
+      kv[u] = __fsub_rn(kv[u], s_mean[d0 + u]);
+      qmx = fmaxf(qmx, fabsf(qv[u]));
+      kmx = fmaxf(kmx, fabsf(kv[u]));
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1) {
       qmx = fmaxf(qmx, __shfl_xor_sync(0xffffffffu, qmx, o));
       kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
     }
@@ -434,32 +457,34 @@ __global__ void __launch_bounds__(256)
     const float qinv = qmx > 0.0f ? __fdiv_rn(1.0f, qs) : 0.0f;
     const float kss = kmx > 0.0f ? __fdiv_rn(kmx, 127.0f) : 0.0f;
     const float kinv = kmx > 0.0f ? __fdiv_rn(1.0f, kss) : 0.0f;
-    int a0 = 0, a1 = 0, b0 = 0, b1 = 0, ksum = 0;
-    if (qmx > 0.0f) {
-      a0 = max(-128, min(127, rne_int(__fmul_rn(qv0, qinv))));
-      a1 = max(-128, min(127, rne_int(__fmul_rn(qv1, qinv))));
-    }
-    if (kmx > 0.0f) {
-      b0 = rne_int(__fmul_rn(kv0, kinv));
-      b1 = rne_int(__fmul_rn(kv1, kinv));
-      ksum = b0 + b1;
-      b0 = max(-128, min(127, b0));
-      b1 = max(-128, min(127, b1));
-    }
-    const int c0 = max(-128, min(127, rne_int(__fmul_rn(vv0, s_vinv[lane]))));
-    const int c1 = max(-128, min(127, rne_int(__fmul_rn(vv1, s_vinv[lane + 32]))));
-    qa[plane * 64 + lane] = (uint8_t)(a0 + 128);
-    qa[plane * 64 + lane + 32] = (uint8_t)(a1 + 128);
-    kq[plane * 64 + lane] = (int8_t)b0;
-    kq[plane * 64 + lane + 32] = (int8_t)b1;
-    vq[plane * 64 + lane] = (int8_t)c0;
-    vq[plane * 64 + lane + 32] = (int8_t)c1;
+    uint32_t qw[2] = {0, 0}, kw[2] = {0, 0}, vw[2] = {0, 0};
+    int ksum = 0;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) ksum += __shfl_xor_sync(0xffffffffu, ksum, o);
-    if (lane == 0) {
-      sq[plane] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
-      ks[plane] = kss;
-      kzc[plane] = kmx > 0.0f ? __fmul_rn(128.0f, (float)ksum) : 0.0f;
+    for (int u = 0; u < 8; u++) {
+      int a = 0, b = 0;
+      if (qmx > 0.0f) a = max(-128, min(127, rne_int(__fmul_rn(qv[u], qinv))));
+      if (kmx > 0.0f) {
+        b = rne_int(__fmul_rn(kv[u], kinv));
+        ksum += b;
+        b = max(-128, min(127, b));
+      }
+      const int c = max(-128, min(127, rne_int(__fmul_rn(vv[u], s_vinv[d0 + u]))));
+      qw[u >> 2] |= (uint32_t)(a + 128) << (8 * (u & 3));
+      kw[u >> 2] |= (uint32_t)(b & 0xff) << (8 * (u & 3));
+      vw[u >> 2] |= (uint32_t)(c & 0xff) << (8 * (u & 3));
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1) ksum += __shfl_xor_sync(0xffffffffu, ksum, o);
+    if (ok) {
+      const size_t plane = (size_t)h * N + t0 + j;
+      *reinterpret_cast<uint2 *>(qa + plane * 64 + d0) = make_uint2(qw[0], qw[1]);
+      *reinterpret_cast<uint2 *>(kq + plane * 64 + d0) = make_uint2(kw[0], kw[1]);
+      *reinterpret_cast<uint2 *>(vq + plane * 64 + d0) = make_uint2(vw[0], vw[1]);
+      if ((lane & 7) == 0) {
+        sq[plane] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
+        ks[plane] = kss;
+        kzc[plane] = kmx > 0.0f ? __fmul_rn(128.0f, (float)ksum) : 0.0f;
+      }
     }
   }
 }
