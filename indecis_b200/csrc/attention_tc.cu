@@ -85,9 +85,120 @@ __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// The scalar-tail exp (at most V-1 keys per row) out of line, so that the
-// vector-body form alone is evaluated for the other keys.
-__device__ __noinline__ float exp_tail_call(float v) { return exp_tail(v); }
+
+// One query row's view of a tile of scores: valid key columns [a, b) and the
+// columns [t0, t1) that take the scalar-tail exp (ExpShift's last len % V
+// keys), all relative to the tile's first key; sq is the row's scale.
+struct ScoreRow {
+  int a, b, t0, t1;
+  float sq;
+};
+
+// MaxOf over the valid columns of the 16-key chunk at TMEM column tcol.
+// zcm holds 128*sum(kq) + 1.5*2^23 per key (dequant2m).
+__device__ __forceinline__ float chunk_max(uint32_t tcol, int c, const float *zcm, const float *ks,
+                                           const ScoreRow &w, float mx) {
+  uint32_t acc[16];
+  tmem_ld_32x32b_x16(tcol, acc);
+  tmem_ld_wait();
+  const bool inner = __all_sync(0xffffffffu, c >= w.a && c + 16 <= w.b);
+#pragma unroll
+  for (int v = 0; v < 16; v += 4) {
+    const float4 z = *reinterpret_cast<const float4 *>(zcm + c + v);
+    const float4 k = *reinterpret_cast<const float4 *>(ks + c + v);
+    const float2 s0 = dequant2m((int32_t)acc[v], (int32_t)acc[v + 1], make_float2(z.x, z.y), make_float2(k.x, k.y), w.sq);
+    const float2 s1 =
+        dequant2m((int32_t)acc[v + 2], (int32_t)acc[v + 3], make_float2(z.z, z.w), make_float2(k.z, k.w), w.sq);
+    if (inner) {
+      mx = fmaxf(mx, fmaxf(fmaxf(s0.x, s0.y), fmaxf(s1.x, s1.y)));
+    } else {
+      const int col = c + v;
+      if (col >= w.a && col < w.b) mx = fmaxf(mx, s0.x);
+      if (col + 1 >= w.a && col + 1 < w.b) mx = fmaxf(mx, s0.y);
+      if (col + 2 >= w.a && col + 2 < w.b) mx = fmaxf(mx, s1.x);
+      if (col + 3 >= w.a && col + 3 < w.b) mx = fmaxf(mx, s1.y);
+    }
+  }
+  return mx;
+}
+
+// The quantized softmax weights P = rne(exp(score - mx) * 255) of the 16-key
+// chunk at TMEM column tcol as 16 bytes (0 outside the row's valid keys), all
+// with ExpShift's vector-body exp (tail_fixup then rewrites the row's
+// scalar-tail keys); the sum of the 16 is added to psum. The subtraction is
+// scalar: a packed add after the packed product of dequant2m could be fused
+// into one rounding.
+__device__ __forceinline__ uint4 chunk_p(uint32_t tcol, int c, const float *zcm, const float *ks, const ScoreRow &w,
+                                        float mx, int &psum) {
+  uint32_t acc[16];
+  tmem_ld_32x32b_x16(tcol, acc);
+  tmem_ld_wait();
+  uint32_t bits[16];  // 0x4B400000 + P (low byte P)
+  const bool inner = __all_sync(0xffffffffu, c >= w.a && c + 16 <= w.b);
+#pragma unroll
+  for (int v = 0; v < 16; v += 4) {
+    const float4 z = *reinterpret_cast<const float4 *>(zcm + c + v);
+    const float4 k = *reinterpret_cast<const float4 *>(ks + c + v);
+#pragma unroll
+    for (int h = 0; h < 4; h += 2) {
+      const float2 sc = dequant2m((int32_t)acc[v + h], (int32_t)acc[v + h + 1],
+                                  h ? make_float2(z.z, z.w) : make_float2(z.x, z.y),
+                                  h ? make_float2(k.z, k.w) : make_float2(k.x, k.y), w.sq);
+      const uint2 b = exp_p_bits2(make_float2(__fsub_rn(sc.x, mx), __fsub_rn(sc.y, mx)));
+      bits[v + h] = b.x;
+      bits[v + h + 1] = b.y;
+      if (!inner) {
+        const int col = c + v + h;
+        if (!(col >= w.a && col < w.b)) bits[v + h] = (uint32_t)kMagicBits;
+        if (!(col + 1 >= w.a && col + 1 < w.b)) bits[v + h + 1] = (uint32_t)kMagicBits;
+      }
+    }
+  }
+  uint32_t word[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    word[k] = __byte_perm(__byte_perm(bits[4 * k], bits[4 * k + 1], 0x0040),
+                          __byte_perm(bits[4 * k + 2], bits[4 * k + 3], 0x0040), 0x5410);
+    psum = dp4a_us(word[k], 0x01010101u, psum);
+  }
+  return make_uint4(word[0], word[1], word[2], word[3]);
+}
+
+// ExpShift's scalar-tail keys [t0, t1) of query row r (its last len % V
+// keys; at most V - 1) that lie in this thread's 16-key chunks (parity g):
+// the int32 score is recomputed on the CUDA cores from the quantized Q and K
+// rows in shared memory (the same dot product the tensor cores formed; both
+// tiles [rows][64 B] SWIZZLE_64B, key tiles ktile_bytes apart), dequantized
+// as in chunk_p, and P = rne(exp32(score - mx) * 255) replaces the byte the
+// chunk pass wrote into P ([128 rows][128 B] SWIZZLE_128B per 128 keys).
+// Returns the change of the row's P sum.
+__device__ __noinline__ int tail_fixup(const uint8_t *qtile, const uint8_t *ktile, int ktile_bytes, uint8_t *ptile,
+                                       int r, int g, int t0, int t1, const float *zcm, const float *ks, float sq,
+                                       float mx) {
+  int dsum = 0;  // change of the row's P sum
+  for (int c = t0; c < t1; c++) {
+    if (((c >> 4) & 1) != g) continue;
+    const int kt = c >> 7, kr = c & 127;
+    const uint8_t *qrow = qtile + r * 64;
+    const uint8_t *krow = ktile + kt * ktile_bytes + kr * 64;
+    int acc = 0;
+#pragma unroll
+    for (int ch = 0; ch < 4; ch++) {
+      const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + ((ch ^ ((r >> 1) & 3)) << 4));
+      const uint4 kb = *reinterpret_cast<const uint4 *>(krow + ((ch ^ ((kr >> 1) & 3)) << 4));
+      acc = dp4a_us(qa.x, kb.x, acc);
+      acc = dp4a_us(qa.y, kb.y, acc);
+      acc = dp4a_us(qa.z, kb.z, acc);
+      acc = dp4a_us(qa.w, kb.w, acc);
+    }
+    const float sc = __fmul_rn(__fmul_rn(__fsub_rn(magic_float(acc), zcm[c]), ks[c]), sq);
+    const int p = __float2int_rn(__fmul_rn(exp_tail(__fsub_rn(sc, mx)), 255.0f));
+    uint8_t *pb = ptile + kt * 16384 + r * 128 + ((((c & 127) >> 4) ^ (r & 7)) << 4) + (c & 15);
+    dsum += p - (int)*pb;
+    *pb = (uint8_t)p;
+  }
+  return dsum;
+}
 
 // Block entry: x sequence, y first query, z first key c0 (a multiple of 16),
 // w number of 128-key tiles (1 or 2).
@@ -131,7 +242,7 @@ __global__ void __launch_bounds__(kAtThreads, 2)
     for (int c = threadIdx.x - 64; c < nkt * kAtKT; c += 32 * kAtSoftWarps) {
       const int j = c0 + c;
       s_ks[c] = j < n ? ks[prow + j] : 0.0f;
-      s_kzc[c] = j < n ? kzc[prow + j] : 0.0f;
+      s_kzc[c] = __fadd_rn(j < n ? kzc[prow + j] : 0.0f, kMagic);
     }
   }
   tc_fence_before();
@@ -194,32 +305,24 @@ __global__ void __launch_bounds__(kAtThreads, 2)
     }
     const int len = je - js;
     const int body_end = js + (len / V) * V;  // ExpShift: vector body before, exp32 tail after
-    const int a = valid ? js - c0 : 1 << 30, b = valid ? je - c0 : 0;  // valid columns [a, b)
+    ScoreRow w;
+    w.a = valid ? js - c0 : 1 << 30;  // valid columns [a, b)
+    w.b = valid ? je - c0 : 0;
+    w.t0 = valid ? body_end - c0 : 0;
+    w.t1 = valid ? je - c0 : 0;
+    w.sq = valid ? sq[prow + i] : 0.0f;
     // Columns any row of this warp needs, in 16-key chunks [ch0, ch1).
-    const int wa = __reduce_min_sync(0xffffffffu, a), wb = __reduce_max_sync(0xffffffffu, b);
+    const int wa = __reduce_min_sync(0xffffffffu, w.a), wb = __reduce_max_sync(0xffffffffu, w.b);
     const int ch0 = wb > 0 ? wa / 16 : 0, ch1 = wb > 0 ? (wb + 15) / 16 : 0;
     const int nch = nkt * (kAtKT / 16);
-    const float sqi = valid ? sq[prow + i] : 0.0f;
     float *red = reinterpret_cast<float *>(smem + S::kRed);  // [2][128] max, then [2][128] P sums
     uint8_t *prow_smem = smem + S::kP + r * 128;
     bool ok = mbar_wait(bar_s, 0, kDevTimeoutAccum);
+    ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
     tc_fence_after();
     float mx = -INFINITY;
     if (ok) {
-      for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2) {
-        uint32_t acc[16];
-        tmem_ld_32x32b_x16(tbase + ch * 16, acc);
-        tmem_ld_wait();
-#pragma unroll
-        for (int v = 0; v < 16; v += 2) {
-          const int col = ch * 16 + v;
-          const float2 sc = dequant2((int32_t)acc[v], (int32_t)acc[v + 1],
-                                     *reinterpret_cast<const float2 *>(s_kzc + col),
-                                     *reinterpret_cast<const float2 *>(s_ks + col), sqi);
-          if (col >= a && col < b) mx = fmaxf(mx, sc.x);
-          if (col + 1 >= a && col + 1 < b) mx = fmaxf(mx, sc.y);
-        }
-      }
+      for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2) mx = chunk_max(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx);
     }
     red[g * 128 + r] = mx;
     named_barrier_sync(1, 32 * kAtSoftWarps);
@@ -227,35 +330,14 @@ __global__ void __launch_bounds__(kAtThreads, 2)
     int psum = 0;
     if (ok) {
       for (int ch = g; ch < nch; ch += 2) {
-        uint32_t w[4] = {0, 0, 0, 0};
-        if (ch >= ch0 && ch < ch1) {
-          uint32_t acc[16];
-          tmem_ld_32x32b_x16(tbase + ch * 16, acc);
-          tmem_ld_wait();
-#pragma unroll
-          for (int v = 0; v < 16; v += 2) {
-            const int col = ch * 16 + v;
-            const float2 sc = dequant2((int32_t)acc[v], (int32_t)acc[v + 1],
-                                       *reinterpret_cast<const float2 *>(s_kzc + col),
-                                       *reinterpret_cast<const float2 *>(s_ks + col), sqi);
-            // Scalar subtraction: a packed add after the packed product above
-            // could be fused into one rounding.
-            const float2 x = make_float2(__fsub_rn(sc.x, mx), __fsub_rn(sc.y, mx));
-            float2 e = exp_body2(x);
-            const int j = c0 + col;
-            if (j >= body_end && j < je) e.x = exp_tail_call(x.x);
-            if (j + 1 >= body_end && j + 1 < je) e.y = exp_tail_call(x.y);
-            const float2 e255 = __fmul2_rn(e, f2(255.0f));
-            const uint32_t p0 = (col >= a && col < b) ? (uint32_t)rne_int(e255.x) : 0u;
-            const uint32_t p1 = (col + 1 >= a && col + 1 < b) ? (uint32_t)rne_int(e255.y) : 0u;
-            psum += (int)(p0 + p1);
-            w[v >> 2] |= (p0 | (p1 << 8)) << (8 * (v & 3));
-          }
-        }
+        uint4 pw = make_uint4(0, 0, 0, 0);
+        if (ch >= ch0 && ch < ch1) pw = chunk_p(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx, psum);
         // 16 keys = one 16-byte piece of the row's 128-byte swizzle row.
         const int kc = ch >> 3, piece = ch & 7;
-        *reinterpret_cast<uint4 *>(prow_smem + kc * 16384 + ((piece ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(prow_smem + kc * 16384 + ((piece ^ (r & 7)) << 4)) = pw;
       }
+      if (w.t0 < w.t1)
+        psum += tail_fixup(smem + S::kQ, smem + S::kK, 8192, smem + S::kP, r, g, w.t0, w.t1, s_kzc, s_ks, w.sq, mx);
     }
     tc_fence_before();
     fence_proxy_async_smem();

@@ -561,17 +561,24 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
     at.window = global ? -1 : c.local_attention / 2;
     at.rope_cos = m->rope_cos[global ? 0 : 1];
     at.rope_sin = m->rope_sin[global ? 0 : 1];
-    {
-      ProfScope ps("attn_prep", (double)N * H * 4 * 3 + (double)N * H * 3 + 12.0 * N * m->nh + 8.0 * N * 32, 0, 1, st,
-                   capturing);
-      IG_TRY(launch_attention(at, st));
-    }
-    {
+    if (attn_short_fits(at)) {
       const double pairs = attn_pairs(p, at.window);
-      ProfScope ps("attn_attend", (double)N * H * 7 + 12.0 * N * m->nh, 4.0 * pairs * m->D * m->nh, 1, st, capturing);
-      const int kind = global ? 0 : 1;
-      IG_TRY(launch_attend_tc(at, w.pd.tc[kind], w.pd.ntc[kind], st));
-      IG_TRY(launch_attend(at, w.pd.v1[kind], w.pd.nv1[kind], st));
+      ProfScope ps("attn_short", (double)N * H * 4 * 4 + 8.0 * N * 32, 4.0 * pairs * m->D * m->nh, 1, st, capturing);
+      IG_TRY(launch_attn_short(at, st));
+    } else {
+      {
+        ProfScope ps("attn_prep", (double)N * H * 4 * 3 + (double)N * H * 3 + 12.0 * N * m->nh + 8.0 * N * 32, 0, 1,
+                     st, capturing);
+        IG_TRY(launch_attention(at, st));
+      }
+      {
+        const double pairs = attn_pairs(p, at.window);
+        ProfScope ps("attn_attend", (double)N * H * 7 + 12.0 * N * m->nh, 4.0 * pairs * m->D * m->nh, 1, st,
+                     capturing);
+        const int kind = global ? 0 : 1;
+        IG_TRY(launch_attend_tc(at, w.pd.tc[kind], w.pd.ntc[kind], st));
+        IG_TRY(launch_attend(at, w.pd.v1[kind], w.pd.nv1[kind], st));
+      }
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->ctx, w.ctx, H * 4, H * 4, N, st));
     {
@@ -1082,9 +1089,13 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
     cudaMemcpyAsync(d_rs, p.row_seq.data(), 4 * N, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(d_tc, p.tc[0].data(), 16 * p.tc[0].size(), cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(d_v1, p.v1[0].data(), 8 * p.v1[0].size(), cudaMemcpyHostToDevice, st);
-    rc = launch_attention(a, st);
-    if (!rc) rc = launch_attend_tc(a, d_tc, (int)p.tc[0].size(), st);
-    if (!rc) rc = launch_attend(a, d_v1, (int)p.v1[0].size(), st);
+    if (attn_short_fits(a)) {
+      rc = launch_attn_short(a, st);
+    } else {
+      rc = launch_attention(a, st);
+      if (!rc) rc = launch_attend_tc(a, d_tc, (int)p.tc[0].size(), st);
+      if (!rc) rc = launch_attend(a, d_v1, (int)p.v1[0].size(), st);
+    }
     if (rc) fail(rc, "ig_attention launch failed");
   }
   cudaStreamSynchronize(st);

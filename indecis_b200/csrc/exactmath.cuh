@@ -62,12 +62,31 @@ __device__ __forceinline__ float exp_shift_at(float x, float m, int t, int len, 
 
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
-// exp_body for two values (a - b is a + (-b) in IEEE arithmetic).
-__device__ __forceinline__ float2 exp_body2(float2 v) {
-  const bool u0 = v.x < -87.3f, u1 = v.y < -87.3f;
-  v.x = fminf(fmaxf(v.x, -87.3f), 88.7f);
-  v.y = fminf(fmaxf(v.y, -87.3f), 88.7f);
-  const float2 n = __fadd2_rn(__ffma2_rn(v, f2(1.44269504088896341f), f2(12582912.0f)), f2(-12582912.0f));
+// Integer <-> float without a conversion instruction (those run at an eighth
+// of the FP32 rate). For an integer |v| < 2^22 the bits 0x4B400000 + v are the
+// float 1.5*2^23 + v exactly; and for a float |x| < 2^22, x + 1.5*2^23 is
+// rounded to nearest-even at unit spacing, so its bits minus 0x4B400000 are
+// rne(x), the value __float2int_rn gives.
+constexpr float kMagic = 12582912.0f;
+constexpr int kMagicBits = 0x4B400000;
+__device__ __forceinline__ float magic_float(int32_t v) { return __int_as_float(kMagicBits + v); }
+__device__ __forceinline__ int magic_rne(float x) { return __float_as_int(__fadd_rn(x, kMagic)) - kMagicBits; }
+
+// The softmax weight bits of ExpShift's vector body for two scores:
+// 0x4B400000 + P with P = rne(RN(e * 255)), e = exp_body(v), for v <= 0 (a
+// score minus its row's maximum). Every P equals rne(RN(exp_body(v) * 255)):
+//   - the upper clamp cannot apply; below -87.3, exp_body's 0 and the value
+//     at the clamp both give e*255 < 0.5, so P = 0 either way;
+//   - e = y * 2^n (y the polynomial, n from t = v*log2e + 1.5*2^23, whose
+//     bits hold 0x4B400000 + n) is exact while normal, so RN(e * 255) = RN(y * 255) * 2^n,
+//     and RN(RN(y * 255) * 2^n + 1.5*2^23) (one fused step, the product being
+//     exact) holds rne of it in its low bits; where e or e*255 would be
+//     subnormal both sides give P = 0.
+__device__ __forceinline__ uint2 exp_p_bits2(float2 v) {
+  v.x = fmaxf(v.x, -87.3f);
+  v.y = fmaxf(v.y, -87.3f);
+  const float2 t = __ffma2_rn(v, f2(1.44269504088896341f), f2(kMagic));
+  const float2 n = __fadd2_rn(t, f2(-kMagic));
   float2 r = __ffma2_rn(n, f2(-0.693359375f), v);
   r = __ffma2_rn(n, f2(2.12194440e-4f), r);
   float2 p = __ffma2_rn(r, f2(1.9875691500e-4f), f2(1.3981999507e-3f));
@@ -76,10 +95,21 @@ __device__ __forceinline__ float2 exp_body2(float2 v) {
   p = __ffma2_rn(r, p, f2(1.6666665459e-1f));
   p = __ffma2_rn(r, p, f2(5.0000001201e-1f));
   const float2 y = __fadd2_rn(__ffma2_rn(__fmul2_rn(p, r), r, r), f2(1.0f));
-  const float2 pw = make_float2(__int_as_float((__float2int_rn(n.x) + 127) << 23),
-                                __int_as_float((__float2int_rn(n.y) + 127) << 23));
-  const float2 e = __fmul2_rn(y, pw);
-  return make_float2(u0 ? 0.0f : e.x, u1 ? 0.0f : e.y);
+  const float2 z = __fmul2_rn(y, f2(255.0f));
+  // 2^n from t's bits (0x4B400000 + n): (n + 127) << 23.
+  const float2 pw = make_float2(__int_as_float((__float_as_int(t.x) << 23) + ((127 - kMagicBits) << 23)),
+                                __int_as_float((__float_as_int(t.y) << 23) + ((127 - kMagicBits) << 23)));
+  const float2 b = __ffma2_rn(z, pw, f2(kMagic));
+  return make_uint2(__float_as_uint(b.x), __float_as_uint(b.y));
+}
+
+// dequant2 for |acc| < 2^22 with zcm = zc + 1.5*2^23 (exact while
+// |zc| < 2^22): (1.5*2^23 + acc) - zcm is acc - zc, an integer below 2^23 in
+// magnitude, so it is exact, as float(acc) - zc is.
+__device__ __forceinline__ float2 dequant2m(int32_t a0, int32_t a1, float2 zcm, float2 sb, float sa) {
+  float2 v = __fadd2_rn(make_float2(magic_float(a0), magic_float(a1)), make_float2(-zcm.x, -zcm.y));
+  v = __fmul2_rn(v, sb);
+  return __fmul2_rn(v, f2(sa));
 }
 
 // ((float(acc) - zc) * sb) * sa for two columns.

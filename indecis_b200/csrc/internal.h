@@ -90,6 +90,10 @@ int attn_query_block();
 int attn_tc_fits(int n, int i0, int window, int *c0_out, int *nkt_out);
 int attn_tc_query_block();
 int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaStream_t st);
+// Prepare + attend in one kernel (attention_short.cu): D = 64, sequences of at
+// most 128 tokens, H a multiple of 4; RoPE applied when rope_cos is set.
+bool attn_short_fits(const AttnArgs &a);
+int launch_attn_short(const AttnArgs &a, cudaStream_t st);
 
 // Device error flag (kernels' bounded waits).
 int read_device_error(int reset);

@@ -6,5 +6,6 @@
 #include "rows_ln.cu"
 #include "attention.cu"
 #include "attention_tc.cu"
+#include "attention_short.cu"
 #include "capi.cu"
 #include "noalloc.cu"
