@@ -180,7 +180,13 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // ---- exact arithmetic helpers ------------------------------------------------
 
 // Round to nearest even, as VCVTPS2DQ and linalg/int8.go:205-210 roundHalfEven.
-__device__ __forceinline__ int rne_int(float v) { return __float2int_rn(v); }
+// Float -> int32 as VCVTPS2DQ converts under round-to-nearest-even, the
+// conversion of the reference's quantRowAVX2 / quantColsAVX2: NaN and values
+// outside the int32 range give INT_MIN ("integer indefinite"), where
+// __float2int_rn alone would saturate (and give 0 for NaN).
+__device__ __forceinline__ int rne_int(float v) {
+  return fabsf(v) < 2147483648.0f ? __float2int_rn(v) : (int)0x80000000u;
+}
 
 // ((float(acc) - zc) * sb) * sa: the reference's dequant order, no FMA
 // (linalg/kernel_vnni_amd64.s:144-200).

@@ -62,6 +62,14 @@ __device__ __forceinline__ float exp_shift_at(float x, float m, int t, int len, 
 
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
+// max(a, b) that returns NaN when either input is NaN (fmaxf ignores NaN).
+// A row maximum taken with it is NaN exactly when the row holds a NaN.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
 // Integer <-> float without a conversion instruction (those run at an eighth
 // of the FP32 rate). For an integer |v| < 2^22 the bits 0x4B400000 + v are the
 // float 1.5*2^23 + v exactly; and for a float |x| < 2^22, x + 1.5*2^23 is

@@ -2,6 +2,7 @@
 // globals (the error flag) without relocatable device code.
 #include "gemm_i8.cu"
 #include "gemm_persist.cu"
+#include "rows_fast.cu"
 #include "rows.cu"
 #include "rows_ln.cu"
 #include "attention.cu"

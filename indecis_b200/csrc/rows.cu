@@ -253,7 +253,9 @@ int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps
                     int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
   if (gamma) {
-    const int rc = launch_ln_group<false>(x, nullptr, 0, nullptr, gamma, M, H, eps, V, xn, q, ldq, sa, st);
+    int rc = launch_ln8<false>(x, nullptr, 0, nullptr, gamma, M, H, eps, V, xn, q, ldq, sa, st);
+    if (rc != -1) return rc;
+    rc = launch_ln_group<false>(x, nullptr, 0, nullptr, gamma, M, H, eps, V, xn, q, ldq, sa, st);
     if (rc != -1) return rc;
   }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;
@@ -267,7 +269,9 @@ int launch_embed_checked(const int32_t *ids, int vocab, const float *emb, const 
                          double eps, int V, float *x, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
   {
-    const int rc = launch_ln_group<true>(nullptr, ids, vocab, emb, gamma, M, H, eps, V, x, q, ldq, sa, st);
+    int rc = launch_ln8<true>(nullptr, ids, vocab, emb, gamma, M, H, eps, V, x, q, ldq, sa, st);
+    if (rc != -1) return rc;
+    rc = launch_ln_group<true>(nullptr, ids, vocab, emb, gamma, M, H, eps, V, x, q, ldq, sa, st);
     if (rc != -1) return rc;
   }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;
@@ -279,6 +283,10 @@ int launch_embed_checked(const int32_t *ids, int vocab, const float *emb, const 
 
 int launch_quant_rows(const float *x, int ldx, int M, int K, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
+  {
+    const int rc = launch_quant_rows4(x, ldx, M, K, q, ldq, sa, st);
+    if (rc != -1) return rc;
+  }
   if (!smem_rows_ok(K)) return IG_ERR_BAD_ARG;
   if (set_rows_smem((const void *)quant_rows_kernel, K)) return IG_ERR_CUDA;
   quant_rows_kernel<<<row_blocks(M), 32 * kRowWarps, K * kRowWarps * sizeof(float), st>>>(x, ldx, M, K, q, ldq, sa);

@@ -1,0 +1,229 @@
+// Row kernels with the row width fixed at compile time: LayerNorm (+ int8
+// quantization) for the reference's V = 8 float32 lanes, and per-row
+// quantization of float4-aligned rows. Same arithmetic, in the same order, as
+// ln_group_kernel (rows_ln.cu) and quant_row_warp (rows.cu), which restate
+// linalg/vec_simd.go:281-327 and linalg/int8.go:157-191.
+//
+// LayerNorm: a warp takes 4 rows; lane (r, k) = 8r + k holds elements
+// k, k+8, ..., k+8(NB-1) of row r in registers, which is exactly the
+// reference's lane-k chain, so the ordered sums run without shared memory.
+// The 8 partial sums are combined in float64 in lane order through shuffles.
+// Quantized bytes go through a small shared buffer so that each row leaves
+// in 16-byte stores.
+//
+// Quantization: for a normal scale s = max/127 (max > 0), |x / s| stays
+// below 127 + 2^-20, so rne(x * inv) never needs the int8 clamp and is the
+// low byte of RN(x * inv) + (1.5*2^23 + 128) (q + 128). Rows holding a NaN
+// (found by a NaN-propagating maximum) and other scales take the clamped
+// path, whose conversion follows the reference's (NaN -> INT_MIN).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "exactmath.cuh"
+#include "internal.h"
+
+namespace ig {
+
+__device__ __forceinline__ bool row_scale_normal(float s) { return s >= 1.17549435e-38f && s <= 3.40282347e38f; }
+
+// Byte q + 128 of one value of a row whose maximum is not 0 (clamped path:
+// any scale).
+__device__ __forceinline__ uint32_t quant_byte_slow(float v, float inv) {
+  return (uint32_t)(max(-128, min(127, rne_int(__fmul_rn(v, inv)))) + 128);
+}
+
+template <int NB, bool EMBED>
+__global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, const int32_t *__restrict__ ids,
+                                                  int vocab, const float *__restrict__ emb,
+                                                  const float *__restrict__ gamma, int M, double eps,
+                                                  float *__restrict__ xout, uint8_t *__restrict__ q, int ldq,
+                                                  float *__restrict__ sa) {
+  constexpr int H = 8 * NB;
+  constexpr int QP = H + 8;  // byte pitch: the 4 rows' bytes of one step land in distinct banks
+  __shared__ __align__(16) uint8_t s_q[8][4][QP];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 3, k = lane & 7;
+  const int row = (blockIdx.x * 8 + warp) * 4 + r;
+  const bool rv = row < M;
+  const float *src;
+  if constexpr (EMBED) {
+    int id = rv ? ids[row] : 0;
+    if (id < 0 || id >= vocab) {
+      set_device_error(kDevBadId);
+      id = 0;
+    }
+    src = emb + (size_t)id * H;
+  } else {
+    src = x + (size_t)(rv ? row : 0) * H;
+  }
+  float v[NB];
+#pragma unroll
+  for (int b = 0; b < NB; b++) v[b] = rv ? __ldg(src + k + 8 * b) : 0.0f;
+  float ls = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NB; b++) ls = __fadd_rn(ls, v[b]);
+  double sum = 0.0;
+#pragma unroll
+  for (int kk = 0; kk < 8; kk++) sum = __dadd_rn(sum, (double)__shfl_sync(0xffffffffu, ls, (r << 3) | kk));
+  const float mean = __double2float_rn(__ddiv_rn(sum, (double)H));
+  float lq = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    v[b] = __fsub_rn(v[b], mean);
+    lq = __fmaf_rn(v[b], v[b], lq);
+  }
+  double var = 0.0;
+#pragma unroll
+  for (int kk = 0; kk < 8; kk++) var = __dadd_rn(var, (double)__shfl_sync(0xffffffffu, lq, (r << 3) | kk));
+  const float rstd = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(var, (double)H), eps))));
+  float mx = 0.0f;  // NaN-propagating here; the NaN-ignoring maximum is taken again below if needed
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    v[b] = __fmul_rn(__fmul_rn(v[b], rstd), __ldg(gamma + k + 8 * b));
+    mx = fmax_nan(mx, fabsf(v[b]));
+  }
+  if (xout && rv) {
+    float *dst = xout + (size_t)row * H + k;
+#pragma unroll
+    for (int b = 0; b < NB; b++) dst[8 * b] = v[b];
+  }
+  if (!q) return;
+  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+  const bool has_nan = mx != mx;
+  if (__any_sync(0xffffffffu, has_nan)) {  // the maximum over the non-NaN values (rows without NaN: the same)
+    mx = 0.0f;
+#pragma unroll
+    for (int b = 0; b < NB; b++) mx = fmaxf(mx, fabsf(v[b]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+  }
+  float scale = 0.0f, inv = 0.0f;
+  if (mx > 0.0f) {
+    scale = __fdiv_rn(mx, 127.0f);
+    inv = __fdiv_rn(1.0f, scale);
+  }
+  if (k == 0 && rv) sa[row] = scale;
+  uint8_t *sq = s_q[warp][r];
+  if (mx == 0.0f) {  // a zero row quantizes to 128s (linalg/int8.go:157-191)
+#pragma unroll
+    for (int b = 0; b < NB; b++) sq[k + 8 * b] = 128;
+  } else if (!has_nan && row_scale_normal(scale)) {
+#pragma unroll
+    for (int b = 0; b < NB; b++) sq[k + 8 * b] = (uint8_t)__float_as_uint(__fadd_rn(__fmul_rn(v[b], inv), kMagic + 128.0f));
+  } else {
+#pragma unroll
+    for (int b = 0; b < NB; b++) sq[k + 8 * b] = (uint8_t)quant_byte_slow(v[b], inv);
+  }
+  __syncwarp();
+  if (rv) {
+    uint8_t *dq = q + (size_t)row * ldq;
+    for (int c = k; c < H / 8; c += 8)
+      *reinterpret_cast<uint2 *>(dq + 8 * c) = *reinterpret_cast<const uint2 *>(sq + 8 * c);
+  }
+}
+
+// One warp per row; lane takes float4 chunks lane, lane + 32, ... (K % 4 == 0).
+template <int NJ>
+__global__ void __launch_bounds__(256) quant_rows4_kernel(const float *__restrict__ x, int ldx, int M, int K,
+                                                          uint8_t *__restrict__ q, int ldq, float *__restrict__ sa) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * ldx);
+  const int nq = K >> 2;
+  float4 v[NJ];
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NJ; j++) {
+    const int c = lane + 32 * j;
+    v[j] = c < nq ? __ldg(src + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+#pragma unroll
+  for (int j = 0; j < NJ; j++)
+    mx = fmax_nan(fmax_nan(mx, fmax_nan(fabsf(v[j].x), fabsf(v[j].y))), fmax_nan(fabsf(v[j].z), fabsf(v[j].w)));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const bool has_nan = mx != mx;
+  if (has_nan) {  // the maximum over the non-NaN values
+    mx = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NJ; j++)
+      mx = fmaxf(fmaxf(mx, fmaxf(fabsf(v[j].x), fabsf(v[j].y))), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  float scale = 0.0f, inv = 0.0f;
+  if (mx > 0.0f) {
+    scale = __fdiv_rn(mx, 127.0f);
+    inv = __fdiv_rn(1.0f, scale);
+  }
+  const bool zero = mx == 0.0f, fast = !has_nan && row_scale_normal(scale);
+  uint8_t *dq = q + (size_t)row * ldq;
+#pragma unroll
+  for (int j = 0; j < NJ; j++) {
+    const int c = lane + 32 * j;
+    if (c >= nq) continue;
+    uint32_t w;
+    if (zero) {
+      w = 0x80808080u;
+    } else if (fast) {
+      const float2 p0 = __fmul2_rn(make_float2(v[j].x, v[j].y), f2(inv));
+      const float2 p1 = __fmul2_rn(make_float2(v[j].z, v[j].w), f2(inv));
+      const uint32_t b0 = __float_as_uint(__fadd_rn(p0.x, kMagic + 128.0f));
+      const uint32_t b1 = __float_as_uint(__fadd_rn(p0.y, kMagic + 128.0f));
+      const uint32_t b2 = __float_as_uint(__fadd_rn(p1.x, kMagic + 128.0f));
+      const uint32_t b3 = __float_as_uint(__fadd_rn(p1.y, kMagic + 128.0f));
+      w = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+    } else {
+      w = quant_byte_slow(v[j].x, inv) | (quant_byte_slow(v[j].y, inv) << 8) | (quant_byte_slow(v[j].z, inv) << 16) |
+          (quant_byte_slow(v[j].w, inv) << 24);
+    }
+    *reinterpret_cast<uint32_t *>(dq + 4 * c) = w;
+  }
+  if (lane == 0) sa[row] = scale;
+}
+
+// LayerNorm (+ quantization) for V = 8 and H in {64, 128, 256}; -1 when this
+// path does not apply.
+template <bool EMBED>
+static int launch_ln8(const float *x, const int32_t *ids, int vocab, const float *emb, const float *gamma, int M,
+                      int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
+  if (V != 8 || !gamma) return -1;
+  if (q && ((ldq & 7) || (reinterpret_cast<uintptr_t>(q) & 7))) return -1;
+  const int blocks = (M + 31) / 32;
+#define IG_LN8(NB)                                                                                                 \
+  case 8 * NB:                                                                                                     \
+    ln8_kernel<NB, EMBED><<<blocks, 256, 0, st>>>(x, ids, vocab, emb, gamma, M, eps, xout, q, ldq, sa);           \
+    break;
+  switch (H) {
+    IG_LN8(8)
+    IG_LN8(16)
+    IG_LN8(32)
+    default:
+      return -1;
+  }
+#undef IG_LN8
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
+// Row quantization for K % 4 == 0, K <= 1024, aligned rows; -1 otherwise.
+static int launch_quant_rows4(const float *x, int ldx, int M, int K, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
+  if ((K & 3) || (ldx & 3) || (ldq & 3) || K > 1024 || K <= 0) return -1;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 3)) return -1;
+  const int nj = (K / 4 + 31) / 32;
+  const int blocks = (M + 7) / 8;
+  switch (nj) {
+    case 1: quant_rows4_kernel<1><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    case 2: quant_rows4_kernel<2><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    case 3: quant_rows4_kernel<3><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    case 4: quant_rows4_kernel<4><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    case 5:
+    case 6: quant_rows4_kernel<6><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    default: quant_rows4_kernel<8><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
+}  // namespace ig

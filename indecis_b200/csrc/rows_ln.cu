@@ -95,6 +95,7 @@ __global__ void ln_group_kernel(const float *__restrict__ x, const int32_t *__re
   for (int rr = 0; rr < rpw && row0 + rr < M; rr++) {
     const int rowr = row0 + rr;
     const float invr = __shfl_sync(0xffffffffu, inv, rr * V);
+    const float scaler = __shfl_sync(0xffffffffu, scale, rr * V);
     const float *srr = s + rr * P;
     if (xout) {
       float *dst = xout + (size_t)rowr * H;
@@ -108,7 +109,7 @@ __global__ void ln_group_kernel(const float *__restrict__ x, const int32_t *__re
     if (q) {
       uint8_t *dq = q + (size_t)rowr * ldq;
       auto qv = [&](float v) -> uint32_t {
-        if (invr == 0.0f) return 128u;
+        if (scaler == 0.0f) return 128u;  // a zero row
         const int t = max(-128, min(127, rne_int(__fmul_rn(v, invr))));
         return (uint32_t)(t + 128);
       };
