@@ -181,49 +181,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-      } else if constexpr (EPI == kEpiRope) {
-        // Columns in head groups of 64: the first rope_cols are rotated
-        // (Rope, linalg/vec_simd.go:404-425) at the row's position.
-        const int pos = row_ok ? ep.pos[row] : 0;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 64) {
-          uint32_t r1[32], r2[32];
-          tmem_ld_32x32b_x32(tbase + c, r1);
-          tmem_ld_32x32b_x32(tbase + c + 32, r2);
-          tmem_ld_wait();
-          if (!row_ok) continue;
-          const int j0 = n0 + c;
-          float x1[32], x2[32];
-#pragma unroll
-          for (int v = 0; v < 32; v++) {
-            x1[v] = dequant1((int32_t)r1[v], s_zc[c + v], s_sb[c + v], sa);
-            x2[v] = dequant1((int32_t)r2[v], s_zc[c + 32 + v], s_sb[c + 32 + v], sa);
-          }
-          if (j0 < ep.rope_cols) {
-            const float *cs = ep.rope_cos + (size_t)pos * 32;
-            const float *sn = ep.rope_sin + (size_t)pos * 32;
-#pragma unroll
-            for (int v = 0; v < 32; v++) {
-              const float a = x1[v], b = x2[v], co = __ldg(cs + v), si = __ldg(sn + v);
-              x1[v] = __fsub_rn(__fmul_rn(a, co), __fmul_rn(b, si));
-              x2[v] = __fadd_rn(__fmul_rn(b, co), __fmul_rn(a, si));
-            }
-          }
-          float *dst = ep.C + (size_t)row * ep.ldc + j0;
-          if (vec_ok && j0 + 64 <= N) {
-#pragma unroll
-            for (int v = 0; v < 32; v += 4) {
-              *reinterpret_cast<float4 *>(dst + v) = make_float4(x1[v], x1[v + 1], x1[v + 2], x1[v + 3]);
-              *reinterpret_cast<float4 *>(dst + 32 + v) = make_float4(x2[v], x2[v + 1], x2[v + 2], x2[v + 3]);
-            }
-          } else {
-#pragma unroll
-            for (int v = 0; v < 32; v++) {
-              if (j0 + v < N) dst[v] = x1[v];
-              if (j0 + 32 + v < N) dst[32 + v] = x2[v];
-            }
-          }
-        }
       } else if constexpr (EPI == kEpiGeglu) {
         // Tile columns [0, BN/2) hold GELU inputs, [BN/2, BN) the matching
         // gates (weights interleaved at pack time); output columns
@@ -330,7 +287,6 @@ int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t s
   int bn = g.bn;
   if (bn != 128 && bn != 256) bn = g.N > 128 ? 256 : 128;
   if (epi == kEpiGeglu) bn = 256;
-  if (epi == kEpiRope && (bn % 64)) return IG_ERR_BAD_ARG;
   CUtensorMap ma, mb;
   if (make_map_u8(&ma, g.A, g.M, g.K, g.lda, kBM) || make_map_u8(&mb, g.B, g.N, g.K, g.ldb, bn))
     return IG_ERR_CUDA;
@@ -345,7 +301,6 @@ int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t s
   switch (epi) {
     IG_GEMM_CASE(kEpiF32)
     IG_GEMM_CASE(kEpiI32)
-    IG_GEMM_CASE(kEpiRope)
     case kEpiGeglu:
       e = launch_bn<256, kEpiGeglu>(ma, mb, g.M, g.N, g.K, ep, st);
       break;

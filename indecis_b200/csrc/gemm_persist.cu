@@ -24,20 +24,31 @@
 
 namespace ig {
 
-// Epilogue warps: two per TMEM lane quarter, taking alternate column chunks.
-constexpr int kPEpiWarps = 8;
-constexpr int kPThreads = 64 + 32 * kPEpiWarps;
+// Epilogue warps per TMEM lane quarter: four for the GeGLU epilogue, whose
+// arithmetic needs warps enough to cover its latencies; two for the plain
+// stores, which are bound by the TMA store stream.
+template <int EPI>
+struct PEpi {
+  static constexpr int kWarps = EPI == kEpiGeglu ? 16 : 8;
+  static constexpr int kGroups = kWarps / 4;  // warps per lane quarter
+  static constexpr int kThreads = 64 + 32 * kWarps;
+};
 
-template <int BN>
+template <int BN, int EPI>
 struct PGemmSmem {
-  static constexpr int kStages = BN == 256 ? 3 : 4;
+  static constexpr int kEpiWarps = PEpi<EPI>::kWarps;
+  // K is a few 128-byte blocks per tile here (hidden sizes of a few hundred),
+  // so two to four stages keep the tensor cores fed; the rest of shared
+  // memory double-buffers the epilogue warps' staging.
+  static constexpr int kStages = kEpiWarps == 16 ? (BN == 256 ? 2 : 3) : (BN == 256 ? 3 : 4);
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStaging = kStages * kStageBytes;  // per epilogue warp 2 x [32 rows][128 B]
-  static constexpr int kBar = kStaging + kPEpiWarps * 2 * 4096;
+  static constexpr int kBar = kStaging + kEpiWarps * 2 * 4096;
   static constexpr int kTmemSlot = kBar + 8 * (2 * kStages + 4);
   static constexpr int kTotal = kTmemSlot + 16 + 1024;
+  static_assert(kTotal <= 227 * 1024, "shared memory");
 };
 
 // Dequantized accumulators of columns j0..j0+15, the column scales read four
@@ -91,20 +102,14 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // One warp's 32 x 32 float sub-tile: thread = row; writes the row into the
 // 128-byte-swizzled staging buffer, then lane 0 issues the bulk store.
 struct StageWriter {
-  uint8_t *bufs;  // two 4 KB buffers
+  uint8_t *bufs;  // two 4 KB buffers, used in turn
   int count = 0;
+  // The next buffer, once the bulk store that last used it has read it.
   __device__ __forceinline__ uint8_t *begin(int lane) {
     uint8_t *b = bufs + (count & 1) * 4096;
     if (lane == 0) bulk_wait_read<1>();
     __syncwarp();
     return b;
-  }
-  // Both buffers at once (all earlier stores of this warp have read theirs).
-  __device__ __forceinline__ void begin2(int lane, uint8_t **a, uint8_t **b) {
-    if (lane == 0) bulk_wait_read<0>();
-    __syncwarp();
-    *a = bufs;
-    *b = bufs + 4096;
   }
   // Columns [16*half, 16*half+16) of the warp's 32-column row.
   __device__ __forceinline__ static void put_half(uint8_t *b, int lane, int half, const float (&v)[16]) {
@@ -134,31 +139,18 @@ struct StageWriter {
     }
     count++;
   }
-  // Stores two buffers (one bulk group each), written after begin2.
-  __device__ __forceinline__ void finish2(const CUtensorMap *map, uint8_t *a, uint8_t *b, int lane, int col_a,
-                                          bool store_b, int col_b, int row0) {
-    fence_proxy_async_shared();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(map, a, col_a, row0);
-      bulk_commit();
-      if (store_b) {
-        tma_store_2d(map, b, col_b, row0);
-        bulk_commit();
-      }
-    }
-  }
   __device__ __forceinline__ static void fence_proxy_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
 };
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kPThreads, 1)
+__global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
     gemm_persist_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                         const __grid_constant__ CUtensorMap mapC, int M, int N, int K, GemmEpilogue ep) {
-  using S = PGemmSmem<BN>;
+  using S = PGemmSmem<BN, EPI>;
   constexpr int kStages = S::kStages;
+  constexpr int kPGroups = PEpi<EPI>::kGroups;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::kBar);
@@ -182,7 +174,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], kPEpiWarps);
+      mbar_init(&acce[b], PEpi<EPI>::kWarps);
     }
     fence_barrier_init();
   }
@@ -245,7 +237,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   } else {
     const int q = warp & 3;            // TMEM lane quarter
     const int e = warp - 2;            // epilogue warp 0..7
-    const int g = e >> 2;              // which alternate column chunks
+    const int g = e >> 2;              // column chunks g, g + kPGroups, ...
     StageWriter sw{smem + S::kStaging + e * 8192};
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
@@ -261,7 +253,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const float sa = (EPI != kEpiI32 && row_ok) ? __ldg(ep.sa + row) : 0.0f;
       if constexpr (EPI == kEpiF32 || EPI == kEpiI32) {
 #pragma unroll 1
-        for (int c = g * 32; c < BN; c += 64) {
+        for (int c = g * 32; c < BN; c += 32 * kPGroups) {
           if (n0 + c >= N) continue;
           uint8_t *buf = sw.begin(lane);
 #pragma unroll
@@ -280,51 +272,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
           }
           sw.finish(&mapC, buf, lane, n0 + c, row0, EPI == kEpiF32 && ep.accumulate);
         }
-      } else if constexpr (EPI == kEpiRope) {
-        // Head groups of 64 columns: x1 = [c, c+32), x2 = [c+32, c+64).
-        const int pos = row_ok ? __ldg(ep.pos + row) : 0;
-#pragma unroll 1
-        for (int c = g * 64; c < BN; c += 128) {
-          const int j0 = n0 + c;
-          if (j0 >= N) continue;
-          uint8_t *ba, *bb;
-          sw.begin2(lane, &ba, &bb);
-#pragma unroll
-          for (int h = 0; h < 2; h++) {
-            uint32_t r1[16], r2[16];
-            tmem_ld_32x32b_x16(tbase + c + 16 * h, r1);
-            tmem_ld_32x32b_x16(tbase + c + 32 + 16 * h, r2);
-            tmem_ld_wait();
-            float x1[16], x2[16];
-            dequant16(r1, ep.sb, ep.zc, j0 + 16 * h, N, sa, x1);
-            dequant16(r2, ep.sb, ep.zc, j0 + 32 + 16 * h, N, sa, x2);
-            if (j0 < ep.rope_cols) {
-              const float4 *cs = reinterpret_cast<const float4 *>(ep.rope_cos + (size_t)pos * 32 + 16 * h);
-              const float4 *sn = reinterpret_cast<const float4 *>(ep.rope_sin + (size_t)pos * 32 + 16 * h);
-#pragma unroll
-              for (int k4 = 0; k4 < 4; k4++) {
-                const float4 co = __ldg(cs + k4), si = __ldg(sn + k4);
-                const float cv[4] = {co.x, co.y, co.z, co.w}, sv[4] = {si.x, si.y, si.z, si.w};
-#pragma unroll
-                for (int m = 0; m < 4; m++) {
-                  const int k = 4 * k4 + m;
-                  const float a = x1[k], bv = x2[k];
-                  x1[k] = __fsub_rn(__fmul_rn(a, cv[m]), __fmul_rn(bv, sv[m]));
-                  x2[k] = __fadd_rn(__fmul_rn(bv, cv[m]), __fmul_rn(a, sv[m]));
-                }
-              }
-            }
-            StageWriter::put_half(ba, lane, h, x1);
-            StageWriter::put_half(bb, lane, h, x2);
-          }
-          sw.finish2(&mapC, ba, bb, lane, j0, j0 + 32 < N, j0 + 32, row0);
-        }
       } else if constexpr (EPI == kEpiGeglu) {
         // Tile columns [0, BN/2) are GELU inputs, [BN/2, BN) their gates.
         constexpr int H2 = BN / 2;
         const int g0 = n0 / 2;
 #pragma unroll 1
-        for (int c = g * 32; c < H2; c += 64) {
+        for (int c = g * 32; c < H2; c += 32 * kPGroups) {
           if (g0 + c >= ep.geglu_n) continue;
           uint8_t *buf = sw.begin(lane);
 #pragma unroll
@@ -399,7 +352,7 @@ static int num_sms() {
 template <int BN, int EPI>
 static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc, int M, int N,
                                   int K, const GemmEpilogue &ep, cudaStream_t st) {
-  using S = PGemmSmem<BN>;
+  using S = PGemmSmem<BN, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(gemm_persist_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -409,7 +362,7 @@ static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, 
   }
   const int ntiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
-  gemm_persist_kernel<BN, EPI><<<grid, kPThreads, S::kTotal, st>>>(ma, mb, mc, M, N, K, ep);
+  gemm_persist_kernel<BN, EPI><<<grid, PEpi<EPI>::kThreads, S::kTotal, st>>>(ma, mb, mc, M, N, K, ep);
   return cudaGetLastError();
 }
 
@@ -420,8 +373,6 @@ static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, 
   void *out = epi == kEpiI32 ? (void *)ep.acc_out : (void *)ep.C;
   if (!out || (reinterpret_cast<uintptr_t>(out) & 15) || (ep.ldc & 3)) return -1;
   if (epi != kEpiI32 && ((reinterpret_cast<uintptr_t>(ep.sb) | reinterpret_cast<uintptr_t>(ep.zc)) & 15)) return -1;
-  if (epi == kEpiRope && ((reinterpret_cast<uintptr_t>(ep.rope_cos) | reinterpret_cast<uintptr_t>(ep.rope_sin)) & 15))
-    return -1;
   const int out_cols = epi == kEpiGeglu ? ep.geglu_n : g.N;
   CUtensorMap mc;
   if (make_map_out32(&mc, out, g.M, out_cols, ep.ldc, epi == kEpiI32)) return IG_ERR_CUDA;
@@ -434,7 +385,6 @@ static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, 
   switch (epi) {
     IG_PCASE(kEpiF32)
     IG_PCASE(kEpiI32)
-    IG_PCASE(kEpiRope)
     case kEpiGeglu:
       e = launch_persist<256, kEpiGeglu>(ma, mb, mc, g.M, g.N, g.K, ep, st);
       break;

@@ -7,7 +7,7 @@
 
 namespace ig {
 
-enum Epilogue : int { kEpiF32 = 0, kEpiI32 = 1, kEpiRope = 2, kEpiGeglu = 3 };
+enum Epilogue : int { kEpiF32 = 0, kEpiI32 = 1, kEpiGeglu = 3 };
 
 struct GemmArgs {
   const uint8_t *A;  // [M][lda] uint8 activations (q + 128)
@@ -25,10 +25,6 @@ struct GemmEpilogue {
   int32_t *acc_out; // int32 output (kEpiI32)
   int ldc;
   int accumulate;   // C = dequant + C
-  // kEpiRope
-  const int32_t *pos;
-  const float *rope_cos, *rope_sin;  // [positions][32]
-  int rope_cols;
   // kEpiGeglu
   int geglu_n;  // GeGLU output width (intermediate size)
 };

@@ -302,6 +302,10 @@ int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, 
 int launch_head_logits(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z, int ldz,
                        cudaStream_t st) {
   if (nx <= 0 || rows <= 0) return 0;
+  if (nx >= 256) {
+    const int rc = launch_head_logits_tok(w, b, rows, H, x, nx, z, ldz, st);
+    if (rc != -1) return rc;
+  }
   if (rows <= 16 && nx >= 1024) {
     head_logits_rows_kernel<<<(nx + 127) / 128, 128, 0, st>>>(w, b, rows, H, x, nx, z, ldz);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;

@@ -185,6 +185,61 @@ __global__ void __launch_bounds__(256) quant_rows4_kernel(const float *__restric
   if (lane == 0) sa[row] = scale;
 }
 
+// head.logits (heads.go:62-74) for many tokens: z[t][r] = sum_i double(w[r][i])
+// * double(x[t][i]) in order, + double(b[r]). One token per thread, its R
+// rows side by side. The product of two floats is exact in float64, so the
+// fused multiply-add gives the bits of the reference's separate multiply and
+// add. The weights are widened to float64 once per block, in shared memory
+// ([H][R], read as broadcasts).
+template <int R>
+__global__ void __launch_bounds__(128) head_logits_tok_kernel(const float *__restrict__ w, const float *__restrict__ b,
+                                                              int H, const float *__restrict__ x, int nx,
+                                                              double *__restrict__ z, int ldz) {
+  extern __shared__ double s_w[];
+  for (int e = threadIdx.x; e < H * R; e += blockDim.x) {
+    const int i = e / R, r = e - i * R;
+    s_w[e] = (double)__ldg(w + (size_t)r * H + i);
+  }
+  __syncthreads();
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= nx) return;
+  const float4 *xt = reinterpret_cast<const float4 *>(x + (size_t)t * H);
+  double s[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) s[r] = 0.0;
+  for (int i4 = 0; i4 < H / 4; i4++) {
+    const float4 xv = __ldg(xt + i4);
+    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const double xd = (double)xs[u];
+      const double *wr = s_w + (size_t)(4 * i4 + u) * R;
+#pragma unroll
+      for (int r = 0; r < R; r++) s[r] = __fma_rn(wr[r], xd, s[r]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; r++) z[(size_t)t * ldz + r] = __dadd_rn(s[r], (double)__ldg(b + r));
+}
+
+static int launch_head_logits_tok(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z,
+                                  int ldz, cudaStream_t st) {
+  if (rows < 1 || rows > 16 || (H & 3) || (reinterpret_cast<uintptr_t>(x) & 15)) return -1;
+  const size_t smem = (size_t)H * rows * sizeof(double);
+  if (smem > 48 * 1024) return -1;
+  const int blocks = (nx + 127) / 128;
+  switch (rows) {
+#define IG_HT(R)                                                                                      \
+  case R:                                                                                            \
+    head_logits_tok_kernel<R><<<blocks, 128, smem, st>>>(w, b, H, x, nx, z, ldz);                    \
+    break;
+    IG_HT(1) IG_HT(2) IG_HT(3) IG_HT(4) IG_HT(5) IG_HT(6) IG_HT(7) IG_HT(8)
+    IG_HT(9) IG_HT(10) IG_HT(11) IG_HT(12) IG_HT(13) IG_HT(14) IG_HT(15) IG_HT(16)
+#undef IG_HT
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
 // LayerNorm (+ quantization) for V = 8 and H in {64, 128, 256}; -1 when this
 // path does not apply.
 template <bool EMBED>

@@ -133,3 +133,21 @@ def test_head_logits(tiny):
         assert np.array_equal(z, ref)
     a = heads[2].answer(logits[2][0])
     assert abs(sum(a["Probs"].values()) - 1) < 1e-12
+
+
+def test_head_logits_many(tiny):
+    """The per-token and pooled heads over enough tokens and sequences for
+    the block-wide float64 kernel (300 sequences, about 6000 tokens)."""
+    import oracle
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Head
+    cfg, om, gm, _ = tiny
+    heads = [Head(h["name"], h["kind"], h["w"], h["b"] - np.float32(0.02)) for h in S.heads(cfg["hidden"], seed=4)]
+    gm.SetHeads(heads)
+    ids, offs = S.ids_varlen(300, 1, 40, cfg["vocab"], seed=12)
+    logits, _ = gm.Logits((ids, offs))
+    pooled = om.encode(ids, offs, threads=8)
+    tokens = om.encode(ids, offs, mode=1, threads=8)
+    for h, z in zip(heads, logits):
+        ref = oracle.head_logits(h.w, h.b, tokens if h.kind == "spans" else pooled)
+        assert np.array_equal(z, ref), h.name
