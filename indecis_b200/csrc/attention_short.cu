@@ -15,10 +15,11 @@
 //      quantizes Q per row (uint8, q+128; scale times the score scale kept);
 //   A. K rotated in place;
 //   B. warps 0-1: ordered float32 K column sums (the mean); warps 2-3: V
-//      column maxima (attention8.go:224-269);
-//   C. K rows centred and quantized per key (scale, 128*sum(kq)) and V per
-//      column; the K, Q and V tiles ([128][64 B] SWIZZLE_64B; rows past n:
-//      zeros, Q 128s) are written over the f32 rows once all have been read;
+//      column maxima (attention8.go:224-269), after which warps 4-7 quantize
+//      V per column, a row each, while the K sums run;
+//   C. K rows centred and quantized per key (scale, 128*sum(kq)); the K, Q
+//      and V tiles ([128][64 B] SWIZZLE_64B; rows past n: zeros, Q 128s) are
+//      written over the f32 rows once all have been read;
 //   D. warp 0 issues S = Q.K^T (M=128, N=128, K=64) into TMEM; all 8 warps
 //      run the softmax (MaxOf, ExpShift vector body, P = rne(e*255), the
 //      scalar-tail keys recomputed by tail_fixup, sp) into P; warp 0 issues
@@ -62,7 +63,7 @@ struct AttnShortSmem {
   static constexpr int kVs = kMean + 256;   // 64
   static constexpr int kVinv = kVs + 256;   // 64
   static constexpr int kBar = kVinv + 256;  // 4 mbarriers
-  static constexpr int kTmem = kBar + 32;
+  static constexpr int kTmem = kBar + 32;   // TMEM base address; V fast-path flag at +4
   static constexpr int kTotal = kTmem + 16 + 1024;
   static_assert(kO + 128 * kOPitch * 4 <= kRed, "ctx staging overlaps the exchange");
   static_assert(kShortCtasPerSm * (kTotal + 1024) <= 228 * 1024, "three CTAs per SM");
@@ -156,6 +157,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   uint64_t *bar_p = bar_load + 2;
   uint64_t *bar_o = bar_load + 3;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::kTmem);
+  volatile int *s_vfast = reinterpret_cast<volatile int *>(smem + S::kTmem + 4);
 
   const int s = blockIdx.x, h = blockIdx.y;
   const int t0 = offs[s];
@@ -167,6 +169,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
 
   // 1. K and V by TMA; Q and the RoPE factors straight into registers.
   if (tid == 0) {
+    *s_vfast = 1;
     prefetch_tensormap(&mqkv);
     mbar_init(bar_load, 1);
     mbar_init(bar_s, 1);
@@ -260,9 +263,9 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   }
   __syncthreads();
 
-  // B. K column means (ordered float32 sums over the rotated keys); V
-  // column maxima.
-  bool vnormal = true;
+  // B. Warps 0-1: K column means (ordered float32 sums over the rotated
+  // keys). Warps 2-3: V column maxima; then warps 4-7 quantize V per column,
+  // one row each, into its tile (over the f32 V rows once all are read).
   if (tid < 64) {
     float acc = 0.0f;
     int r = 0;
@@ -296,13 +299,45 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
     const float sc = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
     s_vs[d] = sc;
     s_vinv[d] = mx > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
-    vnormal = mn == mn && (mx == 0.0f || scale_is_normal(sc));  // vinv = 0: every byte is rne(v * 0)
+    // vinv = 0 (a zero column): every byte is rne(v * 0).
+    if (!(mn == mn && (mx == 0.0f || scale_is_normal(sc)))) *s_vfast = 0;
+    named_barrier_sync(2, 192);  // the V scales are in shared memory
+  } else {
+    named_barrier_sync(2, 192);
+    const int vr = tid - 128;
+    const bool vfast = *s_vfast != 0;
+    uint32_t vw[16];
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      float4 lo = make_float4(0.0f, 0.0f, 0.0f, 0.0f), hi = lo;
+      if (vr < n) {
+        lo = *f32_chunk(vf, vr, c);
+        hi = *f32_chunk(vf, vr, 8 + c);
+      }
+      const float4 il = *reinterpret_cast<const float4 *>(s_vinv + 4 * c);
+      const float4 ih = *reinterpret_cast<const float4 *>(s_vinv + 32 + 4 * c);
+      if (vfast) {
+        vw[c] = quant4_fast_s8(lo.x, lo.y, lo.z, lo.w, make_float2(il.x, il.y), make_float2(il.z, il.w));
+        vw[8 + c] = quant4_fast_s8(hi.x, hi.y, hi.z, hi.w, make_float2(ih.x, ih.y), make_float2(ih.z, ih.w));
+      } else {
+        vw[c] = pack_low_bytes(quant_bits(__fmul_rn(lo.x, il.x)), quant_bits(__fmul_rn(lo.y, il.y)),
+                               quant_bits(__fmul_rn(lo.z, il.z)), quant_bits(__fmul_rn(lo.w, il.w)));
+        vw[8 + c] = pack_low_bytes(quant_bits(__fmul_rn(hi.x, ih.x)), quant_bits(__fmul_rn(hi.y, ih.y)),
+                                   quant_bits(__fmul_rn(hi.z, ih.z)), quant_bits(__fmul_rn(hi.w, ih.w)));
+      }
+    }
+    named_barrier_sync(3, 128);  // every f32 V row has been read
+    // Tile chunk t holds dimensions 16t..16t+15: f32 chunks 4t..4t+3.
+    *tile_chunk(smem + S::kVt, vr, 0) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+    *tile_chunk(smem + S::kVt, vr, 1) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+    *tile_chunk(smem + S::kVt, vr, 2) = make_uint4(vw[8], vw[9], vw[10], vw[11]);
+    *tile_chunk(smem + S::kVt, vr, 3) = make_uint4(vw[12], vw[13], vw[14], vw[15]);
   }
-  const bool vfast = __syncthreads_and(vnormal);
+  __syncthreads();
 
   // C. K rows: centred, x = rne(kv * kinv) (the key's sum takes x before the
-  // int8 clamp; a zero row gives kinv = 0, so x = 0). V rows per column.
-  uint32_t kw[8], vw[8];
+  // int8 clamp; a zero row gives kinv = 0, so x = 0).
+  uint32_t kw[8];
   {
     float kv[32];
 #pragma unroll
@@ -363,33 +398,11 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       s_kzc[rr] = __fadd_rn(kmx > 0.0f ? __fmul_rn(128.0f, (float)ksum) : 0.0f, kMagic);  // zcm for dequant2m
     }
   }
-#pragma unroll
-  for (int k = 0; k < 4; k++) {
-    const int c = 4 * hh + k;
-    float4 lo = make_float4(0.0f, 0.0f, 0.0f, 0.0f), hi = lo;
-    if (rr < n) {
-      lo = *f32_chunk(vf, rr, c);
-      hi = *f32_chunk(vf, rr, 8 + c);
-    }
-    const float4 il = *reinterpret_cast<const float4 *>(s_vinv + 4 * c);
-    const float4 ih = *reinterpret_cast<const float4 *>(s_vinv + 32 + 4 * c);
-    if (vfast) {
-      vw[k] = quant4_fast_s8(lo.x, lo.y, lo.z, lo.w, make_float2(il.x, il.y), make_float2(il.z, il.w));
-      vw[4 + k] = quant4_fast_s8(hi.x, hi.y, hi.z, hi.w, make_float2(ih.x, ih.y), make_float2(ih.z, ih.w));
-      continue;
-    }
-    vw[k] = pack_low_bytes(quant_bits(__fmul_rn(lo.x, il.x)), quant_bits(__fmul_rn(lo.y, il.y)),
-                           quant_bits(__fmul_rn(lo.z, il.z)), quant_bits(__fmul_rn(lo.w, il.w)));
-    vw[4 + k] = pack_low_bytes(quant_bits(__fmul_rn(hi.x, ih.x)), quant_bits(__fmul_rn(hi.y, ih.y)),
-                               quant_bits(__fmul_rn(hi.z, ih.z)), quant_bits(__fmul_rn(hi.w, ih.w)));
-  }
-  __syncthreads();  // every f32 row has been read
+  __syncthreads();  // every f32 K row has been read
   *tile_chunk(smem + S::kKt, rr, hh) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
   *tile_chunk(smem + S::kKt, rr, 2 + hh) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
   *tile_chunk(smem + S::kQt, rr, hh) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
   *tile_chunk(smem + S::kQt, rr, 2 + hh) = make_uint4(qw[4], qw[5], qw[6], qw[7]);
-  *tile_chunk(smem + S::kVt, rr, hh) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
-  *tile_chunk(smem + S::kVt, rr, 2 + hh) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
   fence_proxy_async_smem();  // the tiles are read by the tensor cores
   tc_fence_before();
   __syncthreads();
@@ -397,20 +410,33 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   const uint32_t tmem = *tmem_slot;
 
   // D. Attend.
+  const int q = warp & 3;   // TMEM lane quarter: rows [32q, 32q+32)
+  const int g = warp >> 2;  // 16-key chunks with parity g
+  const int r = q * 32 + lane;
+  const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+  // Every row's score accumulator of key j starts at 0x4B400000 - 128*sum(kq_j)
+  // (the bits of 1.5*2^23 + (acc - zc) once the products are added).
+#pragma unroll
+  for (int c16 = 0; c16 < 4; c16++) {
+    uint32_t init[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) init[u] = 2u * (uint32_t)kMagicBits - __float_as_uint(s_kzc[64 * g + 16 * c16 + u]);
+    tmem_st_32x32b_x16(tbase + 64 * g + 16 * c16, init);
+  }
+  tmem_st_wait();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   if (tid == 0) {
     constexpr uint32_t idesc_s = idesc_u8s8(128, 128);
     const uint32_t q_base = smem_u32(smem + S::kQt), k_base = smem_u32(smem + S::kKt);
 #pragma unroll
     for (int kk = 0; kk < 2; kk++)
-      mma_u8s8(tmem, smem_desc_k_sw64(q_base + kk * 32), smem_desc_k_sw64(k_base + kk * 32), idesc_s, kk);
+      mma_u8s8(tmem, smem_desc_k_sw64(q_base + kk * 32), smem_desc_k_sw64(k_base + kk * 32), idesc_s, 1);
     mma_commit(bar_s);
   }
   __syncwarp();
-  const int q = warp & 3;   // TMEM lane quarter: rows [32q, 32q+32)
-  const int g = warp >> 2;  // 16-key chunks with parity g
-  const int r = q * 32 + lane;
   const bool valid = r < n;
-  const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
   int js = 0, je = n;
   if (window >= 0) {
     js = max(0, r - window);
@@ -431,17 +457,18 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   ok = ok && mbar_wait(bar_s, 0, kDevTimeoutAccum);
   ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
   tc_fence_after();
-  float mx = -INFINITY;
+  float mx = -INFINITY;  // of (acc - zc) * ks; times sq below
   if (ok) {
-    for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2) mx = chunk_max(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx);
+    for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2)
+      mx = chunk_max<true>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx);
   }
   red[g * 128 + r] = mx;
   __syncthreads();
-  mx = fmaxf(red[r], red[128 + r]);
+  mx = __fmul_rn(fmaxf(red[r], red[128 + r]), w.sq);
   int psum = 0;
   for (int ch = g; ch < 8; ch += 2) {
     uint4 pw = make_uint4(0, 0, 0, 0);
-    if (ok && ch >= ch0 && ch < ch1) pw = chunk_p(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx, psum);
+    if (ok && ch >= ch0 && ch < ch1) pw = chunk_p<true>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx, psum);
     *reinterpret_cast<uint4 *>(prow_smem + ((ch ^ (r & 7)) << 4)) = pw;
   }
   if (ok && w.t0 < w.t1)

@@ -94,21 +94,33 @@ struct ScoreRow {
   float sq;
 };
 
+// Scores (acc - zc) * ks [* sq] of two keys. PRE: the accumulators started
+// from 0x4B400000 - 128*sum(kq) (written into TMEM before the MMA), so their
+// bits are the float 1.5*2^23 + (acc - zc) and one subtraction recovers
+// acc - zc exactly; otherwise zcm holds 128*sum(kq) + 1.5*2^23 (dequant2m).
+template <bool PRE>
+__device__ __forceinline__ float2 score2(uint32_t a0, uint32_t a1, float2 zcm, float2 ks, float sq, bool with_sq) {
+  if constexpr (PRE) {
+    const float2 u = __fmul2_rn(__fadd2_rn(make_float2(__uint_as_float(a0), __uint_as_float(a1)), f2(-kMagic)), ks);
+    return with_sq ? __fmul2_rn(u, f2(sq)) : u;
+  } else {
+    return dequant2m((int32_t)a0, (int32_t)a1, zcm, ks, sq);
+  }
+}
+
 // MaxOf over the valid columns of the 16-key chunk at TMEM column tcol.
-// zcm holds 128*sum(kq) + 1.5*2^23 per key (dequant2m).
-__device__ __forceinline__ float chunk_max(uint32_t tcol, int c, const float *zcm, const float *ks,
-                                           const ScoreRow &w, float mx) {
-  uint32_t acc[16];
-  tmem_ld_32x32b_x16(tcol, acc);
-  tmem_ld_wait();
+// PRE: the maximum of (acc - zc) * ks, before the row's sq (x -> x * sq is
+// non-decreasing for sq >= 0, so the row maximum is that maximum times sq).
+template <bool PRE>
+__device__ __forceinline__ float chunk_max_acc(const uint32_t (&acc)[16], int c, const float *zcm, const float *ks,
+                                               const ScoreRow &w, float mx) {
   const bool inner = __all_sync(0xffffffffu, c >= w.a && c + 16 <= w.b);
 #pragma unroll
   for (int v = 0; v < 16; v += 4) {
-    const float4 z = *reinterpret_cast<const float4 *>(zcm + c + v);
+    const float4 z = PRE ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : *reinterpret_cast<const float4 *>(zcm + c + v);
     const float4 k = *reinterpret_cast<const float4 *>(ks + c + v);
-    const float2 s0 = dequant2m((int32_t)acc[v], (int32_t)acc[v + 1], make_float2(z.x, z.y), make_float2(k.x, k.y), w.sq);
-    const float2 s1 =
-        dequant2m((int32_t)acc[v + 2], (int32_t)acc[v + 3], make_float2(z.z, z.w), make_float2(k.z, k.w), w.sq);
+    const float2 s0 = score2<PRE>(acc[v], acc[v + 1], make_float2(z.x, z.y), make_float2(k.x, k.y), w.sq, false);
+    const float2 s1 = score2<PRE>(acc[v + 2], acc[v + 3], make_float2(z.z, z.w), make_float2(k.z, k.w), w.sq, false);
     if (inner) {
       mx = fmaxf(mx, fmaxf(fmaxf(s0.x, s0.y), fmaxf(s1.x, s1.y)));
     } else {
@@ -128,22 +140,19 @@ __device__ __forceinline__ float chunk_max(uint32_t tcol, int c, const float *zc
 // scalar-tail keys); the sum of the 16 is added to psum. The subtraction is
 // scalar: a packed add after the packed product of dequant2m could be fused
 // into one rounding.
-__device__ __forceinline__ uint4 chunk_p(uint32_t tcol, int c, const float *zcm, const float *ks, const ScoreRow &w,
-                                        float mx, int &psum) {
-  uint32_t acc[16];
-  tmem_ld_32x32b_x16(tcol, acc);
-  tmem_ld_wait();
+template <bool PRE>
+__device__ __forceinline__ uint4 chunk_p_acc(const uint32_t (&acc)[16], int c, const float *zcm, const float *ks,
+                                            const ScoreRow &w, float mx, int &psum) {
   uint32_t bits[16];  // 0x4B400000 + P (low byte P)
   const bool inner = __all_sync(0xffffffffu, c >= w.a && c + 16 <= w.b);
 #pragma unroll
   for (int v = 0; v < 16; v += 4) {
-    const float4 z = *reinterpret_cast<const float4 *>(zcm + c + v);
+    const float4 z = PRE ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : *reinterpret_cast<const float4 *>(zcm + c + v);
     const float4 k = *reinterpret_cast<const float4 *>(ks + c + v);
 #pragma unroll
     for (int h = 0; h < 4; h += 2) {
-      const float2 sc = dequant2m((int32_t)acc[v + h], (int32_t)acc[v + h + 1],
-                                  h ? make_float2(z.z, z.w) : make_float2(z.x, z.y),
-                                  h ? make_float2(k.z, k.w) : make_float2(k.x, k.y), w.sq);
+      const float2 sc = score2<PRE>(acc[v + h], acc[v + h + 1], h ? make_float2(z.z, z.w) : make_float2(z.x, z.y),
+                                    h ? make_float2(k.z, k.w) : make_float2(k.x, k.y), w.sq, true);
       const uint2 b = exp_p_bits2(make_float2(__fsub_rn(sc.x, mx), __fsub_rn(sc.y, mx)));
       bits[v + h] = b.x;
       bits[v + h + 1] = b.y;
@@ -162,6 +171,24 @@ __device__ __forceinline__ uint4 chunk_p(uint32_t tcol, int c, const float *zcm,
     psum = dp4a_us(word[k], 0x01010101u, psum);
   }
   return make_uint4(word[0], word[1], word[2], word[3]);
+}
+
+template <bool PRE>
+__device__ __forceinline__ float chunk_max(uint32_t tcol, int c, const float *zcm, const float *ks,
+                                           const ScoreRow &w, float mx) {
+  uint32_t acc[16];
+  tmem_ld_32x32b_x16(tcol, acc);
+  tmem_ld_wait();
+  return chunk_max_acc<PRE>(acc, c, zcm, ks, w, mx);
+}
+
+template <bool PRE>
+__device__ __forceinline__ uint4 chunk_p(uint32_t tcol, int c, const float *zcm, const float *ks, const ScoreRow &w,
+                                        float mx, int &psum) {
+  uint32_t acc[16];
+  tmem_ld_32x32b_x16(tcol, acc);
+  tmem_ld_wait();
+  return chunk_p_acc<PRE>(acc, c, zcm, ks, w, mx, psum);
 }
 
 // ExpShift's scalar-tail keys [t0, t1) of query row r (its last len % V
@@ -322,7 +349,8 @@ __global__ void __launch_bounds__(kAtThreads, 2)
     tc_fence_after();
     float mx = -INFINITY;
     if (ok) {
-      for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2) mx = chunk_max(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx);
+      for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2)
+        mx = chunk_max<false>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx);
     }
     red[g * 128 + r] = mx;
     named_barrier_sync(1, 32 * kAtSoftWarps);
@@ -331,7 +359,7 @@ __global__ void __launch_bounds__(kAtThreads, 2)
     if (ok) {
       for (int ch = g; ch < nch; ch += 2) {
         uint4 pw = make_uint4(0, 0, 0, 0);
-        if (ch >= ch0 && ch < ch1) pw = chunk_p(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx, psum);
+        if (ch >= ch0 && ch < ch1) pw = chunk_p<false>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx, psum);
         // 16 keys = one 16-byte piece of the row's 128-byte swizzle row.
         const int kc = ch >> 3, piece = ch & 7;
         *reinterpret_cast<uint4 *>(prow_smem + kc * 16384 + ((piece ^ (r & 7)) << 4)) = pw;
