@@ -77,13 +77,6 @@ __device__ __forceinline__ uint64_t smem_desc_mn_sw64(uint32_t saddr) {
   return d;
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
 
 
 // One query row's view of a tile of scores: valid key columns [a, b) and the

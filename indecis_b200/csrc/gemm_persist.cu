@@ -144,6 +144,69 @@ struct StageWriter {
   }
 };
 
+// One output tile's epilogue for one warp: TMEM lane quarter at tbase (row0 its
+// first row, sa the thread's row scale), column chunks g, g + GROUPS, ...
+template <int BN, int EPI, int GROUPS>
+__device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int row0, float sa, int g, int lane,
+                                              StageWriter &sw, const CUtensorMap *mapC, const GemmEpilogue &ep) {
+  constexpr int kPGroups = GROUPS;
+  if constexpr (EPI == kEpiF32 || EPI == kEpiI32) {
+#pragma unroll 1
+    for (int c = g * 32; c < BN; c += 32 * kPGroups) {
+      if (n0 + c >= N) continue;
+      uint8_t *buf = sw.begin(lane);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tbase + c + 16 * h, r);
+        tmem_ld_wait();
+        float v[16];
+        if constexpr (EPI == kEpiI32) {
+#pragma unroll
+          for (int k = 0; k < 16; k++) v[k] = __int_as_float((int)r[k]);
+        } else {
+          dequant16(r, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, v);
+        }
+        StageWriter::put_half(buf, lane, h, v);
+      }
+      sw.finish(mapC, buf, lane, n0 + c, row0, EPI == kEpiF32 && ep.accumulate);
+    }
+  } else if constexpr (EPI == kEpiGeglu) {
+    // Tile columns [0, BN/2) are GELU inputs, [BN/2, BN) their gates.
+    constexpr int H2 = BN / 2;
+    const int g0 = n0 / 2;
+#pragma unroll 1
+    for (int c = g * 32; c < H2; c += 32 * kPGroups) {
+      if (g0 + c >= ep.geglu_n) continue;
+      uint8_t *buf = sw.begin(lane);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        uint32_t ra[16], rg[16];
+        tmem_ld_32x32b_x16(tbase + c + 16 * h, ra);
+        tmem_ld_32x32b_x16(tbase + H2 + c + 16 * h, rg);
+        tmem_ld_wait();
+        float a[16], gt[16];
+        dequant16(ra, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, a);
+        dequant16(rg, ep.sb, ep.zc, n0 + H2 + c + 16 * h, N, sa, gt);
+        const int i0 = g0 + c + 16 * h;  // GeGLU column of a[0]
+        if (i0 + 16 <= (ep.geglu_n & ~15)) {
+#pragma unroll
+          for (int k = 0; k < 16; k += 2) {
+            const float2 o2 = gelu_mul_fma2(make_float2(a[k], a[k + 1]), make_float2(gt[k], gt[k + 1]));
+            a[k] = o2.x;
+            a[k + 1] = o2.y;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; k++) a[k] = gelu_mul_at(a[k], gt[k], i0 + k, ep.geglu_n);
+        }
+        StageWriter::put_half(buf, lane, h, a);
+      }
+      sw.finish(mapC, buf, lane, g0 + c, row0, false);
+    }
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
     gemm_persist_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
@@ -251,61 +314,7 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
       const int row0 = m0 + q * 32;
       const uint32_t tbase = tmem + b * BN + ((uint32_t)(q * 32) << 16);
       const float sa = (EPI != kEpiI32 && row_ok) ? __ldg(ep.sa + row) : 0.0f;
-      if constexpr (EPI == kEpiF32 || EPI == kEpiI32) {
-#pragma unroll 1
-        for (int c = g * 32; c < BN; c += 32 * kPGroups) {
-          if (n0 + c >= N) continue;
-          uint8_t *buf = sw.begin(lane);
-#pragma unroll
-          for (int h = 0; h < 2; h++) {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(tbase + c + 16 * h, r);
-            tmem_ld_wait();
-            float v[16];
-            if constexpr (EPI == kEpiI32) {
-#pragma unroll
-              for (int k = 0; k < 16; k++) v[k] = __int_as_float((int)r[k]);
-            } else {
-              dequant16(r, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, v);
-            }
-            StageWriter::put_half(buf, lane, h, v);
-          }
-          sw.finish(&mapC, buf, lane, n0 + c, row0, EPI == kEpiF32 && ep.accumulate);
-        }
-      } else if constexpr (EPI == kEpiGeglu) {
-        // Tile columns [0, BN/2) are GELU inputs, [BN/2, BN) their gates.
-        constexpr int H2 = BN / 2;
-        const int g0 = n0 / 2;
-#pragma unroll 1
-        for (int c = g * 32; c < H2; c += 32 * kPGroups) {
-          if (g0 + c >= ep.geglu_n) continue;
-          uint8_t *buf = sw.begin(lane);
-#pragma unroll
-          for (int h = 0; h < 2; h++) {
-            uint32_t ra[16], rg[16];
-            tmem_ld_32x32b_x16(tbase + c + 16 * h, ra);
-            tmem_ld_32x32b_x16(tbase + H2 + c + 16 * h, rg);
-            tmem_ld_wait();
-            float a[16], gt[16];
-            dequant16(ra, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, a);
-            dequant16(rg, ep.sb, ep.zc, n0 + H2 + c + 16 * h, N, sa, gt);
-            const int i0 = g0 + c + 16 * h;  // GeGLU column of a[0]
-            if (i0 + 16 <= (ep.geglu_n & ~15)) {
-#pragma unroll
-              for (int k = 0; k < 16; k += 2) {
-                const float2 o2 = gelu_mul_fma2(make_float2(a[k], a[k + 1]), make_float2(gt[k], gt[k + 1]));
-                a[k] = o2.x;
-                a[k + 1] = o2.y;
-              }
-            } else {
-#pragma unroll
-              for (int k = 0; k < 16; k++) a[k] = gelu_mul_at(a[k], gt[k], i0 + k, ep.geglu_n);
-            }
-            StageWriter::put_half(buf, lane, h, a);
-          }
-          sw.finish(&mapC, buf, lane, g0 + c, row0, false);
-        }
-      }
+      epilogue_tile<BN, EPI, kPGroups>(tbase, n0, N, row0, sa, g, lane, sw, &mapC, ep);
       // This accumulator buffer is drained: hand it back to the MMA warp.
       tc_fence_before();
       __syncwarp();

@@ -277,6 +277,8 @@ class Model:
         bad = C.c_int32(0)
         rc = lib().or_encode(self._h, ids, offs, nseq, mode, out, threads, 1 if fast else 0,
                              C.byref(dump) if dump is not None else None, C.byref(bad))
+        if rc == 2:
+            raise ValueError("modernbert: inconsistent batch")
         if rc != 0:
             raise ValueError(f"modernbert: id {bad.value} out of vocabulary")
         return (out, arrays) if dump_layer is not None else out

@@ -137,6 +137,10 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
               int threads, int fast, or_dump *dump, int32_t *bad_id) {
   const or_config &cfg = m->cfg;
   const int H = cfg.hidden, I = cfg.intermediate, nh = cfg.heads, D = H / nh, half = D / 2, VL = cfg.V;
+  // infer.go:245-247: a consistent batch (offsets from 0, non-decreasing).
+  if (nseq < 0 || offs[0] != 0) return 2;
+  for (int i = 0; i < nseq; i++)
+    if (offs[i + 1] < offs[i]) return 2;
   const int64_t N = offs[nseq];
   // infer.go:307-315: every id in [0, vocab).
   for (int64_t t = 0; t < N; t++)

@@ -137,7 +137,8 @@ void or_model_packed(const or_model *m, int l, int which, const int8_t **q, cons
                      const float **zc, int *k, int *n);
 
 /* mode: 0 pooled (mean or CLS per config) [nseq][H]; 1 token states [N][H].
- * Returns 0, or 1 with *bad_id set when an id is out of the vocabulary.
+ * Returns 0, 1 with *bad_id set when an id is out of the vocabulary, or 2 for
+ * offsets that do not start at 0 or decrease.
  * threads <= 1: scalar reference loops. threads > 1 or fast != 0: the CPU
  * baseline (cpu_baseline.cpp), bitwise equal to the scalar loops. */
 int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int nseq, int mode, float *out,

@@ -66,6 +66,23 @@ def test_c1_batch_bitexact(igdev, oracle_lib):
     assert np.array_equal(_bits(got), _bits(ref))
 
 
+def test_c1_varlen_bitexact(igdev, oracle_lib):
+    """C1's dimensions on ragged sequences (1..200 tokens: partial GEMM row
+    blocks, the fused short-sequence attention and the tensor-core attention
+    for sequences over 128 tokens), through the pooled, per-token and dump
+    entry points, bit for bit."""
+    from indecis_b200 import synthetic as S
+    om, gm, _ = _models(S.C1, gamma_noise=0.1)
+    ids, offs = S.ids_varlen(40, 1, 200, S.C1["vocab"], seed=21)
+    ref_tok = om.encode(ids, offs, mode=1, threads=8)
+    got_tok = gm.EncodeTokens((ids, offs))
+    assert np.array_equal(_bits(got_tok), _bits(ref_tok))
+    ref = om.encode(ids, offs, threads=8)
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(ref))
+    out, _ = gm.encode_dump((ids, offs), layer=3)
+    assert np.array_equal(_bits(out), _bits(ref))
+
+
 def test_batch_composition_and_threads(tiny):
     """concurrency_test.go:12: a sequence's result is the same alone, in any
     batch, and under concurrent calls on one shared model."""

@@ -233,3 +233,15 @@ def test_out_of_vocabulary(oracle_lib):
     m = oracle.Model(cfg, S.weights(cfg))
     with pytest.raises(ValueError, match="id 50 out of vocabulary"):
         m.encode(np.array([1, 50], np.int32), np.array([0, 2], np.int64))
+
+
+def test_encode_rejects_inconsistent_offsets(oracle_lib):
+    """infer.go:245-247: offsets must start at 0 and never decrease."""
+    import oracle
+    from indecis_b200 import synthetic as S
+    cfg = S.tiny(layers=1, hidden=64, heads=2, intermediate=96, vocab=100)
+    om = oracle.Model(cfg, S.weights(cfg))
+    ids = np.arange(10, dtype=np.int32)
+    for offs in ([0, 6, 4, 10], [1, 5, 10]):
+        with pytest.raises(ValueError, match="inconsistent"):
+            om.encode(ids, np.asarray(offs, np.int64))
