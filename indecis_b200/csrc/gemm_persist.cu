@@ -37,30 +37,38 @@ struct PEpi {
 template <int BN, int EPI>
 struct PGemmSmem {
   static constexpr int kEpiWarps = PEpi<EPI>::kWarps;
-  // K is a few 128-byte blocks per tile here (hidden sizes of a few hundred),
-  // so two to four stages keep the tensor cores fed; the rest of shared
-  // memory double-buffers the epilogue warps' staging.
-  static constexpr int kStages = kEpiWarps == 16 ? (BN == 256 ? 2 : 3) : (BN == 256 ? 3 : 4);
+  // Two staging buffers per epilogue warp. The plain epilogue holds the
+  // column scales in shared memory (when N <= kMaxCols); the GeGLU one, with
+  // twice the warps, reads them from global memory.
+  static constexpr int kStageBufs = 2;
+  static constexpr int kMaxCols = EPI == kEpiGeglu ? 0 : 1024;
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStaging = kStages * kStageBytes;  // per epilogue warp 2 x [32 rows][128 B]
-  static constexpr int kBar = kStaging + kEpiWarps * 2 * 4096;
+  static constexpr int kStagingBytes = kEpiWarps * kStageBufs * 4096;
+  // K is a few 128-byte blocks per tile here (hidden sizes of a few hundred),
+  // so two to four stages keep the tensor cores fed.
+  static constexpr int kStagesRaw = (224 * 1024 - kStagingBytes - 8 * kMaxCols) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 4 ? 4 : kStagesRaw;
+  static constexpr int kStaging = kStages * kStageBytes;  // per epilogue warp kStageBufs x [32 rows][128 B]
+  static constexpr int kCols = kStaging + kStagingBytes;  // sb[kMaxCols], zc[kMaxCols]
+  static constexpr int kBar = kCols + 8 * kMaxCols;
   static constexpr int kTmemSlot = kBar + 8 * (2 * kStages + 4);
   static constexpr int kTotal = kTmemSlot + 16 + 1024;
+  static_assert(kStages >= 2, "two stages at least");
   static_assert(kTotal <= 227 * 1024, "shared memory");
 };
 
 // Dequantized accumulators of columns j0..j0+15, the column scales read four
-// at a time (sb, zc 16-byte aligned; columns past N read column N-1 and are
-// clipped by the store).
+// at a time (sb, zc 16-byte aligned, in shared or global memory; columns past
+// N read column N-1 and are clipped by the store).
 __device__ __forceinline__ void dequant16(const uint32_t (&r)[16], const float *__restrict__ sb,
                                           const float *__restrict__ zc, int j0, int N, float sa, float (&o)[16]) {
   if (j0 + 16 <= N) {
 #pragma unroll
     for (int k = 0; k < 16; k += 4) {
-      const float4 b = __ldg(reinterpret_cast<const float4 *>(sb + j0 + k));
-      const float4 z = __ldg(reinterpret_cast<const float4 *>(zc + j0 + k));
+      const float4 b = *reinterpret_cast<const float4 *>(sb + j0 + k);
+      const float4 z = *reinterpret_cast<const float4 *>(zc + j0 + k);
       const float2 lo = dequant2((int32_t)r[k], (int32_t)r[k + 1], make_float2(z.x, z.y), make_float2(b.x, b.y), sa);
       const float2 hi =
           dequant2((int32_t)r[k + 2], (int32_t)r[k + 3], make_float2(z.z, z.w), make_float2(b.z, b.w), sa);
@@ -73,7 +81,7 @@ __device__ __forceinline__ void dequant16(const uint32_t (&r)[16], const float *
 #pragma unroll
     for (int k = 0; k < 16; k++) {
       const int j = min(j0 + k, N - 1);
-      o[k] = dequant1((int32_t)r[k], __ldg(zc + j), __ldg(sb + j), sa);
+      o[k] = dequant1((int32_t)r[k], zc[j], sb[j], sa);
     }
   }
 }
@@ -101,13 +109,14 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 
 // One warp's 32 x 32 float sub-tile: thread = row; writes the row into the
 // 128-byte-swizzled staging buffer, then lane 0 issues the bulk store.
+template <int NBUF>
 struct StageWriter {
-  uint8_t *bufs;  // two 4 KB buffers, used in turn
+  uint8_t *bufs;  // NBUF 4 KB buffers, used in turn
   int count = 0;
   // The next buffer, once the bulk store that last used it has read it.
   __device__ __forceinline__ uint8_t *begin(int lane) {
-    uint8_t *b = bufs + (count & 1) * 4096;
-    if (lane == 0) bulk_wait_read<1>();
+    uint8_t *b = bufs + (count % NBUF) * 4096;
+    if (lane == 0) bulk_wait_read<NBUF - 1>();
     __syncwarp();
     return b;
   }
@@ -146,9 +155,10 @@ struct StageWriter {
 
 // One output tile's epilogue for one warp: TMEM lane quarter at tbase (row0 its
 // first row, sa the thread's row scale), column chunks g, g + GROUPS, ...
-template <int BN, int EPI, int GROUPS>
+template <int BN, int EPI, int GROUPS, int NBUF>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int row0, float sa, int g, int lane,
-                                              StageWriter &sw, const CUtensorMap *mapC, const GemmEpilogue &ep) {
+                                              StageWriter<NBUF> &sw, const CUtensorMap *mapC,
+                                              const GemmEpilogue &ep) {
   constexpr int kPGroups = GROUPS;
   if constexpr (EPI == kEpiF32 || EPI == kEpiI32) {
 #pragma unroll 1
@@ -167,7 +177,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int
         } else {
           dequant16(r, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, v);
         }
-        StageWriter::put_half(buf, lane, h, v);
+        StageWriter<NBUF>::put_half(buf, lane, h, v);
       }
       sw.finish(mapC, buf, lane, n0 + c, row0, EPI == kEpiF32 && ep.accumulate);
     }
@@ -200,7 +210,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int
 #pragma unroll
           for (int k = 0; k < 16; k++) a[k] = gelu_mul_at(a[k], gt[k], i0 + k, ep.geglu_n);
         }
-        StageWriter::put_half(buf, lane, h, a);
+        StageWriter<NBUF>::put_half(buf, lane, h, a);
       }
       sw.finish(mapC, buf, lane, g0 + c, row0, false);
     }
@@ -301,7 +311,19 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
     const int q = warp & 3;            // TMEM lane quarter
     const int e = warp - 2;            // epilogue warp 0..7
     const int g = e >> 2;              // column chunks g, g + kPGroups, ...
-    StageWriter sw{smem + S::kStaging + e * 8192};
+    StageWriter<S::kStageBufs> sw{smem + S::kStaging + e * S::kStageBufs * 4096};
+    // The column scales in shared memory, once per CTA.
+    GemmEpilogue eps = ep;
+    if (N <= S::kMaxCols && EPI == kEpiF32) {
+      float *s_sb = reinterpret_cast<float *>(smem + S::kCols), *s_zc = s_sb + S::kMaxCols;
+      for (int j = threadIdx.x - 64; j < N; j += 32 * PEpi<EPI>::kWarps) {
+        s_sb[j] = __ldg(ep.sb + j);
+        s_zc[j] = __ldg(ep.zc + j);
+      }
+      named_barrier_sync(2, 32 * PEpi<EPI>::kWarps);
+      eps.sb = s_sb;
+      eps.zc = s_zc;
+    }
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
       const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
@@ -314,7 +336,7 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
       const int row0 = m0 + q * 32;
       const uint32_t tbase = tmem + b * BN + ((uint32_t)(q * 32) << 16);
       const float sa = (EPI != kEpiI32 && row_ok) ? __ldg(ep.sa + row) : 0.0f;
-      epilogue_tile<BN, EPI, kPGroups>(tbase, n0, N, row0, sa, g, lane, sw, &mapC, ep);
+      epilogue_tile<BN, EPI, kPGroups, S::kStageBufs>(tbase, n0, N, row0, sa, g, lane, sw, &mapC, eps);
       // This accumulator buffer is drained: hand it back to the MMA warp.
       tc_fence_before();
       __syncwarp();
