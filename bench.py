@@ -205,7 +205,21 @@ def run_reference(args, world, rank):
 # GPU leg
 # ---------------------------------------------------------------------------
 
-def roofline(report, pk):
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch
+# per sequence, from one ncu capture of the C1 workload at 512 sequences
+# (profiles/attn_short_c1_512seq.txt, profiles/gemm_rows_c1_512seq.txt); a
+# launch processes the whole step's sequences, so the per-launch traffic is
+# this times the sequences per step (traffic grows with the sequences).
+NCU_BYTES_PER_SEQ = {
+    "attn_short": (201441536 + 38391040) / 512,
+    "gemm_qkv": (21466368 + 145374976) / 512,
+    "gemm_wo_residual": (88436736 + 11129856) / 512,
+    "gemm_wi_geglu": (21517824 + 42096384) / 512,
+    "ln_quant": (67132672 + 3182080) / 512,
+}
+
+
+def roofline(report, pk, nseq):
     ks = [k for k in report["kernels"] if k["records"] > 0 and k["ms"] > 0]
     top = max(ks, key=lambda k: k["ms"])
     total_ms = sum(k["ms"] for k in ks)
@@ -224,7 +238,10 @@ def roofline(report, pk):
         rf = {"bound": "hbm", "achieved": ach, "peak": pk["hbm"], "unit": "GB/s", "frac": ach / pk["hbm"]}
         peak_note = f"{pk['src']} HBM copy bandwidth"
     rf.update({"kernel": top["name"], "share": top["ms"] / total_ms, "ms_per_launch": per_ms,
-               "algorithmic_bytes": bytes_, "algorithmic_ops": ops, "peak_source": peak_note, "traffic": None})
+               "algorithmic_bytes": bytes_, "algorithmic_ops": ops, "peak_source": peak_note})
+    per_seq = NCU_BYTES_PER_SEQ.get(top["name"])
+    rf["traffic"] = per_seq * nseq if per_seq else None
+    rf["traffic_source"] = "ncu dram bytes at 512 sequences, scaled" if per_seq else None
     return rf
 
 
@@ -358,7 +375,7 @@ def run_ours(args, world, rank, local):
         line = {"metric": METRIC, "value": value, "unit": "seq/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config_obj(args, world),
-                "e2e": e2e, "gpu_launches": report["launches"], "roofline": roofline(report, pk),
+                "e2e": e2e, "gpu_launches": report["launches"], "roofline": roofline(report, pk, nseq),
                 "kernels": {k["name"]: {"ms": round(k["ms"], 3), "launches": k["launches"]}
                             for k in report["kernels"]},
                 "clocks": clk, "cpu_baseline": cpu, "gemm_sweep": gemm}
