@@ -60,7 +60,8 @@ typedef struct ig_config {
  * Per-layer arrays have `layers` entries; attn_norm[0] is ignored (layer 0
  * has no attention norm). Weights are copied; the views are not retained. */
 typedef struct ig_weights {
-  const float *tok_embeddings; /* [vocab][hidden] embeddings.tok_embeddings.weight */
+  const float *tok_embeddings; /* [vocab][hidden] embeddings.tok_embeddings.weight, or NULL when
+                                  ig_model_set_embeddings supplies the table */
   const float *emb_norm;       /* [hidden] embeddings.norm.weight */
   const float *final_norm;     /* [hidden] final_norm.weight */
   const float *const *attn_norm; /* [hidden] layers.%d.attn_norm.weight */
@@ -82,6 +83,25 @@ typedef struct ig_head {
 
 typedef struct ig_model ig_model;
 
+/* Embedding table formats (embeddings.go:9-68). */
+#define IG_EMB_F32 0  /* float32 [vocab][hidden] */
+#define IG_EMB_BF16 1 /* bf16 [vocab][hidden] (value = bits << 16), with float32 rows for some ids */
+#define IG_EMB_INT8 2 /* int8 [vocab][hidden] times a float32 scale per row */
+
+/* An embedding table as the reference's mappedEmbeddings holds it
+ * (newMappedEmbeddings, newInt8Embeddings: embeddings.go:24-47). Only the
+ * fields of `format` are read. */
+typedef struct ig_embedding_table {
+  int32_t format;
+  const float *f32;         /* IG_EMB_F32: [vocab][hidden] */
+  const uint16_t *bf16;     /* IG_EMB_BF16: [vocab][hidden] bf16 bits */
+  int32_t n_exact;          /* IG_EMB_BF16: rows kept in float32 */
+  const int32_t *exact_ids; /* [n_exact] token ids, each in [0, vocab) */
+  const float *exact_rows;  /* [n_exact][hidden] */
+  const int8_t *i8;         /* IG_EMB_INT8: [vocab][hidden] */
+  const float *scale;       /* IG_EMB_INT8: [vocab] */
+} ig_embedding_table;
+
 /* Replaces modernbert.FromTensors + SetInt8(true) + the first-use packing
  * (infer.go:119-135, :184-219): validates the config, uploads the weights to
  * `device` and quantizes each layer matrix per output channel (PackB8,
@@ -91,6 +111,15 @@ IG_API int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t de
 /* Releases the model's device memory. Replaces Invalidate (infer.go:95-100)
  * for the device copy: a changed model is destroyed and created again. */
 IG_API void ig_model_destroy(ig_model *m);
+
+/* Replaces SetEmbeddingTable (internal/modernbert/infer.go:20-25) with a
+ * table uploaded in its stored format and read row by row in the embedding
+ * gather (Row, embeddings.go:49-68): bf16 rows widen exactly (bits << 16), an
+ * id listed in exact_ids takes its float32 row, int8 rows are
+ * float32(int8) * scale[id]. Copied; replaces the table given at creation.
+ * Must not run concurrently with an encode on the same model. Errors:
+ * IG_ERR_BAD_ARG ("indecis: exact row %d out of vocabulary", a missing array). */
+IG_API int ig_model_set_embeddings(ig_model *m, const ig_embedding_table *t);
 
 /* Replaces the heads of Model (heads.go:29-48, model.go:312-341); copied. */
 IG_API int ig_model_set_heads(ig_model *m, int32_t nheads, const ig_head *heads);

@@ -25,7 +25,11 @@ IG_MODE_TOKENS = 1
 SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_encode", "ig_encode_device",
            "ig_logits", "ig_last_error", "ig_device_error", "ig_gemm_u8s8", "ig_quantize_rows",
            "ig_layernorm_quant", "ig_pack_b8", "ig_attention", "ig_encode_dump", "ig_logits_device",
-           "ig_profile", "ig_profile_report", "ig_attention_noalloc"]
+           "ig_profile", "ig_profile_report", "ig_attention_noalloc", "ig_model_set_embeddings"]
+
+IG_EMB_F32 = 0
+IG_EMB_BF16 = 1
+IG_EMB_INT8 = 2
 
 
 class IgConfig(C.Structure):
@@ -40,6 +44,11 @@ class IgWeights(C.Structure):
                 ("attn_norm", C.POINTER(C.c_void_p)), ("wqkv", C.POINTER(C.c_void_p)),
                 ("wo", C.POINTER(C.c_void_p)), ("mlp_norm", C.POINTER(C.c_void_p)),
                 ("wi", C.POINTER(C.c_void_p)), ("wo_mlp", C.POINTER(C.c_void_p))]
+
+
+class IgEmbeddingTable(C.Structure):
+    _fields_ = [("format", C.c_int32), ("f32", C.c_void_p), ("bf16", C.c_void_p), ("n_exact", C.c_int32),
+                ("exact_ids", C.c_void_p), ("exact_rows", C.c_void_p), ("i8", C.c_void_p), ("scale", C.c_void_p)]
 
 
 class IgHead(C.Structure):
@@ -86,6 +95,7 @@ def load() -> C.CDLL:
     L.ig_encode_dump.argtypes = [vp, vp, vp, i32, i32, vp, C.c_size_t, C.POINTER(IgDump)]
     L.ig_logits_device.argtypes = [vp, vp, vp, i32, vp, vp, vp]
     L.ig_attention_noalloc.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
+    L.ig_model_set_embeddings.argtypes = [vp, C.POINTER(IgEmbeddingTable)]
     L.ig_profile.argtypes = [i32]
     L.ig_profile_report.argtypes = [C.c_char_p, C.c_size_t]
     L.ig_profile_report.restype = C.c_int64

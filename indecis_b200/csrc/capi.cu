@@ -175,7 +175,9 @@ struct ig_model {
   ig_config cfg{};
   int device = 0;
   int H = 0, I = 0, nh = 0, D = 0, ldk = 0, NI = 0;
-  float *emb = nullptr, *emb_norm = nullptr, *final_norm = nullptr;
+  EmbTable emb{-1, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};  // fmt -1: no table yet
+  std::vector<void *> emb_allocs;  // the table's device arrays (replaced by ig_model_set_embeddings)
+  float *emb_norm = nullptr, *final_norm = nullptr;
   std::vector<DevLayer> layers;
   std::mutex mu;  // rope tables, heads, workspace pool
   int rope_npos = 0;
@@ -191,6 +193,7 @@ struct ig_model {
     cudaDeviceSynchronize();
     pool.clear();
     for (void *p : allocs) cudaFree(p);
+    for (void *p : emb_allocs) cudaFree(p);
     for (void *p : retired) cudaFree(p);
     for (auto &h : heads) {
       cudaFree(h.w);
@@ -508,6 +511,7 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
   if (N == 0) return 0;
   {
     ProfScope ps("embed_ln_quant", (double)N * (8 + 9.0 * H) + 4.0 * H, 0, 1, st, capturing);
+    if (m->emb.fmt < 0) return fail(IG_ERR_BAD_ARG, "modernbert: no embedding table");
     IG_TRY(launch_embed_checked(d_ids, c.vocab, m->emb, m->emb_norm, N, H, c.norm_eps, V, w.x, w.xq, m->ldk, w.sa,
                                 st));
   }
@@ -785,7 +789,14 @@ int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, i
   m->ldk = (int)align_up(std::max(c.hidden, c.intermediate), 16);
   m->NI = (c.intermediate + 127) / 128 * 256;
   const int H = m->H, I = m->I;
-  IG_TRY(upload(m.get(), &m->emb, w->tok_embeddings, (size_t)c.vocab * H));
+  if (w->tok_embeddings) {
+    float *e = nullptr;
+    IG_CU(cudaMalloc(&e, (size_t)c.vocab * H * sizeof(float)));
+    m->emb_allocs.push_back(e);
+    IG_CU(cudaMemcpy(e, w->tok_embeddings, (size_t)c.vocab * H * sizeof(float), cudaMemcpyHostToDevice));
+    m->emb.fmt = IG_EMB_F32;
+    m->emb.f32 = e;
+  }
   IG_TRY(upload(m.get(), &m->emb_norm, w->emb_norm, H));
   IG_TRY(upload(m.get(), &m->final_norm, w->final_norm, H));
   float *tmp = nullptr;
@@ -821,6 +832,58 @@ int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, i
 }
 
 void ig_model_destroy(ig_model *m) { delete m; }
+
+int ig_model_set_embeddings(ig_model *m, const ig_embedding_table *t) {
+  t_last_error.clear();
+  if (!m || !t) return fail(IG_ERR_BAD_ARG, "null argument");
+  const int V = m->cfg.vocab, H = m->H;
+  DeviceGuard dg(m->device);
+  EmbTable e{t->format, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  std::vector<void *> allocs;
+  auto put = [&](const void *src, size_t bytes) -> void * {
+    void *d = nullptr;
+    if (cudaMalloc(&d, std::max<size_t>(bytes, 16)) != cudaSuccess) return nullptr;
+    allocs.push_back(d);
+    if (bytes && cudaMemcpy(d, src, bytes, cudaMemcpyHostToDevice) != cudaSuccess) return nullptr;
+    return d;
+  };
+  auto undo = [&](int code, const std::string &msg) {
+    for (void *p : allocs) cudaFree(p);
+    return fail(code, msg);
+  };
+  if (t->format == IG_EMB_F32) {
+    if (!t->f32) return fail(IG_ERR_BAD_ARG, "indecis: float32 table missing");
+    if (!(e.f32 = (const float *)put(t->f32, (size_t)V * H * 4))) return undo(IG_ERR_CUDA, "cudaMalloc failed");
+  } else if (t->format == IG_EMB_BF16) {
+    if (!t->bf16 || t->n_exact < 0 || (t->n_exact && (!t->exact_ids || !t->exact_rows)))
+      return fail(IG_ERR_BAD_ARG, "indecis: malformed exact rows");
+    // newMappedEmbeddings (embeddings.go:33-47): id -> rank, a later listing of
+    // an id replacing an earlier one, as the reference's map does.
+    std::vector<int32_t> idx(V, -1);
+    for (int i = 0; i < t->n_exact; i++) {
+      const int id = t->exact_ids[i];
+      if (id < 0 || id >= V) return fail(IG_ERR_BAD_ARG, "indecis: exact row " + std::to_string(id) + " out of vocabulary");
+      idx[id] = i;
+    }
+    if (!(e.bf16 = (const uint16_t *)put(t->bf16, (size_t)V * H * 2)) ||
+        !(e.exact_idx = (const int32_t *)put(idx.data(), (size_t)V * 4)) ||
+        !(e.exact_rows = (const float *)put(t->exact_rows, (size_t)t->n_exact * H * 4)))
+      return undo(IG_ERR_CUDA, "cudaMalloc failed");
+  } else if (t->format == IG_EMB_INT8) {
+    if (!t->i8 || !t->scale) return fail(IG_ERR_BAD_ARG, "indecis: int8 table or scales missing");
+    if (!(e.i8 = (const int8_t *)put(t->i8, (size_t)V * H)) || !(e.scale = (const float *)put(t->scale, (size_t)V * 4)))
+      return undo(IG_ERR_CUDA, "cudaMalloc failed");
+  } else {
+    return fail(IG_ERR_BAD_ARG, "unknown embedding table format");
+  }
+  // The old table is released once no queued work can read it.
+  std::lock_guard<std::mutex> lk(m->mu);
+  cudaDeviceSynchronize();
+  for (void *p : m->emb_allocs) cudaFree(p);
+  m->emb_allocs = std::move(allocs);
+  m->emb = e;
+  return 0;
+}
 
 int ig_model_set_heads(ig_model *m, int32_t nheads, const ig_head *heads) {
   t_last_error.clear();

@@ -36,8 +36,30 @@ int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t s
 // uint8 q [M][ldq] + sa. gamma == nullptr: no norm, quantize x itself.
 int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps, int V, float *xn, uint8_t *q,
                     int ldq, float *sa, cudaStream_t st);
+// An embedding table on the device in its stored format (Row,
+// embeddings.go:49-68): f32 rows; bf16 rows widened exactly, with float32
+// rows for the ids whose exact_idx >= 0; or int8 rows times a row scale.
+struct EmbTable {
+  int fmt;  // IG_EMB_F32 / IG_EMB_BF16 / IG_EMB_INT8
+  const float *f32;
+  const uint16_t *bf16;
+  const int32_t *exact_idx;  // [vocab] -> row of exact_rows, or -1
+  const float *exact_rows;
+  const int8_t *i8;
+  const float *scale;
+};
+// Element j of row id (id in range).
+__device__ __forceinline__ float emb_elem(const EmbTable &t, int id, int j, int H) {
+  if (t.fmt == IG_EMB_BF16) {
+    const int e = __ldg(t.exact_idx + id);
+    if (e >= 0) return __ldg(t.exact_rows + (size_t)e * H + j);
+    return __uint_as_float((uint32_t)__ldg(t.bf16 + (size_t)id * H + j) << 16);
+  }
+  if (t.fmt == IG_EMB_INT8) return __fmul_rn((float)__ldg(t.i8 + (size_t)id * H + j), __ldg(t.scale + id));
+  return __ldg(t.f32 + (size_t)id * H + j);
+}
 // Embedding gather then LayerNorm: x = LN(emb[ids]) (f32), and its quantized copy.
-int launch_embed_checked(const int32_t *ids, int vocab, const float *emb, const float *gamma, int M, int H,
+int launch_embed_checked(const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M, int H,
                          double eps, int V, float *x, uint8_t *q, int ldq, float *sa, cudaStream_t st);
 // Per-row quantization of f32 rows (ld elements apart).
 int launch_quant_rows(const float *x, int ldx, int M, int K, uint8_t *q, int ldq, float *sa, cudaStream_t st);

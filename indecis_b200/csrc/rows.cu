@@ -23,7 +23,7 @@ constexpr int kRowWarps = 8;
 
 // Several rows per warp (rows_ln.cu); -1 when it does not apply.
 template <bool EMBED>
-static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const float *emb, const float *gamma, int M,
+static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M,
                            int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa, cudaStream_t st);
 
 // Per-row quantization of the n values in s_row (shared), by one warp.
@@ -101,7 +101,7 @@ __global__ void ln_quant_kernel(const float *__restrict__ x, const float *__rest
 
 // Embedding gather (infer.go:361-367) + LayerNorm(emb_norm) (:368). An id
 // outside [0, vocab) is recorded in g_device_error and reads row 0.
-__global__ void embed_ln_quant_kernel(const int32_t *__restrict__ ids, int vocab, const float *__restrict__ emb,
+__global__ void embed_ln_quant_kernel(const int32_t *__restrict__ ids, int vocab, const EmbTable emb,
                                       const float *__restrict__ gamma, int M, int H, double eps, int V,
                                       float *__restrict__ x, uint8_t *__restrict__ q, int ldq, float *__restrict__ sa) {
   extern __shared__ float s_rows[];
@@ -114,8 +114,7 @@ __global__ void embed_ln_quant_kernel(const int32_t *__restrict__ ids, int vocab
     if (lane == 0) set_device_error(kDevBadId);
     id = 0;
   }
-  const float *src = emb + (size_t)id * H;
-  for (int i = lane; i < H; i += 32) s_x[i] = __ldg(src + i);
+  for (int i = lane; i < H; i += 32) s_x[i] = emb_elem(emb, id, i, H);
   __syncwarp();
   layernorm_warp(s_x, gamma, H, eps, V, lane);
   float *dst = x + (size_t)row * H;
@@ -253,9 +252,9 @@ int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps
                     int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
   if (gamma) {
-    int rc = launch_ln8<false>(x, nullptr, 0, nullptr, gamma, M, H, eps, V, xn, q, ldq, sa, st);
+    int rc = launch_ln8<false>(x, nullptr, 0, EmbTable{}, gamma, M, H, eps, V, xn, q, ldq, sa, st);
     if (rc != -1) return rc;
-    rc = launch_ln_group<false>(x, nullptr, 0, nullptr, gamma, M, H, eps, V, xn, q, ldq, sa, st);
+    rc = launch_ln_group<false>(x, nullptr, 0, EmbTable{}, gamma, M, H, eps, V, xn, q, ldq, sa, st);
     if (rc != -1) return rc;
   }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;
@@ -265,7 +264,7 @@ int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 
-int launch_embed_checked(const int32_t *ids, int vocab, const float *emb, const float *gamma, int M, int H,
+int launch_embed_checked(const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M, int H,
                          double eps, int V, float *x, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
   {

@@ -35,7 +35,7 @@ __device__ __forceinline__ uint32_t quant_byte_slow(float v, float inv) {
 
 template <int NB, bool EMBED>
 __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, const int32_t *__restrict__ ids,
-                                                  int vocab, const float *__restrict__ emb,
+                                                  int vocab, const EmbTable emb,
                                                   const float *__restrict__ gamma, int M, double eps,
                                                   float *__restrict__ xout, uint8_t *__restrict__ q, int ldq,
                                                   float *__restrict__ sa) {
@@ -45,20 +45,26 @@ __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 3, k = lane & 7;
   const int row = (blockIdx.x * 8 + warp) * 4 + r;
   const bool rv = row < M;
-  const float *src;
+  float v[NB];
   if constexpr (EMBED) {
     int id = rv ? ids[row] : 0;
     if (id < 0 || id >= vocab) {
       set_device_error(kDevBadId);
       id = 0;
     }
-    src = emb + (size_t)id * H;
-  } else {
-    src = x + (size_t)(rv ? row : 0) * H;
-  }
-  float v[NB];
+    if (emb.fmt == IG_EMB_F32) {
+      const float *src = emb.f32 + (size_t)id * H;
 #pragma unroll
-  for (int b = 0; b < NB; b++) v[b] = rv ? __ldg(src + k + 8 * b) : 0.0f;
+      for (int b = 0; b < NB; b++) v[b] = rv ? __ldg(src + k + 8 * b) : 0.0f;
+    } else {
+#pragma unroll
+      for (int b = 0; b < NB; b++) v[b] = rv ? emb_elem(emb, id, k + 8 * b, H) : 0.0f;
+    }
+  } else {
+    const float *src = x + (size_t)(rv ? row : 0) * H;
+#pragma unroll
+    for (int b = 0; b < NB; b++) v[b] = rv ? __ldg(src + k + 8 * b) : 0.0f;
+  }
   float ls = 0.0f;
 #pragma unroll
   for (int b = 0; b < NB; b++) ls = __fadd_rn(ls, v[b]);
@@ -243,7 +249,7 @@ static int launch_head_logits_tok(const float *w, const float *b, int rows, int 
 // LayerNorm (+ quantization) for V = 8 and H in {64, 128, 256}; -1 when this
 // path does not apply.
 template <bool EMBED>
-static int launch_ln8(const float *x, const int32_t *ids, int vocab, const float *emb, const float *gamma, int M,
+static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M,
                       int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   if (V != 8 || !gamma) return -1;
   if (q && ((ldq & 7) || (reinterpret_cast<uintptr_t>(q) & 7))) return -1;

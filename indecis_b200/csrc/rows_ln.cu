@@ -19,7 +19,7 @@ namespace ig {
 
 template <bool EMBED>
 __global__ void ln_group_kernel(const float *__restrict__ x, const int32_t *__restrict__ ids, int vocab,
-                                const float *__restrict__ emb, const float *__restrict__ gamma, int M, int H,
+                                const EmbTable emb, const float *__restrict__ gamma, int M, int H,
                                 double eps, int V, int P, int wpb, float *__restrict__ xout, uint8_t *__restrict__ q,
                                 int ldq, float *__restrict__ sa) {
   extern __shared__ float s_all[];
@@ -31,17 +31,21 @@ __global__ void ln_group_kernel(const float *__restrict__ x, const int32_t *__re
   for (int r = 0; r < rpw && row0 + r < M; r++) {
     const int row = row0 + r;
     const float *src;
+    float *dst = s + r * P;
     if constexpr (EMBED) {
       int id = ids[row];
       if (id < 0 || id >= vocab) {
         if (lane == 0) set_device_error(kDevBadId);
         id = 0;
       }
-      src = emb + (size_t)id * H;
+      if (emb.fmt != IG_EMB_F32) {  // rows widened element by element
+        for (int i = lane; i < H; i += 32) dst[i] = emb_elem(emb, id, i, H);
+        continue;
+      }
+      src = emb.f32 + (size_t)id * H;
     } else {
       src = x + (size_t)row * H;
     }
-    float *dst = s + r * P;
     if ((H & 3) == 0 && (P & 3) == 0) {
       for (int i = lane * 4; i < H; i += 128)
         *reinterpret_cast<float4 *>(dst + i) = __ldg(reinterpret_cast<const float4 *>(src + i));
@@ -143,7 +147,7 @@ static bool ln_group_geometry(int H, int V, int *P, int *wpb, size_t *smem) {
 }
 
 template <bool EMBED>
-static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const float *emb, const float *gamma, int M,
+static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M,
                            int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   int P = 0, wpb = 0;
   size_t smem = 0;

@@ -134,6 +134,48 @@ _TENSOR_NAMES = {
 }
 
 
+class MappedEmbeddings:
+    """indecis mappedEmbeddings (embeddings.go:9-68): bf16 rows [vocab][hidden]
+    (value = bits << 16) with float32 rows for the ids training modified; or
+    an int8 table with a float32 scale per row (newInt8Embeddings). Row gives
+    a row on the host; Model.SetEmbeddingTable uploads the table as stored."""
+
+    def __init__(self, hidden: int, bf16=None, exact_ids=None, exact_rows=None, i8=None, scale=None):
+        self.h = hidden
+        if i8 is not None:
+            self.i8 = np.ascontiguousarray(i8, np.int8)
+            self.scale = np.ascontiguousarray(scale, np.float32)
+            if self.i8.size != len(self.scale) * hidden:
+                raise ModernBertError(f"indecis: int8 table of {self.i8.size} bytes for {len(self.scale)} rows")
+            self.bf16 = None
+            return
+        self.i8 = None
+        self.bf16 = np.ascontiguousarray(bf16, np.uint16).reshape(-1, hidden)
+        ids = np.ascontiguousarray([] if exact_ids is None else exact_ids, np.int32)
+        rows = np.ascontiguousarray(np.zeros((0, hidden)) if exact_rows is None else exact_rows, np.float32)
+        if rows.size != len(ids) * hidden:
+            raise ModernBertError("indecis: malformed exact rows")
+        vocab = self.bf16.shape[0]
+        self.exact = {}
+        for i, r in enumerate(ids.tolist()):
+            if r < 0 or r >= vocab:
+                raise ModernBertError(f"indecis: exact row {r} out of vocabulary")
+            self.exact[r] = i
+        self.exact_ids, self.exact_rows = ids, rows.reshape(len(ids), hidden)
+
+    def Row(self, id_: int) -> np.ndarray:
+        if self.i8 is not None:
+            return (self.i8.reshape(-1, self.h)[id_].astype(np.float32) * self.scale[id_]).astype(np.float32)
+        if id_ in self.exact:
+            return self.exact_rows[self.exact[id_]].copy()
+        return (self.bf16[id_].astype(np.uint32) << 16).view(np.float32)
+
+    def matrix(self) -> np.ndarray:
+        """The whole table in float32 (EmbeddingMatrix, infer.go:39-50)."""
+        vocab = (self.i8.size // self.h) if self.i8 is not None else self.bf16.shape[0]
+        return np.stack([self.Row(i) for i in range(vocab)]).astype(np.float32)
+
+
 class Model:
     """modernbert.Model restricted to int8 inference on one GPU."""
 
@@ -221,6 +263,18 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    # ---- embedding table (infer.go:12-25, embeddings.go) ----
+    def SetEmbeddingTable(self, t: "MappedEmbeddings"):
+        """Replaces the float32 table with t, uploaded in its stored format and
+        widened in the embedding gather."""
+        if t.i8 is not None:
+            tab = _capi.IgEmbeddingTable(format=_capi.IG_EMB_INT8, i8=t.i8.ctypes.data, scale=t.scale.ctypes.data)
+        else:
+            tab = _capi.IgEmbeddingTable(format=_capi.IG_EMB_BF16, bf16=t.bf16.ctypes.data, n_exact=len(t.exact_ids),
+                                         exact_ids=t.exact_ids.ctypes.data, exact_rows=t.exact_rows.ctypes.data)
+        _capi.check(_capi.load().ig_model_set_embeddings(self._h, C.byref(tab)))
+        self.emb_table = t
 
     # ---- switches (infer.go:115-135) ----
     def SetInt8(self, on: bool):
