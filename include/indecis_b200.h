@@ -236,6 +236,76 @@ typedef struct ig_dump {
 IG_API int ig_encode_dump(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
                    size_t out_len, ig_dump *dump);
 
+/* ---- Spans questions (spans.go): long texts read in windows, per-token BIO
+ * tags decoded into passages. The window planning, log-softmax and Viterbi
+ * decoding are host code (no device, callable without a GPU); the encoder
+ * and the per-token heads of ig_infer_windows run on the device. ---- */
+
+/* A slice [start, end) of a text's tokens read in one encoder pass; the
+ * tokens [keep_from, keep_to) take their tags from it (window, spans.go:314). */
+typedef struct ig_window {
+  int32_t start, end, keep_from, keep_to;
+} ig_window;
+
+/* planWindows (spans.go:322-334): cuts n tokens into windows of at most
+ * `size` tokens, each reading up to `margin` tokens (at most (size-1)/4) of
+ * context beside the slice it keeps. *count receives the number of windows;
+ * out (may be NULL) receives them when cap allows, else IG_ERR_BAD_ARG. */
+IG_API int ig_plan_windows(int32_t n, int32_t size, int32_t margin, ig_window *out, int32_t cap, int32_t *count);
+
+/* logSoftmax (spans.go:293-311): out = z/T - log sum exp(z/T), T <= 0 read as 1. */
+IG_API int ig_log_softmax(const double *z, int32_t n, double temperature, double *out);
+
+/* A passage found by a Spans question (Span, spans.go:43-50): bytes
+ * [start, end) of the text, `type` the index of its option. */
+typedef struct ig_span {
+  int32_t type, start, end;
+  double confidence; /* mean probability of the passage's tags */
+} ig_span;
+
+/* decodeSpans (spans.go:172-246): the most probable consistent BIO tag
+ * sequence of logp [ntok][ntags] (log-probabilities; tag 0 outside, 1+2k
+ * begins a passage of type k, 2+2k continues it; bias added to every tag
+ * but outside), then its passages: from the first token's core (its leading
+ * spaces skipped) to the last token's end, edge punctuation trimmed.
+ * offsets [ntok][2] are the tokens' byte ranges in text. *nspans receives
+ * the number of passages (at most ntok); out receives them when cap allows,
+ * else IG_ERR_BAD_ARG. tags (optional, [ntok]) receives the decoded tags. */
+IG_API int ig_decode_spans(const double *logp, int32_t ntok, int32_t ntags, double bias, const char *text,
+                           int64_t text_len, const int32_t *offsets, int32_t *tags, ig_span *out, int32_t cap,
+                           int32_t *nspans);
+
+/* answerSpans (spans.go:479-491): ig_log_softmax of each token's logits
+ * (z [ntok][ldz], the first ntags used) at `temperature`, then
+ * ig_decode_spans. */
+IG_API int ig_answer_spans(const double *z, int32_t ntok, int32_t ldz, int32_t ntags, double temperature, double bias,
+                           const char *text, int64_t text_len, const int32_t *offsets, ig_span *out, int32_t cap,
+                           int32_t *nspans);
+
+/* ig_logits with every sequence pooled by the mean of its rows whatever the
+ * config's pooling (meanRows, spans.go:464-477): the pooled heads of a
+ * model with Spans questions read that mean. */
+IG_API int ig_window_logits(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, double *logits,
+                            size_t logits_len, double *token_logits, size_t token_len);
+
+/* The Spans branch of infer (spans.go:385-461) for ninputs tokenized texts:
+ * ids the texts' tokens end to end (no special tokens), offs[ninputs+1]
+ * their starts. Each text is cut by ig_plan_windows into windows of
+ * max(max_len - nprefix - nsuffix, 1) tokens with a margin of a sixteenth
+ * of that; each window is framed by prefix and suffix and encoded, up to
+ * batch_size windows per device pass (<= 0: all in one). logits
+ * [ninputs][sum of pooled rows] receives the pooled heads of each text's
+ * first window, token_logits [offs[ninputs]][sum of per-token rows] the
+ * per-token heads of each text token, from the window that keeps it. */
+IG_API int ig_infer_windows(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ninputs,
+                            const int32_t *prefix, int32_t nprefix, const int32_t *suffix, int32_t nsuffix,
+                            int32_t max_len, int32_t batch_size, double *logits, size_t logits_len,
+                            double *token_logits, size_t token_len);
+
+/* Rows of the heads set by ig_model_set_heads: *pooled_rows and
+ * *token_rows receive the sums over pooled and per-token heads. */
+IG_API int ig_model_head_rows(ig_model *m, int32_t *pooled_rows, int32_t *token_rows);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,7 +25,9 @@ IG_MODE_TOKENS = 1
 SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_encode", "ig_encode_device",
            "ig_logits", "ig_last_error", "ig_device_error", "ig_gemm_u8s8", "ig_quantize_rows",
            "ig_layernorm_quant", "ig_pack_b8", "ig_attention", "ig_encode_dump", "ig_logits_device",
-           "ig_profile", "ig_profile_report", "ig_attention_noalloc", "ig_model_set_embeddings"]
+           "ig_profile", "ig_profile_report", "ig_attention_noalloc", "ig_model_set_embeddings",
+           "ig_plan_windows", "ig_log_softmax", "ig_decode_spans", "ig_answer_spans", "ig_window_logits",
+           "ig_infer_windows", "ig_model_head_rows"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -53,6 +55,14 @@ class IgEmbeddingTable(C.Structure):
 
 class IgHead(C.Structure):
     _fields_ = [("rows", C.c_int32), ("per_token", C.c_int32), ("w", C.c_void_p), ("b", C.c_void_p)]
+
+
+class IgWindow(C.Structure):
+    _fields_ = [("start", C.c_int32), ("end", C.c_int32), ("keep_from", C.c_int32), ("keep_to", C.c_int32)]
+
+
+class IgSpan(C.Structure):
+    _fields_ = [("type", C.c_int32), ("start", C.c_int32), ("end", C.c_int32), ("confidence", C.c_double)]
 
 
 class IgDump(C.Structure):
@@ -96,6 +106,15 @@ def load() -> C.CDLL:
     L.ig_logits_device.argtypes = [vp, vp, vp, i32, vp, vp, vp]
     L.ig_attention_noalloc.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
     L.ig_model_set_embeddings.argtypes = [vp, C.POINTER(IgEmbeddingTable)]
+    i32p, f64 = C.POINTER(C.c_int32), C.c_double
+    L.ig_plan_windows.argtypes = [i32, i32, i32, C.POINTER(IgWindow), i32, i32p]
+    L.ig_log_softmax.argtypes = [vp, i32, f64, vp]
+    L.ig_decode_spans.argtypes = [vp, i32, i32, f64, C.c_char_p, C.c_int64, vp, vp, C.POINTER(IgSpan), i32, i32p]
+    L.ig_answer_spans.argtypes = [vp, i32, i32, i32, f64, f64, C.c_char_p, C.c_int64, vp, C.POINTER(IgSpan), i32,
+                                  i32p]
+    L.ig_window_logits.argtypes = [vp, vp, vp, i32, vp, C.c_size_t, vp, C.c_size_t]
+    L.ig_infer_windows.argtypes = [vp, vp, vp, i32, vp, i32, vp, i32, i32, i32, vp, C.c_size_t, vp, C.c_size_t]
+    L.ig_model_head_rows.argtypes = [vp, i32p, i32p]
     L.ig_profile.argtypes = [i32]
     L.ig_profile_report.argtypes = [C.c_char_p, C.c_size_t]
     L.ig_profile_report.restype = C.c_int64

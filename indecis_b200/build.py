@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libindecis_b200.so")
-SOURCES = ["libindecis_b200.cu"]
+SOURCES = ["libindecis_b200.cu", "spans.cpp"]
 HEADERS = ["common.cuh", "exactmath.cuh", "internal.h", "gemm_i8.cu", "gemm_persist.cu", "rows_fast.cu", "rows.cu", "rows_ln.cu", "attention.cu", "attention_tc.cu", "attention_short.cu", "capi.cu", "noalloc.cu"]
 
 NVCC_FLAGS = [
@@ -49,7 +49,7 @@ def build(verbose: bool = False, force: bool = False, extra: list[str] | None = 
     objs = []
     for src in SOURCES:
         sp = os.path.join(CSRC, src)
-        op = os.path.join(objdir, src.replace(".cu", ".o"))
+        op = os.path.join(objdir, os.path.splitext(src)[0] + ".o")
         objs.append(op)
         if force or _stale(op, [sp] + header_paths):
             cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), *[f"-I{i}" for i in inc], "-c", sp, "-o", op]

@@ -37,6 +37,15 @@ static int fail(int code, const std::string &msg) {
   return code;
 }
 
+// Error reporting for the host-only entry points built in their own object
+// (spans.cpp): one last-error slot per thread for the whole library.
+int report_error(int code, const std::string &msg) { return fail(code, msg); }
+void clear_error() { t_last_error.clear(); }
+
+// Pooled by the mean of each sequence's rows whatever the config's pooling
+// (meanRows, spans.go:464-477); internal to ig_window_logits.
+constexpr int kModeMeanRows = 2;
+
 #define IG_CU(x)                                                                         \
   do {                                                                                   \
     cudaError_t e_ = (x);                                                                \
@@ -653,9 +662,9 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
     ProfScope ps("ln_final", (double)N * 8.0 * H + 4.0 * H, 0, 1, st, capturing);
     IG_TRY(launch_ln_quant(w.x, m->final_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
   }
-  if (mode == IG_MODE_POOLED) {
+  if (mode != IG_MODE_TOKENS) {
     ProfScope ps("pool", (double)N * 4.0 * H + 4.0 * p.nseq * H, 0, 1, st, capturing);
-    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, c.pooling == IG_POOL_CLS, w.pooled, st));
+    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st));
   }
   return 0;
 }
@@ -703,7 +712,8 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
                 size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len) {
   t_last_error.clear();
   if (!m || (nseq > 0 && !offs)) return fail(IG_ERR_BAD_ARG, "null argument");
-  if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS) return fail(IG_ERR_BAD_ARG, "bad mode");
+  if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS && !(mode == kModeMeanRows && !out))
+    return fail(IG_ERR_BAD_ARG, "bad mode");
   DeviceGuard dg(m->device);
   Plan p;
   const int win[2] = {-1, m->cfg.local_attention / 2};
@@ -727,7 +737,7 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   if (!w->own_stream) IG_CU(cudaStreamCreateWithFlags(&w->own_stream, cudaStreamNonBlocking));
   st = w->own_stream;
   int rc = upload_plan(*w, p, ids, st);
-  const int enc_mode = (logits || tlog) ? IG_MODE_POOLED : mode;
+  const int enc_mode = (logits || tlog) ? (mode == kModeMeanRows ? kModeMeanRows : IG_MODE_POOLED) : mode;
   if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump);
   if (!rc && (logits || tlog))
     rc = run_heads(m, *w, p, st, logits ? w->logits : nullptr, tlog ? w->tlogits : nullptr, false);
@@ -913,12 +923,31 @@ int ig_model_set_heads(ig_model *m, int32_t nheads, const ig_head *heads) {
 int ig_encode(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
               size_t out_len) {
   if (!out) return fail(IG_ERR_BAD_ARG, "null output");
+  if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS) return fail(IG_ERR_BAD_ARG, "bad mode");
   return encode_host(m, ids, offs, nseq, mode, out, out_len, nullptr, nullptr, 0, nullptr, 0);
 }
 
 int ig_encode_dump(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
                    size_t out_len, ig_dump *dump) {
+  if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS) return fail(IG_ERR_BAD_ARG, "bad mode");
   return encode_host(m, ids, offs, nseq, mode, out, out_len, dump, nullptr, 0, nullptr, 0);
+}
+
+int ig_window_logits(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, double *logits,
+                     size_t logits_len, double *token_logits, size_t token_len) {
+  if (!logits && !token_logits) return fail(IG_ERR_BAD_ARG, "no output");
+  return encode_host(m, ids, offs, nseq, kModeMeanRows, nullptr, 0, nullptr, logits, logits_len, token_logits,
+                     token_len);
+}
+
+int ig_model_head_rows(ig_model *m, int32_t *pooled_rows, int32_t *token_rows) {
+  t_last_error.clear();
+  if (!m || !pooled_rows || !token_rows) return fail(IG_ERR_BAD_ARG, "null argument");
+  int32_t pl = 0, tl = 0;
+  std::lock_guard<std::mutex> lk(m->mu);
+  for (auto &h : m->heads) (h.per_token ? tl : pl) += h.rows;
+  *pooled_rows = pl, *token_rows = tl;
+  return 0;
 }
 
 int ig_logits(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, double *logits, size_t logits_len,
