@@ -13,6 +13,7 @@ ranks.
 
   python bench.py [--gpus N --steps K --warmup W]   # this implementation
   python bench.py --impl reference ...               # the reference's CPU path
+  python bench.py --workload c5 ...                  # config 5: the SigLIP vision tower (images/s)
 """
 from __future__ import annotations
 
@@ -44,6 +45,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target length of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--workload", default="c1", choices=["c1", "c5"],
+                    help="c1: the ModernBERT headline (default); c5: the SigLIP ViT-B/16 vision tower")
+    ap.add_argument("--images-per-step", type=int, default=512, help="c5: images per step, shared by all ranks")
     return ap.parse_args()
 
 
@@ -386,9 +390,191 @@ def run_ours(args, world, rank, local):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# C5: the SigLIP ViT-B/16 vision tower
+# ---------------------------------------------------------------------------
+
+C5_METRIC = "SigLIP ViT-B/16 int8 vision tower images/s (224 px, 196 patches)"
+FP32_KERNELS = {"vis_attn_f32", "vis_patch_embed", "vis_head_kv", "vis_head_mlp", "vis_head_attn"}
+
+
+def c5_config(args, world, per_rank):
+    return {"workload": "C5 SigLIP ViT-B/16 vision tower, int8 layers (hidden 768, 12 layers, 12x64 heads, MLP 3072 "
+                        "GELU-tanh, biases, LLM.int8 outlier split on fc2), float32 patch embedding, attention and "
+                        "attention-pooling head; pixels uniform in [-1, 1]",
+            "images_per_step": args.images_per_step, "images_per_step_per_gpu": per_rank, "image_size": 224,
+            "patches": 196, "parallelism": f"image shard x{world}, no collective",
+            "l2": "inputs and activations larger than L2 (fc1 output alone is images*196*12 KiB)",
+            "weights": "random-init seed 42, 4 massive fc1 channels per layer"}
+
+
+def c5_cpu(n_images: int, threads: int):
+    import oracle
+    from indecis_b200 import synthetic as S
+    oracle.build()
+    om = oracle.SigLIP(S.C5, S.siglip_weights(S.C5, seed=42))
+    px = S.pixels(n_images, 224, seed=5)
+    om.forward(px[:1], patches=False, threads=threads, fast=True)
+    t0 = time.perf_counter()
+    om.forward(px, patches=False, threads=threads, fast=True)
+    return time.perf_counter() - t0, oracle
+
+
+def run_reference_c5(args, world, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    n = max(1, min(threads, 16))
+    ts = []
+    oracle = None
+    for _ in range(max(1, args.steps)):
+        t, oracle = c5_cpu(n, threads)
+        ts.append(t)
+    total = sum(ts)
+    v = n * len(ts) / total
+    line = {"metric": C5_METRIC, "value": v, "unit": "img/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": len(ts), "warmup": 1, "ms_per_step": 1000 * total / len(ts), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8+f32", "data": "synthetic",
+            "config": {**c5_config(args, 1, n), "images_per_step": n, "note": "bounded CPU sample per step"},
+            "cpu_baseline": {"value": v, "unit": "img/s", "cores": threads, "kind": "port",
+                             "sample": f"{n} images per step, oracle C++ port of internal/siglip (images over "
+                                       f"{threads} threads, VNNI integer products)"},
+            "e2e": {"value": v, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def c5_roofline(report, pk, sm_mhz):
+    ks = [k for k in report["kernels"] if k["records"] > 0 and k["ms"] > 0]
+    total = sum(k["ms"] for k in ks)
+    fp32_peak = 148 * 128 * 2 * (sm_mhz or 1965.0) * 1e6 / 1e12  # CUDA-core FMA rate at the SM clock
+    int8_peak = 2.0 * pk["bf16"]
+    out = []
+    for k in sorted(ks, key=lambda k: -k["ms"])[:4]:
+        per_ms = k["ms"] / k["records"]
+        ops, byts = k["ops"] / k["records"], k["bytes"] / k["records"]
+        if k["name"] in FP32_KERNELS and ops:
+            ach = ops / (per_ms * 1e-3) / 1e12
+            r = {"bound": "fp32", "achieved": ach, "peak": fp32_peak, "unit": "TFLOP/s", "frac": ach / fp32_peak,
+                 "peak_source": f"148 SMs x 128 FP32 FMA/clk at the sampled {sm_mhz or 1965.0:.0f} MHz (nominal)"}
+        elif ops and ops / (int8_peak * 1e12) > byts / (pk["hbm"] * 1e9):
+            ach = ops / (per_ms * 1e-3) / 1e12
+            r = {"bound": "tensor", "achieved": ach, "peak": int8_peak, "unit": "TOP/s", "frac": ach / int8_peak,
+                 "peak_source": f"int8 dense = 2 x {pk['src']} bf16 burst"}
+        else:
+            ach = byts / (per_ms * 1e-3) / 1e9
+            r = {"bound": "hbm", "achieved": ach, "peak": pk["hbm"], "unit": "GB/s", "frac": ach / pk["hbm"],
+                 "peak_source": f"{pk['src']} HBM copy bandwidth"}
+        r.update({"kernel": k["name"], "share": k["ms"] / total, "ms_per_launch": per_ms, "traffic": None})
+        out.append(r)
+    return out
+
+
+def run_ours_c5(args, world, rank, local):
+    import torch
+    from indecis_b200 import _capi, build
+    from indecis_b200 import synthetic as S
+    from indecis_b200.siglip import Vision, VisionConfig
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    build.build()
+    pk = peaks()
+    vis = Vision.from_arrays(VisionConfig.from_dict(S.C5), S.siglip_weights(S.C5, seed=42), device=local)
+    L = _capi.load()
+    total = args.images_per_step
+    lo, hi = rank * total // world, (rank + 1) * total // world
+    n = hi - lo
+    px_host = S.pixels(total, 224, seed=5)[lo:hi]
+    d_px = torch.from_numpy(px_host).cuda()
+    d_out = torch.empty((n, 768), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        _capi.check(L.ig_vision_forward_device(vis._h, d_px.data_ptr(), n, 0, None, d_out.data_ptr(),
+                                               stream.cuda_stream))
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = Clocks(physical_gpu(local))
+    _capi.profile(True)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    report = _capi.profile_report()
+    _capi.profile(False)
+    value = total * args.steps / (ms / 1e3)
+
+    # End to end through the host API: pixels from host memory, embeddings back.
+    e2e_steps = max(3, min(args.steps, 10))
+    vis.Embed(px_host)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        vis.Embed(px_host)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e = {"value": total * e2e_steps / e2e_s, "unit": "img/s", "h2d_bytes_per_step": int(px_host.nbytes),
+           "d2h_bytes_per_step": int(n * 768 * 4),
+           "api": "ig_vision_forward (host pixels, synchronous), host clock around device-synchronized calls"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        k = max(1, min(threads, 16))
+        t, _ = c5_cpu(k, threads)
+        cpu = {"value": k / t, "unit": "img/s", "cores": threads, "kind": "port",
+               "sample": f"{k} C5 images, oracle C++ port of internal/siglip (images over {threads} threads, VNNI "
+                         f"integer products, scalar float32 chains), {t:.1f} s"}
+    if rank == 0:
+        rl = c5_roofline(report, pk, clk["sm_mhz"] if clk else None)
+        line = {"metric": C5_METRIC, "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "int8+f32", "data": "synthetic", "config": c5_config(args, world, n),
+                "e2e": e2e, "gpu_launches": report["launches"], "roofline": rl[0], "roofline_top4": rl,
+                "kernels": {k["name"]: {"ms": round(k["ms"], 3), "launches": k["launches"]}
+                            for k in report["kernels"]},
+                "clocks": clk, "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup()
+    if args.workload == "c5":
+        if args.impl == "reference":
+            run_reference_c5(args, world, rank)
+        else:
+            run_ours_c5(args, world, rank, local)
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
         return

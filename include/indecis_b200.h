@@ -306,6 +306,81 @@ IG_API int ig_infer_windows(ig_model *m, const int32_t *ids, const int64_t *offs
  * *token_rows receive the sums over pooled and per-token heads. */
 IG_API int ig_model_head_rows(ig_model *m, int32_t *pooled_rows, int32_t *token_rows);
 
+/* ---- SigLIP vision tower (internal/siglip): int8 layers, float32 patch
+ * embedding, attention and pooling head, as the reference computes them.
+ * The seam is Vision.forward (internal/siglip/vision.go:101-141), reached by
+ * Embed and Forward (vision.go:85-99); one call takes a batch of images. ---- */
+
+/* Dimensions (Config, siglip.go:26-33 with ReadConfig's defaults applied). */
+typedef struct ig_vision_config {
+  int32_t hidden, layers, heads, mlp, image_size, patch_size;
+  double eps;
+  int32_t simd_lanes; /* float32 lanes of LayerNorm/ExpShift/GeluTanh sums (8: AVX2) */
+} ig_vision_config;
+
+/* Float32 weights in transformers layouts ([out][in] matrices), as
+ * loadVision reads them (vision.go:30-80); q, k, v stacked into wqkv. */
+typedef struct ig_vision_weights {
+  const float *patch_w, *patch_b; /* [H][3*P*P] conv weight in (channel, y, x) order, [H] */
+  const float *pos;               /* [T][H], T = (image_size/patch_size)^2 */
+  const float *const *ln1_g, *const *ln1_b, *const *ln2_g, *const *ln2_b; /* [layers] of [H] */
+  const float *const *wqkv, *const *bqkv; /* [layers] of [3H][H], [3H] */
+  const float *const *wo, *const *bo;     /* [layers] of [H][H], [H] */
+  const float *const *w1, *const *b1;     /* [layers] of [mlp][H], [mlp] */
+  const float *const *w2, *const *b2;     /* [layers] of [H][mlp], [H] */
+  const float *post_g, *post_b;           /* [H] */
+  const float *probe;                     /* [H] */
+  const float *in_w, *in_b;               /* [3H][H], [3H] pooling attention in_proj */
+  const float *hout_w, *hout_b;           /* [H][H], [H] */
+  const float *hln_g, *hln_b;             /* [H] */
+  const float *hfc1_w, *hfc1_b;           /* [mlp][H], [mlp] */
+  const float *hfc2_w, *hfc2_b;           /* [H][mlp], [H] */
+} ig_vision_weights;
+
+typedef struct ig_vision ig_vision;
+
+/* loadVision with int8 layers (vision.go:30-80, encoder.go:95-156): weights
+ * copied to `device`, each layer matrix quantized per output channel there,
+ * the probe's query computed once. head_dim must be 64 and the patches at
+ * most 256 in this build (IG_ERR_UNSUPPORTED otherwise). */
+IG_API int ig_vision_create(const ig_vision_config *cfg, const ig_vision_weights *w, int32_t device,
+                            ig_vision **out);
+IG_API void ig_vision_destroy(ig_vision *v);
+
+/* Vision.forward on n images of normalized pixels [n][3][S][S] (host
+ * buffers): layer 0 runs every layer; layer > 0 stops after that many layers
+ * unless pooled is wanted. patches (may be NULL) receives [n][T][H] — the
+ * states after `layer` layers, or the final ones (after post_layernorm) for
+ * layer 0; pooled (may be NULL) the embeddings [n][H] (Embed). Errors:
+ * IG_ERR_BAD_ARG "siglip: layer %d, the tower has %d". */
+IG_API int ig_vision_forward(ig_vision *v, const float *pixels, int32_t n, int32_t layer, float *patches,
+                             size_t patches_len, float *pooled, size_t pooled_len);
+
+/* ig_vision_forward on device buffers, enqueued on `stream` (NULL: legacy
+ * default stream). Calls on one ig_vision are serialized. */
+IG_API int ig_vision_forward_device(ig_vision *v, const float *d_pixels, int32_t n, int32_t layer,
+                                    float *d_patches, float *d_pooled, void *stream);
+
+/* Intermediates of one layer for parity checks (NULL fields skipped); rows
+ * are images x patches. */
+typedef struct ig_vision_dump {
+  int32_t layer;
+  float *x_embed;               /* [n*T][H] patch embedding + positions */
+  uint8_t *h1q; float *h1q_s;   /* LN1 output quantized [n*T][H], [n*T] */
+  float *qkv;                   /* [n*T][3H] with bias */
+  float *attn;                  /* [n*T][H] attention output */
+  float *x_attn;                /* [n*T][H] residual after attention */
+  uint8_t *h2q; float *h2q_s;   /* LN2 output quantized */
+  float *mlp;                   /* [n*T][mlp] GeluTanh(fc1) */
+  int32_t *outliers;            /* [n][32] fc2 input channels computed in float32, in order */
+  int32_t *noutliers;           /* [n] */
+  uint8_t *mq; float *mq_s;     /* fc2 input quantized, those channels zeroed */
+  float *x_mlp;                 /* [n*T][H] residual after the MLP */
+} ig_vision_dump;
+
+IG_API int ig_vision_dump_layer(ig_vision *v, const float *pixels, int32_t n, ig_vision_dump *dump, float *pooled,
+                                size_t pooled_len);
+
 #ifdef __cplusplus
 }
 #endif

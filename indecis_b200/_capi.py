@@ -27,7 +27,8 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_layernorm_quant", "ig_pack_b8", "ig_attention", "ig_encode_dump", "ig_logits_device",
            "ig_profile", "ig_profile_report", "ig_attention_noalloc", "ig_model_set_embeddings",
            "ig_plan_windows", "ig_log_softmax", "ig_decode_spans", "ig_answer_spans", "ig_window_logits",
-           "ig_infer_windows", "ig_model_head_rows"]
+           "ig_infer_windows", "ig_model_head_rows", "ig_vision_create", "ig_vision_destroy", "ig_vision_forward",
+           "ig_vision_forward_device", "ig_vision_dump_layer"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -63,6 +64,28 @@ class IgWindow(C.Structure):
 
 class IgSpan(C.Structure):
     _fields_ = [("type", C.c_int32), ("start", C.c_int32), ("end", C.c_int32), ("confidence", C.c_double)]
+
+
+class IgVisionConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("layers", C.c_int32), ("heads", C.c_int32), ("mlp", C.c_int32),
+                ("image_size", C.c_int32), ("patch_size", C.c_int32), ("eps", C.c_double), ("simd_lanes", C.c_int32)]
+
+
+VISION_FLAT = ("patch_w", "patch_b", "pos")
+VISION_LAYER = ("ln1_g", "ln1_b", "ln2_g", "ln2_b", "wqkv", "bqkv", "wo", "bo", "w1", "b1", "w2", "b2")
+VISION_TAIL = ("post_g", "post_b", "probe", "in_w", "in_b", "hout_w", "hout_b", "hln_g", "hln_b", "hfc1_w", "hfc1_b",
+               "hfc2_w", "hfc2_b")
+
+
+class IgVisionWeights(C.Structure):
+    _fields_ = ([(n, C.c_void_p) for n in VISION_FLAT] + [(n, C.POINTER(C.c_void_p)) for n in VISION_LAYER] +
+                [(n, C.c_void_p) for n in VISION_TAIL])
+
+
+class IgVisionDump(C.Structure):
+    _fields_ = [("layer", C.c_int32)] + [(n, C.c_void_p) for n in (
+        "x_embed", "h1q", "h1q_s", "qkv", "attn", "x_attn", "h2q", "h2q_s", "mlp", "outliers", "noutliers", "mq",
+        "mq_s", "x_mlp")]
 
 
 class IgDump(C.Structure):
@@ -115,6 +138,12 @@ def load() -> C.CDLL:
     L.ig_window_logits.argtypes = [vp, vp, vp, i32, vp, C.c_size_t, vp, C.c_size_t]
     L.ig_infer_windows.argtypes = [vp, vp, vp, i32, vp, i32, vp, i32, i32, i32, vp, C.c_size_t, vp, C.c_size_t]
     L.ig_model_head_rows.argtypes = [vp, i32p, i32p]
+    L.ig_vision_create.argtypes = [C.POINTER(IgVisionConfig), C.POINTER(IgVisionWeights), i32, C.POINTER(C.c_void_p)]
+    L.ig_vision_destroy.argtypes = [vp]
+    L.ig_vision_destroy.restype = None
+    L.ig_vision_forward.argtypes = [vp, vp, i32, i32, vp, C.c_size_t, vp, C.c_size_t]
+    L.ig_vision_forward_device.argtypes = [vp, vp, i32, i32, vp, vp, vp]
+    L.ig_vision_dump_layer.argtypes = [vp, vp, i32, C.POINTER(IgVisionDump), vp, C.c_size_t]
     L.ig_profile.argtypes = [i32]
     L.ig_profile_report.argtypes = [C.c_char_p, C.c_size_t]
     L.ig_profile_report.restype = C.c_int64

@@ -201,4 +201,39 @@ __device__ __forceinline__ float gelu_mul_at(float x, float gate, int i, int n) 
   return i < (n & ~15) ? gelu_mul_fma(x, gate) : gelu_mul_scalar(x, gate);
 }
 
+// ---- GELU, tanh form: x * sigmoid(2u), u = sqrt(2/pi) * (x + 0.044715 x^3) ----
+
+// The vector body of linalg.GeluTanh (vec_simd.go:166-197), one lane: the
+// exponent of Cephes' expf with FMA, then an IEEE division.
+__device__ __forceinline__ float gelu_tanh_body(float x) {
+  float v = __fmul_rn(x, x);
+  v = __fmaf_rn(v, 0.044715f, 1.0f);
+  v = __fmul_rn(v, x);
+  v = __fmul_rn(v, -1.5957691216057308f);  // -2*sqrt(2/pi), rounded once to float32
+  v = fminf(fmaxf(v, -87.3f), 88.7f);
+  const float n = __fsub_rn(__fmaf_rn(v, 1.44269504088896341f, 12582912.0f), 12582912.0f);
+  float r = __fmaf_rn(n, -0.693359375f, v);
+  r = __fmaf_rn(n, 2.12194440e-4f, r);
+  float p = __fmaf_rn(r, 1.9875691500e-4f, 1.3981999507e-3f);
+  p = __fmaf_rn(r, p, 8.3334519073e-3f);
+  p = __fmaf_rn(r, p, 4.1665795894e-2f);
+  p = __fmaf_rn(r, p, 1.6666665459e-1f);
+  p = __fmaf_rn(r, p, 5.0000001201e-1f);
+  const float y = __fadd_rn(__fmaf_rn(__fmul_rn(p, r), r, r), 1.0f);
+  const float pw = __int_as_float((__float2int_rn(n) + 127) << 23);
+  return __fdiv_rn(x, __fadd_rn(1.0f, __fmul_rn(y, pw)));
+}
+
+// geluTanhScalar (fastmath.go:28-32): separate roundings, exp32.
+__device__ __forceinline__ float gelu_tanh_tail(float x) {
+  const float t = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+  const float u = __fmul_rn(0.7978845608028654f, __fadd_rn(x, t));
+  return __fdiv_rn(x, __fadd_rn(1.0f, exp_tail(__fmul_rn(-2.0f, u))));
+}
+
+// Element i of a GeluTanh call over len values with V lanes.
+__device__ __forceinline__ float gelu_tanh_at(float x, long long i, long long len, int V) {
+  return i < len - len % V ? gelu_tanh_body(x) : gelu_tanh_tail(x);
+}
+
 }  // namespace ig

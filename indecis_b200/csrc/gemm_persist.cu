@@ -29,7 +29,7 @@ namespace ig {
 // stores, which are bound by the TMA store stream.
 template <int EPI>
 struct PEpi {
-  static constexpr int kWarps = EPI == kEpiGeglu ? 16 : 8;
+  static constexpr int kWarps = (EPI == kEpiGeglu || EPI == kEpiGeluTanh) ? 16 : 8;
   static constexpr int kGroups = kWarps / 4;  // warps per lane quarter
   static constexpr int kThreads = 64 + 32 * kWarps;
 };
@@ -41,7 +41,7 @@ struct PGemmSmem {
   // column scales in shared memory (when N <= kMaxCols); the GeGLU one, with
   // twice the warps, reads them from global memory.
   static constexpr int kStageBufs = 2;
-  static constexpr int kMaxCols = EPI == kEpiGeglu ? 0 : 1024;
+  static constexpr int kMaxCols = (EPI == kEpiF32 || EPI == kEpiI32) ? 1024 : 0;
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -153,6 +153,24 @@ struct StageWriter {
   }
 };
 
+// v[k] + bias[j0 + k] for the 16 columns j0.. (AddTo after MatMul8N); columns
+// past N read column N-1 and are clipped by the store.
+__device__ __forceinline__ void add_bias16(float (&v)[16], const float *__restrict__ bias, int j0, int N) {
+  if (j0 + 16 <= N) {
+#pragma unroll
+    for (int k = 0; k < 16; k += 4) {
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + j0 + k));
+      v[k] = __fadd_rn(v[k], b.x);
+      v[k + 1] = __fadd_rn(v[k + 1], b.y);
+      v[k + 2] = __fadd_rn(v[k + 2], b.z);
+      v[k + 3] = __fadd_rn(v[k + 3], b.w);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; k++) v[k] = __fadd_rn(v[k], __ldg(bias + min(j0 + k, N - 1)));
+  }
+}
+
 // One output tile's epilogue for one warp: TMEM lane quarter at tbase (row0 its
 // first row, sa the thread's row scale), column chunks g, g + GROUPS, ...
 template <int BN, int EPI, int GROUPS, int NBUF>
@@ -180,6 +198,38 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int
         StageWriter<NBUF>::put_half(buf, lane, h, v);
       }
       sw.finish(mapC, buf, lane, n0 + c, row0, EPI == kEpiF32 && ep.accumulate);
+    }
+  } else if constexpr (EPI == kEpiF32Bias || EPI == kEpiGeluTanh) {
+    // GeluTanh runs over each segment of seg_rows rows as one call: its
+    // element index decides the vector body or the scalar tail.
+    const long long seg_len = (long long)ep.seg_rows * N;
+    const long long seg_row = (long long)((row0 + lane) % ep.seg_rows) * N;
+    const long long body_end = seg_len - seg_len % ep.V;
+#pragma unroll 1
+    for (int c = g * 32; c < BN; c += 32 * kPGroups) {
+      if (n0 + c >= N) continue;
+      uint8_t *buf = sw.begin(lane);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tbase + c + 16 * h, r);
+        tmem_ld_wait();
+        float v[16];
+        const int j0 = n0 + c + 16 * h;
+        dequant16(r, ep.sb, ep.zc, j0, N, sa, v);
+        add_bias16(v, ep.bias, j0, N);
+        if constexpr (EPI == kEpiGeluTanh) {
+          if (seg_row + j0 + 16 <= body_end) {
+#pragma unroll
+            for (int k = 0; k < 16; k++) v[k] = gelu_tanh_body(v[k]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 16; k++) v[k] = gelu_tanh_at(v[k], seg_row + j0 + k, seg_len, ep.V);
+          }
+        }
+        StageWriter<NBUF>::put_half(buf, lane, h, v);
+      }
+      sw.finish(mapC, buf, lane, n0 + c, row0, EPI == kEpiF32Bias && ep.accumulate);
     }
   } else if constexpr (EPI == kEpiGeglu) {
     // Tile columns [0, BN/2) are GELU inputs, [BN/2, BN) their gates.
@@ -404,6 +454,10 @@ static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, 
   void *out = epi == kEpiI32 ? (void *)ep.acc_out : (void *)ep.C;
   if (!out || (reinterpret_cast<uintptr_t>(out) & 15) || (ep.ldc & 3)) return -1;
   if (epi != kEpiI32 && ((reinterpret_cast<uintptr_t>(ep.sb) | reinterpret_cast<uintptr_t>(ep.zc)) & 15)) return -1;
+  if (epi == kEpiF32Bias || epi == kEpiGeluTanh) {
+    if (!ep.bias || (reinterpret_cast<uintptr_t>(ep.bias) & 15)) return IG_ERR_BAD_ARG;
+    if (epi == kEpiGeluTanh && (ep.seg_rows < 1 || ep.V < 1)) return IG_ERR_BAD_ARG;
+  }
   const int out_cols = epi == kEpiGeglu ? ep.geglu_n : g.N;
   CUtensorMap mc;
   if (make_map_out32(&mc, out, g.M, out_cols, ep.ldc, epi == kEpiI32)) return IG_ERR_CUDA;
@@ -416,6 +470,8 @@ static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, 
   switch (epi) {
     IG_PCASE(kEpiF32)
     IG_PCASE(kEpiI32)
+    IG_PCASE(kEpiF32Bias)
+    IG_PCASE(kEpiGeluTanh)
     case kEpiGeglu:
       e = launch_persist<256, kEpiGeglu>(ma, mb, mc, g.M, g.N, g.K, ep, st);
       break;

@@ -7,7 +7,13 @@
 
 namespace ig {
 
-enum Epilogue : int { kEpiF32 = 0, kEpiI32 = 1, kEpiGeglu = 3 };
+enum Epilogue : int {
+  kEpiF32 = 0,
+  kEpiI32 = 1,
+  kEpiGeglu = 3,
+  kEpiF32Bias = 4,   // C (+)= dequant + bias[j]   (MatMul8N then AddTo(bias), accumulate: AddTo(x, .))
+  kEpiGeluTanh = 5,  // C = GeluTanh(dequant + bias[j])
+};
 
 struct GemmArgs {
   const uint8_t *A;  // [M][lda] uint8 activations (q + 128)
@@ -27,6 +33,10 @@ struct GemmEpilogue {
   int accumulate;   // C = dequant + C
   // kEpiGeglu
   int geglu_n;  // GeGLU output width (intermediate size)
+  // kEpiF32Bias, kEpiGeluTanh
+  const float *bias;  // [N], 16-byte aligned
+  int seg_rows;       // kEpiGeluTanh: rows per GeluTanh call (its vector/tail split), >= 1
+  int V;              // float32 lanes of that split
 };
 
 int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t st);
@@ -36,6 +46,10 @@ int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t s
 // uint8 q [M][ldq] + sa. gamma == nullptr: no norm, quantize x itself.
 int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps, int V, float *xn, uint8_t *q,
                     int ldq, float *sa, cudaStream_t st);
+// LayerNorm with a bias (LayerNormRow then AddTo(beta): the SigLIP norms),
+// optional f32 output (may be x itself) and optional quantized copy.
+int launch_ln_beta(const float *x, const float *gamma, const float *beta, int M, int H, double eps, int V, float *xout,
+                   uint8_t *q, int ldq, float *sa, cudaStream_t st);
 // An embedding table on the device in its stored format (Row,
 // embeddings.go:49-68): f32 rows; bf16 rows widened exactly, with float32
 // rows for the ids whose exact_idx >= 0; or int8 rows times a row scale.
@@ -115,5 +129,43 @@ int launch_attn_short(const AttnArgs &a, cudaStream_t st);
 
 // Device error flag (kernels' bounded waits).
 int read_device_error(int reset);
+
+// ---- SigLIP pieces (siglip.cu) ----
+// C[r][c] = chain(A[r] . W[c]) (+ bias[c]) (-> GeluTanh) (+ add[..][c]): the
+// float32 product of linalg/gemm.go, one FMA chain per 256-deep block.
+struct F32Gemm {
+  const float *A;      // [M][lda] rows, or nullptr with pix
+  int lda;
+  const float *pix;    // patch rows read from pixels [n][3][S][S] (T patches per image)
+  int S, P, T;
+  const float *W;      // [N][ldw]
+  int ldw;
+  int M, N, K;
+  const float *bias;   // [N] or nullptr
+  int gelu_seg_rows;   // > 0: GeluTanh after the bias, calls of that many rows
+  int V;
+  const float *add;    // nullptr, or + add[(add_mod ? r % add_mod : r) * ldadd + c] last
+  int ldadd, add_mod;
+  float *C;
+  int ldc;
+  bool vec_a, vec_w;   // set by the launcher
+};
+int launch_f32_gemm(const F32Gemm &p, cudaStream_t st);
+// Float attention of the vision layers over the qkv rows [n*T][3H] -> ctx [n*T][H].
+int launch_attn_f32(const float *qkv, int nimg, int T, int H, int nh, float scale, int V, float *ctx,
+                    cudaStream_t st);
+// Attention pooling: the probe's query over the K|V rows [n*T][2H] -> att [n][H].
+int launch_pool_attn(const float *kv, const float *probe_q, int nimg, int T, int H, int nh, float scale, int V,
+                     float *att, cudaStream_t st);
+// MatMul8Outliers, before the int8 product: per image the outlier channels
+// of x [n*T][K] (out [n][32], nout [n]), their values moved to outv
+// [n*T][32] and zeroed in x. colmax [n][K] and cand [n][K] are scratch.
+int launch_outliers_select(const float *x, int nimg, int T, int K, float ratio, float *colmax, int32_t *cand,
+                           int32_t *out, int32_t *nout, float *outv, cudaStream_t st);
+// After it: x += (c + the outlier terms in order) + bias, c the int8 product
+// [n*T][N], q/scale the packed weights.
+int launch_outliers_fixup(const float *c, int nimg, int T, int N, const int32_t *out, const int32_t *nout,
+                          const float *outv, const int8_t *q, int ldq, const float *scale, const float *bias, float *x,
+                          cudaStream_t st);
 
 }  // namespace ig

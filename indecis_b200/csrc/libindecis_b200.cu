@@ -8,5 +8,7 @@
 #include "attention.cu"
 #include "attention_tc.cu"
 #include "attention_short.cu"
+#include "siglip.cu"
 #include "capi.cu"
+#include "siglip_capi.cu"
 #include "noalloc.cu"

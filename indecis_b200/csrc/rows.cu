@@ -23,8 +23,9 @@ constexpr int kRowWarps = 8;
 
 // Several rows per warp (rows_ln.cu); -1 when it does not apply.
 template <bool EMBED>
-static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M,
-                           int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa, cudaStream_t st);
+static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma,
+                           const float *beta, int M, int H, double eps, int V, float *xout, uint8_t *q, int ldq,
+                           float *sa, cudaStream_t st);
 
 // Per-row quantization of the n values in s_row (shared), by one warp.
 __device__ __forceinline__ void quant_row_warp(const float *s_row, int n, uint8_t *q, float *sa, int lane) {
@@ -254,7 +255,7 @@ int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps
   if (gamma) {
     int rc = launch_ln8<false>(x, nullptr, 0, EmbTable{}, gamma, M, H, eps, V, xn, q, ldq, sa, st);
     if (rc != -1) return rc;
-    rc = launch_ln_group<false>(x, nullptr, 0, EmbTable{}, gamma, M, H, eps, V, xn, q, ldq, sa, st);
+    rc = launch_ln_group<false>(x, nullptr, 0, EmbTable{}, gamma, nullptr, M, H, eps, V, xn, q, ldq, sa, st);
     if (rc != -1) return rc;
   }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;
@@ -264,13 +265,21 @@ int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 
+int launch_ln_beta(const float *x, const float *gamma, const float *beta, int M, int H, double eps, int V, float *xout,
+                   uint8_t *q, int ldq, float *sa, cudaStream_t st) {
+  if (M <= 0) return 0;
+  if (!gamma || !beta) return IG_ERR_BAD_ARG;
+  const int rc = launch_ln_group<false>(x, nullptr, 0, EmbTable{}, gamma, beta, M, H, eps, V, xout, q, ldq, sa, st);
+  return rc == -1 ? IG_ERR_UNSUPPORTED : rc;
+}
+
 int launch_embed_checked(const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M, int H,
                          double eps, int V, float *x, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
   {
     int rc = launch_ln8<true>(nullptr, ids, vocab, emb, gamma, M, H, eps, V, x, q, ldq, sa, st);
     if (rc != -1) return rc;
-    rc = launch_ln_group<true>(nullptr, ids, vocab, emb, gamma, M, H, eps, V, x, q, ldq, sa, st);
+    rc = launch_ln_group<true>(nullptr, ids, vocab, emb, gamma, nullptr, M, H, eps, V, x, q, ldq, sa, st);
     if (rc != -1) return rc;
   }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;

@@ -271,7 +271,7 @@ static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTa
 
 // Row quantization for K % 4 == 0, K <= 1024, aligned rows; -1 otherwise.
 static int launch_quant_rows4(const float *x, int ldx, int M, int K, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
-  if ((K & 3) || (ldx & 3) || (ldq & 3) || K > 1024 || K <= 0) return -1;
+  if ((K & 3) || (ldx & 3) || (ldq & 3) || K > 3072 || K <= 0) return -1;
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 3)) return -1;
   const int nj = (K / 4 + 31) / 32;
   const int blocks = (M + 7) / 8;
@@ -282,7 +282,16 @@ static int launch_quant_rows4(const float *x, int ldx, int M, int K, uint8_t *q,
     case 4: quant_rows4_kernel<4><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
     case 5:
     case 6: quant_rows4_kernel<6><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
-    default: quant_rows4_kernel<8><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    case 7:
+    case 8: quant_rows4_kernel<8><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    default:
+      if (nj <= 12)
+        quant_rows4_kernel<12><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa);
+      else if (nj <= 16)
+        quant_rows4_kernel<16><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa);
+      else
+        quant_rows4_kernel<24><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa);
+      break;
   }
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }

@@ -19,7 +19,8 @@ namespace ig {
 
 template <bool EMBED>
 __global__ void ln_group_kernel(const float *__restrict__ x, const int32_t *__restrict__ ids, int vocab,
-                                const EmbTable emb, const float *__restrict__ gamma, int M, int H,
+                                const EmbTable emb, const float *__restrict__ gamma, const float *__restrict__ beta,
+                                int M, int H,
                                 double eps, int V, int P, int wpb, float *__restrict__ xout, uint8_t *__restrict__ q,
                                 int ldq, float *__restrict__ sa) {
   extern __shared__ float s_all[];
@@ -81,7 +82,8 @@ __global__ void ln_group_kernel(const float *__restrict__ x, const int32_t *__re
     const float rstd = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(var, (double)H), eps))));
     __syncwarp();
     for (int i = k; i < H; i += V) {
-      const float o = __fmul_rn(__fmul_rn(__fsub_rn(sr[i], mean), rstd), __ldg(gamma + i));
+      float o = __fmul_rn(__fmul_rn(__fsub_rn(sr[i], mean), rstd), __ldg(gamma + i));
+      if (beta) o = __fadd_rn(o, __ldg(beta + i));  // AddTo(o, beta) after LayerNormRow
       sr[i] = o;
       mx = fmaxf(mx, fabsf(o));
     }
@@ -147,8 +149,9 @@ static bool ln_group_geometry(int H, int V, int *P, int *wpb, size_t *smem) {
 }
 
 template <bool EMBED>
-static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M,
-                           int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
+static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma,
+                           const float *beta, int M, int H, double eps, int V, float *xout, uint8_t *q, int ldq,
+                           float *sa, cudaStream_t st) {
   int P = 0, wpb = 0;
   size_t smem = 0;
   if (!ln_group_geometry(H, V, &P, &wpb, &smem)) return -1;
@@ -158,8 +161,8 @@ static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const 
     return IG_ERR_CUDA;
   const int rows_per_block = wpb * (32 / V);
   const int blocks = (M + rows_per_block - 1) / rows_per_block;
-  ln_group_kernel<EMBED><<<blocks, 32 * wpb, smem, st>>>(x, ids, vocab, emb, gamma, M, H, eps, V, P, wpb, xout, q,
-                                                          ldq, sa);
+  ln_group_kernel<EMBED><<<blocks, 32 * wpb, smem, st>>>(x, ids, vocab, emb, gamma, beta, M, H, eps, V, P, wpb, xout,
+                                                          q, ldq, sa);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 

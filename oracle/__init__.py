@@ -100,6 +100,17 @@ def lib():
                             C.POINTER(C.c_int32)]
     L.or_head_logits.argtypes = [f32p, f32p, C.c_int, C.c_int, f32p, C.c_int, f64p]
     L.or_cpu_features.restype = C.c_int
+    L.or_siglip_create.restype = C.c_void_p
+    L.or_siglip_create.argtypes = [C.c_void_p, C.c_void_p]
+    L.or_siglip_destroy.argtypes = [C.c_void_p]
+    L.or_siglip_forward.restype = C.c_int
+    L.or_siglip_forward.argtypes = [C.c_void_p, f32p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                    C.c_void_p]
+    L.or_linear_f32.argtypes = [f32p, f32p, C.c_int, f32p, C.c_void_p, C.c_int, C.c_int]
+    L.or_gelu_tanh.argtypes = [f32p, f32p, C.c_int, C.c_int]
+    L.or_siglip_softmax.argtypes = [f32p, C.c_int, C.c_float, C.c_int]
+    L.or_matmul8_outliers.argtypes = [f32p, f32p, C.c_int, i8p, f32p, f32p, C.c_int, C.c_int, C.c_float, i32p,
+                                      C.POINTER(C.c_int32)]
     _lib = L
     return L
 
@@ -282,3 +293,100 @@ class Model:
         if rc != 0:
             raise ValueError(f"modernbert: id {bad.value} out of vocabulary")
         return (out, arrays) if dump_layer is not None else out
+
+
+# ---- SigLIP vision tower (oracle/siglip.cpp) -----------------------------------
+
+class SiglipConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("layers", C.c_int), ("heads", C.c_int), ("mlp", C.c_int),
+                ("image_size", C.c_int), ("patch_size", C.c_int), ("eps", C.c_double), ("V", C.c_int)]
+
+
+SIGLIP_FLAT = ("patch_w", "patch_b", "pos")
+SIGLIP_LAYER = ("ln1_g", "ln1_b", "ln2_g", "ln2_b", "wqkv", "bqkv", "wo", "bo", "w1", "b1", "w2", "b2")
+SIGLIP_TAIL = ("post_g", "post_b", "probe", "in_w", "in_b", "hout_w", "hout_b", "hln_g", "hln_b", "hfc1_w", "hfc1_b",
+               "hfc2_w", "hfc2_b")
+
+
+class SiglipWeights(C.Structure):
+    _fields_ = ([(n, C.c_void_p) for n in SIGLIP_FLAT] + [(n, C.POINTER(C.c_void_p)) for n in SIGLIP_LAYER] +
+                [(n, C.c_void_p) for n in SIGLIP_TAIL])
+
+
+class SiglipDump(C.Structure):
+    _fields_ = [("layer", C.c_int)] + [(n, C.c_void_p) for n in (
+        "x_embed", "h1q", "h1q_s", "qkv", "attn", "x_attn", "h2q", "h2q_s", "mlp", "outliers", "noutliers", "mq",
+        "mq_s", "x_mlp")]
+
+
+def siglip_dump_arrays(n, T, H, M):
+    N = n * T
+    return dict(x_embed=np.zeros((N, H), np.float32), h1q=np.zeros((N, H), np.uint8), h1q_s=np.zeros(N, np.float32),
+                qkv=np.zeros((N, 3 * H), np.float32), attn=np.zeros((N, H), np.float32),
+                x_attn=np.zeros((N, H), np.float32), h2q=np.zeros((N, H), np.uint8), h2q_s=np.zeros(N, np.float32),
+                mlp=np.zeros((N, M), np.float32), outliers=np.zeros((n, 32), np.int32),
+                noutliers=np.zeros(n, np.int32), mq=np.zeros((N, M), np.uint8), mq_s=np.zeros(N, np.float32),
+                x_mlp=np.zeros((N, H), np.float32))
+
+
+class SigLIP:
+    """Oracle SigLIP vision tower over float32 weights (synthetic.siglip_weights layout)."""
+
+    def __init__(self, cfg: dict, weights: dict):
+        self.cfg = cfg
+        L = cfg["layers"]
+        self._keep = {k: (np.ascontiguousarray(v, np.float32) if not isinstance(v, list)
+                          else [np.ascontiguousarray(a, np.float32) for a in v]) for k, v in weights.items()}
+        W = self._keep
+        self._ptrs = {}
+        fields = {}
+        for n in SIGLIP_FLAT + SIGLIP_TAIL:
+            fields[n] = W[n].ctypes.data
+        for n in SIGLIP_LAYER:
+            arr = (C.c_void_p * L)(*[a.ctypes.data for a in W[n]])
+            self._ptrs[n] = arr
+            fields[n] = C.cast(arr, C.POINTER(C.c_void_p))
+        self._w = SiglipWeights(**fields)
+        self._c = SiglipConfig(hidden=cfg["hidden"], layers=L, heads=cfg["heads"], mlp=cfg["mlp"],
+                               image_size=cfg["image_size"], patch_size=cfg["patch_size"], eps=cfg["eps"],
+                               V=cfg.get("V", 8))
+        self._h = lib().or_siglip_create(C.byref(self._c), C.byref(self._w))
+        self.T = (cfg["image_size"] // cfg["patch_size"]) ** 2
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().or_siglip_destroy(self._h)
+            self._h = None
+
+    def forward(self, pixels, layer=0, patches=True, pooled=True, threads=1, fast=False, dump_layer=None):
+        """Vision.forward on [n][3][S][S] pixels -> (patches [n][T][H] or None, pooled [n][H] or None[, dump])."""
+        px = np.ascontiguousarray(pixels, np.float32)
+        n, H = px.shape[0], self.cfg["hidden"]
+        pa = np.zeros((n, self.T, H), np.float32) if patches else None
+        po = np.zeros((n, H), np.float32) if pooled else None
+        arrays, dump = {}, None
+        if dump_layer is not None:
+            arrays = siglip_dump_arrays(n, self.T, H, self.cfg["mlp"])
+            dump = SiglipDump(layer=dump_layer, **{k: v.ctypes.data for k, v in arrays.items()})
+        rc = lib().or_siglip_forward(self._h, px, n, layer, pa.ctypes.data if pa is not None else None,
+                                     po.ctypes.data if po is not None else None, threads, 1 if fast else 0,
+                                     C.byref(dump) if dump is not None else None)
+        if rc:
+            raise ValueError(f"siglip: layer {layer}, the tower has {self.cfg['layers']}")
+        return (pa, po, arrays) if dump_layer is not None else (pa, po)
+
+
+def linear_f32(x, W, b=None):
+    x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+    W = np.ascontiguousarray(W, np.float32)
+    out = np.zeros((x.shape[0], W.shape[0]), np.float32)
+    bb = None if b is None else np.ascontiguousarray(b, np.float32)
+    lib().or_linear_f32(out, x, x.shape[0], W, bb.ctypes.data if bb is not None else None, W.shape[1], W.shape[0])
+    return out
+
+
+def gelu_tanh(a, V=8):
+    a = np.ascontiguousarray(a, np.float32).ravel()
+    o = np.zeros_like(a)
+    lib().or_gelu_tanh(o, a, a.size, V)
+    return o

@@ -16,84 +16,12 @@
 
 using namespace orc;
 
-struct PackedMat {
-  int k = 0, n = 0;
-  std::vector<int8_t> q;       // [n][k]
-  std::vector<int8_t> panels;  // [n/16][k/4][16][4] for the fast GEMM
-  std::vector<float> scale, zc;
-  std::vector<int32_t> colsum;
-};
-
 struct or_model {
   or_config cfg;
   std::vector<float> emb, emb_norm, final_norm;
   std::vector<std::vector<float>> attn_norm, mlp_norm;
   std::vector<PackedMat> qkv, o, wi, womlp;
 };
-
-static void pack(PackedMat &p, const float *w, int k, int n) {
-  p.k = k;
-  p.n = n;
-  p.q.resize((size_t)n * k);
-  p.scale.resize(n);
-  p.zc.resize(n);
-  p.colsum.resize(n);
-  pack_b8(w, k, n, true, p.q.data(), p.scale.data(), p.colsum.data(), p.zc.data());
-  pack_panels(p.q.data(), n, k, p.panels);
-}
-
-// linalg/parallel.go:38-72 ParallelN: about four slices per worker, each a
-// multiple of grain, taken with an atomic counter.
-template <class F>
-static void parallel_n(int workers, int n, int grain, F fn) {
-  if (n <= 0) return;
-  grain = std::max(1, grain);
-  if (workers <= 1 || n <= grain) {
-    fn(0, n);
-    return;
-  }
-  int step = ((n + 4 * workers - 1) / (4 * workers) + grain - 1) / grain * grain;
-  workers = std::min(workers, (n + step - 1) / step);
-  std::atomic<int> next(0);
-  auto run = [&]() {
-    for (;;) {
-      int lo = next.fetch_add(1) * step;
-      if (lo >= n) return;
-      fn(lo, std::min(lo + step, n));
-    }
-  };
-  std::vector<std::thread> ts;
-  for (int w = 1; w < workers; w++) ts.emplace_back(run);
-  run();
-  for (auto &t : ts) t.join();
-}
-
-// One MatMul8N call on rows [lo, hi): c (+)= dequant(quant(a) . W^T).
-struct GemmScratch {
-  std::vector<uint8_t> aq;
-  std::vector<float> sa;
-  std::vector<int32_t> acc;
-};
-
-static void matmul_rows(const PackedMat &W, const float *a, float *c, int rows, bool accumulate, bool fast,
-                        GemmScratch &s, uint8_t *aq_dump, float *sa_dump, int32_t *acc_dump) {
-  const int k = W.k, n = W.n;
-  const int kp = (k + 3) / 4 * 4;
-  const int rp = (rows + 5) / 6 * 6;
-  s.aq.assign((size_t)rp * kp, 128);
-  s.sa.assign(rp, 0.0f);
-  s.acc.resize((size_t)rows * n);
-  for (int i = 0; i < rows; i++) quantize_a_row(a + (size_t)i * k, k, s.aq.data() + (size_t)i * kp, &s.sa[i]);
-  if (fast)
-    gemm_u8s8_fast(s.aq.data(), W.panels.data(), rp, n, kp, 0, rows, s.acc.data());
-  else
-    gemm_u8s8(s.aq.data(), kp, W.q.data(), k, rows, n, k, s.acc.data());
-  dequant(s.acc.data(), rows, n, s.sa.data(), W.scale.data(), W.zc.data(), c, accumulate);
-  if (aq_dump)
-    for (int i = 0; i < rows; i++) std::memcpy(aq_dump + (size_t)i * k, s.aq.data() + (size_t)i * kp, k);
-  if (sa_dump) std::memcpy(sa_dump, s.sa.data(), sizeof(float) * rows);
-  if (acc_dump) std::memcpy(acc_dump, s.acc.data(), sizeof(int32_t) * rows * n);
-}
 
 extern "C" {
 

@@ -19,6 +19,10 @@
  *   linalg/fastmath.go:9-51                erf32, exp32 (scalar tails)
  *   internal/modernbert/model.go:256-277   RoPE cos/sin table
  *   heads.go:63-74                         head.logits (float64)
+ *   internal/siglip/encoder.go, vision.go  SigLIP vision tower (siglip.cpp)
+ *   linalg/gemm.go:65-240                  float32 products (chain per 256-deep block)
+ *   linalg/int8.go:281-349                 MatMul8Outliers
+ *   linalg/vec_simd.go:166-202             GeluTanh
  *
  * Parity status (stated here because it bounds what the oracle proves):
  *   - The reference cannot run in this environment (it is Go 1.27 with
@@ -146,6 +150,72 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
 
 /* head.logits: z[r] = sum_i double(w[r][i])*double(x[i]) + double(b[r]). */
 void or_head_logits(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z);
+
+/* ---- SigLIP vision tower (internal/siglip) ----------------------------------- */
+typedef struct {
+  int hidden, layers, heads, mlp, image_size, patch_size;
+  double eps;
+  int V; /* float32 lanes of the reference's portable SIMD (8 = AVX2) */
+} or_siglip_config;
+
+/* Float32 weights in transformers layouts ([out][in] matrices). */
+typedef struct {
+  const float *patch_w, *patch_b; /* [H][3*P*P] (channel, y, x), [H] */
+  const float *pos;               /* [T][H] */
+  const float *const *ln1_g, *const *ln1_b, *const *ln2_g, *const *ln2_b; /* [L] of [H] */
+  const float *const *wqkv, *const *bqkv; /* [L] of [3H][H] (q, k, v stacked), [3H] */
+  const float *const *wo, *const *bo;     /* [L] of [H][H], [H] */
+  const float *const *w1, *const *b1;     /* [L] of [M][H], [M] */
+  const float *const *w2, *const *b2;     /* [L] of [H][M], [H] */
+  const float *post_g, *post_b;           /* [H] */
+  const float *probe;                     /* [H] */
+  const float *in_w, *in_b;               /* [3H][H], [3H]: pooling attention projections */
+  const float *hout_w, *hout_b;           /* [H][H], [H] */
+  const float *hln_g, *hln_b;             /* [H] */
+  const float *hfc1_w, *hfc1_b;           /* [M][H], [M] */
+  const float *hfc2_w, *hfc2_b;           /* [H][M], [H] */
+} or_siglip_weights;
+
+/* Intermediate values of one layer for one call (NULL: not wanted). Rows are
+ * images x patches. */
+typedef struct {
+  int layer;
+  float *x_embed;            /* [n*T][H] patch embedding + positions */
+  uint8_t *h1q; float *h1q_s;/* LN1 output quantized */
+  float *qkv;                /* [n*T][3H] (with bias) */
+  float *attn;               /* [n*T][H] attention output */
+  float *x_attn;             /* [n*T][H] residual after attention */
+  uint8_t *h2q; float *h2q_s;/* LN2 output quantized */
+  float *mlp;                /* [n*T][M] GELU(fc1) */
+  int32_t *outliers;         /* [n][32] fc2 input channels computed in float32 */
+  int32_t *noutliers;        /* [n] */
+  uint8_t *mq; float *mq_s;  /* fc2 input quantized, outlier channels zeroed */
+  float *x_mlp;              /* [n*T][H] residual after the MLP */
+} or_siglip_dump;
+
+typedef struct or_siglip or_siglip;
+or_siglip *or_siglip_create(const or_siglip_config *cfg, const or_siglip_weights *w);
+void or_siglip_destroy(or_siglip *m);
+/* Vision.forward (internal/siglip/vision.go:101-141) on n images of
+ * normalized pixels [n][3][S][S]. layer 0 runs every layer; layer > 0 stops
+ * after that many layers unless pooled is wanted, and patches then hold the
+ * states after that layer. patches [n][T][H] and pooled [n][H] may be NULL.
+ * threads > 1 spreads the images over threads; fast != 0 uses the VNNI
+ * integer products (same integers). Returns 0, or 1 for a bad layer. */
+int or_siglip_forward(const or_siglip *m, const float *pixels, int n, int layer, float *patches, float *pooled,
+                      int threads, int fast, or_siglip_dump *dump);
+/* The float32 products of linalg/gemm.go (MatMulPackedN + AddTo): dst[r][o] =
+ * the sum over k of x[r][k]*W[o][k] as one FMA chain per 256-deep block,
+ * blocks added in order, then + b[o] (b may be NULL). */
+void or_linear_f32(float *dst, const float *x, int rows, const float *W, const float *b, int in, int out);
+/* linalg.GeluTanh over n values (V-lane vector body, scalar tail). */
+void or_gelu_tanh(float *o, const float *a, int n, int V);
+/* internal/siglip/encoder.go:236-251 softmax(s*scale) in place. */
+void or_siglip_softmax(float *s, int n, float scale, int V);
+/* linalg.MatMul8Outliers (linalg/int8.go:281-349) with the packed weights of
+ * or_pack_b8; out receives the chosen channels in the order they are added. */
+void or_matmul8_outliers(float *c, const float *a, int m, const int8_t *q, const float *scale, const float *zc, int k,
+                         int n, float ratio, int32_t *out, int32_t *nout);
 
 /* CPU features used by the baseline (bit 0: AVX-VNNI, bit 1: AVX512-VNNI). */
 int or_cpu_features(void);

@@ -3,6 +3,9 @@
 #pragma once
 #include <stdint.h>
 
+#include <algorithm>
+#include <atomic>
+#include <thread>
 #include <vector>
 
 namespace orc {
@@ -46,5 +49,53 @@ void gemm_u8s8_fast(const uint8_t *A, const int8_t *Bpanels, int M, int N, int K
 // Panels of 16 output channels, 4 depths per 32-bit word (linalg/int8.go:25-34).
 void pack_panels(const int8_t *q, int N, int K, std::vector<int8_t> &out);
 int cpu_features();
+
+struct PackedMat {
+  int k = 0, n = 0;
+  std::vector<int8_t> q;       // [n][k]
+  std::vector<int8_t> panels;  // [n/16][k/4][16][4] for the fast GEMM
+  std::vector<float> scale, zc;
+  std::vector<int32_t> colsum;
+};
+
+
+void pack(PackedMat &p, const float *w, int k, int n);
+
+// linalg/parallel.go:38-72 ParallelN: about four slices per worker, each a
+// multiple of grain, taken with an atomic counter.
+template <class F>
+inline void parallel_n(int workers, int n, int grain, F fn) {
+  if (n <= 0) return;
+  grain = std::max(1, grain);
+  if (workers <= 1 || n <= grain) {
+    fn(0, n);
+    return;
+  }
+  int step = ((n + 4 * workers - 1) / (4 * workers) + grain - 1) / grain * grain;
+  workers = std::min(workers, (n + step - 1) / step);
+  std::atomic<int> next(0);
+  auto run = [&]() {
+    for (;;) {
+      int lo = next.fetch_add(1) * step;
+      if (lo >= n) return;
+      fn(lo, std::min(lo + step, n));
+    }
+  };
+  std::vector<std::thread> ts;
+  for (int w = 1; w < workers; w++) ts.emplace_back(run);
+  run();
+  for (auto &t : ts) t.join();
+}
+
+// One MatMul8N call on rows [lo, hi): c (+)= dequant(quant(a) . W^T).
+struct GemmScratch {
+  std::vector<uint8_t> aq;
+  std::vector<float> sa;
+  std::vector<int32_t> acc;
+};
+
+void matmul_rows(const PackedMat &W, const float *a, float *c, int rows, bool accumulate, bool fast,
+                 GemmScratch &s, uint8_t *aq_dump, float *sa_dump, int32_t *acc_dump);
+
 
 }  // namespace orc

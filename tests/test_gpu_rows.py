@@ -35,7 +35,7 @@ def test_layernorm_lanes_16(igdev, oracle_lib):
     assert np.array_equal(xn.cpu().numpy().view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("K", [1, 32, 256, 301, 384, 768, 1024, 1152, 4096])
+@pytest.mark.parametrize("K", [1, 32, 256, 301, 384, 768, 1024, 1152, 2048, 3072, 4096])
 def test_quantize_rows_bitexact(igdev, oracle_lib, K):
     from indecis_b200 import ops
     rng = np.random.default_rng(K)
