@@ -306,6 +306,35 @@ IG_API int ig_infer_windows(ig_model *m, const int32_t *ids, const int64_t *offs
  * *token_rows receive the sums over pooled and per-token heads. */
 IG_API int ig_model_head_rows(ig_model *m, int32_t *pooled_rows, int32_t *token_rows);
 
+/* Vocabulary size and hidden width of a model. */
+IG_API int ig_model_dims(ig_model *m, int32_t *vocab, int32_t *hidden);
+
+/* ---- Batching front end (WithBatching, model.go:137-160; batch.go) ----
+ * Concurrent callers' EncodeSeqs requests are coalesced into device
+ * batches: a worker takes the first pending request, then those already
+ * queued while the batch holds fewer than max_rows positions (<= 0: 512),
+ * encodes them in one pass and returns each caller its rows. Workers of
+ * every model (one per GPU) share one queue; max_wait_us > 0 lets a worker
+ * wait that long for more requests while its batch is short (0: the
+ * reference's behaviour, never wait). A request whose ids fail is answered
+ * alone, with its own error. */
+typedef struct ig_batcher ig_batcher;
+/* The encoder a batcher drives: pooled [nseq][hidden] of the sequences at
+ * offs (0 or an IG_ERR_* status). */
+typedef int (*ig_batch_encode_fn)(void *user, const int32_t *ids, const int64_t *offs, int32_t nseq, float *pooled);
+IG_API int ig_batcher_create(ig_model *const *models, int32_t nmodels, int32_t workers_per_model, int32_t max_rows,
+                             int32_t max_wait_us, ig_batcher **out);
+/* The same over any encoder (one `users` entry per device). */
+IG_API int ig_batcher_create_fn(ig_batch_encode_fn fn, void *const *users, int32_t nusers, int32_t hidden,
+                                int32_t workers_per_user, int32_t max_rows, int32_t max_wait_us, ig_batcher **out);
+/* Finishes the queued requests, then stops the workers. */
+IG_API void ig_batcher_destroy(ig_batcher *b);
+/* EncodeSeqs through the batcher (blocking, thread-safe): pooled [nseq][hidden]. */
+IG_API int ig_batcher_encode(ig_batcher *b, const int32_t *ids, const int64_t *offs, int32_t nseq, float *pooled,
+                             size_t pooled_len);
+/* Requests taken, device passes run and positions encoded so far. */
+IG_API int ig_batcher_stats(ig_batcher *b, int64_t *requests, int64_t *batches, int64_t *rows);
+
 /* ---- SigLIP vision tower (internal/siglip): int8 layers, float32 patch
  * embedding, attention and pooling head, as the reference computes them.
  * The seam is Vision.forward (internal/siglip/vision.go:101-141), reached by

@@ -28,7 +28,8 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_profile", "ig_profile_report", "ig_attention_noalloc", "ig_model_set_embeddings",
            "ig_plan_windows", "ig_log_softmax", "ig_decode_spans", "ig_answer_spans", "ig_window_logits",
            "ig_infer_windows", "ig_model_head_rows", "ig_vision_create", "ig_vision_destroy", "ig_vision_forward",
-           "ig_vision_forward_device", "ig_vision_dump_layer"]
+           "ig_vision_forward_device", "ig_vision_dump_layer", "ig_model_dims", "ig_batcher_create",
+           "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -64,6 +65,10 @@ class IgWindow(C.Structure):
 
 class IgSpan(C.Structure):
     _fields_ = [("type", C.c_int32), ("start", C.c_int32), ("end", C.c_int32), ("confidence", C.c_double)]
+
+
+BATCH_ENCODE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_int32), C.POINTER(C.c_int64), C.c_int32,
+                             C.POINTER(C.c_float))
 
 
 class IgVisionConfig(C.Structure):
@@ -144,6 +149,14 @@ def load() -> C.CDLL:
     L.ig_vision_forward.argtypes = [vp, vp, i32, i32, vp, C.c_size_t, vp, C.c_size_t]
     L.ig_vision_forward_device.argtypes = [vp, vp, i32, i32, vp, vp, vp]
     L.ig_vision_dump_layer.argtypes = [vp, vp, i32, C.POINTER(IgVisionDump), vp, C.c_size_t]
+    L.ig_model_dims.argtypes = [vp, i32p, i32p]
+    L.ig_batcher_create.argtypes = [C.POINTER(C.c_void_p), i32, i32, i32, i32, C.POINTER(C.c_void_p)]
+    L.ig_batcher_create_fn.argtypes = [BATCH_ENCODE_FN, C.POINTER(C.c_void_p), i32, i32, i32, i32, i32,
+                                       C.POINTER(C.c_void_p)]
+    L.ig_batcher_destroy.argtypes = [vp]
+    L.ig_batcher_destroy.restype = None
+    L.ig_batcher_encode.argtypes = [vp, vp, vp, i32, vp, C.c_size_t]
+    L.ig_batcher_stats.argtypes = [vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]
     L.ig_profile.argtypes = [i32]
     L.ig_profile_report.argtypes = [C.c_char_p, C.c_size_t]
     L.ig_profile_report.restype = C.c_int64

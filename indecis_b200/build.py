@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libindecis_b200.so")
-SOURCES = ["libindecis_b200.cu", "spans.cpp"]
+SOURCES = ["libindecis_b200.cu", "spans.cpp", "batcher.cpp"]
 HEADERS = ["common.cuh", "exactmath.cuh", "internal.h", "gemm_i8.cu", "gemm_persist.cu", "rows_fast.cu", "rows.cu", "rows_ln.cu", "attention.cu", "attention_tc.cu", "attention_short.cu", "siglip.cu", "capi.cu", "siglip_capi.cu", "noalloc.cu"]
 
 NVCC_FLAGS = [

@@ -940,6 +940,13 @@ int ig_window_logits(ig_model *m, const int32_t *ids, const int64_t *offs, int32
                      token_len);
 }
 
+int ig_model_dims(ig_model *m, int32_t *vocab, int32_t *hidden) {
+  if (!m) return fail(IG_ERR_BAD_ARG, "null model");
+  if (vocab) *vocab = m->cfg.vocab;
+  if (hidden) *hidden = m->H;
+  return 0;
+}
+
 int ig_model_head_rows(ig_model *m, int32_t *pooled_rows, int32_t *token_rows) {
   t_last_error.clear();
   if (!m || !pooled_rows || !token_rows) return fail(IG_ERR_BAD_ARG, "null argument");

@@ -4,7 +4,9 @@
 //   exp: Cephes expf as linalg/vec_simd.go:216-264 (vector body, FMA) and
 //        linalg/fastmath.go:35-51 (scalar tail, no FMA);
 //   GELU(erf) x gate: the Eigen/XLA erf rational of linalg/fastmath.go:7-26,
-//        in the FMA order of linalg/gelu_amd64.s:165-225.
+//        in the FMA order of linalg/gelu_amd64.s:165-225;
+//   GELU(tanh): x / (1 + exp(-2u)) as linalg/vec_simd.go:166-197 (vector body,
+//        FMA) and fastmath.go:28-32 (scalar tail), IEEE division.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -27,6 +29,29 @@ __device__ __forceinline__ float exp_body(float v) {
   const int ni = __float2int_rn(n);
   const float pw = __int_as_float((ni + 127) << 23);
   return under ? 0.0f : __fmul_rn(y, pw);
+}
+
+// exp_body for two lanes (packed f32x2 steps, each rounding as the scalar one;
+// no packed add is fed by a packed multiply).
+__device__ __forceinline__ float2 exp_body2(float2 v) {
+  const bool ux = v.x < -87.3f, uy = v.y < -87.3f;
+  v.x = fminf(fmaxf(v.x, -87.3f), 88.7f);
+  v.y = fminf(fmaxf(v.y, -87.3f), 88.7f);
+  const float2 t = __ffma2_rn(v, make_float2(1.44269504088896341f, 1.44269504088896341f),
+                              make_float2(12582912.0f, 12582912.0f));
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  float2 r = __ffma2_rn(n, make_float2(-0.693359375f, -0.693359375f), v);
+  r = __ffma2_rn(n, make_float2(2.12194440e-4f, 2.12194440e-4f), r);
+  float2 p = __ffma2_rn(r, make_float2(1.9875691500e-4f, 1.9875691500e-4f), make_float2(1.3981999507e-3f, 1.3981999507e-3f));
+  p = __ffma2_rn(r, p, make_float2(8.3334519073e-3f, 8.3334519073e-3f));
+  p = __ffma2_rn(r, p, make_float2(4.1665795894e-2f, 4.1665795894e-2f));
+  p = __ffma2_rn(r, p, make_float2(1.6666665459e-1f, 1.6666665459e-1f));
+  p = __ffma2_rn(r, p, make_float2(5.0000001201e-1f, 5.0000001201e-1f));
+  const float2 y = __fadd2_rn(__ffma2_rn(__fmul2_rn(p, r), r, r), make_float2(1.0f, 1.0f));
+  // 2^n from t's bits (0x4B400000 + n): (n + 127) << 23.
+  const float px = __int_as_float((__float_as_int(t.x) << 23) + ((127 - 0x4B400000) << 23));
+  const float py = __int_as_float((__float_as_int(t.y) << 23) + ((127 - 0x4B400000) << 23));
+  return make_float2(ux ? 0.0f : __fmul_rn(y.x, px), uy ? 0.0f : __fmul_rn(y.y, py));
 }
 
 // Scalar-tail exp (exp32, fastmath.go:35-51): separate roundings throughout.
@@ -222,6 +247,33 @@ __device__ __forceinline__ float gelu_tanh_body(float x) {
   const float y = __fadd_rn(__fmaf_rn(__fmul_rn(p, r), r, r), 1.0f);
   const float pw = __int_as_float((__float2int_rn(n) + 127) << 23);
   return __fdiv_rn(x, __fadd_rn(1.0f, __fmul_rn(y, pw)));
+}
+
+// gelu_tanh_body for two lanes: the same roundings with paired f32x2
+// operations wherever a packed add is not fed by a packed multiply; the
+// final 1 + y*2^n and the division stay scalar.
+__device__ __forceinline__ float2 gelu_tanh_body2(float2 x) {
+  float2 v = __fmul2_rn(x, x);
+  v = __ffma2_rn(v, f2(0.044715f), f2(1.0f));
+  v = __fmul2_rn(v, x);
+  v = __fmul2_rn(v, f2(-1.5957691216057308f));
+  v.x = fminf(fmaxf(v.x, -87.3f), 88.7f);
+  v.y = fminf(fmaxf(v.y, -87.3f), 88.7f);
+  const float2 t = __ffma2_rn(v, f2(1.44269504088896341f), f2(kMagic));
+  const float2 n = __fadd2_rn(t, f2(-kMagic));
+  float2 r = __ffma2_rn(n, f2(-0.693359375f), v);
+  r = __ffma2_rn(n, f2(2.12194440e-4f), r);
+  float2 p = __ffma2_rn(r, f2(1.9875691500e-4f), f2(1.3981999507e-3f));
+  p = __ffma2_rn(r, p, f2(8.3334519073e-3f));
+  p = __ffma2_rn(r, p, f2(4.1665795894e-2f));
+  p = __ffma2_rn(r, p, f2(1.6666665459e-1f));
+  p = __ffma2_rn(r, p, f2(5.0000001201e-1f));
+  const float2 y = __fadd2_rn(__ffma2_rn(__fmul2_rn(p, r), r, r), f2(1.0f));
+  // 2^n from t's bits (0x4B400000 + n): (n + 127) << 23.
+  const float pwx = __int_as_float((__float_as_int(t.x) << 23) + ((127 - kMagicBits) << 23));
+  const float pwy = __int_as_float((__float_as_int(t.y) << 23) + ((127 - kMagicBits) << 23));
+  return make_float2(__fdiv_rn(x.x, __fadd_rn(1.0f, __fmul_rn(y.x, pwx))),
+                     __fdiv_rn(x.y, __fadd_rn(1.0f, __fmul_rn(y.y, pwy))));
 }
 
 // geluTanhScalar (fastmath.go:28-32): separate roundings, exp32.

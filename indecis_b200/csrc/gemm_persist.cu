@@ -175,8 +175,8 @@ __device__ __forceinline__ void add_bias16(float (&v)[16], const float *__restri
 // first row, sa the thread's row scale), column chunks g, g + GROUPS, ...
 template <int BN, int EPI, int GROUPS, int NBUF>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int row0, float sa, int g, int lane,
-                                              StageWriter<NBUF> &sw, const CUtensorMap *mapC,
-                                              const GemmEpilogue &ep) {
+                                              StageWriter<NBUF> &sw, const CUtensorMap *mapC, const GemmEpilogue &ep,
+                                              int ep_rows) {
   constexpr int kPGroups = GROUPS;
   if constexpr (EPI == kEpiF32 || EPI == kEpiI32) {
 #pragma unroll 1
@@ -221,7 +221,11 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int
         if constexpr (EPI == kEpiGeluTanh) {
           if (seg_row + j0 + 16 <= body_end) {
 #pragma unroll
-            for (int k = 0; k < 16; k++) v[k] = gelu_tanh_body(v[k]);
+            for (int k = 0; k < 16; k += 2) {
+              const float2 o2 = gelu_tanh_body2(make_float2(v[k], v[k + 1]));
+              v[k] = o2.x;
+              v[k + 1] = o2.y;
+            }
           } else {
 #pragma unroll
             for (int k = 0; k < 16; k++) v[k] = gelu_tanh_at(v[k], seg_row + j0 + k, seg_len, ep.V);
@@ -230,6 +234,49 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int
         StageWriter<NBUF>::put_half(buf, lane, h, v);
       }
       sw.finish(mapC, buf, lane, n0 + c, row0, EPI == kEpiF32Bias && ep.accumulate);
+    }
+  } else if constexpr (EPI == kEpiOutlierRes) {
+    // The int8 product of the rest, then this row's image's outlier terms in
+    // order, then the bias; added into C (the residual) by the TMA reduce.
+    const int row = row0 + lane;
+    const int img = row / ep.seg_rows;
+    const bool row_ok = row < ep_rows;
+    const int cnt = row_ok ? __ldg(ep.nout + img) : 0;
+    const float *ov = ep.outv + (size_t)row * 32;
+    const float *ow = ep.outw + (size_t)img * 32 * N;
+#pragma unroll 1
+    for (int c = g * 32; c < BN; c += 32 * kPGroups) {
+      if (n0 + c >= N) continue;
+      uint8_t *buf = sw.begin(lane);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tbase + c + 16 * h, r);
+        tmem_ld_wait();
+        float v[16];
+        const int j0 = n0 + c + 16 * h;
+        dequant16(r, ep.sb, ep.zc, j0, N, sa, v);
+        for (int k = 0; k < cnt; k++) {
+          const float xv = __ldg(ov + k);
+          const float *wk = ow + (size_t)k * N;
+          if (j0 + 16 <= N) {
+#pragma unroll
+            for (int t = 0; t < 16; t += 4) {
+              const float4 w4 = __ldg(reinterpret_cast<const float4 *>(wk + j0 + t));
+              v[t] = __fadd_rn(v[t], __fmul_rn(xv, w4.x));
+              v[t + 1] = __fadd_rn(v[t + 1], __fmul_rn(xv, w4.y));
+              v[t + 2] = __fadd_rn(v[t + 2], __fmul_rn(xv, w4.z));
+              v[t + 3] = __fadd_rn(v[t + 3], __fmul_rn(xv, w4.w));
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < 16; t++) v[t] = __fadd_rn(v[t], __fmul_rn(xv, __ldg(wk + min(j0 + t, N - 1))));
+          }
+        }
+        add_bias16(v, ep.bias, j0, N);
+        StageWriter<NBUF>::put_half(buf, lane, h, v);
+      }
+      sw.finish(mapC, buf, lane, n0 + c, row0, true);
     }
   } else if constexpr (EPI == kEpiGeglu) {
     // Tile columns [0, BN/2) are GELU inputs, [BN/2, BN) their gates.
@@ -386,7 +433,7 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
       const int row0 = m0 + q * 32;
       const uint32_t tbase = tmem + b * BN + ((uint32_t)(q * 32) << 16);
       const float sa = (EPI != kEpiI32 && row_ok) ? __ldg(ep.sa + row) : 0.0f;
-      epilogue_tile<BN, EPI, kPGroups, S::kStageBufs>(tbase, n0, N, row0, sa, g, lane, sw, &mapC, eps);
+      epilogue_tile<BN, EPI, kPGroups, S::kStageBufs>(tbase, n0, N, row0, sa, g, lane, sw, &mapC, eps, M);
       // This accumulator buffer is drained: hand it back to the MMA warp.
       tc_fence_before();
       __syncwarp();
@@ -454,9 +501,13 @@ static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, 
   void *out = epi == kEpiI32 ? (void *)ep.acc_out : (void *)ep.C;
   if (!out || (reinterpret_cast<uintptr_t>(out) & 15) || (ep.ldc & 3)) return -1;
   if (epi != kEpiI32 && ((reinterpret_cast<uintptr_t>(ep.sb) | reinterpret_cast<uintptr_t>(ep.zc)) & 15)) return -1;
-  if (epi == kEpiF32Bias || epi == kEpiGeluTanh) {
+  if (epi == kEpiF32Bias || epi == kEpiGeluTanh || epi == kEpiOutlierRes) {
     if (!ep.bias || (reinterpret_cast<uintptr_t>(ep.bias) & 15)) return IG_ERR_BAD_ARG;
     if (epi == kEpiGeluTanh && (ep.seg_rows < 1 || ep.V < 1)) return IG_ERR_BAD_ARG;
+    if (epi == kEpiOutlierRes &&
+        (ep.seg_rows < 1 || !ep.nout || !ep.outv || !ep.outw || (reinterpret_cast<uintptr_t>(ep.outw) & 15) ||
+         (g.N & 3)))
+      return IG_ERR_BAD_ARG;
   }
   const int out_cols = epi == kEpiGeglu ? ep.geglu_n : g.N;
   CUtensorMap mc;
@@ -472,6 +523,7 @@ static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, 
     IG_PCASE(kEpiI32)
     IG_PCASE(kEpiF32Bias)
     IG_PCASE(kEpiGeluTanh)
+    IG_PCASE(kEpiOutlierRes)
     case kEpiGeglu:
       e = launch_persist<256, kEpiGeglu>(ma, mb, mc, g.M, g.N, g.K, ep, st);
       break;

@@ -13,6 +13,7 @@ enum Epilogue : int {
   kEpiGeglu = 3,
   kEpiF32Bias = 4,   // C (+)= dequant + bias[j]   (MatMul8N then AddTo(bias), accumulate: AddTo(x, .))
   kEpiGeluTanh = 5,  // C = GeluTanh(dequant + bias[j])
+  kEpiOutlierRes = 6,  // C += (dequant + outlier terms in order) + bias[j]  (MatMul8Outliers, then AddTo twice)
 };
 
 struct GemmArgs {
@@ -35,8 +36,14 @@ struct GemmEpilogue {
   int geglu_n;  // GeGLU output width (intermediate size)
   // kEpiF32Bias, kEpiGeluTanh
   const float *bias;  // [N], 16-byte aligned
-  int seg_rows;       // kEpiGeluTanh: rows per GeluTanh call (its vector/tail split), >= 1
+  int seg_rows;       // kEpiGeluTanh: rows per GeluTanh call (its vector/tail split), >= 1;
+                      // kEpiOutlierRes: rows per image
   int V;              // float32 lanes of that split
+  // kEpiOutlierRes: per image its outlier count, the rows' set-aside values
+  // [M][32] and the dequantized weight rows [images][32][N] of those channels.
+  const int32_t *nout;
+  const float *outv;
+  const float *outw;
 };
 
 int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t st);
@@ -163,9 +170,10 @@ int launch_pool_attn(const float *kv, const float *probe_q, int nimg, int T, int
 int launch_outliers_select(const float *x, int nimg, int T, int K, float ratio, float *colmax, int32_t *cand,
                            int32_t *out, int32_t *nout, float *outv, cudaStream_t st);
 // After it: x += (c + the outlier terms in order) + bias, c the int8 product
-// [n*T][N], q/scale the packed weights.
+// [n*T][N], q/scale the packed weights; w [n][32][N] is scratch for the
+// dequantized weight rows of the outlier channels.
 int launch_outliers_fixup(const float *c, int nimg, int T, int N, const int32_t *out, const int32_t *nout,
-                          const float *outv, const int8_t *q, int ldq, const float *scale, const float *bias, float *x,
-                          cudaStream_t st);
+                          const float *outv, const int8_t *q, int ldq, const float *scale, const float *bias, float *w,
+                          float *x, cudaStream_t st);
 
 }  // namespace ig

@@ -253,7 +253,7 @@ int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps
                     int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
   if (gamma) {
-    int rc = launch_ln8<false>(x, nullptr, 0, EmbTable{}, gamma, M, H, eps, V, xn, q, ldq, sa, st);
+    int rc = launch_ln8<false>(x, nullptr, 0, EmbTable{}, gamma, nullptr, M, H, eps, V, xn, q, ldq, sa, st);
     if (rc != -1) return rc;
     rc = launch_ln_group<false>(x, nullptr, 0, EmbTable{}, gamma, nullptr, M, H, eps, V, xn, q, ldq, sa, st);
     if (rc != -1) return rc;
@@ -269,7 +269,9 @@ int launch_ln_beta(const float *x, const float *gamma, const float *beta, int M,
                    uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
   if (!gamma || !beta) return IG_ERR_BAD_ARG;
-  const int rc = launch_ln_group<false>(x, nullptr, 0, EmbTable{}, gamma, beta, M, H, eps, V, xout, q, ldq, sa, st);
+  int rc = launch_ln8<false>(x, nullptr, 0, EmbTable{}, gamma, beta, M, H, eps, V, xout, q, ldq, sa, st);
+  if (rc != -1) return rc;
+  rc = launch_ln_group<false>(x, nullptr, 0, EmbTable{}, gamma, beta, M, H, eps, V, xout, q, ldq, sa, st);
   return rc == -1 ? IG_ERR_UNSUPPORTED : rc;
 }
 
@@ -277,7 +279,7 @@ int launch_embed_checked(const int32_t *ids, int vocab, const EmbTable &emb, con
                          double eps, int V, float *x, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
   if (M <= 0) return 0;
   {
-    int rc = launch_ln8<true>(nullptr, ids, vocab, emb, gamma, M, H, eps, V, x, q, ldq, sa, st);
+    int rc = launch_ln8<true>(nullptr, ids, vocab, emb, gamma, nullptr, M, H, eps, V, x, q, ldq, sa, st);
     if (rc != -1) return rc;
     rc = launch_ln_group<true>(nullptr, ids, vocab, emb, gamma, nullptr, M, H, eps, V, x, q, ldq, sa, st);
     if (rc != -1) return rc;

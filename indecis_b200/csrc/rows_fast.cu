@@ -36,7 +36,8 @@ __device__ __forceinline__ uint32_t quant_byte_slow(float v, float inv) {
 template <int NB, bool EMBED>
 __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, const int32_t *__restrict__ ids,
                                                   int vocab, const EmbTable emb,
-                                                  const float *__restrict__ gamma, int M, double eps,
+                                                  const float *__restrict__ gamma,
+                                                  const float *__restrict__ beta, int M, double eps,
                                                   float *__restrict__ xout, uint8_t *__restrict__ q, int ldq,
                                                   float *__restrict__ sa) {
   constexpr int H = 8 * NB;
@@ -86,6 +87,7 @@ __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, c
 #pragma unroll
   for (int b = 0; b < NB; b++) {
     v[b] = __fmul_rn(__fmul_rn(v[b], rstd), __ldg(gamma + k + 8 * b));
+    if (beta) v[b] = __fadd_rn(v[b], __ldg(beta + k + 8 * b));  // AddTo(o, beta) (SigLIP norms)
     mx = fmax_nan(mx, fabsf(v[b]));
   }
   if (xout && rv) {
@@ -249,19 +251,21 @@ static int launch_head_logits_tok(const float *w, const float *b, int rows, int 
 // LayerNorm (+ quantization) for V = 8 and H in {64, 128, 256}; -1 when this
 // path does not apply.
 template <bool EMBED>
-static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma, int M,
-                      int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa, cudaStream_t st) {
+static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma,
+                      const float *beta, int M, int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa,
+                      cudaStream_t st) {
   if (V != 8 || !gamma) return -1;
   if (q && ((ldq & 7) || (reinterpret_cast<uintptr_t>(q) & 7))) return -1;
   const int blocks = (M + 31) / 32;
 #define IG_LN8(NB)                                                                                                 \
   case 8 * NB:                                                                                                     \
-    ln8_kernel<NB, EMBED><<<blocks, 256, 0, st>>>(x, ids, vocab, emb, gamma, M, eps, xout, q, ldq, sa);           \
+    ln8_kernel<NB, EMBED><<<blocks, 256, 0, st>>>(x, ids, vocab, emb, gamma, beta, M, eps, xout, q, ldq, sa);     \
     break;
   switch (H) {
     IG_LN8(8)
     IG_LN8(16)
     IG_LN8(32)
+    IG_LN8(96)
     default:
       return -1;
   }

@@ -76,7 +76,7 @@ __device__ __forceinline__ void load8_patch(const F32Gemm &p, int r, int k, floa
 }
 
 template <bool PATCH>
-__global__ void __launch_bounds__(256) f32_chain_gemm_kernel(const F32Gemm p) {
+__global__ void __launch_bounds__(256, 2) f32_chain_gemm_kernel(const F32Gemm p) {
   __shared__ __align__(16) float As[2][kFK][kFB + 4];
   __shared__ __align__(16) float Ws[2][kFK][kFB + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(256) f32_chain_gemm_kernel(const F32Gemm p) {
   for (int i = 0; i < 8; i++)
 #pragma unroll
     for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+
   // Output (row, col) of acc[i][j].
   auto orow = [&](int i) { return m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4); };
   auto ocol = [&](int j) { return n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4); };
@@ -187,161 +188,193 @@ int launch_f32_gemm(const F32Gemm &p0, cudaStream_t st) {
 
 // ---- attention: one CTA per (image, head) --------------------------------------
 
-constexpr int kAttMaxT = 256;   // patches held in shared memory
-constexpr int kAttD = 64;       // head dimension
-constexpr int kAttQB = 64;      // queries per block
+constexpr int kAttMaxT = 256;         // patches held in shared memory
+constexpr int kAttD = 64;             // head dimension
+constexpr int kAttQB = 32;            // queries per block
 constexpr int kAttKP = kAttMaxT + 4;  // pitch of K^T rows
-constexpr int kAttSP = kAttQB + 4;    // pitch of score rows (one key per row)
+constexpr int kAttSP = kAttQB + 4;    // pitch of score rows (one key per row) and of Q^T rows
+constexpr int kAttThreads = 512;      // 8 producer warps + 8 consumer warps
 struct AttF32Smem {
-  static constexpr int kKt = 0;                                  // [64][kAttKP]  K^T
-  static constexpr int kV = kKt + kAttD * kAttKP * 4;            // [256][64]     V
-  static constexpr int kQt = kV + kAttMaxT * kAttD * 4;          // [64][kAttSP]  Q^T of the block
-  static constexpr int kSt = kQt + kAttD * kAttSP * 4;           // [256][kAttSP] scores, key-major
-  static constexpr int kTotal = kSt + kAttMaxT * kAttSP * 4;
+  static constexpr int kKt = 0;                                   // [64][kAttKP]     K^T
+  static constexpr int kV = kKt + kAttD * kAttKP * 4;             // [256][64]        V
+  static constexpr int kQt = kV + kAttMaxT * kAttD * 4;           // [2][64][kAttSP]  Q^T of a block
+  static constexpr int kSt = kQt + 2 * kAttD * kAttSP * 4;        // [2][256][kAttSP] scores, key-major
+  static constexpr int kInv = kSt + 2 * kAttMaxT * kAttSP * 4;    // [2][32] 1/sum of each row
+  static constexpr int kTotal = kInv + 2 * kAttQB * 4;
   static_assert(kTotal <= 227 * 1024, "shared memory");
 };
+// Named barriers (0 is __syncthreads): block b's scores ready / its buffer free.
+constexpr int kBarFull = 1, kBarEmpty = 3, kBarProd = 5;
 
-__global__ void __launch_bounds__(256, 1)
+// Warp-specialized: warps 0-7 (producer) load a block of 32 queries,
+// compute its scores S = QK^T (4 queries x 7 key groups per thread, keys
+// lane + 32m, the query values broadcast) and its softmax into one of two
+// score buffers; warps 8-15 (consumer) compute O = PV of the block before
+// (4 queries x 2 dimensions per thread). Every output keeps the reference's
+// chain: S over the head dimension, O over the keys, in order; chains that
+// share an operand run in pairs (f32x2: each lane one fused multiply-add).
+__global__ void __launch_bounds__(kAttThreads, 1)
     attn_f32_kernel(const float *__restrict__ qkv, int T, int H, int nh, float scale, float *__restrict__ ctx) {
   extern __shared__ __align__(16) uint8_t sm[];
   float *Kt = reinterpret_cast<float *>(sm + AttF32Smem::kKt);
   float *Vs = reinterpret_cast<float *>(sm + AttF32Smem::kV);
-  float *Qt = reinterpret_cast<float *>(sm + AttF32Smem::kQt);
-  float *St = reinterpret_cast<float *>(sm + AttF32Smem::kSt);
   const int img = blockIdx.x / nh, h = blockIdx.x % nh;
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t row0 = (size_t)img * T;
   const size_t ld = (size_t)3 * H;
-  const int TP = (T + 63) & ~63;  // keys padded to whole groups of 64 (zeros)
-  for (int idx = tid; idx < TP * 16; idx += 256) {
-    const int u = idx >> 4, j4 = (idx & 15) * 4;
-    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-    if (u < T) {
-      const float *src = qkv + (row0 + u) * ld + h * kAttD + j4;
-      kv = __ldg(reinterpret_cast<const float4 *>(src + H));
-      vv = __ldg(reinterpret_cast<const float4 *>(src + 2 * H));
-    }
+  const int T4 = (T + 3) & ~3;  // keys in whole groups of four (zeros past T)
+  // K^T: lanes run along the keys, so the scalar stores hit distinct banks.
+  for (int idx = tid; idx < T4 * 16; idx += kAttThreads) {
+    const int u = idx % T4, j4 = (idx / T4) * 4;
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (u < T) kv = __ldg(reinterpret_cast<const float4 *>(qkv + (row0 + u) * ld + H + h * kAttD + j4));
     Kt[(j4 + 0) * kAttKP + u] = kv.x;
     Kt[(j4 + 1) * kAttKP + u] = kv.y;
     Kt[(j4 + 2) * kAttKP + u] = kv.z;
     Kt[(j4 + 3) * kAttKP + u] = kv.w;
-    *reinterpret_cast<float4 *>(Vs + u * kAttD + j4) = vv;
   }
-  const int nb = TP / 64;  // key groups of 64
-  const int nv = T - T % 8;  // ExpShift's vector part (V = 8 lanes)
-  for (int q0 = 0; q0 < T; q0 += kAttQB) {
-    for (int idx = tid; idx < kAttQB * 16; idx += 256) {
-      const int qq = idx >> 4, j4 = (idx & 15) * 4;
-      float4 qv = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (q0 + qq < T) qv = __ldg(reinterpret_cast<const float4 *>(qkv + (row0 + q0 + qq) * ld + h * kAttD + j4));
-      Qt[(j4 + 0) * kAttSP + qq] = qv.x;
-      Qt[(j4 + 1) * kAttSP + qq] = qv.y;
-      Qt[(j4 + 2) * kAttSP + qq] = qv.z;
-      Qt[(j4 + 3) * kAttSP + qq] = qv.w;
-    }
-    __syncthreads();
-    // S = Q K^T: queries ty*4.., keys tx*4 + 64b.., one chain over the head
-    // dimension each (the whole dimension is one 256-deep block).
-    {
-      float s[4][16];
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int c = 0; c < 16; c++) s[i][c] = 0.0f;
-#pragma unroll 4
-      for (int j = 0; j < kAttD; j++) {
-        const float4 a = *reinterpret_cast<const float4 *>(Qt + j * kAttSP + ty * 4);
-        const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int b = 0; b < 4; b++) {
-          if (b < nb) {
-            const float4 k = *reinterpret_cast<const float4 *>(Kt + j * kAttKP + tx * 4 + 64 * b);
-            const float kv[4] = {k.x, k.y, k.z, k.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-              for (int c = 0; c < 4; c++) s[i][4 * b + c] = __fmaf_rn(av[i], kv[c], s[i][4 * b + c]);
-          }
-        }
+  for (int idx = tid; idx < T * 16; idx += kAttThreads) {
+    const int u = idx >> 4, j4 = (idx & 15) * 4;
+    *reinterpret_cast<float4 *>(Vs + u * kAttD + j4) =
+        __ldg(reinterpret_cast<const float4 *>(qkv + (row0 + u) * ld + 2 * H + h * kAttD + j4));
+  }
+  __syncthreads();
+  const int nb = (T + kAttQB - 1) / kAttQB;
+  if (warp < 8) {
+    // ---- producer ----
+    const int pt = tid;                    // 0..255
+    const int nv = T - T % 8;              // ExpShift's vector part (V = 8 lanes)
+    const int nkg = (T4 + 31) >> 5;        // key groups of 32
+    const int sq = warp * 4;               // this warp's four queries
+    for (int b = 0; b < nb; b++) {
+      const int q0 = b * kAttQB, buf = b & 1;
+      float *Qt = reinterpret_cast<float *>(sm + AttF32Smem::kQt) + buf * kAttD * kAttSP;
+      float *St = reinterpret_cast<float *>(sm + AttF32Smem::kSt) + buf * kAttMaxT * kAttSP;
+      if (b >= 2) named_barrier_sync(kBarEmpty + buf, kAttThreads);  // the consumer is done with this buffer
+      for (int idx = pt; idx < kAttQB * 16; idx += 256) {
+        const int qq = idx & 31, j4 = (idx >> 5) * 4;
+        float4 qv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q0 + qq < T) qv = __ldg(reinterpret_cast<const float4 *>(qkv + (row0 + q0 + qq) * ld + h * kAttD + j4));
+        Qt[(j4 + 0) * kAttSP + qq] = qv.x;
+        Qt[(j4 + 1) * kAttSP + qq] = qv.y;
+        Qt[(j4 + 2) * kAttSP + qq] = qv.z;
+        Qt[(j4 + 3) * kAttSP + qq] = qv.w;
       }
-      // Scale(s, scale), stored key-major.
-#pragma unroll
-      for (int b = 0; b < 4; b++)
-        if (b < nb)
-#pragma unroll
-          for (int c = 0; c < 4; c++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) St[(tx * 4 + 64 * b + c) * kAttSP + ty * 4 + i] = __fmul_rn(s[i][4 * b + c], scale);
-    }
-    __syncthreads();
-    // softmax of each query row: four threads per row, each running two of
-    // ExpShift's eight lane sums in order; the first combines them, adds the
-    // scalar tail and takes 1/sum.
-    {
-      const int row = tid >> 2, part = tid & 3;
-      float mx = -INFINITY;
-      for (int u = part; u < T; u += 4) mx = fmaxf(mx, St[u * kAttSP + row]);
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      float la = 0.0f, lb = 0.0f;
-      const int ea = 2 * part, eb = 2 * part + 1;
-      for (int u0 = 0; u0 < nv; u0 += 8) {
-        float *pa = St + (u0 + ea) * kAttSP + row, *pb = St + (u0 + eb) * kAttSP + row;
-        const float xa = exp_body(__fsub_rn(*pa, mx)), xb = exp_body(__fsub_rn(*pb, mx));
-        *pa = xa, *pb = xb;
-        la = __fadd_rn(la, xa);
-        lb = __fadd_rn(lb, xb);
-      }
-      const int base = threadIdx.x & ~3 & 31;
-      float lanes[8];
-#pragma unroll
-      for (int p = 0; p < 4; p++) {
-        lanes[2 * p] = __shfl_sync(0xffffffffu, la, base + p);
-        lanes[2 * p + 1] = __shfl_sync(0xffffffffu, lb, base + p);
-      }
-      float inv = 0.0f;
-      if (part == 0) {
-        float sum = 0.0f;
-#pragma unroll
-        for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, lanes[l]);
-        for (int u = nv; u < T; u++) {
-          const float e = exp_tail(__fsub_rn(St[u * kAttSP + row], mx));
-          St[u * kAttSP + row] = e;
-          sum = __fadd_rn(sum, e);
-        }
-        inv = __fdiv_rn(1.0f, sum);
-      }
-      __syncwarp();
-      inv = __shfl_sync(0xffffffffu, inv, base);
-      for (int u = part; u < T; u += 4) St[u * kAttSP + row] = __fmul_rn(St[u * kAttSP + row], inv);
-    }
-    __syncthreads();
-    // O = P V: queries ty*4.., dimensions tx*4.., one chain over the keys.
-    {
-      float o[4][4];
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) o[i][c] = 0.0f;
-#pragma unroll 4
-      for (int u = 0; u < T; u++) {
-        const float4 pv = *reinterpret_cast<const float4 *>(St + u * kAttSP + ty * 4);
-        const float4 vv = *reinterpret_cast<const float4 *>(Vs + u * kAttD + tx * 4);
-        const float pa[4] = {pv.x, pv.y, pv.z, pv.w}, va[4] = {vv.x, vv.y, vv.z, vv.w};
+      named_barrier_sync(kBarProd, 256);
+      // S = Q K^T (one 256-deep block), Scale(s, scale), stored key-major.
+      if (q0 + sq < T) {
+        float2 acc[4][4];  // [query][group pair]: .x group 2p, .y group 2p + 1
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-          for (int c = 0; c < 4; c++) o[i][c] = __fmaf_rn(pa[i], va[c], o[i][c]);
-      }
+          for (int g = 0; g < 4; g++) acc[i][g] = make_float2(0.0f, 0.0f);
+        const float *kr = Kt + lane;
+#pragma unroll 4
+        for (int j = 0; j < kAttD; j++) {
+          const float4 a = *reinterpret_cast<const float4 *>(Qt + j * kAttSP + sq);
+          const float av[4] = {a.x, a.y, a.z, a.w};
+          const float *kj = kr + j * kAttKP;
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int q = q0 + ty * 4 + i;
-        if (q < T)
-          *reinterpret_cast<float4 *>(ctx + (row0 + q) * H + h * kAttD + tx * 4) =
-              make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+          for (int g = 0; g < 4; g++) {
+            if (2 * g < nkg) {
+              const float2 kk = make_float2(kj[64 * g], kj[64 * g + 32]);
+#pragma unroll
+              for (int i = 0; i < 4; i++) acc[i][g] = __ffma2_rn(make_float2(av[i], av[i]), kk, acc[i][g]);
+            }
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+          const int u = lane + 32 * m;
+          if (m < nkg && u < T4) {
+            float sv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) sv[i] = __fmul_rn((m & 1) ? acc[i][m >> 1].y : acc[i][m >> 1].x, scale);
+            *reinterpret_cast<float4 *>(St + u * kAttSP + sq) = make_float4(sv[0], sv[1], sv[2], sv[3]);
+          }
+        }
       }
+      named_barrier_sync(kBarProd, 256);
+      // softmax of each query row: eight threads per row, thread p running
+      // ExpShift's lane p in order (two exponentials at a time, summed in
+      // order); the first combines the lane sums, adds the scalar tail and
+      // takes 1/sum.
+      if (q0 + (warp << 2) < T) {
+        const int row = pt >> 3, part = pt & 7;
+        float mx = -INFINITY;
+        for (int u = part; u < T; u += 8) mx = fmaxf(mx, St[u * kAttSP + row]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        float l = 0.0f;
+        int u = part;
+        for (; u + 8 < nv; u += 16) {
+          float *p0 = St + u * kAttSP + row, *p1 = p0 + 8 * kAttSP;
+          const float2 e = exp_body2(make_float2(__fsub_rn(*p0, mx), __fsub_rn(*p1, mx)));
+          *p0 = e.x, *p1 = e.y;
+          l = __fadd_rn(__fadd_rn(l, e.x), e.y);
+        }
+        if (u < nv) {
+          float *p0 = St + u * kAttSP + row;
+          const float e = exp_body(__fsub_rn(*p0, mx));
+          *p0 = e;
+          l = __fadd_rn(l, e);
+        }
+        const int base = lane & ~7;
+        float inv = 0.0f;
+        float lanes[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) lanes[k] = __shfl_sync(0xffffffffu, l, base + k);
+        if (part == 0) {
+          float sum = 0.0f;
+#pragma unroll
+          for (int k = 0; k < 8; k++) sum = __fadd_rn(sum, lanes[k]);
+          for (int t = nv; t < T; t++) {
+            const float e = exp_tail(__fsub_rn(St[t * kAttSP + row], mx));
+            St[t * kAttSP + row] = e;
+            sum = __fadd_rn(sum, e);
+          }
+          inv = __fdiv_rn(1.0f, sum);
+        }
+        // Scale(s, 1/sum) is left to the consumer, which multiplies each
+        // weight as it reads it (the same single rounding).
+        if (part == 0) reinterpret_cast<float *>(sm + AttF32Smem::kInv)[buf * kAttQB + row] = inv;
+      }
+      named_barrier_arrive(kBarFull + buf, kAttThreads);  // block b's exponentials and 1/sum are ready
     }
-    __syncthreads();
+  } else {
+    // ---- consumer: O = P V, one chain over the keys each ----
+    const int cw = warp - 8;
+    const int oq = (cw & 1) * 16 + (lane & 3) * 4, od = (cw >> 1) * 16 + (lane >> 2) * 2;
+    for (int b = 0; b < nb; b++) {
+      const int q0 = b * kAttQB, buf = b & 1;
+      const float *St = reinterpret_cast<const float *>(sm + AttF32Smem::kSt) + buf * kAttMaxT * kAttSP;
+      named_barrier_sync(kBarFull + buf, kAttThreads);
+      if (q0 + (cw & 1) * 16 < T) {
+        const float4 iv = *reinterpret_cast<const float4 *>(sm + AttF32Smem::kInv + (buf * kAttQB + oq) * 4);
+        const float2 i01 = make_float2(iv.x, iv.y), i23 = make_float2(iv.z, iv.w);
+        float2 o[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[i] = make_float2(0.0f, 0.0f);
+#pragma unroll 4
+        for (int t = 0; t < T; t++) {
+          const float4 ev = *reinterpret_cast<const float4 *>(St + t * kAttSP + oq);
+          const float2 p01 = __fmul2_rn(make_float2(ev.x, ev.y), i01), p23 = __fmul2_rn(make_float2(ev.z, ev.w), i23);
+          const float4 pv = make_float4(p01.x, p01.y, p23.x, p23.y);
+          const float2 vv = *reinterpret_cast<const float2 *>(Vs + t * kAttD + od);
+          o[0] = __ffma2_rn(make_float2(pv.x, pv.x), vv, o[0]);
+          o[1] = __ffma2_rn(make_float2(pv.y, pv.y), vv, o[1]);
+          o[2] = __ffma2_rn(make_float2(pv.z, pv.z), vv, o[2]);
+          o[3] = __ffma2_rn(make_float2(pv.w, pv.w), vv, o[3]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int q = q0 + oq + i;
+          if (q < T) *reinterpret_cast<float2 *>(ctx + (row0 + q) * H + h * kAttD + od) = o[i];
+        }
+      }
+      if (b + 2 < nb) named_barrier_arrive(kBarEmpty + buf, kAttThreads);  // the producer may refill it
+    }
   }
 }
 
@@ -357,7 +390,7 @@ int launch_attn_f32(const float *qkv, int nimg, int T, int H, int nh, float scal
       return IG_ERR_CUDA;
     attr = true;
   }
-  attn_f32_kernel<<<nimg * nh, 256, AttF32Smem::kTotal, st>>>(qkv, T, H, nh, scale, ctx);
+  attn_f32_kernel<<<nimg * nh, kAttThreads, AttF32Smem::kTotal, st>>>(qkv, T, H, nh, scale, ctx);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 
@@ -517,29 +550,49 @@ __global__ void outlier_gather_kernel(float *__restrict__ x, int M, int T, int K
   }
 }
 
+// The dequantized weight rows of each image's outlier channels:
+// w[img][k][col] = float(q[col][j_k]) * scale[col] (MatMul8Outliers' w).
+__global__ void __launch_bounds__(256) outlier_weights_kernel(const int32_t *__restrict__ out,
+                                                              const int32_t *__restrict__ nout, int N,
+                                                              const int8_t *__restrict__ q, int ldq,
+                                                              const float *__restrict__ scale, float *__restrict__ w) {
+  const int img = blockIdx.y, k = blockIdx.z;
+  if (k >= __ldg(nout + img)) return;
+  const int jk = __ldg(out + img * 32 + k);
+  for (int col = blockIdx.x * 256 + threadIdx.x; col < N; col += gridDim.x * 256)
+    w[((size_t)img * 32 + k) * N + col] = __fmul_rn((float)__ldg(q + (size_t)col * ldq + jk), __ldg(scale + col));
+}
+
 // x[row][col] += ((c + sum_k outv[k] * w_k[col]) + bias[col]), c the int8
-// product, the outlier terms added in order, w_k = float(q[col][j_k]) * scale.
-__global__ void __launch_bounds__(128) outlier_fixup_kernel(const float *__restrict__ c, int T, int N,
-                                                            const int32_t *__restrict__ out,
+// product, the outlier terms added in order. One thread per (row, 4 columns).
+__global__ void __launch_bounds__(256) outlier_fixup_kernel(const float *__restrict__ c, int M, int T, int N,
                                                             const int32_t *__restrict__ nout,
-                                                            const float *__restrict__ outv, const int8_t *__restrict__ q,
-                                                            int ldq, const float *__restrict__ scale,
+                                                            const float *__restrict__ outv,
+                                                            const float *__restrict__ w,
                                                             const float *__restrict__ bias, float *__restrict__ x) {
-  __shared__ float w[32][128];
-  const int img = blockIdx.y, col = blockIdx.x * 128 + threadIdx.x;
-  const int n = nout[img];
-  const bool ok = col < N;
-  for (int k = 0; k < n; k++)
-    w[k][threadIdx.x] = ok ? __fmul_rn((float)q[(size_t)col * ldq + out[img * 32 + k]], __ldg(scale + col)) : 0.0f;
-  if (!ok) return;
-  const float b = __ldg(bias + col);
-  for (int t = 0; t < T; t++) {
-    const size_t row = (size_t)img * T + t;
-    float v = c[row * N + col];
-    for (int k = 0; k < n; k++) v = __fadd_rn(v, __fmul_rn(__ldg(outv + row * 32 + k), w[k][threadIdx.x]));
-    v = __fadd_rn(v, b);
-    x[row * N + col] = __fadd_rn(x[row * N + col], v);
+  const int n4 = N >> 2;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)M * n4) return;
+  const int row = (int)(idx / n4), col = (int)(idx % n4) * 4;
+  const int img = row / T, cnt = __ldg(nout + img);
+  const size_t e = (size_t)row * N + col;
+  const float4 cv = __ldg(reinterpret_cast<const float4 *>(c + e));
+  float v[4] = {cv.x, cv.y, cv.z, cv.w};
+  for (int k = 0; k < cnt; k++) {
+    const float xv = __ldg(outv + (size_t)row * 32 + k);
+    const float4 wk = __ldg(reinterpret_cast<const float4 *>(w + ((size_t)img * 32 + k) * N + col));
+    v[0] = __fadd_rn(v[0], __fmul_rn(xv, wk.x));
+    v[1] = __fadd_rn(v[1], __fmul_rn(xv, wk.y));
+    v[2] = __fadd_rn(v[2], __fmul_rn(xv, wk.z));
+    v[3] = __fadd_rn(v[3], __fmul_rn(xv, wk.w));
   }
+  const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + col));
+  float4 xv = *reinterpret_cast<const float4 *>(x + e);
+  xv.x = __fadd_rn(xv.x, __fadd_rn(v[0], b.x));
+  xv.y = __fadd_rn(xv.y, __fadd_rn(v[1], b.y));
+  xv.z = __fadd_rn(xv.z, __fadd_rn(v[2], b.z));
+  xv.w = __fadd_rn(xv.w, __fadd_rn(v[3], b.w));
+  *reinterpret_cast<float4 *>(x + e) = xv;
 }
 
 int launch_outliers_select(const float *x, int nimg, int T, int K, float ratio, float *colmax, int32_t *cand,
@@ -553,10 +606,16 @@ int launch_outliers_select(const float *x, int nimg, int T, int K, float ratio, 
 }
 
 int launch_outliers_fixup(const float *c, int nimg, int T, int N, const int32_t *out, const int32_t *nout,
-                          const float *outv, const int8_t *q, int ldq, const float *scale, const float *bias, float *x,
-                          cudaStream_t st) {
+                          const float *outv, const int8_t *q, int ldq, const float *scale, const float *bias, float *w,
+                          float *x, cudaStream_t st) {
   if (nimg <= 0) return 0;
-  outlier_fixup_kernel<<<dim3((N + 127) / 128, nimg), 128, 0, st>>>(c, T, N, out, nout, outv, q, ldq, scale, bias, x);
+  if (N % 4 || ((reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(bias) |
+                 reinterpret_cast<uintptr_t>(w)) & 15))
+    return IG_ERR_BAD_ARG;  // (c may be null: then only the weight rows)
+  outlier_weights_kernel<<<dim3((N + 255) / 256, nimg, 32), 256, 0, st>>>(out, nout, N, q, ldq, scale, w);
+  if (!c) return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;  // the GEMM epilogue adds them
+  const long long total = (long long)nimg * T * (N / 4);
+  outlier_fixup_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(c, nimg * T, T, N, nout, outv, w, bias, x);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 

@@ -39,7 +39,7 @@ struct VisWork {
   std::vector<void *> allocs;
   float *x = nullptr, *qkv = nullptr, *ctx = nullptr, *tmp = nullptr, *mlp = nullptr, *kv = nullptr;
   uint8_t *xq = nullptr;
-  float *sa = nullptr, *colmax = nullptr, *outv = nullptr;
+  float *sa = nullptr, *colmax = nullptr, *outv = nullptr, *outw = nullptr;
   int32_t *cand = nullptr, *outl = nullptr, *nout = nullptr;
   float *att = nullptr, *hout = nullptr, *hn = nullptr, *hm = nullptr, *pooled = nullptr, *pix = nullptr;
   float *patches = nullptr;  // the patch states Forward returns
@@ -121,6 +121,7 @@ int vis_work(ig_vision *m, int n, VisWork **out) {
     IG_TRY(vis_alloc(L, &w->outl, (size_t)n * 32));
     IG_TRY(vis_alloc(L, &w->nout, (size_t)n));
     IG_TRY(vis_alloc(L, &w->outv, N * 32));
+    IG_TRY(vis_alloc(L, &w->outw, (size_t)n * 32 * H));
     IG_TRY(vis_alloc(L, &w->att, (size_t)n * H));
     IG_TRY(vis_alloc(L, &w->hout, (size_t)n * H));
     IG_TRY(vis_alloc(L, &w->hn, (size_t)n * H));
@@ -231,16 +232,18 @@ int vis_run(ig_vision *m, VisWork &w, const float *d_pix, int n, int layer, bool
       IG_TRY(copy_rows_d2h(dump->mq_s, w.sa, 4, 4, N, st));
     }
     {
-      GemmArgs g{w.xq, Y.fc2.q, (int)N, Y.fc2.n, M, m->ldk, Y.fc2.ld, 0};
-      GemmEpilogue e{};
-      e.sa = w.sa, e.sb = Y.fc2.scale, e.zc = Y.fc2.zc, e.C = w.tmp, e.ldc = H;
-      ProfScope ps("vis_gemm_fc2", vis_gemm_bytes(N, H, M, 4.0 * H), 2.0 * N * H * M, 1, st);
-      IG_TRY(gemm_u8s8(g, e, kEpiF32, st));
+      ProfScope ps("vis_outlier_weights", (double)n * 32 * H * 5, 0, 1, st);
+      IG_TRY(launch_outliers_fixup(nullptr, n, T, H, w.outl, w.nout, w.outv, Y.fc2.q, Y.fc2.ld, Y.fc2.scale, Y.b2,
+                                   w.outw, w.x, st));
     }
     {
-      ProfScope ps("vis_fc2_fixup", N * 12.0 * H, 0, 1, st);
-      IG_TRY(launch_outliers_fixup(w.tmp, n, T, H, w.outl, w.nout, w.outv, Y.fc2.q, Y.fc2.ld, Y.fc2.scale, Y.b2, w.x,
-                                   st));
+      // fc2: the int8 product of the rest, the outlier terms, the bias, added to x.
+      GemmArgs g{w.xq, Y.fc2.q, (int)N, Y.fc2.n, M, m->ldk, Y.fc2.ld, 0};
+      GemmEpilogue e{};
+      e.sa = w.sa, e.sb = Y.fc2.scale, e.zc = Y.fc2.zc, e.bias = Y.b2, e.C = w.x, e.ldc = H, e.accumulate = 1;
+      e.seg_rows = T, e.nout = w.nout, e.outv = w.outv, e.outw = w.outw;
+      ProfScope ps("vis_gemm_fc2_residual", vis_gemm_bytes(N, H, M, 8.0 * H + 16.0), 2.0 * N * H * M, 1, st);
+      IG_TRY(gemm_u8s8(g, e, kEpiOutlierRes, st));
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->x_mlp, w.x, H * 4, H * 4, N, st));
     if (l + 1 == layer && d_patches)
