@@ -282,6 +282,24 @@ IG_API int ig_answer_spans(const double *z, int32_t ntok, int32_t ldz, int32_t n
                            const char *text, int64_t text_len, const int32_t *offsets, ig_span *out, int32_t cap,
                            int32_t *nspans);
 
+/* The tags ig_answer_spans decodes, for many texts at once on the device
+ * (the log-softmax and the Viterbi pass; one warp per text): d_z device
+ * logits [offs[ntexts]][ldz] (the first ntags used), texts at host offsets
+ * offs[ntexts+1], d_tags [offs[ntexts]] (device). At most 32 tags
+ * (IG_ERR_UNSUPPORTED beyond). exp and log are the device's double-precision
+ * functions: scores tied to the last bit may decide differently from the
+ * host's. Enqueued on `stream`. */
+IG_API int ig_spans_tags_device(const double *d_z, int64_t ldz, const int64_t *offs, int32_t ntexts, int32_t ntags,
+                                double temperature, double bias, int32_t *d_tags, void *stream);
+/* ig_spans_tags_device on host buffers, on `device` (synchronous). */
+IG_API int ig_spans_tags(const double *z, int64_t ldz, const int64_t *offs, int32_t ntexts, int32_t ntags,
+                         double temperature, double bias, int32_t *tags, int32_t device);
+/* The passages of one text's tag sequence (decodeSpans' extraction,
+ * spans.go:222-245), confidences from the tempered log-softmax of z. */
+IG_API int ig_spans_from_tags(const double *z, int32_t ntok, int32_t ldz, int32_t ntags, double temperature,
+                              const int32_t *tags, const char *text, int64_t text_len, const int32_t *offsets,
+                              ig_span *out, int32_t cap, int32_t *nspans);
+
 /* ig_logits with every sequence pooled by the mean of its rows whatever the
  * config's pooling (meanRows, spans.go:464-477): the pooled heads of a
  * model with Spans questions read that mean. */

@@ -29,7 +29,8 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_plan_windows", "ig_log_softmax", "ig_decode_spans", "ig_answer_spans", "ig_window_logits",
            "ig_infer_windows", "ig_model_head_rows", "ig_vision_create", "ig_vision_destroy", "ig_vision_forward",
            "ig_vision_forward_device", "ig_vision_dump_layer", "ig_model_dims", "ig_batcher_create",
-           "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats"]
+           "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats",
+           "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -150,6 +151,10 @@ def load() -> C.CDLL:
     L.ig_vision_forward_device.argtypes = [vp, vp, i32, i32, vp, vp, vp]
     L.ig_vision_dump_layer.argtypes = [vp, vp, i32, C.POINTER(IgVisionDump), vp, C.c_size_t]
     L.ig_model_dims.argtypes = [vp, i32p, i32p]
+    L.ig_spans_tags_device.argtypes = [vp, C.c_int64, vp, i32, i32, f64, f64, vp, vp]
+    L.ig_spans_tags.argtypes = [vp, C.c_int64, vp, i32, i32, f64, f64, vp, i32]
+    L.ig_spans_from_tags.argtypes = [vp, i32, i32, i32, f64, vp, C.c_char_p, C.c_int64, vp, C.POINTER(IgSpan), i32,
+                                     i32p]
     L.ig_batcher_create.argtypes = [C.POINTER(C.c_void_p), i32, i32, i32, i32, C.POINTER(C.c_void_p)]
     L.ig_batcher_create_fn.argtypes = [BATCH_ENCODE_FN, C.POINTER(C.c_void_p), i32, i32, i32, i32, i32,
                                        C.POINTER(C.c_void_p)]

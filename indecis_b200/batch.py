@@ -41,7 +41,7 @@ class Batcher:
             models = list(models)
             arr = (C.c_void_p * len(models))(*[m._h for m in models])
             rc = L.ig_batcher_create(arr, len(models), workers, max_rows, max_wait_us, C.byref(h))
-            self.hidden = models[0].cfg.hidden_size
+            self.hidden = models[0].Cfg.hidden_size
             self._models = models  # kept alive while the workers use them
         _capi.check(rc)
         self._h = h.value

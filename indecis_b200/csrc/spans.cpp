@@ -3,8 +3,9 @@
 // Spans head, and the most probable consistent tag sequence gives the
 // passages. Host code: the windows are planned here, framed and sent to the
 // device in batches (ig_window_logits: encoder and per-token heads on the
-// GPU), and the decoding runs on the host, where a long text's Viterbi pass
-// is a few microseconds per token and sequential in tokens.
+// GPU), and the decoding runs on the host (0.25 us per token); the tags of
+// many texts at once can also come from the device (spans_device.cu), the
+// passages then being extracted here (ig_spans_from_tags).
 #include <stdint.h>
 
 #include <algorithm>
@@ -241,6 +242,13 @@ void viterbi(const double *logp, int n, int C, double bias, int32_t *tags) {
   for (int t = n - 1; t > 0; t--) tags[t - 1] = back[(size_t)t * C + tags[t]];
 }
 
+// The passages of a tag sequence (decodeSpans, spans.go:222-245): each
+// starts at a beginning (or a stray inside) tag, from its token's core to
+// the end of the last inside tag that follows, trimmed of edge punctuation;
+// its confidence is the mean of exp(logp) of its tags.
+int extract(const double *logp, int32_t ntok, int32_t ntags, const int32_t *tags, const char *text, int64_t text_len,
+            const int32_t *offsets, ig_span *out, int32_t cap, int32_t *nspans);
+
 int decode(const double *logp, int32_t ntok, int32_t ntags, double bias, const char *text, int64_t text_len,
            const int32_t *offsets, int32_t *tags_out, ig_span *out, int32_t cap, int32_t *nspans) {
   if (ntok < 0 || ntags < 1 || ntags > 32767 || !nspans || text_len < 0 ||
@@ -251,6 +259,12 @@ int decode(const double *logp, int32_t ntok, int32_t ntags, double bias, const c
   std::vector<int32_t> tags(ntok);
   viterbi(logp, ntok, ntags, bias, tags.data());
   if (tags_out) std::copy(tags.begin(), tags.end(), tags_out);
+  return extract(logp, ntok, ntags, tags.data(), text, text_len, offsets, out, cap, nspans);
+}
+
+int extract(const double *logp, int32_t ntok, int32_t ntags, const int32_t *tags, const char *text, int64_t text_len,
+            const int32_t *offsets, ig_span *out, int32_t cap, int32_t *nspans) {
+  *nspans = 0;
   const unsigned char *tb = reinterpret_cast<const unsigned char *>(text);
   auto bad_offset = [&](int t) {
     return report_error(IG_ERR_BAD_ARG, "indecis: token " + std::to_string(t) + " [" + std::to_string(offsets[2 * t]) +
@@ -333,6 +347,22 @@ int ig_answer_spans(const double *z, int32_t ntok, int32_t ldz, int32_t ntags, d
   std::vector<double> logp((size_t)ntok * ntags);
   for (int t = 0; t < ntok; t++) log_softmax(z + (size_t)t * ldz, ntags, temperature, logp.data() + (size_t)t * ntags);
   return decode(logp.data(), ntok, ntags, bias, text, text_len, offsets, nullptr, out, cap, nspans);
+}
+
+int ig_spans_from_tags(const double *z, int32_t ntok, int32_t ldz, int32_t ntags, double temperature,
+                       const int32_t *tags, const char *text, int64_t text_len, const int32_t *offsets, ig_span *out,
+                       int32_t cap, int32_t *nspans) {
+  ig::clear_error();
+  if (ntok < 0 || ntags < 1 || ldz < ntags || !nspans || text_len < 0 ||
+      (ntok > 0 && (!z || !tags || !offsets || (text_len > 0 && !text))) || (cap > 0 && !out))
+    return report_error(IG_ERR_BAD_ARG, "indecis: bad span arguments");
+  *nspans = 0;
+  if (ntok == 0) return 0;
+  for (int t = 0; t < ntok; t++)
+    if (tags[t] < 0 || tags[t] >= ntags) return report_error(IG_ERR_BAD_ARG, "indecis: tag out of range");
+  std::vector<double> logp((size_t)ntok * ntags);
+  for (int t = 0; t < ntok; t++) log_softmax(z + (size_t)t * ldz, ntags, temperature, logp.data() + (size_t)t * ntags);
+  return extract(logp.data(), ntok, ntags, tags, text, text_len, offsets, out, cap, nspans);
 }
 
 int ig_infer_windows(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ninputs, const int32_t *prefix,

@@ -158,3 +158,34 @@ def infer_windows(model, texts, prefix, suffix, max_len: int, batch_size: int = 
                 po += h.rows
         out.append(inf)
     return out
+
+
+def spans_tags(zs, temperature: float = 1.0, bias: float = 0.0, device: int = 0):
+    """The tags of answer_spans for many texts at once, decoded on the device
+    (ig_spans_tags: log-softmax and Viterbi, one warp per text). zs: per text
+    its logits [tokens][tags]. Returns one int32 array of tags per text."""
+    zs = [np.ascontiguousarray(z, np.float64) for z in zs]
+    ntags = next((z.shape[1] for z in zs if z.ndim == 2 and z.shape[0]), 1)
+    offs = np.zeros(len(zs) + 1, np.int64)
+    offs[1:] = np.cumsum([z.shape[0] if z.ndim == 2 else 0 for z in zs])
+    flat = np.concatenate([z.reshape(-1, ntags) for z in zs]) if offs[-1] else np.zeros((0, ntags))
+    flat = np.ascontiguousarray(flat, np.float64)
+    tags = np.zeros(int(offs[-1]), np.int32)
+    _capi.check(_capi.load().ig_spans_tags(flat.ctypes.data, ntags, offs.ctypes.data, len(zs), ntags,
+                                           float(temperature), float(bias), tags.ctypes.data, device))
+    return [tags[offs[i]:offs[i + 1]] for i in range(len(zs))]
+
+
+def spans_from_tags(options, text, offsets, z, tags, temperature: float = 1.0) -> list[Span]:
+    """decodeSpans' passage extraction for a given tag sequence (ig_spans_from_tags)."""
+    z = np.ascontiguousarray(z, np.float64)
+    ntok = z.shape[0] if z.ndim == 2 else 0
+    ntags = z.shape[1] if ntok else span_tag_count(len(options))
+    o = _offsets(offsets, ntok)
+    t = np.ascontiguousarray(tags, np.int32)
+    tb = _text_bytes(text)
+    found = (_capi.IgSpan * max(ntok, 1))()
+    n = C.c_int32()
+    _capi.check(_capi.load().ig_spans_from_tags(z.ctypes.data, ntok, ntags, ntags, float(temperature), t.ctypes.data,
+                                                tb, len(tb), o.ctypes.data, found, ntok, C.byref(n)))
+    return _spans(options, tb, found, n.value)

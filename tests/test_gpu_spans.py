@@ -91,3 +91,31 @@ def test_infer_windows_errors(igdev):
     with pytest.raises(_capi.IgError):
         SP.infer_windows(gm, [[1, 2]], [2], [1], 0)
     assert SP.infer_windows(gm, [], [2], [1], 40) == []
+
+
+def test_device_viterbi_matches_host(igdev):
+    """The tags decoded on the device (ig_spans_tags: one warp per text) equal
+    the host's Viterbi pass, and the passages extracted from them equal
+    answer_spans, over many texts at once (real tokenizations, random logits,
+    temperatures and a bias)."""
+    from indecis_b200 import spans as SP
+    recs = [json.loads(line) for line in open(GOLDEN, encoding="utf-8")]
+    rng = np.random.default_rng(31)
+    opts = ["PER", "LOC", "ORG", "MISC"]
+    zs = [rng.standard_normal((len(r["ids"]), 9)) * 3 for r in recs]
+    zs += [rng.standard_normal((n, 9)) * 3 for n in (1, 2, 500, 0)]
+    for T, bias in ((1.0, 0.0), (0.3, 0.7), (2.0, -0.4)):
+        dev = SP.spans_tags(zs, T, bias)
+        for z, tags in zip(zs, dev):
+            n = z.shape[0]
+            if n == 0:
+                assert len(tags) == 0
+                continue
+            logp = np.stack([SP.log_softmax(z[t], T) for t in range(n)])
+            text = "x" * n
+            offs = [[i, i + 1] for i in range(n)]
+            _, host = SP.decode_spans(opts, text, offs, logp, bias, with_tags=True)
+            assert np.array_equal(tags, host)
+        for r, z, tags in zip(recs, zs, dev):
+            assert SP.spans_from_tags(opts, r["text"], r["offsets"], z, tags, T) == \
+                SP.answer_spans(opts, r["text"], r["offsets"], z, T, bias)
