@@ -324,6 +324,15 @@ IG_API int ig_infer_windows(ig_model *m, const int32_t *ids, const int64_t *offs
  * *token_rows receive the sums over pooled and per-token heads. */
 IG_API int ig_model_head_rows(ig_model *m, int32_t *pooled_rows, int32_t *token_rows);
 
+/* SetInt8 (infer.go:115-135): on != 0 (the state after ig_model_create)
+ * computes the layers in int8; 0 switches the model to the reference's
+ * float32 path (float products in its FMA-chain order, RoPE in place,
+ * attendBlocks' blocked softmax, the erf GELU x gate: infer.go:304-430,
+ * :590-650), from float32 copies of the weights kept at creation. Must not
+ * run concurrently with an encode on the same model. The per-layer dump
+ * (ig_encode_dump) is of the int8 path only. */
+IG_API int ig_model_set_int8(ig_model *m, int32_t on);
+
 /* Vocabulary size and hidden width of a model. */
 IG_API int ig_model_dims(ig_model *m, int32_t *vocab, int32_t *hidden);
 

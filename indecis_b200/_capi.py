@@ -30,7 +30,7 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_infer_windows", "ig_model_head_rows", "ig_vision_create", "ig_vision_destroy", "ig_vision_forward",
            "ig_vision_forward_device", "ig_vision_dump_layer", "ig_model_dims", "ig_batcher_create",
            "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats",
-           "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags"]
+           "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags", "ig_model_set_int8"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -151,6 +151,7 @@ def load() -> C.CDLL:
     L.ig_vision_forward_device.argtypes = [vp, vp, i32, i32, vp, vp, vp]
     L.ig_vision_dump_layer.argtypes = [vp, vp, i32, C.POINTER(IgVisionDump), vp, C.c_size_t]
     L.ig_model_dims.argtypes = [vp, i32p, i32p]
+    L.ig_model_set_int8.argtypes = [vp, i32]
     L.ig_spans_tags_device.argtypes = [vp, C.c_int64, vp, i32, i32, f64, f64, vp, vp]
     L.ig_spans_tags.argtypes = [vp, C.c_int64, vp, i32, i32, f64, f64, vp, i32]
     L.ig_spans_from_tags.argtypes = [vp, i32, i32, i32, f64, vp, C.c_char_p, C.c_int64, vp, C.POINTER(IgSpan), i32,

@@ -124,6 +124,8 @@ struct DevMat {
 struct DevLayer {
   DevMat qkv, o, wi, wom;
   float *attn_norm = nullptr, *mlp_norm = nullptr;
+  // float32 weights [out][in] for the path without SetInt8
+  float *fqkv = nullptr, *fo = nullptr, *fwi = nullptr, *fwom = nullptr;
 };
 
 struct DevHead {
@@ -140,8 +142,9 @@ struct Plan {
   std::vector<int32_t> offs, row_seq, pos;
   std::vector<int4> tc[2];
   std::vector<int2> v1[2];
+  std::vector<int2> fb;  // float path: (sequence, first query) of each block of 64 queries
   size_t block_bytes() const {
-    return 16 * (tc[0].size() + tc[1].size()) + 8 * (v1[0].size() + v1[1].size());
+    return 16 * (tc[0].size() + tc[1].size()) + 8 * (v1[0].size() + v1[1].size() + fb.size());
   }
 };
 
@@ -150,12 +153,16 @@ struct PlanDev {
   const int4 *tc[2] = {nullptr, nullptr};
   const int2 *v1[2] = {nullptr, nullptr};
   int ntc[2] = {0, 0}, nv1[2] = {0, 0};
+  const int2 *fb = nullptr;
+  int nfb = 0;
 };
 
 // Device buffers of one encode call, sized for `rows` rows and `nseq` sequences.
 struct Workspace {
   int device = 0;
   size_t rows_cap = 0, seq_cap = 0, blk_cap = 0, tl_cap = 0, pl_cap = 0;
+  bool f32_cap = false;  // holds the float path's MLP buffer
+  float *zf = nullptr;   // float path: [rows][2I] Wi output
   void *dev = nullptr;
   void *host = nullptr;  // pinned staging
   size_t host_bytes = 0;
@@ -188,6 +195,7 @@ struct ig_model {
   std::vector<void *> emb_allocs;  // the table's device arrays (replaced by ig_model_set_embeddings)
   float *emb_norm = nullptr, *final_norm = nullptr;
   std::vector<DevLayer> layers;
+  bool f32 = false;  // SetInt8(false): the float32 path
   std::mutex mu;  // rope tables, heads, workspace pool
   int rope_npos = 0;
   float *rope_cos[2] = {nullptr, nullptr}, *rope_sin[2] = {nullptr, nullptr};
@@ -312,6 +320,7 @@ int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2]) {
     p.tc[k].clear();
     p.v1[k].clear();
   }
+  p.fb.clear();
   p.max_len = 0;
   const int qb = attn_query_block();
   for (int s = 0; s < nseq; s++) {
@@ -323,6 +332,7 @@ int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2]) {
       p.row_seq[offs[s] + t] = s;
       p.pos[offs[s] + t] = t;
     }
+    for (int i0 = 0; i0 < n; i0 += 64) p.fb.push_back(make_int2(s, i0));
     for (int k = 0; k < 2; k++) {
       if (windows[k] < -1) continue;
       for (int i0 = 0; i0 < n; i0 += attn_tc_query_block()) {
@@ -352,7 +362,7 @@ struct Carve {
 };
 
 void carve_ws(Workspace &w, const ig_model *m, char *base, size_t rows, size_t seqs, size_t blks, size_t tl,
-              size_t pl, size_t *total) {
+              size_t pl, bool f32, size_t *total) {
   Carve c{base};
   const size_t H = m->H, I = m->I, nh = m->nh, D = m->D;
   w.ids = c.take<int32_t>(rows);
@@ -379,6 +389,7 @@ void carve_ws(Workspace &w, const ig_model *m, char *base, size_t rows, size_t s
   w.pooled = c.take<float>(seqs * H);
   w.logits = c.take<double>(seqs * pl);
   w.tlogits = c.take<double>(rows * tl);
+  w.zf = f32 ? c.take<float>(rows * 2 * I) : nullptr;
   *total = c.off;
 }
 
@@ -400,7 +411,9 @@ int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st
   }
   const size_t rows = std::max<size_t>(p.N, 1), seqs = std::max<size_t>(p.nseq, 1),
                blks = std::max<size_t>(p.block_bytes(), 16);
-  if (rows > w->rows_cap || seqs > w->seq_cap || blks > w->blk_cap || tl > w->tl_cap || pl > w->pl_cap) {
+  const bool f32 = m->f32 || w->f32_cap;
+  if (rows > w->rows_cap || seqs > w->seq_cap || blks > w->blk_cap || tl > w->tl_cap || pl > w->pl_cap ||
+      f32 != w->f32_cap) {
     if (capturing) return fail(IG_ERR_BAD_ARG, "workspace must be sized before stream capture");
     IG_CU(cudaEventSynchronize(w->done));
     if (w->dev) IG_CU(cudaFree(w->dev));
@@ -408,9 +421,10 @@ int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st
     const size_t r2 = std::max(rows, w->rows_cap), s2 = std::max(seqs, w->seq_cap), b2 = std::max(blks, w->blk_cap);
     const size_t t2 = std::max(tl, w->tl_cap), p2 = std::max(pl, w->pl_cap);
     size_t total = 0;
-    carve_ws(*w, m, nullptr, r2, s2, b2, t2, p2, &total);
+    carve_ws(*w, m, nullptr, r2, s2, b2, t2, p2, f32, &total);
     IG_CU(cudaMalloc(&w->dev, total));
-    carve_ws(*w, m, reinterpret_cast<char *>(w->dev), r2, s2, b2, t2, p2, &total);
+    carve_ws(*w, m, reinterpret_cast<char *>(w->dev), r2, s2, b2, t2, p2, f32, &total);
+    w->f32_cap = f32;
     w->rows_cap = r2;
     w->seq_cap = s2;
     w->blk_cap = b2;
@@ -454,6 +468,7 @@ int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream
   put(p.pos.data(), sizeof(int32_t) * p.N);
   for (int k = 0; k < 2; k++) put(p.tc[k].data(), 16 * p.tc[k].size());
   for (int k = 0; k < 2; k++) put(p.v1[k].data(), 8 * p.v1[k].size());
+  put(p.fb.data(), 8 * p.fb.size());
   if (host_ids) put(host_ids, sizeof(int32_t) * p.N);
   // The device buffers are carved separately: issue one copy per region
   // from the pinned staging (small, contiguous on the host).
@@ -480,6 +495,8 @@ int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream
     w.pd.nv1[k] = (int)p.v1[k].size();
     bo += 8 * p.v1[k].size();
   }
+  w.pd.fb = reinterpret_cast<const int2 *>(w.blocks + bo);
+  w.pd.nfb = (int)p.fb.size();
   if (host_ids && p.N) IG_CU(cudaMemcpyAsync(w.ids, h + o, sizeof(int32_t) * p.N, cudaMemcpyHostToDevice, st));
   return 0;
 }
@@ -512,12 +529,82 @@ double attn_pairs(const Plan &p, int window) {
   return pairs;
 }
 
+// The float32 path (run without SetInt8, infer.go:304-430): float products
+// in the reference's chain order, RoPE in place, attendBlocks, GeluMul.
+int run_encoder_f32(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, int mode, cudaStream_t st,
+                    bool capturing) {
+  const ig_config &c = m->cfg;
+  const int H = m->H, I = m->I, N = p.N, V = c.simd_lanes;
+  if (!w.zf) return fail(IG_ERR_BAD_ARG, "workspace without the float buffers");
+  {
+    ProfScope ps("f32_embed_ln", (double)N * (8 + 8.0 * H) + 4.0 * H, 0, 1, st, capturing);
+    if (m->emb.fmt < 0) return fail(IG_ERR_BAD_ARG, "modernbert: no embedding table");
+    IG_TRY(launch_embed_checked(d_ids, c.vocab, m->emb, m->emb_norm, N, H, c.norm_eps, V, w.x, nullptr, 0, nullptr,
+                                st));
+  }
+  const float scale = (float)(1.0 / std::sqrt((double)m->D));
+  auto product = [&](const char *name, const float *A, int K, const float *W, int Nout, float *C, bool acc) {
+    F32Gemm g{};
+    g.A = A, g.lda = K, g.W = W, g.ldw = K, g.M = N, g.N = Nout, g.K = K, g.C = C, g.ldc = Nout, g.accumulate = acc;
+    g.V = V;
+    ProfScope ps(name, 4.0 * N * K + 4.0 * Nout * K + (acc ? 8.0 : 4.0) * N * Nout, 2.0 * N * Nout * K, 1, st,
+                 capturing);
+    return launch_f32_gemm(g, st);
+  };
+  for (int l = 0; l < c.layers; l++) {
+    const DevLayer &L = m->layers[l];
+    const bool global = l % c.global_every == 0;
+    const float *in = w.x;
+    if (l > 0) {
+      ProfScope ps("f32_ln", (double)N * 8.0 * H + 4.0 * H, 0, 1, st, capturing);
+      IG_TRY(launch_ln_quant(w.x, L.attn_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
+      in = w.xn;
+    }
+    IG_TRY(product("f32_gemm_qkv", in, H, L.fqkv, 3 * H, w.qkv, false));
+    {
+      ProfScope ps("f32_rope", (double)N * 16.0 * H, 0, 1, st, capturing);
+      IG_TRY(launch_rope_f32(w.qkv, w.pos, N, H, m->nh, m->rope_cos[global ? 0 : 1], m->rope_sin[global ? 0 : 1],
+                             st));
+    }
+    {
+      const int window = global ? -1 : c.local_attention / 2;
+      ProfScope ps("f32_attend_blocks", (double)N * 16.0 * H, 4.0 * attn_pairs(p, window) * m->D * m->nh, 1, st,
+                   capturing);
+      IG_TRY(launch_attend_blocks_f32(w.qkv, w.offs, w.pd.fb, w.pd.nfb, H, m->nh, window, scale, V, w.ctx, st));
+    }
+    IG_TRY(product("f32_gemm_wo", w.ctx, H, L.fo, H, w.x, true));
+    {
+      ProfScope ps("f32_ln", (double)N * 8.0 * H + 4.0 * H, 0, 1, st, capturing);
+      IG_TRY(launch_ln_quant(w.x, L.mlp_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
+    }
+    IG_TRY(product("f32_gemm_wi", w.xn, H, L.fwi, 2 * I, w.zf, false));
+    {
+      ProfScope ps("f32_gelu_mul", (double)N * 12.0 * I, 0, 1, st, capturing);
+      IG_TRY(launch_gelu_mul_rows(w.zf, N, I, w.g, st));
+    }
+    IG_TRY(product("f32_gemm_womlp", w.g, I, L.fwom, H, w.x, true));
+  }
+  {
+    ProfScope ps("ln_final", (double)N * 8.0 * H + 4.0 * H, 0, 1, st, capturing);
+    IG_TRY(launch_ln_quant(w.x, m->final_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
+  }
+  if (mode != IG_MODE_TOKENS) {
+    ProfScope ps("pool", (double)N * 4.0 * H + 4.0 * p.nseq * H, 0, 1, st, capturing);
+    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st));
+  }
+  return 0;
+}
+
 int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, int mode, cudaStream_t st,
                 ig_dump *dump, bool capturing = false) {
   const ig_config &c = m->cfg;
   const int H = m->H, I = m->I, N = p.N;
   const int V = c.simd_lanes;
   if (N == 0) return 0;
+  if (m->f32) {
+    if (dump) return fail(IG_ERR_UNSUPPORTED, "the per-layer dump is of the int8 path");
+    return run_encoder_f32(m, w, d_ids, p, mode, st, capturing);
+  }
   {
     ProfScope ps("embed_ln_quant", (double)N * (8 + 9.0 * H) + 4.0 * H, 0, 1, st, capturing);
     if (m->emb.fmt < 0) return fail(IG_ERR_BAD_ARG, "modernbert: no embedding table");
@@ -832,6 +919,11 @@ int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, i
     if (!rc) rc = pack_matrix(m.get(), L.o, w->wo[l], H, H, {}, tmp, dperm);
     if (!rc) rc = pack_matrix(m.get(), L.wi, w->wi[l], 2 * I, H, wi_perm, tmp, dperm);
     if (!rc) rc = pack_matrix(m.get(), L.wom, w->wo_mlp[l], H, I, {}, tmp, dperm);
+    // float32 copies for SetInt8(false)
+    if (!rc) rc = upload(m.get(), &L.fqkv, w->wqkv[l], (size_t)3 * H * H);
+    if (!rc) rc = upload(m.get(), &L.fo, w->wo[l], (size_t)H * H);
+    if (!rc) rc = upload(m.get(), &L.fwi, w->wi[l], (size_t)2 * I * H);
+    if (!rc) rc = upload(m.get(), &L.fwom, w->wo_mlp[l], (size_t)H * I);
   }
   cudaFree(tmp);
   cudaFree(dperm);
@@ -938,6 +1030,16 @@ int ig_window_logits(ig_model *m, const int32_t *ids, const int64_t *offs, int32
   if (!logits && !token_logits) return fail(IG_ERR_BAD_ARG, "no output");
   return encode_host(m, ids, offs, nseq, kModeMeanRows, nullptr, 0, nullptr, logits, logits_len, token_logits,
                      token_len);
+}
+
+int ig_model_set_int8(ig_model *m, int32_t on) {
+  t_last_error.clear();
+  if (!m) return fail(IG_ERR_BAD_ARG, "null model");
+  if (on == 0 && m->D != 64) return fail(IG_ERR_UNSUPPORTED, "the float path needs a head dimension of 64");
+  if (on == 0 && m->cfg.simd_lanes != 8) return fail(IG_ERR_UNSUPPORTED, "the float path needs simd_lanes 8");
+  std::lock_guard<std::mutex> lk(m->mu);
+  m->f32 = on == 0;
+  return 0;
 }
 
 int ig_model_dims(ig_model *m, int32_t *vocab, int32_t *hidden) {

@@ -155,9 +155,22 @@ struct F32Gemm {
   int ldadd, add_mod;
   float *C;
   int ldc;
+  bool accumulate;     // C += each block's chain (MatMulPackedN with accumulate); no bias/GELU/add then
   bool vec_a, vec_w;   // set by the launcher
 };
 int launch_f32_gemm(const F32Gemm &p, cudaStream_t st);
+
+// ---- the float32 encoder path (encoder_f32.cu) ----
+// Rope (vec_simd.go:408-425) in place on the q and k heads of qkv rows
+// [N][3H], positions pos[N], tables [npos][D/2].
+int launch_rope_f32(float *qkv, const int32_t *pos, int N, int H, int nh, const float *cos_, const float *sin_,
+                    cudaStream_t st);
+// GeluMul (vec_simd.go:121-160) of each row: g[r] = gelu(z[r][:I]) * z[r][I:].
+int launch_gelu_mul_rows(const float *z, int N, int I, float *g, cudaStream_t st);
+// attendBlocks (internal/modernbert/infer.go:590-650) for every (sequence,
+// head, block of 64 queries): tasks [ntasks] = (sequence, first query).
+int launch_attend_blocks_f32(const float *qkv, const int32_t *seq_off, const int2 *tasks, int ntasks, int H, int nh,
+                             int window, float scale, int V, float *ctx, cudaStream_t st);
 // Float attention of the vision layers over the qkv rows [n*T][3H] -> ctx [n*T][H].
 int launch_attn_f32(const float *qkv, int nimg, int T, int H, int nh, float scale, int V, float *ctx,
                     cudaStream_t st);

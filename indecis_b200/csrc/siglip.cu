@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(256, 2) f32_chain_gemm_kernel(const F32Gemm p)
     // first is stored into C and the next ones added to it.
     const int kend = (kt + 1) * kFK;
     if (kend % kKc == 0 && kt + 1 < nk) {
-      const bool first = kend <= kKc;
+      const bool first = kend <= kKc && !p.accumulate;
 #pragma unroll
       for (int i = 0; i < 8; i++) {
         const int r = orow(i);
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(256, 2) f32_chain_gemm_kernel(const F32Gemm p)
     __syncthreads();
   }
   const long long seg_len = (long long)p.gelu_seg_rows * p.N;
-  const bool one_block = p.K <= kKc;
+  const bool one_block = p.K <= kKc && !p.accumulate;
 #pragma unroll
   for (int i = 0; i < 8; i++) {
     const int r = orow(i);
@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(256, 2) f32_chain_gemm_kernel(const F32Gemm p)
 int launch_f32_gemm(const F32Gemm &p0, cudaStream_t st) {
   if (p0.M <= 0 || p0.N <= 0) return 0;
   if (p0.K <= 0 || !p0.W || !p0.C || (!p0.A && !p0.pix)) return IG_ERR_BAD_ARG;
+  if (p0.accumulate && (p0.bias || p0.gelu_seg_rows > 0 || p0.add)) return IG_ERR_BAD_ARG;
   F32Gemm p = p0;
   auto al16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   p.vec_w = al16(p.W) && p.ldw % 4 == 0;

@@ -278,9 +278,10 @@ class Model:
 
     # ---- switches (infer.go:115-135) ----
     def SetInt8(self, on: bool):
-        if not on:
-            raise ModernBertError("modernbert: the device path computes in int8 only (SetInt8(false) is not available)")
-        self._int8 = True
+        """SetInt8 (infer.go:115-135): int8 layers (the default here), or the
+        reference's float32 path on the device."""
+        _capi.check(_capi.load().ig_model_set_int8(self._h, 1 if on else 0))
+        self._int8 = bool(on)
 
     # ---- inference (infer.go:237-299) ----
     def _run(self, seqs, mode):

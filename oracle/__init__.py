@@ -99,6 +99,8 @@ def lib():
     L.or_encode.argtypes = [C.c_void_p, i32p, i64p, C.c_int, C.c_int, f32p, C.c_int, C.c_int, C.c_void_p,
                             C.POINTER(C.c_int32)]
     L.or_head_logits.argtypes = [f32p, f32p, C.c_int, C.c_int, f32p, C.c_int, f64p]
+    L.or_encode_f32.restype = C.c_int
+    L.or_encode_f32.argtypes = [C.c_void_p, i32p, i64p, C.c_int, C.c_int, f32p, C.c_int, C.POINTER(C.c_int32)]
     L.or_cpu_features.restype = C.c_int
     L.or_siglip_create.restype = C.c_void_p
     L.or_siglip_create.argtypes = [C.c_void_p, C.c_void_p]
@@ -264,6 +266,21 @@ class Model:
         if getattr(self, "_h", None):
             lib().or_model_destroy(self._h)
             self._h = None
+
+    def encode_f32(self, ids, offs, mode=0, threads=1):
+        """The float32 path (the reference without SetInt8)."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        offs = np.ascontiguousarray(offs, np.int64)
+        nseq = len(offs) - 1
+        N = int(offs[-1])
+        out = np.zeros((nseq if mode == 0 else N, self.cfg["hidden"]), np.float32)
+        bad = C.c_int32(0)
+        rc = lib().or_encode_f32(self._h, ids, offs, nseq, mode, out, threads, C.byref(bad))
+        if rc == 2:
+            raise ValueError("modernbert: inconsistent batch")
+        if rc != 0:
+            raise ValueError(f"modernbert: id {bad.value} out of vocabulary")
+        return out
 
     def encode(self, ids, offs, mode=0, threads=1, fast=False, dump_layer=None):
         ids = np.ascontiguousarray(ids, np.int32)

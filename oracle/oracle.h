@@ -148,6 +148,12 @@ void or_model_packed(const or_model *m, int l, int which, const int8_t **q, cons
 int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int nseq, int mode, float *out,
               int threads, int fast, or_dump *dump, int32_t *bad_id);
 
+/* The encoder without SetInt8 (float32 products as linalg/gemm.go, RoPE in
+ * place, attendBlocks' blocked softmax, infer.go:304-430, :590-650); same
+ * arguments and return values as or_encode. */
+int or_encode_f32(const or_model *m, const int32_t *ids, const int64_t *offs, int nseq, int mode, float *out,
+                  int threads, int32_t *bad_id);
+
 /* head.logits: z[r] = sum_i double(w[r][i])*double(x[i]) + double(b[r]). */
 void or_head_logits(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z);
 
