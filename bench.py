@@ -31,6 +31,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
 METRIC = "int8 encoder seq/s (128 tok)"
+METRIC_F32 = "float32 encoder seq/s (128 tok)"
+F32_PATH_KERNELS = {"f32_gemm_qkv", "f32_gemm_wo", "f32_gemm_wi", "f32_gemm_womlp", "f32_attend_blocks"}
 SEQ_LEN = 128
 BATCH = 32
 
@@ -45,8 +47,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target length of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c5"],
-                    help="c1: the ModernBERT headline (default); c5: the SigLIP ViT-B/16 vision tower")
+    ap.add_argument("--workload", default="c1", choices=["c1", "c1-f32", "c5"],
+                    help="c1: the ModernBERT headline (default); c1-f32: the same model on the float32 path "
+                         "(SetInt8(false)); c5: the SigLIP ViT-B/16 vision tower")
     ap.add_argument("--images-per-step", type=int, default=512, help="c5: images per step, shared by all ranks")
     return ap.parse_args()
 
@@ -179,6 +182,24 @@ def cpu_baseline(target_s: float):
                       f"tiles, {threads} threads, {t:.1f} s"}
 
 
+def cpu_baseline_f32(target_s: float):
+    """The float32 path of the oracle port on all host threads, a bounded sample."""
+    model, oracle = cpu_model()
+    threads = os.cpu_count() or 1
+    ids, offs = workload(BATCH, 7)
+    t0 = time.perf_counter()
+    model.encode_f32(ids, offs, threads=threads)
+    t1 = time.perf_counter() - t0
+    batches = int(max(1, min(50, target_s / max(t1, 1e-3))))
+    ids, offs = workload(batches * BATCH, 8)
+    t0 = time.perf_counter()
+    model.encode_f32(ids, offs, threads=threads)
+    t = time.perf_counter() - t0
+    return {"value": batches * BATCH / t, "unit": "seq/s", "cores": threads, "kind": "port",
+            "sample": f"{batches} batches of 32x128 (C1) through the oracle's float32 path (scalar FMA chains), "
+                      f"{threads} threads, {t:.1f} s"}
+
+
 def run_reference(args, world, rank):
     """The reference's CPU implementation of the path (the oracle port, since
     the Go reference cannot run on this image), on all host threads."""
@@ -295,6 +316,9 @@ def run_ours(args, world, rank, local):
     model = Model.from_arrays(cfg, S.weights(S.C1, seed=42), device=local)
     heads = [Head(h["name"], h["kind"], h["w"], h["b"]) for h in S.heads(cfg.hidden_size)]
     model.SetHeads(heads)
+    f32 = args.workload == "c1-f32"
+    if f32:
+        model.SetInt8(False)
     L = _capi.load()
 
     nseq = args.seqs_per_step
@@ -369,17 +393,24 @@ def run_ours(args, world, rank, local):
                                                 "device-synchronized calls"}
 
     gemm = None
-    if rank == 0 and not args.no_gemm:
+    if rank == 0 and not args.no_gemm and not f32:
         gemm = [gemm_point(65536, 2304, 768, pk), gemm_point(65536, 768, 256, pk)]
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.cpu_seconds)
+        cpu = cpu_baseline(args.cpu_seconds) if not f32 else cpu_baseline_f32(args.cpu_seconds)
 
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": "seq/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config_obj(args, world),
-                "e2e": e2e, "gpu_launches": report["launches"], "roofline": roofline(report, pk, nseq),
+        cfg_obj = config_obj(args, world)
+        if f32:
+            cfg_obj["path"] = "float32 (SetInt8(false)): float products in the reference's FMA-chain order"
+            rf = c5_roofline(report, pk, clk["sm_mhz"] if clk else None, fp32_names=F32_PATH_KERNELS)
+        else:
+            rf = roofline(report, pk, nseq)
+        line = {"metric": METRIC_F32 if f32 else METRIC, "value": value, "unit": "seq/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32" if f32 else "int8", "data": "synthetic",
+                "config": cfg_obj, "e2e": e2e, "gpu_launches": report["launches"],
+                "roofline": rf[0] if f32 else rf,
                 "kernels": {k["name"]: {"ms": round(k["ms"], 3), "launches": k["launches"]}
                             for k in report["kernels"]},
                 "clocks": clk, "cpu_baseline": cpu, "gemm_sweep": gemm}
@@ -443,7 +474,7 @@ def run_reference_c5(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def c5_roofline(report, pk, sm_mhz):
+def c5_roofline(report, pk, sm_mhz, fp32_names=None):
     ks = [k for k in report["kernels"] if k["records"] > 0 and k["ms"] > 0]
     total = sum(k["ms"] for k in ks)
     fp32_peak = 148 * 128 * 2 * (sm_mhz or 1965.0) * 1e6 / 1e12  # CUDA-core FMA rate at the SM clock
@@ -452,7 +483,7 @@ def c5_roofline(report, pk, sm_mhz):
     for k in sorted(ks, key=lambda k: -k["ms"])[:4]:
         per_ms = k["ms"] / k["records"]
         ops, byts = k["ops"] / k["records"], k["bytes"] / k["records"]
-        if k["name"] in FP32_KERNELS and ops:
+        if k["name"] in (fp32_names or FP32_KERNELS) and ops:
             ach = ops / (per_ms * 1e-3) / 1e12
             r = {"bound": "fp32", "achieved": ach, "peak": fp32_peak, "unit": "TFLOP/s", "frac": ach / fp32_peak,
                  "peak_source": f"148 SMs x 128 FP32 FMA/clk at the sampled {sm_mhz or 1965.0:.0f} MHz (nominal)"}
@@ -578,7 +609,7 @@ def main():
     if args.impl == "reference":
         run_reference(args, world, rank)
         return
-    run_ours(args, world, rank, local)
+    run_ours(args, world, rank, local)  # c1 and c1-f32
 
 
 if __name__ == "__main__":

@@ -61,9 +61,11 @@ constexpr int kAbK = 128;    // kBlock (infer.go:538)
 constexpr int kAbD = 64;     // head dimension
 constexpr int kAbSP = kAbK + 4;  // pitch of a score row (query-major)
 struct AbSmem {
-  static constexpr int kKt = 0;                           // [64][128]   K^T of the key block
-  static constexpr int kV = kKt + kAbD * kAbK * 4;        // [128][64]   V of the key block
-  static constexpr int kQt = kV + kAbK * kAbD * 4;        // [64][64]    scaled Q^T of this query block
+  // K^T [64][128] of the key block, then its V [128][64] in the same place:
+  // V is copied in (cp.async) while the softmax runs, once S is computed.
+  static constexpr int kKt = 0;
+  static constexpr int kV = 0;
+  static constexpr int kQt = kKt + kAbD * kAbK * 4;       // [64][64]    scaled Q^T of this query block
   static constexpr int kS = kQt + kAbD * kAbQ * 4;        // [64][132]   scores / weights, query-major
   static constexpr int kRow = kS + kAbQ * kAbSP * 4;      // mx[64], sum[64], corr[64]
   static constexpr int kTotal = kRow + 3 * kAbQ * 4;
@@ -81,7 +83,7 @@ __device__ __forceinline__ float go_max_f(float a, float b) {
 // before each key block's P V is added (one chain over the block's keys,
 // then added: MatMulPackedN with accumulate). ExpShift runs over each row's
 // window slice of the block, its eight lanes counted from the slice start.
-__global__ void __launch_bounds__(256) attend_blocks_f32_kernel(const float *__restrict__ qkv,
+__global__ void __launch_bounds__(256, 2) attend_blocks_f32_kernel(const float *__restrict__ qkv,
                                                                 const int32_t *__restrict__ seq_off,
                                                                 const int2 *__restrict__ tasks, int H, int nh,
                                                                 int window, float scale, float *__restrict__ ctx) {
@@ -130,12 +132,6 @@ __global__ void __launch_bounds__(256) attend_blocks_f32_kernel(const float *__r
       Kt[(j4 + 2) * kAbK + u] = kv.z;
       Kt[(j4 + 3) * kAbK + u] = kv.w;
     }
-    for (int idx = tid; idx < kAbK * 16; idx += 256) {
-      const int u = idx >> 4, j4 = (idx & 15) * 4;
-      float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (u < cols) vv = __ldg(reinterpret_cast<const float4 *>(qkv + (size_t)(off + jb + u) * ld + 2 * H + h * kAbD + j4));
-      *reinterpret_cast<float4 *>(Vs + u * kAbD + j4) = vv;
-    }
     __syncthreads();
     // S = (scaled Q) K^T: warp w takes queries 8w.., lane the keys lane + 32m.
     {
@@ -162,6 +158,12 @@ __global__ void __launch_bounds__(256) attend_blocks_f32_kernel(const float *__r
         for (int m = 0; m < 4; m++) S[(warp * 8 + i) * kAbSP + lane + 32 * m] = acc[i][m];
     }
     __syncthreads();
+    // K^T is consumed: V of the block comes into its place during the softmax
+    // (the rows past the block's keys are never read).
+    for (int idx = tid; idx < cols * 16; idx += 256) {
+      const int u = idx >> 4, j4 = (idx & 15) * 4;
+      cp_async16(Vs + u * kAbD + j4, qkv + (size_t)(off + jb + u) * ld + 2 * H + h * kAbD + j4);
+    }
     // The softmax update of each row: four threads per row, thread p running
     // ExpShift's lanes 2p and 2p + 1 over the row's window slice.
     {
@@ -220,6 +222,7 @@ __global__ void __launch_bounds__(256) attend_blocks_f32_kernel(const float *__r
         for (int u = part; u < cols; u += 4)
           if (!live || u < cs || u >= ce) sr[u] = 0.0f;
     }
+    cp_async_wait_all();
     __syncthreads();
     // o = o * corr, then o += (one chain over the block's keys).
     if (qo < rows) {
