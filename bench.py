@@ -64,6 +64,9 @@ def peaks():
 
 
 def dist_setup():
+    # Rank 0's stdout carries one JSON line: keep NCCL's version banner (printed
+    # to stdout at NCCL_DEBUG=VERSION or above) off it.
+    os.environ["NCCL_DEBUG"] = os.environ.get("IG_BENCH_NCCL_DEBUG", "WARN")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
