@@ -63,14 +63,26 @@ def peaks():
         return dict(hbm=6650.0, bf16=1590.0, src="fallback")
 
 
+_JSON_FD = 1  # where the result line goes
+
+
 def dist_setup():
-    # Rank 0's stdout carries one JSON line: keep NCCL's version banner (printed
-    # to stdout at NCCL_DEBUG=VERSION or above) off it.
-    os.environ["NCCL_DEBUG"] = os.environ.get("IG_BENCH_NCCL_DEBUG", "WARN")
+    global _JSON_FD
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        # Rank 0's stdout carries one JSON line: libraries that print to fd 1
+        # (NCCL's version banner at communicator creation) go to stderr.
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
     return world, rank, local
+
+
+def emit(line: dict):
+    """The result line, on the process's original stdout."""
+    os.write(_JSON_FD, (json.dumps(line) + "\n").encode())
 
 
 class Clocks:
@@ -226,7 +238,7 @@ def run_reference(args, world, rank):
                              "sample": f"one 32x128 batch per step, oracle C++ port (Go reference not runnable: no Go "
                                        f"toolchain), {isa}, {threads} threads"},
             "e2e": {"value": v, "unit": "seq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -417,7 +429,7 @@ def run_ours(args, world, rank, local):
                 "kernels": {k["name"]: {"ms": round(k["ms"], 3), "launches": k["launches"]}
                             for k in report["kernels"]},
                 "clocks": clk, "cpu_baseline": cpu, "gemm_sweep": gemm}
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -474,7 +486,7 @@ def run_reference_c5(args, world, rank):
                              "sample": f"{n} images per step, oracle C++ port of internal/siglip (images over "
                                        f"{threads} threads, VNNI integer products)"},
             "e2e": {"value": v, "unit": "img/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def c5_roofline(report, pk, sm_mhz, fp32_names=None):
@@ -593,7 +605,7 @@ def run_ours_c5(args, world, rank, local):
                 "kernels": {k["name"]: {"ms": round(k["ms"], 3), "launches": k["launches"]}
                             for k in report["kernels"]},
                 "clocks": clk, "cpu_baseline": cpu}
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

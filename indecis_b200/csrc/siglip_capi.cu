@@ -105,6 +105,9 @@ int vis_pack(ig_vision *m, VisMat &dm, const float *w, int n, int k, float *tmp)
 
 int vis_work(ig_vision *m, int n, VisWork **out) {
   if (!m->work || m->work->cap < n) {
+    // Calls on device buffers return once enqueued: let them finish before
+    // the workspace they use is replaced.
+    if (m->work) IG_CU(cudaDeviceSynchronize());
     auto w = std::make_unique<VisWork>();
     const size_t N = (size_t)n * m->T, H = m->H, M = m->M;
     auto &L = w->allocs;
