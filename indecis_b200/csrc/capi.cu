@@ -22,6 +22,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "common.cuh"
@@ -166,6 +167,9 @@ struct Workspace {
   void *dev = nullptr;
   void *host = nullptr;  // pinned staging
   size_t host_bytes = 0;
+  void *ohost = nullptr;  // pinned staging of the outputs of a pipelined host call (two slots)
+  size_t ohost_bytes = 0;
+  cudaEvent_t oev[2] = {nullptr, nullptr};  // a slot's device-to-host copy finished
   cudaStream_t own_stream = nullptr;
   cudaEvent_t done = nullptr;
   int32_t *ids, *offs, *row_seq, *pos;
@@ -178,6 +182,9 @@ struct Workspace {
   ~Workspace() {
     if (dev) cudaFree(dev);
     if (host) cudaFreeHost(host);
+    if (ohost) cudaFreeHost(ohost);
+    for (cudaEvent_t e : oev)
+      if (e) cudaEventDestroy(e);
     if (done) cudaEventDestroy(done);
     if (own_stream) cudaStreamDestroy(own_stream);
   }
@@ -395,7 +402,10 @@ void carve_ws(Workspace &w, const ig_model *m, char *base, size_t rows, size_t s
 
 // Takes a workspace with room for the plan; `st` then waits for the
 // workspace's previous user.
-int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st, bool capturing, Workspace **out) {
+// A workspace from the model's pool with room for `rows` rows, `seqs`
+// sequences, `blks` bytes of block lists and `hb` bytes of pinned plan staging.
+int acquire_ws_sized(ig_model *m, size_t rows, size_t seqs, size_t blks, size_t hb, size_t tl, size_t pl,
+                     cudaStream_t st, bool capturing, Workspace **out) {
   std::unique_ptr<Workspace> w;
   {
     std::lock_guard<std::mutex> lk(m->mu);
@@ -409,8 +419,7 @@ int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st
     w->device = m->device;
     IG_CU(cudaEventCreateWithFlags(&w->done, cudaEventDisableTiming));
   }
-  const size_t rows = std::max<size_t>(p.N, 1), seqs = std::max<size_t>(p.nseq, 1),
-               blks = std::max<size_t>(p.block_bytes(), 16);
+  rows = std::max<size_t>(rows, 1), seqs = std::max<size_t>(seqs, 1), blks = std::max<size_t>(blks, 16);
   const bool f32 = m->f32 || w->f32_cap;
   if (rows > w->rows_cap || seqs > w->seq_cap || blks > w->blk_cap || tl > w->tl_cap || pl > w->pl_cap ||
       f32 != w->f32_cap) {
@@ -431,7 +440,6 @@ int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st
     w->tl_cap = t2;
     w->pl_cap = p2;
   }
-  const size_t hb = sizeof(int32_t) * (p.nseq + 1 + 3 * (size_t)p.N) + p.block_bytes() + 64;
   if (hb > w->host_bytes) {
     if (capturing) return fail(IG_ERR_BAD_ARG, "workspace must be sized before stream capture");
     IG_CU(cudaEventSynchronize(w->done));
@@ -448,6 +456,16 @@ int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st
   return 0;
 }
 
+// Pinned staging bytes of a plan's upload (offsets, row -> sequence,
+// positions, ids, block lists).
+size_t plan_host_bytes(const Plan &p) {
+  return sizeof(int32_t) * (p.nseq + 1 + 3 * (size_t)p.N) + p.block_bytes() + 64;
+}
+
+int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st, bool capturing, Workspace **out) {
+  return acquire_ws_sized(m, p.N, p.nseq, p.block_bytes(), plan_host_bytes(p), tl, pl, st, capturing, out);
+}
+
 void release_ws(ig_model *m, Workspace *w, cudaStream_t st, bool capturing) {
   if (!capturing) cudaEventRecord(w->done, st);
   std::lock_guard<std::mutex> lk(m->mu);
@@ -455,9 +473,10 @@ void release_ws(ig_model *m, Workspace *w, cudaStream_t st, bool capturing) {
 }
 
 // Uploads the plan's metadata (offsets, row -> sequence, positions, query
-// blocks, and optionally the host ids) with one copy.
-int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream_t st) {
-  char *h = reinterpret_cast<char *>(w.host);
+// blocks, and optionally the host ids) through the pinned staging at
+// host_off, one copy per device region.
+int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream_t st, size_t host_off = 0) {
+  char *h = reinterpret_cast<char *>(w.host) + host_off;
   size_t off = 0;
   auto put = [&](const void *src, size_t bytes) {
     std::memcpy(h + off, src, bytes);
@@ -795,6 +814,120 @@ int check_ids(const ig_model *m, const int32_t *ids, int64_t N) {
   return 0;
 }
 
+// A host call whose outputs are large runs in chunks of whole sequences on
+// the workspace's stream: each chunk's outputs go to one of two pinned slots,
+// and while the device computes chunk k the host copies chunk k - 1 from its
+// slot into the caller's (pageable) buffers. A sequence's results do not
+// depend on the other sequences of its pass, so the bits are those of one pass.
+constexpr int kPipeMinRows = 16384;        // fewest rows of a chunk
+constexpr size_t kPipeMinBytes = 2 << 20;  // smallest output worth pipelining
+constexpr int kPipeChunks = 4;
+
+int encode_host_pipelined(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode,
+                          float *out, double *logits, double *tlog, const Plan &full, size_t pl, size_t tl) {
+  const int win[2] = {-1, m->cfg.local_attention / 2};
+  const size_t H = m->H;
+  // Chunk boundaries: about equal token counts, every chunk with a token.
+  const int nch = std::max(1, std::min(kPipeChunks, full.N / kPipeMinRows));
+  std::vector<int> cut{0};
+  for (int k = 1; k < nch; k++) {
+    const int64_t target = (int64_t)full.N * k / nch;
+    int c = (int)(std::lower_bound(offs, offs + nseq + 1, target) - offs);
+    c = std::min(c, nseq);
+    if (c > cut.back() && offs[c] > offs[cut.back()]) cut.push_back(c);
+  }
+  if (offs[nseq] > offs[cut.back()] || cut.size() == 1) cut.push_back(nseq);
+  else cut.back() = nseq;
+  const int nc = (int)cut.size() - 1;
+  std::vector<Plan> plans(nc);
+  std::vector<size_t> hoff(nc + 1, 0);
+  size_t rows = 0, seqs = 0, blks = 0, slot = 0;
+  for (int k = 0; k < nc; k++) {
+    const int c0 = cut[k], c1 = cut[k + 1];
+    std::vector<int64_t> so(c1 - c0 + 1);
+    for (int i = c0; i <= c1; i++) so[i - c0] = offs[i] - offs[c0];
+    IG_TRY(make_plan(so.data(), c1 - c0, plans[k], win));
+    const Plan &q = plans[k];
+    rows = std::max(rows, (size_t)q.N), seqs = std::max(seqs, (size_t)q.nseq);
+    blks = std::max(blks, q.block_bytes());
+    hoff[k + 1] = hoff[k] + align_up(plan_host_bytes(q), 64);
+    const size_t ob = (logits ? 8 * (size_t)q.nseq * pl : 0) + (tlog ? 8 * (size_t)q.N * tl : 0) +
+                      (out ? sizeof(float) * H * (mode == IG_MODE_POOLED ? q.nseq : q.N) : 0);
+    slot = std::max(slot, align_up(ob, 256));
+  }
+  Workspace *w = nullptr;
+  IG_TRY(acquire_ws_sized(m, rows, seqs, blks, hoff[nc], tl, pl, nullptr, false, &w));
+  int rc = 0;
+  if (!w->own_stream && cudaStreamCreateWithFlags(&w->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+    rc = fail(IG_ERR_CUDA, "stream creation");
+  const cudaStream_t st = w->own_stream;
+  if (!rc && 2 * slot > w->ohost_bytes) {
+    if (w->ohost) cudaFreeHost(w->ohost);
+    w->ohost = nullptr;
+    w->ohost_bytes = 0;
+    if (cudaMallocHost(&w->ohost, 2 * slot) != cudaSuccess) rc = fail(IG_ERR_CUDA, "pinned output staging");
+    else w->ohost_bytes = 2 * slot;
+  }
+  for (int e = 0; e < 2 && !rc; e++)
+    if (!w->oev[e] && cudaEventCreateWithFlags(&w->oev[e], cudaEventDisableTiming) != cudaSuccess)
+      rc = fail(IG_ERR_CUDA, "event creation");
+  const int enc_mode = (logits || tlog) ? (mode == kModeMeanRows ? kModeMeanRows : IG_MODE_POOLED) : mode;
+  char *slots = reinterpret_cast<char *>(w->ohost);
+  // The chunk's outputs: device source, caller's destination, bytes.
+  auto pieces = [&](int k, std::vector<std::tuple<const void *, void *, size_t>> &v) {
+    const Plan &q = plans[k];
+    const int64_t r0 = offs[cut[k]];
+    v.clear();
+    if (logits && q.nseq && pl) v.emplace_back(w->logits, logits + (size_t)cut[k] * pl, 8 * (size_t)q.nseq * pl);
+    if (tlog && q.N && tl) v.emplace_back(w->tlogits, tlog + (size_t)r0 * tl, 8 * (size_t)q.N * tl);
+    if (out) {
+      if (mode == IG_MODE_POOLED)
+        v.emplace_back(w->pooled, out + (size_t)cut[k] * H, sizeof(float) * H * q.nseq);
+      else
+        v.emplace_back(w->xn, out + (size_t)r0 * H, sizeof(float) * H * q.N);
+    }
+  };
+  std::vector<std::tuple<const void *, void *, size_t>> pc;
+  auto copy_out = [&](int k) {
+    if (cudaEventSynchronize(w->oev[k & 1]) != cudaSuccess) return fail(IG_ERR_CUDA, "encode: output copy");
+    pieces(k, pc);
+    size_t o = (size_t)(k & 1) * slot;
+    for (auto &t : pc) {
+      std::memcpy(std::get<1>(t), slots + o, std::get<2>(t));
+      o += std::get<2>(t);
+    }
+    return 0;
+  };
+  int issued = 0;
+  for (int k = 0; k < nc && !rc; k++) {
+    const Plan &q = plans[k];
+    rc = upload_plan(*w, q, ids + offs[cut[k]], st, hoff[k]);
+    if (!rc) rc = run_encoder(m, *w, w->ids, q, enc_mode, st, nullptr);
+    if (!rc && (logits || tlog))
+      rc = run_heads(m, *w, q, st, logits ? w->logits : nullptr, tlog ? w->tlogits : nullptr, false);
+    if (!rc) {
+      pieces(k, pc);
+      size_t o = (size_t)(k & 1) * slot;
+      for (auto &t : pc) {
+        if (cudaMemcpyAsync(slots + o, std::get<0>(t), std::get<2>(t), cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+          rc = fail(IG_ERR_CUDA, "copy of the output");
+          break;
+        }
+        o += std::get<2>(t);
+      }
+    }
+    if (!rc && cudaEventRecord(w->oev[k & 1], st) != cudaSuccess) rc = fail(IG_ERR_CUDA, "event record");
+    if (!rc) issued = k + 1;
+    if (!rc && k > 0) rc = copy_out(k - 1);
+  }
+  if (!rc && issued == nc) rc = copy_out(nc - 1);
+  cudaError_t se = cudaStreamSynchronize(st);
+  release_ws(m, w, st, false);
+  if (rc) return rc;
+  if (se != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(se));
+  return 0;
+}
+
 int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
                 size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len) {
   t_last_error.clear();
@@ -818,6 +951,10 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   if (logits && logits_len < (size_t)nseq * pl) return fail(IG_ERR_BAD_ARG, "logits too short");
   if (tlog && tlog_len < (size_t)p.N * tl) return fail(IG_ERR_BAD_ARG, "token logits too short");
   IG_TRY(ensure_rope(m, p.max_len));
+  const size_t out_bytes = (logits ? 8 * (size_t)nseq * pl : 0) + (tlog ? 8 * (size_t)p.N * tl : 0) +
+                           (out ? sizeof(float) * need : 0);
+  if (!dump && nseq >= 2 && p.N >= 2 * kPipeMinRows && out_bytes >= kPipeMinBytes)
+    return encode_host_pipelined(m, ids, offs, nseq, mode, out, logits, tlog, p, pl, tl);
   Workspace *w = nullptr;
   cudaStream_t st = nullptr;
   IG_TRY(acquire_ws(m, p, tl, pl, nullptr, false, &w));

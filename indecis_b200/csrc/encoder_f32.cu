@@ -110,11 +110,13 @@ __global__ void __launch_bounds__(256, 2) attend_blocks_f32_kernel(const float *
     Qt[(j4 + 3) * kAbQ + qq] = __fmul_rn(qv.w, scale);
   }
   if (tid < kAbQ) s_mx[tid] = -INFINITY, s_sum[tid] = 0.0f;
-  // P V tile of this thread: query qo, dimensions dg..dg+15.
-  const int qo = tid >> 2, dg = (tid & 3) * 16;
-  float o[16];
+  // P V tile of this thread: queries 4qg..4qg+3, dimensions 4dq..4dq+3.
+  const int qg = tid >> 4, dq = tid & 15;
+  float o[4][4];
 #pragma unroll
-  for (int d = 0; d < 16; d++) o[d] = 0.0f;
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) o[i][c] = 0.0f;
   for (int jb = 0; jb < n; jb += kAbK) {
     const int je = min(n, jb + kAbK), cols = je - jb;
     // The query blocks the reference visits for this key block (infer.go:609-614).
@@ -133,7 +135,7 @@ __global__ void __launch_bounds__(256, 2) attend_blocks_f32_kernel(const float *
       Kt[(j4 + 3) * kAbK + u] = kv.w;
     }
     __syncthreads();
-    // S = (scaled Q) K^T: warp w takes queries 8w.., lane the keys lane + 32m.
+    // S = (scaled Q) K^T: warp w takes queries 8w.., lane the keys 4 lane..4 lane + 3.
     {
       float acc[8][4];
 #pragma unroll
@@ -145,8 +147,8 @@ __global__ void __launch_bounds__(256, 2) attend_blocks_f32_kernel(const float *
         const float4 a0 = *reinterpret_cast<const float4 *>(Qt + j * kAbQ + warp * 8);
         const float4 a1 = *reinterpret_cast<const float4 *>(Qt + j * kAbQ + warp * 8 + 4);
         const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const float *kj = Kt + j * kAbK + lane;
-        const float kv[4] = {kj[0], kj[32], kj[64], kj[96]};
+        const float4 k4 = *reinterpret_cast<const float4 *>(Kt + j * kAbK + 4 * lane);
+        const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
         for (int i = 0; i < 8; i++)
 #pragma unroll
@@ -154,8 +156,8 @@ __global__ void __launch_bounds__(256, 2) attend_blocks_f32_kernel(const float *
       }
 #pragma unroll
       for (int i = 0; i < 8; i++)
-#pragma unroll
-        for (int m = 0; m < 4; m++) S[(warp * 8 + i) * kAbSP + lane + 32 * m] = acc[i][m];
+        *reinterpret_cast<float4 *>(S + (warp * 8 + i) * kAbSP + 4 * lane) =
+            make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
     }
     __syncthreads();
     // K^T is consumed: V of the block comes into its place during the softmax
@@ -224,42 +226,69 @@ __global__ void __launch_bounds__(256, 2) attend_blocks_f32_kernel(const float *
     }
     cp_async_wait_all();
     __syncthreads();
-    // o = o * corr, then o += (one chain over the block's keys).
-    if (qo < rows) {
-      const float c = s_corr[qo];
-      float acc[16];
+    // o = o * corr, then o += (one chain over the block's keys, in key
+    // order: four keys' weights of a query come in one 16-byte read).
+    if (4 * qg < rows) {
+      float acc[4][4];
 #pragma unroll
-      for (int d = 0; d < 16; d++) acc[d] = 0.0f;
-      const float *pr = S + qo * kAbSP;
-      for (int u = 0; u < cols; u++) {
-        const float p = pr[u];
-        const float4 *vr = reinterpret_cast<const float4 *>(Vs + u * kAbD + dg);
+      for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int q4 = 0; q4 < 4; q4++) {
-          const float4 v4 = vr[q4];
-          acc[4 * q4] = __fmaf_rn(p, v4.x, acc[4 * q4]);
-          acc[4 * q4 + 1] = __fmaf_rn(p, v4.y, acc[4 * q4 + 1]);
-          acc[4 * q4 + 2] = __fmaf_rn(p, v4.z, acc[4 * q4 + 2]);
-          acc[4 * q4 + 3] = __fmaf_rn(p, v4.w, acc[4 * q4 + 3]);
+        for (int c = 0; c < 4; c++) acc[i][c] = 0.0f;
+      const float *pr = S + 4 * qg * kAbSP;
+      const float *vc = Vs + 4 * dq;
+      const int cols4 = cols & ~3;
+      for (int u = 0; u < cols4; u += 4) {
+        float pv[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float4 p4 = *reinterpret_cast<const float4 *>(pr + i * kAbSP + u);
+          pv[i][0] = p4.x, pv[i][1] = p4.y, pv[i][2] = p4.z, pv[i][3] = p4.w;
+        }
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          const float4 v4 = *reinterpret_cast<const float4 *>(vc + (u + t) * kAbD);
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            acc[i][0] = __fmaf_rn(pv[i][t], v4.x, acc[i][0]);
+            acc[i][1] = __fmaf_rn(pv[i][t], v4.y, acc[i][1]);
+            acc[i][2] = __fmaf_rn(pv[i][t], v4.z, acc[i][2]);
+            acc[i][3] = __fmaf_rn(pv[i][t], v4.w, acc[i][3]);
+          }
+        }
+      }
+      for (int u = cols4; u < cols; u++) {
+        const float4 v4 = *reinterpret_cast<const float4 *>(vc + u * kAbD);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float p = pr[i * kAbSP + u];
+          acc[i][0] = __fmaf_rn(p, v4.x, acc[i][0]);
+          acc[i][1] = __fmaf_rn(p, v4.y, acc[i][1]);
+          acc[i][2] = __fmaf_rn(p, v4.z, acc[i][2]);
+          acc[i][3] = __fmaf_rn(p, v4.w, acc[i][3]);
         }
       }
 #pragma unroll
-      for (int d = 0; d < 16; d++) {
-        if (c != 1.0f) o[d] = __fmul_rn(o[d], c);
-        o[d] = __fadd_rn(o[d], acc[d]);
+      for (int i = 0; i < 4; i++) {
+        const float c = s_corr[4 * qg + i];
+#pragma unroll
+        for (int d = 0; d < 4; d++) {
+          if (c != 1.0f) o[i][d] = __fmul_rn(o[i][d], c);
+          o[i][d] = __fadd_rn(o[i][d], acc[i][d]);
+        }
       }
     }
   }
   __syncthreads();
   // Scale(o, 1/sum).
-  if (qo < rows) {
-    const float inv = __fdiv_rn(1.0f, s_sum[qo]);
-    float *dst = ctx + (size_t)(off + i0 + qo) * H + h * kAbD + dg;
 #pragma unroll
-    for (int q4 = 0; q4 < 4; q4++)
-      *reinterpret_cast<float4 *>(dst + 4 * q4) = make_float4(__fmul_rn(o[4 * q4], inv), __fmul_rn(o[4 * q4 + 1], inv),
-                                                              __fmul_rn(o[4 * q4 + 2], inv),
-                                                              __fmul_rn(o[4 * q4 + 3], inv));
+  for (int i = 0; i < 4; i++) {
+    const int q = 4 * qg + i;
+    if (q < rows) {
+      const float inv = __fdiv_rn(1.0f, s_sum[q]);
+      *reinterpret_cast<float4 *>(ctx + (size_t)(off + i0 + q) * H + h * kAbD + 4 * dq) =
+          make_float4(__fmul_rn(o[i][0], inv), __fmul_rn(o[i][1], inv), __fmul_rn(o[i][2], inv),
+                      __fmul_rn(o[i][3], inv));
+    }
   }
 }
 

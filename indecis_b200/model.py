@@ -289,7 +289,7 @@ class Model:
         nseq = len(offs) - 1
         H = self.Cfg.hidden_size
         rows = nseq if mode == _capi.IG_MODE_POOLED else int(offs[-1])
-        out = np.zeros((rows, H), np.float32)
+        out = np.empty((rows, H), np.float32)  # every row is written
         rc = _capi.load().ig_encode(self._h, ids.ctypes.data, offs.ctypes.data, nseq, mode, out.ctypes.data,
                                     out.size)
         if rc == _capi.IG_ERR_OUT_OF_VOCAB:
@@ -345,8 +345,8 @@ class Model:
         N = int(offs[-1])
         pr = sum(h.rows for h in self.heads if h.kind != "spans")
         tr = sum(h.rows for h in self.heads if h.kind == "spans")
-        z = np.zeros((nseq, pr), np.float64)
-        zt = np.zeros((N, tr), np.float64) if tr else None
+        z = np.empty((nseq, pr), np.float64)  # every entry is written
+        zt = np.empty((N, tr), np.float64) if tr else None
         rc = _capi.load().ig_logits(self._h, ids.ctypes.data, offs.ctypes.data, nseq, z.ctypes.data, z.size,
                                     zt.ctypes.data if zt is not None else None, zt.size if zt is not None else 0)
         if rc == _capi.IG_ERR_OUT_OF_VOCAB:

@@ -109,8 +109,8 @@ class Vision:
         pool, the embeddings [n][H]."""
         px = self._pixels(pixels)
         n, H = px.shape[0], self.cfg.hidden
-        pa = np.zeros((n, self.cfg.Patches(), H), np.float32)
-        po = np.zeros((n, H), np.float32) if pool else None
+        pa = np.empty((n, self.cfg.Patches(), H), np.float32)  # every entry is written
+        po = np.empty((n, H), np.float32) if pool else None
         rc = _capi.load().ig_vision_forward(self._h, px.ctypes.data, n, int(layer), pa.ctypes.data, pa.size,
                                             po.ctypes.data if po is not None else None, po.size if po is not None else 0)
         if rc == _capi.IG_ERR_BAD_ARG:
@@ -122,7 +122,7 @@ class Vision:
         """Vision.Embed (vision.go:85-88): the pooled embedding [n][H] of each image."""
         px = self._pixels(pixels)
         n, H = px.shape[0], self.cfg.hidden
-        po = np.zeros((n, H), np.float32)
+        po = np.empty((n, H), np.float32)
         rc = _capi.load().ig_vision_forward(self._h, px.ctypes.data, n, 0, None, 0, po.ctypes.data, po.size)
         if rc == _capi.IG_ERR_BAD_ARG:
             raise SiglipError(_capi.last_error())

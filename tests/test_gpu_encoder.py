@@ -168,3 +168,54 @@ def test_head_logits_many(tiny):
     for h, z in zip(heads, logits):
         ref = oracle.head_logits(h.w, h.b, tokens if h.kind == "spans" else pooled)
         assert np.array_equal(z, ref), h.name
+
+
+def test_host_pipeline_matches_one_pass(igdev):
+    """A host call with large outputs runs in chunks of sequences, copying
+    each chunk out while the next computes; its logits, pooled rows and token
+    states equal one device pass over the whole batch bit for bit (ragged
+    lengths, empty sequences at the chunk edges included)."""
+    import torch
+    from indecis_b200 import _capi
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Config, Head, Model
+    gm = Model.from_arrays(Config.from_dict(S.C1), S.weights(S.C1, seed=42))
+    heads = [Head(h["name"], h["kind"], h["w"], h["b"]) for h in S.heads(S.C1["hidden"])]
+    gm.SetHeads(heads)
+    rng = np.random.default_rng(8)
+    lens = rng.integers(1, 200, 700)
+    lens[[0, 1, 349, 350, 351, 699]] = 0
+    offs = np.zeros(len(lens) + 1, np.int64)
+    offs[1:] = np.cumsum(lens)
+    ids = rng.integers(4, S.C1["vocab"], int(offs[-1])).astype(np.int32)
+    assert offs[-1] >= 2 * 16384  # pipelined in chunks
+    seqs = [ids[offs[i]:offs[i + 1]] for i in range(len(lens))]
+    host, _ = gm.Logits(seqs)
+    L = _capi.load()
+    pr = sum(h.rows for h in heads if h.kind != "spans")
+    tr = sum(h.rows for h in heads if h.kind == "spans")
+    d_ids = torch.from_numpy(ids).cuda()
+    d_z = torch.empty((len(lens), pr), dtype=torch.float64, device="cuda")
+    d_zt = torch.empty((int(offs[-1]), tr), dtype=torch.float64, device="cuda")
+    st = torch.cuda.current_stream()
+    _capi.check(L.ig_logits_device(gm._h, d_ids.data_ptr(), offs.ctypes.data, len(lens), d_z.data_ptr(),
+                                   d_zt.data_ptr(), st.cuda_stream))
+    torch.cuda.synchronize()
+    z, zt = d_z.cpu().numpy(), d_zt.cpu().numpy()
+    po = to = 0
+    for h, got in zip(heads, host):
+        if h.kind == "spans":
+            assert np.array_equal(got.view(np.uint64), zt[:, to:to + h.rows].view(np.uint64)), h.name
+            to += h.rows
+        else:
+            assert np.array_equal(got.view(np.uint64), z[:, po:po + h.rows].view(np.uint64)), h.name
+            po += h.rows
+    for mode, rows in ((_capi.IG_MODE_POOLED, len(lens)), (_capi.IG_MODE_TOKENS, int(offs[-1]))):
+        d_out = torch.empty((rows, S.C1["hidden"]), dtype=torch.float32, device="cuda")
+        _capi.check(L.ig_encode_device(gm._h, d_ids.data_ptr(), offs.ctypes.data, len(lens), mode,
+                                       d_out.data_ptr(), st.cuda_stream))
+        torch.cuda.synchronize()
+        got = gm.EncodeSeqs(seqs) if mode == _capi.IG_MODE_POOLED else gm.EncodeTokens(seqs)
+        got = np.concatenate(got) if isinstance(got, list) else got
+        assert np.array_equal(_bits(got), _bits(d_out.cpu().numpy())), mode
+    gm.close()
