@@ -17,12 +17,14 @@
 
 #include <algorithm>
 #include <atomic>
+#include <condition_variable>
+#include <deque>
 #include <cmath>
 #include <cstring>
 #include <memory>
 #include <mutex>
 #include <string>
-#include <tuple>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -167,9 +169,9 @@ struct Workspace {
   void *dev = nullptr;
   void *host = nullptr;  // pinned staging
   size_t host_bytes = 0;
-  void *ohost = nullptr;  // pinned staging of the outputs of a pipelined host call (two slots)
+  void *ohost = nullptr;  // pinned staging of a host call's large outputs
   size_t ohost_bytes = 0;
-  cudaEvent_t oev[2] = {nullptr, nullptr};  // a slot's device-to-host copy finished
+  std::vector<cudaEvent_t> pev;  // one per staged piece: its device-to-host copy finished
   cudaStream_t own_stream = nullptr;
   cudaEvent_t done = nullptr;
   int32_t *ids, *offs, *row_seq, *pos;
@@ -183,8 +185,7 @@ struct Workspace {
     if (dev) cudaFree(dev);
     if (host) cudaFreeHost(host);
     if (ohost) cudaFreeHost(ohost);
-    for (cudaEvent_t e : oev)
-      if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : pev) cudaEventDestroy(e);
     if (done) cudaEventDestroy(done);
     if (own_stream) cudaStreamDestroy(own_stream);
   }
@@ -313,11 +314,27 @@ int ensure_rope(ig_model *m, int npos) {
 
 // windows[k]: the half window of attention kind k (-1: global); kinds whose
 // window is < -1 are not planned.
-int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2]) {
+// Checks a batch's offsets (the errors of run's batch checks) and returns
+// its row count and longest sequence.
+int scan_offsets(const int64_t *offs, int nseq, int64_t *rows, int *max_len) {
   if (nseq < 0 || !offs) return fail(IG_ERR_BAD_ARG, "modernbert: inconsistent batch");
   if (offs[0] != 0) return fail(IG_ERR_BAD_ARG, "modernbert: offs[0] must be 0");
   const int64_t N = offs[nseq];
   if (N < 0 || N > (int64_t)INT32_MAX / 4) return fail(IG_ERR_BAD_ARG, "modernbert: batch too large");
+  int64_t ml = 0;
+  for (int s = 0; s < nseq; s++) {
+    if (offs[s + 1] < offs[s]) return fail(IG_ERR_BAD_ARG, "modernbert: decreasing offsets");
+    ml = std::max(ml, offs[s + 1] - offs[s]);
+  }
+  *rows = N;
+  *max_len = (int)ml;
+  return 0;
+}
+
+int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2]) {
+  int64_t N = 0;
+  int ml = 0;
+  IG_TRY(scan_offsets(offs, nseq, &N, &ml));
   p.nseq = nseq;
   p.N = (int)N;
   p.offs.resize(nseq + 1);
@@ -331,7 +348,6 @@ int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2]) {
   p.max_len = 0;
   const int qb = attn_query_block();
   for (int s = 0; s < nseq; s++) {
-    if (offs[s + 1] < offs[s]) return fail(IG_ERR_BAD_ARG, "modernbert: decreasing offsets");
     p.offs[s] = (int32_t)offs[s];
     const int n = (int)(offs[s + 1] - offs[s]);
     p.max_len = std::max(p.max_len, n);
@@ -814,117 +830,123 @@ int check_ids(const ig_model *m, const int32_t *ids, int64_t N) {
   return 0;
 }
 
-// A host call whose outputs are large runs in chunks of whole sequences on
-// the workspace's stream: each chunk's outputs go to one of two pinned slots,
-// and while the device computes chunk k the host copies chunk k - 1 from its
-// slot into the caller's (pageable) buffers. A sequence's results do not
-// depend on the other sequences of its pass, so the bits are those of one pass.
-constexpr int kPipeMinRows = 16384;        // fewest rows of a chunk
-constexpr size_t kPipeMinBytes = 2 << 20;  // smallest output worth pipelining
-constexpr int kPipeChunks = 4;
+// Large outputs of a host call reach the caller's (pageable) memory through
+// the workspace's pinned staging: the device copies 2 MB pieces there, and as
+// each piece lands the host copies it on with a few threads, while the later
+// pieces are in flight. A pageable destination takes about a quarter of the
+// link's rate from a single copying thread.
+constexpr size_t kStageMinBytes = 2 << 20;  // smaller outputs are copied directly
+constexpr size_t kStagePiece = 2 << 20;
 
-int encode_host_pipelined(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode,
-                          float *out, double *logits, double *tlog, const Plan &full, size_t pl, size_t tl) {
-  const int win[2] = {-1, m->cfg.local_attention / 2};
-  const size_t H = m->H;
-  // Chunk boundaries: about equal token counts, every chunk with a token.
-  const int nch = std::max(1, std::min(kPipeChunks, full.N / kPipeMinRows));
-  std::vector<int> cut{0};
-  for (int k = 1; k < nch; k++) {
-    const int64_t target = (int64_t)full.N * k / nch;
-    int c = (int)(std::lower_bound(offs, offs + nseq + 1, target) - offs);
-    c = std::min(c, nseq);
-    if (c > cut.back() && offs[c] > offs[cut.back()]) cut.push_back(c);
+class CopyPool {
+ public:
+  static CopyPool &get() {
+    static CopyPool *pool = new CopyPool();  // lives until the process ends
+    return *pool;
   }
-  if (offs[nseq] > offs[cut.back()] || cut.size() == 1) cut.push_back(nseq);
-  else cut.back() = nseq;
-  const int nc = (int)cut.size() - 1;
-  std::vector<Plan> plans(nc);
-  std::vector<size_t> hoff(nc + 1, 0);
-  size_t rows = 0, seqs = 0, blks = 0, slot = 0;
-  for (int k = 0; k < nc; k++) {
-    const int c0 = cut[k], c1 = cut[k + 1];
-    std::vector<int64_t> so(c1 - c0 + 1);
-    for (int i = c0; i <= c1; i++) so[i - c0] = offs[i] - offs[c0];
-    IG_TRY(make_plan(so.data(), c1 - c0, plans[k], win));
-    const Plan &q = plans[k];
-    rows = std::max(rows, (size_t)q.N), seqs = std::max(seqs, (size_t)q.nseq);
-    blks = std::max(blks, q.block_bytes());
-    hoff[k + 1] = hoff[k] + align_up(plan_host_bytes(q), 64);
-    const size_t ob = (logits ? 8 * (size_t)q.nseq * pl : 0) + (tlog ? 8 * (size_t)q.N * tl : 0) +
-                      (out ? sizeof(float) * H * (mode == IG_MODE_POOLED ? q.nseq : q.N) : 0);
-    slot = std::max(slot, align_up(ob, 256));
-  }
-  Workspace *w = nullptr;
-  IG_TRY(acquire_ws_sized(m, rows, seqs, blks, hoff[nc], tl, pl, nullptr, false, &w));
-  int rc = 0;
-  if (!w->own_stream && cudaStreamCreateWithFlags(&w->own_stream, cudaStreamNonBlocking) != cudaSuccess)
-    rc = fail(IG_ERR_CUDA, "stream creation");
-  const cudaStream_t st = w->own_stream;
-  if (!rc && 2 * slot > w->ohost_bytes) {
-    if (w->ohost) cudaFreeHost(w->ohost);
-    w->ohost = nullptr;
-    w->ohost_bytes = 0;
-    if (cudaMallocHost(&w->ohost, 2 * slot) != cudaSuccess) rc = fail(IG_ERR_CUDA, "pinned output staging");
-    else w->ohost_bytes = 2 * slot;
-  }
-  for (int e = 0; e < 2 && !rc; e++)
-    if (!w->oev[e] && cudaEventCreateWithFlags(&w->oev[e], cudaEventDisableTiming) != cudaSuccess)
-      rc = fail(IG_ERR_CUDA, "event creation");
-  const int enc_mode = (logits || tlog) ? (mode == kModeMeanRows ? kModeMeanRows : IG_MODE_POOLED) : mode;
-  char *slots = reinterpret_cast<char *>(w->ohost);
-  // The chunk's outputs: device source, caller's destination, bytes.
-  auto pieces = [&](int k, std::vector<std::tuple<const void *, void *, size_t>> &v) {
-    const Plan &q = plans[k];
-    const int64_t r0 = offs[cut[k]];
-    v.clear();
-    if (logits && q.nseq && pl) v.emplace_back(w->logits, logits + (size_t)cut[k] * pl, 8 * (size_t)q.nseq * pl);
-    if (tlog && q.N && tl) v.emplace_back(w->tlogits, tlog + (size_t)r0 * tl, 8 * (size_t)q.N * tl);
-    if (out) {
-      if (mode == IG_MODE_POOLED)
-        v.emplace_back(w->pooled, out + (size_t)cut[k] * H, sizeof(float) * H * q.nseq);
-      else
-        v.emplace_back(w->xn, out + (size_t)r0 * H, sizeof(float) * H * q.N);
-    }
-  };
-  std::vector<std::tuple<const void *, void *, size_t>> pc;
-  auto copy_out = [&](int k) {
-    if (cudaEventSynchronize(w->oev[k & 1]) != cudaSuccess) return fail(IG_ERR_CUDA, "encode: output copy");
-    pieces(k, pc);
-    size_t o = (size_t)(k & 1) * slot;
-    for (auto &t : pc) {
-      std::memcpy(std::get<1>(t), slots + o, std::get<2>(t));
-      o += std::get<2>(t);
-    }
-    return 0;
-  };
-  int issued = 0;
-  for (int k = 0; k < nc && !rc; k++) {
-    const Plan &q = plans[k];
-    rc = upload_plan(*w, q, ids + offs[cut[k]], st, hoff[k]);
-    if (!rc) rc = run_encoder(m, *w, w->ids, q, enc_mode, st, nullptr);
-    if (!rc && (logits || tlog))
-      rc = run_heads(m, *w, q, st, logits ? w->logits : nullptr, tlog ? w->tlogits : nullptr, false);
-    if (!rc) {
-      pieces(k, pc);
-      size_t o = (size_t)(k & 1) * slot;
-      for (auto &t : pc) {
-        if (cudaMemcpyAsync(slots + o, std::get<0>(t), std::get<2>(t), cudaMemcpyDeviceToHost, st) != cudaSuccess) {
-          rc = fail(IG_ERR_CUDA, "copy of the output");
-          break;
-        }
-        o += std::get<2>(t);
+  // memcpy(dst, src, n), split across the pool's threads and the caller.
+  void copy(char *dst, const char *src, size_t n) {
+    const size_t parts = std::min<size_t>(nthreads_ + 1, std::max<size_t>(1, n / kMinPart));
+    const size_t per = align_up((n + parts - 1) / parts, 64);
+    Batch b;
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      for (size_t o = per; o < n; o += per) {
+        jobs_.push_back({dst + o, src + o, std::min(per, n - o), &b});
+        b.left++;
       }
     }
-    if (!rc && cudaEventRecord(w->oev[k & 1], st) != cudaSuccess) rc = fail(IG_ERR_CUDA, "event record");
-    if (!rc) issued = k + 1;
-    if (!rc && k > 0) rc = copy_out(k - 1);
+    cv_.notify_all();
+    std::memcpy(dst, src, std::min(per, n));
+    std::unique_lock<std::mutex> lk(b.mu);
+    b.cv.wait(lk, [&] { return b.left == 0; });
   }
-  if (!rc && issued == nc) rc = copy_out(nc - 1);
-  cudaError_t se = cudaStreamSynchronize(st);
-  release_ws(m, w, st, false);
-  if (rc) return rc;
-  if (se != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(se));
+
+ private:
+  static constexpr size_t kMinPart = 256 << 10;
+  struct Batch {
+    std::mutex mu;
+    std::condition_variable cv;
+    size_t left = 0;
+  };
+  struct Job {
+    char *dst;
+    const char *src;
+    size_t n;
+    Batch *b;
+  };
+  CopyPool() {
+    const unsigned hc = std::thread::hardware_concurrency();
+    nthreads_ = std::max(1u, std::min(7u, hc / 2));
+    for (unsigned i = 0; i < nthreads_; i++) std::thread([this] { run(); }).detach();
+  }
+  void run() {
+    for (;;) {
+      Job j;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return !jobs_.empty(); });
+        j = jobs_.front();
+        jobs_.pop_front();
+      }
+      std::memcpy(j.dst, j.src, j.n);
+      std::lock_guard<std::mutex> lk(j.b->mu);
+      if (--j.b->left == 0) j.b->cv.notify_all();
+    }
+  }
+  unsigned nthreads_ = 1;
+  std::mutex mu_;
+  std::condition_variable cv_;
+  std::deque<Job> jobs_;
+};
+
+struct OutCopy {
+  const void *src;  // device
+  void *dst;        // host
+  size_t bytes;
+};
+
+// Copies the outputs to the host through the pinned staging (enqueued on st
+// after the work that produces them) and returns once all have arrived.
+int copy_out_staged(Workspace &w, cudaStream_t st, const std::vector<OutCopy> &outs) {
+  size_t total = 0;
+  for (auto &o : outs) total += o.bytes;
+  if (total > w.ohost_bytes) {
+    IG_CU(cudaStreamSynchronize(st));  // the earlier user of the staging has finished
+    if (w.ohost) IG_CU(cudaFreeHost(w.ohost));
+    w.ohost = nullptr;
+    w.ohost_bytes = 0;
+    IG_CU(cudaMallocHost(&w.ohost, total));
+    w.ohost_bytes = total;
+  }
+  struct Piece {
+    const char *src;
+    char *dst;
+    size_t n, at;
+  };
+  std::vector<Piece> ps;
+  size_t at = 0;
+  for (auto &o : outs)
+    for (size_t k = 0; k < o.bytes; k += kStagePiece) {
+      const size_t n = std::min(kStagePiece, o.bytes - k);
+      ps.push_back({static_cast<const char *>(o.src) + k, static_cast<char *>(o.dst) + k, n, at});
+      at += n;
+    }
+  while (w.pev.size() < ps.size()) {
+    cudaEvent_t e;
+    IG_CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    w.pev.push_back(e);
+  }
+  char *stage = static_cast<char *>(w.ohost);
+  for (size_t i = 0; i < ps.size(); i++) {
+    IG_CU(cudaMemcpyAsync(stage + ps[i].at, ps[i].src, ps[i].n, cudaMemcpyDeviceToHost, st));
+    IG_CU(cudaEventRecord(w.pev[i], st));
+  }
+  for (size_t i = 0; i < ps.size(); i++) {
+    const cudaError_t e = cudaEventSynchronize(w.pev[i]);
+    if (e != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(e));
+    CopyPool::get().copy(ps[i].dst, stage + ps[i].at, ps[i].n);
+  }
   return 0;
 }
 
@@ -935,13 +957,13 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS && !(mode == kModeMeanRows && !out))
     return fail(IG_ERR_BAD_ARG, "bad mode");
   DeviceGuard dg(m->device);
-  Plan p;
-  const int win[2] = {-1, m->cfg.local_attention / 2};
-  IG_TRY(make_plan(offs, nseq, p, win));
-  if (p.N > 0 && !ids) return fail(IG_ERR_BAD_ARG, "null ids");
-  IG_TRY(check_ids(m, ids, p.N));
+  int64_t nrows = 0;
+  int max_len = 0;
+  IG_TRY(scan_offsets(offs, nseq, &nrows, &max_len));
+  if (nrows > 0 && !ids) return fail(IG_ERR_BAD_ARG, "null ids");
+  IG_TRY(check_ids(m, ids, nrows));
   const size_t H = m->H;
-  const size_t need = mode == IG_MODE_POOLED ? (size_t)nseq * H : (size_t)p.N * H;
+  const size_t need = mode == IG_MODE_POOLED ? (size_t)nseq * H : (size_t)nrows * H;
   if (out && out_len < need) return fail(IG_ERR_BAD_ARG, "output too short");
   size_t pl = 0, tl = 0;
   if (logits || tlog) {
@@ -949,12 +971,13 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
     for (auto &h : m->heads) (h.per_token ? tl : pl) += h.rows;
   }
   if (logits && logits_len < (size_t)nseq * pl) return fail(IG_ERR_BAD_ARG, "logits too short");
-  if (tlog && tlog_len < (size_t)p.N * tl) return fail(IG_ERR_BAD_ARG, "token logits too short");
-  IG_TRY(ensure_rope(m, p.max_len));
-  const size_t out_bytes = (logits ? 8 * (size_t)nseq * pl : 0) + (tlog ? 8 * (size_t)p.N * tl : 0) +
+  if (tlog && tlog_len < (size_t)nrows * tl) return fail(IG_ERR_BAD_ARG, "token logits too short");
+  IG_TRY(ensure_rope(m, max_len));
+  const size_t out_bytes = (logits ? 8 * (size_t)nseq * pl : 0) + (tlog ? 8 * (size_t)nrows * tl : 0) +
                            (out ? sizeof(float) * need : 0);
-  if (!dump && nseq >= 2 && p.N >= 2 * kPipeMinRows && out_bytes >= kPipeMinBytes)
-    return encode_host_pipelined(m, ids, offs, nseq, mode, out, logits, tlog, p, pl, tl);
+  Plan p;
+  const int win[2] = {-1, m->cfg.local_attention / 2};
+  IG_TRY(make_plan(offs, nseq, p, win));
   Workspace *w = nullptr;
   cudaStream_t st = nullptr;
   IG_TRY(acquire_ws(m, p, tl, pl, nullptr, false, &w));
@@ -965,19 +988,19 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump);
   if (!rc && (logits || tlog))
     rc = run_heads(m, *w, p, st, logits ? w->logits : nullptr, tlog ? w->tlogits : nullptr, false);
-  if (!rc && (logits || tlog)) {
-    if (!rc && logits && nseq && pl)
-      rc = cudaMemcpyAsync(logits, w->logits, sizeof(double) * nseq * pl, cudaMemcpyDeviceToHost, st) ? IG_ERR_CUDA : 0;
-    if (!rc && tlog && p.N && tl)
-      rc = cudaMemcpyAsync(tlog, w->tlogits, sizeof(double) * p.N * tl, cudaMemcpyDeviceToHost, st) ? IG_ERR_CUDA : 0;
+  std::vector<OutCopy> outs;
+  if (logits && nseq && pl) outs.push_back({w->logits, logits, sizeof(double) * nseq * pl});
+  if (tlog && p.N && tl) outs.push_back({w->tlogits, tlog, sizeof(double) * p.N * tl});
+  if (out && need) {
+    if (mode == IG_MODE_POOLED && p.N == 0) std::memset(out, 0, need * sizeof(float));
+    else outs.push_back({mode == IG_MODE_POOLED ? w->pooled : w->xn, out, need * sizeof(float)});
   }
-  if (!rc && out && need) {
-    const float *src = mode == IG_MODE_POOLED ? w->pooled : w->xn;
-    if (mode == IG_MODE_POOLED && p.N == 0) {
-      std::memset(out, 0, need * sizeof(float));
-    } else if (cudaMemcpyAsync(out, src, need * sizeof(float), cudaMemcpyDeviceToHost, st) != cudaSuccess) {
-      rc = fail(IG_ERR_CUDA, "copy of the output");
-    }
+  if (!rc && out_bytes >= kStageMinBytes) {
+    rc = copy_out_staged(*w, st, outs);
+  } else {
+    for (auto &o : outs)
+      if (!rc && cudaMemcpyAsync(o.dst, o.src, o.bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        rc = fail(IG_ERR_CUDA, "copy of the output");
   }
   cudaError_t se = cudaStreamSynchronize(st);
   release_ws(m, w, st, false);
