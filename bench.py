@@ -400,8 +400,11 @@ def run_ours(args, world, rank, local):
         model.Logits(seqs)
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    nblocks = sum((int(offs[i + 1] - offs[i]) + 15) // 16 for i in range(nseq))
-    h2d = 4 * N + 4 * (nseq + 1) + 8 * N + 8 * nblocks  # ids + offsets, row->sequence, positions, query blocks
+    # ids + offsets + the plan's block lists: per sequence of 128 tokens one
+    # 16-byte tensor-core entry per attention kind and one 8-byte float-path
+    # entry per 64 queries (row tables are filled on the device)
+    blocks = sum(2 * 16 * ((n + 127) // 128) + 8 * ((n + 63) // 64) for n in np.diff(offs).tolist())
+    h2d = 4 * N + 4 * (nseq + 1) + blocks
     d2h = 8 * nseq * pooled_rows + 8 * N * token_rows
     e2e = {"value": world * nseq * e2e_steps / e2e_s, "unit": "seq/s", "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "api": "ig_logits (host buffers, synchronous), host clock around "

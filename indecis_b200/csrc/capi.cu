@@ -331,15 +331,17 @@ int scan_offsets(const int64_t *offs, int nseq, int64_t *rows, int *max_len) {
   return 0;
 }
 
-int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2]) {
+// host_rows: also the row -> sequence and position tables on the host (the
+// encoder paths fill them on the device from the offsets instead).
+int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2], bool host_rows = false) {
   int64_t N = 0;
   int ml = 0;
   IG_TRY(scan_offsets(offs, nseq, &N, &ml));
   p.nseq = nseq;
   p.N = (int)N;
   p.offs.resize(nseq + 1);
-  p.row_seq.resize(N);
-  p.pos.resize(N);
+  p.row_seq.resize(host_rows ? N : 0);
+  p.pos.resize(host_rows ? N : 0);
   for (int k = 0; k < 2; k++) {
     p.tc[k].clear();
     p.v1[k].clear();
@@ -351,10 +353,11 @@ int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2]) {
     p.offs[s] = (int32_t)offs[s];
     const int n = (int)(offs[s + 1] - offs[s]);
     p.max_len = std::max(p.max_len, n);
-    for (int t = 0; t < n; t++) {
-      p.row_seq[offs[s] + t] = s;
-      p.pos[offs[s] + t] = t;
-    }
+    if (host_rows)
+      for (int t = 0; t < n; t++) {
+        p.row_seq[offs[s] + t] = s;
+        p.pos[offs[s] + t] = t;
+      }
     for (int i0 = 0; i0 < n; i0 += 64) p.fb.push_back(make_int2(s, i0));
     for (int k = 0; k < 2; k++) {
       if (windows[k] < -1) continue;
@@ -472,10 +475,9 @@ int acquire_ws_sized(ig_model *m, size_t rows, size_t seqs, size_t blks, size_t 
   return 0;
 }
 
-// Pinned staging bytes of a plan's upload (offsets, row -> sequence,
-// positions, ids, block lists).
+// Pinned staging bytes of a plan's upload (offsets, ids, block lists).
 size_t plan_host_bytes(const Plan &p) {
-  return sizeof(int32_t) * (p.nseq + 1 + 3 * (size_t)p.N) + p.block_bytes() + 64;
+  return sizeof(int32_t) * (p.nseq + 1 + (size_t)p.N) + p.block_bytes() + 64;
 }
 
 int acquire_ws(ig_model *m, const Plan &p, size_t tl, size_t pl, cudaStream_t st, bool capturing, Workspace **out) {
@@ -488,19 +490,17 @@ void release_ws(ig_model *m, Workspace *w, cudaStream_t st, bool capturing) {
   m->pool.emplace_back(w);
 }
 
-// Uploads the plan's metadata (offsets, row -> sequence, positions, query
-// blocks, and optionally the host ids) through the pinned staging at
-// host_off, one copy per device region.
-int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream_t st, size_t host_off = 0) {
-  char *h = reinterpret_cast<char *>(w.host) + host_off;
+// Uploads the plan's metadata (offsets, query blocks, and optionally the host
+// ids) through the pinned staging, one copy per device region, and fills the
+// row -> sequence and position tables on the device from the offsets.
+int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream_t st, bool capturing = false) {
+  char *h = reinterpret_cast<char *>(w.host);
   size_t off = 0;
   auto put = [&](const void *src, size_t bytes) {
     std::memcpy(h + off, src, bytes);
     off += bytes;
   };
   put(p.offs.data(), sizeof(int32_t) * (p.nseq + 1));
-  put(p.row_seq.data(), sizeof(int32_t) * p.N);
-  put(p.pos.data(), sizeof(int32_t) * p.N);
   for (int k = 0; k < 2; k++) put(p.tc[k].data(), 16 * p.tc[k].size());
   for (int k = 0; k < 2; k++) put(p.v1[k].data(), 8 * p.v1[k].size());
   put(p.fb.data(), 8 * p.fb.size());
@@ -511,10 +511,8 @@ int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream
   IG_CU(cudaMemcpyAsync(w.offs, h + o, sizeof(int32_t) * (p.nseq + 1), cudaMemcpyHostToDevice, st));
   o += sizeof(int32_t) * (p.nseq + 1);
   if (p.N) {
-    IG_CU(cudaMemcpyAsync(w.row_seq, h + o, sizeof(int32_t) * p.N, cudaMemcpyHostToDevice, st));
-    o += sizeof(int32_t) * p.N;
-    IG_CU(cudaMemcpyAsync(w.pos, h + o, sizeof(int32_t) * p.N, cudaMemcpyHostToDevice, st));
-    o += sizeof(int32_t) * p.N;
+    ProfScope ps("plan_rows", 8.0 * p.N + 4.0 * (p.nseq + 1), 0, 1, st, capturing);
+    IG_TRY(launch_fill_rows(w.offs, p.nseq, w.row_seq, w.pos, st));
   }
   const size_t bb = p.block_bytes();
   if (bb) IG_CU(cudaMemcpyAsync(w.blocks, h + o, bb, cudaMemcpyHostToDevice, st));
@@ -1243,7 +1241,7 @@ int ig_encode_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int
   IG_TRY(ensure_rope(m, p.max_len));
   Workspace *w = nullptr;
   IG_TRY(acquire_ws(m, p, 0, 0, st, capturing, &w));
-  int rc = upload_plan(*w, p, nullptr, st);
+  int rc = upload_plan(*w, p, nullptr, st, capturing);
   if (!rc) rc = run_encoder(m, *w, d_ids, p, mode, st, nullptr, capturing);
   if (!rc && p.N) {
     const size_t H = m->H;
@@ -1274,7 +1272,7 @@ int ig_logits_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int
   IG_TRY(ensure_rope(m, p.max_len));
   Workspace *w = nullptr;
   IG_TRY(acquire_ws(m, p, 0, 0, st, capturing, &w));
-  int rc = upload_plan(*w, p, nullptr, st);
+  int rc = upload_plan(*w, p, nullptr, st, capturing);
   if (!rc) rc = run_encoder(m, *w, d_ids, p, IG_MODE_POOLED, st, nullptr, capturing);
   if (!rc) rc = run_heads(m, *w, p, st, d_logits, d_token_logits, capturing);
   release_ws(m, w, st, capturing);
@@ -1404,7 +1402,7 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
   if (!qkv || !ctx || !offs || heads <= 0 || hidden % heads) return fail(IG_ERR_BAD_ARG, "bad argument");
   Plan p;
   const int win[2] = {window < 0 ? -1 : window, -2};
-  IG_TRY(make_plan(offs, nseq, p, win));
+  IG_TRY(make_plan(offs, nseq, p, win, true));
   if (p.N == 0) return 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const size_t N = p.N, nh = heads, D = hidden / heads;

@@ -85,6 +85,9 @@ int launch_embed_checked(const int32_t *ids, int vocab, const EmbTable &emb, con
 // Per-row quantization of f32 rows (ld elements apart).
 int launch_quant_rows(const float *x, int ldx, int M, int K, uint8_t *q, int ldq, float *sa, cudaStream_t st);
 // Mean (float64, token order) or first-token pooling.
+// Row -> sequence and position within it of every row of a batch, from its
+// int32 offsets (one CTA per sequence).
+int launch_fill_rows(const int32_t *offs, int nseq, int32_t *row_seq, int32_t *pos, cudaStream_t st);
 int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, float *out, cudaStream_t st);
 // Head logits in float64: z[t][r] = sum_i w[r][i] x[t][i] + b[r] (heads.go:62-74).
 int launch_head_logits(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z,

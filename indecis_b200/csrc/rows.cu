@@ -303,6 +303,21 @@ int launch_quant_rows(const float *x, int ldx, int M, int K, uint8_t *q, int ldq
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 
+__global__ void fill_rows_kernel(const int32_t *__restrict__ offs, int32_t *__restrict__ row_seq,
+                                 int32_t *__restrict__ pos) {
+  const int s = blockIdx.x, t0 = offs[s], n = offs[s + 1] - t0;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    row_seq[t0 + t] = s;
+    pos[t0 + t] = t;
+  }
+}
+
+int launch_fill_rows(const int32_t *offs, int nseq, int32_t *row_seq, int32_t *pos, cudaStream_t st) {
+  if (nseq <= 0) return 0;
+  fill_rows_kernel<<<nseq, 128, 0, st>>>(offs, row_seq, pos);
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
 int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, float *out, cudaStream_t st) {
   if (nseq <= 0) return 0;
   pool_kernel<<<nseq, 256, 0, st>>>(xn, offs, H, cls, out);
