@@ -86,7 +86,11 @@ def emit(line: dict):
 
 
 class Clocks:
-    """nvidia-smi samples of one GPU during the timed region."""
+    """Clock samples of one GPU during the timed region: NVML read every 20 ms
+    from a thread (so short timed regions get samples too), else nvidia-smi
+    every 100 ms. Reads only; no setting of the GPU is changed."""
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    NVML_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -94,8 +98,30 @@ class Clocks:
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.p = None
+        self.thread = None
+
+    def _nvml_loop(self, h, nv):
+        while not self.halt.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except Exception:
+                pass
+            self.halt.wait(0.02)
 
     def start(self):
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.samples, self.halt = [], threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(h, nv), daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                        "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
@@ -104,6 +130,14 @@ class Clocks:
             self.p = None
 
     def stop(self):
+        if self.thread is not None:
+            self.halt.set()
+            self.thread.join()
+            if not self.samples:
+                return None
+            reasons = sorted({n for _, r in self.samples for n, b in self.NVML_BITS.items() if r & b})
+            return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
         if self.p is None:
             return None
         self.p.terminate()
