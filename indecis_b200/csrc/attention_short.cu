@@ -25,7 +25,10 @@
 //      scalar-tail keys recomputed by tail_fixup, sp) into P; warp 0 issues
 //      O = P.V (V as an MN-major operand) over S's columns; the warps stage
 //      ctx = (float(acc)*vs)*sp in shared memory and store it with
-//      row-contiguous 16-byte writes.
+//      row-contiguous 16-byte writes; or, launched as one cluster per
+//      sequence, quantize ctx per row over the cluster's heads (row maxima
+//      exchanged through distributed shared memory) and store the int8 row
+//      pieces and the row scales instead.
 // Every float operation is the one attn_prep_* and attn_tc_kernel perform, in
 // the same order, so the results are the same bits.
 #include <cuda.h>
@@ -140,7 +143,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
     attn_short_kernel(const __grid_constant__ CUtensorMap mqkv, const float *__restrict__ qkv,
                       const int32_t *__restrict__ offs, int H, int nh, int window, int V, float scale,
                       const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
-                      float *__restrict__ ctx) {
+                      float *__restrict__ ctx, uint8_t *__restrict__ xq, int ldq, float *__restrict__ sa) {
   using S = AttnShortSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -502,6 +505,67 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   uint32_t o[32];
   tmem_ld_32x32b_x32(tbase + 32 * g, o);
   tmem_ld_wait();
+  if (xq != nullptr) {
+    // ctx quantized per row over all heads (the launch's cluster holds the
+    // sequence's nh heads, one CTA each): quant_rows4_kernel's arithmetic on
+    // the row maximum, gathered through distributed shared memory.
+    const float *vsc = s_vs + 32 * g;
+    float v[32], pn = 0.0f, pi = 0.0f;  // NaN-propagating / NaN-ignoring |maximum|
+#pragma unroll
+    for (int d = 0; d < 32; d++) {
+      v[d] = dequant_o(o[d], vsc[d], sp);
+      pn = fmax_nan(pn, fabsf(v[d]));
+      pi = fmaxf(pi, fabsf(v[d]));
+    }
+    float *xn = reinterpret_cast<float *>(smem + S::kO);  // [2][128] per half row
+    float *xi = xn + 256;
+    float *cn = xi + 256, *ci = cn + 128;  // [128] this CTA's row maxima
+    xn[g * 128 + r] = pn;
+    xi[g * 128 + r] = pi;
+    __syncthreads();
+    if (tid < 128) {
+      cn[tid] = fmax_nan(xn[tid], xn[128 + tid]);
+      ci[tid] = fmaxf(xi[tid], xi[128 + tid]);
+    }
+    cluster_sync_all();
+    float mn = 0.0f, mi = 0.0f;
+    for (int c = 0; c < nh; c++) {
+      mn = fmax_nan(mn, ld_dsmem_f32(cn + r, (uint32_t)c));
+      mi = fmaxf(mi, ld_dsmem_f32(ci + r, (uint32_t)c));
+    }
+    const bool has_nan = mn != mn;
+    const float mx = has_nan ? mi : mn;
+    float qs = 0.0f, qinv = 0.0f;
+    if (mx > 0.0f) {
+      qs = __fdiv_rn(mx, 127.0f);
+      qinv = __fdiv_rn(1.0f, qs);
+    }
+    const bool fast = !has_nan && row_scale_normal(qs), store = ok && valid;
+    uint4 *dst = reinterpret_cast<uint4 *>(xq + (size_t)(t0 + r) * ldq + h * 64 + 32 * g);
+#pragma unroll
+    for (int hf = 0; hf < 2; hf++) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float *x4 = v + 16 * hf + 4 * k;
+        if (mx == 0.0f)
+          wv[k] = 0x80808080u;
+        else if (fast)
+          wv[k] = quant4_fast(x4[0], x4[1], x4[2], x4[3], f2(qinv), f2(qinv));
+        else
+          wv[k] = quant_byte_slow(x4[0], qinv) | (quant_byte_slow(x4[1], qinv) << 8) |
+                  (quant_byte_slow(x4[2], qinv) << 16) | (quant_byte_slow(x4[3], qinv) << 24);
+      }
+      if (store) dst[hf] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+    if (store && h == 0 && g == 0) sa[t0 + r] = qs;
+    cluster_sync_all();  // no CTA leaves while the others read its maxima
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem, 128);
+    }
+    return;
+  }
   // Stage the row's 32 dimensions, then copy the valid rows out with each
   // row's 256 bytes written contiguously.
   float *ostage = reinterpret_cast<float *>(smem + S::kO);
@@ -556,9 +620,36 @@ int launch_attn_short(const AttnArgs &a, cudaStream_t st) {
       return IG_ERR_CUDA;
     attr = true;
   }
+  if (a.xq) {
+    if (!attn_short_quantizes(a)) return IG_ERR_UNSUPPORTED;
+    // One cluster per sequence: its nh head CTAs share the row maxima.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(a.nseq, a.nh);
+    cfg.blockDim = dim3(kShortThreads);
+    cfg.dynamicSmemBytes = AttnShortSmem::kTotal;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = a.nh;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, attn_short_kernel, map, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos,
+                           a.rope_sin, a.ctx, a.xq, a.ldq, a.sa) != cudaSuccess)
+      return IG_ERR_CUDA;
+    return 0;
+  }
   attn_short_kernel<<<dim3(a.nseq, a.nh), kShortThreads, AttnShortSmem::kTotal, st>>>(
-      map, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos, a.rope_sin, a.ctx);
+      map, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos, a.rope_sin, a.ctx, nullptr, 0, nullptr);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
+// The row quantization needs the whole row in one cluster (nh <= 8 CTAs, a
+// portable cluster size), H = nh * 64, and 16-byte aligned row pieces.
+bool attn_short_quantizes(const AttnArgs &a) {
+  return attn_short_fits(a) && a.nh >= 1 && a.nh <= 8 && a.H == a.nh * 64 && a.xq && a.sa && (a.ldq % 16) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.xq) & 15) == 0;
 }
 
 }  // namespace ig

@@ -694,9 +694,23 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
     at.window = global ? -1 : c.local_attention / 2;
     at.rope_cos = m->rope_cos[global ? 0 : 1];
     at.rope_sin = m->rope_sin[global ? 0 : 1];
+    // ctx quantized inside the short-sequence kernel unless this layer is dumped.
+    at.xq = nullptr;
+    at.sa = nullptr;
+    bool ctx_quantized = false;
+    if (attn_short_fits(at) && !dl) {
+      AttnArgs aq = at;
+      aq.xq = w.xq;
+      aq.ldq = m->ldk;
+      aq.sa = w.sa;
+      ctx_quantized = attn_short_quantizes(aq);
+      if (ctx_quantized) at = aq;
+    }
     if (attn_short_fits(at)) {
       const double pairs = attn_pairs(p, at.window);
-      ProfScope ps("attn_short", (double)N * H * 4 * 4 + 8.0 * N * 32, 4.0 * pairs * m->D * m->nh, 1, st, capturing);
+      const double out_bytes = ctx_quantized ? (double)N * H + 4.0 * N : 4.0 * N * H;
+      ProfScope ps(ctx_quantized ? "attn_short_quant" : "attn_short", (double)N * H * 4 * 3 + out_bytes + 8.0 * N * 32,
+                   4.0 * pairs * m->D * m->nh, 1, st, capturing);
       IG_TRY(launch_attn_short(at, st));
     } else {
       {
@@ -714,7 +728,7 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       }
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->ctx, w.ctx, H * 4, H * 4, N, st));
-    {
+    if (!ctx_quantized) {
       ProfScope ps("quant_rows", (double)N * (5.0 * H + 4), 0, 1, st, capturing);
       IG_TRY(launch_quant_rows(w.ctx, H, N, H, w.xq, m->ldk, w.sa, st));
     }

@@ -122,8 +122,15 @@ struct AttnArgs {
   const int32_t *row_seq;  // [N] sequence of each row
   int N;
   float *ctx;           // [N][H] output
-  // optional int32 dumps (parity): none in the hot path
+  // Optional (the fused short-sequence kernel, nh <= 8): instead of ctx, its
+  // per-row int8 quantization (quant_rows over all heads of a row: bytes
+  // q + 128 into xq with row pitch ldq, scales into sa).
+  uint8_t *xq = nullptr;
+  int ldq = 0;
+  float *sa = nullptr;
 };
+// Whether launch_attn_short can quantize ctx itself (AttnArgs::xq).
+bool attn_short_quantizes(const AttnArgs &a);
 int launch_attention(const AttnArgs &a, cudaStream_t st);
 int launch_attend(const AttnArgs &a, const int2 *d_blocks, int nblocks, cudaStream_t st);
 int attn_query_block();
