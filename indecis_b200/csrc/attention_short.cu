@@ -27,7 +27,7 @@
 //      ctx = (float(acc)*vs)*sp in shared memory and store it with
 //      row-contiguous 16-byte writes; or, launched as one cluster per
 //      sequence, quantize ctx per row over the cluster's heads (row maxima
-//      exchanged through distributed shared memory) and store the int8 row
+//      pushed to every CTA of the cluster through shared memory) and store the int8 row
 //      pieces and the row scales instead.
 // Every float operation is the one attn_prep_* and attn_tc_kernel perform, in
 // the same order, so the results are the same bits.
@@ -67,7 +67,8 @@ struct AttnShortSmem {
   static constexpr int kVinv = kVs + 256;   // 64
   static constexpr int kBar = kVinv + 256;  // 4 mbarriers
   static constexpr int kTmem = kBar + 32;   // TMEM base address; V fast-path flag at +4
-  static constexpr int kTotal = kTmem + 16 + 1024;
+  static constexpr int kXch = kTmem + 16;   // [8][128] row maxima of the cluster's CTAs (ctx quantization)
+  static constexpr int kTotal = kXch + 8 * 128 * 4 + 1024;
   static_assert(kO + 128 * kOPitch * 4 <= kRed, "ctx staging overlaps the exchange");
   static_assert(kShortCtasPerSm * (kTotal + 1024) <= 228 * 1024, "three CTAs per SM");
 };
@@ -107,6 +108,9 @@ __device__ __forceinline__ void rope4(float4 &lo, float4 &hi, float4 c, float4 s
 __device__ __forceinline__ float dequant_o(uint32_t acc, float vs, float sp) {
   return __fmul_rn(__fmul_rn(__fsub_rn(magic_float((int32_t)acc), kMagic), vs), sp);
 }
+
+// x with its sign bit set.
+__device__ __forceinline__ float neg_bits(float x) { return __int_as_float(__float_as_int(x) | 0x80000000); }
 
 // The low bytes of four words as one word (byte k from word k).
 __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -508,33 +512,41 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   if (xq != nullptr) {
     // ctx quantized per row over all heads (the launch's cluster holds the
     // sequence's nh heads, one CTA each): quant_rows4_kernel's arithmetic on
-    // the row maximum, gathered through distributed shared memory.
+    // the row maximum, each CTA's part pushed to every CTA of the cluster
+    // through distributed shared memory.
     const float *vsc = s_vs + 32 * g;
-    float v[32], pn = 0.0f, pi = 0.0f;  // NaN-propagating / NaN-ignoring |maximum|
+    // Row maxima travel as |maximum| over the non-NaN values with the sign
+    // bit set where a NaN was seen: the NaN-propagating maximum is NaN
+    // exactly then, and otherwise equals the other.
+    float v[32], pi = 0.0f;
+    bool pnan = false;
 #pragma unroll
     for (int d = 0; d < 32; d++) {
       v[d] = dequant_o(o[d], vsc[d], sp);
-      pn = fmax_nan(pn, fabsf(v[d]));
       pi = fmaxf(pi, fabsf(v[d]));
+      pnan |= v[d] != v[d];
     }
-    float *xn = reinterpret_cast<float *>(smem + S::kO);  // [2][128] per half row
-    float *xi = xn + 256;
-    float *cn = xi + 256, *ci = cn + 128;  // [128] this CTA's row maxima
-    xn[g * 128 + r] = pn;
-    xi[g * 128 + r] = pi;
+    float *xh = reinterpret_cast<float *>(smem + S::kO);  // [2][128] per half row
+    float *gx = reinterpret_cast<float *>(smem + S::kXch);  // [8][128] per cluster CTA, pushed by it
+    xh[g * 128 + r] = pnan ? neg_bits(pi) : pi;
     __syncthreads();
     if (tid < 128) {
-      cn[tid] = fmax_nan(xn[tid], xn[128 + tid]);
-      ci[tid] = fmaxf(xi[tid], xi[128 + tid]);
+      const float a = xh[tid], b = xh[128 + tid];
+      const float m = fmaxf(fabsf(a), fabsf(b));
+      const float e = (signbit(a) || signbit(b)) ? neg_bits(m) : m;
+      const uint32_t me = cluster_ctarank();
+      for (int c = 0; c < nh; c++) st_dsmem_f32(gx + me * 128 + tid, (uint32_t)c, e);
     }
+    // The exchange region is used by nothing else, and after this every CTA
+    // reads only its own shared memory, so none waits for the others to leave.
     cluster_sync_all();
-    float mn = 0.0f, mi = 0.0f;
+    float mx = 0.0f;
+    bool has_nan = false;
     for (int c = 0; c < nh; c++) {
-      mn = fmax_nan(mn, ld_dsmem_f32(cn + r, (uint32_t)c));
-      mi = fmaxf(mi, ld_dsmem_f32(ci + r, (uint32_t)c));
+      const float e = gx[c * 128 + r];
+      mx = fmaxf(mx, fabsf(e));
+      has_nan |= signbit(e);
     }
-    const bool has_nan = mn != mn;
-    const float mx = has_nan ? mi : mn;
     float qs = 0.0f, qinv = 0.0f;
     if (mx > 0.0f) {
       qs = __fdiv_rn(mx, 127.0f);
@@ -559,7 +571,6 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       if (store) dst[hf] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
     }
     if (store && h == 0 && g == 0) sa[t0 + r] = qs;
-    cluster_sync_all();  // no CTA leaves while the others read its maxima
     if (warp == 1) {
       tc_fence_after();
       tmem_dealloc(tmem, 128);

@@ -49,13 +49,11 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// A float of CTA `rank`'s shared memory at the offset of p in this CTA's.
-__device__ __forceinline__ float ld_dsmem_f32(const void *p, uint32_t rank) {
+// Stores v into CTA `rank`'s shared memory at the offset of p in this CTA's.
+__device__ __forceinline__ void st_dsmem_f32(void *p, uint32_t rank, float v) {
   uint32_t a;
-  float v;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
-  return v;
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
