@@ -286,6 +286,7 @@ def run_reference(args, world, rank):
 # this times the sequences per step (traffic grows with the sequences).
 NCU_BYTES_PER_SEQ = {
     "attn_short": (201441536 + 38391040) / 512,
+    "attn_short_quant": (201448192 + 11332864) / 512,
     "gemm_qkv": (21466368 + 145374976) / 512,
     "gemm_wo_residual": (88436736 + 11129856) / 512,
     "gemm_wi_geglu": (21517824 + 42096384) / 512,
