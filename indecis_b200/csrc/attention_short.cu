@@ -109,6 +109,17 @@ __device__ __forceinline__ float dequant_o(uint32_t acc, float vs, float sp) {
   return __fmul_rn(__fmul_rn(__fsub_rn(magic_float((int32_t)acc), kMagic), vs), sp);
 }
 
+// max(0, |v[0]|, ..., |v[31]|), NaN-propagating (PROP) or NaN-ignoring, as a
+// tree of four chains: both maxima are associative (max.NaN returns the
+// canonical NaN), so the value is the one chain's.
+template <bool PROP>
+__device__ __forceinline__ float absmax32(const float (&v)[32]) {
+  float m[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int u = 0; u < 32; u++) m[u & 3] = PROP ? fmax_nan(m[u & 3], fabsf(v[u])) : fmaxf(m[u & 3], fabsf(v[u]));
+  return PROP ? fmax_nan(fmax_nan(m[0], m[1]), fmax_nan(m[2], m[3])) : fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
 // x with its sign bit set.
 __device__ __forceinline__ float neg_bits(float x) { return __int_as_float(__float_as_int(x) | 0x80000000); }
 
@@ -219,15 +230,11 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   {
     // Row maximum, NaN-propagating first: a row holding a NaN takes the
     // clamped path (with the NaN-ignoring maximum, as the reference's).
-    float qmx = 0.0f;
-#pragma unroll
-    for (int u = 0; u < 32; u++) qmx = fmax_nan(qmx, fabsf(qv[u]));
+    float qmx = absmax32<true>(qv);
     qmx = fmax_nan(qmx, __shfl_xor_sync(0xffffffffu, qmx, 1));
     const bool qnan = qmx != qmx;
     if (__any_sync(0xffffffffu, qnan)) {
-      qmx = 0.0f;
-#pragma unroll
-      for (int u = 0; u < 32; u++) qmx = fmaxf(qmx, fabsf(qv[u]));
+      qmx = absmax32<false>(qv);
       qmx = fmaxf(qmx, __shfl_xor_sync(0xffffffffu, qmx, 1));
     }
     const float qs = qmx > 0.0f ? __fdiv_rn(qmx, 127.0f) : 0.0f;
@@ -287,27 +294,28 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
     s_mean[tid] = __fmul_rn(acc, __fdiv_rn(1.0f, (float)n));
   } else if (tid < 128) {
     const int d = tid - 64;
-    float m[4] = {0.0f, 0.0f, 0.0f, 0.0f}, mn = 0.0f;  // NaN-ignoring, NaN-propagating
+    float m[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // NaN-ignoring maxima
+    bool nan = false;                       // a NaN in the column
     int r = 0;
     for (; r + 4 <= n; r += 4) {
 #pragma unroll
       for (int u = 0; u < 4; u++) {
         const float a = fabsf(f32_at(vf, r + u, d));
         m[u] = fmaxf(m[u], a);
-        mn = fmax_nan(mn, a);
+        nan |= a != a;
       }
     }
     for (; r < n; r++) {
       const float a = fabsf(f32_at(vf, r, d));
       m[0] = fmaxf(m[0], a);
-      mn = fmax_nan(mn, a);
+      nan |= a != a;
     }
     const float mx = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
     const float sc = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
     s_vs[d] = sc;
     s_vinv[d] = mx > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
     // vinv = 0 (a zero column): every byte is rne(v * 0).
-    if (!(mn == mn && (mx == 0.0f || scale_is_normal(sc)))) *s_vfast = 0;
+    if (nan || !(mx == 0.0f || scale_is_normal(sc))) *s_vfast = 0;
     named_barrier_sync(2, 192);  // the V scales are in shared memory
   } else {
     named_barrier_sync(2, 192);
@@ -362,15 +370,11 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       kv[4 * k] = lo.x, kv[4 * k + 1] = lo.y, kv[4 * k + 2] = lo.z, kv[4 * k + 3] = lo.w;
       kv[16 + 4 * k] = hi.x, kv[17 + 4 * k] = hi.y, kv[18 + 4 * k] = hi.z, kv[19 + 4 * k] = hi.w;
     }
-    float kmx = 0.0f;
-#pragma unroll
-    for (int u = 0; u < 32; u++) kmx = fmax_nan(kmx, fabsf(kv[u]));
+    float kmx = absmax32<true>(kv);
     kmx = fmax_nan(kmx, __shfl_xor_sync(0xffffffffu, kmx, 1));
     const bool knan = kmx != kmx;
     if (__any_sync(0xffffffffu, knan)) {
-      kmx = 0.0f;
-#pragma unroll
-      for (int u = 0; u < 32; u++) kmx = fmaxf(kmx, fabsf(kv[u]));
+      kmx = absmax32<false>(kv);
       kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, 1));
     }
     const float kss = kmx > 0.0f ? __fdiv_rn(kmx, 127.0f) : 0.0f;
@@ -380,12 +384,17 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
     if (kmx == 0.0f) {  // a zero key: zero bytes, scale and sum (attention8.go:240-251)
 #pragma unroll
       for (int k = 0; k < 8; k++) kw[k] = 0u;
-    } else if (!slow) {  // bytes are x itself: sum them as signed bytes
+    } else if (!slow) {  // bytes are x itself: sum them as signed bytes (two exact integer chains)
+      int ks2 = 0;
 #pragma unroll
       for (int k = 0; k < 8; k++) {
         kw[k] = quant4_fast_s8(kv[4 * k], kv[4 * k + 1], kv[4 * k + 2], kv[4 * k + 3], f2(kinv), f2(kinv));
-        ksum = dp4a_ss(kw[k], 0x01010101u, ksum);
+        if (k & 1)
+          ks2 = dp4a_ss(kw[k], 0x01010101u, ks2);
+        else
+          ksum = dp4a_ss(kw[k], 0x01010101u, ksum);
       }
+      ksum += ks2;
     } else {  // the reference's conversion (NaN -> INT_MIN, summed before the clamp)
 #pragma unroll
       for (int k = 0; k < 8; k++) {

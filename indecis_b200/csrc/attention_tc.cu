@@ -196,21 +196,28 @@ __device__ __noinline__ int tail_fixup(const uint8_t *qtile, const uint8_t *ktil
                                        int r, int g, int t0, int t1, const float *zcm, const float *ks, float sq,
                                        float mx) {
   int dsum = 0;  // change of the row's P sum
-  for (int c = t0; c < t1; c++) {
-    if (((c >> 4) & 1) != g) continue;
+  if (t0 >= t1) return 0;
+  uint4 qa4[4];
+  const uint8_t *qrow = qtile + r * 64;
+#pragma unroll
+  for (int ch = 0; ch < 4; ch++) qa4[ch] = *reinterpret_cast<const uint4 *>(qrow + ((ch ^ ((r >> 1) & 3)) << 4));
+  // The tail keys in this thread's 16-key chunks (parity g), chunk by chunk.
+  int ck = t0 >> 4;
+  ck += (ck & 1) != g;
+  for (int c = max(t0, 16 * ck); c < t1; c = (c & 15) == 15 ? c + 17 : c + 1) {
     const int kt = c >> 7, kr = c & 127;
-    const uint8_t *qrow = qtile + r * 64;
     const uint8_t *krow = ktile + kt * ktile_bytes + kr * 64;
-    int acc = 0;
+    int part[4] = {0, 0, 0, 0};  // four exact integer chains, summed after
 #pragma unroll
     for (int ch = 0; ch < 4; ch++) {
-      const uint4 qa = *reinterpret_cast<const uint4 *>(qrow + ((ch ^ ((r >> 1) & 3)) << 4));
+      const uint4 qa = qa4[ch];
       const uint4 kb = *reinterpret_cast<const uint4 *>(krow + ((ch ^ ((kr >> 1) & 3)) << 4));
-      acc = dp4a_us(qa.x, kb.x, acc);
-      acc = dp4a_us(qa.y, kb.y, acc);
-      acc = dp4a_us(qa.z, kb.z, acc);
-      acc = dp4a_us(qa.w, kb.w, acc);
+      part[ch] = dp4a_us(qa.x, kb.x, part[ch]);
+      part[ch] = dp4a_us(qa.y, kb.y, part[ch]);
+      part[ch] = dp4a_us(qa.z, kb.z, part[ch]);
+      part[ch] = dp4a_us(qa.w, kb.w, part[ch]);
     }
+    const int acc = (part[0] + part[1]) + (part[2] + part[3]);
     const float sc = __fmul_rn(__fmul_rn(__fsub_rn(magic_float(acc), zcm[c]), ks[c]), sq);
     const int p = __float2int_rn(__fmul_rn(exp_tail(__fsub_rn(sc, mx)), 255.0f));
     uint8_t *pb = ptile + kt * 16384 + r * 128 + ((((c & 127) >> 4) ^ (r & 7)) << 4) + (c & 15);

@@ -67,10 +67,13 @@ float exp_body(float v) {
   return under ? 0.0f : y * pw;
 }
 
+// The widest SIMD width a configuration may name (simd_lanes in [1, 32]).
+constexpr int kMaxLanes = 32;
+
 // linalg/vec_simd.go:216-264 ExpShift: x[i] = exp(x[i]-m); lanes in V-wide
 // blocks use the FMA body, the tail (n mod V) uses exp32. Returns the sum.
 float exp_shift(float *x, int n, float m, int V) {
-  float lanes[16] = {0};
+  float lanes[kMaxLanes] = {0};
   int i = 0;
   for (; i + V <= n; i += V) {
     for (int k = 0; k < V; k++) {
@@ -148,7 +151,7 @@ void gelu_mul(float *o, const float *a, const float *b, int n) {
 
 // linalg/vec_simd.go:281-327 LayerNormRow with V float32 lanes.
 void layernorm_row(float *o, const float *x, const float *gamma, int n, double eps, int V) {
-  float lanes[16] = {0};
+  float lanes[kMaxLanes] = {0};
   int i = 0;
   for (; i + V <= n; i += V)
     for (int k = 0; k < V; k++) lanes[k] += x[i + k];
@@ -156,7 +159,7 @@ void layernorm_row(float *o, const float *x, const float *gamma, int n, double e
   for (int k = 0; k < V; k++) sum += (double)lanes[k];
   for (; i < n; i++) sum += (double)x[i];
   const float mean = (float)(sum / (double)n);
-  float sq[16] = {0};
+  float sq[kMaxLanes] = {0};
   i = 0;
   for (; i + V <= n; i += V)
     for (int k = 0; k < V; k++) {

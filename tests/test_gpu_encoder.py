@@ -222,3 +222,19 @@ def test_host_staged_outputs_match_device(igdev):
         got = np.concatenate(got) if isinstance(got, list) else got
         assert np.array_equal(_bits(got), _bits(d_out.cpu().numpy())), mode
     gm.close()
+
+
+@pytest.mark.parametrize("lanes", [16, 32])
+def test_simd_lanes_bitexact(igdev, oracle_lib, lanes):
+    """ExpShift and LayerNorm at 16 and 32 float32 lanes (an AVX-512 or wider
+    reference build): the softmax's scalar tail then holds up to lanes - 1
+    keys per row, spanning several 16-key chunks of the attention kernels;
+    short and long, local and global sequences, bit-exact."""
+    from indecis_b200 import synthetic as S
+    cfg = S.tiny(layers=3, hidden=256, heads=4, intermediate=384, vocab=1000)
+    cfg["V"] = lanes
+    om, gm, _ = _models(cfg, seed=7)
+    ids, offs = S.ids_varlen(12, 1, 300, cfg["vocab"], seed=lanes)
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(om.encode(ids, offs)))
+    assert np.array_equal(_bits(gm.EncodeTokens((ids, offs))), _bits(om.encode(ids, offs, mode=1)))
+    gm.close()

@@ -53,6 +53,24 @@ def test_exp_shift_body_and_tail(oracle_lib):
         assert abs(s - e.astype(np.float64).sum()) <= 1e-5 * e.sum()
 
 
+@pytest.mark.parametrize("V", [1, 16, 32])
+def test_lane_widths(oracle_lib, V):
+    """The lane chains at every width a config may name (simd_lanes 1..32):
+    ExpShift's body sums lane by lane, LayerNorm's mean and variance too;
+    each stays within float32 accuracy of float64."""
+    rng = np.random.default_rng(V)
+    for n in (V - 1 if V > 1 else 1, 2 * V + 5, 129):
+        x = rng.uniform(-20, 0, n).astype(np.float32)
+        e, s = oracle_lib.exp_shift(x, 0.0, V)
+        assert np.allclose(e, np.exp(x.astype(np.float64)), rtol=5e-7, atol=0)
+        assert abs(s - e.astype(np.float64).sum()) <= 1e-5 * e.sum()
+        xr = rng.standard_normal((3, n)).astype(np.float32)
+        o = oracle_lib.layernorm(xr, np.ones(n, np.float32), V=V)
+        d = xr.astype(np.float64)
+        want = (d - d.mean(1, keepdims=True)) / np.sqrt(d.var(1, keepdims=True) + 1e-5)
+        assert np.abs(o - want).max() <= 1e-4
+
+
 @pytest.mark.parametrize("n", [1, 7, 16, 37, 384, 1153])
 def test_vector_ops(oracle_lib, n):
     """linalg/vec_test.go:9 TestVectorOps: AbsMax exact, QuantizeRow exact,
