@@ -172,6 +172,8 @@ struct Workspace {
   void *ohost = nullptr;  // pinned staging of a host call's large outputs
   size_t ohost_bytes = 0;
   std::vector<cudaEvent_t> pev;  // one per staged piece: its device-to-host copy finished
+  std::vector<cudaEvent_t> cev;  // one per output chunk: computed on own_stream
+  cudaStream_t copy_stream = nullptr;  // device-to-host copies that overlap the last kernels
   cudaStream_t own_stream = nullptr;
   cudaEvent_t done = nullptr;
   int32_t *ids, *offs, *row_seq, *pos;
@@ -186,6 +188,8 @@ struct Workspace {
     if (host) cudaFreeHost(host);
     if (ohost) cudaFreeHost(ohost);
     for (cudaEvent_t e : pev) cudaEventDestroy(e);
+    for (cudaEvent_t e : cev) cudaEventDestroy(e);
+    if (copy_stream) cudaStreamDestroy(copy_stream);
     if (done) cudaEventDestroy(done);
     if (own_stream) cudaStreamDestroy(own_stream);
   }
@@ -565,7 +569,7 @@ double attn_pairs(const Plan &p, int window) {
 // The float32 path (run without SetInt8, infer.go:304-430): float products
 // in the reference's chain order, RoPE in place, attendBlocks, GeluMul.
 int run_encoder_f32(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, int mode, cudaStream_t st,
-                    bool capturing) {
+                    bool capturing, bool tail) {
   const ig_config &c = m->cfg;
   const int H = m->H, I = m->I, N = p.N, V = c.simd_lanes;
   if (!w.zf) return fail(IG_ERR_BAD_ARG, "workspace without the float buffers");
@@ -617,6 +621,7 @@ int run_encoder_f32(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan 
     }
     IG_TRY(product("f32_gemm_womlp", w.g, I, L.fwom, H, w.x, true));
   }
+  if (!tail) return 0;  // the final norm and pooling are left to the caller
   {
     ProfScope ps("ln_final", (double)N * 8.0 * H + 4.0 * H, 0, 1, st, capturing);
     IG_TRY(launch_ln_quant(w.x, m->final_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
@@ -628,15 +633,17 @@ int run_encoder_f32(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan 
   return 0;
 }
 
+// tail = false stops before the final norm and the pooling (the caller runs
+// them, e.g. in row chunks whose outputs are copied out as they finish).
 int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, int mode, cudaStream_t st,
-                ig_dump *dump, bool capturing = false) {
+                ig_dump *dump, bool capturing = false, bool tail = true) {
   const ig_config &c = m->cfg;
   const int H = m->H, I = m->I, N = p.N;
   const int V = c.simd_lanes;
   if (N == 0) return 0;
   if (m->f32) {
     if (dump) return fail(IG_ERR_UNSUPPORTED, "the per-layer dump is of the int8 path");
-    return run_encoder_f32(m, w, d_ids, p, mode, st, capturing);
+    return run_encoder_f32(m, w, d_ids, p, mode, st, capturing, tail);
   }
   {
     ProfScope ps("embed_ln_quant", (double)N * (8 + 9.0 * H) + 4.0 * H, 0, 1, st, capturing);
@@ -792,6 +799,7 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->x_mlp, w.x, H * 4, H * 4, N, st));
   }
+  if (!tail) return 0;  // the final norm and pooling are left to the caller
   {
     ProfScope ps("ln_final", (double)N * 8.0 * H + 4.0 * H, 0, 1, st, capturing);
     IG_TRY(launch_ln_quant(w.x, m->final_norm, N, H, c.norm_eps, V, w.xn, nullptr, 0, nullptr, st));
@@ -962,6 +970,103 @@ int copy_out_staged(Workspace &w, cudaStream_t st, const std::vector<OutCopy> &o
   return 0;
 }
 
+// The encoder's tail when per-token logits go to the host: the final norm and
+// the per-token heads run in row chunks on st, and each chunk's logits are
+// copied out on the workspace's copy stream as soon as they exist, so the
+// copies overlap the later chunks' kernels; then the pooling, the pooled
+// heads and their copy. Returns once every output is in the caller's memory.
+constexpr int kTailChunks = 4;
+constexpr int kTailMinRows = 16384;
+
+int run_tail_staged(ig_model *m, Workspace &w, const Plan &p, int mode, cudaStream_t st, double *logits, double *tlog,
+                    size_t pl, size_t tl) {
+  const ig_config &c = m->cfg;
+  const int H = m->H, N = p.N;
+  std::vector<DevHead> hs;
+  {
+    std::lock_guard<std::mutex> lk(m->mu);
+    hs = m->heads;
+  }
+  const size_t tbytes = sizeof(double) * (size_t)N * tl, pbytes = logits ? sizeof(double) * (size_t)p.nseq * pl : 0;
+  if (tbytes + pbytes > w.ohost_bytes) {
+    IG_CU(cudaStreamSynchronize(st));
+    if (w.ohost) IG_CU(cudaFreeHost(w.ohost));
+    w.ohost = nullptr;
+    w.ohost_bytes = 0;
+    IG_CU(cudaMallocHost(&w.ohost, tbytes + pbytes));
+    w.ohost_bytes = tbytes + pbytes;
+  }
+  if (!w.copy_stream) IG_CU(cudaStreamCreateWithFlags(&w.copy_stream, cudaStreamNonBlocking));
+  while ((int)w.cev.size() < kTailChunks + 2) {
+    cudaEvent_t e;
+    IG_CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    w.cev.push_back(e);
+  }
+  while ((int)w.pev.size() < kTailChunks + 1) {
+    cudaEvent_t e;
+    IG_CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    w.pev.push_back(e);
+  }
+  char *stage = static_cast<char *>(w.ohost);
+  const int per = (int)align_up((size_t)(N + kTailChunks - 1) / kTailChunks, 32);
+  struct Piece {
+    void *dst;
+    size_t at, bytes;
+  };
+  std::vector<Piece> ps;
+  for (int r0 = 0; r0 < N; r0 += per) {
+    const int r1 = std::min(N, r0 + per), n = r1 - r0;
+    {
+      ProfScope pr("ln_final", (double)n * 8.0 * H + 4.0 * H, 0, 1, st);
+      IG_TRY(launch_ln_quant(w.x + (size_t)r0 * H, m->final_norm, n, H, c.norm_eps, c.simd_lanes, w.xn + (size_t)r0 * H,
+                             nullptr, 0, nullptr, st));
+    }
+    size_t to = 0;
+    for (auto &h : hs) {
+      if (!h.per_token) continue;
+      ProfScope pr("head_logits", (double)n * (4.0 * H + 8.0 * h.rows), 2.0 * n * h.rows * H, 1, st);
+      IG_TRY(launch_head_logits(h.w, h.b, h.rows, H, w.xn + (size_t)r0 * H, n, w.tlogits + (size_t)r0 * tl + to,
+                                (int)tl, st));
+      to += h.rows;
+    }
+    const int k = (int)ps.size();
+    IG_CU(cudaEventRecord(w.cev[k], st));
+    IG_CU(cudaStreamWaitEvent(w.copy_stream, w.cev[k], 0));
+    const size_t at = sizeof(double) * (size_t)r0 * tl, bytes = sizeof(double) * (size_t)n * tl;
+    IG_CU(cudaMemcpyAsync(stage + at, w.tlogits + (size_t)r0 * tl, bytes, cudaMemcpyDeviceToHost, w.copy_stream));
+    IG_CU(cudaEventRecord(w.pev[k], w.copy_stream));
+    ps.push_back({reinterpret_cast<char *>(tlog) + at, at, bytes});
+  }
+  if (mode != IG_MODE_TOKENS) {
+    ProfScope pr("pool", (double)N * 4.0 * H + 4.0 * p.nseq * H, 0, 1, st);
+    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st));
+  }
+  if (logits && p.nseq && pl) {
+    size_t po = 0;
+    for (auto &h : hs) {
+      if (h.per_token) continue;
+      ProfScope pr("head_logits", (double)p.nseq * (4.0 * H + 8.0 * h.rows), 2.0 * p.nseq * h.rows * H, 1, st);
+      IG_TRY(launch_head_logits(h.w, h.b, h.rows, H, w.pooled, p.nseq, w.logits + po, (int)pl, st));
+      po += h.rows;
+    }
+    const int k = (int)ps.size();
+    IG_CU(cudaEventRecord(w.cev[k], st));
+    IG_CU(cudaStreamWaitEvent(w.copy_stream, w.cev[k], 0));
+    IG_CU(cudaMemcpyAsync(stage + tbytes, w.logits, pbytes, cudaMemcpyDeviceToHost, w.copy_stream));
+    IG_CU(cudaEventRecord(w.pev[k], w.copy_stream));
+    ps.push_back({logits, tbytes, pbytes});
+  }
+  // st waits for the copies, so the workspace is reused only after them.
+  IG_CU(cudaEventRecord(w.cev[kTailChunks + 1], w.copy_stream));
+  IG_CU(cudaStreamWaitEvent(st, w.cev[kTailChunks + 1], 0));
+  for (size_t i = 0; i < ps.size(); i++) {
+    const cudaError_t e = cudaEventSynchronize(w.pev[i]);
+    if (e != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(e));
+    CopyPool::get().copy(static_cast<char *>(ps[i].dst), stage + ps[i].at, ps[i].bytes);
+  }
+  return 0;
+}
+
 int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
                 size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len) {
   t_last_error.clear();
@@ -997,7 +1102,19 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   st = w->own_stream;
   int rc = upload_plan(*w, p, ids, st);
   const int enc_mode = (logits || tlog) ? (mode == kModeMeanRows ? kModeMeanRows : IG_MODE_POOLED) : mode;
-  if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump);
+  // Per-token logits for the host: the tail runs in chunks whose copies
+  // overlap the kernels after them.
+  const bool chunked_tail = tlog && tl && !out && !dump && p.N >= kTailMinRows && out_bytes >= kStageMinBytes;
+  if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump, false, !chunked_tail);
+  if (!rc && chunked_tail) {
+    rc = run_tail_staged(m, *w, p, enc_mode, st, logits, tlog, pl, tl);
+    if (w->copy_stream) cudaStreamSynchronize(w->copy_stream);  // also after an early error
+    cudaError_t se = cudaStreamSynchronize(st);
+    release_ws(m, w, st, false);
+    if (rc) return rc;
+    if (se != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(se));
+    return 0;
+  }
   if (!rc && (logits || tlog))
     rc = run_heads(m, *w, p, st, logits ? w->logits : nullptr, tlog ? w->tlogits : nullptr, false);
   std::vector<OutCopy> outs;

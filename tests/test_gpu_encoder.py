@@ -238,3 +238,26 @@ def test_simd_lanes_bitexact(igdev, oracle_lib, lanes):
     assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(om.encode(ids, offs)))
     assert np.array_equal(_bits(gm.EncodeTokens((ids, offs))), _bits(om.encode(ids, offs, mode=1)))
     gm.close()
+
+
+def test_window_logits_chunked_tail(igdev):
+    """Spans windows at a size whose final norm and per-token heads run in
+    row chunks with overlapped copies give the same logits as the same
+    windows encoded a few at a time (unchunked)."""
+    from indecis_b200 import spans as SP
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Config, Head, Model
+    gm = Model.from_arrays(Config.from_dict(S.C1), S.weights(S.C1, seed=42))
+    gm.SetHeads([Head(h["name"], h["kind"], h["w"], h["b"]) for h in S.heads(S.C1["hidden"])])
+    rng = np.random.default_rng(5)
+    texts = [rng.integers(4, S.C1["vocab"], int(n)).tolist() for n in rng.integers(200, 2000, 40)]
+    big = SP.infer_windows(gm, texts, [2], [1], 128)
+    small = SP.infer_windows(gm, texts, [2], [1], 128, batch_size=8)
+    assert sum(len(t) for t in texts) >= 16384
+    for a, b in zip(big, small):
+        for x, y in zip(a.pooled + a.tokens, b.pooled + b.tokens):
+            if x is None:
+                assert y is None
+            else:
+                assert np.array_equal(np.asarray(x).view(np.uint64), np.asarray(y).view(np.uint64))
+    gm.close()
