@@ -494,6 +494,11 @@ static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, 
   return cudaGetLastError();
 }
 
+// The CTA-pair kernel (gemm_pair.cu) for deep products with 256-column
+// tiles; -1 when it is not taken.
+static int gemm_pair_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, const CUtensorMap &ma,
+                         const CUtensorMap &mc, cudaStream_t st);
+
 // Persistent path when the output suits TMA stores; returns -1 to ask the
 // caller for the plain kernel.
 static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, int bn, const CUtensorMap &ma,
@@ -512,6 +517,10 @@ static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, 
   const int out_cols = epi == kEpiGeglu ? ep.geglu_n : g.N;
   CUtensorMap mc;
   if (make_map_out32(&mc, out, g.M, out_cols, ep.ldc, epi == kEpiI32)) return IG_ERR_CUDA;
+  if (bn == 256) {
+    const int prc = gemm_pair_try(g, ep, epi, ma, mc, st);
+    if (prc != -1) return prc;
+  }
   cudaError_t e;
 #define IG_PCASE(E)                                                                         \
   case E:                                                                                   \
