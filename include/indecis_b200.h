@@ -171,6 +171,16 @@ IG_API const char *ig_last_error(void);
  * in ig_encode_device); reset != 0 clears it. Synchronizes the device. */
 IG_API int32_t ig_device_error(int32_t reset);
 
+/* Self-check of the GELU vector body's division shortcut (an FMA-refined
+ * reciprocal in place of the IEEE division of geluMulAVX2's VDIVPS,
+ * linalg/gelu_amd64.s:165-225): over every float t in [-4, 4] on the current
+ * device, mismatches[0] = quotients that differ from the IEEE quotient and
+ * mismatches[1] = values of 1 + quotient that differ (the GELU uses the
+ * quotient only through 1 + erf; 0 required); first_bad_bits (optional) = the
+ * smallest |t| bits of the latter; histogram (optional, [2][256]) = both
+ * counts by the biased exponent of t. Synchronizes the device. */
+IG_API int ig_check_gelu_division(int64_t *mismatches, uint32_t *first_bad_bits, int64_t *histogram);
+
 /* ---- per-operation entry points (device pointers, enqueued on stream) ---- */
 
 /* MatMul8N's integer product and dequantization (linalg/int8.go:88-155):

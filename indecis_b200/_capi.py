@@ -30,7 +30,8 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_infer_windows", "ig_model_head_rows", "ig_vision_create", "ig_vision_destroy", "ig_vision_forward",
            "ig_vision_forward_device", "ig_vision_dump_layer", "ig_model_dims", "ig_batcher_create",
            "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats",
-           "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags", "ig_model_set_int8"]
+           "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags", "ig_model_set_int8",
+           "ig_check_gelu_division"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -134,6 +135,7 @@ def load() -> C.CDLL:
     L.ig_encode_dump.argtypes = [vp, vp, vp, i32, i32, vp, C.c_size_t, C.POINTER(IgDump)]
     L.ig_logits_device.argtypes = [vp, vp, vp, i32, vp, vp, vp]
     L.ig_attention_noalloc.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
+    L.ig_check_gelu_division.argtypes = [vp, vp, vp]
     L.ig_model_set_embeddings.argtypes = [vp, C.POINTER(IgEmbeddingTable)]
     i32p, f64 = C.POINTER(C.c_int32), C.c_double
     L.ig_plan_windows.argtypes = [i32, i32, i32, C.POINTER(IgWindow), i32, i32p]

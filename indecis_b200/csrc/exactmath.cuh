@@ -152,6 +152,51 @@ __device__ __forceinline__ float2 dequant2(int32_t a0, int32_t a1, float2 zc, fl
   return __fmul2_rn(v, f2(sa));
 }
 
+// p / q rounded to nearest for the erf rational of the GELU vector body,
+// without the IEEE division's special-case path: a hardware reciprocal
+// estimate, one Newton-Raphson step r = r + r(1 - qr), the quotient y = RN(p r)
+// and Markstein's remainder correction y + (p - q y) r with exact FMA
+// remainders (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; J.-M. Muller et
+// al., Handbook of Floating-Point Arithmetic, division by FMA). Used only
+// where q is the erf denominator of gelu_mul_fma(2): t in [-4, 4] gives
+// q in [-2.4, -0.0142] and |p| <= |q|, so every intermediate is a normal
+// number or zero. ig_check_gelu_division compares it with the IEEE quotient
+// for every float t in [-4, 4] (tests/test_gpu_gelu_division.py): equal bits.
+__device__ __forceinline__ float div_erf(float p, float q) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(q));
+  r = __fmaf_rn(r, __fmaf_rn(-q, r, 1.0f), r);
+  const float y = __fmul_rn(p, r);
+  return __fmaf_rn(__fmaf_rn(-q, y, p), r, y);
+}
+__device__ __forceinline__ float2 div_erf2(float2 p, float2 q) {
+  float2 r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(q.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(q.y));
+  const float2 nq = make_float2(-q.x, -q.y);
+  r = __ffma2_rn(r, __ffma2_rn(nq, r, make_float2(1.0f, 1.0f)), r);
+  const float2 y = __fmul2_rn(p, r);
+  return __ffma2_rn(__ffma2_rn(nq, y, p), r, y);
+}
+
+// The erf rational's numerator and denominator of gelu_mul_fma for a clamped
+// t (gelu_amd64.s:176-195).
+__device__ __forceinline__ void erf_pq_fma(float t, float &p, float &q) {
+  const float t2 = __fmul_rn(t, t);
+  p = __fmaf_rn(t2, -2.72614225801306e-10f, 2.77068142495902e-08f);
+  p = __fmaf_rn(t2, p, -2.10102402082508e-06f);
+  p = __fmaf_rn(t2, p, -5.69250639462346e-05f);
+  p = __fmaf_rn(t2, p, -7.34990630326855e-04f);
+  p = __fmaf_rn(t2, p, -2.95459980854025e-03f);
+  p = __fmaf_rn(t2, p, -1.60960333262415e-02f);
+  p = __fmul_rn(p, t);
+  q = __fmaf_rn(t2, -1.45660718464996e-05f, -2.13374055278905e-04f);
+  q = __fmaf_rn(t2, q, -1.68282697438203e-03f);
+  q = __fmaf_rn(t2, q, -7.37332916720468e-03f);
+  q = __fmaf_rn(t2, q, -1.42647390514189e-02f);
+}
+
 // gelu_mul_fma for two elements.
 __device__ __forceinline__ float2 gelu_mul_fma2(float2 x, float2 gate) {
   float2 t = __fmul2_rn(x, f2(0.7071067811865476f));
@@ -169,7 +214,7 @@ __device__ __forceinline__ float2 gelu_mul_fma2(float2 x, float2 gate) {
   q = __ffma2_rn(t2, q, f2(-1.68282697438203e-03f));
   q = __ffma2_rn(t2, q, f2(-7.37332916720468e-03f));
   q = __ffma2_rn(t2, q, f2(-1.42647390514189e-02f));
-  float2 r = make_float2(__fdiv_rn(p.x, q.x), __fdiv_rn(p.y, q.y));
+  float2 r = div_erf2(p, q);
   r = __fadd2_rn(r, f2(1.0f));
   const float2 g = __fmul2_rn(r, __fmul2_rn(x, f2(0.5f)));
   return __fmul2_rn(g, gate);
@@ -192,7 +237,7 @@ __device__ __forceinline__ float gelu_mul_fma(float x, float gate) {
   q = __fmaf_rn(t2, q, -1.68282697438203e-03f);
   q = __fmaf_rn(t2, q, -7.37332916720468e-03f);
   q = __fmaf_rn(t2, q, -1.42647390514189e-02f);
-  float r = __fdiv_rn(p, q);
+  float r = div_erf(p, q);
   r = __fadd_rn(r, 1.0f);
   const float g = __fmul_rn(r, __fmul_rn(x, 0.5f));
   return __fmul_rn(g, gate);
