@@ -33,6 +33,90 @@ __device__ __forceinline__ uint32_t quant_byte_slow(float v, float inv) {
   return (uint32_t)(max(-128, min(127, rne_int(__fmul_rn(v, inv)))) + 128);
 }
 
+// gamma[k + 8b] read through the read-only cache.
+struct GammaLdg {
+  const float *p;
+  __device__ __forceinline__ float operator()(int b) const { return __ldg(p + b * 8); }
+};
+
+// The rest of LayerNormRow (+ quantizeA) for the row whose lane-k chain
+// values v[b] = x[k + 8b] this lane holds (lane (r, k) of the warp): the
+// float64 combines, mean, variance, rstd, gamma (gam(b) = gamma[k + 8b]),
+// optional beta and f32 output, and the quantized bytes through the warp's
+// shared row buffer sq_row (H + 8 bytes). Every lane of the warp calls it.
+template <int NB, class Gamma>
+__device__ __forceinline__ void ln8_row_finish(float (&v)[NB], const Gamma &gam, const float *__restrict__ beta,
+                                               int r, int k, int row, bool rv, double eps, float *__restrict__ xout,
+                                               uint8_t *__restrict__ q, int ldq, float *__restrict__ sa,
+                                               uint8_t *sq_row) {
+  constexpr int H = 8 * NB;
+  float ls = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NB; b++) ls = __fadd_rn(ls, v[b]);
+  double sum = 0.0;
+#pragma unroll
+  for (int kk = 0; kk < 8; kk++) sum = __dadd_rn(sum, (double)__shfl_sync(0xffffffffu, ls, (r << 3) | kk));
+  const float mean = __double2float_rn(__ddiv_rn(sum, (double)H));
+  float lq = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    v[b] = __fsub_rn(v[b], mean);
+    lq = __fmaf_rn(v[b], v[b], lq);
+  }
+  double var = 0.0;
+#pragma unroll
+  for (int kk = 0; kk < 8; kk++) var = __dadd_rn(var, (double)__shfl_sync(0xffffffffu, lq, (r << 3) | kk));
+  const float rstd = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(var, (double)H), eps))));
+  float mx = 0.0f;  // NaN-propagating here; the NaN-ignoring maximum is taken again below if needed
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    v[b] = __fmul_rn(__fmul_rn(v[b], rstd), gam(b));
+    if (beta) v[b] = __fadd_rn(v[b], __ldg(beta + k + 8 * b));  // AddTo(o, beta) (SigLIP norms)
+    mx = fmax_nan(mx, fabsf(v[b]));
+  }
+  if (xout && rv) {
+    float *dst = xout + (size_t)row * H + k;
+#pragma unroll
+    for (int b = 0; b < NB; b++) dst[8 * b] = v[b];
+  }
+  if (!q) return;
+  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+  const bool has_nan = mx != mx;
+  if (__any_sync(0xffffffffu, has_nan)) {  // the maximum over the non-NaN values (rows without NaN: the same)
+    mx = 0.0f;
+#pragma unroll
+    for (int b = 0; b < NB; b++) mx = fmaxf(mx, fabsf(v[b]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+  }
+  float scale = 0.0f, inv = 0.0f;
+  if (mx > 0.0f) {
+    scale = __fdiv_rn(mx, 127.0f);
+    inv = __fdiv_rn(1.0f, scale);
+  }
+  if (k == 0 && rv) sa[row] = scale;
+  uint8_t *sq = sq_row;
+  if (mx == 0.0f) {  // a zero row quantizes to 128s (linalg/int8.go:157-191)
+#pragma unroll
+    for (int b = 0; b < NB; b++) sq[k + 8 * b] = 128;
+  } else if (!has_nan && row_scale_normal(scale)) {
+#pragma unroll
+    for (int b = 0; b < NB; b++) sq[k + 8 * b] = (uint8_t)__float_as_uint(__fadd_rn(__fmul_rn(v[b], inv), kMagic + 128.0f));
+  } else {
+#pragma unroll
+    for (int b = 0; b < NB; b++) sq[k + 8 * b] = (uint8_t)quant_byte_slow(v[b], inv);
+  }
+  __syncwarp();
+  if (rv) {
+    uint8_t *dq = q + (size_t)row * ldq;
+    for (int c = k; c < H / 8; c += 8)
+      *reinterpret_cast<uint2 *>(dq + 8 * c) = *reinterpret_cast<const uint2 *>(sq + 8 * c);
+  }
+}
+
 template <int NB, bool EMBED>
 __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, const int32_t *__restrict__ ids,
                                                   int vocab, const EmbTable emb,
@@ -66,70 +150,101 @@ __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, c
 #pragma unroll
     for (int b = 0; b < NB; b++) v[b] = rv ? __ldg(src + k + 8 * b) : 0.0f;
   }
-  float ls = 0.0f;
+  ln8_row_finish<NB>(v, GammaLdg{gamma + k}, beta, r, k, row, rv, eps, xout, q, ldq, sa, s_q[warp][r]);
+}
+
+// gamma[k + 8b] held in registers for the whole kernel.
+template <int NB>
+struct GammaRegs {
+  float g[NB];
+  __device__ __forceinline__ float operator()(int b) const { return g[b]; }
+};
+
+// 16-byte-granular bulk copy global -> this CTA's shared memory, completing
+// on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// ln8_kernel for row-contiguous f32 rows, persistent: groups of 32 rows are
+// staged in shared memory by bulk copies (one per row, a padded row pitch so
+// that the lanes' stride-8 chain reads hit distinct banks), three groups in
+// flight per CTA, gamma in registers. The same arithmetic as ln8_kernel
+// (ln8_row_finish); the global traffic is the rows' bytes, read once, in
+// 1 KB copies instead of 32-byte-per-row lane loads.
+template <int NB>
+struct Ln8Staged {
+  static constexpr int H = 8 * NB;
+  static constexpr int kRows = 32;
+  static constexpr int kStages = 3;
+  static constexpr int kPitch = H + 8;  // floats
+  static constexpr int kQP = H + 8;     // bytes
+  static constexpr int kRowBytes = kStages * kRows * kPitch * 4;
+  static constexpr int kQBytes = 8 * 4 * kQP;
+  static constexpr int kBar = (kRowBytes + kQBytes + 15) & ~15;
+  static constexpr int kTotal = kBar + 8 * kStages;
+};
+
+template <int NB>
+__global__ void __launch_bounds__(256, 2) ln8_staged_kernel(const float *__restrict__ x,
+                                                            const float *__restrict__ gamma,
+                                                            const float *__restrict__ beta, int M, double eps,
+                                                            float *__restrict__ xout, uint8_t *__restrict__ q,
+                                                            int ldq, float *__restrict__ sa) {
+  using S = Ln8Staged<NB>;
+  constexpr int H = S::H;
+  extern __shared__ __align__(128) uint8_t ln_smem[];
+  float *rows = reinterpret_cast<float *>(ln_smem);
+  uint8_t *s_q = ln_smem + S::kRowBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(ln_smem + S::kBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 3, k = lane & 7;
+  const int ngroups = (M + S::kRows - 1) / S::kRows;
+
+  GammaRegs<NB> gam;
 #pragma unroll
-  for (int b = 0; b < NB; b++) ls = __fadd_rn(ls, v[b]);
-  double sum = 0.0;
-#pragma unroll
-  for (int kk = 0; kk < 8; kk++) sum = __dadd_rn(sum, (double)__shfl_sync(0xffffffffu, ls, (r << 3) | kk));
-  const float mean = __double2float_rn(__ddiv_rn(sum, (double)H));
-  float lq = 0.0f;
-#pragma unroll
-  for (int b = 0; b < NB; b++) {
-    v[b] = __fsub_rn(v[b], mean);
-    lq = __fmaf_rn(v[b], v[b], lq);
+  for (int b = 0; b < NB; b++) gam.g[b] = __ldg(gamma + k + 8 * b);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; s++) mbar_init(&full[s], 1);
+    fence_barrier_init();
   }
-  double var = 0.0;
+  __syncthreads();
+
+  // Warp 0 stages group grp into stage s: lane i copies row i.
+  auto stage = [&](int grp, int s) {
+    const int r0 = grp * S::kRows;
+    const int nr = min(S::kRows, M - r0);
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(nr * H * 4));
+    __syncwarp();
+    if (lane < nr)
+      bulk_g2s(rows + (size_t)(s * S::kRows + lane) * S::kPitch, x + (size_t)(r0 + lane) * H, H * 4, &full[s]);
+  };
+  if (warp == 0)
+    for (int i = 0; i < S::kStages; i++) {
+      const int grp = blockIdx.x + i * gridDim.x;
+      if (grp < ngroups) stage(grp, i);
+    }
+
+  int it = 0;
+  for (int grp = blockIdx.x; grp < ngroups; grp += gridDim.x, it++) {
+    const int s = it % S::kStages;
+    const bool ok = mbar_wait(&full[s], (uint32_t)(it / S::kStages) & 1, kDevTimeoutFull);
+    if (!__syncthreads_and(ok)) break;
+    const int rl = warp * 4 + r;
+    const int row = grp * S::kRows + rl;
+    const bool rv = row < M;
+    const float *src = rows + (size_t)(s * S::kRows + rl) * S::kPitch + k;
+    float v[NB];
 #pragma unroll
-  for (int kk = 0; kk < 8; kk++) var = __dadd_rn(var, (double)__shfl_sync(0xffffffffu, lq, (r << 3) | kk));
-  const float rstd = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(var, (double)H), eps))));
-  float mx = 0.0f;  // NaN-propagating here; the NaN-ignoring maximum is taken again below if needed
-#pragma unroll
-  for (int b = 0; b < NB; b++) {
-    v[b] = __fmul_rn(__fmul_rn(v[b], rstd), __ldg(gamma + k + 8 * b));
-    if (beta) v[b] = __fadd_rn(v[b], __ldg(beta + k + 8 * b));  // AddTo(o, beta) (SigLIP norms)
-    mx = fmax_nan(mx, fabsf(v[b]));
-  }
-  if (xout && rv) {
-    float *dst = xout + (size_t)row * H + k;
-#pragma unroll
-    for (int b = 0; b < NB; b++) dst[8 * b] = v[b];
-  }
-  if (!q) return;
-  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-  mx = fmax_nan(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-  const bool has_nan = mx != mx;
-  if (__any_sync(0xffffffffu, has_nan)) {  // the maximum over the non-NaN values (rows without NaN: the same)
-    mx = 0.0f;
-#pragma unroll
-    for (int b = 0; b < NB; b++) mx = fmaxf(mx, fabsf(v[b]));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-  }
-  float scale = 0.0f, inv = 0.0f;
-  if (mx > 0.0f) {
-    scale = __fdiv_rn(mx, 127.0f);
-    inv = __fdiv_rn(1.0f, scale);
-  }
-  if (k == 0 && rv) sa[row] = scale;
-  uint8_t *sq = s_q[warp][r];
-  if (mx == 0.0f) {  // a zero row quantizes to 128s (linalg/int8.go:157-191)
-#pragma unroll
-    for (int b = 0; b < NB; b++) sq[k + 8 * b] = 128;
-  } else if (!has_nan && row_scale_normal(scale)) {
-#pragma unroll
-    for (int b = 0; b < NB; b++) sq[k + 8 * b] = (uint8_t)__float_as_uint(__fadd_rn(__fmul_rn(v[b], inv), kMagic + 128.0f));
-  } else {
-#pragma unroll
-    for (int b = 0; b < NB; b++) sq[k + 8 * b] = (uint8_t)quant_byte_slow(v[b], inv);
-  }
-  __syncwarp();
-  if (rv) {
-    uint8_t *dq = q + (size_t)row * ldq;
-    for (int c = k; c < H / 8; c += 8)
-      *reinterpret_cast<uint2 *>(dq + 8 * c) = *reinterpret_cast<const uint2 *>(sq + 8 * c);
+    for (int b = 0; b < NB; b++) v[b] = rv ? src[8 * b] : 0.0f;
+    ln8_row_finish<NB>(v, gam, beta, r, k, row, rv, eps, xout, q, ldq, sa, s_q + (warp * 4 + r) * S::kQP);
+    __syncthreads();  // stage s has been read by every warp
+    if (warp == 0) {
+      const int nxt = grp + S::kStages * gridDim.x;
+      if (nxt < ngroups) stage(nxt, s);
+    }
   }
 }
 
@@ -256,6 +371,28 @@ static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTa
                       cudaStream_t st) {
   if (V != 8 || !gamma) return -1;
   if (q && ((ldq & 7) || (reinterpret_cast<uintptr_t>(q) & 7))) return -1;
+  // The staged kernel for the f32-output norm (the final norm): measured at
+  // C1 (262,144 rows) 90 us against 108 us for ln8_kernel. With quantized
+  // output it ran slower (92 against 82 us: 16 warps per SM, limited by
+  // registers and shared memory, hide the row's float64 chain less well than
+  // ln8_kernel's 32), so the quantizing norms keep ln8_kernel.
+  if (!EMBED && H == 256 && !q && !(reinterpret_cast<uintptr_t>(x) & 15)) {
+    using S = Ln8Staged<32>;
+    static bool attr_set = false;
+    if (!attr_set) {
+      if (cudaFuncSetAttribute(ln8_staged_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal) !=
+          cudaSuccess)
+        return IG_ERR_CUDA;
+      attr_set = true;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int groups = (M + S::kRows - 1) / S::kRows;
+    const int grid = groups < 2 * sms ? groups : 2 * sms;
+    ln8_staged_kernel<32><<<grid, 256, S::kTotal, st>>>(x, gamma, beta, M, eps, xout, q, ldq, sa);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
   const int blocks = (M + 31) / 32;
 #define IG_LN8(NB)                                                                                                 \
   case 8 * NB:                                                                                                     \

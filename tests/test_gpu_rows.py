@@ -108,3 +108,31 @@ def test_layernorm_quant_nan_gamma(igdev, oracle_lib, H):
     assert np.array_equal(got[ok].view(np.uint32), xn_ref[ok].view(np.uint32))
     assert np.array_equal(q.cpu().numpy(), q_ref)
     assert np.array_equal(sa.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+
+
+def test_layernorm_quant_many_rows(igdev, oracle_lib):
+    """Enough rows (H = 256) that every CTA of the staged LayerNorm kernel
+    (the f32-output norm) walks several row groups and reuses each
+    shared-memory stage; zero rows, NaN rows, huge rows and a ragged last group
+    among them. The quantizing kernel runs on the same rows."""
+    from indecis_b200 import ops
+    rng = np.random.default_rng(77)
+    M, H = 40003, 256
+    x = (rng.standard_normal((M, H)) * 2 + rng.uniform(-3, 3, (M, 1))).astype(np.float32)
+    x[5] = 0.0
+    x[1000, 17] = np.nan
+    x[30000] *= 1e30
+    x[M - 1] = 1e-30
+    gamma = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    xn_ref = oracle_lib.layernorm(x, gamma, 1e-5, 8)
+    q_ref, s_ref = oracle_lib.quantize_a(xn_ref)
+    dx, dg = torch.from_numpy(x).cuda(), torch.from_numpy(gamma).cuda()
+    xn, q, sa = ops.layernorm_quant(dx, dg)
+    xn_only, _, _ = ops.layernorm_quant(dx, dg, want_q=False)  # the staged kernel (f32 output only)
+    assert np.array_equal(xn_only.cpu().numpy().view(np.uint32), xn.cpu().numpy().view(np.uint32))
+    got = xn.cpu().numpy()
+    assert np.array_equal(np.isnan(got), np.isnan(xn_ref)) and np.isnan(xn_ref[1000]).all()
+    ok = ~np.isnan(xn_ref)
+    assert np.array_equal(got[ok].view(np.uint32), xn_ref[ok].view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(sa.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
