@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(kAtThreads, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int4 blk = blocks[blockIdx.x];
+  if (blk.w > 2) return;  // a longer key range: attn_tc_long_kernel
   const int s = blk.x, i0 = blk.y, c0 = blk.z, nkt = blk.w;
   const int h = blockIdx.y;
   const int t0 = offs[s];
@@ -402,6 +403,264 @@ __global__ void __launch_bounds__(kAtThreads, 2)
   }
 }
 
+
+// ---- key ranges beyond 256 columns: two passes over 128-key tiles --------------
+//
+// attn_tc_long_kernel handles a 128-query block whose keys span more than two
+// tiles (global layers over sequences longer than 256 tokens). The score
+// tile S = Q.K^T is computed twice per key tile: a first pass takes MaxOf over
+// every valid key of each row, a second recomputes S (the same integer
+// accumulators), forms P = rne(exp(s - max) * 255) with ExpShift's
+// body/tail split by key position, and accumulates O += P.V in TMEM. P's sum
+// and O are integer sums, exact in any order, so the result is the
+// single-pass kernel's (and attention8.go's) bit for bit.
+//
+// One CTA, 10 warps, 256 TMEM columns (S: 0-127, O: 128-191), two CTAs per SM:
+//   warp 0     TMA: Q once; per step K (pass 1) or K and V (pass 2) of one
+//              key tile into a 3-stage ring.
+//   warp 1     MMAs: S per step (after the softmax warps released the
+//              previous S), O += P.V per pass-2 step; commits release the
+//              ring stages and the P buffers.
+//   warps 2-9  as attn_tc_kernel, per tile; P double-buffered in shared memory.
+constexpr int kAlStages = 3;
+
+struct AttnLongSmem {
+  static constexpr int kQ = 0;                             // [128][64 B] SW64
+  static constexpr int kKV = 8192;                         // kAlStages x (K, V) [128][64 B] SW64
+  static constexpr int kP = kKV + kAlStages * 16384;       // 2 x [128][128 B] SW128 (1024-aligned)
+  static constexpr int kKs = kP + 32768;                   // 2 slots x 128 key scales
+  static constexpr int kKzc = kKs + 1024;                  // 2 slots x 128 (kzc + 1.5*2^23)
+  static constexpr int kRed = kKzc + 1024;                 // [2][128] row maxima, then [2][128] P sums
+  static constexpr int kBar = kRed + 2048;                 // 13 mbarriers
+  static constexpr int kTmem = kBar + 128;
+  static constexpr int kTotal = 100 * 1024;
+  static_assert(kP % 1024 == 0, "SW128 P tiles");
+  static_assert(kTmem + 16 + 1024 <= kTotal, "shared memory");
+};
+
+__global__ void __launch_bounds__(kAtThreads, 2)
+    attn_tc_long_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                        const __grid_constant__ CUtensorMap mv, const int4 *__restrict__ blocks,
+                        const int32_t *__restrict__ offs, int N, int H, int nh, int window, int V,
+                        const float *__restrict__ sq, const float *__restrict__ ks, const float *__restrict__ kzc,
+                        const float *__restrict__ vs, float *__restrict__ ctx) {
+  using S = AttnLongSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int4 blk = blocks[blockIdx.x];
+  if (blk.w <= 2) return;  // attn_tc_kernel's block
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + S::kBar);
+  uint64_t *qfull = bar;               // Q landed
+  uint64_t *kfull = bar + 1;           // [kAlStages] stage landed
+  uint64_t *kempty = bar + 4;          // [kAlStages] stage released by the MMAs
+  uint64_t *sfull = bar + 7;           // S computed
+  uint64_t *sfree = bar + 8;           // S read by all softmax warps
+  uint64_t *pfull = bar + 9;           // [2] P buffer written
+  uint64_t *pfree = bar + 11;          // [2] P buffer read by its P.V
+  uint64_t *ofull = bar + 13;          // all P.V done
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::kTmem);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s = blk.x, i0 = blk.y, c0 = blk.z, nkt = blk.w;
+  const int h = blockIdx.y;
+  const int t0 = offs[s];
+  const int n = offs[s + 1] - t0;
+  const int prow = h * N + t0;  // first row of this sequence in the head plane
+  const int steps = 2 * nkt;    // pass 1: tiles 0..nkt-1, pass 2: again
+
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&mq);
+    prefetch_tensormap(&mk);
+    prefetch_tensormap(&mv);
+    mbar_init(qfull, 1);
+    for (int i = 0; i < kAlStages; i++) {
+      mbar_init(&kfull[i], 1);
+      mbar_init(&kempty[i], 1);
+    }
+    mbar_init(sfull, 1);
+    mbar_init(sfree, kAtSoftWarps);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&pfull[i], kAtSoftWarps);
+      mbar_init(&pfree[i], 1);
+    }
+    mbar_init(ofull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(qfull, 8192);
+      tma_load_2d(&mq, smem + S::kQ, qfull, 0, prow + i0);
+      for (int j = 0; j < steps; j++) {
+        const int st = j % kAlStages;
+        const uint32_t ph = (uint32_t)(j / kAlStages) & 1;
+        if (!mbar_wait(&kempty[st], ph ^ 1, kDevTimeoutEmpty)) break;
+        const bool pass2 = j >= nkt;
+        const int kt = pass2 ? j - nkt : j;
+        uint8_t *stage = smem + S::kKV + st * 16384;
+        mbar_arrive_expect_tx(&kfull[st], pass2 ? 16384 : 8192);
+        tma_load_2d(&mk, stage, &kfull[st], 0, prow + c0 + kt * kAtKT);
+        if (pass2) tma_load_2d(&mv, stage + 8192, &kfull[st], 0, prow + c0 + kt * kAtKT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_u8s8(kAtQ, kAtKT);
+      constexpr uint32_t idesc_o = idesc_u8s8(kAtQ, 64) | (1u << 16);  // B (V) MN-major
+      bool ok = mbar_wait(qfull, 0, kDevTimeoutFull);
+      const uint32_t q_base = smem_u32(smem + S::kQ);
+      const uint32_t p_base = smem_u32(smem + S::kP);
+      for (int j = 0; j < steps && ok; j++) {
+        const int st = j % kAlStages;
+        const uint32_t ph = (uint32_t)(j / kAlStages) & 1;
+        const bool pass2 = j >= nkt;
+        const int kt = pass2 ? j - nkt : j;
+        ok = mbar_wait(&kfull[st], ph, kDevTimeoutFull);
+        if (ok && j > 0) ok = mbar_wait(sfree, (uint32_t)(j - 1) & 1, kDevTimeoutEmpty);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(smem + S::kKV + st * 16384);
+#pragma unroll
+        for (int kk = 0; kk < 2; kk++)
+          mma_u8s8(tmem, smem_desc_k_sw64(q_base + kk * 32), smem_desc_k_sw64(k_base + kk * 32), idesc_s, kk);
+        mma_commit(sfull);
+        if (pass2) {
+          const int pb = kt & 1;
+          ok = mbar_wait(&pfull[pb], (uint32_t)(kt >> 1) & 1, kDevTimeoutEmpty);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_u8s8(tmem + 128, smem_desc_k_sw128(p_base + pb * 16384 + kk * 32),
+                     smem_desc_mn_sw64(k_base + 8192 + kk * 32 * 64), idesc_o, (kt | kk) != 0);
+          mma_commit(&pfree[pb]);
+        }
+        mma_commit(&kempty[st]);
+      }
+      mma_commit(ofull);
+    }
+  } else {
+    const int q = warp & 3;         // TMEM lane quarter: rows [32q, 32q+32)
+    const int g = (warp - 2) >> 2;  // 16-key chunks with parity g
+    const int r = q * 32 + lane;
+    const int i = i0 + r;
+    const bool valid = i < n;
+    const int tid = threadIdx.x - 64;  // 0..255
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    int js = 0, je = n;
+    if (window >= 0) {
+      js = max(0, i - window);
+      je = min(n, i + window + 1);
+    }
+    const int len = je - js;
+    const int body_end = js + (len / V) * V;  // ExpShift: vector body before, exp32 tail after
+    const float sqr = valid ? sq[prow + i] : 0.0f;
+    float *red = reinterpret_cast<float *>(smem + S::kRed);
+    bool ok = mbar_wait(qfull, 0, kDevTimeoutFull);  // Q in shared memory for tail_fixup
+    float mx = -INFINITY;
+    int psum = 0;
+    for (int j = 0; j < steps; j++) {
+      const bool pass2 = j >= nkt;
+      const int kt = pass2 ? j - nkt : j;
+      const int st = j % kAlStages;
+      const int tb = c0 + kt * kAtKT;  // first key of the tile
+      // The tile's key scales into slot j & 1 (every softmax warp is past tile
+      // j - 1 once all have reached the barrier below).
+      float *s_ks = reinterpret_cast<float *>(smem + S::kKs) + (j & 1) * 128;
+      float *s_kzc = reinterpret_cast<float *>(smem + S::kKzc) + (j & 1) * 128;
+      {
+        const int c = tid & 127, key = tb + c;
+        if (tid < 128)
+          s_ks[c] = key < n ? ks[prow + key] : 0.0f;
+        else
+          s_kzc[c] = __fadd_rn(key < n ? kzc[prow + key] : 0.0f, kMagic);
+      }
+      named_barrier_sync(1, 32 * kAtSoftWarps);
+      ScoreRow w;
+      w.a = valid ? js - tb : 1 << 30;
+      w.b = valid ? je - tb : 0;
+      w.t0 = valid ? body_end - tb : 0;
+      w.t1 = valid ? je - tb : 0;
+      w.sq = sqr;
+      const int wa = __reduce_min_sync(0xffffffffu, max(w.a, 0)),
+                wb = __reduce_max_sync(0xffffffffu, min(w.b, kAtKT));
+      const int ch0 = wb > wa ? wa / 16 : 0, ch1 = wb > wa ? (wb + 15) / 16 : 0;
+      if (ok) ok = mbar_wait(sfull, (uint32_t)j & 1, kDevTimeoutAccum);
+      ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
+      tc_fence_after();
+      if (!pass2) {
+        if (ok)
+          for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2)
+            mx = chunk_max<false>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sfree);
+        if (kt == nkt - 1) {  // the row maximum over both parities
+          red[g * 128 + r] = mx;
+          named_barrier_sync(1, 32 * kAtSoftWarps);
+          mx = fmaxf(red[r], red[128 + r]);
+        }
+      } else {
+        const int pb = kt & 1;
+        if (kt >= 2 && ok) ok = mbar_wait(&pfree[pb], (uint32_t)((kt >> 1) & 1) ^ 1, kDevTimeoutEmpty);
+        ok = __all_sync(0xffffffffu, ok);
+        uint8_t *ptile = smem + S::kP + pb * 16384;
+        uint8_t *prow_smem = ptile + r * 128;
+        for (int ch = g; ch < kAtKT / 16; ch += 2) {
+          uint4 pw = make_uint4(0, 0, 0, 0);
+          if (ok && ch >= ch0 && ch < ch1) pw = chunk_p<false>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx, psum);
+          *reinterpret_cast<uint4 *>(prow_smem + (((ch & 7) ^ (r & 7)) << 4)) = pw;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sfree);
+        const int ta = max(w.t0, 0), tz = min(w.t1, kAtKT);
+        if (ok && ta < tz)
+          psum += tail_fixup(smem + S::kQ, smem + S::kKV + st * 16384, 8192, ptile, r, g, ta, tz, s_kzc, s_ks, w.sq,
+                             mx);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pfull[pb]);
+      }
+    }
+    int *ired = reinterpret_cast<int *>(red) + 256;
+    ired[g * 128 + r] = psum;
+    named_barrier_sync(1, 32 * kAtSoftWarps);
+    psum = ired[r] + ired[128 + r];
+    const float sp = psum > 0 ? __fdiv_rn(1.0f, (float)psum) : 0.0f;
+    if (ok) ok = mbar_wait(ofull, 0, kDevTimeoutAccum);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    // Output dimensions [32g, 32g+32) of the row.
+    uint32_t o[32];
+    tmem_ld_32x32b_x32(tbase + 128 + 32 * g, o);
+    tmem_ld_wait();
+    if (ok && valid) {
+      const float *vsc = vs + ((size_t)s * nh + h) * 64 + 32 * g;
+      float *out = ctx + (size_t)(t0 + i) * H + h * 64 + 32 * g;
+#pragma unroll
+      for (int d = 0; d < 32; d += 4) {
+        const float4 sv = __ldg(reinterpret_cast<const float4 *>(vsc + d));
+        *reinterpret_cast<float4 *>(out + d) =
+            make_float4(dequant1((int32_t)o[d], 0.0f, sv.x, sp), dequant1((int32_t)o[d + 1], 0.0f, sv.y, sp),
+                        dequant1((int32_t)o[d + 2], 0.0f, sv.z, sp), dequant1((int32_t)o[d + 3], 0.0f, sv.w, sp));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 // A [rows][64 B] plane as TMA tiles of box_rows x 64 B, SWIZZLE_64B.
 static int make_map_rows64(CUtensorMap *map, const void *base, int rows, int box_rows) {
   auto enc = get_encode_fn();
@@ -423,9 +682,8 @@ int attn_tc_fits(int n, int i0, int window, int *c0_out, int *nkt_out) {
     c1 = min(n, i0 + kAtQ + window);
   }
   const int width = c1 - c0;
-  if (width > 2 * kAtKT) return 0;
   *c0_out = c0;
-  *nkt_out = (width + kAtKT - 1) / kAtKT;
+  *nkt_out = (width + kAtKT - 1) / kAtKT;  // more than 2: attn_tc_long_kernel
   return 1;
 }
 
@@ -442,13 +700,23 @@ int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaS
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcSmem::kTotal) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(attn_tc_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AttnLongSmem::kTotal) != cudaSuccess)
       return IG_ERR_CUDA;
     attr = true;
   }
+  // Blocks of at most two key tiles run in attn_tc_kernel, longer ones in
+  // attn_tc_long_kernel; each kernel returns at once on the other's blocks.
   attn_tc_kernel<<<dim3(nblocks, a.nh), kAtThreads, AttnTcSmem::kTotal, st>>>(
       mq, mk, mv, d_blocks, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx);
-  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+  if (a.max_len > 2 * kAtKT) {
+    attn_tc_long_kernel<<<dim3(nblocks, a.nh), kAtThreads, AttnLongSmem::kTotal, st>>>(
+        mq, mk, mv, d_blocks, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx);
+    if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+  }
+  return 0;
 }
 
 }  // namespace ig

@@ -87,3 +87,19 @@ def test_attention_many_rows(igdev, oracle_lib, window):
     ctx = ops.attention(torch.from_numpy(qkv).cuda(), H, nh, offs, window).cpu().numpy()
     bad = np.argwhere(ctx.view(np.uint32) != ref.view(np.uint32))
     assert len(bad) == 0, f"{len(np.unique(bad[:, 0]))} rows differ, first {bad[:3].tolist()}"
+
+
+@pytest.mark.parametrize("lens", [[257], [384], [385, 511, 640], [1000, 2, 300, 700]])
+def test_attention_long_key_tiles(igdev, oracle_lib, lens):
+    """Global layers over more than two 128-key tiles: the two-pass kernel
+    (row maximum over every tile, then P and O per tile), with sequence ends
+    on and off tile boundaries and the ExpShift tail across them; every row of
+    every sequence bit-exact."""
+    from indecis_b200 import ops
+    H, nh = 256, 4
+    qkv, offs = _qkv(lens, H, nh, seed=sum(lens) * 7 + 1)
+    ref = _ref(oracle_lib, qkv, offs, H, nh, -1)
+    ctx = ops.attention(torch.from_numpy(qkv).cuda(), H, nh, offs, -1).cpu().numpy()
+    assert not np.isnan(ctx).any()
+    bad = np.argwhere(ctx.view(np.uint32) != ref.view(np.uint32))
+    assert len(bad) == 0, f"{len(np.unique(bad[:, 0]))} rows differ, first {bad[:3].tolist()}"
