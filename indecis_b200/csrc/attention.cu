@@ -60,12 +60,116 @@ __global__ void attn_stats_kernel(const float *__restrict__ qkv, const int32_t *
   }
 }
 
+// attn_stats_kernel for D = 64 with the (sequence, head) slices of K and V
+// (and, with ROPE, the rows' cos/sin factors) staged in shared memory by
+// cp.async, 32 rows per stage and three stages in flight: thread d < 64 runs
+// the ordered float32 sum of dimension d (of K rotated at each row's position
+// when ROPE), the other 192 threads the V column maxima over interleaved rows
+// (maxima combine in any order). The same values as attn_stats_kernel /
+// attn_prep_kernel, with nothing but shared-memory reads and the adds on the
+// sum's dependency chain.
+constexpr int kStRows = 32, kStStages = 3;
+constexpr int kStStageFloats = 2 * kStRows * 64 + 2 * kStRows * 32;  // K, V, cos, sin
+
+template <bool ROPE>
+__global__ void __launch_bounds__(256)
+    attn_stats64_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ offs, int H, int nh,
+                        const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
+                        float *__restrict__ kmean, float *__restrict__ vs, float *__restrict__ vinv) {
+  extern __shared__ __align__(16) float st_smem[];  // [stages][K 32x64, V 32x64, cos 32x32, sin 32x32]
+  __shared__ float s_vmax[3][64];
+  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int t0 = offs[s], n = offs[s + 1] - t0;
+  const size_t ld = 3 * (size_t)H;
+  const float *kbase = qkv + (size_t)t0 * ld + H + h * 64;
+  const int nchunks = (n + kStRows - 1) / kStRows;
+  // Stage chunk c: 32 rows x 16 float4 of K and of V (four 16-byte copies a
+  // thread), and 32 rows x 8 float4 of cos and of sin (one each).
+  auto stage = [&](int c) {
+    if (c < nchunks) {
+      float *dst = st_smem + (size_t)(c % kStStages) * kStStageFloats;
+#pragma unroll
+      for (int e = tid; e < 2 * kStRows * 16; e += 256) {
+        const int kv = e >> 9, r = (e >> 4) & 31, q4 = e & 15;
+        const int row = c * kStRows + r;
+        if (row < n) cp_async16(dst + (kv * kStRows + r) * 64 + q4 * 4, kbase + (size_t)row * ld + kv * H + q4 * 4);
+      }
+      if (ROPE) {
+        const int tab = tid >> 7, r = (tid >> 3) & 15, q4 = tid & 7;  // 2 tables x 16 rows x 8 float4, twice
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+          const int row = c * kStRows + half * 16 + r;
+          if (row < n)
+            cp_async16(dst + 2 * kStRows * 64 + (tab * kStRows + half * 16 + r) * 32 + q4 * 4,
+                       (tab ? rope_sin : rope_cos) + (size_t)row * 32 + q4 * 4);
+        }
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int c = 0; c < kStStages - 1; c++) stage(c);
+  float acc = 0.0f;  // K sum (tid < 64) or V maximum (others)
+  const int vd = (tid - 64) & 63, vsub = (tid - 64) >> 6;
+  for (int c = 0; c < nchunks; c++) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kStStages - 2) : "memory");
+    __syncthreads();
+    const float *kc = st_smem + (size_t)(c % kStStages) * kStStageFloats;
+    const float *vc = kc + kStRows * 64;
+    const float *cc = kc + 2 * kStRows * 64, *sc = cc + kStRows * 32;
+    const int rows = min(kStRows, n - c * kStRows);
+    if (tid < 64) {
+      const int i = tid & 31;
+      if (rows == kStRows) {
+#pragma unroll 8
+        for (int r = 0; r < kStRows; r++) {
+          float kval = kc[r * 64 + tid];
+          if constexpr (ROPE) {
+            const float a = kval, b = kc[r * 64 + (tid ^ 32)], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
+            kval = tid < 32 ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn))
+                            : __fadd_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+          }
+          acc = __fadd_rn(acc, kval);
+        }
+      } else {
+        for (int r = 0; r < rows; r++) {
+          float kval = kc[r * 64 + tid];
+          if constexpr (ROPE) {
+            const float a = kval, b = kc[r * 64 + (tid ^ 32)], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
+            kval = tid < 32 ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn))
+                            : __fadd_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+          }
+          acc = __fadd_rn(acc, kval);
+        }
+      }
+    } else {
+      for (int r = vsub; r < rows; r += 3) acc = fmaxf(acc, fabsf(vc[r * 64 + vd]));
+    }
+    __syncthreads();  // this stage is read: refill it
+    stage(c + kStStages - 1);
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (tid >= 64) s_vmax[vsub][vd] = acc;
+  __syncthreads();
+  if (tid < 64) {
+    const size_t o = ((size_t)s * nh + h) * 64 + tid;
+    kmean[o] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
+    const float mx = fmaxf(fmaxf(s_vmax[0][tid], s_vmax[1][tid]), s_vmax[2][tid]);
+    const float scv = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
+    vs[o] = scv;
+    vinv[o] = mx > 0.0f ? __fdiv_rn(1.0f, scv) : 0.0f;
+  }
+}
+
 // One warp per (row, head); D <= 128 (each lane holds D/32 values).
-__global__ void attn_quant_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ row_seq, int N, int H,
-                                  int nh, int D, float scale, const float *__restrict__ kmean,
-                                  const float *__restrict__ vinv, uint8_t *__restrict__ qa, float *__restrict__ sq,
-                                  int8_t *__restrict__ kq, float *__restrict__ ks, float *__restrict__ kzc,
-                                  int8_t *__restrict__ vq) {
+// With rope_cos (D = 64: lane l holds dimensions l and l + 32, a rotate_half
+// pair) q and k are rotated at the row's position in its sequence first, as
+// attn_prep_kernel does.
+__global__ void attn_quant_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ row_seq,
+                                  const int32_t *__restrict__ offs, int N, int H, int nh, int D, float scale,
+                                  const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
+                                  const float *__restrict__ kmean, const float *__restrict__ vinv,
+                                  uint8_t *__restrict__ qa, float *__restrict__ sq, int8_t *__restrict__ kq,
+                                  float *__restrict__ ks, float *__restrict__ kzc, int8_t *__restrict__ vq) {
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (gw >= N * nh) return;
   const int row = gw / nh, h = gw % nh;
@@ -83,8 +187,24 @@ __global__ void attn_quant_kernel(const float *__restrict__ qkv, const int32_t *
     qv[u] = kv[u] = vv[u] = 0.0f;
     if (d < D) {
       qv[u] = base[d];
-      kv[u] = __fsub_rn(base[H + d], km[d]);
+      kv[u] = base[H + d];
       vv[u] = base[2 * H + d];
+    }
+  }
+  if (rope_cos) {  // Rope (linalg/vec_simd.go:404-425): separate roundings, no FMA
+    const int pos = row - offs[s];
+    const float c = __ldg(rope_cos + (size_t)pos * 32 + lane), sn = __ldg(rope_sin + (size_t)pos * 32 + lane);
+    const float q1 = qv[0], q2 = qv[1], k1 = kv[0], k2 = kv[1];
+    qv[0] = __fsub_rn(__fmul_rn(q1, c), __fmul_rn(q2, sn));
+    qv[1] = __fadd_rn(__fmul_rn(q2, c), __fmul_rn(q1, sn));
+    kv[0] = __fsub_rn(__fmul_rn(k1, c), __fmul_rn(k2, sn));
+    kv[1] = __fadd_rn(__fmul_rn(k2, c), __fmul_rn(k1, sn));
+  }
+#pragma unroll
+  for (int u = 0; u < kMax; u++) {
+    const int d = lane + 32 * u;
+    if (d < D) {
+      kv[u] = __fsub_rn(kv[u], km[d]);
       qmx = fmaxf(qmx, fabsf(qv[u]));
       kmx = fmaxf(kmx, fabsf(kv[u]));
     }
@@ -505,6 +625,33 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
                                                                    a.ks, a.kzc, a.vq);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
+  if (a.nseq > 0 && a.N > 0 && a.D == 64 && a.V >= 1 && a.max_len > kShortSeq && (a.H % 4) == 0 && a.row_seq &&
+      !(reinterpret_cast<uintptr_t>(a.qkv) & 15)) {
+    // Long sequences: statistics per (sequence, head), then one warp per
+    // (row, head) for the rotation and quantization.
+    const int smem = kStStages * kStStageFloats * (int)sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+      if (cudaFuncSetAttribute(attn_stats64_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+              cudaSuccess ||
+          cudaFuncSetAttribute(attn_stats64_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+              cudaSuccess)
+        return IG_ERR_CUDA;
+      attr = true;
+    }
+    if (a.rope_cos)
+      attn_stats64_kernel<true><<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, a.rope_cos,
+                                                                        a.rope_sin, a.kmean, a.vs, a.vinv);
+    else
+      attn_stats64_kernel<false><<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, nullptr, nullptr,
+                                                                         a.kmean, a.vs, a.vinv);
+    if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+    const long long warps = (long long)a.N * a.nh;
+    attn_quant_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+        a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.D, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq,
+        a.kq, a.ks, a.kzc, a.vq);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
   if (a.nseq > 0 && a.N > 0 && a.D <= 128 && (a.D % 4) == 0 && a.V >= 1) {
     attn_prep_kernel<<<dim3(a.nseq, a.nh), 256, 0, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.D, a.scale, a.rope_cos,
                                                           a.rope_sin, a.vs, a.qa, a.sq, a.kq, a.ks, a.kzc, a.vq);
@@ -521,8 +668,9 @@ int launch_attention_two_pass(const AttnArgs &a, cudaStream_t st) {
   attn_stats_kernel<<<dim3(a.nseq, a.nh), sthreads, 0, st>>>(a.qkv, a.offs, a.H, a.nh, a.D, a.kmean, a.vs, a.vinv);
   if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
   const int warps = a.N * a.nh;
-  attn_quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(a.qkv, a.row_seq, a.N, a.H, a.nh, a.D, a.scale,
-                                                             a.kmean, a.vinv, a.qa, a.sq, a.kq, a.ks, a.kzc, a.vq);
+  attn_quant_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.D,
+                                                             a.scale, nullptr, nullptr, a.kmean, a.vinv, a.qa, a.sq,
+                                                             a.kq, a.ks, a.kzc, a.vq);
   if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
   return 0;
 }
