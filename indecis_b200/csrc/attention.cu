@@ -160,6 +160,97 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// attn_quant_kernel for D = 64 with one warp per row over all its heads: the
+// row's sequence, position and RoPE factors are read once, and successive
+// heads' loads are independent. Lane l holds dimensions l and l + 32 (a
+// rotate_half pair); the bytes are gathered by shuffles so that each plane's
+// 64-byte row leaves in 16-bit stores. The same arithmetic as
+// attn_quant_kernel / attn_prep_kernel.
+__global__ void __launch_bounds__(256)
+    attn_quant64_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ row_seq,
+                        const int32_t *__restrict__ offs, int N, int H, int nh, float scale,
+                        const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
+                        const float *__restrict__ kmean, const float *__restrict__ vinv, uint8_t *__restrict__ qa,
+                        float *__restrict__ sq, int8_t *__restrict__ kq, float *__restrict__ ks,
+                        float *__restrict__ kzc, int8_t *__restrict__ vq) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= N) return;
+  const int s = row_seq[row];
+  float c = 1.0f, sn = 0.0f;
+  if (rope_cos) {
+    const int pos = row - offs[s];
+    c = __ldg(rope_cos + (size_t)pos * 32 + lane);
+    sn = __ldg(rope_sin + (size_t)pos * 32 + lane);
+  }
+  const float *base = qkv + (size_t)row * 3 * H;
+  // Lane m < 16 stores dimensions 2m, 2m+1; lane 16 + m dimensions 32+2m, 33+2m.
+  const bool hi_half = lane >= 16;
+  const int src = (2 * lane) & 31;
+  const uint32_t pick = hi_half ? 0x0062u : 0x0040u;
+  const int off = hi_half ? 32 + 2 * (lane - 16) : 2 * lane;
+#pragma unroll 2
+  for (int h = 0; h < nh; h++) {
+    const float *b = base + h * 64;
+    const float *km = kmean + ((size_t)s * nh + h) * 64;
+    const float *vi = vinv + ((size_t)s * nh + h) * 64;
+    float q1 = b[lane], q2 = b[lane + 32], k1 = b[H + lane], k2 = b[H + lane + 32];
+    const float v1 = b[2 * H + lane], v2 = b[2 * H + lane + 32];
+    if (rope_cos) {  // Rope (linalg/vec_simd.go:404-425): separate roundings, no FMA
+      const float qa_ = q1, qb_ = q2, ka_ = k1, kb_ = k2;
+      q1 = __fsub_rn(__fmul_rn(qa_, c), __fmul_rn(qb_, sn));
+      q2 = __fadd_rn(__fmul_rn(qb_, c), __fmul_rn(qa_, sn));
+      k1 = __fsub_rn(__fmul_rn(ka_, c), __fmul_rn(kb_, sn));
+      k2 = __fadd_rn(__fmul_rn(kb_, c), __fmul_rn(ka_, sn));
+    }
+    k1 = __fsub_rn(k1, __ldg(km + lane));
+    k2 = __fsub_rn(k2, __ldg(km + lane + 32));
+    float qmx = fmaxf(fmaxf(0.0f, fabsf(q1)), fabsf(q2));
+    float kmx = fmaxf(fmaxf(0.0f, fabsf(k1)), fabsf(k2));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      qmx = fmaxf(qmx, __shfl_xor_sync(0xffffffffu, qmx, o));
+      kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+    }
+    // Q (attention8.go:210-220): uint8 with the 128 offset.
+    const float qs = qmx > 0.0f ? __fdiv_rn(qmx, 127.0f) : 0.0f;
+    const float qinv = qmx > 0.0f ? __fdiv_rn(1.0f, qs) : 0.0f;
+    // K (attention8.go:240-251): centred, int8, scale and 128*sum.
+    const float kss = kmx > 0.0f ? __fdiv_rn(kmx, 127.0f) : 0.0f;
+    const float kinv = kmx > 0.0f ? __fdiv_rn(1.0f, kss) : 0.0f;
+    int qa1 = qmx > 0.0f ? rne_int(__fmul_rn(q1, qinv)) : 0, qa2 = qmx > 0.0f ? rne_int(__fmul_rn(q2, qinv)) : 0;
+    qa1 = max(-128, min(127, qa1)) + 128;
+    qa2 = max(-128, min(127, qa2)) + 128;
+    int kb1 = 0, kb2 = 0, ksum = 0;
+    if (kmx > 0.0f) {
+      kb1 = rne_int(__fmul_rn(k1, kinv));
+      kb2 = rne_int(__fmul_rn(k2, kinv));
+      ksum = kb1 + kb2;
+      kb1 = max(-128, min(127, kb1));
+      kb2 = max(-128, min(127, kb2));
+    }
+    const int vb1 = max(-128, min(127, rne_int(__fmul_rn(v1, __ldg(vi + lane))))),
+              vb2 = max(-128, min(127, rne_int(__fmul_rn(v2, __ldg(vi + lane + 32)))));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ksum += __shfl_xor_sync(0xffffffffu, ksum, o);
+    // Byte 0: dimension lane, byte 2: dimension lane + 32.
+    const uint32_t wq = (uint32_t)qa1 | ((uint32_t)qa2 << 16);
+    const uint32_t wk = ((uint32_t)kb1 & 0xFFu) | (((uint32_t)kb2 & 0xFFu) << 16);
+    const uint32_t wv = ((uint32_t)vb1 & 0xFFu) | (((uint32_t)vb2 & 0xFFu) << 16);
+    const uint32_t q_lo = __shfl_sync(0xffffffffu, wq, src), q_hi = __shfl_sync(0xffffffffu, wq, src + 1);
+    const uint32_t k_lo = __shfl_sync(0xffffffffu, wk, src), k_hi = __shfl_sync(0xffffffffu, wk, src + 1);
+    const uint32_t v_lo = __shfl_sync(0xffffffffu, wv, src), v_hi = __shfl_sync(0xffffffffu, wv, src + 1);
+    const size_t plane = (size_t)h * N + row;
+    *reinterpret_cast<uint16_t *>(qa + plane * 64 + off) = (uint16_t)__byte_perm(q_lo, q_hi, pick);
+    *reinterpret_cast<uint16_t *>(kq + plane * 64 + off) = (uint16_t)__byte_perm(k_lo, k_hi, pick);
+    *reinterpret_cast<uint16_t *>(vq + plane * 64 + off) = (uint16_t)__byte_perm(v_lo, v_hi, pick);
+    if (lane == 0) {
+      sq[plane] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
+      ks[plane] = kss;
+      kzc[plane] = kmx > 0.0f ? __fmul_rn(128.0f, (float)ksum) : 0.0f;
+    }
+  }
+}
+
 // One warp per (row, head); D <= 128 (each lane holds D/32 values).
 // With rope_cos (D = 64: lane l holds dimensions l and l + 32, a rotate_half
 // pair) q and k are rotated at the row's position in its sequence first, as
@@ -628,7 +719,7 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.nseq > 0 && a.N > 0 && a.D == 64 && a.V >= 1 && a.max_len > kShortSeq && (a.H % 4) == 0 && a.row_seq &&
       !(reinterpret_cast<uintptr_t>(a.qkv) & 15)) {
     // Long sequences: statistics per (sequence, head), then one warp per
-    // (row, head) for the rotation and quantization.
+    // row (all its heads) for the rotation and quantization.
     const int smem = kStStages * kStStageFloats * (int)sizeof(float);
     static bool attr = false;
     if (!attr) {
@@ -646,9 +737,8 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
       attn_stats64_kernel<false><<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, nullptr, nullptr,
                                                                          a.kmean, a.vs, a.vinv);
     if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
-    const long long warps = (long long)a.N * a.nh;
-    attn_quant_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
-        a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.D, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq,
+    attn_quant64_kernel<<<(unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st>>>(
+        a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq,
         a.kq, a.ks, a.kzc, a.vq);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
