@@ -214,16 +214,17 @@ IG_API int ig_pack_b8(const float *w, int32_t n, int32_t k, int8_t *q, int32_t l
 IG_API int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t *offs, int32_t nseq,
                  int32_t window, int32_t simd_lanes, float *ctx, void *stream);
 
-/* ig_attention for callers that cannot allocate device memory (code running
- * under CUDA graph capture, processes that reserve all device memory up front,
- * latency-critical paths that must not synchronize the device through
- * cudaMalloc/cudaFree). No counterpart in the reference: its attention buffers
- * are Go slices. Same arguments and result as ig_attention, but the work
- * buffers come from one array of 32 MiB built into the library, held on every
- * GPU that loads it until the process exits; inputs needing more scratch fail
- * with IG_ERR_BAD_ARG. The first call on a device looks up the array's address
- * (make it before any stream capture). All calls share the array: calls that
- * overlap on the GPU race. Asynchronous on `stream`. */
+/* ig_attention for callers that cannot allocate device memory (processes that
+ * reserve all device memory up front, latency-critical paths that must not
+ * synchronize the device through cudaMalloc/cudaFree). No counterpart in the
+ * reference: its attention buffers are Go slices. Same arguments and result as
+ * ig_attention, but the work buffers come from one array of 32 MiB built into
+ * the library, held on every GPU that loads it until the process exits; inputs
+ * needing more scratch fail with IG_ERR_BAD_ARG, sequences longer than 10240
+ * tokens with IG_ERR_UNSUPPORTED, both before any GPU work. The first call on
+ * a device looks up the array's address (make it before any stream capture).
+ * The offsets are read from host memory during the call. All calls share the
+ * array: calls that overlap on the GPU race. Asynchronous on `stream`. */
 IG_API int ig_attention_noalloc(const float *qkv, int32_t hidden, int32_t heads, const int64_t *offs, int32_t nseq,
                                 int32_t window, int32_t simd_lanes, float *ctx, void *stream);
 

@@ -704,13 +704,8 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.rope_cos && a.D != 64) return IG_ERR_UNSUPPORTED;
   if (a.rope_cos && a.nseq > 0 && a.N > 0 && a.max_len <= kShortSeq && (a.H % 4) == 0) {
     const int smem = 3 * kShortSeq * 64 * (int)sizeof(float);
-    static bool attr = false;
-    if (!attr) {
-      if (cudaFuncSetAttribute(attn_prep_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-          cudaSuccess)
-        return IG_ERR_CUDA;
-      attr = true;
-    }
+    static SmemOptIn attr;
+    if (attr.ensure((const void *)attn_prep_short_kernel, smem) != cudaSuccess) return IG_ERR_CUDA;
     attn_prep_short_kernel<<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.scale,
                                                                    a.rope_cos, a.rope_sin, a.vs, a.qa, a.sq, a.kq,
                                                                    a.ks, a.kzc, a.vq);
@@ -721,15 +716,10 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     // Long sequences: statistics per (sequence, head), then one warp per
     // row (all its heads) for the rotation and quantization.
     const int smem = kStStages * kStStageFloats * (int)sizeof(float);
-    static bool attr = false;
-    if (!attr) {
-      if (cudaFuncSetAttribute(attn_stats64_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-              cudaSuccess ||
-          cudaFuncSetAttribute(attn_stats64_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-              cudaSuccess)
-        return IG_ERR_CUDA;
-      attr = true;
-    }
+    static SmemOptIn attr_t, attr_f;
+    if (attr_t.ensure((const void *)attn_stats64_kernel<true>, smem) != cudaSuccess ||
+        attr_f.ensure((const void *)attn_stats64_kernel<false>, smem) != cudaSuccess)
+      return IG_ERR_CUDA;
     if (a.rope_cos)
       attn_stats64_kernel<true><<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, a.rope_cos,
                                                                         a.rope_sin, a.kmean, a.vs, a.vinv);
@@ -770,13 +760,8 @@ int launch_attend(const AttnArgs &a, const int2 *d_blocks, int nblocks, cudaStre
   if (nblocks <= 0) return 0;
   const size_t smem = (size_t)kAttnWarps * a.max_len * (sizeof(float) + 1);
   if (smem > 200 * 1024) return IG_ERR_UNSUPPORTED;
-  static size_t smem_set = 0;
-  if (smem > 48 * 1024 && smem > smem_set) {
-    if (cudaFuncSetAttribute(attn_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return IG_ERR_CUDA;
-    smem_set = smem;
-  }
+  static SmemOptIn attr;
+  if (smem > 48 * 1024 && attr.ensure((const void *)attn_attend_kernel, (int)smem) != cudaSuccess) return IG_ERR_CUDA;
   attn_attend_kernel<<<dim3(nblocks, a.nh), 32 * kAttnWarps, smem, st>>>(
       d_blocks, a.offs, a.N, a.H, a.nh, a.D, a.window, a.V, a.max_len, a.qa, a.sq, a.kq, a.ks, a.kzc, a.vq, a.vs,
       a.ctx);

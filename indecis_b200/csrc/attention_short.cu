@@ -633,13 +633,8 @@ int launch_attn_short(const AttnArgs &a, cudaStream_t st) {
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return IG_ERR_CUDA;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnShortSmem::kTotal) !=
-        cudaSuccess)
-      return IG_ERR_CUDA;
-    attr = true;
-  }
+  static SmemOptIn attr;
+  if (attr.ensure((const void *)attn_short_kernel, AttnShortSmem::kTotal) != cudaSuccess) return IG_ERR_CUDA;
   if (a.xq) {
     if (!attn_short_quantizes(a)) return IG_ERR_UNSUPPORTED;
     // One cluster per sequence: its nh head CTAs share the row maxima.

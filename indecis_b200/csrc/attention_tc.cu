@@ -697,15 +697,10 @@ int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaS
   if (make_map_rows64(&mq, a.qa, rows, kAtQ) || make_map_rows64(&mk, a.kq, rows, kAtKT) ||
       make_map_rows64(&mv, a.vq, rows, kAtKT))
     return IG_ERR_CUDA;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcSmem::kTotal) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(attn_tc_long_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             AttnLongSmem::kTotal) != cudaSuccess)
-      return IG_ERR_CUDA;
-    attr = true;
-  }
+  static SmemOptIn attr_tc, attr_long;
+  if (attr_tc.ensure((const void *)attn_tc_kernel, AttnTcSmem::kTotal) != cudaSuccess ||
+      attr_long.ensure((const void *)attn_tc_long_kernel, AttnLongSmem::kTotal) != cudaSuccess)
+    return IG_ERR_CUDA;
   // Blocks of at most two key tiles run in attn_tc_kernel, longer ones in
   // attn_tc_long_kernel; each kernel returns at once on the other's blocks.
   attn_tc_kernel<<<dim3(nblocks, a.nh), kAtThreads, AttnTcSmem::kTotal, st>>>(

@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 namespace ig {
 
 // Error codes a kernel can leave in g_device_error (first one wins).
@@ -258,5 +261,49 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
   asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
+
+// ---- host: per-device launch settings ------------------------------------------
+
+constexpr int kMaxDevices = 64;
+
+// A kernel's opt-in to more than 48 KB of dynamic shared memory. The attribute
+// set by cudaFuncSetAttribute belongs to the current device, so the limit
+// already raised is remembered per device ordinal: a process that drives
+// several GPUs raises it on each of them. The limit only grows (a launch that
+// needs less never lowers it under a concurrent launch that needs more), and
+// the raise happens under a lock, so concurrent callers see it done before
+// they launch. One static instance per kernel.
+struct SmemOptIn {
+  std::atomic<int> bytes[kMaxDevices];
+  std::mutex mu;
+  cudaError_t ensure(const void *fn, int want) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (bytes[dev].load(std::memory_order_acquire) >= want) return cudaSuccess;
+    std::lock_guard<std::mutex> lk(mu);
+    if (bytes[dev].load(std::memory_order_relaxed) >= want) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+    if (e == cudaSuccess) bytes[dev].store(want, std::memory_order_release);
+    return e;
+  }
+};
+
+// A per-device integer computed once on first use (SM counts, occupancy
+// figures); get() runs fn() with the device current. 0 is stored as "unknown".
+struct PerDevice {
+  std::atomic<int> v[kMaxDevices];
+  template <typename F>
+  int get(F fn) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return fn();
+    int x = v[dev].load(std::memory_order_acquire);
+    if (x) return x - 1;
+    x = fn();
+    v[dev].store(x + 1, std::memory_order_release);
+    return x;
+  }
+};
 
 }  // namespace ig

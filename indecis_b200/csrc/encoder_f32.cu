@@ -297,13 +297,8 @@ int launch_attend_blocks_f32(const float *qkv, const int32_t *seq_off, const int
   if (ntasks <= 0) return 0;
   if (H != nh * kAbD || V != 8) return IG_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(ctx)) & 15) return IG_ERR_BAD_ARG;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attend_blocks_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AbSmem::kTotal) !=
-        cudaSuccess)
-      return IG_ERR_CUDA;
-    attr = true;
-  }
+  static SmemOptIn attr;
+  if (attr.ensure((const void *)attend_blocks_f32_kernel, AbSmem::kTotal) != cudaSuccess) return IG_ERR_CUDA;
   attend_blocks_f32_kernel<<<dim3(ntasks, nh), 256, AbSmem::kTotal, st>>>(qkv, seq_off, tasks, H, nh, window, scale,
                                                                            ctx);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;

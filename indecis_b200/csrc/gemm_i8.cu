@@ -263,13 +263,9 @@ template <int BN, int EPI>
 static cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, int M, int N, int K,
                              const GemmEpilogue &ep, cudaStream_t st) {
   using S = GemmSmem<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_u8s8_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         S::kTotal);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static SmemOptIn attr;
+  cudaError_t e = attr.ensure((const void *)gemm_u8s8_kernel<BN, EPI>, S::kTotal);
+  if (e != cudaSuccess) return e;
   dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
   gemm_u8s8_kernel<BN, EPI><<<grid, kGemmThreads, S::kTotal, st>>>(ma, mb, M, N, K, ep);
   return cudaGetLastError();

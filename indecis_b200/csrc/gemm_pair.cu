@@ -264,8 +264,8 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
 // Clusters of two that can be resident at once for this kernel (0: none).
 template <int EPI>
 static int pair_max_clusters() {
-  static int n = -1;
-  if (n < 0) {
+  static PerDevice clusters;
+  return clusters.get([] {
     using S = PairSmem<EPI>;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -283,9 +283,8 @@ static int pair_max_clusters() {
       (void)cudaGetLastError();
       c = 0;
     }
-    n = c;
-  }
-  return n;
+    return c;
+  });
 }
 
 template <int EPI>
@@ -293,13 +292,9 @@ static cudaError_t launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, con
                                int K, const GemmEpilogue &ep, cudaStream_t st, bool *launched) {
   using S = PairSmem<EPI>;
   *launched = false;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static SmemOptIn smem_attr;
+  const cudaError_t se = smem_attr.ensure((const void *)gemm_pair_kernel<EPI>, S::kTotal);
+  if (se != cudaSuccess) return se;
   const int maxc = pair_max_clusters<EPI>();
   if (maxc <= 0) return cudaSuccess;  // not launched: the caller takes the single-CTA kernel
   const int ntiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + S::kBN - 1) / S::kBN);

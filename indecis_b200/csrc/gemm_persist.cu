@@ -467,27 +467,22 @@ static int make_map_out32(CUtensorMap *map, const void *base, int rows, int cols
 }
 
 static int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
+  static PerDevice sms;
+  return sms.get([] {
+    int dev = 0, n = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
+    return n > 0 ? n : 148;
+  });
 }
 
 template <int BN, int EPI>
 static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mc, int M, int N,
                                   int K, const GemmEpilogue &ep, cudaStream_t st) {
   using S = PGemmSmem<BN, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_persist_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         S::kTotal);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static SmemOptIn attr;
+  cudaError_t e = attr.ensure((const void *)gemm_persist_kernel<BN, EPI>, S::kTotal);
+  if (e != cudaSuccess) return e;
   const int ntiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   gemm_persist_kernel<BN, EPI><<<grid, PEpi<EPI>::kThreads, S::kTotal, st>>>(ma, mb, mc, M, N, K, ep);

@@ -3,12 +3,10 @@
 //
 // ig_attention obtains its work buffers (quantized Q/K/V, their scales, the
 // per-sequence statistics and the query-block table) with cudaMalloc on every
-// call. Some callers cannot do that: code that runs while a CUDA graph is
-// being captured (cudaMalloc is not a stream operation, so it cannot be
-// recorded and interferes with the capture), serving processes that reserve
-// all device memory when they start and forbid allocations afterwards (a
-// later cudaMalloc fails or fragments their pool), and latency-critical paths
-// where cudaMalloc/cudaFree would synchronize the device and stall every other
+// call. Some callers cannot do that: serving processes that reserve all
+// device memory when they start and forbid allocations afterwards (a later
+// cudaMalloc fails or fragments their pool), and latency-critical paths where
+// cudaMalloc/cudaFree would synchronize the device and stall every other
 // stream. This variant computes the same result with its work buffers carved
 // out of one fixed array compiled into the library:
 //
@@ -16,6 +14,10 @@
 //     library's device image, so every GPU on which the library's kernels are
 //     loaded holds it until the process exits. Inputs needing more are
 //     rejected with IG_ERR_BAD_ARG before anything is enqueued.
+//   * length: the attend kernel keeps each warp's score row in shared
+//     memory, so a sequence may hold at most kNoAllocMaxLen (10240) tokens;
+//     longer ones are rejected with IG_ERR_UNSUPPORTED before anything is
+//     enqueued (ig_attention takes them through its tensor-core kernels).
 //   * set-up: the first call on a device, with that device current, looks up
 //     the array's device address (cudaGetSymbolAddress) and caches it. Make
 //     that first call before any stream capture that contains the entry point.
@@ -28,7 +30,8 @@
 //     stream or guard them.
 //   * no allocation: no cudaMalloc, cudaFree, pinned or heap allocation; the
 //     host work is scalar loops over the offsets and one cudaMemcpyAsync of
-//     the offsets into the array.
+//     the offsets (host memory) into the array, which has taken its copy of
+//     them when the call returns.
 // The call is asynchronous on `stream`: ctx is complete when the stream is.
 #include <cuda_runtime.h>
 
@@ -43,6 +46,9 @@
 namespace ig {
 
 constexpr size_t kNoAllocScratchBytes = 32u << 20;
+// The attend kernel's shared memory is kAttnWarps score rows of max_len
+// floats plus max_len bytes each, at most 200 KB.
+constexpr int kNoAllocMaxLen = 200 * 1024 / (kAttnWarps * 5);
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // int64 offsets -> int32 offsets, row -> sequence, and the query-block table
@@ -106,6 +112,10 @@ extern "C" int ig_attention_noalloc(const float *qkv, int32_t hidden, int32_t he
   }
   const int64_t N = offs[nseq];
   if (N == 0) return 0;
+  if (max_len > kNoAllocMaxLen)
+    return fail(IG_ERR_UNSUPPORTED, "ig_attention_noalloc: a sequence of " + std::to_string(max_len) +
+                                        " tokens is longer than the " + std::to_string(kNoAllocMaxLen) +
+                                        " this entry point takes; use ig_attention");
   const size_t nh = heads, D = hidden / heads;
   // Carve the scratch: each buffer starts on a 256-byte boundary.
   size_t off = 0;

@@ -240,12 +240,9 @@ static inline int row_blocks(int M) { return (M + kRowWarps - 1) / kRowWarps; }
 
 static int smem_rows_ok(int H) { return H > 0 && (size_t)H * kRowWarps * sizeof(float) <= 200 * 1024; }
 
-static int set_rows_smem(const void *fn, int H) {
+static int set_rows_smem(SmemOptIn &attr, const void *fn, int H) {
   const int bytes = H * kRowWarps * (int)sizeof(float);
-  if (bytes > 48 * 1024) {
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
-      return IG_ERR_CUDA;
-  }
+  if (bytes > 48 * 1024 && attr.ensure(fn, bytes) != cudaSuccess) return IG_ERR_CUDA;
   return 0;
 }
 
@@ -259,7 +256,8 @@ int launch_ln_quant(const float *x, const float *gamma, int M, int H, double eps
     if (rc != -1) return rc;
   }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;
-  if (set_rows_smem((const void *)ln_quant_kernel, H)) return IG_ERR_CUDA;
+  static SmemOptIn attr;
+  if (set_rows_smem(attr, (const void *)ln_quant_kernel, H)) return IG_ERR_CUDA;
   ln_quant_kernel<<<row_blocks(M), 32 * kRowWarps, H * kRowWarps * sizeof(float), st>>>(x, gamma, M, H, eps, V, xn,
                                                                                           q, ldq, sa);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
@@ -285,7 +283,8 @@ int launch_embed_checked(const int32_t *ids, int vocab, const EmbTable &emb, con
     if (rc != -1) return rc;
   }
   if (!smem_rows_ok(H) || V < 1 || V > 32) return IG_ERR_BAD_ARG;
-  if (set_rows_smem((const void *)embed_ln_quant_kernel, H)) return IG_ERR_CUDA;
+  static SmemOptIn attr;
+  if (set_rows_smem(attr, (const void *)embed_ln_quant_kernel, H)) return IG_ERR_CUDA;
   embed_ln_quant_kernel<<<row_blocks(M), 32 * kRowWarps, H * kRowWarps * sizeof(float), st>>>(
       ids, vocab, emb, gamma, M, H, eps, V, x, q, ldq, sa);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
@@ -298,7 +297,8 @@ int launch_quant_rows(const float *x, int ldx, int M, int K, uint8_t *q, int ldq
     if (rc != -1) return rc;
   }
   if (!smem_rows_ok(K)) return IG_ERR_BAD_ARG;
-  if (set_rows_smem((const void *)quant_rows_kernel, K)) return IG_ERR_CUDA;
+  static SmemOptIn attr;
+  if (set_rows_smem(attr, (const void *)quant_rows_kernel, K)) return IG_ERR_CUDA;
   quant_rows_kernel<<<row_blocks(M), 32 * kRowWarps, K * kRowWarps * sizeof(float), st>>>(x, ldx, M, K, q, ldq, sa);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }

@@ -378,13 +378,8 @@ static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTa
   // ln8_kernel's 32), so the quantizing norms keep ln8_kernel.
   if (!EMBED && H == 256 && !q && !(reinterpret_cast<uintptr_t>(x) & 15)) {
     using S = Ln8Staged<32>;
-    static bool attr_set = false;
-    if (!attr_set) {
-      if (cudaFuncSetAttribute(ln8_staged_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal) !=
-          cudaSuccess)
-        return IG_ERR_CUDA;
-      attr_set = true;
-    }
+    static SmemOptIn attr;
+    if (attr.ensure((const void *)ln8_staged_kernel<32>, S::kTotal) != cudaSuccess) return IG_ERR_CUDA;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -155,9 +155,8 @@ static int launch_ln_group(const float *x, const int32_t *ids, int vocab, const 
   int P = 0, wpb = 0;
   size_t smem = 0;
   if (!ln_group_geometry(H, V, &P, &wpb, &smem)) return -1;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(ln_group_kernel<EMBED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-          cudaSuccess)
+  static SmemOptIn attr;
+  if (smem > 48 * 1024 && attr.ensure((const void *)ln_group_kernel<EMBED>, (int)smem) != cudaSuccess)
     return IG_ERR_CUDA;
   const int rows_per_block = wpb * (32 / V);
   const int blocks = (M + rows_per_block - 1) / rows_per_block;

@@ -384,13 +384,8 @@ int launch_attn_f32(const float *qkv, int nimg, int T, int H, int nh, float scal
   if (nimg <= 0) return 0;
   if (H != nh * kAttD || T < 1 || T > kAttMaxT || V != 8) return IG_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(ctx)) & 15) return IG_ERR_BAD_ARG;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AttF32Smem::kTotal) !=
-        cudaSuccess)
-      return IG_ERR_CUDA;
-    attr = true;
-  }
+  static SmemOptIn attr;
+  if (attr.ensure((const void *)attn_f32_kernel, AttF32Smem::kTotal) != cudaSuccess) return IG_ERR_CUDA;
   attn_f32_kernel<<<nimg * nh, kAttThreads, AttF32Smem::kTotal, st>>>(qkv, T, H, nh, scale, ctx);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }

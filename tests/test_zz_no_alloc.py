@@ -1,14 +1,15 @@
 """ig_attention_noalloc — the allocation-free attention entry point.
 
-Callers that cannot allocate device memory (work recorded into a CUDA graph,
-servers that reserve all device memory at start-up, paths that must not let
-cudaMalloc/cudaFree synchronize the device) use this variant; its work
-buffers live in a fixed 32 MiB array inside the library. The test calls it
+Callers that cannot allocate device memory (servers that reserve all device
+memory at start-up, paths that must not let cudaMalloc/cudaFree synchronize
+the device) use this variant; its work buffers live in a fixed 32 MiB array
+inside the library. The test calls it
 through the C ABI twice in a row, on different inputs, and checks each
 result against the allocating entry point ig_attention (bit for bit, the
 tolerance every attention test here uses), so contents left in the shared
 array by one call cannot leak into the next. It also checks that inputs too
-large for the array are refused with a clear error before any GPU work.
+large for the array, or sequences longer than its attend kernel takes, are
+refused with a clear error before any GPU work.
 
 This file is collected last on purpose: if it fails, a run that stops at the
 first failure has already run every other test.
@@ -64,3 +65,14 @@ def test_noalloc_rejects_oversize(igdev):
                                            torch.cuda.current_stream().cuda_stream)
     assert rc == _capi.IG_ERR_BAD_ARG
     assert "bytes of scratch" in _capi.last_error()
+
+
+def test_noalloc_rejects_overlong_sequence(igdev):
+    from indecis_b200 import _capi
+    H, nh = 256, 4
+    offs = np.array([0, 11000], np.int64)  # fits the scratch array, but over the 10240-token limit
+    small = torch.zeros((1, 3 * H), dtype=torch.float32, device="cuda")
+    rc = _capi.load().ig_attention_noalloc(small.data_ptr(), H, nh, offs.ctypes.data, 1, -1, 8, small.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream)
+    assert rc == _capi.IG_ERR_UNSUPPORTED
+    assert "longer than the 10240" in _capi.last_error()
