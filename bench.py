@@ -48,9 +48,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target length of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c1-f32", "c5"],
+    ap.add_argument("--workload", default="c1", choices=["c1", "c1-f32", "c3", "c3-varlen", "c4", "c5"],
                     help="c1: the ModernBERT headline (default); c1-f32: the same model on the float32 path "
-                         "(SetInt8(false)); c5: the SigLIP ViT-B/16 vision tower")
+                         "(SetInt8(false)); c3: 8 x 4096-token sequences; c3-varlen: 256 sequences of U[8,512] "
+                         "tokens; c4: the base-size model on 256 x 512 tokens; c5: the SigLIP ViT-B/16 vision tower")
     ap.add_argument("--images-per-step", type=int, default=512, help="c5: images per step, shared by all ranks")
     return ap.parse_args()
 
@@ -181,99 +182,162 @@ def workload(seqs: int, seed: int):
     return S.ids_fixed(seqs, SEQ_LEN, S.C1["vocab"], seed=seed)
 
 
-def config_obj(args, world):
-    return {"workload": "C1 ModernBERT int8 forward + heads (vocab 16384, hidden 256, 6 layers, 4x64 heads, GeGLU 384, "
-                        "local 128 / global every 3rd), noul+choice5+score5+spans9 heads",
-            "seq_len": SEQ_LEN, "batch": BATCH, "seqs_per_step_per_gpu": args.seqs_per_step,
-            "batches_per_step_per_gpu": args.seqs_per_step // BATCH, "global_batch": args.seqs_per_step * world,
-            "parallelism": f"sequence shard x{world}, no collective",
-            "l2": "inputs and activations larger than L2 (x alone is seqs*128*1 KiB)", "weights": "random-init seed 42"}
+# The encoder workloads. `per_gpu` sequences per GPU per step (the global
+# batch is per_gpu x N, cut into one contiguous cost-balanced range per rank);
+# `make(nseq)` draws the global batch with the config's seed.
+def encoder_spec(args):
+    from indecis_b200 import synthetic as S
+    w = args.workload
+    if w in ("c1", "c1-f32"):
+        return dict(name=w, cfg=S.C1, per_gpu=args.seqs_per_step, heads=True,
+                    make=lambda n: S.ids_fixed(n, SEQ_LEN, S.C1["vocab"], seed=1),
+                    metric=METRIC_F32 if w == "c1-f32" else METRIC,
+                    desc="C1 ModernBERT int8 forward + heads (vocab 16384, hidden 256, 6 layers, 4x64 heads, GeGLU "
+                         "384, local 128 / global every 3rd), noul+choice5+score5+spans9 heads",
+                    shape={"seq_len": SEQ_LEN, "batch": BATCH})
+    if w == "c3":
+        return dict(name=w, cfg=S.C1, per_gpu=8, heads=False,
+                    make=lambda n: S.ids_fixed(n, 4096, S.C1["vocab"], seed=31),
+                    metric="int8 encoder seq/s (4096 tok)",
+                    desc="C3 long inputs: the C1 model (6 layers, layers 0 and 3 global over all 4096 tokens, the "
+                         "others local 128), 8 x 4096 tokens, mean-pooled output",
+                    shape={"seq_len": 4096, "batch": 8})
+    if w == "c3-varlen":
+        return dict(name=w, cfg=S.C1, per_gpu=256, heads=False,
+                    make=lambda n: S.ids_varlen(n, 8, 512, S.C1["vocab"], seed=3),
+                    metric="int8 encoder seq/s (varlen U[8,512])",
+                    desc="C3 variable-length unpadded batch: the C1 model, 256 sequences of U[8,512] tokens (seed 3), "
+                         "mean-pooled output",
+                    shape={"seq_len": "U[8,512]", "batch": 256})
+    if w == "c4":
+        return dict(name=w, cfg=S.C4, per_gpu=256, heads=False,
+                    make=lambda n: S.ids_fixed(n, 512, S.C4["vocab"], seed=41),
+                    metric="int8 encoder seq/s (512 tok, base)",
+                    desc="C4 base ModernBERT int8 encoder (vocab 262144, hidden 768, 22 layers, 12x64 heads, GeGLU "
+                         "1152, local 128 / global every 3rd), 256 x 512 tokens, mean-pooled embedding output",
+                    shape={"seq_len": 512, "batch": 256})
+    raise ValueError(w)
+
+
+def config_obj(args, world, spec=None):
+    spec = spec or encoder_spec(args)
+    per = spec["per_gpu"]
+    c = {"workload": spec["desc"], **spec["shape"], "seqs_per_step_per_gpu": per, "global_batch": per * world,
+         "parallelism": f"sequence shard x{world} (contiguous cost-balanced ranges of one global batch), no collective",
+         "weights": "random-init seed 42"}
+    if spec["name"] in ("c1", "c1-f32"):
+        c["batches_per_step_per_gpu"] = per // BATCH
+        c["l2"] = "inputs and activations larger than L2 (x alone is seqs*128*1 KiB)"
+    elif spec["name"] == "c4":
+        c["l2"] = "inputs and activations larger than L2 (x alone is 256*512*3 KiB = 384 MiB)"
+    else:
+        c["l2"] = "L2 flushed (256 MiB write, untimed) before every timed step"
+    return c
 
 
 # ---------------------------------------------------------------------------
 # CPU legs (the oracle port of the reference path; test/bench infrastructure)
 # ---------------------------------------------------------------------------
 
-def cpu_model():
+def cpu_model(spec):
     import oracle
     from indecis_b200 import synthetic as S
     oracle.build()
-    model = oracle.Model(S.C1, S.weights(S.C1, seed=42))
-    model.heads = S.heads(S.C1["hidden"])
+    model = oracle.Model(spec["cfg"], S.weights(spec["cfg"], seed=42))
+    model.heads = S.heads(spec["cfg"]["hidden"]) if spec["heads"] else []
     return model, oracle
 
 
-def cpu_sample(model, batches: int, threads: int, seed: int = 1):
-    """Encoder + heads on `batches` batches of 32x128: token states, float64
-    mean pooling in token order, then every head's float64 logits."""
+# Sequences per CPU call: C1 goes in the reference's batches of 32
+# (forEachPooled, model.go:391-415); a long or base-size sequence alone.
+CPU_UNIT = {"c1": BATCH, "c1-f32": BATCH, "c3": 1, "c3-varlen": 16, "c4": 1}
+
+
+def cpu_sample(model, spec, ids, offs, units: int, threads: int, f32: bool = False):
+    """The oracle port over the first `units` CPU calls of the batch: for the
+    heads workloads token states, float64 mean pooling in token order and
+    every head's float64 logits; otherwise the pooled encoder output.
+    Returns (seconds, sequences)."""
     import oracle
-    ids, offs = workload(batches * BATCH, seed)
+    u = CPU_UNIT[spec["name"]]
     t0 = time.perf_counter()
-    for b in range(batches):
-        lo, hi = b * BATCH, (b + 1) * BATCH
+    done = 0
+    for b in range(units):
+        lo, hi = b * u, min((b + 1) * u, len(offs) - 1)
+        if lo >= hi:
+            break
         o = offs[lo:hi + 1] - offs[lo]
-        tokens = model.encode(ids[offs[lo]:offs[hi]], o, mode=1, threads=threads, fast=True)
-        pooled = np.stack([tokens[o[i]:o[i + 1]].astype(np.float64).mean(0) for i in range(BATCH)]).astype(np.float32)
-        for h in model.heads:
-            oracle.head_logits(h["w"], h["b"], tokens if h["kind"] == "spans" else pooled)
-    return time.perf_counter() - t0
+        x = ids[offs[lo]:offs[hi]]
+        if f32:
+            model.encode_f32(x, o, threads=threads)
+        elif model.heads:
+            tokens = model.encode(x, o, mode=1, threads=threads, fast=True)
+            pooled = np.stack([tokens[o[i]:o[i + 1]].astype(np.float64).mean(0)
+                               for i in range(hi - lo)]).astype(np.float32)
+            for h in model.heads:
+                oracle.head_logits(h["w"], h["b"], tokens if h["kind"] == "spans" else pooled)
+        else:
+            model.encode(x, o, mode=0, threads=threads, fast=True)
+        done += hi - lo
+    return time.perf_counter() - t0, done
 
 
-def cpu_baseline(target_s: float):
-    model, oracle = cpu_model()
-    threads = os.cpu_count() or 1
-    t1 = cpu_sample(model, 1, threads)
-    batches = int(max(1, min(200, target_s / max(t1, 1e-3))))
-    t = cpu_sample(model, batches, threads, seed=2)
+def cpu_isa(oracle):
     feats = oracle.lib().or_cpu_features()
-    isa = "AVX-VNNI" if feats & 1 else ("AVX512-VNNI" if feats & 2 else "scalar int")
-    return {"value": batches * BATCH / t, "unit": "seq/s", "cores": threads, "kind": "port",
-            "sample": f"{batches} batches of 32x128 (C1), oracle C++ port of the reference int8 path, {isa} 6x16 "
-                      f"tiles, {threads} threads, {t:.1f} s"}
+    return "AVX-VNNI" if feats & 1 else ("AVX512-VNNI" if feats & 2 else "scalar int")
 
 
-def cpu_baseline_f32(target_s: float):
-    """The float32 path of the oracle port on all host threads, a bounded sample."""
-    model, oracle = cpu_model()
+def cpu_baseline(spec, target_s: float, f32: bool = False):
+    """The oracle port on all host threads, a bounded sample (about target_s)
+    of the workload's own sequences."""
+    model, oracle = cpu_model(spec)
     threads = os.cpu_count() or 1
-    ids, offs = workload(BATCH, 7)
-    t0 = time.perf_counter()
-    model.encode_f32(ids, offs, threads=threads)
-    t1 = time.perf_counter() - t0
-    batches = int(max(1, min(50, target_s / max(t1, 1e-3))))
-    ids, offs = workload(batches * BATCH, 8)
-    t0 = time.perf_counter()
-    model.encode_f32(ids, offs, threads=threads)
-    t = time.perf_counter() - t0
-    return {"value": batches * BATCH / t, "unit": "seq/s", "cores": threads, "kind": "port",
-            "sample": f"{batches} batches of 32x128 (C1) through the oracle's float32 path (scalar FMA chains), "
-                      f"{threads} threads, {t:.1f} s"}
+    ids, offs = spec["make"](max(spec["per_gpu"], 200 * CPU_UNIT[spec["name"]]))
+    t1, _ = cpu_sample(model, spec, ids, offs, 1, threads, f32)  # warm-up, and the size of one call
+    units = int(max(1, min(200, target_s / max(t1, 1e-3))))
+    t, n = cpu_sample(model, spec, ids, offs, units, threads, f32)
+    path = "float32 path (scalar FMA chains)" if f32 else f"int8 path, {cpu_isa(oracle)} 6x16 tiles"
+    return {"value": n / t, "unit": "seq/s", "cores": threads, "kind": "port",
+            "sample": f"{n} sequences of the workload in calls of {CPU_UNIT[spec['name']]}, oracle C++ port of the "
+                      f"reference {path}, {threads} threads, {t:.1f} s"}
 
 
 def run_reference(args, world, rank):
     """The reference's CPU implementation of the path (the oracle port, since
-    the Go reference cannot run on this image), on all host threads."""
+    the Go reference cannot run on this image), on all host threads; each
+    step one CPU call of the workload (a bounded sample)."""
     if rank != 0:
         return
-    model, oracle = cpu_model()
+    spec = encoder_spec(args)
+    f32 = args.workload == "c1-f32"
+    model, oracle = cpu_model(spec)
     threads = os.cpu_count() or 1
-    for _ in range(args.warmup):
-        cpu_sample(model, 1, threads)
-    ts = [cpu_sample(model, 1, threads, seed=3 + k) for k in range(args.steps)]
-    total = sum(ts)
-    v = args.steps * BATCH / total
-    feats = oracle.lib().or_cpu_features()
-    isa = "AVX-VNNI" if feats & 1 else ("AVX512-VNNI" if feats & 2 else "scalar int")
-    line = {"metric": METRIC, "value": v, "unit": "seq/s", "impl": "reference", "n_gpus": args.gpus,
+    u = CPU_UNIT[spec["name"]]
+    ids, offs = spec["make"](max(spec["per_gpu"], (args.steps + args.warmup) * u))
+    for k in range(args.warmup):
+        cpu_sample(model, spec, *shift(ids, offs, k * u), 1, threads, f32)
+    total, n = 0.0, 0
+    for k in range(args.steps):
+        t, m = cpu_sample(model, spec, *shift(ids, offs, (args.warmup + k) * u), 1, threads, f32)
+        total, n = total + t, n + m
+    v = n / total
+    path = "float32 path" if f32 else f"int8 path, {cpu_isa(oracle)}"
+    line = {"metric": spec["metric"], "value": v, "unit": "seq/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {**config_obj(args, 1), "seqs_per_step_per_gpu": BATCH, "batches_per_step_per_gpu": 1,
-                       "global_batch": BATCH, "note": "one 32x128 batch per step (bounded CPU sample)"},
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32" if f32 else "int8",
+            "data": "synthetic", "config": config_obj(args, args.gpus, spec),
             "cpu_baseline": {"value": v, "unit": "seq/s", "cores": threads, "kind": "port",
-                             "sample": f"one 32x128 batch per step, oracle C++ port (Go reference not runnable: no Go "
-                                       f"toolchain), {isa}, {threads} threads"},
+                             "sample": f"each step one CPU call of {u} sequence(s) of the workload (bounded sample), "
+                                       f"oracle C++ port of the reference {path} (Go reference not runnable: no Go "
+                                       f"toolchain), {threads} threads"},
             "e2e": {"value": v, "unit": "seq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
+
+
+def shift(ids, offs, s0):
+    """The batch from sequence s0 on (offsets rebased)."""
+    t0 = int(offs[s0])
+    return ids[t0:], offs[s0:] - t0
 
 
 # ---------------------------------------------------------------------------
@@ -295,7 +359,7 @@ NCU_BYTES_PER_SEQ = {
 }
 
 
-def roofline(report, pk, nseq):
+def roofline(report, pk, nseq, workload="c1"):
     ks = [k for k in report["kernels"] if k["records"] > 0 and k["ms"] > 0]
     top = max(ks, key=lambda k: k["ms"])
     total_ms = sum(k["ms"] for k in ks)
@@ -315,7 +379,7 @@ def roofline(report, pk, nseq):
         peak_note = f"{pk['src']} HBM copy bandwidth"
     rf.update({"kernel": top["name"], "share": top["ms"] / total_ms, "ms_per_launch": per_ms,
                "algorithmic_bytes": bytes_, "algorithmic_ops": ops, "peak_source": peak_note})
-    per_seq = NCU_BYTES_PER_SEQ.get(top["name"])
+    per_seq = NCU_BYTES_PER_SEQ.get(top["name"]) if workload == "c1" else None
     rf["traffic"] = per_seq * nseq if per_seq else None
     rf["traffic_source"] = "ncu dram bytes at 512 sequences, scaled" if per_seq else None
     return rf
@@ -372,55 +436,113 @@ def gemm_sweep(pk):
             "int8_peak_tops": 2.0 * pk["bf16"], "int8_peak_source": "2 x measured bf16 burst (no int8 entry)"}
 
 
-def run_ours(args, world, rank, local):
+def dist_init(world, local):
+    import datetime
     import torch
-    from indecis_b200 import _capi, build
-    from indecis_b200 import synthetic as S
-    from indecis_b200.model import Config, Head, Model
-
     torch.cuda.set_device(local)
     if world > 1:
         import torch.distributed as dist
-        import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, v):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def batch32_calls(model, spec, heads):
+    """The literal call shape of the reference's callers: EncodeSeqs / Decide
+    batches of 32 sequences (forEachPooled, model.go:391-415), each one host
+    call of ig_logits (ids from host memory, float64 logits back). Sequential
+    calls from one thread, then 8 threads calling concurrently."""
+    import threading
+    ids, offs = spec["make"](32 * 64)
+    batches = [shift(ids, offs, 32 * k) for k in range(64)]
+    batches = [(x[:int(o[32])], o[:33]) for x, o in batches]
+    for b in batches[:4]:
+        model.Logits(b)
+    t0 = time.perf_counter()
+    for b in batches:
+        model.Logits(b)
+    seq_s = time.perf_counter() - t0
+
+    def client(k):
+        for b in batches[k::8]:
+            model.Logits(b)
+
+    ts = [threading.Thread(target=client, args=(k,)) for k in range(8)]
+    t0 = time.perf_counter()
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    par_s = time.perf_counter() - t0
+    n = 32 * len(batches)
+    return {"seqs_per_call": 32, "calls": len(batches), "ms_per_call": 1000 * seq_s / len(batches),
+            "seq_s_one_caller": n / seq_s, "seq_s_8_callers": n / par_s,
+            "api": "ig_logits, host buffers, one 32x128 batch per call"}
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    from indecis_b200 import _capi, build, shard
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Config, Head, Model
+
+    spec = encoder_spec(args)
+    dist_init(world, local)
     build.build()
     pk = peaks()
-    cfg = Config.from_dict(S.C1)
-    model = Model.from_arrays(cfg, S.weights(S.C1, seed=42), device=local)
-    heads = [Head(h["name"], h["kind"], h["w"], h["b"]) for h in S.heads(cfg.hidden_size)]
-    model.SetHeads(heads)
+    cfg = Config.from_dict(spec["cfg"])
+    model = Model.from_arrays(cfg, S.weights(spec["cfg"], seed=42), device=local)
+    heads = [Head(h["name"], h["kind"], h["w"], h["b"]) for h in S.heads(cfg.hidden_size)] if spec["heads"] else []
+    if heads:
+        model.SetHeads(heads)
     f32 = args.workload == "c1-f32"
     if f32:
         model.SetInt8(False)
     L = _capi.load()
 
-    nseq = args.seqs_per_step
-    ids, offs = workload(nseq, seed=1 + rank)
+    # The global batch, cut into one contiguous cost-balanced range per rank
+    # (every rank derives the same cut from the same offsets).
+    gids, goffs = spec["make"](spec["per_gpu"] * world)
+    costs = shard.seq_costs(goffs, cfg.num_hidden_layers, cfg.global_attn_every_n_layers, cfg.local_attention,
+                            cfg.hidden_size)
+    s0, s1 = shard.shard_ranges(goffs, world, costs)[rank]
+    ids, offs = shard.local_batch(gids, goffs, s0, s1)
+    nseq = s1 - s0
     N = int(offs[-1])
+    H = cfg.hidden_size
     pooled_rows = sum(h.rows for h in heads if h.kind != "spans")
     token_rows = sum(h.rows for h in heads if h.kind == "spans")
     d_ids = torch.from_numpy(ids).cuda()
-    d_logits = torch.empty((nseq, pooled_rows), dtype=torch.float64, device="cuda")
-    d_tlog = torch.empty((N, token_rows), dtype=torch.float64, device="cuda")
     stream = torch.cuda.current_stream()
+    if heads:
+        d_logits = torch.empty((nseq, pooled_rows), dtype=torch.float64, device="cuda")
+        d_tlog = torch.empty((N, token_rows), dtype=torch.float64, device="cuda")
 
-    def step():
-        _capi.check(L.ig_logits_device(model._h, d_ids.data_ptr(), offs.ctypes.data, nseq, d_logits.data_ptr(),
-                                       d_tlog.data_ptr(), stream.cuda_stream))
+        def step():
+            _capi.check(L.ig_logits_device(model._h, d_ids.data_ptr(), offs.ctypes.data, nseq, d_logits.data_ptr(),
+                                           d_tlog.data_ptr(), stream.cuda_stream))
+    else:
+        d_out = torch.empty((nseq, H), dtype=torch.float32, device="cuda")
 
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
+        def step():
+            _capi.check(L.ig_encode_device(model._h, d_ids.data_ptr(), offs.ctypes.data, nseq, _capi.IG_MODE_POOLED,
+                                           d_out.data_ptr(), stream.cuda_stream))
 
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        import torch.distributed as dist
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if spec["name"] in ("c3", "c3-varlen") else None
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -428,69 +550,88 @@ def run_ours(args, world, rank, local):
     # ---- timed region: device events on the launching stream -------------
     clocks = Clocks(physical_gpu(local))
     _capi.profile(True)
-    barrier()
+    barrier(world)
     torch.cuda.synchronize()
     clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_local = e0.elapsed_time(e1)
+    else:
+        # the L2 is flushed before every step, outside the timed events
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for e0, e1 in ev:
+            flush.fill_(1)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms_local = sum(e0.elapsed_time(e1) for e0, e1 in ev)
+    barrier(world)
     clk = clocks.stop()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms = max_over_ranks(world, ms_local)
     report = _capi.profile_report()
     _capi.profile(False)
-    value = world * nseq * args.steps / (ms / 1e3)
+    gseq = spec["per_gpu"] * world
+    value = gseq * args.steps / (ms / 1e3)
     dev_err = L.ig_device_error(1)
     if dev_err:
         raise RuntimeError(f"device error {dev_err}")
+    del flush
 
-    # ---- end to end: the host API (ids from host memory, logits back) -----
+    # ---- end to end: the host API (ids from host memory, results back) ----
     e2e_steps = max(3, min(args.steps, 20))
     seqs = (ids, offs)
-    model.Logits(seqs)
-    barrier()
+    run_host = (lambda: model.Logits(seqs)) if heads else (lambda: model.EncodeSeqs(seqs))
+    run_host()
+    barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        model.Logits(seqs)
+        run_host()
     torch.cuda.synchronize()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    # ids + offsets + the plan's block lists: per sequence of 128 tokens one
-    # 16-byte tensor-core entry per attention kind and one 8-byte float-path
+    e2e_s = max_over_ranks(world, time.perf_counter() - t0)
+    # ids + offsets + the plan's block lists: per sequence one 16-byte
+    # tensor-core entry per 128 queries and attention kind, and one 8-byte
     # entry per 64 queries (row tables are filled on the device)
     blocks = sum(2 * 16 * ((n + 127) // 128) + 8 * ((n + 63) // 64) for n in np.diff(offs).tolist())
     h2d = 4 * N + 4 * (nseq + 1) + blocks
-    d2h = 8 * nseq * pooled_rows + 8 * N * token_rows
-    e2e = {"value": world * nseq * e2e_steps / e2e_s, "unit": "seq/s", "h2d_bytes_per_step": h2d,
-           "d2h_bytes_per_step": d2h, "api": "ig_logits (host buffers, synchronous), host clock around "
-                                                "device-synchronized calls"}
+    d2h = 8 * nseq * pooled_rows + 8 * N * token_rows if heads else 4 * nseq * H
+    e2e = {"value": gseq * e2e_steps / e2e_s, "unit": "seq/s", "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h,
+           "api": ("ig_logits" if heads else "ig_encode (pooled)") + " (host buffers, synchronous), host clock around "
+                  "device-synchronized calls; each rank's call covers its range of the global batch"}
 
+    extra = {}
+    if rank == 0 and spec["name"] == "c1":
+        extra["c1_batch32"] = batch32_calls(model, spec, heads)
     gemm = None
-    if rank == 0 and not args.no_gemm and not f32:
+    if rank == 0 and not args.no_gemm and spec["name"] == "c1":
         gemm = gemm_sweep(pk)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.cpu_seconds) if not f32 else cpu_baseline_f32(args.cpu_seconds)
+        cpu = cpu_baseline(spec, args.cpu_seconds, f32)
 
     if rank == 0:
-        cfg_obj = config_obj(args, world)
+        cfg_obj = config_obj(args, world, spec)
         if f32:
             cfg_obj["path"] = "float32 (SetInt8(false)): float products in the reference's FMA-chain order"
-            rf = c5_roofline(report, pk, clk["sm_mhz"] if clk else None, fp32_names=F32_PATH_KERNELS)
+            rf = c5_roofline(report, pk, clk["sm_mhz"] if clk else None, fp32_names=F32_PATH_KERNELS)[0]
         else:
-            rf = roofline(report, pk, nseq)
-        line = {"metric": METRIC_F32 if f32 else METRIC, "value": value, "unit": "seq/s", "n_gpus": world,
+            rf = roofline(report, pk, nseq, spec["name"])
+        line = {"metric": spec["metric"], "value": value, "unit": "seq/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32" if f32 else "int8", "data": "synthetic",
-                "config": cfg_obj, "e2e": e2e, "gpu_launches": report["launches"],
-                "roofline": rf[0] if f32 else rf,
+                "config": cfg_obj, "e2e": e2e, "gpu_launches": report["launches"], "roofline": rf,
                 "kernels": {k["name"]: {"ms": round(k["ms"], 3), "launches": k["launches"]}
                             for k in report["kernels"]},
-                "clocks": clk, "cpu_baseline": cpu, "gemm_sweep": gemm}
+                "clocks": clk, "cpu_baseline": cpu, **extra, "gemm_sweep": gemm}
         emit(line)
+    model.close()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -108,6 +108,61 @@ typedef struct ig_embedding_table {
  * linalg/int8.go:36-77) on the device. */
 IG_API int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, ig_model **out);
 
+/* Tensor dtypes as a safetensors file stores them (safetensors.go:200-245). */
+#define IG_DT_F32 0
+#define IG_DT_BF16 1 /* value = bits << 16 */
+#define IG_DT_F16 2  /* IEEE binary16, widened exactly */
+#define IG_DT_I8 3   /* the integer's value */
+
+/* A host tensor in its stored dtype. */
+typedef struct ig_tensor {
+  int32_t dtype; /* IG_DT_* */
+  const void *data;
+} ig_tensor;
+
+/* The layer tensors of a model as its file stores them (Load reads every
+ * tensor but the embedding table decoded to float32, model.go:661-735, and
+ * the layer matrices lazily through SetCompact). Shapes as ig_weights;
+ * attn_norm[0] is ignored. The embedding table comes separately, as stored,
+ * through ig_model_set_embeddings (required before encoding). */
+typedef struct ig_stored_weights {
+  ig_tensor emb_norm, final_norm;
+  const ig_tensor *attn_norm, *wqkv, *wo, *mlp_norm, *wi, *wo_mlp; /* [layers] */
+} ig_stored_weights;
+
+/* ig_model_create from tensors as stored: each is copied to the device in
+ * its own dtype (half the bytes of float32 for bf16 checkpoints) and decoded
+ * there exactly as the reference's safetensors reader decodes it (decode,
+ * safetensors.go:218-245) before PackB8; the result is bit-identical to
+ * ig_model_create on the decoded float32 tensors. Errors: IG_ERR_BAD_ARG for
+ * a missing tensor or an unknown dtype. */
+IG_API int ig_model_create_stored(const ig_config *cfg, const ig_stored_weights *w, int32_t device, ig_model **out);
+
+/* ig_model_create on several GPUs of this process: one replica of the
+ * weights per listed device. The host entry points (ig_encode, ig_logits,
+ * ig_window_logits, ig_infer_windows, the batcher) split each call's
+ * sequences into contiguous ranges balanced by cost (GEMM work ~ n,
+ * attention ~ n x keys per query), encode every range on its own GPU from
+ * its own host thread, and write each range's rows into its slice of the
+ * caller's output: no collective, no peer memory. Calls under 8192 rows per
+ * GPU use fewer GPUs, those with the fewest calls in flight. Results are
+ * bit-identical to one device's (sequences are independent:
+ * linalg/int8_test.go:149, concurrency_test.go:51-60). This is the batch
+ * sharding across the GPUs of one box that EncodeSeqs' callers
+ * (model.go:391-426, batch.go:24-81) reach with no change. One device listed:
+ * the same as ig_model_create. The device-buffer entry points
+ * (ig_encode_device, ig_logits_device) take a replica (ig_model_replica). */
+IG_API int ig_model_create_multi(const ig_config *cfg, const ig_weights *w, const int32_t *devices, int32_t ndevices,
+                                 ig_model **out);
+/* ig_model_create_stored on several GPUs, as ig_model_create_multi. */
+IG_API int ig_model_create_stored_multi(const ig_config *cfg, const ig_stored_weights *w, const int32_t *devices,
+                                        int32_t ndevices, ig_model **out);
+/* Replica `index` of a model and its device (the model itself, index 0, for
+ * a single-device model); borrowed: destroyed with the model. */
+IG_API int ig_model_replica(ig_model *m, int32_t index, ig_model **replica, int32_t *device);
+/* Number of devices a model runs on. */
+IG_API int ig_model_device_count(ig_model *m, int32_t *n);
+
 /* Releases the model's device memory. Replaces Invalidate (infer.go:95-100)
  * for the device copy: a changed model is destroyed and created again. */
 IG_API void ig_model_destroy(ig_model *m);

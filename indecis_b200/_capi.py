@@ -31,7 +31,8 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_vision_forward_device", "ig_vision_dump_layer", "ig_model_dims", "ig_batcher_create",
            "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats",
            "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags", "ig_model_set_int8",
-           "ig_check_gelu_division"]
+           "ig_check_gelu_division", "ig_model_create_multi", "ig_model_replica", "ig_model_device_count",
+           "ig_model_create_stored", "ig_model_create_stored_multi"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -50,6 +51,19 @@ class IgWeights(C.Structure):
                 ("attn_norm", C.POINTER(C.c_void_p)), ("wqkv", C.POINTER(C.c_void_p)),
                 ("wo", C.POINTER(C.c_void_p)), ("mlp_norm", C.POINTER(C.c_void_p)),
                 ("wi", C.POINTER(C.c_void_p)), ("wo_mlp", C.POINTER(C.c_void_p))]
+
+
+IG_DT = {"F32": 0, "BF16": 1, "F16": 2, "I8": 3}
+
+
+class IgTensor(C.Structure):
+    _fields_ = [("dtype", C.c_int32), ("data", C.c_void_p)]
+
+
+class IgStoredWeights(C.Structure):
+    _fields_ = [("emb_norm", IgTensor), ("final_norm", IgTensor), ("attn_norm", C.POINTER(IgTensor)),
+                ("wqkv", C.POINTER(IgTensor)), ("wo", C.POINTER(IgTensor)), ("mlp_norm", C.POINTER(IgTensor)),
+                ("wi", C.POINTER(IgTensor)), ("wo_mlp", C.POINTER(IgTensor))]
 
 
 class IgEmbeddingTable(C.Structure):
@@ -116,8 +130,15 @@ def load() -> C.CDLL:
         raise LibraryMissing(f"{LIB_PATH} is not built: run `python -m indecis_b200.build` (no CPU fallback exists)")
     L = C.CDLL(LIB_PATH)
     vp, i32, i64p = C.c_void_p, C.c_int32, C.POINTER(C.c_int64)
+    i32p = C.POINTER(C.c_int32)
     L.ig_model_create.argtypes = [C.POINTER(IgConfig), C.POINTER(IgWeights), i32, C.POINTER(C.c_void_p)]
     L.ig_model_create.restype = C.c_int
+    L.ig_model_create_multi.argtypes = [C.POINTER(IgConfig), C.POINTER(IgWeights), i32p, i32, C.POINTER(C.c_void_p)]
+    L.ig_model_create_stored.argtypes = [C.POINTER(IgConfig), C.POINTER(IgStoredWeights), i32, C.POINTER(C.c_void_p)]
+    L.ig_model_create_stored_multi.argtypes = [C.POINTER(IgConfig), C.POINTER(IgStoredWeights), i32p, i32,
+                                               C.POINTER(C.c_void_p)]
+    L.ig_model_replica.argtypes = [vp, i32, C.POINTER(C.c_void_p), i32p]
+    L.ig_model_device_count.argtypes = [vp, i32p]
     L.ig_model_destroy.argtypes = [vp]
     L.ig_model_destroy.restype = None
     L.ig_model_set_heads.argtypes = [vp, i32, C.POINTER(IgHead)]
@@ -137,7 +158,7 @@ def load() -> C.CDLL:
     L.ig_attention_noalloc.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
     L.ig_check_gelu_division.argtypes = [vp, vp, vp]
     L.ig_model_set_embeddings.argtypes = [vp, C.POINTER(IgEmbeddingTable)]
-    i32p, f64 = C.POINTER(C.c_int32), C.c_double
+    f64 = C.c_double
     L.ig_plan_windows.argtypes = [i32, i32, i32, C.POINTER(IgWindow), i32, i32p]
     L.ig_log_softmax.argtypes = [vp, i32, f64, vp]
     L.ig_decode_spans.argtypes = [vp, i32, i32, f64, C.c_char_p, C.c_int64, vp, vp, C.POINTER(IgSpan), i32, i32p]

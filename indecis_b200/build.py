@@ -15,7 +15,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libindecis_b200.so")
 SOURCES = ["libindecis_b200.cu", "spans.cpp", "batcher.cpp"]
-HEADERS = ["common.cuh", "exactmath.cuh", "internal.h", "gemm_i8.cu", "gemm_persist.cu", "gemm_pair.cu", "rows_fast.cu", "rows.cu", "rows_ln.cu", "attention.cu", "attention_tc.cu", "attention_short.cu", "siglip.cu", "encoder_f32.cu", "capi.cu", "siglip_capi.cu", "spans_device.cu", "noalloc.cu", "selfcheck.cu"]
+HEADERS = ["common.cuh", "exactmath.cuh", "internal.h", "gemm_i8.cu", "gemm_persist.cu", "gemm_pair.cu", "rows_fast.cu", "rows.cu", "rows_ln.cu", "attention.cu", "attention_tc.cu", "attention_short.cu", "siglip.cu", "encoder_f32.cu", "capi.cu", "multi.cu", "siglip_capi.cu", "spans_device.cu", "noalloc.cu", "selfcheck.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -195,6 +195,33 @@ struct Workspace {
   }
 };
 
+// Stored elements -> float32, exactly as the reference decodes them on read
+// (safetensors decode, safetensors/safetensors.go:218-245): BF16 is the
+// high half of the float32 bits; F16 is IEEE binary16 widened exactly (signed
+// zeros, subnormals scaled by 2^-24, infinities and NaNs with their payload
+// moved to the top of the float32 mantissa); I8 is the integer's value.
+__global__ void widen_kernel(const void *__restrict__ src, int dtype, size_t n, float *__restrict__ dst) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    float v;
+    if (dtype == IG_DT_BF16) {
+      v = __uint_as_float((uint32_t)static_cast<const uint16_t *>(src)[i] << 16);
+    } else if (dtype == IG_DT_F16) {
+      const uint32_t h = static_cast<const uint16_t *>(src)[i];
+      const uint32_t sign = (h >> 15) << 31, e = (h >> 10) & 0x1f, f = h & 0x3ff;
+      if (e == 0) {
+        v = __uint_as_float(sign | __float_as_uint(__fmul_rn((float)f, 0x1p-24f)));  // zero or subnormal: exact
+      } else if (e == 0x1f) {
+        v = __uint_as_float(sign | 0x7f800000u | (f << 13));
+      } else {
+        v = __uint_as_float(sign | ((e + 112) << 23) | (f << 13));
+      }
+    } else {
+      v = (float)static_cast<const int8_t *>(src)[i];
+    }
+    dst[i] = v;
+  }
+}
+
 }  // namespace ig
 
 using namespace ig;
@@ -215,7 +242,15 @@ struct ig_model {
   std::vector<DevHead> heads;
   std::vector<std::unique_ptr<Workspace>> pool;
   std::vector<void *> allocs;
+  // A model on several GPUs (ig_model_create_multi): one replica per device,
+  // owned; the group itself holds no device memory.
+  std::vector<ig_model *> replicas;
+  std::atomic<int> inflight{0};  // host calls running on this model (shard placement)
   ~ig_model() {
+    if (!replicas.empty()) {
+      for (ig_model *r : replicas) delete r;
+      return;
+    }
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(device);
@@ -258,9 +293,9 @@ int upload(ig_model *m, float **dst, const float *src, size_t count) {
   return 0;
 }
 
-// Quantizes a float32 [n][k] host matrix into a DevMat with n_out packed
+// Quantizes a float32 [n][k] device matrix into a DevMat with n_out packed
 // rows (perm chooses their source rows).
-int pack_matrix(ig_model *m, DevMat &dm, const float *w, int n, int k, const std::vector<int32_t> &perm, float *tmp,
+int pack_matrix(ig_model *m, DevMat &dm, const float *d_w, int n, int k, const std::vector<int32_t> &perm,
                 int32_t *d_perm) {
   const int n_out = perm.empty() ? n : (int)perm.size();
   dm.n = n_out;
@@ -269,13 +304,50 @@ int pack_matrix(ig_model *m, DevMat &dm, const float *w, int n, int k, const std
   IG_TRY(dev_alloc(m, &dm.q, (size_t)n_out * dm.ld));
   IG_TRY(dev_alloc(m, &dm.scale, n_out));
   IG_TRY(dev_alloc(m, &dm.zc, n_out));
-  IG_CU(cudaMemcpy(tmp, w, (size_t)n * k * sizeof(float), cudaMemcpyHostToDevice));
   if (!perm.empty()) IG_CU(cudaMemcpy(d_perm, perm.data(), perm.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
-  IG_TRY(launch_pack_b8(tmp, n, k, perm.empty() ? nullptr : d_perm, n_out, dm.q, dm.ld, dm.scale, dm.zc, nullptr,
+  IG_TRY(launch_pack_b8(d_w, n, k, perm.empty() ? nullptr : d_perm, n_out, dm.q, dm.ld, dm.scale, dm.zc, nullptr,
                         0));
   IG_CU(cudaDeviceSynchronize());
   return 0;
 }
+
+// A host tensor as its safetensors file stores it.
+struct TensorView {
+  int dtype;  // IG_DT_*
+  const void *data;
+};
+
+size_t dtype_size(int dtype) {
+  return dtype == IG_DT_F32 ? 4 : dtype == IG_DT_I8 ? 1 : 2;
+}
+
+// Fills n float32 elements of device memory from a stored host tensor; stage
+// is a device buffer of at least 2n bytes for the narrow formats.
+int fetch_f32(float *dst, const TensorView &t, size_t n, void *stage) {
+  if (!t.data) return fail(IG_ERR_BAD_ARG, "modernbert: tensor missing");
+  if (t.dtype == IG_DT_F32) {
+    IG_CU(cudaMemcpy(dst, t.data, n * sizeof(float), cudaMemcpyHostToDevice));
+    return 0;
+  }
+  if (t.dtype != IG_DT_BF16 && t.dtype != IG_DT_F16 && t.dtype != IG_DT_I8)
+    return fail(IG_ERR_BAD_ARG, "unsupported dtype " + std::to_string(t.dtype));
+  IG_CU(cudaMemcpy(stage, t.data, n * dtype_size(t.dtype), cudaMemcpyHostToDevice));
+  widen_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256>>>(stage, t.dtype, n, dst);
+  IG_CU(cudaGetLastError());
+  return 0;
+}
+
+int upload_view(ig_model *m, float **dst, const TensorView &t, size_t count, void *stage) {
+  IG_TRY(dev_alloc(m, dst, count));
+  return fetch_f32(*dst, t, count, stage);
+}
+
+// The weights a model is made from: every tensor as its file stores it.
+struct WeightSource {
+  const float *tok_embeddings;  // float32 table, or NULL
+  TensorView emb_norm, final_norm;
+  std::vector<TensorView> attn_norm, wqkv, wo, mlp_norm, wi, wo_mlp;
+};
 
 // RoPE cos/sin of the reference's table (internal/modernbert/model.go:255-277),
 // computed on the host in float64 as there, for npos positions.
@@ -1067,10 +1139,21 @@ int run_tail_staged(ig_model *m, Workspace &w, const Plan &p, int mode, cudaStre
   return 0;
 }
 
+// Host calls on a model spread over several GPUs (multi.cu).
+int encode_group(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
+                 size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len);
+
 int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
                 size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len) {
   t_last_error.clear();
   if (!m || (nseq > 0 && !offs)) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (!m->replicas.empty())
+    return encode_group(m, ids, offs, nseq, mode, out, out_len, dump, logits, logits_len, tlog, tlog_len);
+  struct InFlight {
+    std::atomic<int> &n;
+    explicit InFlight(std::atomic<int> &c) : n(c) { n++; }
+    ~InFlight() { n--; }
+  } inflight(m->inflight);
   if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS && !(mode == kModeMeanRows && !out))
     return fail(IG_ERR_BAD_ARG, "bad mode");
   DeviceGuard dg(m->device);
@@ -1142,9 +1225,13 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
 
 extern "C" {
 
-int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, ig_model **out) {
+}  // extern "C"
+
+namespace {
+
+int create_model(const ig_config *cfg, const WeightSource &w, int32_t device, ig_model **out) {
   t_last_error.clear();
-  if (!cfg || !w || !out) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (!cfg || !out) return fail(IG_ERR_BAD_ARG, "null argument");
   *out = nullptr;
   const ig_config &c = *cfg;
   // Config.validate (internal/modernbert/model.go:64-80).
@@ -1158,6 +1245,11 @@ int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, i
   if (c.simd_lanes < 1 || c.simd_lanes > 32) return fail(IG_ERR_BAD_ARG, "simd_lanes must be in [1, 32]");
   if (c.hidden / c.heads != 64) return fail(IG_ERR_UNSUPPORTED, "head dimension must be 64 in this build");
   if (c.hidden > 4096 || c.intermediate > 8192) return fail(IG_ERR_UNSUPPORTED, "hidden/intermediate too large");
+  for (int l = 0; l < c.layers; l++)
+    if (!w.wqkv[l].data || !w.wo[l].data || !w.wi[l].data || !w.wo_mlp[l].data || !w.mlp_norm[l].data ||
+        (l > 0 && !w.attn_norm[l].data))
+      return fail(IG_ERR_BAD_ARG, "modernbert: tensor of layer " + std::to_string(l) + " missing");
+  if (!w.emb_norm.data || !w.final_norm.data) return fail(IG_ERR_BAD_ARG, "modernbert: norm tensor missing");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
     return fail(IG_ERR_NO_DEVICE, "no such CUDA device");
@@ -1175,21 +1267,28 @@ int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, i
   m->ldk = (int)align_up(std::max(c.hidden, c.intermediate), 16);
   m->NI = (c.intermediate + 127) / 128 * 256;
   const int H = m->H, I = m->I;
-  if (w->tok_embeddings) {
+  if (w.tok_embeddings) {
     float *e = nullptr;
     IG_CU(cudaMalloc(&e, (size_t)c.vocab * H * sizeof(float)));
     m->emb_allocs.push_back(e);
-    IG_CU(cudaMemcpy(e, w->tok_embeddings, (size_t)c.vocab * H * sizeof(float), cudaMemcpyHostToDevice));
+    IG_CU(cudaMemcpy(e, w.tok_embeddings, (size_t)c.vocab * H * sizeof(float), cudaMemcpyHostToDevice));
     m->emb.fmt = IG_EMB_F32;
     m->emb.f32 = e;
   }
-  IG_TRY(upload(m.get(), &m->emb_norm, w->emb_norm, H));
-  IG_TRY(upload(m.get(), &m->final_norm, w->final_norm, H));
-  float *tmp = nullptr;
+  void *stage = nullptr;
   int32_t *dperm = nullptr;
-  const size_t tmp_elems = (size_t)std::max(3 * H, 2 * I) * std::max(H, I);
-  IG_CU(cudaMalloc(&tmp, tmp_elems * sizeof(float)));
+  const size_t stage_elems = (size_t)std::max(3 * H, 2 * I) * std::max(H, I);
+  IG_CU(cudaMalloc(&stage, stage_elems * 2));
   IG_CU(cudaMalloc(&dperm, sizeof(int32_t) * m->NI));
+  struct Free {
+    void *a, *b;
+    ~Free() {
+      cudaFree(a);
+      cudaFree(b);
+    }
+  } free_tmp{stage, dperm};
+  IG_TRY(upload_view(m.get(), &m->emb_norm, w.emb_norm, H, stage));
+  IG_TRY(upload_view(m.get(), &m->final_norm, w.final_norm, H, stage));
   // Wi rows interleaved per 128: [input 128t.., gate 128t..] so one 256-wide
   // tile holds matching GELU inputs and gates.
   std::vector<int32_t> wi_perm(m->NI);
@@ -1199,27 +1298,71 @@ int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, i
     wi_perm[p] = ch < I ? (r < 128 ? ch : I + ch) : -1;
   }
   m->layers.resize(c.layers);
-  int rc = 0;
-  for (int l = 0; l < c.layers && !rc; l++) {
+  for (int l = 0; l < c.layers; l++) {
     DevLayer &L = m->layers[l];
-    if (l > 0) rc = upload(m.get(), &L.attn_norm, w->attn_norm[l], H);
-    if (!rc) rc = upload(m.get(), &L.mlp_norm, w->mlp_norm[l], H);
-    if (!rc) rc = pack_matrix(m.get(), L.qkv, w->wqkv[l], 3 * H, H, {}, tmp, dperm);
-    if (!rc) rc = pack_matrix(m.get(), L.o, w->wo[l], H, H, {}, tmp, dperm);
-    if (!rc) rc = pack_matrix(m.get(), L.wi, w->wi[l], 2 * I, H, wi_perm, tmp, dperm);
-    if (!rc) rc = pack_matrix(m.get(), L.wom, w->wo_mlp[l], H, I, {}, tmp, dperm);
-    // float32 copies for SetInt8(false)
-    if (!rc) rc = upload(m.get(), &L.fqkv, w->wqkv[l], (size_t)3 * H * H);
-    if (!rc) rc = upload(m.get(), &L.fo, w->wo[l], (size_t)H * H);
-    if (!rc) rc = upload(m.get(), &L.fwi, w->wi[l], (size_t)2 * I * H);
-    if (!rc) rc = upload(m.get(), &L.fwom, w->wo_mlp[l], (size_t)H * I);
+    if (l > 0) IG_TRY(upload_view(m.get(), &L.attn_norm, w.attn_norm[l], H, stage));
+    IG_TRY(upload_view(m.get(), &L.mlp_norm, w.mlp_norm[l], H, stage));
+    // The float32 matrices (kept for SetInt8(false)) are quantized from the
+    // device copy (PackB8 of the decoded weights, as the reference packs them).
+    IG_TRY(upload_view(m.get(), &L.fqkv, w.wqkv[l], (size_t)3 * H * H, stage));
+    IG_TRY(upload_view(m.get(), &L.fo, w.wo[l], (size_t)H * H, stage));
+    IG_TRY(upload_view(m.get(), &L.fwi, w.wi[l], (size_t)2 * I * H, stage));
+    IG_TRY(upload_view(m.get(), &L.fwom, w.wo_mlp[l], (size_t)H * I, stage));
+    IG_TRY(pack_matrix(m.get(), L.qkv, L.fqkv, 3 * H, H, {}, dperm));
+    IG_TRY(pack_matrix(m.get(), L.o, L.fo, H, H, {}, dperm));
+    IG_TRY(pack_matrix(m.get(), L.wi, L.fwi, 2 * I, H, wi_perm, dperm));
+    IG_TRY(pack_matrix(m.get(), L.wom, L.fwom, H, I, {}, dperm));
   }
-  cudaFree(tmp);
-  cudaFree(dperm);
-  if (rc) return rc;
   IG_TRY(ensure_rope(m.get(), 512));
   *out = m.release();
   return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ig_model_create(const ig_config *cfg, const ig_weights *w, int32_t device, ig_model **out) {
+  t_last_error.clear();
+  if (!cfg || !w || !out) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (cfg->layers <= 0 || cfg->layers > 4096) return fail(IG_ERR_BAD_ARG, "modernbert: invalid dimensions");
+  if (!w->attn_norm || !w->wqkv || !w->wo || !w->mlp_norm || !w->wi || !w->wo_mlp)
+    return fail(IG_ERR_BAD_ARG, "null argument");
+  WeightSource src;
+  src.tok_embeddings = w->tok_embeddings;
+  src.emb_norm = {IG_DT_F32, w->emb_norm};
+  src.final_norm = {IG_DT_F32, w->final_norm};
+  for (int l = 0; l < cfg->layers; l++) {
+    src.attn_norm.push_back({IG_DT_F32, l > 0 ? w->attn_norm[l] : nullptr});
+    src.wqkv.push_back({IG_DT_F32, w->wqkv[l]});
+    src.wo.push_back({IG_DT_F32, w->wo[l]});
+    src.mlp_norm.push_back({IG_DT_F32, w->mlp_norm[l]});
+    src.wi.push_back({IG_DT_F32, w->wi[l]});
+    src.wo_mlp.push_back({IG_DT_F32, w->wo_mlp[l]});
+  }
+  return create_model(cfg, src, device, out);
+}
+
+int ig_model_create_stored(const ig_config *cfg, const ig_stored_weights *w, int32_t device, ig_model **out) {
+  t_last_error.clear();
+  if (!cfg || !w || !out) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (cfg->layers <= 0 || cfg->layers > 4096) return fail(IG_ERR_BAD_ARG, "modernbert: invalid dimensions");
+  if (!w->attn_norm || !w->wqkv || !w->wo || !w->mlp_norm || !w->wi || !w->wo_mlp)
+    return fail(IG_ERR_BAD_ARG, "null argument");
+  WeightSource src;
+  src.tok_embeddings = nullptr;  // ig_model_set_embeddings uploads the table as stored
+  auto tv = [](const ig_tensor tensor) { return TensorView{tensor.dtype, tensor.data}; };
+  src.emb_norm = tv(w->emb_norm);
+  src.final_norm = tv(w->final_norm);
+  for (int l = 0; l < cfg->layers; l++) {
+    src.attn_norm.push_back(l > 0 ? tv(w->attn_norm[l]) : TensorView{IG_DT_F32, nullptr});
+    src.wqkv.push_back(tv(w->wqkv[l]));
+    src.wo.push_back(tv(w->wo[l]));
+    src.mlp_norm.push_back(tv(w->mlp_norm[l]));
+    src.wi.push_back(tv(w->wi[l]));
+    src.wo_mlp.push_back(tv(w->wo_mlp[l]));
+  }
+  return create_model(cfg, src, device, out);
 }
 
 void ig_model_destroy(ig_model *m) { delete m; }
@@ -1227,6 +1370,9 @@ void ig_model_destroy(ig_model *m) { delete m; }
 int ig_model_set_embeddings(ig_model *m, const ig_embedding_table *t) {
   t_last_error.clear();
   if (!m || !t) return fail(IG_ERR_BAD_ARG, "null argument");
+  for (ig_model *r : m->replicas)
+    if (int rc = ig_model_set_embeddings(r, t)) return rc;
+  if (!m->replicas.empty()) return 0;
   const int V = m->cfg.vocab, H = m->H;
   DeviceGuard dg(m->device);
   EmbTable e{t->format, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -1279,6 +1425,9 @@ int ig_model_set_embeddings(ig_model *m, const ig_embedding_table *t) {
 int ig_model_set_heads(ig_model *m, int32_t nheads, const ig_head *heads) {
   t_last_error.clear();
   if (!m || nheads < 0 || (nheads && !heads)) return fail(IG_ERR_BAD_ARG, "null argument");
+  for (ig_model *r : m->replicas)
+    if (int rc = ig_model_set_heads(r, nheads, heads)) return rc;
+  if (!m->replicas.empty()) return 0;
   DeviceGuard dg(m->device);
   std::vector<DevHead> hs(nheads);
   for (int i = 0; i < nheads; i++) {
@@ -1326,6 +1475,8 @@ int ig_model_set_int8(ig_model *m, int32_t on) {
   if (!m) return fail(IG_ERR_BAD_ARG, "null model");
   if (on == 0 && m->D != 64) return fail(IG_ERR_UNSUPPORTED, "the float path needs a head dimension of 64");
   if (on == 0 && m->cfg.simd_lanes != 8) return fail(IG_ERR_UNSUPPORTED, "the float path needs simd_lanes 8");
+  for (ig_model *r : m->replicas)
+    if (int rc = ig_model_set_int8(r, on)) return rc;
   std::lock_guard<std::mutex> lk(m->mu);
   m->f32 = on == 0;
   return 0;
@@ -1341,6 +1492,7 @@ int ig_model_dims(ig_model *m, int32_t *vocab, int32_t *hidden) {
 int ig_model_head_rows(ig_model *m, int32_t *pooled_rows, int32_t *token_rows) {
   t_last_error.clear();
   if (!m || !pooled_rows || !token_rows) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (!m->replicas.empty()) return ig_model_head_rows(m->replicas[0], pooled_rows, token_rows);
   int32_t pl = 0, tl = 0;
   std::lock_guard<std::mutex> lk(m->mu);
   for (auto &h : m->heads) (h.per_token ? tl : pl) += h.rows;
@@ -1360,6 +1512,8 @@ int ig_encode_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int
   t_last_error.clear();
   if (!m || !offs || !d_out) return fail(IG_ERR_BAD_ARG, "null argument");
   if (mode != IG_MODE_POOLED && mode != IG_MODE_TOKENS) return fail(IG_ERR_BAD_ARG, "bad mode");
+  if (!m->replicas.empty())
+    return fail(IG_ERR_BAD_ARG, "a model on several devices takes device buffers through ig_model_replica");
   DeviceGuard dg(m->device);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -1391,6 +1545,8 @@ int ig_logits_device(ig_model *m, const int32_t *d_ids, const int64_t *offs, int
                      double *d_token_logits, void *stream) {
   t_last_error.clear();
   if (!m || !offs || (!d_logits && !d_token_logits)) return fail(IG_ERR_BAD_ARG, "null argument");
+  if (!m->replicas.empty())
+    return fail(IG_ERR_BAD_ARG, "a model on several devices takes device buffers through ig_model_replica");
   DeviceGuard dg(m->device);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;

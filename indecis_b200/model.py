@@ -177,7 +177,9 @@ class MappedEmbeddings:
 
 
 class Model:
-    """modernbert.Model restricted to int8 inference on one GPU."""
+    """modernbert.Model restricted to inference on the device. `device` is one
+    GPU ordinal, or a list of them: the model is then replicated on each and
+    every call's sequences are split across them by cost (no collective)."""
 
     def __init__(self, cfg: Config, handle, device: int):
         self.Cfg = cfg
@@ -250,8 +252,71 @@ class Model:
                             final_norm=keep[2].ctypes.data, **fields)
         c = cfg.to_c()
         h = C.c_void_p()
-        _capi.check(lib.ig_model_create(C.byref(c), C.byref(w), device, C.byref(h)))
+        if isinstance(device, (list, tuple)):
+            devs = (C.c_int32 * len(device))(*device)
+            _capi.check(lib.ig_model_create_multi(C.byref(c), C.byref(w), devs, len(device), C.byref(h)))
+        else:
+            _capi.check(lib.ig_model_create(C.byref(c), C.byref(w), device, C.byref(h)))
         return cls(cfg, h, device)
+
+    @classmethod
+    def FromStored(cls, cfg: Config, stored: dict, table: "MappedEmbeddings", device=0) -> "Model":
+        """Load's path (model.go:661-735) without decoding on the host: every
+        layer tensor goes to the device in its stored dtype and is decoded there
+        as safetensors decodes it; the embedding table is uploaded as stored.
+        stored maps transformers names to (dtype, raw array): "F32" float32,
+        "BF16" / "F16" uint16 bits, "I8" int8."""
+        cfg.validate()
+        H, I, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers
+        lib = _capi.load()
+        keep = []
+
+        def view(name, *shape):
+            t = stored.get(name, stored.get("model." + name))
+            if t is None:
+                raise ModernBertError(f"modernbert: tensor {name} missing")
+            dt, raw = t
+            want = {"F32": np.float32, "BF16": np.uint16, "F16": np.uint16, "I8": np.int8}.get(dt)
+            raw = np.ascontiguousarray(raw, want)
+            if list(raw.shape) != list(shape):
+                raise ModernBertError(f"modernbert: {name}: shape {list(raw.shape)}, expected {list(shape)}")
+            keep.append(raw)
+            return _capi.IgTensor(dtype=_capi.IG_DT[dt] if isinstance(dt, str) else int(dt), data=raw.ctypes.data)
+
+        per = {k: (_capi.IgTensor * L)() for k in ("attn_norm", "wqkv", "wo", "mlp_norm", "wi", "wo_mlp")}
+        for l in range(L):
+            p = f"layers.{l}."
+            if l > 0:
+                per["attn_norm"][l] = view(p + "attn_norm.weight", H)
+            per["wqkv"][l] = view(p + "attn.Wqkv.weight", 3 * H, H)
+            per["wo"][l] = view(p + "attn.Wo.weight", H, H)
+            per["mlp_norm"][l] = view(p + "mlp_norm.weight", H)
+            per["wi"][l] = view(p + "mlp.Wi.weight", 2 * I, H)
+            per["wo_mlp"][l] = view(p + "mlp.Wo.weight", H, I)
+        w = _capi.IgStoredWeights(emb_norm=view("embeddings.norm.weight", H), final_norm=view("final_norm.weight", H),
+                                  **{k: C.cast(v, C.POINTER(_capi.IgTensor)) for k, v in per.items()})
+        c = cfg.to_c()
+        h = C.c_void_p()
+        if isinstance(device, (list, tuple)):
+            devs = (C.c_int32 * len(device))(*device)
+            _capi.check(lib.ig_model_create_stored_multi(C.byref(c), C.byref(w), devs, len(device), C.byref(h)))
+        else:
+            _capi.check(lib.ig_model_create_stored(C.byref(c), C.byref(w), device, C.byref(h)))
+        m = cls(cfg, h, device)
+        m.SetEmbeddingTable(table)
+        return m
+
+    def replica(self, i: int):
+        """(handle, device) of replica i: the handle that the device-buffer
+        entry points take for that GPU (borrowed; it lives with the model)."""
+        h, d = C.c_void_p(), C.c_int32()
+        _capi.check(_capi.load().ig_model_replica(self._h, i, C.byref(h), C.byref(d)))
+        return h, d.value
+
+    def device_count(self) -> int:
+        n = C.c_int32()
+        _capi.check(_capi.load().ig_model_device_count(self._h, C.byref(n)))
+        return n.value
 
     def close(self):
         if getattr(self, "_h", None):

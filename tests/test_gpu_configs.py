@@ -1,5 +1,14 @@
-"""The encoder at the other BASELINE shapes, bit-exact against the oracle at
-sizes the oracle finishes in seconds:
+"""The encoder at the other BASELINE shapes, bit-exact against the oracle.
+
+At full size (the oracle's threaded VNNI path takes seconds to a minute):
+
+  C3 long: 8 sequences of 4096 tokens through the whole C1 model (global
+     layers 0 and 3 over all 4096 keys, local layers with the half-window 64);
+  C3 varlen: the 256 unpadded sequences of U[8, 512] tokens (seed 3);
+  C4: the base model itself (22 layers, vocab 262144, hidden 768, 12 heads,
+     intermediate 1152) on four 512-token sequences, pooled and token states.
+
+At reduced sizes:
 
   C3 (C1's model): two 1024-token sequences (global layers over 1024 keys:
      the attention path for long key ranges) and a ragged batch with lengths
@@ -61,3 +70,39 @@ def test_c4_layer_shape(igdev, oracle_lib):
     for k in ("qkv", "ctx", "x_attn", "x_mlp"):
         assert np.array_equal(_bits(dg[k]), _bits(do[k])), k
     assert np.array_equal(_bits(rg), _bits(ro))
+
+
+def _host_threads():
+    import os
+    return max(1, os.cpu_count() or 1)
+
+
+def test_c3_full_long(igdev, oracle_lib):
+    from indecis_b200 import synthetic as S
+    om, gm = _models(S.C1)
+    ids, offs = S.ids_fixed(8, 4096, S.C1["vocab"], seed=31)
+    t = _host_threads()
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(om.encode(ids, offs, threads=t, fast=True)))
+    assert np.array_equal(_bits(gm.EncodeTokens((ids, offs))),
+                          _bits(om.encode(ids, offs, mode=1, threads=t, fast=True)))
+
+
+def test_c3_full_varlen(igdev, oracle_lib):
+    from indecis_b200 import synthetic as S
+    om, gm = _models(S.C1)
+    ids, offs = S.ids_varlen(256, 8, 512, S.C1["vocab"], seed=3)
+    t = _host_threads()
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(om.encode(ids, offs, threads=t, fast=True)))
+    assert np.array_equal(_bits(gm.EncodeTokens((ids, offs))),
+                          _bits(om.encode(ids, offs, mode=1, threads=t, fast=True)))
+
+
+def test_c4_full_model(igdev, oracle_lib):
+    from indecis_b200 import synthetic as S
+    om, gm = _models(S.C4, seed=42, gamma_noise=0.0)
+    ids, offs = S.ids_fixed(4, 512, S.C4["vocab"], seed=41)
+    t = _host_threads()
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(om.encode(ids, offs, threads=t, fast=True)))
+    assert np.array_equal(_bits(gm.EncodeTokens((ids, offs))),
+                          _bits(om.encode(ids, offs, mode=1, threads=t, fast=True)))
+    gm.close()
