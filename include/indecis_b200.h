@@ -5,9 +5,10 @@
  * github.com/bornholm/indecis (paths relative to that module). The seam is
  * internal/modernbert/infer.go:304 `func (m *Model) run(seqs [][]int32,
  * done func(xn []float32, offs []int)) error`, the single place where the
- * int8 forward runs; a build-tagged cgo file gives it a device branch (see
- * INTEGRATION.md). Plain pointers and sizes only; no allocation is handed to
- * the caller. All entry points are reentrant: a model is read-only after
+ * int8 forward runs; a cgo file under the build tag indecisgpu
+ * (go/internal/modernbert/infer_gpu.go in this repository) gives it a device
+ * branch that calls ig_encode. Plain pointers and sizes only; no allocation is
+ * handed to the caller. All entry points are reentrant: a model is read-only after
  * creation and every call takes its own workspace and stream.
  *
  * Status codes: 0 on success, otherwise an IG_ERR_* value; ig_last_error()
@@ -162,6 +163,8 @@ IG_API int ig_model_create_stored_multi(const ig_config *cfg, const ig_stored_we
 IG_API int ig_model_replica(ig_model *m, int32_t index, ig_model **replica, int32_t *device);
 /* Number of devices a model runs on. */
 IG_API int ig_model_device_count(ig_model *m, int32_t *n);
+/* Number of sm_100 devices this process can use (0 without a driver or GPU). */
+IG_API int ig_device_count(int32_t *n);
 
 /* Releases the model's device memory. Replaces Invalidate (infer.go:95-100)
  * for the device copy: a changed model is destroyed and created again. */

@@ -32,7 +32,7 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats",
            "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags", "ig_model_set_int8",
            "ig_check_gelu_division", "ig_model_create_multi", "ig_model_replica", "ig_model_device_count",
-           "ig_model_create_stored", "ig_model_create_stored_multi"]
+           "ig_model_create_stored", "ig_model_create_stored_multi", "ig_device_count"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -139,6 +139,7 @@ def load() -> C.CDLL:
                                                C.POINTER(C.c_void_p)]
     L.ig_model_replica.argtypes = [vp, i32, C.POINTER(C.c_void_p), i32p]
     L.ig_model_device_count.argtypes = [vp, i32p]
+    L.ig_device_count.argtypes = [i32p]
     L.ig_model_destroy.argtypes = [vp]
     L.ig_model_destroy.restype = None
     L.ig_model_set_heads.argtypes = [vp, i32, C.POINTER(IgHead)]

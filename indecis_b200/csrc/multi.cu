@@ -173,6 +173,22 @@ int ig_model_replica(ig_model *m, int32_t index, ig_model **replica, int32_t *de
   return 0;
 }
 
+int ig_device_count(int32_t *n) {
+  t_last_error.clear();
+  if (!n) return fail(IG_ERR_BAD_ARG, "null argument");
+  *n = 0;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  for (int d = 0; d < count; d++) {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, d) == cudaSuccess && p.major == 10) ++*n;
+  }
+  return 0;
+}
+
 int ig_model_device_count(ig_model *m, int32_t *n) {
   t_last_error.clear();
   if (!m || !n) return fail(IG_ERR_BAD_ARG, "null argument");

@@ -22,6 +22,11 @@ class ModernBertError(ValueError):
     """An error the reference returns as a Go `error` (same wording)."""
 
 
+def _go_quote(s: str) -> str:
+    """Go's %q of a printable string: double quotes, backslash escapes."""
+    return '"' + s.replace("\\", "\\\\").replace('"', '\\"') + '"'
+
+
 @dataclass
 class Config:
     """modernbert.Config (internal/modernbert/model.go:25-49)."""
@@ -78,11 +83,11 @@ class Config:
         if self.global_attn_every_n_layers <= 0 or self.local_attention <= 0:
             raise ModernBertError("modernbert: invalid attention windows")
         if self.hidden_activation != "gelu":
-            raise ModernBertError(f"modernbert: activation {self.hidden_activation!r} not supported")
+            raise ModernBertError(f"modernbert: activation {_go_quote(self.hidden_activation)} not supported")
         if self.attention_bias or self.mlp_bias or self.norm_bias:
             raise ModernBertError("modernbert: biases are not supported")
         if self.classifier_pooling not in ("", "mean", "cls"):
-            raise ModernBertError(f"modernbert: pooling {self.classifier_pooling!r} not supported")
+            raise ModernBertError(f"modernbert: pooling {_go_quote(self.classifier_pooling)} not supported")
 
     def to_c(self) -> _capi.IgConfig:
         return _capi.IgConfig(vocab=self.vocab_size, hidden=self.hidden_size, layers=self.num_hidden_layers,
