@@ -282,6 +282,25 @@ def cpu_sample(model, spec, ids, offs, units: int, threads: int, f32: bool = Fal
     return time.perf_counter() - t0, done
 
 
+def encoder_gop(cfg, lens) -> float:
+    """Algorithmic int8 operations (2 per multiply-add) of the encoder over
+    sequences of the given lengths: the four projections per token and layer,
+    and S = QK^T plus O = PV over each query's keys (the local window on
+    local layers)."""
+    H, I, L, nh = cfg["hidden"], cfg["intermediate"], cfg["layers"], cfg["heads"]
+    D, w = H // nh, cfg["local_attention"] // 2
+    proj = H * 3 * H + H * H + H * 2 * I + I * H
+    macs = 0
+    for n in lens:
+        n = int(n)
+        i = np.arange(n)
+        local = int((np.minimum(n, i + w + 1) - np.maximum(0, i - w)).sum())
+        for l in range(L):
+            keys = n * n if l % cfg["global_every"] == 0 else local
+            macs += proj * n + 2 * D * nh * keys
+    return 2.0 * macs / 1e9
+
+
 def cpu_isa(oracle):
     feats = oracle.lib().or_cpu_features()
     return "AVX-VNNI" if feats & 1 else ("AVX512-VNNI" if feats & 2 else "scalar int")
@@ -295,11 +314,23 @@ def cpu_baseline(spec, target_s: float, f32: bool = False):
     ids, offs = spec["make"](max(spec["per_gpu"], 200 * CPU_UNIT[spec["name"]]))
     t1, _ = cpu_sample(model, spec, ids, offs, 1, threads, f32)  # warm-up, and the size of one call
     units = int(max(1, min(200, target_s / max(t1, 1e-3))))
+    oracle.phase_seconds(reset=True)
     t, n = cpu_sample(model, spec, ids, offs, units, threads, f32)
-    path = "float32 path (scalar FMA chains)" if f32 else f"int8 path, {cpu_isa(oracle)} 6x16 tiles"
-    return {"value": n / t, "unit": "seq/s", "cores": threads, "kind": "port",
-            "sample": f"{n} sequences of the workload in calls of {CPU_UNIT[spec['name']]}, oracle C++ port of the "
-                      f"reference {path}, {threads} threads, {t:.1f} s"}
+    ph = oracle.phase_seconds(reset=True)
+    path = ("float32 path (scalar FMA chains)" if f32 else
+            f"int8 path: {cpu_isa(oracle)} 6x16 tiles for the projections and for attention's S = QK^T and "
+            f"O = PV, AVX2 (8 float32 lanes) LayerNorm, row quantization, RoPE, ExpShift and GeluMul")
+    out = {"value": n / t, "unit": "seq/s", "cores": threads, "kind": "port",
+           "sample": f"{n} sequences of the workload in calls of {CPU_UNIT[spec['name']]}, oracle C++ port of the "
+                     f"reference {path}, {threads} threads, {t:.1f} s"}
+    if not f32:
+        gop = encoder_gop(spec["cfg"], np.diff(offs[:n + 1]))
+        tot = sum(ph) or 1.0
+        out["gop_per_s"] = gop / t
+        out["gop_per_s_per_thread"] = gop / t / threads
+        out["phase_share"] = {"norms_qkv_rope": ph[0] / tot, "attention": ph[1] / tot,
+                              "out_proj_norm_mlp": ph[2] / tot}
+    return out
 
 
 def run_reference(args, world, rank):
@@ -329,7 +360,9 @@ def run_reference(args, world, rank):
             "cpu_baseline": {"value": v, "unit": "seq/s", "cores": threads, "kind": "port",
                              "sample": f"each step one CPU call of {u} sequence(s) of the workload (bounded sample), "
                                        f"oracle C++ port of the reference {path} (Go reference not runnable: no Go "
-                                       f"toolchain), {threads} threads"},
+                                       f"toolchain), {threads} threads"
+                                       + ("" if f32 else ": VNNI 6x16 tiles for the projections and attention, AVX2 "
+                                                         "8-lane LayerNorm, quantization, RoPE, ExpShift, GeluMul")},
             "e2e": {"value": v, "unit": "seq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
 

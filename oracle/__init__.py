@@ -102,6 +102,7 @@ def lib():
     L.or_encode_f32.restype = C.c_int
     L.or_encode_f32.argtypes = [C.c_void_p, i32p, i64p, C.c_int, C.c_int, f32p, C.c_int, C.POINTER(C.c_int32)]
     L.or_cpu_features.restype = C.c_int
+    L.or_phase_seconds.argtypes = [f64p, C.c_int]
     L.or_siglip_create.restype = C.c_void_p
     L.or_siglip_create.argtypes = [C.c_void_p, C.c_void_p]
     L.or_siglip_destroy.argtypes = [C.c_void_p]
@@ -118,6 +119,14 @@ def lib():
 
 
 # ---- thin numpy wrappers ----------------------------------------------------
+
+
+def phase_seconds(reset: bool = True):
+    """Wall seconds of the encoder's phases since the last reset:
+    (norms + QKV + RoPE, attention, output projection + norm + MLP)."""
+    out = np.zeros(3, np.float64)
+    lib().or_phase_seconds(out, 1 if reset else 0)
+    return tuple(float(v) for v in out)
 
 def round_half_even(v: float) -> float:
     return lib().or_round_half_even(v)

@@ -37,11 +37,11 @@ void pack_panels(const int8_t *q, int N, int K, std::vector<int8_t> &out) {
       const uint8_t *a = A + (size_t)i0 * K;                                                          \
       const int8_t *bp = Bp + (size_t)p * kq * 64;                                                    \
       __m256i c[6][2];                                                                                \
-      for (int r = 0; r < 6; r++) c[r][0] = c[r][1] = _mm256_setzero_si256();                         \
+      _Pragma("GCC unroll 6") for (int r = 0; r < 6; r++) c[r][0] = c[r][1] = _mm256_setzero_si256();  \
       for (int q = 0; q < kq; q++) {                                                                  \
         __m256i b0 = _mm256_loadu_si256((const __m256i *)(bp + q * 64));                              \
         __m256i b1 = _mm256_loadu_si256((const __m256i *)(bp + q * 64 + 32));                         \
-        for (int r = 0; r < 6; r++) {                                                                 \
+        _Pragma("GCC unroll 6") for (int r = 0; r < 6; r++) {                                         \
           int32_t w;                                                                                  \
           std::memcpy(&w, a + (size_t)r * K + q * 4, 4);                                              \
           __m256i av = _mm256_set1_epi32(w);                                                          \
@@ -50,7 +50,7 @@ void pack_panels(const int8_t *q, int N, int K, std::vector<int8_t> &out) {
         }                                                                                             \
       }                                                                                               \
       alignas(32) int32_t t[6][16];                                                                   \
-      for (int r = 0; r < 6; r++) {                                                                   \
+      _Pragma("GCC unroll 6") for (int r = 0; r < 6; r++) {                                           \
         _mm256_store_si256((__m256i *)&t[r][0], c[r][0]);                                             \
         _mm256_store_si256((__m256i *)&t[r][8], c[r][1]);                                             \
       }                                                                                               \

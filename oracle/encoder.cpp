@@ -6,8 +6,11 @@
 // the integer products on AVX-VNNI (cpu_baseline.cpp).
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
+#include <mutex>
 #include <cstring>
+#include <memory>
 #include <thread>
 #include <vector>
 
@@ -15,6 +18,24 @@
 #include "oracle_internal.h"
 
 using namespace orc;
+
+namespace {
+// Wall time of the encoder's phases summed over calls (the CPU baseline's
+// per-phase split): 0 norms + QKV + RoPE, 1 attention, 2 output projection,
+// norm and MLP.
+std::mutex g_phase_mu;
+double g_phase_s[3] = {0, 0, 0};
+struct PhaseClock {
+  int phase;
+  std::chrono::steady_clock::time_point t0 = std::chrono::steady_clock::now();
+  explicit PhaseClock(int p) : phase(p) {}
+  ~PhaseClock() {
+    const double s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    std::lock_guard<std::mutex> lk(g_phase_mu);
+    g_phase_s[phase] += s;
+  }
+};
+}  // namespace
 
 struct or_model {
   or_config cfg;
@@ -88,6 +109,15 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
   if (mode == 0) std::memset(out, 0, sizeof(float) * (size_t)nseq * H);
   if (N == 0) return 0;
   const bool use_fast = fast != 0 || threads > 1;
+  // The CPU baseline's vector forms (AVX2, V = 8, VNNI attention tiles): the
+  // same bits as the scalar loops.
+  const bool simd = use_fast && VL == 8 && simd8_ok();
+  auto norm = [&](float *o, const float *xr, const float *gamma) {
+    if (simd)
+      layernorm_row8(o, xr, gamma, H, cfg.norm_eps);
+    else
+      layernorm_row(o, xr, gamma, H, cfg.norm_eps, VL);
+  };
   const int workers = std::max(1, threads);
   std::vector<float> x((size_t)N * H), xn((size_t)N * H), qkv((size_t)N * 3 * H), ctx((size_t)N * H);
   std::vector<int32_t> pos(N);
@@ -97,7 +127,7 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
     for (int64_t t = offs[i]; t < offs[i + 1]; t++) pos[t] = (int32_t)(t - offs[i]);
   }
   for (int64_t r = 0; r < N; r++) std::memcpy(&xn[r * H], &m->emb[(size_t)ids[r] * H], sizeof(float) * H);
-  for (int64_t r = 0; r < N; r++) layernorm_row(&x[r * H], &xn[r * H], m->emb_norm.data(), H, cfg.norm_eps, VL);
+  for (int64_t r = 0; r < N; r++) norm(&x[r * H], &xn[r * H], m->emb_norm.data());
   if (dump && dump->emb_ln) std::memcpy(dump->emb_ln, x.data(), sizeof(float) * N * H);
 
   // infer.go:570-572 sliceRows.
@@ -115,12 +145,12 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
     }
     const bool dl = dump && dump->layer == l;
     // Norm, QKV projection, RoPE (infer.go:382-400).
+    std::unique_ptr<PhaseClock> clock(new PhaseClock(0));
     parallel_n(workers, (int)N, slice, [&](int lo, int hi) {
       GemmScratch s;
       const float *in = &x[(size_t)lo * H];
       if (l > 0) {
-        for (int r = lo; r < hi; r++)
-          layernorm_row(&xn[(size_t)r * H], &x[(size_t)r * H], m->attn_norm[l].data(), H, cfg.norm_eps, VL);
+        for (int r = lo; r < hi; r++) norm(&xn[(size_t)r * H], &x[(size_t)r * H], m->attn_norm[l].data());
         in = &xn[(size_t)lo * H];
       }
       matmul_rows(m->qkv[l], in, &qkv[(size_t)lo * 3 * H], hi - lo, false, use_fast, s,
@@ -131,7 +161,8 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
       for (int r = lo; r < hi; r++) {
         const int t = pos[r];
         float *row = &qkv[(size_t)r * 3 * H];
-        for (int h = 0; h < 2 * nh; h++) rope(row + h * D, &rc[(size_t)t * half], &rs[(size_t)t * half], half);
+        for (int h = 0; h < 2 * nh; h++)
+          (simd ? rope8 : rope)(row + h * D, &rc[(size_t)t * half], &rs[(size_t)t * half], half);
       }
     });
 
@@ -139,8 +170,41 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
     // block of queries.
     const int window = global ? -1 : cfg.local_attention / 2;
     const float scale = (float)(1.0 / std::sqrt((double)D));
-    std::vector<AttnPrep> prep((size_t)nseq * nh);
-    parallel_n(workers, nseq * nh, 1, [&](int lo, int hi) {
+    clock.reset(new PhaseClock(1));
+    if (simd) {
+      // The CPU baseline: prepare per (sequence, head), then the blocks of
+      // queries, S and O on VNNI tiles (linalg/attention8.go:298-376).
+      std::vector<AttnPrep8> prep8((size_t)nseq * nh);
+      parallel_n(workers, nseq * nh, 1, [&](int lo, int hi) {
+        for (int task = lo; task < hi; task++) {
+          const int bi = task / nh, h = task % nh;
+          const int64_t off = offs[bi];
+          const int n = (int)(offs[bi + 1] - off);
+          if (n == 0) continue;
+          const float *rows = &qkv[(size_t)off * 3 * H];
+          attn_prepare8(rows + h * D, rows + H + h * D, rows + 2 * H + h * D, 3 * H, n, D, scale, prep8[task]);
+        }
+      });
+      struct Blk8 {
+        int task, i0;
+      };
+      std::vector<Blk8> blocks8;
+      for (int bi = 0; bi < nseq; bi++)
+        for (int h = 0; h < nh; h++)
+          for (int i0 = 0; i0 < offs[bi + 1] - offs[bi]; i0 += kAttnBlock8) blocks8.push_back({bi * nh + h, i0});
+      parallel_n(workers, (int)blocks8.size(), 1, [&](int lo, int hi) {
+        AttnScratch8 sc;
+        for (int b = lo; b < hi; b++) {
+          const int bi = blocks8[b].task / nh, h = blocks8[b].task % nh;
+          const int64_t off = offs[bi];
+          const int n = (int)(offs[bi + 1] - off);
+          attend8(prep8[blocks8[b].task], blocks8[b].i0, std::min(n, blocks8[b].i0 + kAttnBlock8), window,
+                  &ctx[(size_t)(off + blocks8[b].i0) * H + h * D], H, sc);
+        }
+      });
+    }
+    std::vector<AttnPrep> prep(simd ? 0 : (size_t)nseq * nh);
+    if (!simd) parallel_n(workers, nseq * nh, 1, [&](int lo, int hi) {
       for (int task = lo; task < hi; task++) {
         const int bi = task / nh, h = task % nh;
         const int64_t off = offs[bi];
@@ -155,7 +219,7 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
     };
     std::vector<Blk> blocks;
     const int AttnBlock = 48;
-    for (int bi = 0; bi < nseq; bi++)
+    for (int bi = 0; bi < nseq && !simd; bi++)
       for (int h = 0; h < nh; h++)
         for (int i0 = 0; i0 < offs[bi + 1] - offs[bi]; i0 += AttnBlock) blocks.push_back({bi * nh + h, i0});
     parallel_n(workers, (int)blocks.size(), 1, [&](int lo, int hi) {
@@ -174,6 +238,7 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
     if (dl && dump->ctx) std::memcpy(dump->ctx, ctx.data(), sizeof(float) * N * H);
 
     // Output projection, norm, MLP (infer.go:402-425).
+    clock.reset(new PhaseClock(2));
     std::vector<float> xa;
     if (dl && dump->x_attn) xa.resize((size_t)N * H);
     parallel_n(workers, (int)N, slice, [&](int lo, int hi) {
@@ -183,14 +248,14 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
                   dl && dump->cq ? dump->cq + (size_t)lo * H : nullptr, dl && dump->cq_s ? dump->cq_s + lo : nullptr,
                   nullptr);
       if (!xa.empty()) std::memcpy(&xa[(size_t)lo * H], &x[(size_t)lo * H], sizeof(float) * rows * H);
-      for (int r = lo; r < hi; r++)
-        layernorm_row(&xn[(size_t)r * H], &x[(size_t)r * H], m->mlp_norm[l].data(), H, cfg.norm_eps, VL);
+      for (int r = lo; r < hi; r++) norm(&xn[(size_t)r * H], &x[(size_t)r * H], m->mlp_norm[l].data());
       std::vector<float> z((size_t)rows * 2 * I), g((size_t)rows * I);
       matmul_rows(m->wi[l], &xn[(size_t)lo * H], z.data(), rows, false, use_fast, s,
                   dl && dump->hq ? dump->hq + (size_t)lo * H : nullptr, dl && dump->hq_s ? dump->hq_s + lo : nullptr,
                   nullptr);
       if (dl && dump->z) std::memcpy(dump->z + (size_t)lo * 2 * I, z.data(), sizeof(float) * rows * 2 * I);
-      for (int r = 0; r < rows; r++) gelu_mul(&g[(size_t)r * I], &z[(size_t)r * 2 * I], &z[(size_t)r * 2 * I + I], I);
+      for (int r = 0; r < rows; r++)
+        (simd ? gelu_mul8 : gelu_mul)(&g[(size_t)r * I], &z[(size_t)r * 2 * I], &z[(size_t)r * 2 * I + I], I);
       matmul_rows(m->womlp[l], g.data(), &x[(size_t)lo * H], rows, true, use_fast, s,
                   dl && dump->gq ? dump->gq + (size_t)lo * I : nullptr, dl && dump->gq_s ? dump->gq_s + lo : nullptr,
                   nullptr);
@@ -199,7 +264,7 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
     if (dl && dump->x_mlp) std::memcpy(dump->x_mlp, x.data(), sizeof(float) * N * H);
   }
   // Final norm (infer.go:427) then pooling (infer.go:261-289).
-  for (int64_t r = 0; r < N; r++) layernorm_row(&xn[r * H], &x[r * H], m->final_norm.data(), H, cfg.norm_eps, VL);
+  for (int64_t r = 0; r < N; r++) norm(&xn[r * H], &x[r * H], m->final_norm.data());
   if (mode == 1) {
     std::memcpy(out, xn.data(), sizeof(float) * N * H);
     return 0;
@@ -221,6 +286,14 @@ int or_encode(const or_model *m, const int32_t *ids, const int64_t *offs, int ns
 }
 
 int or_cpu_features(void) { return cpu_features(); }
+
+void or_phase_seconds(double *out, int reset) {
+  std::lock_guard<std::mutex> lk(g_phase_mu);
+  for (int i = 0; i < 3; i++) {
+    out[i] = g_phase_s[i];
+    if (reset) g_phase_s[i] = 0;
+  }
+}
 
 }  // extern "C"
 

@@ -225,6 +225,9 @@ void or_matmul8_outliers(float *c, const float *a, int m, const int8_t *q, const
 
 /* CPU features used by the baseline (bit 0: AVX-VNNI, bit 1: AVX512-VNNI). */
 int or_cpu_features(void);
+/* Wall seconds of or_encode's phases summed since the last reset: [0] norms,
+   QKV and RoPE, [1] attention, [2] output projection, norm and MLP. */
+void or_phase_seconds(double *out, int reset);
 
 #ifdef __cplusplus
 }

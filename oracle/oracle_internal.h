@@ -97,5 +97,32 @@ struct GemmScratch {
 void matmul_rows(const PackedMat &W, const float *a, float *c, int rows, bool accumulate, bool fast,
                  GemmScratch &s, uint8_t *aq_dump, float *sa_dump, int32_t *acc_dump);
 
+// Vector forms of the CPU baseline (cpu_simd.cpp): AVX2 with V = 8 lanes and
+// VNNI attention tiles, bit-equal to the scalar functions above.
+bool simd8_ok();  // AVX2 + FMA + a VNNI form on this host
+void layernorm_row8(float *o, const float *x, const float *gamma, int n, double eps);
+float quant_row8(int8_t *dst, const float *x, const float *mean, int n, bool flip, int32_t *sum);
+void quantize_a_row8(const float *x, int k, uint8_t *q, float *sa);
+void dequant_row8(const int32_t *acc, int N, float sa, const float *sb, const float *zc, float *c, bool accumulate);
+float exp_shift8(float *x, int n, float m);
+void gelu_mul8(float *o, const float *a, const float *b, int n);
+void rope8(float *x, const float *c, const float *s, int half);
+
+constexpr int kAttnBlock8 = 48;  // queries scored at a time (linalg/attention8.go:26, 8 x 6)
+struct AttnPrep8 {
+  AttnPrep base;
+  int n16 = 0;                // keys padded to whole 16-key panels
+  std::vector<uint8_t> qpad;  // qa plus 6 padding rows
+  std::vector<int8_t> kp, vp;  // K [n16/16][D/4][16][4]; V [D/16][n16/4][16][4]
+  std::vector<float> ks16, kzc16, sq6;  // key scales and sums padded to n16, query scales to n + 6
+};
+struct AttnScratch8 {
+  std::vector<float> s;
+  std::vector<uint8_t> p;
+  std::vector<float> sp;
+};
+void attn_prepare8(const float *q, const float *k, const float *v, int ld, int n, int D, float scale, AttnPrep8 &P);
+void attend8(const AttnPrep8 &P, int i0, int i1, int window, float *o, int ldo, AttnScratch8 &sc);
+
 
 }  // namespace orc

@@ -26,12 +26,21 @@ void matmul_rows(const PackedMat &W, const float *a, float *c, int rows, bool ac
   s.aq.assign((size_t)rp * kp, 128);
   s.sa.assign(rp, 0.0f);
   s.acc.resize((size_t)rows * n);
-  for (int i = 0; i < rows; i++) quantize_a_row(a + (size_t)i * k, k, s.aq.data() + (size_t)i * kp, &s.sa[i]);
+  // The fast path (the CPU baseline) also quantizes and dequantizes in AVX2:
+  // the same bits.
+  const bool simd = fast && simd8_ok();
+  for (int i = 0; i < rows; i++)
+    (simd ? quantize_a_row8 : quantize_a_row)(a + (size_t)i * k, k, s.aq.data() + (size_t)i * kp, &s.sa[i]);
   if (fast)
     gemm_u8s8_fast(s.aq.data(), W.panels.data(), rp, n, kp, 0, rows, s.acc.data());
   else
     gemm_u8s8(s.aq.data(), kp, W.q.data(), k, rows, n, k, s.acc.data());
-  dequant(s.acc.data(), rows, n, s.sa.data(), W.scale.data(), W.zc.data(), c, accumulate);
+  if (simd)
+    for (int i = 0; i < rows; i++)
+      dequant_row8(s.acc.data() + (size_t)i * n, n, s.sa[i], W.scale.data(), W.zc.data(), c + (size_t)i * n,
+                   accumulate);
+  else
+    dequant(s.acc.data(), rows, n, s.sa.data(), W.scale.data(), W.zc.data(), c, accumulate);
   if (aq_dump)
     for (int i = 0; i < rows; i++) std::memcpy(aq_dump + (size_t)i * k, s.aq.data() + (size_t)i * kp, k);
   if (sa_dump) std::memcpy(sa_dump, s.sa.data(), sizeof(float) * rows);

@@ -244,6 +244,39 @@ def test_cpu_baseline_bitexact(oracle_lib):
     assert np.array_equal(t1.view(np.uint32), t2.view(np.uint32))
 
 
+@pytest.mark.parametrize("case", ["d32_windows", "ragged_widths", "extreme"])
+def test_cpu_baseline_vector_forms_bitexact(oracle_lib, case):
+    """The CPU baseline's AVX2 / VNNI forms (LayerNorm lanes, row quantization,
+    ExpShift, GeluMul, RoPE, attention tiles) equal the scalar loops bit for
+    bit: head dimension 32 with local windows over long sequences, widths that
+    leave scalar tails (hidden 200, intermediate 100, D = 50: the vector
+    attention declines and the scalar one runs), and weights large enough to
+    overflow to infinity (the rows with non-finite values take the scalar
+    form)."""
+    import oracle
+    from indecis_b200 import synthetic as S
+    if case == "d32_windows":
+        cfg = S.tiny(layers=3, hidden=128, heads=4, intermediate=192, vocab=300)
+        ids, offs = S.ids_varlen(6, 1, 400, cfg["vocab"], seed=8)
+        W = S.weights(cfg)
+    elif case == "ragged_widths":
+        cfg = S.tiny(layers=2, hidden=200, heads=4, intermediate=100, vocab=300)
+        ids, offs = S.ids_varlen(5, 1, 170, cfg["vocab"], seed=9)
+        W = S.weights(cfg)
+    else:
+        cfg = S.tiny(layers=2, hidden=128, heads=2, intermediate=192, vocab=300)
+        ids, offs = S.ids_varlen(4, 3, 140, cfg["vocab"], seed=10)
+        W = S.weights(cfg)
+        W["wqkv"][1] = (W["wqkv"][1] * np.float32(1e37)).astype(np.float32)
+        W["wi"][0] = (W["wi"][0] * np.float32(1e36)).astype(np.float32)
+        W["wo"][0][:5] = 0.0
+    m = oracle.Model(cfg, W)
+    for mode in (0, 1):
+        a = m.encode(ids, offs, mode=mode)
+        b = m.encode(ids, offs, mode=mode, threads=3, fast=True)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), mode
+
+
 def test_out_of_vocabulary(oracle_lib):
     import oracle
     from indecis_b200 import synthetic as S

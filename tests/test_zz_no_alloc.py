@@ -59,9 +59,12 @@ def test_noalloc_matches_allocating_entry_point(igdev):
 def test_noalloc_rejects_oversize(igdev):
     from indecis_b200 import _capi
     H, nh = 256, 4
-    offs = np.array([0, 200000], np.int64)  # needs far more than 32 MiB of scratch
+    # 100 sequences of 10000 tokens: each within the length limit, together
+    # far more than 32 MiB of scratch.
+    offs = np.arange(0, 1_000_001, 10_000, dtype=np.int64)
     small = torch.zeros((1, 3 * H), dtype=torch.float32, device="cuda")
-    rc = _capi.load().ig_attention_noalloc(small.data_ptr(), H, nh, offs.ctypes.data, 1, 64, 8, small.data_ptr(),
+    rc = _capi.load().ig_attention_noalloc(small.data_ptr(), H, nh, offs.ctypes.data, len(offs) - 1, 64, 8,
+                                           small.data_ptr(),
                                            torch.cuda.current_stream().cuda_stream)
     assert rc == _capi.IG_ERR_BAD_ARG
     assert "bytes of scratch" in _capi.last_error()
