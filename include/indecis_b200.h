@@ -250,6 +250,16 @@ IG_API int ig_gemm_u8s8(const uint8_t *A, int32_t lda, const int8_t *B, int32_t 
                  const float *sa, const float *sb, const float *zc, float *C, int32_t ldc, int32_t accumulate,
                  int32_t *acc_out, void *stream);
 
+/* The encoder's Wi product with its GeGLU epilogue and the output rows
+ * quantized in the same kernel (MatMul8N + GeluMul + quantizeA of
+ * internal/modernbert/infer.go:416-423, linalg/int8.go:157-191): B holds the
+ * 2I weight rows interleaved per 128 (the GELU inputs of GeGLU columns
+ * 128t..128t+127, then their gates), sa/sb/zc as ig_gemm_u8s8; out q [M][ldq]
+ * uint8 (q + 128) and sa_out [M]. I a multiple of 128, at most 1024. */
+IG_API int ig_gemm_geglu_quant(const uint8_t *A, int32_t lda, const int8_t *B, int32_t ldb, int32_t M, int32_t I,
+                               int32_t K, const float *sa, const float *sb, const float *zc, uint8_t *q, int32_t ldq,
+                               float *sa_out, void *stream);
+
 /* quantizeA (linalg/int8.go:157-191): per row s = max|x|/127,
  * q = rne(x * (1/s)) + 128 (all 128 and s = 0 for a zero row). */
 IG_API int ig_quantize_rows(const float *x, int32_t ldx, int32_t M, int32_t K, uint8_t *q, int32_t ldq, float *sa,

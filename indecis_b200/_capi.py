@@ -32,7 +32,7 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats",
            "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags", "ig_model_set_int8",
            "ig_check_gelu_division", "ig_model_create_multi", "ig_model_replica", "ig_model_device_count",
-           "ig_model_create_stored", "ig_model_create_stored_multi", "ig_device_count"]
+           "ig_model_create_stored", "ig_model_create_stored_multi", "ig_device_count", "ig_gemm_geglu_quant"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -151,6 +151,7 @@ def load() -> C.CDLL:
     L.ig_device_error.restype = i32
     L.ig_gemm_u8s8.argtypes = [vp, i32, vp, i32, i32, i32, i32, vp, vp, vp, vp, i32, i32, vp, vp]
     L.ig_quantize_rows.argtypes = [vp, i32, i32, i32, vp, i32, vp, vp]
+    L.ig_gemm_geglu_quant.argtypes = [vp, i32, vp, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp]
     L.ig_layernorm_quant.argtypes = [vp, vp, i32, i32, C.c_double, i32, vp, vp, i32, vp, vp]
     L.ig_pack_b8.argtypes = [vp, i32, i32, vp, i32, vp, vp, vp, vp]
     L.ig_attention.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]

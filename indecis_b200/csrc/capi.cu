@@ -180,6 +180,7 @@ struct Workspace {
   char *blocks;  // PlanDev lists
   PlanDev pd;
   float *x, *xn, *sa, *qkv, *ctx, *g, *sq, *ks, *kzc, *kmean, *vs, *vinv, *pooled;
+  float *sg;  // row scales of the quantized GeGLU output (kEpiGegluQ; its bytes go over g)
   uint8_t *xq, *qa;
   int8_t *kq, *vq;
   double *logits, *tlogits;
@@ -463,6 +464,26 @@ struct Carve {
   }
 };
 
+// IG_QKV_FUSE=0 runs the QKV projection as its own GEMM (float32 qkv in HBM)
+// before the short-sequence attention kernel (the same bits; for comparisons).
+static bool qkv_fuse_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_QKV_FUSE");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
+// IG_GEGLU_QUANT=0 keeps the GeGLU output in float32 and quantizes it in a
+// separate pass (the same bits; for comparisons).
+static bool geglu_quant_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_GEGLU_QUANT");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
 void carve_ws(Workspace &w, const ig_model *m, char *base, size_t rows, size_t seqs, size_t blks, size_t tl,
               size_t pl, bool f32, size_t *total) {
   Carve c{base};
@@ -478,7 +499,8 @@ void carve_ws(Workspace &w, const ig_model *m, char *base, size_t rows, size_t s
   w.xq = c.take<uint8_t>(rows * m->ldk);
   w.qkv = c.take<float>(rows * 3 * H);
   w.ctx = c.take<float>(rows * H);
-  w.g = c.take<float>(rows * I);
+  w.g = c.take<float>(rows * std::max<size_t>(I, ((size_t)m->ldk + 3) / 4));
+  w.sg = c.take<float>(rows);
   w.qa = c.take<uint8_t>(rows * nh * D);
   w.kq = c.take<int8_t>(rows * nh * D);
   w.vq = c.take<int8_t>(rows * nh * D);
@@ -836,20 +858,34 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       IG_TRY(copy_rows_d2h(dump->hq, w.xq, H, m->ldk, N, st));
       IG_TRY(copy_rows_d2h(dump->hq_s, w.sa, 4, 4, N, st));
     }
+    // The GeGLU output quantized in the Wi epilogue (one cluster per row
+    // block; its bytes over g, its scales in sg) unless this layer is dumped,
+    // or through g in float32 and a quantization pass.
+    GemmEpilogue eq{};
+    eq.geglu_n = I;
+    eq.q_out = reinterpret_cast<uint8_t *>(w.g);
+    eq.ldq = m->ldk;
+    eq.sa_out = w.sg;
+    const bool gq_fused = !dl && geglu_quant_enabled() && gemm_geglu_q_fits(2 * I, eq);
     {
       GemmArgs g{w.xq, L.wi.q, N, L.wi.n, H, m->ldk, L.wi.ld, 256};
-      GemmEpilogue e{};
+      GemmEpilogue e = eq;
       e.sa = w.sa;
       e.sb = L.wi.scale;
       e.zc = L.wi.zc;
       e.C = w.g;
       e.ldc = I;
-      e.geglu_n = I;
-      ProfScope ps("gemm_wi_geglu", gemm_bytes(N, 2 * I, H, 4.0 * I), 2.0 * N * 2 * I * H, 1, st, capturing);
-      IG_TRY(gemm_u8s8(g, e, kEpiGeglu, st));
+      if (gq_fused) {
+        ProfScope ps("gemm_wi_geglu_quant", gemm_bytes(N, 2 * I, H, (double)I + 4.0), 2.0 * N * 2 * I * H, 1, st,
+                     capturing);
+        IG_TRY(gemm_u8s8(g, e, kEpiGegluQ, st));
+      } else {
+        ProfScope ps("gemm_wi_geglu", gemm_bytes(N, 2 * I, H, 4.0 * I), 2.0 * N * 2 * I * H, 1, st, capturing);
+        IG_TRY(gemm_u8s8(g, e, kEpiGeglu, st));
+      }
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->g, w.g, I * 4, I * 4, N, st));
-    {
+    if (!gq_fused) {
       ProfScope ps("quant_rows", (double)N * (5.0 * I + 4), 0, 1, st, capturing);
       IG_TRY(launch_quant_rows(w.g, I, N, I, w.xq, m->ldk, w.sa, st));
     }
@@ -858,9 +894,9 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       IG_TRY(copy_rows_d2h(dump->gq_s, w.sa, 4, 4, N, st));
     }
     {
-      GemmArgs g{w.xq, L.wom.q, N, L.wom.n, I, m->ldk, L.wom.ld, 0};
+      GemmArgs g{gq_fused ? reinterpret_cast<const uint8_t *>(w.g) : w.xq, L.wom.q, N, L.wom.n, I, m->ldk, L.wom.ld, 0};
       GemmEpilogue e{};
-      e.sa = w.sa;
+      e.sa = gq_fused ? w.sg : w.sa;
       e.sb = L.wom.scale;
       e.zc = L.wom.zc;
       e.C = w.x;
@@ -1030,6 +1066,16 @@ int copy_out_staged(Workspace &w, cudaStream_t st, const std::vector<OutCopy> &o
     w.pev.push_back(e);
   }
   char *stage = static_cast<char *>(w.ohost);
+  if (total < kStageMinBytes) {
+    // Small outputs: one wait, then plain host copies on this thread (a
+    // device-to-pageable copy would go through the driver's shared staging,
+    // which serializes concurrent callers).
+    for (auto &pc : ps) IG_CU(cudaMemcpyAsync(stage + pc.at, pc.src, pc.n, cudaMemcpyDeviceToHost, st));
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(e));
+    for (auto &pc : ps) std::memcpy(pc.dst, stage + pc.at, pc.n);
+    return 0;
+  }
   for (size_t i = 0; i < ps.size(); i++) {
     IG_CU(cudaMemcpyAsync(stage + ps[i].at, ps[i].src, ps[i].n, cudaMemcpyDeviceToHost, st));
     IG_CU(cudaEventRecord(w.pev[i], st));
@@ -1207,7 +1253,7 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
     if (mode == IG_MODE_POOLED && p.N == 0) std::memset(out, 0, need * sizeof(float));
     else outs.push_back({mode == IG_MODE_POOLED ? w->pooled : w->xn, out, need * sizeof(float)});
   }
-  if (!rc && out_bytes >= kStageMinBytes) {
+  if (!rc && out_bytes > 0) {
     rc = copy_out_staged(*w, st, outs);
   } else {
     for (auto &o : outs)
@@ -1658,6 +1704,29 @@ int ig_gemm_u8s8(const uint8_t *A, int32_t lda, const int8_t *B, int32_t ldb, in
   e.acc_out = acc_out;
   int rc = gemm_u8s8(g, e, acc_out ? kEpiI32 : kEpiF32, reinterpret_cast<cudaStream_t>(stream));
   if (rc) return fail(rc, "ig_gemm_u8s8: bad shape, stride or alignment (lda/ldb multiples of 16, >= K)");
+  return 0;
+}
+
+int ig_gemm_geglu_quant(const uint8_t *A, int32_t lda, const int8_t *B, int32_t ldb, int32_t M, int32_t I, int32_t K,
+                        const float *sa, const float *sb, const float *zc, uint8_t *q, int32_t ldq, float *sa_out,
+                        void *stream) {
+  t_last_error.clear();
+  if (M < 0 || I < 0 || K < 0) return fail(IG_ERR_BAD_ARG, "negative size");
+  if (!A || !B || !sa || !sb || !zc || !q || !sa_out) return fail(IG_ERR_BAD_ARG, "null argument");
+  GemmArgs g{A, B, M, 2 * I, K, lda, ldb, 256};
+  GemmEpilogue e{};
+  e.sa = sa;
+  e.sb = sb;
+  e.zc = zc;
+  e.geglu_n = I;
+  e.q_out = q;
+  e.ldq = ldq;
+  e.sa_out = sa_out;
+  if (!gemm_geglu_q_fits(2 * I, e))
+    return fail(IG_ERR_UNSUPPORTED, "ig_gemm_geglu_quant: I must be a multiple of 128 and at most 1024, ldq a "
+                                    "multiple of 16 and >= I, q 16-byte aligned");
+  int rc = gemm_u8s8(g, e, kEpiGegluQ, reinterpret_cast<cudaStream_t>(stream));
+  if (rc) return fail(rc, "ig_gemm_geglu_quant: bad shape, stride or alignment");
   return 0;
 }
 

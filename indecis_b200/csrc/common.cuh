@@ -58,6 +58,14 @@ __device__ __forceinline__ void st_dsmem_f32(void *p, uint32_t rank, float v) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
+// Arrives on the mbarrier at the offset of bar in CTA `rank`'s shared memory,
+// releasing this thread's earlier writes (st.shared::cluster included) to
+// the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t *bar, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(bar)), "r"(rank));
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(a) : "memory");
+}
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -84,6 +92,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with cluster-scope acquire: the phase's arrivals came from other
+// CTAs of the cluster (mbar_arrive_cluster), whose writes become visible.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Gives up after about
 // two seconds (a wait that long means a lost arrival): records `code` in
 // g_device_error and returns false so the caller can wind down.
@@ -92,6 +114,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int co
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0 && globaltimer() - t0 > 2000000000ull) {
+      set_device_error(code);
+      return false;
+    }
+  }
+}
+
+// mbar_wait for a barrier that other CTAs of the cluster arrive on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((it & 255u) == 0 && globaltimer() - t0 > 2000000000ull) {
       set_device_error(code);
       return false;

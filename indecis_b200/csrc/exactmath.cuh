@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace ig {
 
 // Vector-body exp of v = x - m (ExpShift, vec_simd.go:235-248).
@@ -93,6 +95,17 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   float d;
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
   return d;
+}
+
+// Row quantization (linalg/int8.go:157-191 quantizeA): a scale RN(max/127)
+// that is a normal float lets every byte take the fast rounding; otherwise
+// (NaN rows, subnormal or infinite scales) each byte takes the clamped path.
+__device__ __forceinline__ bool row_scale_normal(float s) { return s >= 1.17549435e-38f && s <= 3.40282347e38f; }
+
+// Byte q + 128 of one value of a row whose maximum is not 0 (clamped path:
+// any scale).
+__device__ __forceinline__ uint32_t quant_byte_slow(float v, float inv) {
+  return (uint32_t)(max(-128, min(127, rne_int(__fmul_rn(v, inv)))) + 128);
 }
 
 // Integer <-> float without a conversion instruction (those run at an eighth

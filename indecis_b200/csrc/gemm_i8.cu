@@ -282,7 +282,7 @@ int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t s
   if ((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.B)) & 15) return IG_ERR_BAD_ARG;
   int bn = g.bn;
   if (bn != 128 && bn != 256) bn = g.N > 128 ? 256 : 128;
-  if (epi == kEpiGeglu) bn = 256;
+  if (epi == kEpiGeglu || epi == kEpiGegluQ) bn = 256;
   CUtensorMap ma, mb;
   if (make_map_u8(&ma, g.A, g.M, g.K, g.lda, kBM) || make_map_u8(&mb, g.B, g.N, g.K, g.ldb, bn))
     return IG_ERR_CUDA;

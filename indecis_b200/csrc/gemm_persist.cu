@@ -29,7 +29,7 @@ namespace ig {
 // stores, which are bound by the TMA store stream.
 template <int EPI>
 struct PEpi {
-  static constexpr int kWarps = (EPI == kEpiGeglu || EPI == kEpiGeluTanh) ? 16 : 8;
+  static constexpr int kWarps = (EPI == kEpiGeglu || EPI == kEpiGegluQ || EPI == kEpiGeluTanh) ? 16 : 8;
   static constexpr int kGroups = kWarps / 4;  // warps per lane quarter
   static constexpr int kThreads = 64 + 32 * kWarps;
 };
@@ -45,15 +45,23 @@ struct PGemmSmem {
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = BN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStagingBytes = kEpiWarps * kStageBufs * 4096;
+  // kEpiGegluQ stores its int8 rows directly (no staging) and keeps the row
+  // maxima exchange: [4 warps per lane quarter][128 rows] partial maxima and
+  // [2 parities][8 cluster CTAs][128 rows] pushed by the cluster's CTAs.
+  static constexpr bool kQ = EPI == kEpiGegluQ;
+  static constexpr int kStagingBytes = kQ ? 0 : kEpiWarps * kStageBufs * 4096;
+  static constexpr int kXchBytes = kQ ? (4 * 128 + 2 * 8 * 128) * 4 + 16 : 0;
   // K is a few 128-byte blocks per tile here (hidden sizes of a few hundred),
   // so two to four stages keep the tensor cores fed.
-  static constexpr int kStagesRaw = (224 * 1024 - kStagingBytes - 8 * kMaxCols) / kStageBytes;
+  static constexpr int kStagesRaw = (224 * 1024 - kStagingBytes - 8 * kMaxCols - kXchBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 4 ? 4 : kStagesRaw;
   static constexpr int kStaging = kStages * kStageBytes;  // per epilogue warp kStageBufs x [32 rows][128 B]
   static constexpr int kCols = kStaging + kStagingBytes;  // sb[kMaxCols], zc[kMaxCols]
-  static constexpr int kBar = kCols + 8 * kMaxCols;
-  static constexpr int kTmemSlot = kBar + 8 * (2 * kStages + 4);
+  static constexpr int kXPart = kCols + 8 * kMaxCols;     // kEpiGegluQ exchange (float [4][128])
+  static constexpr int kXBuf = kXPart + 4 * 128 * 4;      // float [2][8][128]
+  static constexpr int kXFlag = kXBuf + 2 * 8 * 128 * 4;  // abort flag
+  static constexpr int kBar = kCols + 8 * kMaxCols + kXchBytes;
+  static constexpr int kTmemSlot = kBar + 8 * (2 * kStages + 6);
   static constexpr int kTotal = kTmemSlot + 16 + 1024;
   static_assert(kStages >= 2, "two stages at least");
   static_assert(kTotal <= 227 * 1024, "shared memory");
@@ -314,6 +322,113 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int
   }
 }
 
+// kEpiGegluQ, one output tile for one epilogue warp (lane quarter q, column
+// group g of four): the 32 GeGLU values of its row (as kEpiGeglu computes
+// them), then the row quantized over all geglu_n columns as
+// quant_rows4_kernel does (linalg/int8.go:157-191 quantizeA). The row's
+// maximum is formed in three steps: each thread's |maximum| over its 32
+// values (NaN-ignoring, the sign bit set when a NaN was seen: the
+// NaN-propagating maximum is NaN exactly then), the four column groups of
+// this CTA through shared memory, and the cluster's CTAs (one per 256-column
+// tile of the same 128-row block) by st.shared::cluster into every CTA's
+// exchange buffer with a cluster-scope arrive on its barrier. The TMEM
+// accumulator is handed back as soon as the values are in registers.
+// Returns false when a wait ran out (the caller then stops waiting).
+template <int BN>
+__device__ __forceinline__ bool epilogue_geglu_q(uint32_t tbase, int n0, int m0, int M, float sa, int q, int g, int lane,
+                                                 const GemmEpilogue &ep, uint64_t *acce_b, float *xpart, float *xbuf,
+                                                 uint64_t *xfull, int it, int csize, uint32_t rank, bool ok) {
+  constexpr int H2 = BN / 2;
+  const int g0 = n0 / 2, c = g * 32;
+  const int r = q * 32 + lane, row = m0 + r;
+  float v[32];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    uint32_t ra[16], rg[16];
+    tmem_ld_32x32b_x16(tbase + c + 16 * h, ra);
+    tmem_ld_32x32b_x16(tbase + H2 + c + 16 * h, rg);
+    tmem_ld_wait();
+    float a[16], gt[16];
+    dequant16(ra, ep.sb, ep.zc, n0 + c + 16 * h, 1 << 30, sa, a);
+    dequant16(rg, ep.sb, ep.zc, n0 + H2 + c + 16 * h, 1 << 30, sa, gt);
+#pragma unroll
+    for (int k = 0; k < 16; k += 2) {
+      const float2 o2 = gelu_mul_fma2(make_float2(a[k], a[k + 1]), make_float2(gt[k], gt[k + 1]));
+      v[16 * h + k] = o2.x;
+      v[16 * h + k + 1] = o2.y;
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(acce_b);
+  float m = 0.0f;
+  bool nan = false;
+#pragma unroll
+  for (int k = 0; k < 32; k++) {
+    m = fmaxf(m, fabsf(v[k]));
+    nan |= v[k] != v[k];
+  }
+  xpart[g * 128 + r] = nan ? -m : m;  // -0.0 keeps the sign bit for a zero maximum
+  named_barrier_sync(3, 512);
+  const int par = it & 1;
+  if (g == 0) {
+    float e = 0.0f;
+    bool en = false;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float x = xpart[k * 128 + r];
+      e = fmaxf(e, fabsf(x));
+      en |= signbit(x);
+    }
+    e = en ? -e : e;
+    float *slot = xbuf + (par * 8 + (int)rank) * 128 + r;
+    for (int cr = 0; cr < csize; cr++) {
+      st_dsmem_f32(slot, (uint32_t)cr, e);
+      mbar_arrive_cluster(&xfull[par], (uint32_t)cr);
+    }
+  }
+  ok = ok && mbar_wait_cluster(&xfull[par], (uint32_t)(it >> 1) & 1u, kDevTimeoutAccum);
+  float mx = 0.0f;
+  bool has_nan = false;
+  for (int cr = 0; cr < csize; cr++) {
+    const float x = xbuf[(par * 8 + cr) * 128 + r];
+    mx = fmaxf(mx, fabsf(x));
+    has_nan |= signbit(x);
+  }
+  float qs = 0.0f, qinv = 0.0f;
+  if (mx > 0.0f) {
+    qs = __fdiv_rn(mx, 127.0f);
+    qinv = __fdiv_rn(1.0f, qs);
+  }
+  const bool fast = !has_nan && row_scale_normal(qs);
+  uint32_t w[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const float *x4 = v + 4 * k;
+    if (mx == 0.0f) {
+      w[k] = 0x80808080u;
+    } else if (fast) {
+      const float2 p0 = __fmul2_rn(make_float2(x4[0], x4[1]), f2(qinv));
+      const float2 p1 = __fmul2_rn(make_float2(x4[2], x4[3]), f2(qinv));
+      const uint32_t b0 = __float_as_uint(__fadd_rn(p0.x, kMagic + 128.0f));
+      const uint32_t b1 = __float_as_uint(__fadd_rn(p0.y, kMagic + 128.0f));
+      const uint32_t b2 = __float_as_uint(__fadd_rn(p1.x, kMagic + 128.0f));
+      const uint32_t b3 = __float_as_uint(__fadd_rn(p1.y, kMagic + 128.0f));
+      w[k] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+    } else {
+      w[k] = quant_byte_slow(x4[0], qinv) | (quant_byte_slow(x4[1], qinv) << 8) |
+             (quant_byte_slow(x4[2], qinv) << 16) | (quant_byte_slow(x4[3], qinv) << 24);
+    }
+  }
+  if (ok && row < M) {
+    uint4 *dst = reinterpret_cast<uint4 *>(ep.q_out + (size_t)row * ep.ldq + g0 + c);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    if (rank == 0 && g == 0) ep.sa_out[row] = qs;
+  }
+  return ok;
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
     gemm_persist_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
@@ -346,12 +461,20 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
       mbar_init(&accf[b], 1);
       mbar_init(&acce[b], PEpi<EPI>::kWarps);
     }
+    if constexpr (S::kQ) {
+      // Each phase of a row-maximum exchange barrier completes when all 128
+      // rows of every CTA of the cluster (one per column tile) have arrived.
+      for (int b = 0; b < 2; b++) mbar_init(&acce[2 + b], 128 * tiles_n);
+      *reinterpret_cast<volatile int *>(smem + S::kXFlag) = 0;
+    }
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // The cluster's barriers are initialised before any CTA arrives on them.
+  if constexpr (S::kQ) cluster_sync_all();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -422,7 +545,29 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
       eps.zc = s_zc;
     }
     int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
+    if constexpr (S::kQ) {
+      // Every epilogue warp takes part in every tile's exchange (named
+      // barrier, cluster barrier phases) whatever happens, so a wait that ran
+      // out only sets the abort flag: later tiles skip their waits.
+      volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::kXFlag);
+      float *xpart = reinterpret_cast<float *>(smem + S::kXPart);
+      float *xbuf = reinterpret_cast<float *>(smem + S::kXBuf);
+      const uint32_t rank = cluster_ctarank();
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
+        const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
+        const int b = it & 1;
+        const uint32_t u = (uint32_t)(it >> 1);
+        bool ok = *abort_flag == 0 && mbar_wait(&accf[b], u & 1, kDevTimeoutAccum);
+        tc_fence_after();
+        const int row = m0 + q * 32 + lane;
+        const float sa = row < M ? __ldg(ep.sa + row) : 0.0f;
+        const uint32_t tbase = tmem + b * BN + ((uint32_t)(q * 32) << 16);
+        ok = epilogue_geglu_q<BN>(tbase, n0, m0, M, sa, q, g, lane, ep, &acce[b], xpart, xbuf, acce + 2, it, tiles_n,
+                                  rank, ok);
+        if (!ok) *abort_flag = 1;
+      }
+    }
+    for (int t = blockIdx.x; t < ntiles && !S::kQ; t += gridDim.x, it++) {
       const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * BN;
       const int b = it & 1;
       const uint32_t u = (uint32_t)(it >> 1);
@@ -449,6 +594,8 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 2 * BN);
   }
+  // No CTA leaves while another may still write its exchange buffer.
+  if constexpr (S::kQ) cluster_sync_all();
 }
 
 // f32 (or int32) output [rows][cols] with row stride ld elements: TMA boxes of
@@ -483,10 +630,38 @@ static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, 
   static SmemOptIn attr;
   cudaError_t e = attr.ensure((const void *)gemm_persist_kernel<BN, EPI>, S::kTotal);
   if (e != cudaSuccess) return e;
-  const int ntiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int tiles_n = (N + BN - 1) / BN, mblocks = (M + kBM - 1) / kBM;
+  const int ntiles = mblocks * tiles_n;
+  if constexpr (S::kQ) {
+    // One cluster of tiles_n CTAs per 128-row block at a time: the grid is a
+    // whole number of clusters, so CTA rank r always takes column tile r.
+    int clusters = num_sms() / tiles_n;
+    if (clusters > mblocks) clusters = mblocks;
+    if (clusters < 1) clusters = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(clusters * tiles_n);
+    cfg.blockDim = dim3(PEpi<EPI>::kThreads);
+    cfg.dynamicSmemBytes = S::kTotal;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = tiles_n;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_persist_kernel<BN, EPI>, ma, mb, mc, M, N, K, ep);
+  }
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   gemm_persist_kernel<BN, EPI><<<grid, PEpi<EPI>::kThreads, S::kTotal, st>>>(ma, mb, mc, M, N, K, ep);
   return cudaGetLastError();
+}
+
+// kEpiGegluQ needs whole 128-column GeGLU tiles (so each CTA's columns are
+// all valid), at most 8 tiles (a portable cluster), and 16-byte row pieces.
+bool gemm_geglu_q_fits(int N, const GemmEpilogue &ep) {
+  return ep.geglu_n > 0 && ep.geglu_n % 128 == 0 && N == 2 * ep.geglu_n && N / 256 <= 8 && ep.q_out &&
+         ep.sa_out && ep.ldq >= ep.geglu_n && ep.ldq % 16 == 0 && (reinterpret_cast<uintptr_t>(ep.q_out) & 15) == 0;
 }
 
 // The CTA-pair kernel (gemm_pair.cu) for deep products with 256-column
@@ -498,6 +673,14 @@ static int gemm_pair_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, con
 // caller for the plain kernel.
 static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, int bn, const CUtensorMap &ma,
                             const CUtensorMap &mb, cudaStream_t st) {
+  if (epi == kEpiGegluQ) {
+    // No float output: the quantized rows are stored by the epilogue itself.
+    if (bn != 256 || !gemm_geglu_q_fits(g.N, ep) ||
+        ((reinterpret_cast<uintptr_t>(ep.sb) | reinterpret_cast<uintptr_t>(ep.zc)) & 15))
+      return IG_ERR_UNSUPPORTED;
+    const cudaError_t e = launch_persist<256, kEpiGegluQ>(ma, mb, mb, g.M, g.N, g.K, ep, st);
+    return e == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
   void *out = epi == kEpiI32 ? (void *)ep.acc_out : (void *)ep.C;
   if (!out || (reinterpret_cast<uintptr_t>(out) & 15) || (ep.ldc & 3)) return -1;
   if (epi != kEpiI32 && ((reinterpret_cast<uintptr_t>(ep.sb) | reinterpret_cast<uintptr_t>(ep.zc)) & 15)) return -1;

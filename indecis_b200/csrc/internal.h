@@ -14,6 +14,8 @@ enum Epilogue : int {
   kEpiF32Bias = 4,   // C (+)= dequant + bias[j]   (MatMul8N then AddTo(bias), accumulate: AddTo(x, .))
   kEpiGeluTanh = 5,  // C = GeluTanh(dequant + bias[j])
   kEpiOutlierRes = 6,  // C += (dequant + outlier terms in order) + bias[j]  (MatMul8Outliers, then AddTo twice)
+  kEpiGegluQ = 7,      // kEpiGeglu, then the output row quantized (quantizeA) into q_out + sa_out: a cluster per
+                       // row block, its CTAs (one per 256-column tile) exchanging the row maxima
 };
 
 struct GemmArgs {
@@ -32,8 +34,13 @@ struct GemmEpilogue {
   int32_t *acc_out; // int32 output (kEpiI32)
   int ldc;
   int accumulate;   // C = dequant + C
-  // kEpiGeglu
+  // kEpiGeglu, kEpiGegluQ
   int geglu_n;  // GeGLU output width (intermediate size)
+  // kEpiGegluQ: the quantized GeGLU rows (uint8 q + 128, row stride ldq) and
+  // their scales; neither may alias the A operand or sa.
+  uint8_t *q_out;
+  int ldq;
+  float *sa_out;
   // kEpiF32Bias, kEpiGeluTanh
   const float *bias;  // [N], 16-byte aligned
   int seg_rows;       // kEpiGeluTanh: rows per GeluTanh call (its vector/tail split), >= 1;
@@ -47,6 +54,8 @@ struct GemmEpilogue {
 };
 
 int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t st);
+// Whether the GeGLU GEMM can quantize its output rows itself (kEpiGegluQ).
+bool gemm_geglu_q_fits(int N, const GemmEpilogue &ep);
 
 // ---- row kernels (rows.cu) ----
 // x (f32 [M][H]) -> LayerNorm (gamma) -> optional xn out -> per-row quantized
@@ -128,6 +137,16 @@ struct AttnArgs {
   uint8_t *xq = nullptr;
   int ldq = 0;
   float *sa = nullptr;
+  // Optional (the fused short-sequence kernel with the QKV projection in
+  // front, qkv unused): the normalized rows quantized (uint8 q + 128, row
+  // pitch lda, scales xa_s) and the QKV weights (int8 [3H][ldw] output
+  // channel rows, scales wsb, 128 * column sums wzc).
+  const uint8_t *xa = nullptr;
+  int lda = 0;
+  const float *xa_s = nullptr;
+  const int8_t *wqkv = nullptr;
+  int ldw = 0;
+  const float *wsb = nullptr, *wzc = nullptr;
 };
 // Whether launch_attn_short can quantize ctx itself (AttnArgs::xq).
 bool attn_short_quantizes(const AttnArgs &a);
@@ -143,6 +162,9 @@ int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaS
 // most 128 tokens, H a multiple of 4; RoPE applied when rope_cos is set.
 bool attn_short_fits(const AttnArgs &a);
 int launch_attn_short(const AttnArgs &a, cudaStream_t st);
+// Whether the short-sequence kernel can also compute the QKV projection
+// (AttnArgs::xa, ::wqkv; ctx quantized into xq): H = nh * 64 of 128 or 256.
+bool attn_short_projects(const AttnArgs &a);
 
 // Device error flag (kernels' bounded waits).
 int read_device_error(int reset);

@@ -25,14 +25,6 @@
 
 namespace ig {
 
-__device__ __forceinline__ bool row_scale_normal(float s) { return s >= 1.17549435e-38f && s <= 3.40282347e38f; }
-
-// Byte q + 128 of one value of a row whose maximum is not 0 (clamped path:
-// any scale).
-__device__ __forceinline__ uint32_t quant_byte_slow(float v, float inv) {
-  return (uint32_t)(max(-128, min(127, rne_int(__fmul_rn(v, inv)))) + 128);
-}
-
 // gamma[k + 8b] read through the read-only cache.
 struct GammaLdg {
   const float *p;

@@ -50,6 +50,27 @@ def gemm_u8s8(A, B, K=None, sa=None, sb=None, zc=None, C=None, accumulate=False,
     return C
 
 
+def gemm_geglu_quant(A, B, I, sa, sb, zc, K=None, ldq=None):
+    """The Wi product with the GeGLU epilogue and the output quantized per
+    row in the same kernel: B int8 [2I][ldb], rows interleaved per 128 (GELU
+    inputs, then gates). Returns (q uint8 [M][ldq], scales [M])."""
+    _need(A, torch.uint8, "A")
+    _need(B, torch.int8, "B")
+    for t, n in ((sa, "sa"), (sb, "sb"), (zc, "zc")):
+        _need(t, torch.float32, n)
+    M, lda = A.shape
+    N, ldb = B.shape
+    if N != 2 * I:
+        raise ValueError("B must hold 2I rows")
+    K = K if K is not None else lda
+    ldq = ldq or I
+    q = torch.full((M, ldq), 0xAB, dtype=torch.uint8, device=A.device)
+    s = torch.full((M,), float("nan"), dtype=torch.float32, device=A.device)
+    _capi.check(_capi.load().ig_gemm_geglu_quant(_ptr(A), lda, _ptr(B), ldb, M, I, K, _ptr(sa), _ptr(sb), _ptr(zc),
+                                                 _ptr(q), ldq, _ptr(s), _stream()))
+    return q, s
+
+
 def quantize_rows(x, ldq=None):
     _need(x, torch.float32, "x")
     M, K = x.shape

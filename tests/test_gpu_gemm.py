@@ -94,3 +94,66 @@ def test_gemm_sweep_shapes(igdev, oracle_lib, M, N, K):
     # size-independent property over all rows: exact integer product vs int64 numpy
     full = (A.astype(np.int64) @ B.astype(np.int64).T)
     assert np.array_equal(acc.astype(np.int64), full)
+
+
+def _geglu_quant_ref(oracle_lib, A, B, K, I, sa, sb, zc):
+    """Wi product, GeGLU (interleaved rows: per 128 columns the GELU inputs,
+    then their gates) and quantizeA of each output row, on the oracle."""
+    acc = oracle_lib.gemm_u8s8(np.ascontiguousarray(A[:, :K]), np.ascontiguousarray(B[:, :K]))
+    z = oracle_lib.dequant(acc, sa, sb, zc)
+    j = np.arange(I)
+    inp = z[:, 256 * (j // 128) + j % 128]
+    gate = z[:, 256 * (j // 128) + 128 + j % 128]
+    g = oracle_lib.gelu_mul(inp, gate).reshape(inp.shape)
+    return oracle_lib.quantize_a(g)
+
+
+@pytest.mark.parametrize("M,I,K", [(300, 384, 256), (1, 128, 256), (15360, 384, 256), (777, 1024, 384),
+                                   (129, 256, 96)])
+def test_gemm_geglu_quant_bitexact(igdev, oracle_lib, M, I, K):
+    """The Wi GEMM whose epilogue computes GeGLU and quantizes each output row
+    over the cluster of its column tiles equals the oracle's MatMul8N,
+    GeluMul and quantizeA (internal/modernbert/infer.go:416-423,
+    linalg/int8.go:157-191) bit for bit: bytes and row scales, many row
+    blocks per cluster (15360 rows), clusters of 1 to 8 CTAs, and rows that
+    take the clamped path: a NaN row scale (NaN values), a huge one (values
+    that overflow to infinity), a zero one (a zero row) and a tiny one
+    (subnormal outputs and scale)."""
+    from indecis_b200 import ops
+    A, B, sa, sb, zc = _case(M, 2 * I, K, seed=M + I)
+    special = {3: np.nan, 4: 1e30, 5: 0.0, 6: 1e-30}
+    for r, v in special.items():
+        if r < M:
+            sa[r] = v
+    q_ref, s_ref = _geglu_quant_ref(oracle_lib, A, B, K, I, sa, sb, zc)
+    dA, dB, dsa, dsb, dzc = _dev(A, B, sa, sb, zc)
+    ldq = I + 16
+    q, s = ops.gemm_geglu_quant(dA, dB, I, dsa, dsb, dzc, K=K, ldq=ldq)
+    q, s = q.cpu().numpy(), s.cpu().numpy()
+    assert np.array_equal(q[:, :I], q_ref)
+    assert (q[:, I:] == 0xAB).all()  # nothing written past the row's I bytes
+    assert np.array_equal(s.view(np.uint32), s_ref.view(np.uint32))
+
+
+def test_gemm_residual_subnormal(igdev, oracle_lib):
+    """The residual store x + dequant through the TMA reduce-add keeps IEEE
+    addition on subnormal operands (the reference's VADDPS with no flush to
+    zero): subnormal old values, subnormal dequantized values, and sums that
+    cross the normal boundary."""
+    from indecis_b200 import ops
+    M, N, K = 260, 256, 256
+    A, B, sa, sb, zc = _case(M, N, K, seed=11)
+    sa[:] = np.float32(1e-41)  # dequantized values around 1e-41 .. 1e-36, many subnormal
+    sa[::7] = np.float32(1e-3)
+    acc_ref = oracle_lib.gemm_u8s8(np.ascontiguousarray(A[:, :K]), np.ascontiguousarray(B[:, :K]))
+    rng = np.random.default_rng(5)
+    tiny = np.float32(1.17549435e-38)
+    old = (rng.uniform(-4, 4, (M, N)) * tiny).astype(np.float32)  # subnormal and just-normal values
+    old[1::5] = rng.standard_normal((len(range(1, M, 5)), N)).astype(np.float32)
+    dA, dB, dsa, dsb, dzc = _dev(A, B, sa, sb, zc)
+    dC = torch.from_numpy(old.copy()).cuda()
+    ops.gemm_u8s8(dA, dB, K=K, sa=dsa, sb=dsb, zc=dzc, C=dC, accumulate=True)
+    want = oracle_lib.dequant(acc_ref, sa, sb, zc, C_old=old)
+    got = dC.cpu().numpy()
+    assert (np.abs(want[np.abs(want) > 0]) < tiny).any()  # subnormal results are present
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
