@@ -65,10 +65,18 @@ struct AttnShortSmem {
   static constexpr int kMean = kSq + 512;   // 64
   static constexpr int kVs = kMean + 256;   // 64
   static constexpr int kVinv = kVs + 256;   // 64
-  static constexpr int kBar = kVinv + 256;  // 4 mbarriers
-  static constexpr int kTmem = kBar + 32;   // TMEM base address; V fast-path flag at +4
+  static constexpr int kBar = kVinv + 256;  // 6 mbarriers
+  static constexpr int kTmem = kBar + 48;   // TMEM base address; V fast-path flag at +4
   static constexpr int kXch = kTmem + 16;   // [8][128] row maxima of the cluster's CTAs (ctx quantization)
-  static constexpr int kTotal = kXch + 8 * 128 * 4 + 1024;
+  static constexpr int kQx = kXch + 8 * 128 * 4;  // [2][128] Q row half-maxima (fused projection)
+  static constexpr int kTotal = kQx + 2 * 128 * 4 + 1024;
+  // Fused projection: the operands of the Q product (A = the sequence's
+  // quantized rows, [128][128 B] SWIZZLE_128B per 128-byte K block; B = the
+  // head's 64 Q weight rows) and then of the K|V product (B = its 64 K and
+  // 64 V weight rows, [128][128 B] per K block, over the Q weights) lie where
+  // the f32 K and V slices go once the products have read them.
+  static constexpr int kA = 0;
+  static constexpr int kB = 32768;
   static_assert(kO + 128 * kOPitch * 4 <= kRed, "ctx staging overlaps the exchange");
   static_assert(kShortCtasPerSm * (kTotal + 1024) <= 228 * 1024, "three CTAs per SM");
 };
@@ -154,11 +162,49 @@ __device__ __forceinline__ uint32_t quant4_fast_s8(float a, float b, float c, fl
   return quant4_fast(a, b, c, d, inv01, inv23) ^ 0x80808080u;
 }
 
+// Presets 16 TMEM columns of a projection accumulator (this thread's lane) to
+// the bits 2 * 0x4B400000 - bits(zc + 1.5*2^23) = 0x4B400000 - zc (zc is
+// 128 * a column sum, an integer below 2^22 in magnitude), so that after the
+// products the accumulator holds the float 1.5*2^23 + (acc - zc):
+// |acc - zc| = |sum (x_q) w| <= 128 * 127 * H < 2^22 for H <= 256.
+__device__ __forceinline__ void tmem_preset_zc16(uint32_t taddr, const float *__restrict__ zc) {
+  uint32_t v[16];
+#pragma unroll
+  for (int k = 0; k < 16; k += 4) {
+    const float4 z = __ldg(reinterpret_cast<const float4 *>(zc + k));
+    v[k] = 2u * (uint32_t)kMagicBits - __float_as_uint(__fadd_rn(z.x, kMagic));
+    v[k + 1] = 2u * (uint32_t)kMagicBits - __float_as_uint(__fadd_rn(z.y, kMagic));
+    v[k + 2] = 2u * (uint32_t)kMagicBits - __float_as_uint(__fadd_rn(z.z, kMagic));
+    v[k + 3] = 2u * (uint32_t)kMagicBits - __float_as_uint(__fadd_rn(z.w, kMagic));
+  }
+  tmem_st_32x32b_x16(taddr, v);
+}
+
+// ((float(acc) - zc) * sb) * sa of four accumulators preset by
+// tmem_preset_zc16: the subtraction of 1.5*2^23 recovers acc - zc exactly (as
+// float(acc) - zc is exact: both are integers below 2^24), then the two
+// products of the QKV GEMM's epilogue.
+__device__ __forceinline__ float4 dequant_preset4(const uint32_t *a, const float *__restrict__ sb, float sa) {
+  const float4 b = __ldg(reinterpret_cast<const float4 *>(sb));
+  float2 lo = __fadd2_rn(make_float2(__uint_as_float(a[0]), __uint_as_float(a[1])), f2(-kMagic));
+  float2 hi = __fadd2_rn(make_float2(__uint_as_float(a[2]), __uint_as_float(a[3])), f2(-kMagic));
+  lo = __fmul2_rn(__fmul2_rn(lo, make_float2(b.x, b.y)), f2(sa));
+  hi = __fmul2_rn(__fmul2_rn(hi, make_float2(b.z, b.w)), f2(sa));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
+// QKV: the kernel also computes the (sequence, head) slices of the QKV
+// projection (internal/modernbert/infer.go:388-390, MatMul8N with the
+// quantized normalized rows) on the tensor cores: mqkv then maps the
+// quantized rows [N][H] (uint8), mw the QKV weights [3H][H] (int8); xa_s,
+// wsb, wzc are the row scales, column scales and 128 * column sums.
+template <bool QKV>
 __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
-    attn_short_kernel(const __grid_constant__ CUtensorMap mqkv, const float *__restrict__ qkv,
-                      const int32_t *__restrict__ offs, int H, int nh, int window, int V, float scale,
-                      const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
-                      float *__restrict__ ctx, uint8_t *__restrict__ xq, int ldq, float *__restrict__ sa) {
+    attn_short_kernel(const __grid_constant__ CUtensorMap mqkv, const __grid_constant__ CUtensorMap mw,
+                      const float *__restrict__ qkv, const int32_t *__restrict__ offs, int H, int nh, int window,
+                      int V, float scale, const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
+                      float *__restrict__ ctx, uint8_t *__restrict__ xq, int ldq, float *__restrict__ sa,
+                      const float *__restrict__ xa_s, const float *__restrict__ wsb, const float *__restrict__ wzc) {
   using S = AttnShortSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -174,6 +220,8 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   uint64_t *bar_s = bar_load + 1;
   uint64_t *bar_p = bar_load + 2;
   uint64_t *bar_o = bar_load + 3;
+  uint64_t *bar_b = bar_load + 4;  // fused projection: the K|V weight rows have landed
+  uint64_t *bar_m = bar_load + 5;  // fused projection: a product is complete (Q, then K|V)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::kTmem);
   volatile int *s_vfast = reinterpret_cast<volatile int *>(smem + S::kTmem + 4);
 
@@ -185,62 +233,122 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   const int rr = tid >> 1, hh = tid & 1;
   const bool rope = rope_cos != nullptr;
 
-  // 1. K and V by TMA; Q and the RoPE factors straight into registers.
-  if (tid == 0) {
-    *s_vfast = 1;
-    prefetch_tensormap(&mqkv);
-    mbar_init(bar_load, 1);
-    mbar_init(bar_s, 1);
-    mbar_init(bar_p, kShortThreads);
-    mbar_init(bar_o, 1);
-    fence_barrier_init();
-    mbar_arrive_expect_tx(bar_load, 4 * S::kHalf);
-#pragma unroll
-    for (int x = 0; x < 2; x++)
-#pragma unroll
-      for (int half = 0; half < 2; half++)
-        tma_load_2d(&mqkv, smem + x * 32768 + half * S::kHalf, bar_load, (x + 1) * H + h * 64 + half * 32, t0);
-  }
-  if (warp == 1) tmem_alloc(tmem_slot, 128);
-  float qv[32];  // [0,16): dimensions 16hh.., [16,32): 32+16hh..
-  if (rr < n) {
-    const float *qrow = qkv + (size_t)(t0 + rr) * 3 * H + h * 64 + 16 * hh;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const float4 lo = __ldg(reinterpret_cast<const float4 *>(qrow + 4 * k));
-      const float4 hi = __ldg(reinterpret_cast<const float4 *>(qrow + 32 + 4 * k));
-      qv[4 * k] = lo.x, qv[4 * k + 1] = lo.y, qv[4 * k + 2] = lo.z, qv[4 * k + 3] = lo.w;
-      qv[16 + 4 * k] = hi.x, qv[17 + 4 * k] = hi.y, qv[18 + 4 * k] = hi.z, qv[19 + 4 * k] = hi.w;
-    }
-    if (rope) {
-#pragma unroll
-      for (int k = 0; k < 4; k++) {
-        const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)rr * 32 + 16 * hh + 4 * k));
-        const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)rr * 32 + 16 * hh + 4 * k));
-        const float c4[4] = {rc.x, rc.y, rc.z, rc.w}, s4[4] = {rs.x, rs.y, rs.z, rs.w};
-#pragma unroll
-        for (int u = 0; u < 4; u++) rope1(qv[4 * k + u], qv[16 + 4 * k + u], c4[u], s4[u]);
+  uint32_t qw[8];  // this thread's half of its Q row, quantized (bytes q + 128)
+  int qr = rr, qh = hh;  // that row and half
+  bool ok;
+  if constexpr (QKV) {
+    // 1'. The projection: Q = A . Wq^T (N = 64) into TMEM, the Q rows
+    // dequantized, rotated and quantized in registers; then K|V = A . Wkv^T
+    // (N = 128) over the same columns, K rotated into the f32 K slice and V
+    // into the f32 V slice. Thread (lane quarter q4, half hq) takes row
+    // r = 32 q4 + lane (its TMEM lane) and dimensions 16hq.., 32+16hq..
+    const int nkb = H >> 7;  // 128-byte K blocks of the projection
+    if (tid == 0) {
+      *s_vfast = 1;
+      prefetch_tensormap(&mqkv);
+      prefetch_tensormap(&mw);
+      mbar_init(bar_load, 1);
+      mbar_init(bar_s, 1);
+      mbar_init(bar_p, kShortThreads);
+      mbar_init(bar_o, 1);
+      mbar_init(bar_b, 1);
+      mbar_init(bar_m, 1);
+      fence_barrier_init();
+      // A: 128 rows from the sequence's first (rows past it are never used);
+      // B: the head's 64 Q weight rows.
+      mbar_arrive_expect_tx(bar_load, nkb * (16384 + 8192));
+      for (int kb = 0; kb < nkb; kb++) {
+        tma_load_2d(&mqkv, smem + S::kA + kb * 16384, bar_load, kb * 128, t0);
+        tma_load_2d(&mw, smem + S::kB + kb * 8192, bar_load, kb * 128, h * 64);
       }
     }
-  } else {
+    if (warp == 1) tmem_alloc(tmem_slot, 128);
+    const int q4 = warp & 3, hq = warp >> 2, r = q4 * 32 + lane;
+    qr = r;
+    qh = hq;
+    tc_fence_before();
+    __syncthreads();  // barriers initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tm = *tmem_slot;
+    const uint32_t trow = tm + ((uint32_t)(q4 * 32) << 16);
+    const uint32_t a_base = smem_u32(smem + S::kA), b_base = smem_u32(smem + S::kB);
+    tmem_preset_zc16(trow + 16 * hq, wzc + h * 64 + 16 * hq);
+    tmem_preset_zc16(trow + 32 + 16 * hq, wzc + h * 64 + 32 + 16 * hq);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      const bool okl = mbar_wait(bar_load, 0, kDevTimeoutFull);
+      tc_fence_after();
+      if (okl)
+        for (int kb = 0; kb < nkb; kb++)
 #pragma unroll
-    for (int u = 0; u < 32; u++) qv[u] = 0.0f;
-  }
-  uint32_t qw[8];
-  {
-    // Row maximum, NaN-propagating first: a row holding a NaN takes the
-    // clamped path (with the NaN-ignoring maximum, as the reference's).
-    float qmx = absmax32<true>(qv);
-    qmx = fmax_nan(qmx, __shfl_xor_sync(0xffffffffu, qmx, 1));
-    const bool qnan = qmx != qmx;
-    if (__any_sync(0xffffffffu, qnan)) {
-      qmx = absmax32<false>(qv);
-      qmx = fmaxf(qmx, __shfl_xor_sync(0xffffffffu, qmx, 1));
+          for (int kk = 0; kk < 4; kk++)
+            mma_u8s8(tm, smem_desc_k_sw128(a_base + kb * 16384 + kk * 32),
+                     smem_desc_k_sw128(b_base + kb * 8192 + kk * 32), idesc_u8s8(128, 64), 1);
+      mma_commit(bar_m);
+      // The Q weights' region takes the K and V weight rows once the products
+      // have read it.
+      if (okl && mbar_wait(bar_m, 0, kDevTimeoutAccum)) {
+        mbar_arrive_expect_tx(bar_b, nkb * 16384);
+        for (int kb = 0; kb < nkb; kb++) {
+          tma_load_2d(&mw, smem + S::kB + kb * 16384, bar_b, kb * 128, H + h * 64);
+          tma_load_2d(&mw, smem + S::kB + kb * 16384 + 8192, bar_b, kb * 128, 2 * H + h * 64);
+        }
+      }
     }
+    __syncwarp();
+    ok = mbar_wait(bar_m, 0, kDevTimeoutAccum);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    const float sar = r < n ? __ldg(xa_s + t0 + r) : 0.0f;
+    float qv[32];
+    {
+      uint32_t a0[16], a1[16];
+      tmem_ld_32x32b_x16(trow + 16 * hq, a0);
+      tmem_ld_32x32b_x16(trow + 32 + 16 * hq, a1);
+      tmem_ld_wait();
+      const float *qb_lo = wsb + h * 64 + 16 * hq, *qb_hi = qb_lo + 32;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float4 lo = dequant_preset4(a0 + 4 * k, qb_lo + 4 * k, sar);
+        const float4 hi = dequant_preset4(a1 + 4 * k, qb_hi + 4 * k, sar);
+        qv[4 * k] = lo.x, qv[4 * k + 1] = lo.y, qv[4 * k + 2] = lo.z, qv[4 * k + 3] = lo.w;
+        qv[16 + 4 * k] = hi.x, qv[17 + 4 * k] = hi.y, qv[18 + 4 * k] = hi.z, qv[19 + 4 * k] = hi.w;
+      }
+    }
+    if (r < n) {
+      if (rope) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)r * 32 + 16 * hq + 4 * k));
+          const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)r * 32 + 16 * hq + 4 * k));
+          const float c4[4] = {rc.x, rc.y, rc.z, rc.w}, s4[4] = {rs.x, rs.y, rs.z, rs.w};
+#pragma unroll
+          for (int u = 0; u < 4; u++) rope1(qv[4 * k + u], qv[16 + 4 * k + u], c4[u], s4[u]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 32; u++) qv[u] = 0.0f;
+    }
+    // The row's maximum over both halves (the other half is another warp's):
+    // |maximum| over the non-NaN values, the sign bit set where a NaN was seen.
+    float *s_qx = reinterpret_cast<float *>(smem + S::kQx);
+    const float qm = absmax32<false>(qv);
+    bool qn = false;
+#pragma unroll
+    for (int u = 0; u < 32; u++) qn |= qv[u] != qv[u];
+    s_qx[hq * 128 + r] = qn ? neg_bits(qm) : qm;
+    tc_fence_before();
+    __syncthreads();  // the Q accumulators are read, the half maxima written
+    tc_fence_after();
+    const float qo = s_qx[(hq ^ 1) * 128 + r];
+    const float qmx = fmaxf(qm, fabsf(qo));
+    const bool qnan = qn || signbit(qo);
     const float qs = qmx > 0.0f ? __fdiv_rn(qmx, 127.0f) : 0.0f;
     const float qinv = qmx > 0.0f ? __fdiv_rn(1.0f, qs) : 0.0f;
-    // Byte q + 128, q = clamp(rne(x * qinv)); a row whose maximum is 0 is all
-    // 128 (attention8.go:210-220).
     if (qmx == 0.0f) {
 #pragma unroll
       for (int k = 0; k < 8; k++) qw[k] = 0x80808080u;
@@ -257,25 +365,154 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
         qw[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
       }
     }
-    if (hh == 0) s_sq[rr] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
-  }
-  __syncthreads();  // barriers initialised
-  bool ok = mbar_wait(bar_load, 0, kDevTimeoutFull);
-
-  // A. K rotated in place (the RoPE factors are read again; they are cached).
-  if (rope && rr < n) {
+    if (hq == 0) s_sq[r] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
+    // K|V: columns 0-63 K, 64-127 V.
+    tmem_preset_zc16(trow + 16 * hq, wzc + H + h * 64 + 16 * hq);
+    tmem_preset_zc16(trow + 32 + 16 * hq, wzc + H + h * 64 + 32 + 16 * hq);
+    tmem_preset_zc16(trow + 64 + 16 * hq, wzc + 2 * H + h * 64 + 16 * hq);
+    tmem_preset_zc16(trow + 96 + 16 * hq, wzc + 2 * H + h * 64 + 32 + 16 * hq);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      const bool okb = ok && mbar_wait(bar_b, 0, kDevTimeoutFull);
+      tc_fence_after();
+      if (okb)
+        for (int kb = 0; kb < nkb; kb++)
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int c = 4 * hh + k;
-      const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)rr * 32 + 16 * hh + 4 * k));
-      const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)rr * 32 + 16 * hh + 4 * k));
-      float4 lo = *f32_chunk(kf, rr, c), hi = *f32_chunk(kf, rr, 8 + c);
-      rope4(lo, hi, rc, rs);
-      *f32_chunk(kf, rr, c) = lo;
-      *f32_chunk(kf, rr, 8 + c) = hi;
+          for (int kk = 0; kk < 4; kk++)
+            mma_u8s8(tm, smem_desc_k_sw128(a_base + kb * 16384 + kk * 32),
+                     smem_desc_k_sw128(b_base + kb * 16384 + kk * 32), idesc_u8s8(128, 128), 1);
+      mma_commit(bar_m);
     }
+    __syncwarp();
+    ok = ok && mbar_wait(bar_m, 1, kDevTimeoutAccum);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    // The products have read the operand tiles: K and V (f32) go over them.
+    {
+      uint32_t a0[16], a1[16];
+      tmem_ld_32x32b_x16(trow + 16 * hq, a0);
+      tmem_ld_32x32b_x16(trow + 32 + 16 * hq, a1);
+      tmem_ld_wait();
+      const float *kb_lo = wsb + H + h * 64 + 16 * hq, *kb_hi = kb_lo + 32;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        float4 lo = dequant_preset4(a0 + 4 * k, kb_lo + 4 * k, sar);
+        float4 hi = dequant_preset4(a1 + 4 * k, kb_hi + 4 * k, sar);
+        if (rope && r < n) {
+          const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)r * 32 + 16 * hq + 4 * k));
+          const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)r * 32 + 16 * hq + 4 * k));
+          rope4(lo, hi, rc, rs);
+        }
+        *f32_chunk(kf, r, 4 * hq + k) = lo;
+        *f32_chunk(kf, r, 8 + 4 * hq + k) = hi;
+      }
+      tmem_ld_32x32b_x16(trow + 64 + 16 * hq, a0);
+      tmem_ld_32x32b_x16(trow + 96 + 16 * hq, a1);
+      tmem_ld_wait();
+      const float *vb_lo = wsb + 2 * H + h * 64 + 16 * hq, *vb_hi = vb_lo + 32;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        *f32_chunk(vf, r, 4 * hq + k) = dequant_preset4(a0 + 4 * k, vb_lo + 4 * k, sar);
+        *f32_chunk(vf, r, 8 + 4 * hq + k) = dequant_preset4(a1 + 4 * k, vb_hi + 4 * k, sar);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  } else {
+    // 1. K and V by TMA; Q and the RoPE factors straight into registers.
+    if (tid == 0) {
+      *s_vfast = 1;
+      prefetch_tensormap(&mqkv);
+      mbar_init(bar_load, 1);
+      mbar_init(bar_s, 1);
+      mbar_init(bar_p, kShortThreads);
+      mbar_init(bar_o, 1);
+      fence_barrier_init();
+      mbar_arrive_expect_tx(bar_load, 4 * S::kHalf);
+  #pragma unroll
+      for (int x = 0; x < 2; x++)
+  #pragma unroll
+        for (int half = 0; half < 2; half++)
+          tma_load_2d(&mqkv, smem + x * 32768 + half * S::kHalf, bar_load, (x + 1) * H + h * 64 + half * 32, t0);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 128);
+    float qv[32];  // [0,16): dimensions 16hh.., [16,32): 32+16hh..
+    if (rr < n) {
+      const float *qrow = qkv + (size_t)(t0 + rr) * 3 * H + h * 64 + 16 * hh;
+  #pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float4 lo = __ldg(reinterpret_cast<const float4 *>(qrow + 4 * k));
+        const float4 hi = __ldg(reinterpret_cast<const float4 *>(qrow + 32 + 4 * k));
+        qv[4 * k] = lo.x, qv[4 * k + 1] = lo.y, qv[4 * k + 2] = lo.z, qv[4 * k + 3] = lo.w;
+        qv[16 + 4 * k] = hi.x, qv[17 + 4 * k] = hi.y, qv[18 + 4 * k] = hi.z, qv[19 + 4 * k] = hi.w;
+      }
+      if (rope) {
+  #pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)rr * 32 + 16 * hh + 4 * k));
+          const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)rr * 32 + 16 * hh + 4 * k));
+          const float c4[4] = {rc.x, rc.y, rc.z, rc.w}, s4[4] = {rs.x, rs.y, rs.z, rs.w};
+  #pragma unroll
+          for (int u = 0; u < 4; u++) rope1(qv[4 * k + u], qv[16 + 4 * k + u], c4[u], s4[u]);
+        }
+      }
+    } else {
+  #pragma unroll
+      for (int u = 0; u < 32; u++) qv[u] = 0.0f;
+    }
+    {
+      // Row maximum, NaN-propagating first: a row holding a NaN takes the
+      // clamped path (with the NaN-ignoring maximum, as the reference's).
+      float qmx = absmax32<true>(qv);
+      qmx = fmax_nan(qmx, __shfl_xor_sync(0xffffffffu, qmx, 1));
+      const bool qnan = qmx != qmx;
+      if (__any_sync(0xffffffffu, qnan)) {
+        qmx = absmax32<false>(qv);
+        qmx = fmaxf(qmx, __shfl_xor_sync(0xffffffffu, qmx, 1));
+      }
+      const float qs = qmx > 0.0f ? __fdiv_rn(qmx, 127.0f) : 0.0f;
+      const float qinv = qmx > 0.0f ? __fdiv_rn(1.0f, qs) : 0.0f;
+      // Byte q + 128, q = clamp(rne(x * qinv)); a row whose maximum is 0 is all
+      // 128 (attention8.go:210-220).
+      if (qmx == 0.0f) {
+  #pragma unroll
+        for (int k = 0; k < 8; k++) qw[k] = 0x80808080u;
+      } else if (!qnan && scale_is_normal(qs)) {
+  #pragma unroll
+        for (int k = 0; k < 8; k++)
+          qw[k] = quant4_fast(qv[4 * k], qv[4 * k + 1], qv[4 * k + 2], qv[4 * k + 3], f2(qinv), f2(qinv));
+      } else {
+  #pragma unroll
+        for (int k = 0; k < 8; k++) {
+          uint32_t b[4];
+  #pragma unroll
+          for (int u = 0; u < 4; u++) b[u] = quant_bits(__fmul_rn(qv[4 * k + u], qinv)) + 128u;
+          qw[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+        }
+      }
+      if (hh == 0) s_sq[rr] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
+    }
+    __syncthreads();  // barriers initialised
+    ok = mbar_wait(bar_load, 0, kDevTimeoutFull);
+
+    // A. K rotated in place (the RoPE factors are read again; they are cached).
+    if (rope && rr < n) {
+  #pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int c = 4 * hh + k;
+        const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)rr * 32 + 16 * hh + 4 * k));
+        const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)rr * 32 + 16 * hh + 4 * k));
+        float4 lo = *f32_chunk(kf, rr, c), hi = *f32_chunk(kf, rr, 8 + c);
+        rope4(lo, hi, rc, rs);
+        *f32_chunk(kf, rr, c) = lo;
+        *f32_chunk(kf, rr, 8 + c) = hi;
+      }
+    }
+    __syncthreads();
   }
-  __syncthreads();
 
   // B. Warps 0-1: K column means (ordered float32 sums over the rotated
   // keys). Warps 2-3: V column maxima; then warps 4-7 quantize V per column,
@@ -417,8 +654,8 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
   __syncthreads();  // every f32 K row has been read
   *tile_chunk(smem + S::kKt, rr, hh) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
   *tile_chunk(smem + S::kKt, rr, 2 + hh) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
-  *tile_chunk(smem + S::kQt, rr, hh) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
-  *tile_chunk(smem + S::kQt, rr, 2 + hh) = make_uint4(qw[4], qw[5], qw[6], qw[7]);
+  *tile_chunk(smem + S::kQt, qr, qh) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+  *tile_chunk(smem + S::kQt, qr, 2 + qh) = make_uint4(qw[4], qw[5], qw[6], qw[7]);
   fence_proxy_async_smem();  // the tiles are read by the tensor cores
   tc_fence_before();
   __syncthreads();
@@ -612,29 +849,66 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
 }
 
 // The 16-byte row loads and stores need H a multiple of 4 and 16-byte
-// aligned qkv and ctx.
+// aligned qkv and ctx (the fused projection reads no qkv).
 bool attn_short_fits(const AttnArgs &a) {
-  return a.D == 64 && a.max_len <= kShortN && (a.H % 4) == 0 && a.V >= 1 &&
-         (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.ctx) & 15) == 0;
+  if (a.D != 64 || a.max_len > kShortN || (a.H % 4) != 0 || a.V < 1) return false;
+  if (a.xa) return attn_short_projects(a);
+  return (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.ctx) & 15) == 0;
+}
+
+// The fused projection: H = nh * 64 in {128, 256} (one or two 128-byte K
+// blocks; |acc - zc| < 2^22 for the preset accumulators), rows and weights
+// with 16-byte aligned pitches, ctx quantized in the kernel.
+bool attn_short_projects(const AttnArgs &a) {
+  return a.xa && a.wqkv && a.xa_s && a.wsb && a.wzc && a.D == 64 && a.max_len <= kShortN && a.V >= 1 &&
+         (a.H == 128 || a.H == 256) && a.H == a.nh * 64 && a.lda >= a.H && a.lda % 16 == 0 && a.ldw >= a.H &&
+         a.ldw % 16 == 0 && ((reinterpret_cast<uintptr_t>(a.xa) | reinterpret_cast<uintptr_t>(a.wqkv)) & 15) == 0 &&
+         ((reinterpret_cast<uintptr_t>(a.wsb) | reinterpret_cast<uintptr_t>(a.wzc)) & 15) == 0 && a.xq && a.sa &&
+         a.nh <= 8 && (a.ldq % 16) == 0 && (reinterpret_cast<uintptr_t>(a.xq) & 15) == 0;
+}
+
+static int map_u8_rows(CUtensorMap *map, const void *base, int rows, int cols, int ld, int box_rows) {
+  auto enc = get_encode_fn();
+  if (!enc) return IG_ERR_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
+  cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? 0
+             : IG_ERR_CUDA;
 }
 
 int launch_attn_short(const AttnArgs &a, cudaStream_t st) {
   if (a.nseq <= 0 || a.N <= 0) return 0;
   if (!attn_short_fits(a)) return IG_ERR_UNSUPPORTED;
-  // qkv as a [N][3H] f32 plane, copied in 32-float x 128-row SWIZZLE_128B boxes.
-  auto enc = get_encode_fn();
-  if (!enc) return IG_ERR_CUDA;
-  CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)3 * a.H, (cuuint64_t)a.N};
-  cuuint64_t strides[1] = {(cuuint64_t)3 * a.H * sizeof(float)};
-  cuuint32_t box[2] = {32, (cuuint32_t)kShortN};
-  cuuint32_t estr[2] = {1, 1};
-  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.qkv), dims, strides, box, estr,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+  const bool proj = a.xa != nullptr;
+  CUtensorMap map, mapw;
+  if (proj) {
+    // The quantized rows [N][H] in [128 rows][128 B] boxes; the QKV weights
+    // [3H][H] in [64 rows][128 B] boxes; both SWIZZLE_128B (UMMA K-major).
+    if (map_u8_rows(&map, a.xa, a.N, a.H, a.lda, 128) || map_u8_rows(&mapw, a.wqkv, 3 * a.H, a.H, a.ldw, 64))
+      return IG_ERR_CUDA;
+  } else {
+    // qkv as a [N][3H] f32 plane, copied in 32-float x 128-row SWIZZLE_128B boxes.
+    auto enc = get_encode_fn();
+    if (!enc) return IG_ERR_CUDA;
+    cuuint64_t dims[2] = {(cuuint64_t)3 * a.H, (cuuint64_t)a.N};
+    cuuint64_t strides[1] = {(cuuint64_t)3 * a.H * sizeof(float)};
+    cuuint32_t box[2] = {32, (cuuint32_t)kShortN};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.qkv), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return IG_ERR_CUDA;
+    mapw = map;
+  }
+  auto kern = proj ? attn_short_kernel<true> : attn_short_kernel<false>;
+  static SmemOptIn attr_plain, attr_proj;
+  if ((proj ? attr_proj : attr_plain).ensure((const void *)kern, AttnShortSmem::kTotal) != cudaSuccess)
     return IG_ERR_CUDA;
-  static SmemOptIn attr;
-  if (attr.ensure((const void *)attn_short_kernel, AttnShortSmem::kTotal) != cudaSuccess) return IG_ERR_CUDA;
   if (a.xq) {
     if (!attn_short_quantizes(a)) return IG_ERR_UNSUPPORTED;
     // One cluster per sequence: its nh head CTAs share the row maxima.
@@ -650,13 +924,15 @@ int launch_attn_short(const AttnArgs &a, cudaStream_t st) {
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, attn_short_kernel, map, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos,
-                           a.rope_sin, a.ctx, a.xq, a.ldq, a.sa) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, kern, map, mapw, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos,
+                           a.rope_sin, a.ctx, a.xq, a.ldq, a.sa, a.xa_s, a.wsb, a.wzc) != cudaSuccess)
       return IG_ERR_CUDA;
     return 0;
   }
-  attn_short_kernel<<<dim3(a.nseq, a.nh), kShortThreads, AttnShortSmem::kTotal, st>>>(
-      map, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos, a.rope_sin, a.ctx, nullptr, 0, nullptr);
+  if (proj) return IG_ERR_UNSUPPORTED;
+  attn_short_kernel<false><<<dim3(a.nseq, a.nh), kShortThreads, AttnShortSmem::kTotal, st>>>(
+      map, mapw, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos, a.rope_sin, a.ctx, nullptr, 0, nullptr,
+      nullptr, nullptr, nullptr);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 

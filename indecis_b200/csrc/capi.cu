@@ -780,6 +780,32 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       IG_TRY(copy_rows_d2h(dump->xq, w.xq, H, m->ldk, N, st));
       IG_TRY(copy_rows_d2h(dump->xq_s, w.sa, 4, 4, N, st));
     }
+    at.window = global ? -1 : c.local_attention / 2;
+    at.rope_cos = m->rope_cos[global ? 0 : 1];
+    at.rope_sin = m->rope_sin[global ? 0 : 1];
+    at.xq = nullptr;
+    at.sa = nullptr;
+    // Sequences of at most 128 tokens: the QKV projection runs inside the
+    // attention kernel (no float qkv in HBM) and ctx is quantized there,
+    // unless this layer is dumped.
+    AttnArgs ap = at;
+    ap.qkv = nullptr;
+    ap.xa = w.xq;
+    ap.lda = m->ldk;
+    ap.xa_s = w.sa;
+    ap.wqkv = L.qkv.q;
+    ap.ldw = L.qkv.ld;
+    ap.wsb = L.qkv.scale;
+    ap.wzc = L.qkv.zc;
+    ap.xq = w.xq;
+    ap.ldq = m->ldk;
+    ap.sa = w.sa;
+    if (!dl && qkv_fuse_enabled() && attn_short_fits(ap)) {
+      const double pairs = attn_pairs(p, ap.window);
+      ProfScope ps("attn_qkv_quant", (double)N * (H + 4) * 2 + 3.0 * H * H + 24.0 * H + 8.0 * N * 32,
+                   2.0 * N * 3 * H * H + 4.0 * pairs * m->D * m->nh, 1, st, capturing);
+      IG_TRY(launch_attn_short(ap, st));
+    } else {
     {
       GemmArgs g{w.xq, L.qkv.q, N, L.qkv.n, H, m->ldk, L.qkv.ld, 256};
       GemmEpilogue e{};
@@ -792,12 +818,7 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
       IG_TRY(gemm_u8s8(g, e, kEpiF32, st));
     }
     if (dl) IG_TRY(copy_rows_d2h(dump->qkv, w.qkv, 3 * H * 4, 3 * H * 4, N, st));
-    at.window = global ? -1 : c.local_attention / 2;
-    at.rope_cos = m->rope_cos[global ? 0 : 1];
-    at.rope_sin = m->rope_sin[global ? 0 : 1];
     // ctx quantized inside the short-sequence kernel unless this layer is dumped.
-    at.xq = nullptr;
-    at.sa = nullptr;
     bool ctx_quantized = false;
     if (attn_short_fits(at) && !dl) {
       AttnArgs aq = at;
@@ -832,6 +853,7 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
     if (!ctx_quantized) {
       ProfScope ps("quant_rows", (double)N * (5.0 * H + 4), 0, 1, st, capturing);
       IG_TRY(launch_quant_rows(w.ctx, H, N, H, w.xq, m->ldk, w.sa, st));
+    }
     }
     if (dl) {
       IG_TRY(copy_rows_d2h(dump->cq, w.xq, H, m->ldk, N, st));

@@ -83,6 +83,31 @@ def test_c1_varlen_bitexact(igdev, oracle_lib):
     assert np.array_equal(_bits(out), _bits(ref))
 
 
+@pytest.mark.parametrize("hidden,heads", [(256, 4), (128, 2)])
+def test_short_sequences_fused_projection(igdev, oracle_lib, hidden, heads):
+    """Batches whose sequences all fit 128 tokens take the attention kernel
+    that computes the QKV projection itself (one and two 128-byte K blocks),
+    and the Wi GEMM that quantizes its GeGLU rows: ragged lengths 1..128
+    (the last sequence's 128-row operand box runs past the batch), an empty
+    sequence between them, and an all-128 batch, bit for bit through the
+    pooled and per-token entry points."""
+    from indecis_b200 import synthetic as S
+    cfg = S.tiny(layers=4, hidden=hidden, heads=heads, intermediate=384, vocab=3000)
+    om, gm, _ = _models(cfg, seed=7, gamma_noise=0.1)
+    _, offs = S.ids_varlen(37, 1, 128, cfg["vocab"], seed=33)
+    lens = list(np.diff(offs))
+    lens[5] = 0
+    lens[20] = 128
+    lens[-1] = 127
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    ids = np.random.default_rng(4).integers(4, cfg["vocab"], int(offs[-1])).astype(np.int32)
+    assert np.array_equal(_bits(gm.EncodeTokens((ids, offs))), _bits(om.encode(ids, offs, mode=1, threads=8)))
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(om.encode(ids, offs, threads=8)))
+    ids2, offs2 = S.ids_fixed(9, 128, cfg["vocab"], seed=34)
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids2, offs2))), _bits(om.encode(ids2, offs2, threads=8)))
+    gm.close()
+
+
 def test_batch_composition_and_threads(tiny):
     """concurrency_test.go:12: a sequence's result is the same alone, in any
     batch, and under concurrent calls on one shared model."""
