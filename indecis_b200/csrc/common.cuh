@@ -66,6 +66,18 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint64_t *bar, uint32_t rank
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(bar)), "r"(rank));
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(a) : "memory");
 }
+// Asynchronous 4-byte store into CTA `rank`'s shared memory at the offset of
+// p, counted as 4 transaction bytes on that CTA's mbarrier at the offset of
+// bar (which the receiver arms with arrive.expect_tx): no release fence, so
+// the thread's earlier global stores are not waited for.
+__device__ __forceinline__ void st_async_f32(float *p, uint32_t rank, float v, uint64_t *bar) {
+  uint32_t a, b;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(b) : "r"(smem_u32(bar)), "r"(rank));
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(a),
+               "r"(__float_as_uint(v)), "r"(b)
+               : "memory");
+}
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

@@ -330,8 +330,9 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int
 // values (NaN-ignoring, the sign bit set when a NaN was seen: the
 // NaN-propagating maximum is NaN exactly then), the four column groups of
 // this CTA through shared memory, and the cluster's CTAs (one per 256-column
-// tile of the same 128-row block) by st.shared::cluster into every CTA's
-// exchange buffer with a cluster-scope arrive on its barrier. The TMEM
+// tile of the same 128-row block) by asynchronous stores (st.async) into
+// every CTA's exchange buffer, counted as transaction bytes on its barrier,
+// which one thread of the receiving CTA arms for the tile. The TMEM
 // accumulator is handed back as soon as the values are in registers.
 // Returns false when a wait ran out (the caller then stops waiting).
 template <int BN>
@@ -341,6 +342,9 @@ __device__ __forceinline__ bool epilogue_geglu_q(uint32_t tbase, int n0, int m0,
   constexpr int H2 = BN / 2;
   const int g0 = n0 / 2, c = g * 32;
   const int r = q * 32 + lane, row = m0 + r;
+  const int par = it & 1;
+  // One thread arms this tile's phase for every CTA's 128 row maxima.
+  if (g == 0 && q == 2 && lane == 0) mbar_arrive_expect_tx(&xfull[par], 128 * 4 * csize);
   float v[32];
 #pragma unroll
   for (int h = 0; h < 2; h++) {
@@ -370,7 +374,6 @@ __device__ __forceinline__ bool epilogue_geglu_q(uint32_t tbase, int n0, int m0,
   }
   xpart[g * 128 + r] = nan ? -m : m;  // -0.0 keeps the sign bit for a zero maximum
   named_barrier_sync(3, 512);
-  const int par = it & 1;
   if (g == 0) {
     float e = 0.0f;
     bool en = false;
@@ -382,12 +385,9 @@ __device__ __forceinline__ bool epilogue_geglu_q(uint32_t tbase, int n0, int m0,
     }
     e = en ? -e : e;
     float *slot = xbuf + (par * 8 + (int)rank) * 128 + r;
-    for (int cr = 0; cr < csize; cr++) {
-      st_dsmem_f32(slot, (uint32_t)cr, e);
-      mbar_arrive_cluster(&xfull[par], (uint32_t)cr);
-    }
+    for (int cr = 0; cr < csize; cr++) st_async_f32(slot, (uint32_t)cr, e, &xfull[par]);
   }
-  ok = ok && mbar_wait_cluster(&xfull[par], (uint32_t)(it >> 1) & 1u, kDevTimeoutAccum);
+  ok = ok && mbar_wait(&xfull[par], (uint32_t)(it >> 1) & 1u, kDevTimeoutAccum);
   float mx = 0.0f;
   bool has_nan = false;
   for (int cr = 0; cr < csize; cr++) {
@@ -462,9 +462,10 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
       mbar_init(&acce[b], PEpi<EPI>::kWarps);
     }
     if constexpr (S::kQ) {
-      // Each phase of a row-maximum exchange barrier completes when all 128
-      // rows of every CTA of the cluster (one per column tile) have arrived.
-      for (int b = 0; b < 2; b++) mbar_init(&acce[2 + b], 128 * tiles_n);
+      // Each phase of a row-maximum exchange barrier completes when this
+      // CTA has armed it and the 128 row maxima of every CTA of the cluster
+      // (one per column tile) have landed.
+      for (int b = 0; b < 2; b++) mbar_init(&acce[2 + b], 1);
       *reinterpret_cast<volatile int *>(smem + S::kXFlag) = 0;
     }
     fence_barrier_init();
@@ -634,12 +635,11 @@ static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, 
   const int ntiles = mblocks * tiles_n;
   if constexpr (S::kQ) {
     // One cluster of tiles_n CTAs per 128-row block at a time: the grid is a
-    // whole number of clusters, so CTA rank r always takes column tile r.
-    int clusters = num_sms() / tiles_n;
-    if (clusters > mblocks) clusters = mblocks;
-    if (clusters < 1) clusters = 1;
+    // whole number of clusters, so CTA rank r always takes column tile r. A
+    // persistent grid must be resident all at once: clusters of one-CTA-per-SM
+    // blocks fit the GPCs only so many times (SMs left over in a GPC take
+    // none), so the cluster count comes from the occupancy query.
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(clusters * tiles_n);
     cfg.blockDim = dim3(PEpi<EPI>::kThreads);
     cfg.dynamicSmemBytes = S::kTotal;
     cfg.stream = st;
@@ -650,6 +650,20 @@ static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, 
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
+    cfg.gridDim = dim3(tiles_n * (num_sms() / tiles_n));
+    static PerDevice resident_by_size[9];
+    const int resident = resident_by_size[tiles_n].get([&] {
+      int r = 0;
+      if (cudaOccupancyMaxActiveClusters(&r, (const void *)gemm_persist_kernel<BN, EPI>, &cfg) != cudaSuccess ||
+          r < 1) {
+        cudaGetLastError();
+        r = num_sms() / tiles_n / 2;
+      }
+      return r;
+    });
+    int clusters = resident < mblocks ? resident : mblocks;
+    if (clusters < 1) clusters = 1;
+    cfg.gridDim = dim3(clusters * tiles_n);
     return cudaLaunchKernelEx(&cfg, gemm_persist_kernel<BN, EPI>, ma, mb, mc, M, N, K, ep);
   }
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
