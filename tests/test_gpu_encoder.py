@@ -86,8 +86,8 @@ def test_c1_varlen_bitexact(igdev, oracle_lib):
 @pytest.mark.parametrize("hidden,heads", [(256, 4), (128, 2)])
 def test_short_sequences_fused_projection(igdev, oracle_lib, hidden, heads):
     """Batches whose sequences all fit 128 tokens take the attention kernel
-    that computes the QKV projection itself (one and two 128-byte K blocks),
-    and the Wi GEMM that quantizes its GeGLU rows: ragged lengths 1..128
+    that computes the QKV projection itself (one and two 128-byte K blocks):
+    ragged lengths 1..128
     (the last sequence's 128-row operand box runs past the batch), an empty
     sequence between them, and an all-128 batch, bit for bit through the
     pooled and per-token entry points."""
