@@ -160,6 +160,157 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The V column maxima of every (sequence, head) (attention8.go:255-269,
+// NaN-ignoring |maxima|: their order does not matter) over row slices: each
+// warp walks kVmRows consecutive rows, lane l holding columns l, l + 32, ...
+// of the row's V block (H / 32 of them), and flushes its maxima with
+// atomicMax on their bits (non-negative floats order as their bits) into
+// vmax[sequence][column] whenever the sequence changes and at the end. vmax
+// starts at zero.
+constexpr int kVmRows = 256;
+template <int NC>
+__global__ void __launch_bounds__(256) attn_vmax_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ row_seq,
+                                                        const int32_t *__restrict__ offs, int N, int H,
+                                                        uint32_t *__restrict__ vmax) {
+  const int wg = (int)((blockIdx.x * 256u + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  const int r0 = wg * kVmRows;
+  if (r0 >= N) return;
+  const int r1 = min(N, r0 + kVmRows);
+  float m[NC];
+#pragma unroll
+  for (int j = 0; j < NC; j++) m[j] = 0.0f;
+  int seq = __ldg(row_seq + r0);
+  auto flush = [&](int sq) {
+#pragma unroll
+    for (int j = 0; j < NC; j++)
+      if (m[j] > 0.0f) atomicMax(vmax + (size_t)sq * H + lane + 32 * j, __float_as_uint(m[j]));
+  };
+  int r = r0;
+  while (r < r1) {
+    // The rows of this slice that belong to the current sequence, four at a
+    // time (independent loads in flight).
+    const int sq = __ldg(row_seq + r);
+    if (sq != seq) {
+      flush(seq);
+#pragma unroll
+      for (int j = 0; j < NC; j++) m[j] = 0.0f;
+      seq = sq;
+    }
+    const int re = min(r1, __ldg(offs + seq + 1));
+    for (; r + 4 <= re; r += 4) {
+      const float *v = qkv + (size_t)r * 3 * H + 2 * H + lane;
+#pragma unroll
+      for (int j = 0; j < NC; j++) {
+        const float a0 = fabsf(__ldg(v + 32 * j)), a1 = fabsf(__ldg(v + 3 * H + 32 * j));
+        const float a2 = fabsf(__ldg(v + 6 * H + 32 * j)), a3 = fabsf(__ldg(v + 9 * H + 32 * j));
+        m[j] = fmaxf(fmaxf(m[j], fmaxf(a0, a1)), fmaxf(a2, a3));
+      }
+    }
+    for (; r < re; r++) {
+      const float *v = qkv + (size_t)r * 3 * H + 2 * H + lane;
+#pragma unroll
+      for (int j = 0; j < NC; j++) m[j] = fmaxf(m[j], fabsf(__ldg(v + 32 * j)));
+    }
+  }
+  flush(seq);
+}
+
+// The ordered float32 K column sums of one (sequence, head) (attention8.go:
+// 224-229: AddTo over the keys in order, then Scale by 1/float32(n)) over the
+// keys rotated at their positions, fed by TMA: per stage 64 rows of the
+// head's K slice (two [64][32 float] boxes) and, with RoPE, of the cos and
+// sin tables, STAGES stages in flight, so one CTA streams a long sequence at
+// the rate its chain consumes it. Threads 0-63 run the chains (one column
+// each), warp 2 issues the copies. Also turns the V maxima (vmax, as bits)
+// into the V scales and inverses, in place.
+constexpr int kKsRows = 64;
+constexpr int kKsStageBytes = 2 * kKsRows * 128 + 2 * kKsRows * 128;  // K halves, cos, sin
+template <int STAGES, bool ROPE>
+__global__ void __launch_bounds__(96)
+    attn_kstats_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mc,
+                       const __grid_constant__ CUtensorMap ms, const int32_t *__restrict__ offs, int H, int nh,
+                       float *__restrict__ kmean, float *__restrict__ vs, float *__restrict__ vinv) {
+  extern __shared__ __align__(1024) uint8_t ks_smem[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ks_smem) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * kKsStageBytes);
+  uint64_t *empty = full + STAGES;
+  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = offs[s], n = offs[s + 1] - t0;
+  const int nchunks = (n + kKsRows - 1) / kKsRows;
+  constexpr uint32_t kBytes = ROPE ? kKsStageBytes : 2 * kKsRows * 128;
+  if (tid == 64) {
+    for (int k = 0; k < STAGES; k++) {
+      mbar_init(&full[k], 1);
+      mbar_init(&empty[k], 2);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 2) {
+    if (tid == 64) {
+      prefetch_tensormap(&mk);
+      if (ROPE) {
+        prefetch_tensormap(&mc);
+        prefetch_tensormap(&ms);
+      }
+      for (int c = 0; c < nchunks; c++) {
+        const int k = c % STAGES;
+        if (c >= STAGES && !mbar_wait(&empty[k], ((c / STAGES) - 1) & 1, kDevTimeoutEmpty)) break;
+        uint8_t *st = smem + k * kKsStageBytes;
+        mbar_arrive_expect_tx(&full[k], kBytes);
+        tma_load_2d(&mk, st, &full[k], H + h * 64, t0 + c * kKsRows);
+        tma_load_2d(&mk, st + kKsRows * 128, &full[k], H + h * 64 + 32, t0 + c * kKsRows);
+        if (ROPE) {
+          tma_load_2d(&mc, st + 2 * kKsRows * 128, &full[k], 0, c * kKsRows);
+          tma_load_2d(&ms, st + 3 * kKsRows * 128, &full[k], 0, c * kKsRows);
+        }
+      }
+    }
+    return;
+  }
+  // Threads 0-63: column tid's chain.
+  const int i = tid & 31, half = tid >> 5, other = half ^ 1;
+  float acc = 0.0f;
+  bool ok = true;
+  for (int c = 0; c < nchunks && ok; c++) {
+    const int k = c % STAGES;
+    ok = mbar_wait(&full[k], (c / STAGES) & 1, kDevTimeoutFull);
+    if (!ok) break;
+    const float *st = reinterpret_cast<const float *>(smem + k * kKsStageBytes);
+    const float *kh = st + half * kKsRows * 32, *ko = st + other * kKsRows * 32;
+    const float *cc = st + 2 * kKsRows * 32, *sc = st + 3 * kKsRows * 32;
+    const int rows = min(kKsRows, n - c * kKsRows);
+    if (rows == kKsRows) {
+#pragma unroll 8
+      for (int r = 0; r < kKsRows; r++) {
+        float kval = kh[r * 32 + i];
+        if constexpr (ROPE) {
+          const float a = kval, b = ko[r * 32 + i], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
+          kval = half == 0 ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+        }
+        acc = __fadd_rn(acc, kval);
+      }
+    } else {
+      for (int r = 0; r < rows; r++) {
+        float kval = kh[r * 32 + i];
+        if constexpr (ROPE) {
+          const float a = kval, b = ko[r * 32 + i], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
+          kval = half == 0 ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+        }
+        acc = __fadd_rn(acc, kval);
+      }
+    }
+    __syncwarp();
+    if (i == 0) mbar_arrive(&empty[k]);
+  }
+  const size_t o = ((size_t)s * nh + h) * 64 + tid;
+  kmean[o] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
+  const float mx = __uint_as_float(reinterpret_cast<const uint32_t *>(vs)[o]);
+  const float scv = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
+  vs[o] = scv;
+  vinv[o] = mx > 0.0f ? __fdiv_rn(1.0f, scv) : 0.0f;
+}
+
 // attn_quant_kernel for D = 64 with one warp per row over all its heads: the
 // row's sequence, position and RoPE factors are read once, and successive
 // heads' loads are independent. Lane l holds dimensions l and l + 32 (a
@@ -700,6 +851,17 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// IG_ATTN_KSTATS=1 takes the split statistics pass for long sequences (V
+// maxima over row slices, then the TMA-fed K chains); by default the
+// one-kernel pass (the same bits).
+static bool kstats_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_ATTN_KSTATS");
+    return s && s[0] == '1';
+  }();
+  return on;
+}
+
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.rope_cos && a.D != 64) return IG_ERR_UNSUPPORTED;
   if (a.rope_cos && a.nseq > 0 && a.N > 0 && a.max_len <= kShortSeq && (a.H % 4) == 0) {
@@ -709,6 +871,79 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     attn_prep_short_kernel<<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.scale,
                                                                    a.rope_cos, a.rope_sin, a.vs, a.qa, a.sq, a.kq,
                                                                    a.ks, a.kzc, a.vq);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
+  if (a.nseq > 0 && a.N > 0 && a.D == 64 && a.V >= 1 && a.max_len > kShortSeq && (a.H % 32) == 0 &&
+      a.H <= 1024 && a.row_seq && !(reinterpret_cast<uintptr_t>(a.qkv) & 15) && kstats_enabled()) {
+    // Long sequences: the V column maxima over row slices (all SMs), the
+    // ordered K sums per (sequence, head) streamed by TMA, then one warp per
+    // row (all its heads) for the rotation and quantization.
+    auto enc = get_encode_fn();
+    if (!enc) return IG_ERR_CUDA;
+    CUtensorMap mk, mc, ms;
+    cuuint32_t estr[2] = {1, 1};
+    {
+      cuuint64_t dims[2] = {(cuuint64_t)3 * a.H, (cuuint64_t)a.N};
+      cuuint64_t strides[1] = {(cuuint64_t)3 * a.H * sizeof(float)};
+      cuuint32_t box[2] = {32, (cuuint32_t)kKsRows};
+      if (enc(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.qkv), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return IG_ERR_CUDA;
+    }
+    mc = mk;
+    ms = mk;
+    if (a.rope_cos) {
+      cuuint64_t dims[2] = {32, (cuuint64_t)a.max_len};
+      cuuint64_t strides[1] = {32 * sizeof(float)};
+      cuuint32_t box[2] = {32, (cuuint32_t)kKsRows};
+      if (enc(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_cos), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+          enc(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_sin), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return IG_ERR_CUDA;
+    }
+    if (cudaMemsetAsync(a.vs, 0, sizeof(float) * (size_t)a.nseq * a.H, st) != cudaSuccess) return IG_ERR_CUDA;
+    const unsigned vblocks = (unsigned)(((long long)(a.N + kVmRows - 1) / kVmRows * 32 + 255) / 256);
+    uint32_t *vbits = reinterpret_cast<uint32_t *>(a.vs);
+    switch (a.H / 32) {
+#define IG_VM(NC) \
+  case NC: attn_vmax_kernel<NC><<<vblocks, 256, 0, st>>>(a.qkv, a.row_seq, a.offs, a.N, a.H, vbits); break;
+      IG_VM(1) IG_VM(2) IG_VM(3) IG_VM(4) IG_VM(5) IG_VM(6) IG_VM(7) IG_VM(8) IG_VM(12) IG_VM(16) IG_VM(24) IG_VM(32)
+#undef IG_VM
+      default: return IG_ERR_UNSUPPORTED;
+    }
+    if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+    // Deep staging (six 32 KB stages, one CTA per SM) when few long
+    // sequences must each stream thousands of rows; two stages otherwise.
+    const bool deep = a.max_len >= 1024;
+    const int smem = (deep ? 6 : 2) * kKsStageBytes + 1024 + 256;
+    static SmemOptIn at6, at6n, at2, at2n;
+    cudaError_t e;
+    if (deep) {
+      auto kr = attn_kstats_kernel<6, true>, kn = attn_kstats_kernel<6, false>;
+      if (at6.ensure((const void *)kr, smem) != cudaSuccess || at6n.ensure((const void *)kn, smem) != cudaSuccess)
+        return IG_ERR_CUDA;
+      if (a.rope_cos)
+        kr<<<dim3(a.nseq, a.nh), 96, smem, st>>>(mk, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
+      else
+        kn<<<dim3(a.nseq, a.nh), 96, smem, st>>>(mk, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
+    } else {
+      auto kr = attn_kstats_kernel<2, true>, kn = attn_kstats_kernel<2, false>;
+      if (at2.ensure((const void *)kr, smem) != cudaSuccess || at2n.ensure((const void *)kn, smem) != cudaSuccess)
+        return IG_ERR_CUDA;
+      if (a.rope_cos)
+        kr<<<dim3(a.nseq, a.nh), 96, smem, st>>>(mk, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
+      else
+        kn<<<dim3(a.nseq, a.nh), 96, smem, st>>>(mk, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
+    }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return IG_ERR_CUDA;
+    attn_quant64_kernel<<<(unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st>>>(
+        a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq,
+        a.kq, a.ks, a.kzc, a.vq);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
   if (a.nseq > 0 && a.N > 0 && a.D == 64 && a.V >= 1 && a.max_len > kShortSeq && (a.H % 4) == 0 && a.row_seq &&

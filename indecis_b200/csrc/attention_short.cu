@@ -68,8 +68,14 @@ struct AttnShortSmem {
   static constexpr int kBar = kVinv + 256;  // 6 mbarriers
   static constexpr int kTmem = kBar + 48;   // TMEM base address; V fast-path flag at +4
   static constexpr int kXch = kTmem + 16;   // [8][128] row maxima of the cluster's CTAs (ctx quantization)
-  static constexpr int kQx = kXch + 8 * 128 * 4;  // [2][128] Q row half-maxima (fused projection)
-  static constexpr int kTotal = kQx + 2 * 128 * 4 + 1024;
+  // Fused projection: the head's 192 column scales and zero corrections
+  // (Q, K, V columns), staged once; the Q row half-maxima [2][128] use the
+  // key scale region, which is written only later.
+  static constexpr int kWsb = kXch + 8 * 128 * 4;
+  static constexpr int kWzc = kWsb + 192 * 4;
+  static constexpr int kQx = kKs;
+  static constexpr int kTotal = kWzc + 192 * 4 + 1024;
+  static_assert(kKs + 1024 <= kSq, "Q half-maxima overlap the query scales");
   // Fused projection: the operands of the Q product (A = the sequence's
   // quantized rows, [128][128 B] SWIZZLE_128B per 128-byte K block; B = the
   // head's 64 Q weight rows) and then of the K|V product (B = its 64 K and
@@ -167,11 +173,11 @@ __device__ __forceinline__ uint32_t quant4_fast_s8(float a, float b, float c, fl
 // 128 * a column sum, an integer below 2^22 in magnitude), so that after the
 // products the accumulator holds the float 1.5*2^23 + (acc - zc):
 // |acc - zc| = |sum (x_q) w| <= 128 * 127 * H < 2^22 for H <= 256.
-__device__ __forceinline__ void tmem_preset_zc16(uint32_t taddr, const float *__restrict__ zc) {
+__device__ __forceinline__ void tmem_preset_zc16(uint32_t taddr, const float *zc) {
   uint32_t v[16];
 #pragma unroll
   for (int k = 0; k < 16; k += 4) {
-    const float4 z = __ldg(reinterpret_cast<const float4 *>(zc + k));
+    const float4 z = *reinterpret_cast<const float4 *>(zc + k);
     v[k] = 2u * (uint32_t)kMagicBits - __float_as_uint(__fadd_rn(z.x, kMagic));
     v[k + 1] = 2u * (uint32_t)kMagicBits - __float_as_uint(__fadd_rn(z.y, kMagic));
     v[k + 2] = 2u * (uint32_t)kMagicBits - __float_as_uint(__fadd_rn(z.z, kMagic));
@@ -184,8 +190,8 @@ __device__ __forceinline__ void tmem_preset_zc16(uint32_t taddr, const float *__
 // tmem_preset_zc16: the subtraction of 1.5*2^23 recovers acc - zc exactly (as
 // float(acc) - zc is exact: both are integers below 2^24), then the two
 // products of the QKV GEMM's epilogue.
-__device__ __forceinline__ float4 dequant_preset4(const uint32_t *a, const float *__restrict__ sb, float sa) {
-  const float4 b = __ldg(reinterpret_cast<const float4 *>(sb));
+__device__ __forceinline__ float4 dequant_preset4(const uint32_t *a, const float *sb, float sa) {
+  const float4 b = *reinterpret_cast<const float4 *>(sb);
   float2 lo = __fadd2_rn(make_float2(__uint_as_float(a[0]), __uint_as_float(a[1])), f2(-kMagic));
   float2 hi = __fadd2_rn(make_float2(__uint_as_float(a[2]), __uint_as_float(a[3])), f2(-kMagic));
   lo = __fmul2_rn(__fmul2_rn(lo, make_float2(b.x, b.y)), f2(sa));
@@ -272,8 +278,17 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
     const uint32_t tm = *tmem_slot;
     const uint32_t trow = tm + ((uint32_t)(q4 * 32) << 16);
     const uint32_t a_base = smem_u32(smem + S::kA), b_base = smem_u32(smem + S::kB);
-    tmem_preset_zc16(trow + 16 * hq, wzc + h * 64 + 16 * hq);
-    tmem_preset_zc16(trow + 32 + 16 * hq, wzc + h * 64 + 32 + 16 * hq);
+    // The head's column scales and zero corrections: column j of part p
+    // (0 Q, 1 K, 2 V) at p * 64 + j.
+    float *s_wsb = reinterpret_cast<float *>(smem + S::kWsb), *s_wzc = reinterpret_cast<float *>(smem + S::kWzc);
+    if (tid < 192) {
+      const int col = (tid >> 6) * H + h * 64 + (tid & 63);
+      s_wsb[tid] = __ldg(wsb + col);
+      s_wzc[tid] = __ldg(wzc + col);
+    }
+    __syncthreads();
+    tmem_preset_zc16(trow + 16 * hq, s_wzc + 16 * hq);
+    tmem_preset_zc16(trow + 32 + 16 * hq, s_wzc + 32 + 16 * hq);
     tmem_st_wait();
     tc_fence_before();
     __syncthreads();
@@ -309,7 +324,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       tmem_ld_32x32b_x16(trow + 16 * hq, a0);
       tmem_ld_32x32b_x16(trow + 32 + 16 * hq, a1);
       tmem_ld_wait();
-      const float *qb_lo = wsb + h * 64 + 16 * hq, *qb_hi = qb_lo + 32;
+      const float *qb_lo = s_wsb + 16 * hq, *qb_hi = qb_lo + 32;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const float4 lo = dequant_preset4(a0 + 4 * k, qb_lo + 4 * k, sar);
@@ -367,10 +382,10 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
     }
     if (hq == 0) s_sq[r] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
     // K|V: columns 0-63 K, 64-127 V.
-    tmem_preset_zc16(trow + 16 * hq, wzc + H + h * 64 + 16 * hq);
-    tmem_preset_zc16(trow + 32 + 16 * hq, wzc + H + h * 64 + 32 + 16 * hq);
-    tmem_preset_zc16(trow + 64 + 16 * hq, wzc + 2 * H + h * 64 + 16 * hq);
-    tmem_preset_zc16(trow + 96 + 16 * hq, wzc + 2 * H + h * 64 + 32 + 16 * hq);
+    tmem_preset_zc16(trow + 16 * hq, s_wzc + 64 + 16 * hq);
+    tmem_preset_zc16(trow + 32 + 16 * hq, s_wzc + 96 + 16 * hq);
+    tmem_preset_zc16(trow + 64 + 16 * hq, s_wzc + 128 + 16 * hq);
+    tmem_preset_zc16(trow + 96 + 16 * hq, s_wzc + 160 + 16 * hq);
     tmem_st_wait();
     tc_fence_before();
     __syncthreads();
@@ -396,7 +411,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       tmem_ld_32x32b_x16(trow + 16 * hq, a0);
       tmem_ld_32x32b_x16(trow + 32 + 16 * hq, a1);
       tmem_ld_wait();
-      const float *kb_lo = wsb + H + h * 64 + 16 * hq, *kb_hi = kb_lo + 32;
+      const float *kb_lo = s_wsb + 64 + 16 * hq, *kb_hi = kb_lo + 32;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         float4 lo = dequant_preset4(a0 + 4 * k, kb_lo + 4 * k, sar);
@@ -412,7 +427,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       tmem_ld_32x32b_x16(trow + 64 + 16 * hq, a0);
       tmem_ld_32x32b_x16(trow + 96 + 16 * hq, a1);
       tmem_ld_wait();
-      const float *vb_lo = wsb + 2 * H + h * 64 + 16 * hq, *vb_hi = vb_lo + 32;
+      const float *vb_lo = s_wsb + 128 + 16 * hq, *vb_hi = vb_lo + 32;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         *f32_chunk(vf, r, 4 * hq + k) = dequant_preset4(a0 + 4 * k, vb_lo + 4 * k, sar);
