@@ -379,10 +379,12 @@ def shift(ids, offs, s0):
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch
 # per sequence, from one ncu capture of the C1 workload at 512 sequences
-# (profiles/attn_short_c1_512seq.txt, profiles/gemm_rows_c1_512seq.txt); a
+# (profiles/attn_qkv_c1_512seq.txt, profiles/attn_short_c1_512seq.txt,
+# profiles/gemm_rows_c1_512seq.txt); a
 # launch processes the whole step's sequences, so the per-launch traffic is
 # this times the sequences per step (traffic grows with the sequences).
 NCU_BYTES_PER_SEQ = {
+    "attn_qkv_quant": (21575680 + 16640) / 512,
     "attn_short": (201441536 + 38391040) / 512,
     "attn_short_quant": (201448192 + 11332864) / 512,
     "gemm_qkv": (21466368 + 145374976) / 512,
