@@ -62,20 +62,28 @@ __global__ void attn_stats_kernel(const float *__restrict__ qkv, const int32_t *
 
 // attn_stats_kernel for D = 64 with the (sequence, head) slices of K and V
 // (and, with ROPE, the rows' cos/sin factors) staged in shared memory by
-// cp.async, 32 rows per stage and three stages in flight: thread d < 64 runs
-// the ordered float32 sum of dimension d (of K rotated at each row's position
-// when ROPE), the other 192 threads the V column maxima over interleaved rows
-// (maxima combine in any order). The same values as attn_stats_kernel /
-// attn_prep_kernel, with nothing but shared-memory reads and the adds on the
-// sum's dependency chain.
-constexpr int kStRows = 32, kStStages = 3;
+// cp.async, 32 rows per stage, STAGES stages in flight. Threads 0-63 run the
+// ordered float32 sums (thread d: dimension d of K, rotated at each row's
+// position when ROPE), reading a stage whose keys the other 192 threads
+// rotated in place while the sums walked the previous stage; those threads
+// also take the V column maxima over interleaved rows (maxima combine in any
+// order). So the sums' chain holds only a shared-memory read and the add per
+// row. The same values as attn_stats_kernel / attn_prep_kernel.
+constexpr int kStRows = 32;
 constexpr int kStStageFloats = 2 * kStRows * 64 + 2 * kStRows * 32;  // K, V, cos, sin
 
-template <bool ROPE>
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_pending() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int STAGES, bool ROPE>
 __global__ void __launch_bounds__(256)
     attn_stats64_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ offs, int H, int nh,
                         const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
                         float *__restrict__ kmean, float *__restrict__ vs, float *__restrict__ vinv) {
+  static_assert(STAGES >= 3, "one stage summed, one rotated, one in flight");
   extern __shared__ __align__(16) float st_smem[];  // [stages][K 32x64, V 32x64, cos 32x32, sin 32x32]
   __shared__ float s_vmax[3][64];
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
@@ -84,10 +92,11 @@ __global__ void __launch_bounds__(256)
   const float *kbase = qkv + (size_t)t0 * ld + H + h * 64;
   const int nchunks = (n + kStRows - 1) / kStRows;
   // Stage chunk c: 32 rows x 16 float4 of K and of V (four 16-byte copies a
-  // thread), and 32 rows x 8 float4 of cos and of sin (one each).
+  // thread), and 32 rows x 8 float4 of cos and of sin (one each). Always one
+  // commit group per call (empty past the last chunk).
   auto stage = [&](int c) {
     if (c < nchunks) {
-      float *dst = st_smem + (size_t)(c % kStStages) * kStStageFloats;
+      float *dst = st_smem + (size_t)(c % STAGES) * kStStageFloats;
 #pragma unroll
       for (int e = tid; e < 2 * kStRows * 16; e += 256) {
         const int kv = e >> 9, r = (e >> 4) & 31, q4 = e & 15;
@@ -105,50 +114,51 @@ __global__ void __launch_bounds__(256)
         }
       }
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    cp_async_commit();
   };
-  for (int c = 0; c < kStStages - 1; c++) stage(c);
-  float acc = 0.0f;  // K sum (tid < 64) or V maximum (others)
+  // Threads 64-255 on chunk c: K rotated in place (pair i, i + 32 of a row by
+  // one thread, rotate_half without FMA), then the V maxima.
+  float vmax = 0.0f;
   const int vd = (tid - 64) & 63, vsub = (tid - 64) >> 6;
-  for (int c = 0; c < nchunks; c++) {
-    asm volatile("cp.async.wait_group %0;" ::"n"(kStStages - 2) : "memory");
-    __syncthreads();
-    const float *kc = st_smem + (size_t)(c % kStStages) * kStStageFloats;
-    const float *vc = kc + kStRows * 64;
-    const float *cc = kc + 2 * kStRows * 64, *sc = cc + kStRows * 32;
+  auto prep = [&](int c) {
+    if (c >= nchunks) return;
+    float *kc = st_smem + (size_t)(c % STAGES) * kStStageFloats;
+    const float *vc = kc + kStRows * 64, *cc = kc + 2 * kStRows * 64, *sc = cc + kStRows * 32;
     const int rows = min(kStRows, n - c * kStRows);
+    if constexpr (ROPE) {
+      for (int e = tid - 64; e < rows * 32; e += 192) {
+        const int r = e >> 5, i = e & 31;
+        const float x1 = kc[r * 64 + i], x2 = kc[r * 64 + i + 32], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
+        kc[r * 64 + i] = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+        kc[r * 64 + i + 32] = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
+      }
+    }
+    for (int r = vsub; r < rows; r += 3) vmax = fmaxf(vmax, fabsf(vc[r * 64 + vd]));
+  };
+  for (int c = 0; c < STAGES - 1; c++) stage(c);
+  cp_async_wait_pending<STAGES - 2>();  // chunk 0 has landed
+  __syncthreads();
+  if (tid >= 64) prep(0);
+  float acc = 0.0f;  // K sum (tid < 64)
+  for (int c = 0; c < nchunks; c++) {
+    cp_async_wait_pending<STAGES - 3>();  // chunk c + 1 has landed
+    __syncthreads();  // chunk c rotated, chunk c - 1's slot free
+    stage(c + STAGES - 1);
     if (tid < 64) {
-      const int i = tid & 31;
+      const float *kc = st_smem + (size_t)(c % STAGES) * kStStageFloats + tid;
+      const int rows = min(kStRows, n - c * kStRows);
       if (rows == kStRows) {
-#pragma unroll 8
-        for (int r = 0; r < kStRows; r++) {
-          float kval = kc[r * 64 + tid];
-          if constexpr (ROPE) {
-            const float a = kval, b = kc[r * 64 + (tid ^ 32)], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
-            kval = tid < 32 ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn))
-                            : __fadd_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
-          }
-          acc = __fadd_rn(acc, kval);
-        }
+#pragma unroll
+        for (int r = 0; r < kStRows; r++) acc = __fadd_rn(acc, kc[r * 64]);
       } else {
-        for (int r = 0; r < rows; r++) {
-          float kval = kc[r * 64 + tid];
-          if constexpr (ROPE) {
-            const float a = kval, b = kc[r * 64 + (tid ^ 32)], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
-            kval = tid < 32 ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn))
-                            : __fadd_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
-          }
-          acc = __fadd_rn(acc, kval);
-        }
+        for (int r = 0; r < rows; r++) acc = __fadd_rn(acc, kc[r * 64]);
       }
     } else {
-      for (int r = vsub; r < rows; r += 3) acc = fmaxf(acc, fabsf(vc[r * 64 + vd]));
+      prep(c + 1);
     }
-    __syncthreads();  // this stage is read: refill it
-    stage(c + kStStages - 1);
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  if (tid >= 64) s_vmax[vsub][vd] = acc;
+  cp_async_wait_pending<0>();
+  if (tid >= 64) s_vmax[vsub][vd] = vmax;
   __syncthreads();
   if (tid < 64) {
     const size_t o = ((size_t)s * nh + h) * 64 + tid;
@@ -158,157 +168,6 @@ __global__ void __launch_bounds__(256)
     vs[o] = scv;
     vinv[o] = mx > 0.0f ? __fdiv_rn(1.0f, scv) : 0.0f;
   }
-}
-
-// The V column maxima of every (sequence, head) (attention8.go:255-269,
-// NaN-ignoring |maxima|: their order does not matter) over row slices: each
-// warp walks kVmRows consecutive rows, lane l holding columns l, l + 32, ...
-// of the row's V block (H / 32 of them), and flushes its maxima with
-// atomicMax on their bits (non-negative floats order as their bits) into
-// vmax[sequence][column] whenever the sequence changes and at the end. vmax
-// starts at zero.
-constexpr int kVmRows = 256;
-template <int NC>
-__global__ void __launch_bounds__(256) attn_vmax_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ row_seq,
-                                                        const int32_t *__restrict__ offs, int N, int H,
-                                                        uint32_t *__restrict__ vmax) {
-  const int wg = (int)((blockIdx.x * 256u + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-  const int r0 = wg * kVmRows;
-  if (r0 >= N) return;
-  const int r1 = min(N, r0 + kVmRows);
-  float m[NC];
-#pragma unroll
-  for (int j = 0; j < NC; j++) m[j] = 0.0f;
-  int seq = __ldg(row_seq + r0);
-  auto flush = [&](int sq) {
-#pragma unroll
-    for (int j = 0; j < NC; j++)
-      if (m[j] > 0.0f) atomicMax(vmax + (size_t)sq * H + lane + 32 * j, __float_as_uint(m[j]));
-  };
-  int r = r0;
-  while (r < r1) {
-    // The rows of this slice that belong to the current sequence, four at a
-    // time (independent loads in flight).
-    const int sq = __ldg(row_seq + r);
-    if (sq != seq) {
-      flush(seq);
-#pragma unroll
-      for (int j = 0; j < NC; j++) m[j] = 0.0f;
-      seq = sq;
-    }
-    const int re = min(r1, __ldg(offs + seq + 1));
-    for (; r + 4 <= re; r += 4) {
-      const float *v = qkv + (size_t)r * 3 * H + 2 * H + lane;
-#pragma unroll
-      for (int j = 0; j < NC; j++) {
-        const float a0 = fabsf(__ldg(v + 32 * j)), a1 = fabsf(__ldg(v + 3 * H + 32 * j));
-        const float a2 = fabsf(__ldg(v + 6 * H + 32 * j)), a3 = fabsf(__ldg(v + 9 * H + 32 * j));
-        m[j] = fmaxf(fmaxf(m[j], fmaxf(a0, a1)), fmaxf(a2, a3));
-      }
-    }
-    for (; r < re; r++) {
-      const float *v = qkv + (size_t)r * 3 * H + 2 * H + lane;
-#pragma unroll
-      for (int j = 0; j < NC; j++) m[j] = fmaxf(m[j], fabsf(__ldg(v + 32 * j)));
-    }
-  }
-  flush(seq);
-}
-
-// The ordered float32 K column sums of one (sequence, head) (attention8.go:
-// 224-229: AddTo over the keys in order, then Scale by 1/float32(n)) over the
-// keys rotated at their positions, fed by TMA: per stage 64 rows of the
-// head's K slice (two [64][32 float] boxes) and, with RoPE, of the cos and
-// sin tables, STAGES stages in flight, so one CTA streams a long sequence at
-// the rate its chain consumes it. Threads 0-63 run the chains (one column
-// each), warp 2 issues the copies. Also turns the V maxima (vmax, as bits)
-// into the V scales and inverses, in place.
-constexpr int kKsRows = 64;
-constexpr int kKsStageBytes = 2 * kKsRows * 128 + 2 * kKsRows * 128;  // K halves, cos, sin
-template <int STAGES, bool ROPE>
-__global__ void __launch_bounds__(96)
-    attn_kstats_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mc,
-                       const __grid_constant__ CUtensorMap ms, const int32_t *__restrict__ offs, int H, int nh,
-                       float *__restrict__ kmean, float *__restrict__ vs, float *__restrict__ vinv) {
-  extern __shared__ __align__(1024) uint8_t ks_smem[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ks_smem) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * kKsStageBytes);
-  uint64_t *empty = full + STAGES;
-  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
-  const int t0 = offs[s], n = offs[s + 1] - t0;
-  const int nchunks = (n + kKsRows - 1) / kKsRows;
-  constexpr uint32_t kBytes = ROPE ? kKsStageBytes : 2 * kKsRows * 128;
-  if (tid == 64) {
-    for (int k = 0; k < STAGES; k++) {
-      mbar_init(&full[k], 1);
-      mbar_init(&empty[k], 2);
-    }
-    fence_barrier_init();
-  }
-  __syncthreads();
-  if (warp == 2) {
-    if (tid == 64) {
-      prefetch_tensormap(&mk);
-      if (ROPE) {
-        prefetch_tensormap(&mc);
-        prefetch_tensormap(&ms);
-      }
-      for (int c = 0; c < nchunks; c++) {
-        const int k = c % STAGES;
-        if (c >= STAGES && !mbar_wait(&empty[k], ((c / STAGES) - 1) & 1, kDevTimeoutEmpty)) break;
-        uint8_t *st = smem + k * kKsStageBytes;
-        mbar_arrive_expect_tx(&full[k], kBytes);
-        tma_load_2d(&mk, st, &full[k], H + h * 64, t0 + c * kKsRows);
-        tma_load_2d(&mk, st + kKsRows * 128, &full[k], H + h * 64 + 32, t0 + c * kKsRows);
-        if (ROPE) {
-          tma_load_2d(&mc, st + 2 * kKsRows * 128, &full[k], 0, c * kKsRows);
-          tma_load_2d(&ms, st + 3 * kKsRows * 128, &full[k], 0, c * kKsRows);
-        }
-      }
-    }
-    return;
-  }
-  // Threads 0-63: column tid's chain.
-  const int i = tid & 31, half = tid >> 5, other = half ^ 1;
-  float acc = 0.0f;
-  bool ok = true;
-  for (int c = 0; c < nchunks && ok; c++) {
-    const int k = c % STAGES;
-    ok = mbar_wait(&full[k], (c / STAGES) & 1, kDevTimeoutFull);
-    if (!ok) break;
-    const float *st = reinterpret_cast<const float *>(smem + k * kKsStageBytes);
-    const float *kh = st + half * kKsRows * 32, *ko = st + other * kKsRows * 32;
-    const float *cc = st + 2 * kKsRows * 32, *sc = st + 3 * kKsRows * 32;
-    const int rows = min(kKsRows, n - c * kKsRows);
-    if (rows == kKsRows) {
-#pragma unroll 8
-      for (int r = 0; r < kKsRows; r++) {
-        float kval = kh[r * 32 + i];
-        if constexpr (ROPE) {
-          const float a = kval, b = ko[r * 32 + i], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
-          kval = half == 0 ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
-        }
-        acc = __fadd_rn(acc, kval);
-      }
-    } else {
-      for (int r = 0; r < rows; r++) {
-        float kval = kh[r * 32 + i];
-        if constexpr (ROPE) {
-          const float a = kval, b = ko[r * 32 + i], cs = cc[r * 32 + i], sn = sc[r * 32 + i];
-          kval = half == 0 ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
-        }
-        acc = __fadd_rn(acc, kval);
-      }
-    }
-    __syncwarp();
-    if (i == 0) mbar_arrive(&empty[k]);
-  }
-  const size_t o = ((size_t)s * nh + h) * 64 + tid;
-  kmean[o] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
-  const float mx = __uint_as_float(reinterpret_cast<const uint32_t *>(vs)[o]);
-  const float scv = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
-  vs[o] = scv;
-  vinv[o] = mx > 0.0f ? __fdiv_rn(1.0f, scv) : 0.0f;
 }
 
 // attn_quant_kernel for D = 64 with one warp per row over all its heads: the
@@ -851,17 +710,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// IG_ATTN_KSTATS=1 takes the split statistics pass for long sequences (V
-// maxima over row slices, then the TMA-fed K chains); by default the
-// one-kernel pass (the same bits).
-static bool kstats_enabled() {
-  static const bool on = [] {
-    const char *s = getenv("IG_ATTN_KSTATS");
-    return s && s[0] == '1';
-  }();
-  return on;
-}
-
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.rope_cos && a.D != 64) return IG_ERR_UNSUPPORTED;
   if (a.rope_cos && a.nseq > 0 && a.N > 0 && a.max_len <= kShortSeq && (a.H % 4) == 0) {
@@ -873,94 +721,21 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
                                                                    a.ks, a.kzc, a.vq);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
-  if (a.nseq > 0 && a.N > 0 && a.D == 64 && a.V >= 1 && a.max_len > kShortSeq && (a.H % 32) == 0 &&
-      a.H <= 1024 && a.row_seq && !(reinterpret_cast<uintptr_t>(a.qkv) & 15) && kstats_enabled()) {
-    // Long sequences: the V column maxima over row slices (all SMs), the
-    // ordered K sums per (sequence, head) streamed by TMA, then one warp per
-    // row (all its heads) for the rotation and quantization.
-    auto enc = get_encode_fn();
-    if (!enc) return IG_ERR_CUDA;
-    CUtensorMap mk, mc, ms;
-    cuuint32_t estr[2] = {1, 1};
-    {
-      cuuint64_t dims[2] = {(cuuint64_t)3 * a.H, (cuuint64_t)a.N};
-      cuuint64_t strides[1] = {(cuuint64_t)3 * a.H * sizeof(float)};
-      cuuint32_t box[2] = {32, (cuuint32_t)kKsRows};
-      if (enc(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.qkv), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return IG_ERR_CUDA;
-    }
-    mc = mk;
-    ms = mk;
-    if (a.rope_cos) {
-      cuuint64_t dims[2] = {32, (cuuint64_t)a.max_len};
-      cuuint64_t strides[1] = {32 * sizeof(float)};
-      cuuint32_t box[2] = {32, (cuuint32_t)kKsRows};
-      if (enc(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_cos), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
-          enc(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_sin), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return IG_ERR_CUDA;
-    }
-    if (cudaMemsetAsync(a.vs, 0, sizeof(float) * (size_t)a.nseq * a.H, st) != cudaSuccess) return IG_ERR_CUDA;
-    const unsigned vblocks = (unsigned)(((long long)(a.N + kVmRows - 1) / kVmRows * 32 + 255) / 256);
-    uint32_t *vbits = reinterpret_cast<uint32_t *>(a.vs);
-    switch (a.H / 32) {
-#define IG_VM(NC) \
-  case NC: attn_vmax_kernel<NC><<<vblocks, 256, 0, st>>>(a.qkv, a.row_seq, a.offs, a.N, a.H, vbits); break;
-      IG_VM(1) IG_VM(2) IG_VM(3) IG_VM(4) IG_VM(5) IG_VM(6) IG_VM(7) IG_VM(8) IG_VM(12) IG_VM(16) IG_VM(24) IG_VM(32)
-#undef IG_VM
-      default: return IG_ERR_UNSUPPORTED;
-    }
-    if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
-    // Deep staging (six 32 KB stages, one CTA per SM) when few long
-    // sequences must each stream thousands of rows; two stages otherwise.
-    const bool deep = a.max_len >= 1024;
-    const int smem = (deep ? 6 : 2) * kKsStageBytes + 1024 + 256;
-    static SmemOptIn at6, at6n, at2, at2n;
-    cudaError_t e;
-    if (deep) {
-      auto kr = attn_kstats_kernel<6, true>, kn = attn_kstats_kernel<6, false>;
-      if (at6.ensure((const void *)kr, smem) != cudaSuccess || at6n.ensure((const void *)kn, smem) != cudaSuccess)
-        return IG_ERR_CUDA;
-      if (a.rope_cos)
-        kr<<<dim3(a.nseq, a.nh), 96, smem, st>>>(mk, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
-      else
-        kn<<<dim3(a.nseq, a.nh), 96, smem, st>>>(mk, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
-    } else {
-      auto kr = attn_kstats_kernel<2, true>, kn = attn_kstats_kernel<2, false>;
-      if (at2.ensure((const void *)kr, smem) != cudaSuccess || at2n.ensure((const void *)kn, smem) != cudaSuccess)
-        return IG_ERR_CUDA;
-      if (a.rope_cos)
-        kr<<<dim3(a.nseq, a.nh), 96, smem, st>>>(mk, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
-      else
-        kn<<<dim3(a.nseq, a.nh), 96, smem, st>>>(mk, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
-    }
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return IG_ERR_CUDA;
-    attn_quant64_kernel<<<(unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st>>>(
-        a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq,
-        a.kq, a.ks, a.kzc, a.vq);
-    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
-  }
   if (a.nseq > 0 && a.N > 0 && a.D == 64 && a.V >= 1 && a.max_len > kShortSeq && (a.H % 4) == 0 && a.row_seq &&
       !(reinterpret_cast<uintptr_t>(a.qkv) & 15)) {
     // Long sequences: statistics per (sequence, head), then one warp per
     // row (all its heads) for the rotation and quantization.
-    const int smem = kStStages * kStStageFloats * (int)sizeof(float);
-    static SmemOptIn attr_t, attr_f;
-    if (attr_t.ensure((const void *)attn_stats64_kernel<true>, smem) != cudaSuccess ||
-        attr_f.ensure((const void *)attn_stats64_kernel<false>, smem) != cudaSuccess)
+    // Few long sequences (one CTA per (sequence, head) streaming thousands
+    // of rows): eight stages in flight, one CTA per SM; otherwise three.
+    static SmemOptIn attr[4];
+    const bool deep = a.max_len >= 1024;
+    const int smem = (deep ? 8 : 3) * kStStageFloats * (int)sizeof(float);
+    auto kern = deep ? (a.rope_cos ? attn_stats64_kernel<8, true> : attn_stats64_kernel<8, false>)
+                     : (a.rope_cos ? attn_stats64_kernel<3, true> : attn_stats64_kernel<3, false>);
+    if (attr[(deep ? 2 : 0) + (a.rope_cos ? 1 : 0)].ensure((const void *)kern, smem) != cudaSuccess)
       return IG_ERR_CUDA;
-    if (a.rope_cos)
-      attn_stats64_kernel<true><<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, a.rope_cos,
-                                                                        a.rope_sin, a.kmean, a.vs, a.vinv);
-    else
-      attn_stats64_kernel<false><<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, nullptr, nullptr,
-                                                                         a.kmean, a.vs, a.vinv);
+    kern<<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, a.rope_cos, a.rope_sin, a.kmean, a.vs,
+                                                 a.vinv);
     if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
     attn_quant64_kernel<<<(unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st>>>(
         a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq,

@@ -168,6 +168,11 @@ __device__ __forceinline__ uint32_t quant4_fast_s8(float a, float b, float c, fl
   return quant4_fast(a, b, c, d, inv01, inv23) ^ 0x80808080u;
 }
 
+// Brings the 128-byte line holding p into L1 (no register is written).
+__device__ __forceinline__ void prefetch_l1(const float *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 // Presets 16 TMEM columns of a projection accumulator (this thread's lane) to
 // the bits 2 * 0x4B400000 - bits(zc + 1.5*2^23) = 0x4B400000 - zc (zc is
 // 128 * a column sum, an integer below 2^22 in magnitude), so that after the
@@ -314,10 +319,17 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       }
     }
     __syncwarp();
+    // The row's RoPE factor rows are brought into L1 while the product runs
+    // (they come from L2 and do not depend on it); read after the drain.
+    const bool rot = rope && r < n;
+    if (rot) {
+      prefetch_l1(rope_cos + (size_t)r * 32 + 16 * hq);
+      prefetch_l1(rope_sin + (size_t)r * 32 + 16 * hq);
+    }
+    const float sar = r < n ? __ldg(xa_s + t0 + r) : 0.0f;
     ok = mbar_wait(bar_m, 0, kDevTimeoutAccum);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    const float sar = r < n ? __ldg(xa_s + t0 + r) : 0.0f;
     float qv[32];
     {
       uint32_t a0[16], a1[16];
@@ -334,7 +346,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       }
     }
     if (r < n) {
-      if (rope) {
+      if (rot) {
 #pragma unroll
         for (int k = 0; k < 4; k++) {
           const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)r * 32 + 16 * hq + 4 * k));
@@ -402,6 +414,12 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       mma_commit(bar_m);
     }
     __syncwarp();
+    // K is rotated with the same factors as Q (same position and pairs):
+    // brought into L1 again while the K|V product runs.
+    if (rot) {
+      prefetch_l1(rope_cos + (size_t)r * 32 + 16 * hq);
+      prefetch_l1(rope_sin + (size_t)r * 32 + 16 * hq);
+    }
     ok = ok && mbar_wait(bar_m, 1, kDevTimeoutAccum);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
@@ -416,7 +434,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       for (int k = 0; k < 4; k++) {
         float4 lo = dequant_preset4(a0 + 4 * k, kb_lo + 4 * k, sar);
         float4 hi = dequant_preset4(a1 + 4 * k, kb_hi + 4 * k, sar);
-        if (rope && r < n) {
+        if (rot) {
           const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)r * 32 + 16 * hq + 4 * k));
           const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)r * 32 + 16 * hq + 4 * k));
           rope4(lo, hi, rc, rs);

@@ -727,7 +727,8 @@ int run_encoder_f32(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan 
   }
   if (mode != IG_MODE_TOKENS) {
     ProfScope ps("pool", (double)N * 4.0 * H + 4.0 * p.nseq * H, 0, 1, st, capturing);
-    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st));
+    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st,
+                       p.max_len, (int)p.N));
   }
   return 0;
 }
@@ -941,7 +942,8 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
   }
   if (mode != IG_MODE_TOKENS) {
     ProfScope ps("pool", (double)N * 4.0 * H + 4.0 * p.nseq * H, 0, 1, st, capturing);
-    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st));
+    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st,
+                       p.max_len, (int)p.N));
   }
   return 0;
 }
@@ -1184,7 +1186,8 @@ int run_tail_staged(ig_model *m, Workspace &w, const Plan &p, int mode, cudaStre
   }
   if (mode != IG_MODE_TOKENS) {
     ProfScope pr("pool", (double)N * 4.0 * H + 4.0 * p.nseq * H, 0, 1, st);
-    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st));
+    IG_TRY(launch_pool(w.xn, w.offs, p.nseq, H, mode == IG_MODE_POOLED && c.pooling == IG_POOL_CLS, w.pooled, st,
+                       p.max_len, (int)p.N));
   }
   if (logits && p.nseq && pl) {
     size_t po = 0;

@@ -97,7 +97,10 @@ int launch_quant_rows(const float *x, int ldx, int M, int K, uint8_t *q, int ldq
 // Row -> sequence and position within it of every row of a batch, from its
 // int32 offsets (one CTA per sequence).
 int launch_fill_rows(const int32_t *offs, int nseq, int32_t *row_seq, int32_t *pos, cudaStream_t st);
-int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, float *out, cudaStream_t st);
+// max_len, nrows: the batch's longest sequence and total rows (long
+// sequences take the TMA-streamed kernel).
+int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, float *out, cudaStream_t st,
+                int max_len, int nrows);
 // Head logits in float64: z[t][r] = sum_i w[r][i] x[t][i] + b[r] (heads.go:62-74).
 int launch_head_logits(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z,
                        int ldz, cudaStream_t st);

@@ -157,6 +157,60 @@ __global__ void pool_kernel(const float *__restrict__ xn, const int32_t *__restr
   }
 }
 
+// pool_kernel's mean for long sequences: the sequence's rows streamed by TMA
+// (per stage 64 rows x 32 columns, kPlStages stages in flight) so that one
+// CTA per (sequence, 32 columns) reads at the rate its float64 chains
+// consume; lane d of warp 0 runs column d's chain in token order (the same
+// additions as pool_kernel), warp 1 issues the copies.
+constexpr int kPlRows = 64, kPlStages = 8;
+__global__ void __launch_bounds__(64) pool_long_kernel(const __grid_constant__ CUtensorMap mx,
+                                                       const int32_t *__restrict__ offs, int H,
+                                                       float *__restrict__ out) {
+  extern __shared__ __align__(128) uint8_t pl_smem[];
+  float *stages = reinterpret_cast<float *>(pl_smem);
+  uint64_t *full = reinterpret_cast<uint64_t *>(pl_smem + kPlStages * kPlRows * 128);
+  uint64_t *empty = full + kPlStages;
+  const int s = blockIdx.x, c0 = blockIdx.y * 32, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t0 = offs[s], n = offs[s + 1] - t0;
+  const int nchunks = (n + kPlRows - 1) / kPlRows;
+  if (threadIdx.x == 32) {
+    for (int k = 0; k < kPlStages; k++) {
+      mbar_init(&full[k], 1);
+      mbar_init(&empty[k], 1);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) {
+      prefetch_tensormap(&mx);
+      for (int c = 0; c < nchunks; c++) {
+        const int k = c % kPlStages;
+        if (c >= kPlStages && !mbar_wait(&empty[k], ((c / kPlStages) - 1) & 1, kDevTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&full[k], kPlRows * 128);
+        tma_load_2d(&mx, stages + k * kPlRows * 32, &full[k], c0, t0 + c * kPlRows);
+      }
+    }
+    return;
+  }
+  double acc = 0.0;
+  for (int c = 0; c < nchunks; c++) {
+    const int k = c % kPlStages;
+    if (!mbar_wait(&full[k], (c / kPlStages) & 1, kDevTimeoutFull)) break;
+    const float *st = stages + k * kPlRows * 32 + lane;
+    const int rows = min(kPlRows, n - c * kPlRows);
+    if (rows == kPlRows) {
+#pragma unroll 16
+      for (int r = 0; r < kPlRows; r++) acc = __dadd_rn(acc, (double)st[r * 32]);
+    } else {
+      for (int r = 0; r < rows; r++) acc = __dadd_rn(acc, (double)st[r * 32]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[k]);
+  }
+  out[(size_t)s * H + c0 + lane] = n > 0 ? __double2float_rn(__ddiv_rn(acc, (double)n)) : 0.0f;
+}
+
 __global__ void head_logits_kernel(const float *__restrict__ w, const float *__restrict__ b, int rows, int H,
                                    const float *__restrict__ x, int nx, double *__restrict__ z, int ldz) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -318,8 +372,28 @@ int launch_fill_rows(const int32_t *offs, int nseq, int32_t *row_seq, int32_t *p
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 
-int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, float *out, cudaStream_t st) {
+int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, float *out, cudaStream_t st,
+                int max_len, int nrows) {
   if (nseq <= 0) return 0;
+  if (!cls && max_len >= 1024 && H % 32 == 0 && nrows > 0 && !(reinterpret_cast<uintptr_t>(xn) & 15)) {
+    // Long sequences: a CTA per (sequence, 32 columns), rows streamed by TMA.
+    auto enc = get_encode_fn();
+    if (!enc) return IG_ERR_CUDA;
+    CUtensorMap map;
+    cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)nrows};
+    cuuint64_t strides[1] = {(cuuint64_t)H * sizeof(float)};
+    cuuint32_t box[2] = {32, (cuuint32_t)kPlRows};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(xn), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return IG_ERR_CUDA;
+    const int smem = kPlStages * kPlRows * 128 + 16 * kPlStages;
+    static SmemOptIn attr;
+    if (attr.ensure((const void *)pool_long_kernel, smem) != cudaSuccess) return IG_ERR_CUDA;
+    pool_long_kernel<<<dim3(nseq, H / 32), 64, smem, st>>>(map, offs, H, out);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
   pool_kernel<<<nseq, 256, 0, st>>>(xn, offs, H, cls, out);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
