@@ -145,6 +145,117 @@ __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, c
   ln8_row_finish<NB>(v, GammaLdg{gamma + k}, beta, r, k, row, rv, eps, xout, q, ldq, sa, s_q[warp][r]);
 }
 
+// ln8_kernel for wide rows (H = 8 NB, NB even), with each lane chain held by
+// two threads: lane (r, hf, k) of the warp (two rows a warp, sixteen lanes a
+// row) holds x[k + 8b] for b in [hf NB/2, (hf + 1) NB/2). The first half of
+// chain k is summed by its hf = 0 thread, which hands the partial sum to the
+// hf = 1 thread by a shuffle; that one adds its half in order. So every sum
+// is the reference's lane-k chain (linalg/vec_simd.go:281-327), while a
+// thread holds half as many values as in ln8_kernel: at H = 768 that is 48
+// registers of row data instead of 96, and three times the warps per SM.
+// The float64 combines, gamma, the maximum and the bytes follow
+// ln8_row_finish.
+template <int NB>
+__global__ void __launch_bounds__(256) ln8h_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
+                                                   int M, double eps, float *__restrict__ xout,
+                                                   uint8_t *__restrict__ q, int ldq, float *__restrict__ sa) {
+  static_assert(NB % 2 == 0, "even chain length");
+  constexpr int H = 8 * NB, NH = NB / 2;
+  constexpr int QP = H + 8;
+  __shared__ __align__(16) uint8_t s_q[8][2][QP];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 4, hf = (lane >> 3) & 1, k = lane & 7;
+  const int row = (blockIdx.x * 8 + warp) * 2 + r;
+  const bool rv = row < M;
+  const int b0 = hf * NH;
+  float v[NH];
+  {
+    const float *src = x + (size_t)(rv ? row : 0) * H + k + 8 * b0;
+#pragma unroll
+    for (int b = 0; b < NH; b++) v[b] = rv ? __ldg(src + 8 * b) : 0.0f;
+  }
+  const unsigned full = 0xffffffffu;
+  // Lane sums: chain k over b = 0 .. NB-1, its two halves in turn.
+  float ls = 0.0f;
+  if (hf == 0) {
+#pragma unroll
+    for (int b = 0; b < NH; b++) ls = __fadd_rn(ls, v[b]);
+  }
+  const float ls_first = __shfl_sync(full, ls, lane ^ 8);
+  if (hf == 1) {
+    ls = ls_first;
+#pragma unroll
+    for (int b = 0; b < NH; b++) ls = __fadd_rn(ls, v[b]);
+  }
+  double sum = 0.0;
+#pragma unroll
+  for (int kk = 0; kk < 8; kk++) sum = __dadd_rn(sum, (double)__shfl_sync(full, ls, (r << 4) | 8 | kk));
+  const float mean = __double2float_rn(__ddiv_rn(sum, (double)H));
+#pragma unroll
+  for (int b = 0; b < NH; b++) v[b] = __fsub_rn(v[b], mean);
+  float lq = 0.0f;
+  if (hf == 0) {
+#pragma unroll
+    for (int b = 0; b < NH; b++) lq = __fmaf_rn(v[b], v[b], lq);
+  }
+  const float lq_first = __shfl_sync(full, lq, lane ^ 8);
+  if (hf == 1) {
+    lq = lq_first;
+#pragma unroll
+    for (int b = 0; b < NH; b++) lq = __fmaf_rn(v[b], v[b], lq);
+  }
+  double var = 0.0;
+#pragma unroll
+  for (int kk = 0; kk < 8; kk++) var = __dadd_rn(var, (double)__shfl_sync(full, lq, (r << 4) | 8 | kk));
+  const float rstd = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(var, (double)H), eps))));
+  float mx = 0.0f;  // NaN-propagating; the NaN-ignoring maximum is taken again below if needed
+#pragma unroll
+  for (int b = 0; b < NH; b++) {
+    v[b] = __fmul_rn(__fmul_rn(v[b], rstd), __ldg(gamma + k + 8 * (b0 + b)));
+    mx = fmax_nan(mx, fabsf(v[b]));
+  }
+  if (xout && rv) {
+    float *dst = xout + (size_t)row * H + k + 8 * b0;
+#pragma unroll
+    for (int b = 0; b < NH; b++) dst[8 * b] = v[b];
+  }
+  if (!q) return;
+#pragma unroll
+  for (int o = 1; o <= 8; o <<= 1) mx = fmax_nan(mx, __shfl_xor_sync(full, mx, o));
+  const bool has_nan = mx != mx;
+  if (__any_sync(full, has_nan)) {  // the maximum over the non-NaN values (rows without NaN: the same)
+    mx = 0.0f;
+#pragma unroll
+    for (int b = 0; b < NH; b++) mx = fmaxf(mx, fabsf(v[b]));
+#pragma unroll
+    for (int o = 1; o <= 8; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(full, mx, o));
+  }
+  float scale = 0.0f, inv = 0.0f;
+  if (mx > 0.0f) {
+    scale = __fdiv_rn(mx, 127.0f);
+    inv = __fdiv_rn(1.0f, scale);
+  }
+  if (k == 0 && hf == 0 && rv) sa[row] = scale;
+  uint8_t *sq = s_q[warp][r] + k + 8 * b0;
+  if (mx == 0.0f) {
+#pragma unroll
+    for (int b = 0; b < NH; b++) sq[8 * b] = 128;
+  } else if (!has_nan && row_scale_normal(scale)) {
+#pragma unroll
+    for (int b = 0; b < NH; b++) sq[8 * b] = (uint8_t)__float_as_uint(__fadd_rn(__fmul_rn(v[b], inv), kMagic + 128.0f));
+  } else {
+#pragma unroll
+    for (int b = 0; b < NH; b++) sq[8 * b] = (uint8_t)quant_byte_slow(v[b], inv);
+  }
+  __syncwarp();
+  if (rv) {
+    uint8_t *dq = q + (size_t)row * ldq;
+    const uint8_t *sr = s_q[warp][r];
+    for (int c = hf * 8 + k; c < H / 8; c += 16)
+      *reinterpret_cast<uint2 *>(dq + 8 * c) = *reinterpret_cast<const uint2 *>(sr + 8 * c);
+  }
+}
+
 // gamma[k + 8b] held in registers for the whole kernel.
 template <int NB>
 struct GammaRegs {
@@ -357,6 +468,15 @@ static int launch_head_logits_tok(const float *w, const float *b, int rows, int 
 
 // LayerNorm (+ quantization) for V = 8 and H in {64, 128, 256}; -1 when this
 // path does not apply.
+// IG_LN_SPLIT=0 keeps ln8_kernel for H = 768 (the same bits; for comparisons).
+static bool ln_split_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_LN_SPLIT");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
 template <bool EMBED>
 static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTable &emb, const float *gamma,
                       const float *beta, int M, int H, double eps, int V, float *xout, uint8_t *q, int ldq, float *sa,
@@ -378,6 +498,12 @@ static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTa
     const int groups = (M + S::kRows - 1) / S::kRows;
     const int grid = groups < 2 * sms ? groups : 2 * sms;
     ln8_staged_kernel<32><<<grid, 256, S::kTotal, st>>>(x, gamma, beta, M, eps, xout, q, ldq, sa);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
+  // Wide rows (H = 768, C4): the split-chain kernel (three times the warps
+  // per SM of ln8_kernel<96>, whose 130 registers leave one block per SM).
+  if (!EMBED && H == 768 && !beta && ln_split_enabled()) {
+    ln8h_kernel<96><<<(M + 15) / 16, 256, 0, st>>>(x, gamma, M, eps, xout, q, ldq, sa);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
   const int blocks = (M + 31) / 32;
