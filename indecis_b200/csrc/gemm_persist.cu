@@ -294,20 +294,15 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int n0, int N, int
     for (int c = g * 32; c < H2; c += 32 * kPGroups) {
       if (g0 + c >= ep.geglu_n) continue;
       uint8_t *buf = sw.begin(lane);
-      // The second half's accumulators load while the first half computes
-      // (tcgen05.wait::ld waits for every earlier load).
-      uint32_t ra[2][16], rg[2][16];
-      tmem_ld_32x32b_x16(tbase + c, ra[0]);
-      tmem_ld_32x32b_x16(tbase + H2 + c, rg[0]);
-      tmem_ld_wait();
-      tmem_ld_32x32b_x16(tbase + c + 16, ra[1]);
-      tmem_ld_32x32b_x16(tbase + H2 + c + 16, rg[1]);
 #pragma unroll
       for (int h = 0; h < 2; h++) {
-        if (h == 1) tmem_ld_wait();
+        uint32_t ra[16], rg[16];
+        tmem_ld_32x32b_x16(tbase + c + 16 * h, ra);
+        tmem_ld_32x32b_x16(tbase + H2 + c + 16 * h, rg);
+        tmem_ld_wait();
         float a[16], gt[16];
-        dequant16(ra[h], ep.sb, ep.zc, n0 + c + 16 * h, N, sa, a);
-        dequant16(rg[h], ep.sb, ep.zc, n0 + H2 + c + 16 * h, N, sa, gt);
+        dequant16(ra, ep.sb, ep.zc, n0 + c + 16 * h, N, sa, a);
+        dequant16(rg, ep.sb, ep.zc, n0 + H2 + c + 16 * h, N, sa, gt);
         const int i0 = g0 + c + 16 * h;  // GeGLU column of a[0]
         if (i0 + 16 <= (ep.geglu_n & ~15)) {
 #pragma unroll
