@@ -276,12 +276,37 @@ static cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, int M
 static int gemm_persist_try(const GemmArgs &g, const GemmEpilogue &ep, int epi, int bn, const CUtensorMap &ma,
                             const CUtensorMap &mb, cudaStream_t st);
 
+// IG_GEMM_SMALL_TILES=0 keeps 256-column tiles for small products (the same
+// bits; for comparisons).
+static bool small_m_tiles_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_GEMM_SMALL_TILES");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
+static int sm_count() {
+  static PerDevice sms;
+  return sms.get([] {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+  });
+}
+
 int gemm_u8s8(const GemmArgs &g, const GemmEpilogue &ep, int epi, cudaStream_t st) {
   if (g.M <= 0 || g.N <= 0) return 0;
   if (g.K <= 0 || (g.lda % 16) || (g.ldb % 16) || g.lda < g.K || g.ldb < g.K) return IG_ERR_BAD_ARG;
   if ((reinterpret_cast<uintptr_t>(g.A) | reinterpret_cast<uintptr_t>(g.B)) & 15) return IG_ERR_BAD_ARG;
   int bn = g.bn;
   if (bn != 128 && bn != 256) bn = g.N > 128 ? 256 : 128;
+  // Small products (a batch of a few thousand rows): 128-column tiles when
+  // 256-column ones would leave SMs without a tile, so every SM shares the
+  // epilogue work that bounds such launches.
+  if (bn == 256 && small_m_tiles_enabled() && (long long)((g.M + kBM - 1) / kBM) * ((g.N + 255) / 256) < sm_count())
+    bn = 128;
   if (epi == kEpiGeglu || epi == kEpiGegluQ) bn = 256;
   CUtensorMap ma, mb;
   if (make_map_u8(&ma, g.A, g.M, g.K, g.lda, kBM) || make_map_u8(&mb, g.B, g.N, g.K, g.ldb, bn))
