@@ -460,15 +460,47 @@ def gemm_point(M, N, K, pk, flush, reps=10):
             "bound": "tensor" if bound >= int8_peak else "hbm", "out": "f32"}
 
 
+def int8_dense_probe(reps=10):
+    """The library's own tcgen05 int8 product on a shape bound by the tensor
+    cores (M = N = 8192, K = 8192, int32 out: 1.1 TOP against 0.4 GB of
+    traffic), median of reps launches with CUDA events: a measured int8
+    dense rate to set beside 2 x the bf16 burst."""
+    import torch
+    from indecis_b200 import ops
+    M = N = K = 8192
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.randint(1, 256, (M, K), dtype=torch.uint8, device="cuda", generator=g)
+    B = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g)
+    for _ in range(3):
+        ops.gemm_u8s8(A, B, int32_out=True)
+    st = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    torch.cuda.synchronize()
+    for e0, e1 in ev:
+        e0.record(st)
+        ops.gemm_u8s8(A, B, int32_out=True)
+        e1.record(st)
+    torch.cuda.synchronize()
+    ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in ev)
+    del A, B
+    torch.cuda.empty_cache()
+    return {"M": M, "N": N, "K": K, "us": round(ms * 1e3, 1), "tops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
+            "kernel": "library GEMM (tcgen05 kind::i8, CTA pair for K >= 1024), int32 out"}
+
+
 def gemm_sweep(pk):
     """Config 2: M in {128, 4096, 65536} x (N, K) in its four shapes."""
     import torch
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # 256 MiB > the 126 MB L2
     pts = [gemm_point(M, N, K, pk, flush) for M in C2_ROWS for N, K in C2_SHAPES]
     del flush
+    probe = int8_dense_probe()
+    for p in pts:
+        p["frac_of_measured_int8"] = round(p["tops"] / probe["tops"], 4)
     return {"points": pts, "timing": "median of 10 reps, each after an L2 flush (256 MiB write), CUDA events; all reps "
                                       "queued behind a device sleep, so host launch time is not timed",
-            "int8_peak_tops": 2.0 * pk["bf16"], "int8_peak_source": "2 x measured bf16 burst (no int8 entry)"}
+            "int8_peak_tops": 2.0 * pk["bf16"], "int8_peak_source": "2 x measured bf16 burst (no int8 entry)",
+            "int8_dense_measured": probe}
 
 
 def dist_init(world, local):
