@@ -192,7 +192,7 @@ __device__ __forceinline__ uint4 chunk_p(uint32_t tcol, int c, const float *zcm,
 // as in chunk_p, and P = rne(exp32(score - mx) * 255) replaces the byte the
 // chunk pass wrote into P ([128 rows][128 B] SWIZZLE_128B per 128 keys).
 // Returns the change of the row's P sum.
-__device__ __noinline__ int tail_fixup(const uint8_t *qtile, const uint8_t *ktile, int ktile_bytes, uint8_t *ptile,
+__device__ __forceinline__ int tail_fixup(const uint8_t *qtile, const uint8_t *ktile, int ktile_bytes, uint8_t *ptile,
                                        int r, int g, int t0, int t1, const float *zcm, const float *ks, float sq,
                                        float mx) {
   int dsum = 0;  // change of the row's P sum
