@@ -104,17 +104,18 @@ __device__ __forceinline__ float2 score2(uint32_t a0, uint32_t a1, float2 zcm, f
 // MaxOf over the valid columns of the 16-key chunk at TMEM column tcol.
 // PRE: the maximum of (acc - zc) * ks, before the row's sq (x -> x * sq is
 // non-decreasing for sq >= 0, so the row maximum is that maximum times sq).
-template <bool PRE>
+// MASK: some column of the chunk may lie outside a row's [a, b) (false when
+// every lane's row takes all 16: no per-column tests).
+template <bool PRE, bool MASK>
 __device__ __forceinline__ float chunk_max_acc(const uint32_t (&acc)[16], int c, const float *zcm, const float *ks,
                                                const ScoreRow &w, float mx) {
-  const bool inner = __all_sync(0xffffffffu, c >= w.a && c + 16 <= w.b);
 #pragma unroll
   for (int v = 0; v < 16; v += 4) {
     const float4 z = PRE ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : *reinterpret_cast<const float4 *>(zcm + c + v);
     const float4 k = *reinterpret_cast<const float4 *>(ks + c + v);
     const float2 s0 = score2<PRE>(acc[v], acc[v + 1], make_float2(z.x, z.y), make_float2(k.x, k.y), w.sq, false);
     const float2 s1 = score2<PRE>(acc[v + 2], acc[v + 3], make_float2(z.z, z.w), make_float2(k.z, k.w), w.sq, false);
-    if (inner) {
+    if (!MASK) {
       mx = fmaxf(mx, fmaxf(fmaxf(s0.x, s0.y), fmaxf(s1.x, s1.y)));
     } else {
       const int col = c + v;
@@ -131,13 +132,12 @@ __device__ __forceinline__ float chunk_max_acc(const uint32_t (&acc)[16], int c,
 // chunk at TMEM column tcol as 16 bytes (0 outside the row's valid keys), all
 // with ExpShift's vector-body exp (tail_fixup then rewrites the row's
 // scalar-tail keys); the sum of the 16 is added to psum. The subtraction is
-// scalar: a packed add after the packed product of dequant2m could be fused
-// into one rounding.
-template <bool PRE>
+// scalar: a packed add after the packed product of dequant2m (or score2) is
+// contracted with it into one rounding (a packed add here changed bits).
+template <bool PRE, bool MASK>
 __device__ __forceinline__ uint4 chunk_p_acc(const uint32_t (&acc)[16], int c, const float *zcm, const float *ks,
                                             const ScoreRow &w, float mx, int &psum) {
   uint32_t bits[16];  // 0x4B400000 + P (low byte P)
-  const bool inner = __all_sync(0xffffffffu, c >= w.a && c + 16 <= w.b);
 #pragma unroll
   for (int v = 0; v < 16; v += 4) {
     const float4 z = PRE ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : *reinterpret_cast<const float4 *>(zcm + c + v);
@@ -149,7 +149,7 @@ __device__ __forceinline__ uint4 chunk_p_acc(const uint32_t (&acc)[16], int c, c
       const uint2 b = exp_p_bits2(make_float2(__fsub_rn(sc.x, mx), __fsub_rn(sc.y, mx)));
       bits[v + h] = b.x;
       bits[v + h + 1] = b.y;
-      if (!inner) {
+      if (MASK) {
         const int col = c + v + h;
         if (!(col >= w.a && col < w.b)) bits[v + h] = (uint32_t)kMagicBits;
         if (!(col + 1 >= w.a && col + 1 < w.b)) bits[v + h + 1] = (uint32_t)kMagicBits;
@@ -166,13 +166,19 @@ __device__ __forceinline__ uint4 chunk_p_acc(const uint32_t (&acc)[16], int c, c
   return make_uint4(word[0], word[1], word[2], word[3]);
 }
 
+// Whether every row of the warp takes all 16 keys of the chunk at column c.
+__device__ __forceinline__ bool chunk_inner(int c, const ScoreRow &w) {
+  return __all_sync(0xffffffffu, c >= w.a && c + 16 <= w.b);
+}
+
 template <bool PRE>
 __device__ __forceinline__ float chunk_max(uint32_t tcol, int c, const float *zcm, const float *ks,
                                            const ScoreRow &w, float mx) {
   uint32_t acc[16];
   tmem_ld_32x32b_x16(tcol, acc);
   tmem_ld_wait();
-  return chunk_max_acc<PRE>(acc, c, zcm, ks, w, mx);
+  if (chunk_inner(c, w)) return chunk_max_acc<PRE, false>(acc, c, zcm, ks, w, mx);
+  return chunk_max_acc<PRE, true>(acc, c, zcm, ks, w, mx);
 }
 
 template <bool PRE>
@@ -181,7 +187,8 @@ __device__ __forceinline__ uint4 chunk_p(uint32_t tcol, int c, const float *zcm,
   uint32_t acc[16];
   tmem_ld_32x32b_x16(tcol, acc);
   tmem_ld_wait();
-  return chunk_p_acc<PRE>(acc, c, zcm, ks, w, mx, psum);
+  if (chunk_inner(c, w)) return chunk_p_acc<PRE, false>(acc, c, zcm, ks, w, mx, psum);
+  return chunk_p_acc<PRE, true>(acc, c, zcm, ks, w, mx, psum);
 }
 
 // ExpShift's scalar-tail keys [t0, t1) of query row r (its last len % V
@@ -422,15 +429,20 @@ __global__ void __launch_bounds__(kAtThreads, 2)
 //              previous S), O += P.V per pass-2 step; commits release the
 //              ring stages and the P buffers.
 //   warps 2-9  as attn_tc_kernel, per tile; P double-buffered in shared memory.
+//              After reading a 16-key chunk of S they write the next tile's
+//              accumulator presets (0x4B400000 - zc) into it, so the scores
+//              come out of TMEM as 1.5*2^23 + (acc - zc) and each needs one
+//              subtraction instead of an integer add and a subtraction.
 constexpr int kAlStages = 3;
 
 struct AttnLongSmem {
   static constexpr int kQ = 0;                             // [128][64 B] SW64
   static constexpr int kKV = 8192;                         // kAlStages x (K, V) [128][64 B] SW64
   static constexpr int kP = kKV + kAlStages * 16384;       // 2 x [128][128 B] SW128 (1024-aligned)
-  static constexpr int kKs = kP + 32768;                   // 2 slots x 128 key scales
-  static constexpr int kKzc = kKs + 1024;                  // 2 slots x 128 (kzc + 1.5*2^23)
-  static constexpr int kRed = kKzc + 1024;                 // [2][128] row maxima, then [2][128] P sums
+  static constexpr int kKs = kP + 32768;                   // 3 slots x 128 key scales
+  static constexpr int kKzc = kKs + 1536;                  // 3 slots x 128 (kzc + 1.5*2^23)
+  static constexpr int kKpre = kKzc + 1536;                // 3 slots x 128 S presets 0x4B400000 - kzc
+  static constexpr int kRed = kKpre + 1536;                // [2][128] row maxima, then [2][128] P sums
   static constexpr int kBar = kRed + 2048;                 // 13 mbarriers
   static constexpr int kTmem = kBar + 128;
   static constexpr int kTotal = 100 * 1024;
@@ -521,13 +533,13 @@ __global__ void __launch_bounds__(kAtThreads, 2)
         const bool pass2 = j >= nkt;
         const int kt = pass2 ? j - nkt : j;
         ok = mbar_wait(&kfull[st], ph, kDevTimeoutFull);
-        if (ok && j > 0) ok = mbar_wait(sfree, (uint32_t)(j - 1) & 1, kDevTimeoutEmpty);
+        if (ok) ok = mbar_wait(sfree, (uint32_t)j & 1, kDevTimeoutEmpty);  // S read, next presets in
         if (!ok) break;
         tc_fence_after();
         const uint32_t k_base = smem_u32(smem + S::kKV + st * 16384);
 #pragma unroll
-        for (int kk = 0; kk < 2; kk++)
-          mma_u8s8(tmem, smem_desc_k_sw64(q_base + kk * 32), smem_desc_k_sw64(k_base + kk * 32), idesc_s, kk);
+        for (int kk = 0; kk < 2; kk++)  // onto the presets
+          mma_u8s8(tmem, smem_desc_k_sw64(q_base + kk * 32), smem_desc_k_sw64(k_base + kk * 32), idesc_s, 1);
         mma_commit(sfull);
         if (pass2) {
           const int pb = kt & 1;
@@ -561,26 +573,70 @@ __global__ void __launch_bounds__(kAtThreads, 2)
     const int body_end = js + (len / V) * V;  // ExpShift: vector body before, exp32 tail after
     const float sqr = valid ? sq[prow + i] : 0.0f;
     float *red = reinterpret_cast<float *>(smem + S::kRed);
+    float *ks_slots = reinterpret_cast<float *>(smem + S::kKs);
+    float *zcm_slots = reinterpret_cast<float *>(smem + S::kKzc);
+    uint32_t *pre_slots = reinterpret_cast<uint32_t *>(smem + S::kKpre);
+    // Step j's key terms live in slot j % 3: slot j + 1 is written at the top
+    // of step j while other threads may still read slot j - 1 in step j - 1.
+    // This thread's key scale (tid < 128) or zero correction of step j's
+    // tile, fetched one step ahead so that no step waits on the global load.
+    auto key_term = [&](int j) {
+      const int kt = j >= nkt ? j - nkt : j;
+      const int key = c0 + kt * kAtKT + (tid & 127);
+      if (tid < 128) return key < n ? ks[prow + key] : 0.0f;
+      return key < n ? kzc[prow + key] : 0.0f;
+    };
+    auto put_term = [&](int j, float v) {
+      const int o = (j % 3) * 128 + (tid & 127);
+      if (tid < 128) {
+        ks_slots[o] = v;
+      } else {
+        const float zm = __fadd_rn(v, kMagic);  // zc + 1.5*2^23 for tail_fixup
+        zcm_slots[o] = zm;
+        pre_slots[o] = 2u * (uint32_t)kMagicBits - __float_as_uint(zm);  // 0x4B400000 - zc
+      }
+    };
+    // Every row's score accumulator of key c starts at 0x4B400000 - zc_c, so
+    // that after the MMA it holds the float 1.5*2^23 + (acc - zc) (chunk_max
+    // and chunk_p with PRE). The softmax warps write the next tile's presets
+    // into each 16-key chunk right after reading it.
+    auto preset_chunk = [&](int ch, const uint32_t *pre) {
+      uint32_t v[16];
+#pragma unroll
+      for (int k = 0; k < 16; k += 4) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(pre + ch * 16 + k);
+        v[k] = u.x, v[k + 1] = u.y, v[k + 2] = u.z, v[k + 3] = u.w;
+      }
+      tmem_st_32x32b_x16(tbase + ch * 16, v);
+    };
+    auto release_s = [&]() {  // S read (and the next tile preset) by this warp
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sfree);
+    };
+    put_term(0, key_term(0));
+    float next_term = steps > 1 ? key_term(1) : 0.0f;
+    named_barrier_sync(1, 32 * kAtSoftWarps);
+    for (int ch = g; ch < kAtKT / 16; ch += 2) preset_chunk(ch, pre_slots);
+    release_s();  // sfree phase 0: the first tile's presets
     bool ok = mbar_wait(qfull, 0, kDevTimeoutFull);  // Q in shared memory for tail_fixup
-    float mx = -INFINITY;
+    float mx = -INFINITY;  // pass 1: of (acc - zc) * ks; times sq at its end
     int psum = 0;
     for (int j = 0; j < steps; j++) {
       const bool pass2 = j >= nkt;
       const int kt = pass2 ? j - nkt : j;
       const int st = j % kAlStages;
       const int tb = c0 + kt * kAtKT;  // first key of the tile
-      // The tile's key scales into slot j & 1 (every softmax warp is past tile
-      // j - 1 once all have reached the barrier below).
-      float *s_ks = reinterpret_cast<float *>(smem + S::kKs) + (j & 1) * 128;
-      float *s_kzc = reinterpret_cast<float *>(smem + S::kKzc) + (j & 1) * 128;
-      {
-        const int c = tid & 127, key = tb + c;
-        if (tid < 128)
-          s_ks[c] = key < n ? ks[prow + key] : 0.0f;
-        else
-          s_kzc[c] = __fadd_rn(key < n ? kzc[prow + key] : 0.0f, kMagic);
+      const bool more = j + 1 < steps;
+      if (more) {
+        put_term(j + 1, next_term);
+        if (j + 2 < steps) next_term = key_term(j + 2);
       }
       named_barrier_sync(1, 32 * kAtSoftWarps);
+      const float *s_ks = ks_slots + (j % 3) * 128;
+      const float *s_kzc = zcm_slots + (j % 3) * 128;
+      const uint32_t *pre_next = pre_slots + ((j + 1) % 3) * 128;
       ScoreRow w;
       w.a = valid ? js - tb : 1 << 30;
       w.b = valid ? je - tb : 0;
@@ -594,16 +650,15 @@ __global__ void __launch_bounds__(kAtThreads, 2)
       ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
       tc_fence_after();
       if (!pass2) {
-        if (ok)
-          for (int ch = ch0 + ((ch0 ^ g) & 1); ch < ch1; ch += 2)
-            mx = chunk_max<false>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sfree);
+        for (int ch = g; ch < kAtKT / 16; ch += 2) {
+          if (ok && ch >= ch0 && ch < ch1) mx = chunk_max<true>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx);
+          if (more) preset_chunk(ch, pre_next);
+        }
+        release_s();
         if (kt == nkt - 1) {  // the row maximum over both parities
           red[g * 128 + r] = mx;
           named_barrier_sync(1, 32 * kAtSoftWarps);
-          mx = fmaxf(red[r], red[128 + r]);
+          mx = __fmul_rn(fmaxf(red[r], red[128 + r]), w.sq);
         }
       } else {
         const int pb = kt & 1;
@@ -613,12 +668,11 @@ __global__ void __launch_bounds__(kAtThreads, 2)
         uint8_t *prow_smem = ptile + r * 128;
         for (int ch = g; ch < kAtKT / 16; ch += 2) {
           uint4 pw = make_uint4(0, 0, 0, 0);
-          if (ok && ch >= ch0 && ch < ch1) pw = chunk_p<false>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx, psum);
+          if (ok && ch >= ch0 && ch < ch1) pw = chunk_p<true>(tbase + ch * 16, ch * 16, s_kzc, s_ks, w, mx, psum);
           *reinterpret_cast<uint4 *>(prow_smem + (((ch & 7) ^ (r & 7)) << 4)) = pw;
+          if (more) preset_chunk(ch, pre_next);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sfree);
+        release_s();
         const int ta = max(w.t0, 0), tz = min(w.t1, kAtKT);
         if (ok && ta < tz)
           psum += tail_fixup(smem + S::kQ, smem + S::kKV + st * 16384, 8192, ptile, r, g, ta, tz, s_kzc, s_ks, w.sq,
@@ -689,8 +743,10 @@ int attn_tc_fits(int n, int i0, int window, int *c0_out, int *nkt_out) {
 
 int attn_tc_query_block() { return kAtQ; }
 
-int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaStream_t st) {
-  if (nblocks <= 0) return 0;
+// d_blocks: nshort blocks of at most two key tiles (attn_tc_kernel), then
+// nlong longer ones (attn_tc_long_kernel).
+int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nshort, int nlong, cudaStream_t st) {
+  if (nshort + nlong <= 0) return 0;
   if (a.D != 64) return IG_ERR_UNSUPPORTED;
   const int rows = a.nh * a.N;
   CUtensorMap mq, mk, mv;
@@ -701,14 +757,14 @@ int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaS
   if (attr_tc.ensure((const void *)attn_tc_kernel, AttnTcSmem::kTotal) != cudaSuccess ||
       attr_long.ensure((const void *)attn_tc_long_kernel, AttnLongSmem::kTotal) != cudaSuccess)
     return IG_ERR_CUDA;
-  // Blocks of at most two key tiles run in attn_tc_kernel, longer ones in
-  // attn_tc_long_kernel; each kernel returns at once on the other's blocks.
-  attn_tc_kernel<<<dim3(nblocks, a.nh), kAtThreads, AttnTcSmem::kTotal, st>>>(
-      mq, mk, mv, d_blocks, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx);
-  if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
-  if (a.max_len > 2 * kAtKT) {
-    attn_tc_long_kernel<<<dim3(nblocks, a.nh), kAtThreads, AttnLongSmem::kTotal, st>>>(
+  if (nshort > 0) {
+    attn_tc_kernel<<<dim3(nshort, a.nh), kAtThreads, AttnTcSmem::kTotal, st>>>(
         mq, mk, mv, d_blocks, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx);
+    if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+  }
+  if (nlong > 0) {
+    attn_tc_long_kernel<<<dim3(nlong, a.nh), kAtThreads, AttnLongSmem::kTotal, st>>>(
+        mq, mk, mv, d_blocks + nshort, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx);
     if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
   }
   return 0;

@@ -143,7 +143,8 @@ struct DevHead {
 struct Plan {
   int nseq = 0, N = 0, max_len = 0;
   std::vector<int32_t> offs, row_seq, pos;
-  std::vector<int4> tc[2];
+  std::vector<int4> tc[2];  // blocks of at most two key tiles first, then the longer ones, longest first
+  int tc_short[2] = {0, 0};  // how many of tc[k] have at most two key tiles
   std::vector<int2> v1[2];
   std::vector<int2> fb;  // float path: (sequence, first query) of each block of 64 queries
   size_t block_bytes() const {
@@ -155,7 +156,7 @@ struct Plan {
 struct PlanDev {
   const int4 *tc[2] = {nullptr, nullptr};
   const int2 *v1[2] = {nullptr, nullptr};
-  int ntc[2] = {0, 0}, nv1[2] = {0, 0};
+  int ntc[2] = {0, 0}, ntc_short[2] = {0, 0}, nv1[2] = {0, 0};
   const int2 *fb = nullptr;
   int nfb = 0;
 };
@@ -449,6 +450,14 @@ int make_plan(const int64_t *offs, int nseq, Plan &p, const int (&windows)[2], b
     }
   }
   p.offs[nseq] = (int32_t)N;
+  // attn_tc_kernel takes the first tc_short blocks and attn_tc_long_kernel the
+  // rest, each with a grid of its own blocks; the long ones in decreasing key
+  // tile count, so that the longest CTAs start first.
+  for (int k = 0; k < 2; k++) {
+    auto mid = std::stable_partition(p.tc[k].begin(), p.tc[k].end(), [](const int4 &b) { return b.w <= 2; });
+    p.tc_short[k] = (int)(mid - p.tc[k].begin());
+    std::stable_sort(mid, p.tc[k].end(), [](const int4 &x, const int4 &y) { return x.w > y.w; });
+  }
   return 0;
 }
 
@@ -624,6 +633,7 @@ int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream
   for (int k = 0; k < 2; k++) {
     w.pd.tc[k] = reinterpret_cast<const int4 *>(w.blocks + bo);
     w.pd.ntc[k] = (int)p.tc[k].size();
+    w.pd.ntc_short[k] = p.tc_short[k];
     bo += 16 * p.tc[k].size();
   }
   for (int k = 0; k < 2; k++) {
@@ -851,7 +861,7 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
         ProfScope ps("attn_attend", (double)N * H * 7 + 12.0 * N * m->nh, 4.0 * pairs * m->D * m->nh, 1, st,
                      capturing);
         const int kind = global ? 0 : 1;
-        IG_TRY(launch_attend_tc(at, w.pd.tc[kind], w.pd.ntc[kind], st));
+        IG_TRY(launch_attend_tc(at, w.pd.tc[kind], w.pd.ntc_short[kind], w.pd.ntc[kind] - w.pd.ntc_short[kind], st));
         IG_TRY(launch_attend(at, w.pd.v1[kind], w.pd.nv1[kind], st));
       }
     }
@@ -1838,7 +1848,7 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
       rc = launch_attn_short(a, st);
     } else {
       rc = launch_attention(a, st);
-      if (!rc) rc = launch_attend_tc(a, d_tc, (int)p.tc[0].size(), st);
+      if (!rc) rc = launch_attend_tc(a, d_tc, p.tc_short[0], (int)p.tc[0].size() - p.tc_short[0], st);
       if (!rc) rc = launch_attend(a, d_v1, (int)p.v1[0].size(), st);
     }
     if (rc) fail(rc, "ig_attention launch failed");

@@ -160,7 +160,7 @@ int attn_query_block();
 // at most 256 columns.
 int attn_tc_fits(int n, int i0, int window, int *c0_out, int *nkt_out);
 int attn_tc_query_block();
-int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nblocks, cudaStream_t st);
+int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nshort, int nlong, cudaStream_t st);
 // Prepare + attend in one kernel (attention_short.cu): D = 64, sequences of at
 // most 128 tokens, H a multiple of 4; RoPE applied when rope_cos is set.
 bool attn_short_fits(const AttnArgs &a);
