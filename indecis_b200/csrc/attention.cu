@@ -276,6 +276,159 @@ __global__ void __launch_bounds__(256, 1)
   cluster_sync_all();  // no CTA leaves while a peer may still write into it
 }
 
+// The statistics of attn_stats64_kernel with each (sequence, head) split by
+// RoPE pair over 32 / P CTAs: CTA (s, h, pg) takes the pairs i in
+// [pg P, pg P + P), dimensions i and 32 + i, over all the sequence's rows in
+// order. A dimension's ordered K sum is one chain in one thread, so no CTA
+// waits for another; the rows stream through a ring of STAGES stages of SR
+// rows, each six TMA boxes [SR rows][P floats] (K and V lower and upper
+// halves, cos, sin; no multicast).
+//   warp 0     lane 0 issues the loads.
+//   warp 1     lanes 0..2P-1: the ordered K sums, one dimension each, over
+//              the rotated keys of each stage as it comes.
+//   warps 2-5  rotate the stage's keys in place (rotate_half without FMA)
+//              and take the V column maxima of its rows (any order).
+// Per stage a full barrier (the loads), a rotated barrier (the four warps)
+// and an empty barrier (the sums); every wait is bounded.
+constexpr int kPgRotWarps = 4;
+constexpr int kPgThreads = 64 + 32 * kPgRotWarps;
+
+template <int P, int SR>
+struct PgLayout {
+  static constexpr int kBox = SR * P;          // floats per box
+  static constexpr int kPitch = kBox + 32;     // box stride (128-byte aligned starts)
+  static constexpr int kStage = 6 * kPitch;    // K lo, K hi, V lo, V hi, cos, sin
+  static int bytes(int stages) { return stages * kStage * 4 + stages * 3 * 8 + kPgRotWarps * 2 * P * 4 + 16; }
+};
+
+template <int P, int SR, int STAGES, bool ROPE>
+__global__ void __launch_bounds__(kPgThreads)
+    attn_stats_pg_kernel(const __grid_constant__ CUtensorMap mqkv, const __grid_constant__ CUtensorMap mcos,
+                         const __grid_constant__ CUtensorMap msin, const int32_t *__restrict__ offs, int H, int nh,
+                         float *__restrict__ kmean, float *__restrict__ vs, float *__restrict__ vinv) {
+  static_assert(P % 4 == 0 && 2 * P <= 32 && (32 * kPgRotWarps) % P == 0, "pair groups");
+  using L = PgLayout<P, SR>;
+  extern __shared__ __align__(128) float pg_smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(pg_smem + STAGES * L::kStage);
+  uint64_t *rotd = full + STAGES;
+  uint64_t *empty = rotd + STAGES;
+  float *vred = reinterpret_cast<float *>(empty + STAGES);  // [kPgRotWarps][2P]
+  const int s = blockIdx.x, h = blockIdx.y, pg = blockIdx.z;
+  const int t0 = offs[s], n = offs[s + 1] - t0;
+  const int nst = (n + SR - 1) / SR;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < STAGES; b++) {
+      mbar_init(&full[b], 1);
+      mbar_init(&rotd[b], kPgRotWarps);
+      mbar_init(&empty[b], 1);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&mqkv);
+      if (ROPE) {
+        prefetch_tensormap(&mcos);
+        prefetch_tensormap(&msin);
+      }
+      const int xk = H + h * 64 + pg * P, xv = 2 * H + h * 64 + pg * P;
+      for (int c = 0; c < nst; c++) {
+        const int b = c % STAGES;
+        if (c >= STAGES && !mbar_wait(&empty[b], (uint32_t)(c / STAGES - 1) & 1, kDevTimeoutEmpty)) break;
+        float *stg = pg_smem + b * L::kStage;
+        mbar_arrive_expect_tx(&full[b], (ROPE ? 6 : 4) * L::kBox * 4);
+        const int y = t0 + c * SR;
+        tma_load_2d(&mqkv, stg, &full[b], xk, y);
+        tma_load_2d(&mqkv, stg + L::kPitch, &full[b], xk + 32, y);
+        tma_load_2d(&mqkv, stg + 2 * L::kPitch, &full[b], xv, y);
+        tma_load_2d(&mqkv, stg + 3 * L::kPitch, &full[b], xv + 32, y);
+        if (ROPE) {
+          tma_load_2d(&mcos, stg + 4 * L::kPitch, &full[b], pg * P, c * SR);
+          tma_load_2d(&msin, stg + 5 * L::kPitch, &full[b], pg * P, c * SR);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // Lane l < P: dimension pg P + l (the K lower box), lane P + l:
+    // 32 + pg P + l (the upper box).
+    const bool act = lane < 2 * P;
+    const int off = lane < P ? lane : L::kPitch + lane - P;
+    float acc = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < nst; c++) {
+      const int b = c % STAGES;
+      ok = ok && mbar_wait(&rotd[b], (uint32_t)(c / STAGES) & 1, kDevTimeoutFull);
+      const float *kc = pg_smem + b * L::kStage + off;
+      const int rows = min(SR, n - c * SR);
+      if (act && ok) {
+        if (rows == SR) {
+          // Whole stage unrolled: the loads run ahead of the add chain.
+#pragma unroll
+          for (int r = 0; r < SR; r++) acc = __fadd_rn(acc, kc[r * P]);
+        } else {
+          for (int r = 0; r < rows; r++) acc = __fadd_rn(acc, kc[r * P]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[b]);
+    }
+    if (act) {
+      const int d = lane < P ? pg * P + lane : 32 + pg * P + lane - P;
+      kmean[((size_t)s * nh + h) * 64 + d] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
+    }
+  } else {
+    // Thread tr keeps pair i = tr % P over rows tr / P, + 128 / P, ...
+    constexpr int kStep = 32 * kPgRotWarps / P;
+    const int tr = threadIdx.x - 64;
+    const int i = tr % P, rb = tr / P;
+    float vlo = 0.0f, vhi = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < nst; c++) {
+      const int b = c % STAGES;
+      ok = ok && mbar_wait(&full[b], (uint32_t)(c / STAGES) & 1, kDevTimeoutFull);
+      float *stg = pg_smem + b * L::kStage;
+      const int rows = ok ? min(SR, n - c * SR) : 0;
+#pragma unroll 4
+      for (int r = rb; r < rows; r += kStep) {
+        const int o = r * P + i;
+        if (ROPE) {
+          const float x1 = stg[o], x2 = stg[L::kPitch + o];
+          const float cs = stg[4 * L::kPitch + o], sn = stg[5 * L::kPitch + o];
+          stg[o] = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+          stg[L::kPitch + o] = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
+        }
+        vlo = fmaxf(vlo, fabsf(stg[2 * L::kPitch + o]));
+        vhi = fmaxf(vhi, fabsf(stg[3 * L::kPitch + o]));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rotd[b]);
+    }
+    // Maxima of the lanes holding the same pair, then over the four warps.
+#pragma unroll
+    for (int o = P; o < 32; o <<= 1) {
+      vlo = fmaxf(vlo, __shfl_xor_sync(0xffffffffu, vlo, o));
+      vhi = fmaxf(vhi, __shfl_xor_sync(0xffffffffu, vhi, o));
+    }
+    if (lane < P) {
+      vred[(warp - 2) * 2 * P + lane] = vlo;
+      vred[(warp - 2) * 2 * P + P + lane] = vhi;
+    }
+    named_barrier_sync(1, 32 * kPgRotWarps);
+    if (tr < 2 * P) {
+      float mx = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kPgRotWarps; w++) mx = fmaxf(mx, vred[w * 2 * P + tr]);
+      const int d = tr < P ? pg * P + tr : 32 + pg * P + tr - P;
+      const size_t o = ((size_t)s * nh + h) * 64 + d;
+      const float scv = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
+      vs[o] = scv;
+      vinv[o] = mx > 0.0f ? __fdiv_rn(1.0f, scv) : 0.0f;
+    }
+  }
+}
+
 // attn_quant_kernel for D = 64 with one warp per row over all its heads: the
 // row's sequence, position and RoPE factors are read once, and successive
 // heads' loads are independent. Lane l holds dimensions l and l + 32 (a
@@ -363,6 +516,203 @@ __global__ void __launch_bounds__(256)
       sq[plane] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
       ks[plane] = kss;
       kzc[plane] = kmx > 0.0f ? __fmul_rn(128.0f, (float)ksum) : 0.0f;
+    }
+  }
+}
+
+// attn_quant64_kernel's bytes and scales for a tile of 64 rows of one
+// sequence and one head, two threads per row: the tile's Q, K and V halves
+// ([64 rows][32 floats] each) and the rows' RoPE factors (positions i0..,
+// contiguous within the sequence) come in by TMA, SWIZZLE_128B (no
+// multicast); thread (rr, hh) holds dimensions 16hh.. and 32 + 16hh.. of row
+// rr (both halves of its rotate_half pairs), so a row maximum or key sum is
+// the thread's and its neighbour's (one shuffle) instead of a 32-lane
+// reduction per head. Q and K take the fast byte conversion where the
+// attention short kernel does (no NaN, normal scale), V the generic one, as
+// attn_quant64_kernel: the same bits.
+constexpr int kQtRows = 64;
+
+template <bool ROPE>
+__global__ void __launch_bounds__(2 * kQtRows)
+    attn_quant_tile_kernel(const __grid_constant__ CUtensorMap mqkv, const __grid_constant__ CUtensorMap mcos,
+                           const __grid_constant__ CUtensorMap msin, const int2 *__restrict__ tiles,
+                           const int32_t *__restrict__ offs, int N, int H, int nh, float scale,
+                           const float *__restrict__ kmean, const float *__restrict__ vinv, uint8_t *__restrict__ qa,
+                           float *__restrict__ sq, int8_t *__restrict__ kq, float *__restrict__ ks,
+                           float *__restrict__ kzc, int8_t *__restrict__ vq) {
+  constexpr int kBox = kQtRows * 128;  // bytes of one [64 rows][32 floats] box
+  extern __shared__ uint8_t qt_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(qt_raw) + 1023) & ~uintptr_t(1023));
+  // Boxes: Q lo, Q hi, K lo, K hi, V lo, V hi, cos, sin.
+  float *s_km = reinterpret_cast<float *>(sm + 8 * kBox);  // [64] K column means
+  float *s_vi = s_km + 64;                                  // [64] V inverse scales
+  uint64_t *bar = reinterpret_cast<uint64_t *>(s_vi + 64);
+  const int2 tile = tiles[blockIdx.x];
+  const int s = tile.x, i0 = tile.y, h = blockIdx.y;
+  const int t0 = offs[s], n = offs[s + 1] - t0;
+  const int tid = threadIdx.x, rr = tid >> 1, hh = tid & 1;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  if (tid < 64) {
+    s_km[tid] = __ldg(kmean + ((size_t)s * nh + h) * 64 + tid);
+  } else {
+    s_vi[tid - 64] = __ldg(vinv + ((size_t)s * nh + h) * 64 + tid - 64);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    prefetch_tensormap(&mqkv);
+    mbar_arrive_expect_tx(bar, (ROPE ? 8 : 6) * kBox);
+    const int y = t0 + i0;
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+      tma_load_2d(&mqkv, sm + (2 * p) * kBox, bar, p * H + h * 64, y);
+      tma_load_2d(&mqkv, sm + (2 * p + 1) * kBox, bar, p * H + h * 64 + 32, y);
+    }
+    if (ROPE) {
+      tma_load_2d(&mcos, sm + 6 * kBox, bar, 0, i0);
+      tma_load_2d(&msin, sm + 7 * kBox, bar, 0, i0);
+    }
+  }
+  const bool ok = mbar_wait(bar, 0, kDevTimeoutFull);
+  const bool valid = ok && i0 + rr < n;
+  // Chunk c (dimensions 4c..4c+3 of a half) of row rr in box b.
+  auto chunk = [&](int b, int c) {
+    return *reinterpret_cast<const float4 *>(sm + b * kBox + rr * 128 + (((c ^ (rr & 7))) << 4));
+  };
+  // v[0..15]: dimensions 16hh.., v[16..31]: 32 + 16hh.. of box pair p.
+  auto load_pair = [&](int p, float (&v)[32]) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float4 lo = chunk(2 * p, 4 * hh + k), hi = chunk(2 * p + 1, 4 * hh + k);
+      v[4 * k] = lo.x, v[4 * k + 1] = lo.y, v[4 * k + 2] = lo.z, v[4 * k + 3] = lo.w;
+      v[16 + 4 * k] = hi.x, v[17 + 4 * k] = hi.y, v[18 + 4 * k] = hi.z, v[19 + 4 * k] = hi.w;
+    }
+  };
+  auto rotate = [&](float (&v)[32]) {  // Rope (linalg/vec_simd.go:404-425): separate roundings, no FMA
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float4 c = chunk(6, 4 * hh + k), sn = chunk(7, 4 * hh + k);
+      const float c4[4] = {c.x, c.y, c.z, c.w}, s4[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float a = v[4 * k + u], b = v[16 + 4 * k + u];
+        v[4 * k + u] = __fsub_rn(__fmul_rn(a, c4[u]), __fmul_rn(b, s4[u]));
+        v[16 + 4 * k + u] = __fadd_rn(__fmul_rn(b, c4[u]), __fmul_rn(a, s4[u]));
+      }
+    }
+  };
+  const size_t plane = (size_t)h * N + t0 + i0 + rr;
+  // Q (attention8.go:210-220): uint8 q + 128, scale times the score scale.
+  {
+    float v[32];
+    load_pair(0, v);
+    if (ROPE) rotate(v);
+    float m = absmax32<true>(v);  // NaN-propagating first: a NaN row takes the generic path
+    m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    const bool nan = m != m;
+    if (nan) {
+      m = absmax32<false>(v);
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    }
+    const float qs = m > 0.0f ? __fdiv_rn(m, 127.0f) : 0.0f;
+    const float inv = m > 0.0f ? __fdiv_rn(1.0f, qs) : 0.0f;
+    uint32_t w[8];
+    if (m == 0.0f) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) w[k] = 0x80808080u;
+    } else if (!nan && scale_is_normal(qs)) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) w[k] = quant4_fast(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3], f2(inv), f2(inv));
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        uint32_t b[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) b[u] = quant_bits(__fmul_rn(v[4 * k + u], inv)) + 128u;
+        w[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+      }
+    }
+    if (valid) {
+      *reinterpret_cast<uint4 *>(qa + plane * 64 + 16 * hh) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4 *>(qa + plane * 64 + 32 + 16 * hh) = make_uint4(w[4], w[5], w[6], w[7]);
+      if (hh == 0) sq[plane] = m > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
+    }
+  }
+  // K (attention8.go:240-251): centred, int8, scale and 128 * sum of the
+  // unclamped bytes; a zero row is zero bytes, scale and sum.
+  {
+    float v[32];
+    load_pair(1, v);
+    if (ROPE) rotate(v);
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+      const int d = 16 * hh + k;
+      v[k] = __fsub_rn(v[k], s_km[d]);
+      v[16 + k] = __fsub_rn(v[16 + k], s_km[32 + d]);
+    }
+    float m = absmax32<true>(v);
+    m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    const bool nan = m != m;
+    if (nan) {
+      m = absmax32<false>(v);
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    }
+    const float kss = m > 0.0f ? __fdiv_rn(m, 127.0f) : 0.0f;
+    const float inv = m > 0.0f ? __fdiv_rn(1.0f, kss) : 0.0f;
+    uint32_t w[8];
+    int sum = 0;
+    if (m == 0.0f) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) w[k] = 0u;
+    } else if (!nan && scale_is_normal(kss)) {  // bytes are q itself: summed as signed bytes
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        w[k] = quant4_fast_s8(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3], f2(inv), f2(inv));
+        sum = dp4a_ss(w[k], 0x01010101u, sum);
+      }
+    } else {  // the reference's conversion (NaN -> INT_MIN, summed before the clamp)
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        uint32_t b[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int x = rne_int(__fmul_rn(v[4 * k + u], inv));
+          sum += x;
+          b[u] = (uint32_t)max(-128, min(127, x));
+        }
+        w[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+      }
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    if (valid) {
+      *reinterpret_cast<uint4 *>(kq + plane * 64 + 16 * hh) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4 *>(kq + plane * 64 + 32 + 16 * hh) = make_uint4(w[4], w[5], w[6], w[7]);
+      if (hh == 0) {
+        ks[plane] = kss;
+        kzc[plane] = m > 0.0f ? __fmul_rn(128.0f, (float)sum) : 0.0f;
+      }
+    }
+  }
+  // V (attention8.go:255-269): int8 per column.
+  {
+    float v[32];
+    load_pair(2, v);
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      uint32_t b[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int j = 4 * k + u, d = j < 16 ? 16 * hh + j : 32 + 16 * hh + j - 16;
+        b[u] = quant_bits(__fmul_rn(v[j], s_vi[d]));
+      }
+      w[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+    }
+    if (valid) {
+      *reinterpret_cast<uint4 *>(vq + plane * 64 + 16 * hh) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4 *>(vq + plane * 64 + 32 + 16 * hh) = make_uint4(w[4], w[5], w[6], w[7]);
     }
   }
 }
@@ -826,6 +1176,111 @@ static bool cluster_stats_enabled() {
   return on;
 }
 
+// IG_ATTN_PG_STATS=0 keeps the cluster kernel for the statistics of long
+// sequences (the same bits; for comparisons).
+static bool pg_stats_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_ATTN_PG_STATS");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
+// attn_stats_pg_kernel over every (sequence, head, pair group) of a: eight
+// pairs per CTA, 128-row stages, six in flight.
+static int launch_stats_pg(const AttnArgs &a, cudaStream_t st) {
+  constexpr int P = 8, SR = 128, STAGES = 6;
+  auto enc = get_encode_fn();
+  if (!enc) return IG_ERR_CUDA;
+  CUtensorMap mq, mc, ms;
+  cuuint32_t estr[2] = {1, 1};
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)(3 * a.H), (cuuint64_t)a.N};
+    cuuint64_t strides[1] = {(cuuint64_t)(3 * a.H) * sizeof(float)};
+    cuuint32_t box[2] = {(cuuint32_t)P, (cuuint32_t)SR};
+    if (enc(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.qkv), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return IG_ERR_CUDA;
+  }
+  mc = mq;
+  ms = mq;
+  if (a.rope_cos) {
+    // The factor tables [positions][32]; positions past max_len are never read.
+    cuuint64_t dims[2] = {32, (cuuint64_t)a.max_len};
+    cuuint64_t strides[1] = {32 * sizeof(float)};
+    cuuint32_t box[2] = {(cuuint32_t)P, (cuuint32_t)SR};
+    if (enc(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_cos), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_sin), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return IG_ERR_CUDA;
+  }
+  const int smem = PgLayout<P, SR>::bytes(STAGES);
+  static SmemOptIn at_r, at_n;
+  auto kern = a.rope_cos ? attn_stats_pg_kernel<P, SR, STAGES, true> : attn_stats_pg_kernel<P, SR, STAGES, false>;
+  if ((a.rope_cos ? at_r : at_n).ensure((const void *)kern, smem) != cudaSuccess) return IG_ERR_CUDA;
+  kern<<<dim3(a.nseq, a.nh, 32 / P), kPgThreads, smem, st>>>(mq, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
+// IG_ATTN_QUANT_TILE=0 keeps the warp-per-row quantization (the same bits;
+// for comparisons).
+static bool quant_tile_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_ATTN_QUANT_TILE");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
+// Q, K, V rotation and quantization of every row of a (D = 64): by 64-row
+// tiles when the plan's tiles are given and qkv suits TMA, else a warp per row.
+static int launch_quant64(const AttnArgs &a, cudaStream_t st) {
+  if (a.row_tiles && a.nrow_tiles > 0 && quant_tile_enabled()) {
+    auto enc = get_encode_fn();
+    if (!enc) return IG_ERR_CUDA;
+    CUtensorMap mq, mc, ms;
+    cuuint32_t estr[2] = {1, 1};
+    cuuint32_t box[2] = {32, (cuuint32_t)kQtRows};
+    {
+      cuuint64_t dims[2] = {(cuuint64_t)(3 * a.H), (cuuint64_t)a.N};
+      cuuint64_t strides[1] = {(cuuint64_t)(3 * a.H) * sizeof(float)};
+      if (enc(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.qkv), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return IG_ERR_CUDA;
+    }
+    mc = mq;
+    ms = mq;
+    if (a.rope_cos) {
+      cuuint64_t dims[2] = {32, (cuuint64_t)a.max_len};
+      cuuint64_t strides[1] = {32 * sizeof(float)};
+      if (enc(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_cos), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+          enc(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_sin), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return IG_ERR_CUDA;
+    }
+    const int smem = 1024 + 8 * kQtRows * 128 + 2 * 64 * 4 + 16;
+    static SmemOptIn at_r, at_n;
+    auto kern = a.rope_cos ? attn_quant_tile_kernel<true> : attn_quant_tile_kernel<false>;
+    if ((a.rope_cos ? at_r : at_n).ensure((const void *)kern, smem) != cudaSuccess) return IG_ERR_CUDA;
+    kern<<<dim3(a.nrow_tiles, a.nh), 2 * kQtRows, smem, st>>>(mq, mc, ms, a.row_tiles, a.offs, a.N, a.H, a.nh,
+                                                               a.scale, a.kmean, a.vinv, a.qa, a.sq, a.kq, a.ks,
+                                                               a.kzc, a.vq);
+    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
+  attn_quant64_kernel<<<(unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st>>>(
+      a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq, a.kq,
+      a.ks, a.kzc, a.vq);
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.rope_cos && a.D != 64) return IG_ERR_UNSUPPORTED;
   if (a.rope_cos && a.nseq > 0 && a.N > 0 && a.max_len <= kShortSeq && (a.H % 4) == 0) {
@@ -843,6 +1298,11 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     // row (all its heads) for the rotation and quantization.
     // Few long sequences: a cluster of kClCtas CTAs per (sequence, head),
     // each holding a slice of the rows in shared memory.
+    if (a.max_len >= 2048 && pg_stats_enabled()) {
+      const int rc = launch_stats_pg(a, st);
+      if (rc) return rc;
+      return launch_quant64(a, st);
+    }
     const int R = (a.max_len + kClCtas - 1) / kClCtas;
     const int cl_smem = (R * 64 + 64 + kClCtas * 64 + 4 * 64) * (int)sizeof(float) + 16;
     if (a.max_len >= 2048 && cl_smem <= 200 * 1024 && cluster_stats_enabled()) {
@@ -864,10 +1324,7 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
       if (cudaLaunchKernelEx(&cfg, kern, a.qkv, a.offs, a.H, a.nh, a.rope_cos, a.rope_sin, a.kmean, a.vs, a.vinv,
                              R) != cudaSuccess)
         return IG_ERR_CUDA;
-      attn_quant64_kernel<<<(unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st>>>(
-          a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq,
-          a.kq, a.ks, a.kzc, a.vq);
-      return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+      return launch_quant64(a, st);
     }
     // Otherwise one CTA per (sequence, head): eight stages in flight for
     // sequences of 1024 tokens or more (one CTA per SM), three below.
@@ -881,10 +1338,7 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     kern<<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, a.rope_cos, a.rope_sin, a.kmean, a.vs,
                                                  a.vinv);
     if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
-    attn_quant64_kernel<<<(unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st>>>(
-        a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq,
-        a.kq, a.ks, a.kzc, a.vq);
-    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+    return launch_quant64(a, st);
   }
   if (a.nseq > 0 && a.N > 0 && a.D <= 128 && (a.D % 4) == 0 && a.V >= 1) {
     attn_prep_kernel<<<dim3(a.nseq, a.nh), 256, 0, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.D, a.scale, a.rope_cos,

@@ -783,6 +783,8 @@ int run_encoder(ig_model *m, Workspace &w, const int32_t *d_ids, const Plan &p, 
   at.vinv = w.vinv;
   at.row_seq = w.row_seq;
   at.N = N;
+  at.row_tiles = w.pd.fb;
+  at.nrow_tiles = w.pd.nfb;
   at.ctx = w.ctx;
   for (int l = 0; l < c.layers; l++) {
     const DevLayer &L = m->layers[l];
@@ -1825,6 +1827,7 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
   int32_t *d_rs = (int32_t *)take(4 * N);
   int4 *d_tc = (int4 *)take(16 * p.tc[0].size());
   int2 *d_v1 = (int2 *)take(8 * p.v1[0].size());
+  int2 *d_fb = (int2 *)take(8 * p.fb.size());
   a.qa = (uint8_t *)take(N * nh * D);
   a.kq = (int8_t *)take(N * nh * D);
   a.vq = (int8_t *)take(N * nh * D);
@@ -1844,6 +1847,9 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
     cudaMemcpyAsync(d_rs, p.row_seq.data(), 4 * N, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(d_tc, p.tc[0].data(), 16 * p.tc[0].size(), cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(d_v1, p.v1[0].data(), 8 * p.v1[0].size(), cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(d_fb, p.fb.data(), 8 * p.fb.size(), cudaMemcpyHostToDevice, st);
+    a.row_tiles = d_fb;
+    a.nrow_tiles = (int)p.fb.size();
     if (attn_short_fits(a)) {
       rc = launch_attn_short(a, st);
     } else {

@@ -346,4 +346,51 @@ __device__ __forceinline__ float gelu_tanh_at(float x, long long i, long long le
   return i < len - len % V ? gelu_tanh_body(x) : gelu_tanh_tail(x);
 }
 
+// ---- per-row int8 quantization pieces (attention8.go:210-269) ----------------
+
+// max(0, |v[0]|, ..., |v[31]|), NaN-propagating (PROP) or NaN-ignoring, as a
+// tree of four chains: both maxima are associative (max.NaN returns the
+// canonical NaN), so the value is the one chain's.
+template <bool PROP>
+__device__ __forceinline__ float absmax32(const float (&v)[32]) {
+  float m[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int u = 0; u < 32; u++) m[u & 3] = PROP ? fmax_nan(m[u & 3], fabsf(v[u])) : fmaxf(m[u & 3], fabsf(v[u]));
+  return PROP ? fmax_nan(fmax_nan(m[0], m[1]), fmax_nan(m[2], m[3])) : fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
+// x with its sign bit set.
+__device__ __forceinline__ float neg_bits(float x) { return __int_as_float(__float_as_int(x) | 0x80000000); }
+
+// The low bytes of four words as one word (byte k from word k).
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// Byte of clamp(rne(x)) (two's complement) in the low byte of the result
+// (rne as the reference's VCVTPS2DQ; any scale).
+__device__ __forceinline__ uint32_t quant_bits(float x) { return (uint32_t)max(-128, min(127, rne_int(x))); }
+
+// For a row (or column) maximum m > 0 whose scale RN(m/127) is a normal
+// float, every |x * inv| with |x| <= m is below 127 + 2^-20, so rne(x * inv)
+// stays in [-127, 127] and the int8 clamp never applies.
+__device__ __forceinline__ bool scale_is_normal(float scale) {
+  return scale >= 1.17549435e-38f && scale <= 3.40282347e38f;
+}
+
+// Four bytes q + 128, q = rne(x * inv), for a normal scale and finite
+// values: the product rounded, then + (1.5*2^23 + 128), whose low byte is
+// q + 128.
+__device__ __forceinline__ uint32_t quant4_fast(float a, float b, float c, float d, float2 inv01, float2 inv23) {
+  const float2 p0 = __fmul2_rn(make_float2(a, b), inv01), p1 = __fmul2_rn(make_float2(c, d), inv23);
+  constexpr float m = kMagic + 128.0f;
+  return pack_low_bytes(__float_as_uint(__fadd_rn(p0.x, m)), __float_as_uint(__fadd_rn(p0.y, m)),
+                        __float_as_uint(__fadd_rn(p1.x, m)), __float_as_uint(__fadd_rn(p1.y, m)));
+}
+// The same bytes as int8 q (two's complement): q + 128 with the top bit
+// flipped.
+__device__ __forceinline__ uint32_t quant4_fast_s8(float a, float b, float c, float d, float2 inv01, float2 inv23) {
+  return quant4_fast(a, b, c, d, inv01, inv23) ^ 0x80808080u;
+}
+
 }  // namespace ig

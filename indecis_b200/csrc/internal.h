@@ -133,6 +133,10 @@ struct AttnArgs {
   float *vs, *vinv;     // [nseq][nh][D]
   const int32_t *row_seq;  // [N] sequence of each row
   int N;
+  // Optional: (sequence, first row) of every 64-row tile of every sequence
+  // (device), for the tiled rotation and quantization of long sequences.
+  const int2 *row_tiles = nullptr;
+  int nrow_tiles = 0;
   float *ctx;           // [N][H] output
   // Optional (the fused short-sequence kernel, nh <= 8): instead of ctx, its
   // per-row int8 quantization (quant_rows over all heads of a row: bytes
