@@ -132,8 +132,8 @@ __device__ __forceinline__ float chunk_max_acc(const uint32_t (&acc)[16], int c,
 // chunk at TMEM column tcol as 16 bytes (0 outside the row's valid keys), all
 // with ExpShift's vector-body exp (tail_fixup then rewrites the row's
 // scalar-tail keys); the sum of the 16 is added to psum. The subtraction is
-// scalar: a packed add after the packed product of dequant2m (or score2) is
-// contracted with it into one rounding (a packed add here changed bits).
+// scalar: with a packed add here (after the packed products of dequant2m or
+// score2) one row in a few thousand came out different, every run.
 template <bool PRE, bool MASK>
 __device__ __forceinline__ uint4 chunk_p_acc(const uint32_t (&acc)[16], int c, const float *zcm, const float *ks,
                                             const ScoreRow &w, float mx, int &psum) {

@@ -121,12 +121,26 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
 // Waits for the phase with the given parity to complete. Gives up after about
 // two seconds (a wait that long means a lost arrival): records `code` in
 // g_device_error and returns false so the caller can wind down.
+// try_wait that may suspend the thread for up to ns nanoseconds (or until
+// the phase completes) instead of returning at once.
+__device__ __forceinline__ bool mbar_try_wait_for(uint64_t *bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0 && globaltimer() - t0 > 2000000000ull) {
+  for (;;) {
+    if (mbar_try_wait_for(bar, parity, 1000000u)) return true;
+    if (globaltimer() - t0 > 2000000000ull) {
       set_device_error(code);
       return false;
     }
