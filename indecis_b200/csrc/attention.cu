@@ -170,112 +170,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// The statistics of attn_stats64_kernel for long sequences, spread over a
-// cluster of kClCtas CTAs per (sequence, head) so that the sequence is read
-// by as many SMs: CTA k takes rows [kR, kR + R), rotates its keys into shared
-// memory (RoPE at each row's position, rotate_half without FMA) and takes the
-// V column maxima of its rows. The ordered K column sums then run CTA after
-// CTA: CTA k continues the 64 sums from the values CTA k - 1 left (received
-// by st.async on its carry barrier) over its rows in order, so the additions
-// are the single chain's, in the same order. Every CTA sends its V maxima to
-// the last CTA, which writes the mean and the V scales.
-constexpr int kClCtas = 8;
-template <bool ROPE>
-__global__ void __launch_bounds__(256, 1)
-    attn_stats_cl_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ offs, int H, int nh,
-                         const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
-                         float *__restrict__ kmean, float *__restrict__ vs, float *__restrict__ vinv, int R) {
-  extern __shared__ __align__(16) float cl_smem[];
-  float *kr = cl_smem;                  // [R][64] rotated K of this CTA's rows
-  float *carry = kr + (size_t)R * 64;   // [64] the sums over the earlier CTAs' rows
-  float *vpart = carry + 64;            // [kClCtas][64] V maxima of every CTA (used in the last)
-  float *vloc = vpart + kClCtas * 64;   // [4][64] this CTA's row-group maxima
-  uint64_t *bar_carry = reinterpret_cast<uint64_t *>(vloc + 4 * 64);
-  uint64_t *bar_v = bar_carry + 1;
-  const int tid = threadIdx.x;
-  const uint32_t k = cluster_ctarank();
-  const int s = blockIdx.x / kClCtas, h = blockIdx.y;
-  const int t0 = offs[s], n = offs[s + 1] - t0;
-  const int r0 = min(n, (int)k * R), rows = min(n, r0 + R) - r0;
-  const size_t ld = 3 * (size_t)H;
-  if (tid == 0) {
-    mbar_init(bar_carry, 1);
-    mbar_init(bar_v, 1);
-    fence_barrier_init();
-  }
-  cluster_sync_all();  // every CTA's barriers exist before any peer writes
-  if (tid == 0) {
-    if (k > 0) mbar_arrive_expect_tx(bar_carry, 64 * 4);
-    if (k == kClCtas - 1) mbar_arrive_expect_tx(bar_v, kClCtas * 64 * 4);
-  }
-  // This CTA's keys, rotated: thread e takes four pairs (4q.., 32 + 4q..) of row r.
-  const float *kb = qkv + (size_t)(t0 + r0) * ld + H + h * 64;
-#pragma unroll 4
-  for (int e = tid; e < rows * 8; e += 256) {
-    const int r = e >> 3, q = e & 7;
-    float4 x1 = __ldg(reinterpret_cast<const float4 *>(kb + (size_t)r * ld + 4 * q));
-    float4 x2 = __ldg(reinterpret_cast<const float4 *>(kb + (size_t)r * ld + 32 + 4 * q));
-    if constexpr (ROPE) {
-      const float4 c = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)(r0 + r) * 32 + 4 * q));
-      const float4 sn = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)(r0 + r) * 32 + 4 * q));
-      const float4 a = x1, b = x2;
-      x1 = make_float4(__fsub_rn(__fmul_rn(a.x, c.x), __fmul_rn(b.x, sn.x)), __fsub_rn(__fmul_rn(a.y, c.y), __fmul_rn(b.y, sn.y)),
-                       __fsub_rn(__fmul_rn(a.z, c.z), __fmul_rn(b.z, sn.z)), __fsub_rn(__fmul_rn(a.w, c.w), __fmul_rn(b.w, sn.w)));
-      x2 = make_float4(__fadd_rn(__fmul_rn(b.x, c.x), __fmul_rn(a.x, sn.x)), __fadd_rn(__fmul_rn(b.y, c.y), __fmul_rn(a.y, sn.y)),
-                       __fadd_rn(__fmul_rn(b.z, c.z), __fmul_rn(a.z, sn.z)), __fadd_rn(__fmul_rn(b.w, c.w), __fmul_rn(a.w, sn.w)));
-    }
-    *reinterpret_cast<float4 *>(kr + r * 64 + 4 * q) = x1;
-    *reinterpret_cast<float4 *>(kr + r * 64 + 32 + 4 * q) = x2;
-  }
-  // V column maxima of this CTA's rows (four interleaved row groups).
-  {
-    const int d = tid & 63, g = tid >> 6;
-    const float *vb = qkv + (size_t)(t0 + r0) * ld + 2 * H + h * 64 + d;
-    float m[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // eight loads in flight
-    int r = g;
-    for (; r + 28 < rows; r += 32) {
-#pragma unroll
-      for (int u = 0; u < 8; u++) m[u] = fmaxf(m[u], fabsf(__ldg(vb + (size_t)(r + 4 * u) * ld)));
-    }
-    for (; r < rows; r += 4) m[0] = fmaxf(m[0], fabsf(__ldg(vb + (size_t)r * ld)));
-    vloc[g * 64 + d] = fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
-  }
-  __syncthreads();
-  if (tid < 64) {
-    const float m = fmaxf(fmaxf(vloc[tid], vloc[64 + tid]), fmaxf(vloc[128 + tid], vloc[192 + tid]));
-    st_async_f32(&vpart[k * 64 + tid], kClCtas - 1, m, bar_v);
-    float acc = 0.0f;
-    bool ok = true;
-    if (k > 0) {
-      ok = mbar_wait(bar_carry, 0, kDevTimeoutFull);
-      acc = carry[tid];
-    }
-    int r = 0;
-    for (; r + 8 <= rows; r += 8) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++) v[u] = kr[(r + u) * 64 + tid];
-#pragma unroll
-      for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, v[u]);
-    }
-    for (; r < rows; r++) acc = __fadd_rn(acc, kr[r * 64 + tid]);
-    if (k < kClCtas - 1) {
-      st_async_f32(&carry[tid], k + 1, acc, bar_carry);
-    } else {
-      ok = mbar_wait(bar_v, 0, kDevTimeoutFull) && ok;
-      float mx = 0.0f;
-#pragma unroll
-      for (int c = 0; c < kClCtas; c++) mx = fmaxf(mx, vpart[c * 64 + tid]);
-      const size_t o = ((size_t)s * nh + h) * 64 + tid;
-      kmean[o] = n > 0 ? __fmul_rn(acc, __fdiv_rn(1.0f, (float)n)) : 0.0f;
-      const float scv = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
-      vs[o] = scv;
-      vinv[o] = mx > 0.0f ? __fdiv_rn(1.0f, scv) : 0.0f;
-    }
-  }
-  cluster_sync_all();  // no CTA leaves while a peer may still write into it
-}
-
 // The statistics of attn_stats64_kernel with each (sequence, head) split by
 // RoPE pair over 32 / P CTAs: CTA (s, h, pg) takes the pairs i in
 // [pg P, pg P + P), dimensions i and 32 + i, over all the sequence's rows in
@@ -1166,18 +1060,8 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// IG_ATTN_CLUSTER_STATS=0 keeps one CTA per (sequence, head) for the
-// statistics of long sequences (the same bits; for comparisons).
-static bool cluster_stats_enabled() {
-  static const bool on = [] {
-    const char *s = getenv("IG_ATTN_CLUSTER_STATS");
-    return !(s && s[0] == '0');
-  }();
-  return on;
-}
-
-// IG_ATTN_PG_STATS=0 keeps the cluster kernel for the statistics of long
-// sequences (the same bits; for comparisons).
+// IG_ATTN_PG_STATS=0 keeps one CTA per (sequence, head) for the statistics of
+// long sequences (the same bits; for comparisons).
 static bool pg_stats_enabled() {
   static const bool on = [] {
     const char *s = getenv("IG_ATTN_PG_STATS");
@@ -1294,36 +1178,12 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
   }
   if (a.nseq > 0 && a.N > 0 && a.D == 64 && a.V >= 1 && a.max_len > kShortSeq && (a.H % 4) == 0 && a.row_seq &&
       !(reinterpret_cast<uintptr_t>(a.qkv) & 15)) {
-    // Long sequences: statistics per (sequence, head), then one warp per
-    // row (all its heads) for the rotation and quantization.
-    // Few long sequences: a cluster of kClCtas CTAs per (sequence, head),
-    // each holding a slice of the rows in shared memory.
+    // Long sequences: the statistics, then the rotation and quantization.
+    // From 2048 tokens the statistics of a (sequence, head) are split over
+    // four CTAs by RoPE pair (few long sequences would leave most SMs idle).
     if (a.max_len >= 2048 && pg_stats_enabled()) {
       const int rc = launch_stats_pg(a, st);
       if (rc) return rc;
-      return launch_quant64(a, st);
-    }
-    const int R = (a.max_len + kClCtas - 1) / kClCtas;
-    const int cl_smem = (R * 64 + 64 + kClCtas * 64 + 4 * 64) * (int)sizeof(float) + 16;
-    if (a.max_len >= 2048 && cl_smem <= 200 * 1024 && cluster_stats_enabled()) {
-      static SmemOptIn at_r, at_n;
-      auto kern = a.rope_cos ? attn_stats_cl_kernel<true> : attn_stats_cl_kernel<false>;
-      if ((a.rope_cos ? at_r : at_n).ensure((const void *)kern, cl_smem) != cudaSuccess) return IG_ERR_CUDA;
-      cudaLaunchConfig_t cfg{};
-      cfg.gridDim = dim3(a.nseq * kClCtas, a.nh);
-      cfg.blockDim = dim3(256);
-      cfg.dynamicSmemBytes = cl_smem;
-      cfg.stream = st;
-      cudaLaunchAttribute at[1];
-      at[0].id = cudaLaunchAttributeClusterDimension;
-      at[0].val.clusterDim.x = kClCtas;
-      at[0].val.clusterDim.y = 1;
-      at[0].val.clusterDim.z = 1;
-      cfg.attrs = at;
-      cfg.numAttrs = 1;
-      if (cudaLaunchKernelEx(&cfg, kern, a.qkv, a.offs, a.H, a.nh, a.rope_cos, a.rope_sin, a.kmean, a.vs, a.vinv,
-                             R) != cudaSuccess)
-        return IG_ERR_CUDA;
       return launch_quant64(a, st);
     }
     // Otherwise one CTA per (sequence, head): eight stages in flight for
