@@ -2,8 +2,12 @@
 // the whole of linalg/attention8.go (Prepare, then Attend over every query)
 // for one (sequence, head) per CTA, with the quantized operands built
 // directly in shared memory in the tensor cores' layouts instead of a global
-// round trip. 8 warps and 67 KB of shared memory, so three CTAs share an SM
-// and one CTA's waits are covered by the others' work.
+// round trip. 8 warps and 73 KB of shared memory, so three CTAs share an SM
+// and one CTA's waits are covered by the others' work. The variant that also
+// computes the QKV projection (QKV below) stages the cos/sin rows of
+// positions 0..127 as well (105 KB, two CTAs per SM with up to 128 registers
+// a thread): per-row RoPE loads from L2, which the 28 KB of L1 left beside
+// three CTAs could not hold, cost it 17% of its time.
 //
 // Threads work on rows in pairs: row rr = tid/2, and thread tid&1 takes
 // dimensions 16hh..16hh+15 and 32+16hh..32+16hh+15 (hh = tid&1), so both
@@ -44,7 +48,11 @@ namespace ig {
 constexpr int kShortN = 128;  // longest sequence this kernel takes
 
 constexpr int kShortThreads = 256;
+// CTAs per SM: three for the plain kernel; two for the projecting one, whose
+// shared memory also holds the RoPE rows (and whose threads may then hold 128
+// registers).
 constexpr int kShortCtasPerSm = 3;
+constexpr int kShortProjCtasPerSm = 2;
 
 // Once a region's f32 rows have been read it holds the quantized tiles; after
 // O = P.V the K region and the start of the V region hold the ctx staging.
@@ -75,6 +83,10 @@ struct AttnShortSmem {
   static constexpr int kWzc = kWsb + 192 * 4;
   static constexpr int kQx = kKs;
   static constexpr int kTotal = kWzc + 192 * 4 + 1024;
+  // The projecting kernel: the cos and sin rows of positions 0..127
+  // ([128][32 f32] each, SWIZZLE_128B), read by the Q and K rotations.
+  static constexpr int kRope = ((kWzc + 192 * 4 + 1023) / 1024) * 1024;
+  static constexpr int kTotalProj = kRope + 2 * 16384 + 1024;
   static_assert(kKs + 1024 <= kSq, "Q half-maxima overlap the query scales");
   // Fused projection: the operands of the Q product (A = the sequence's
   // quantized rows, [128][128 B] SWIZZLE_128B per 128-byte K block; B = the
@@ -85,6 +97,7 @@ struct AttnShortSmem {
   static constexpr int kB = 32768;
   static_assert(kO + 128 * kOPitch * 4 <= kRed, "ctx staging overlaps the exchange");
   static_assert(kShortCtasPerSm * (kTotal + 1024) <= 228 * 1024, "three CTAs per SM");
+  static_assert(kShortProjCtasPerSm * (kTotalProj + 1024) <= 228 * 1024, "two CTAs per SM");
 };
 
 // Chunk c (16 bytes: dimensions 4c..4c+3, c in 0..15) of row r of an f32
@@ -121,11 +134,6 @@ __device__ __forceinline__ void rope4(float4 &lo, float4 &hi, float4 c, float4 s
 // 128 < 2^22, so float(acc) comes from the 1.5*2^23 bit trick exactly.
 __device__ __forceinline__ float dequant_o(uint32_t acc, float vs, float sp) {
   return __fmul_rn(__fmul_rn(__fsub_rn(magic_float((int32_t)acc), kMagic), vs), sp);
-}
-
-// Brings the 128-byte line holding p into L1 (no register is written).
-__device__ __forceinline__ void prefetch_l1(const float *p) {
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
 // Presets 16 TMEM columns of a projection accumulator (this thread's lane) to
@@ -165,8 +173,9 @@ __device__ __forceinline__ float4 dequant_preset4(const uint32_t *a, const float
 // quantized rows [N][H] (uint8), mw the QKV weights [3H][H] (int8); xa_s,
 // wsb, wzc are the row scales, column scales and 128 * column sums.
 template <bool QKV>
-__global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
+__global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kShortCtasPerSm)
     attn_short_kernel(const __grid_constant__ CUtensorMap mqkv, const __grid_constant__ CUtensorMap mw,
+                      const __grid_constant__ CUtensorMap mcos, const __grid_constant__ CUtensorMap msin,
                       const float *__restrict__ qkv, const int32_t *__restrict__ offs, int H, int nh, int window,
                       int V, float scale, const float *__restrict__ rope_cos, const float *__restrict__ rope_sin,
                       float *__restrict__ ctx, uint8_t *__restrict__ xq, int ldq, float *__restrict__ sa,
@@ -222,10 +231,14 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       fence_barrier_init();
       // A: 128 rows from the sequence's first (rows past it are never used);
       // B: the head's 64 Q weight rows.
-      mbar_arrive_expect_tx(bar_load, nkb * (16384 + 8192));
+      mbar_arrive_expect_tx(bar_load, nkb * (16384 + 8192) + (rope ? 32768 : 0));
       for (int kb = 0; kb < nkb; kb++) {
         tma_load_2d(&mqkv, smem + S::kA + kb * 16384, bar_load, kb * 128, t0);
         tma_load_2d(&mw, smem + S::kB + kb * 8192, bar_load, kb * 128, h * 64);
+      }
+      if (rope) {
+        tma_load_2d(&mcos, smem + S::kRope, bar_load, 0, 0);
+        tma_load_2d(&msin, smem + S::kRope + 16384, bar_load, 0, 0);
       }
     }
     if (warp == 1) tmem_alloc(tmem_slot, 128);
@@ -274,13 +287,9 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       }
     }
     __syncwarp();
-    // The row's RoPE factor rows are brought into L1 while the product runs
-    // (they come from L2 and do not depend on it); read after the drain.
+    // The row's RoPE factors come from the cos/sin rows staged with the
+    // operands (positions 0..127; shared memory, not a global load per row).
     const bool rot = rope && r < n;
-    if (rot) {
-      prefetch_l1(rope_cos + (size_t)r * 32 + 16 * hq);
-      prefetch_l1(rope_sin + (size_t)r * 32 + 16 * hq);
-    }
     const float sar = r < n ? __ldg(xa_s + t0 + r) : 0.0f;
     ok = mbar_wait(bar_m, 0, kDevTimeoutAccum);
     ok = __all_sync(0xffffffffu, ok);
@@ -302,10 +311,11 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
     }
     if (r < n) {
       if (rot) {
+        mbar_wait(bar_load, 0, kDevTimeoutFull);  // the RoPE rows have landed
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-          const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)r * 32 + 16 * hq + 4 * k));
-          const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)r * 32 + 16 * hq + 4 * k));
+          const float4 rc = *reinterpret_cast<const float4 *>(smem + S::kRope + r * 128 + (((4 * hq + k) ^ (r & 7)) << 4));
+          const float4 rs = *reinterpret_cast<const float4 *>(smem + S::kRope + 16384 + r * 128 + (((4 * hq + k) ^ (r & 7)) << 4));
           const float c4[4] = {rc.x, rc.y, rc.z, rc.w}, s4[4] = {rs.x, rs.y, rs.z, rs.w};
 #pragma unroll
           for (int u = 0; u < 4; u++) rope1(qv[4 * k + u], qv[16 + 4 * k + u], c4[u], s4[u]);
@@ -369,12 +379,7 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
       mma_commit(bar_m);
     }
     __syncwarp();
-    // K is rotated with the same factors as Q (same position and pairs):
-    // brought into L1 again while the K|V product runs.
-    if (rot) {
-      prefetch_l1(rope_cos + (size_t)r * 32 + 16 * hq);
-      prefetch_l1(rope_sin + (size_t)r * 32 + 16 * hq);
-    }
+    // K is rotated with the same staged factors as Q (same position and pairs).
     ok = ok && mbar_wait(bar_m, 1, kDevTimeoutAccum);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
@@ -390,8 +395,8 @@ __global__ void __launch_bounds__(kShortThreads, kShortCtasPerSm)
         float4 lo = dequant_preset4(a0 + 4 * k, kb_lo + 4 * k, sar);
         float4 hi = dequant_preset4(a1 + 4 * k, kb_hi + 4 * k, sar);
         if (rot) {
-          const float4 rc = __ldg(reinterpret_cast<const float4 *>(rope_cos + (size_t)r * 32 + 16 * hq + 4 * k));
-          const float4 rs = __ldg(reinterpret_cast<const float4 *>(rope_sin + (size_t)r * 32 + 16 * hq + 4 * k));
+          const float4 rc = *reinterpret_cast<const float4 *>(smem + S::kRope + r * 128 + (((4 * hq + k) ^ (r & 7)) << 4));
+          const float4 rs = *reinterpret_cast<const float4 *>(smem + S::kRope + 16384 + r * 128 + (((4 * hq + k) ^ (r & 7)) << 4));
           rope4(lo, hi, rc, rs);
         }
         *f32_chunk(kf, r, 4 * hq + k) = lo;
@@ -893,9 +898,28 @@ int launch_attn_short(const AttnArgs &a, cudaStream_t st) {
       return IG_ERR_CUDA;
     mapw = map;
   }
+  // The RoPE factor rows of positions 0..127 ([rows][32] f32, SWIZZLE_128B),
+  // staged by the projecting kernel.
+  CUtensorMap mcos = map, msin = map;
+  if (proj && a.rope_cos) {
+    auto enc = get_encode_fn();
+    if (!enc) return IG_ERR_CUDA;
+    cuuint64_t dims[2] = {32, (cuuint64_t)a.max_len};
+    cuuint64_t strides[1] = {32 * sizeof(float)};
+    cuuint32_t box[2] = {32, (cuuint32_t)kShortN};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(&mcos, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_cos), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&msin, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.rope_sin), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return IG_ERR_CUDA;
+  }
   auto kern = proj ? attn_short_kernel<true> : attn_short_kernel<false>;
   static SmemOptIn attr_plain, attr_proj;
-  if ((proj ? attr_proj : attr_plain).ensure((const void *)kern, AttnShortSmem::kTotal) != cudaSuccess)
+  const int smem = proj ? AttnShortSmem::kTotalProj : AttnShortSmem::kTotal;
+  if ((proj ? attr_proj : attr_plain).ensure((const void *)kern, smem) != cudaSuccess)
     return IG_ERR_CUDA;
   if (a.xq) {
     if (!attn_short_quantizes(a)) return IG_ERR_UNSUPPORTED;
@@ -903,7 +927,7 @@ int launch_attn_short(const AttnArgs &a, cudaStream_t st) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(a.nseq, a.nh);
     cfg.blockDim = dim3(kShortThreads);
-    cfg.dynamicSmemBytes = AttnShortSmem::kTotal;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
@@ -912,14 +936,14 @@ int launch_attn_short(const AttnArgs &a, cudaStream_t st) {
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, map, mapw, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos,
+    if (cudaLaunchKernelEx(&cfg, kern, map, mapw, mcos, msin, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos,
                            a.rope_sin, a.ctx, a.xq, a.ldq, a.sa, a.xa_s, a.wsb, a.wzc) != cudaSuccess)
       return IG_ERR_CUDA;
     return 0;
   }
   if (proj) return IG_ERR_UNSUPPORTED;
   attn_short_kernel<false><<<dim3(a.nseq, a.nh), kShortThreads, AttnShortSmem::kTotal, st>>>(
-      map, mapw, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos, a.rope_sin, a.ctx, nullptr, 0, nullptr,
+      map, mapw, map, map, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos, a.rope_sin, a.ctx, nullptr, 0, nullptr,
       nullptr, nullptr, nullptr);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
