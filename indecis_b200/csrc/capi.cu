@@ -605,11 +605,17 @@ void release_ws(ig_model *m, Workspace *w, cudaStream_t st, bool capturing) {
 // Uploads the plan's metadata (offsets, query blocks, and optionally the host
 // ids) through the pinned staging, one copy per device region, and fills the
 // row -> sequence and position tables on the device from the offsets.
+// memcpy(dst, src, n) split over the host copy pool's threads (CopyPool).
+void host_copy(char *dst, const char *src, size_t n);
+
 int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream_t st, bool capturing = false) {
   char *h = reinterpret_cast<char *>(w.host);
   size_t off = 0;
   auto put = [&](const void *src, size_t bytes) {
-    std::memcpy(h + off, src, bytes);
+    if (bytes >= (512u << 10))
+      host_copy(h + off, static_cast<const char *>(src), bytes);
+    else
+      std::memcpy(h + off, src, bytes);
     off += bytes;
   };
   put(p.offs.data(), sizeof(int32_t) * (p.nseq + 1));
@@ -993,9 +999,18 @@ int run_heads(ig_model *m, Workspace &w, const Plan &p, cudaStream_t st, double 
 }
 
 int check_ids(const ig_model *m, const int32_t *ids, int64_t N) {
-  for (int64_t t = 0; t < N; t++)
-    if (ids[t] < 0 || ids[t] >= m->cfg.vocab)
-      return fail(IG_ERR_OUT_OF_VOCAB, "modernbert: id " + std::to_string(ids[t]) + " out of vocabulary");
+  // Blocks of ids tested without a branch (a vectorizable OR of unsigned
+  // compares); the first bad id is looked for only in a block that has one.
+  const uint32_t vocab = (uint32_t)m->cfg.vocab;
+  for (int64_t t0 = 0; t0 < N; t0 += 4096) {
+    const int64_t t1 = std::min<int64_t>(N, t0 + 4096);
+    uint32_t bad = 0;
+    for (int64_t t = t0; t < t1; t++) bad |= (uint32_t)((uint32_t)ids[t] >= vocab);
+    if (bad)
+      for (int64_t t = t0; t < t1; t++)
+        if (ids[t] < 0 || ids[t] >= m->cfg.vocab)
+          return fail(IG_ERR_OUT_OF_VOCAB, "modernbert: id " + std::to_string(ids[t]) + " out of vocabulary");
+  }
   return 0;
 }
 
@@ -1069,6 +1084,8 @@ class CopyPool {
   std::deque<Job> jobs_;
 };
 
+void host_copy(char *dst, const char *src, size_t n) { CopyPool::get().copy(dst, src, n); }
+
 struct OutCopy {
   const void *src;  // device
   void *dst;        // host
@@ -1134,7 +1151,7 @@ int copy_out_staged(Workspace &w, cudaStream_t st, const std::vector<OutCopy> &o
 // copied out on the workspace's copy stream as soon as they exist, so the
 // copies overlap the later chunks' kernels; then the pooling, the pooled
 // heads and their copy. Returns once every output is in the caller's memory.
-constexpr int kTailChunks = 4;
+constexpr int kTailChunks = 8;
 constexpr int kTailMinRows = 16384;
 
 int run_tail_staged(ig_model *m, Workspace &w, const Plan &p, int mode, cudaStream_t st, double *logits, double *tlog,
