@@ -394,7 +394,13 @@ NCU_BYTES_PER_SEQ = {
 }
 
 
-def roofline(report, pk, nseq, workload="c1"):
+# Warp instructions of one launch per sequence (smsp__inst_executed.sum of the
+# capture in profiles/attn_qkv_c1_512seq.txt).
+NCU_INST_PER_SEQ = {"attn_qkv_quant": 67596273 / 512}
+B200_SMS = 148
+
+
+def roofline(report, pk, nseq, workload="c1", sm_mhz=None):
     ks = [k for k in report["kernels"] if k["records"] > 0 and k["ms"] > 0]
     top = max(ks, key=lambda k: k["ms"])
     total_ms = sum(k["ms"] for k in ks)
@@ -417,6 +423,14 @@ def roofline(report, pk, nseq, workload="c1"):
     per_seq = NCU_BYTES_PER_SEQ.get(top["name"]) if workload == "c1" else None
     rf["traffic"] = per_seq * nseq if per_seq else None
     rf["traffic_source"] = "ncu dram bytes at 512 sequences, scaled" if per_seq else None
+    # The bound these kernels meet first: instruction issue. Warp instructions
+    # per launch from the same ncu capture, scaled by the sequences, over the
+    # SMs' issue capacity (4 schedulers x the clock seen) in the launch's time.
+    inst = NCU_INST_PER_SEQ.get(top["name"]) if workload == "c1" else None
+    if inst and sm_mhz:
+        cap = B200_SMS * 4 * sm_mhz * 1e6 * per_ms * 1e-3
+        rf["issue"] = {"warp_instructions": inst * nseq, "frac": inst * nseq / cap, "sm_mhz": sm_mhz,
+                       "source": "smsp__inst_executed.sum at 512 sequences (ncu), scaled; 148 SMs x 4 issue slots"}
     return rf
 
 
@@ -689,7 +703,7 @@ def run_ours(args, world, rank, local):
             cfg_obj["path"] = "float32 (SetInt8(false)): float products in the reference's FMA-chain order"
             rf = c5_roofline(report, pk, clk["sm_mhz"] if clk else None, fp32_names=F32_PATH_KERNELS)[0]
         else:
-            rf = roofline(report, pk, nseq, spec["name"])
+            rf = roofline(report, pk, nseq, spec["name"], clk["sm_mhz"] if clk else None)
         line = {"metric": spec["metric"], "value": value, "unit": "seq/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32" if f32 else "int8", "data": "synthetic",
