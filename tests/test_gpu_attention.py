@@ -54,6 +54,21 @@ def test_attention_long_global(igdev, oracle_lib):
     assert np.array_equal(ctx.view(np.uint32), ref.view(np.uint32))
 
 
+def test_attention_long_ragged(igdev, oracle_lib):
+    """Global layers over sequences of 2048 tokens or more with ragged
+    lengths (partial statistics stages and quantization tiles, a sequence end
+    inside a key tile), beside a short sequence."""
+    from indecis_b200 import ops
+    H, nh = 128, 2
+    lens = [2049, 3, 2222]
+    qkv, offs = _qkv(lens, H, nh, seed=29)
+    ref = _ref(oracle_lib, qkv, offs, H, nh, -1)
+    ctx = ops.attention(torch.from_numpy(qkv).cuda(), H, nh, offs, -1).cpu().numpy()
+    assert not np.isnan(ctx).any()
+    bad = np.argwhere(ctx.view(np.uint32) != ref.view(np.uint32))
+    assert len(bad) == 0, f"{len(np.unique(bad[:, 0]))} rows differ, first {bad[:3].tolist()}"
+
+
 def test_attention_accuracy_vs_float(igdev):
     """TestAttend8 bounds: relative error <= 0.03, worst <= 0.25 vs float64."""
     from indecis_b200 import ops

@@ -87,6 +87,23 @@ def test_c3_full_long(igdev, oracle_lib):
                           _bits(om.encode(ids, offs, mode=1, threads=t, fast=True)))
 
 
+def test_c3_long_ragged(igdev, oracle_lib):
+    """Sequences of 2048 tokens or more whose lengths are not multiples of the
+    128-row statistics stages or of the 64-row quantization tiles (the
+    statistics split by RoPE pair, a partial last stage and tile), beside a
+    short one, through the whole C1 model with RoPE."""
+    from indecis_b200 import synthetic as S
+    om, gm = _models(S.C1)
+    rng = np.random.default_rng(5)
+    lens = [2049, 3001, 7, 2300]
+    offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    ids = rng.integers(0, S.C1["vocab"], size=int(offs[-1])).astype(np.int32)
+    t = _host_threads()
+    assert np.array_equal(_bits(gm.EncodeSeqs((ids, offs))), _bits(om.encode(ids, offs, threads=t, fast=True)))
+    assert np.array_equal(_bits(gm.EncodeTokens((ids, offs))),
+                          _bits(om.encode(ids, offs, mode=1, threads=t, fast=True)))
+
+
 def test_c3_full_varlen(igdev, oracle_lib):
     from indecis_b200 import synthetic as S
     om, gm = _models(S.C1)
