@@ -116,6 +116,67 @@ __device__ __forceinline__ uint4 *tile_chunk(uint8_t *base, int r, int c) {
   return reinterpret_cast<uint4 *>(base + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
+
+// The rare branches of the row quantizations (a NaN in the row, or a scale
+// that is not a normal float) out of line, so that the kernel's hot code
+// stays small: the reference's conversion, byte by byte.
+struct Words8 {
+  uint32_t w[8];
+  int sum;  // quant32_s8_slow: the running sum
+};
+struct Vals32 {
+  float4 v[8];
+};
+// Bytes q + 128 of 32 values.
+__device__ __noinline__ Words8 quant32_u8_slow(Vals32 x, float inv) {
+  Words8 r;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const float4 a = x.v[k];
+    r.w[k] = pack_low_bytes(quant_bits(__fmul_rn(a.x, inv)) + 128u, quant_bits(__fmul_rn(a.y, inv)) + 128u,
+                            quant_bits(__fmul_rn(a.z, inv)) + 128u, quant_bits(__fmul_rn(a.w, inv)) + 128u);
+  }
+  return r;
+}
+// int8 bytes of 32 values and sum plus their unclamped conversions.
+__device__ __noinline__ Words8 quant32_s8_slow(Vals32 x, float inv, int sum) {
+  Words8 r;
+  int s = sum;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const float4 a = x.v[k];
+    const float e[4] = {a.x, a.y, a.z, a.w};
+    uint32_t b[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int q = rne_int(__fmul_rn(e[u], inv));
+      s += q;
+      b[u] = (uint32_t)max(-128, min(127, q));
+    }
+    r.w[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
+  }
+  r.sum = s;
+  return r;
+}
+// int8 bytes of 32 values with a scale per value (V's column scales).
+__device__ __noinline__ Words8 quant32_s8_cols_slow(Vals32 x, Vals32 inv) {
+  Words8 r;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const float4 a = x.v[k], i = inv.v[k];
+    r.w[k] = pack_low_bytes(quant_bits(__fmul_rn(a.x, i.x)), quant_bits(__fmul_rn(a.y, i.y)),
+                            quant_bits(__fmul_rn(a.z, i.z)), quant_bits(__fmul_rn(a.w, i.w)));
+  }
+  r.sum = 0;
+  return r;
+}
+__device__ __forceinline__ Vals32 vals32(const float (&v)[32]) {
+  Vals32 x;
+#pragma unroll
+  for (int k = 0; k < 8; k++) x.v[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  return x;
+}
+
 // rotate_half RoPE of the pair (x1, x2) = (x[i], x[i+32]) (linalg/vec_simd.go
 // Rope: separate roundings, no FMA).
 __device__ __forceinline__ void rope1(float &x1, float &x2, float c, float s) {
@@ -349,13 +410,9 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
       for (int k = 0; k < 8; k++)
         qw[k] = quant4_fast(qv[4 * k], qv[4 * k + 1], qv[4 * k + 2], qv[4 * k + 3], f2(qinv), f2(qinv));
     } else {
+      const Words8 r8 = quant32_u8_slow(vals32(qv), qinv);
 #pragma unroll
-      for (int k = 0; k < 8; k++) {
-        uint32_t b[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) b[u] = quant_bits(__fmul_rn(qv[4 * k + u], qinv)) + 128u;
-        qw[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
-      }
+      for (int k = 0; k < 8; k++) qw[k] = r8.w[k];
     }
     if (hq == 0) s_sq[r] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
     // K|V: columns 0-63 K, 64-127 V.
@@ -478,13 +535,9 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
         for (int k = 0; k < 8; k++)
           qw[k] = quant4_fast(qv[4 * k], qv[4 * k + 1], qv[4 * k + 2], qv[4 * k + 3], f2(qinv), f2(qinv));
       } else {
+        const Words8 r8 = quant32_u8_slow(vals32(qv), qinv);
   #pragma unroll
-        for (int k = 0; k < 8; k++) {
-          uint32_t b[4];
-  #pragma unroll
-          for (int u = 0; u < 4; u++) b[u] = quant_bits(__fmul_rn(qv[4 * k + u], qinv)) + 128u;
-          qw[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
-        }
+        for (int k = 0; k < 8; k++) qw[k] = r8.w[k];
       }
       if (hh == 0) s_sq[rr] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
     }
@@ -552,23 +605,31 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
     const int vr = tid - 128;
     const bool vfast = *s_vfast != 0;
     uint32_t vw[16];
+    if (vfast) {
 #pragma unroll
-    for (int c = 0; c < 8; c++) {
-      float4 lo = make_float4(0.0f, 0.0f, 0.0f, 0.0f), hi = lo;
-      if (vr < n) {
-        lo = *f32_chunk(vf, vr, c);
-        hi = *f32_chunk(vf, vr, 8 + c);
-      }
-      const float4 il = *reinterpret_cast<const float4 *>(s_vinv + 4 * c);
-      const float4 ih = *reinterpret_cast<const float4 *>(s_vinv + 32 + 4 * c);
-      if (vfast) {
+      for (int c = 0; c < 8; c++) {
+        float4 lo = make_float4(0.0f, 0.0f, 0.0f, 0.0f), hi = lo;
+        if (vr < n) {
+          lo = *f32_chunk(vf, vr, c);
+          hi = *f32_chunk(vf, vr, 8 + c);
+        }
+        const float4 il = *reinterpret_cast<const float4 *>(s_vinv + 4 * c);
+        const float4 ih = *reinterpret_cast<const float4 *>(s_vinv + 32 + 4 * c);
         vw[c] = quant4_fast_s8(lo.x, lo.y, lo.z, lo.w, make_float2(il.x, il.y), make_float2(il.z, il.w));
         vw[8 + c] = quant4_fast_s8(hi.x, hi.y, hi.z, hi.w, make_float2(ih.x, ih.y), make_float2(ih.z, ih.w));
-      } else {
-        vw[c] = pack_low_bytes(quant_bits(__fmul_rn(lo.x, il.x)), quant_bits(__fmul_rn(lo.y, il.y)),
-                               quant_bits(__fmul_rn(lo.z, il.z)), quant_bits(__fmul_rn(lo.w, il.w)));
-        vw[8 + c] = pack_low_bytes(quant_bits(__fmul_rn(hi.x, ih.x)), quant_bits(__fmul_rn(hi.y, ih.y)),
-                                   quant_bits(__fmul_rn(hi.z, ih.z)), quant_bits(__fmul_rn(hi.w, ih.w)));
+      }
+    } else {  // dimensions 0-31, then 32-63, each with its column's scale
+#pragma unroll
+      for (int half = 0; half < 2; half++) {
+        Vals32 x, inv;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          x.v[c] = vr < n ? *f32_chunk(vf, vr, 8 * half + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          inv.v[c] = *reinterpret_cast<const float4 *>(s_vinv + 32 * half + 4 * c);
+        }
+        const Words8 r8 = quant32_s8_cols_slow(x, inv);
+#pragma unroll
+        for (int c = 0; c < 8; c++) vw[8 * half + c] = r8.w[c];
       }
     }
     named_barrier_sync(3, 128);  // every f32 V row has been read
@@ -626,17 +687,10 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
       }
       ksum += ks2;
     } else {  // the reference's conversion (NaN -> INT_MIN, summed before the clamp)
+      const Words8 r8 = quant32_s8_slow(vals32(kv), kinv, ksum);
 #pragma unroll
-      for (int k = 0; k < 8; k++) {
-        uint32_t b[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int x = rne_int(__fmul_rn(kv[4 * k + u], kinv));
-          ksum += x;
-          b[u] = (uint32_t)max(-128, min(127, x));
-        }
-        kw[k] = pack_low_bytes(b[0], b[1], b[2], b[3]);
-      }
+      for (int k = 0; k < 8; k++) kw[k] = r8.w[k];
+      ksum = r8.sum;
     }
     ksum += __shfl_xor_sync(0xffffffffu, ksum, 1);
     if (hh == 0) {
@@ -793,21 +847,21 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
     }
     const bool fast = !has_nan && row_scale_normal(qs), store = ok && valid;
     uint4 *dst = reinterpret_cast<uint4 *>(xq + (size_t)(t0 + r) * ldq + h * 64 + 32 * g);
+    uint32_t wv[8];
+    if (mx == 0.0f) {
 #pragma unroll
-    for (int hf = 0; hf < 2; hf++) {
-      uint32_t wv[4];
+      for (int k = 0; k < 8; k++) wv[k] = 0x80808080u;
+    } else if (fast) {
 #pragma unroll
-      for (int k = 0; k < 4; k++) {
-        const float *x4 = v + 16 * hf + 4 * k;
-        if (mx == 0.0f)
-          wv[k] = 0x80808080u;
-        else if (fast)
-          wv[k] = quant4_fast(x4[0], x4[1], x4[2], x4[3], f2(qinv), f2(qinv));
-        else
-          wv[k] = quant_byte_slow(x4[0], qinv) | (quant_byte_slow(x4[1], qinv) << 8) |
-                  (quant_byte_slow(x4[2], qinv) << 16) | (quant_byte_slow(x4[3], qinv) << 24);
-      }
-      if (store) dst[hf] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      for (int k = 0; k < 8; k++) wv[k] = quant4_fast(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3], f2(qinv), f2(qinv));
+    } else {
+      const Words8 r8 = quant32_u8_slow(vals32(v), qinv);
+#pragma unroll
+      for (int k = 0; k < 8; k++) wv[k] = r8.w[k];
+    }
+    if (store) {
+      dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
     }
     if (store && h == 0 && g == 0) sa[t0 + r] = qs;
     if (warp == 1) {
