@@ -384,7 +384,7 @@ def shift(ids, offs, s0):
 # launch processes the whole step's sequences, so the per-launch traffic is
 # this times the sequences per step (traffic grows with the sequences).
 NCU_BYTES_PER_SEQ = {
-    "attn_qkv_quant": (21576192 + 0) / 512,
+    "attn_qkv_quant": (21564416 + 2816000) / 512,
     "attn_short": (201441536 + 38391040) / 512,
     "attn_short_quant": (201448192 + 11332864) / 512,
     "gemm_qkv": (21466368 + 145374976) / 512,
@@ -396,7 +396,7 @@ NCU_BYTES_PER_SEQ = {
 
 # Warp instructions of one launch per sequence (smsp__inst_executed.sum of the
 # capture in profiles/attn_qkv_c1_512seq.txt).
-NCU_INST_PER_SEQ = {"attn_qkv_quant": 67596273 / 512}
+NCU_INST_PER_SEQ = {"attn_qkv_quant": 66996374 / 512}
 B200_SMS = 148
 
 
