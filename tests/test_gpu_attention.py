@@ -69,6 +69,63 @@ def test_attention_long_ragged(igdev, oracle_lib):
     assert len(bad) == 0, f"{len(np.unique(bad[:, 0]))} rows differ, first {bad[:3].tolist()}"
 
 
+def _special(qkv, offs, H, cases):
+    """Plants the named special values: Q, K, V rows of the first sequence
+    and small rows of the second."""
+    a, b = int(offs[0]), int(offs[1])
+    plant = {
+        "q_nan": lambda: qkv.__setitem__((a + 3, 5), np.nan),
+        "v_inf": lambda: qkv.__setitem__((a + 11, 2 * H + 200), -np.inf),
+        "v_nan": lambda: qkv.__setitem__((a + 13, 2 * H + 10), np.nan),
+        "zero_rows": lambda: (qkv.__setitem__((a + 15, slice(0, H)), 0.0),
+                              qkv.__setitem__((a + 16, slice(H, 2 * H)), 0.0),
+                              qkv.__setitem__((a + 17, slice(2 * H, 3 * H)), 0.0)),
+        "tiny_scales": lambda: (qkv.__setitem__((b + 2, slice(0, H)), qkv[b + 2, 0:H] * 1e-40),
+                                qkv.__setitem__((b + 4, slice(H, 2 * H)), qkv[b + 4, H:2 * H] * 1e-40)),
+        "k_nan": lambda: qkv.__setitem__((a + 7, H + 70), np.nan),
+        "k_inf": lambda: qkv.__setitem__((a + 9, H + 130), np.inf),
+    }
+    for c in cases:
+        plant[c]()
+
+
+def _compare_special(oracle_lib, lens, cases):
+    from indecis_b200 import ops
+    H, nh = 256, 4
+    qkv, offs = _qkv(lens, H, nh, seed=sum(lens) + 5)
+    _special(qkv, offs, H, cases)
+    ref = _ref(oracle_lib, qkv, offs, H, nh, -1)
+    ctx = ops.attention(torch.from_numpy(qkv).cuda(), H, nh, offs, -1).cpu().numpy()
+    assert np.array_equal(np.isnan(ctx), np.isnan(ref))
+    ok = ~np.isnan(ref)
+    bad = np.argwhere(ctx.view(np.uint32)[ok] != ref.view(np.uint32)[ok])
+    assert len(bad) == 0, f"{len(bad)} values differ"
+
+
+@pytest.mark.parametrize("lens", [[96, 128, 17], [300, 129, 5]])
+def test_attention_special_values(igdev, oracle_lib, lens):
+    """Rows that take the rare quantization branches (sequences up to 128
+    tokens and longer ones): a Q row holding a NaN, a NaN and an infinity in V
+    columns, all-zero Q, K and V rows, and Q and K rows so small that their
+    scale max/127 is subnormal; every output bit as the oracle's (NaN where it
+    has NaN)."""
+    _compare_special(oracle_lib, lens, ["q_nan", "v_inf", "v_nan", "zero_rows", "tiny_scales"])
+
+
+@pytest.mark.xfail(strict=True, reason="non-finite K values: the reference's NaN-keeping ExpShift clamp, INT_MIN "
+                                       "terms in the P sum and 128*sum corrections beyond 2^22 are not reproduced")
+@pytest.mark.parametrize("case", ["k_nan", "k_inf"])
+def test_attention_nonfinite_keys(igdev, oracle_lib, case):
+    """A NaN or an infinity in a K row makes the K column mean non-finite, so
+    every key of that (sequence, head) takes the clamped conversion with
+    INT_MIN in its sum (a 128*sum correction far beyond 2^22, which the
+    kernels' exact integer-to-float shortcut assumes) and the scores can be
+    NaN (which the reference's ExpShift keeps through its clamp and its P
+    quantization adds to the row sum as INT_MIN). The kernels differ from the
+    reference for that (sequence, head); every other output agrees."""
+    _compare_special(oracle_lib, [96, 128, 17], [case])
+
+
 def test_attention_accuracy_vs_float(igdev):
     """TestAttend8 bounds: relative error <= 0.03, worst <= 0.25 vs float64."""
     from indecis_b200 import ops
