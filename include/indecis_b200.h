@@ -217,10 +217,18 @@ IG_API int ig_logits_device(ig_model *m, const int32_t *d_ids, const int64_t *of
  * encoder launch with CUDA events on its stream (outside stream capture);
  * ig_profile(0) stops. ig_profile_report synchronizes the device and writes
  * a JSON summary {"launches": total kernel launches since ig_profile(1),
+ * "graphs_recorded", "graph_runs": CUDA graphs recorded and launched by host
+ * calls since the library loaded (a host call of at most 16384 tokens whose
+ * offsets, mode and outputs repeat the previous call's on the same workspace
+ * replays its kernels as one graph; none while profiling),
  * "kernels": [{name, launches, ms, bytes, ops}]} where bytes and ops are the
  * launches' algorithmic memory traffic and arithmetic; returns its length. */
 IG_API int ig_profile(int32_t enable);
 IG_API int64_t ig_profile_report(char *buf, size_t len);
+/* Restricts the events of ig_profile to the launches recorded under `name`
+ * (a "kernels" name of the report; NULL or "": every launch), so that a timed
+ * run carries events around one kernel only. Call it between runs. */
+IG_API int ig_profile_only(const char *name);
 
 /* Message of the calling thread's last failure ("" if none). */
 IG_API const char *ig_last_error(void);

@@ -32,7 +32,8 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_batcher_create_fn", "ig_batcher_destroy", "ig_batcher_encode", "ig_batcher_stats",
            "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags", "ig_model_set_int8",
            "ig_check_gelu_division", "ig_model_create_multi", "ig_model_replica", "ig_model_device_count",
-           "ig_model_create_stored", "ig_model_create_stored_multi", "ig_device_count", "ig_gemm_geglu_quant"]
+           "ig_model_create_stored", "ig_model_create_stored_multi", "ig_device_count", "ig_gemm_geglu_quant",
+           "ig_profile_only"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -189,6 +190,7 @@ def load() -> C.CDLL:
     L.ig_batcher_encode.argtypes = [vp, vp, vp, i32, vp, C.c_size_t]
     L.ig_batcher_stats.argtypes = [vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]
     L.ig_profile.argtypes = [i32]
+    L.ig_profile_only.argtypes = [C.c_char_p]
     L.ig_profile_report.argtypes = [C.c_char_p, C.c_size_t]
     L.ig_profile_report.restype = C.c_int64
     _lib = L
@@ -207,6 +209,11 @@ class IgError(RuntimeError):
 
 def profile(enable: bool):
     check(load().ig_profile(1 if enable else 0))
+
+
+def profile_only(name: str | None):
+    """Events around the launches recorded under `name` only (None: every launch)."""
+    check(load().ig_profile_only(name.encode() if name else None))
 
 
 def profile_report() -> dict:

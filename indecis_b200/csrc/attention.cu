@@ -87,6 +87,8 @@ __global__ void __launch_bounds__(256)
   extern __shared__ __align__(16) float st_smem[];  // [stages][K 32x64, V 32x64, cos 32x32, sin 32x32]
   __shared__ float s_vmax[3][64];
   const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  dep_wait();
+  dep_trigger();
   const int t0 = offs[s], n = offs[s + 1] - t0;
   const size_t ld = 3 * (size_t)H;
   const float *kbase = qkv + (size_t)t0 * ld + H + h * 64;
@@ -208,6 +210,7 @@ __global__ void __launch_bounds__(kPgThreads)
   uint64_t *empty = rotd + STAGES;
   float *vred = reinterpret_cast<float *>(empty + STAGES);  // [kPgRotWarps][2P]
   const int s = blockIdx.x, h = blockIdx.y, pg = blockIdx.z;
+  dep_wait();
   const int t0 = offs[s], n = offs[s + 1] - t0;
   const int nst = (n + SR - 1) / SR;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -321,6 +324,7 @@ __global__ void __launch_bounds__(kPgThreads)
       vinv[o] = mx > 0.0f ? __fdiv_rn(1.0f, scv) : 0.0f;
     }
   }
+  dep_trigger();  // one wave of long-lived CTAs: the next kernel is let in at the end
 }
 
 // attn_quant_kernel for D = 64 with one warp per row over all its heads: the
@@ -337,6 +341,8 @@ __global__ void __launch_bounds__(256)
                         float *__restrict__ sq, int8_t *__restrict__ kq, float *__restrict__ ks,
                         float *__restrict__ kzc, int8_t *__restrict__ vq) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  dep_wait();
+  dep_trigger();
   if (row >= N) return;
   const int s = row_seq[row];
   float c = 1.0f, sn = 0.0f;
@@ -441,6 +447,8 @@ __global__ void __launch_bounds__(2 * kQtRows)
   float *s_km = reinterpret_cast<float *>(sm + 8 * kBox);  // [64] K column means
   float *s_vi = s_km + 64;                                  // [64] V inverse scales
   uint64_t *bar = reinterpret_cast<uint64_t *>(s_vi + 64);
+  dep_wait();
+  dep_trigger();
   const int2 tile = tiles[blockIdx.x];
   const int s = tile.x, i0 = tile.y, h = blockIdx.y;
   const int t0 = offs[s], n = offs[s + 1] - t0;
@@ -1106,8 +1114,10 @@ static int launch_stats_pg(const AttnArgs &a, cudaStream_t st) {
   static SmemOptIn at_r, at_n;
   auto kern = a.rope_cos ? attn_stats_pg_kernel<P, SR, STAGES, true> : attn_stats_pg_kernel<P, SR, STAGES, false>;
   if ((a.rope_cos ? at_r : at_n).ensure((const void *)kern, smem) != cudaSuccess) return IG_ERR_CUDA;
-  kern<<<dim3(a.nseq, a.nh, 32 / P), kPgThreads, smem, st>>>(mq, mc, ms, a.offs, a.H, a.nh, a.kmean, a.vs, a.vinv);
-  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  return launch_dep(kern, dim3(a.nseq, a.nh, 32 / P), kPgThreads, smem, st, mq, mc, ms, a.offs, a.H, a.nh, a.kmean,
+                    a.vs, a.vinv) == cudaSuccess
+             ? 0
+             : IG_ERR_CUDA;
 }
 
 // IG_ATTN_QUANT_TILE=0 keeps the warp-per-row quantization (the same bits;
@@ -1154,15 +1164,16 @@ static int launch_quant64(const AttnArgs &a, cudaStream_t st) {
     static SmemOptIn at_r, at_n;
     auto kern = a.rope_cos ? attn_quant_tile_kernel<true> : attn_quant_tile_kernel<false>;
     if ((a.rope_cos ? at_r : at_n).ensure((const void *)kern, smem) != cudaSuccess) return IG_ERR_CUDA;
-    kern<<<dim3(a.nrow_tiles, a.nh), 2 * kQtRows, smem, st>>>(mq, mc, ms, a.row_tiles, a.offs, a.N, a.H, a.nh,
-                                                               a.scale, a.kmean, a.vinv, a.qa, a.sq, a.kq, a.ks,
-                                                               a.kzc, a.vq);
-    return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+    return launch_dep(kern, dim3(a.nrow_tiles, a.nh), 2 * kQtRows, smem, st, mq, mc, ms, a.row_tiles, a.offs, a.N,
+                      a.H, a.nh, a.scale, a.kmean, a.vinv, a.qa, a.sq, a.kq, a.ks, a.kzc, a.vq) == cudaSuccess
+               ? 0
+               : IG_ERR_CUDA;
   }
-  attn_quant64_kernel<<<(unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st>>>(
-      a.qkv, a.row_seq, a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq, a.kq,
-      a.ks, a.kzc, a.vq);
-  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  return launch_dep(attn_quant64_kernel, (unsigned)(((long long)a.N * 32 + 255) / 256), 256, 0, st, a.qkv, a.row_seq,
+                    a.offs, a.N, a.H, a.nh, a.scale, a.rope_cos, a.rope_sin, a.kmean, a.vinv, a.qa, a.sq, a.kq, a.ks,
+                    a.kzc, a.vq) == cudaSuccess
+             ? 0
+             : IG_ERR_CUDA;
 }
 
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
@@ -1195,9 +1206,9 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
                      : (a.rope_cos ? attn_stats64_kernel<3, true> : attn_stats64_kernel<3, false>);
     if (attr[(deep ? 2 : 0) + (a.rope_cos ? 1 : 0)].ensure((const void *)kern, smem) != cudaSuccess)
       return IG_ERR_CUDA;
-    kern<<<dim3(a.nseq, a.nh), 256, smem, st>>>(a.qkv, a.offs, a.H, a.nh, a.rope_cos, a.rope_sin, a.kmean, a.vs,
-                                                 a.vinv);
-    if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+    if (launch_dep(kern, dim3(a.nseq, a.nh), 256, smem, st, a.qkv, a.offs, a.H, a.nh, a.rope_cos, a.rope_sin, a.kmean,
+                   a.vs, a.vinv) != cudaSuccess)
+      return IG_ERR_CUDA;
     return launch_quant64(a, st);
   }
   if (a.nseq > 0 && a.N > 0 && a.D <= 128 && (a.D % 4) == 0 && a.V >= 1) {

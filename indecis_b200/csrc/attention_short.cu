@@ -262,6 +262,7 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
   volatile int *s_vfast = reinterpret_cast<volatile int *>(smem + S::kTmem + 4);
 
   const int s = blockIdx.x, h = blockIdx.y;
+  dep_wait();
   const int t0 = offs[s];
   const int n = offs[s + 1] - t0;
   if (n <= 0) return;
@@ -309,6 +310,7 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
     tc_fence_before();
     __syncthreads();  // barriers initialised, TMEM allocated
     tc_fence_after();
+    dep_trigger();
     const uint32_t tm = *tmem_slot;
     const uint32_t trow = tm + ((uint32_t)(q4 * 32) << 16);
     const uint32_t a_base = smem_u32(smem + S::kA), b_base = smem_u32(smem + S::kB);
@@ -542,6 +544,7 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
       if (hh == 0) s_sq[rr] = qmx > 0.0f ? __fmul_rn(qs, scale) : 0.0f;
     }
     __syncthreads();  // barriers initialised
+    dep_trigger();
     ok = mbar_wait(bar_load, 0, kDevTimeoutFull);
 
     // A. K rotated in place (the RoPE factors are read again; they are cached).
@@ -983,23 +986,25 @@ int launch_attn_short(const AttnArgs &a, cudaStream_t st) {
     cfg.blockDim = dim3(kShortThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 1;
     at[0].val.clusterDim.y = a.nh;
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
+    add_dep_attr(at, cfg.numAttrs);
     if (cudaLaunchKernelEx(&cfg, kern, map, mapw, mcos, msin, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos,
                            a.rope_sin, a.ctx, a.xq, a.ldq, a.sa, a.xa_s, a.wsb, a.wzc) != cudaSuccess)
       return IG_ERR_CUDA;
     return 0;
   }
   if (proj) return IG_ERR_UNSUPPORTED;
-  attn_short_kernel<false><<<dim3(a.nseq, a.nh), kShortThreads, AttnShortSmem::kTotal, st>>>(
-      map, mapw, map, map, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos, a.rope_sin, a.ctx, nullptr, 0, nullptr,
-      nullptr, nullptr, nullptr);
-  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  return launch_dep(attn_short_kernel<false>, dim3(a.nseq, a.nh), kShortThreads, AttnShortSmem::kTotal, st, map,
+                    mapw, map, map, a.qkv, a.offs, a.H, a.nh, a.window, a.V, a.scale, a.rope_cos, a.rope_sin, a.ctx,
+                    nullptr, 0, nullptr, nullptr, nullptr, nullptr) == cudaSuccess
+             ? 0
+             : IG_ERR_CUDA;
 }
 
 // The row quantization needs the whole row in one cluster (nh <= 8 CTAs, a

@@ -254,6 +254,7 @@ __global__ void __launch_bounds__(kAtThreads, 2)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::kTmem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  dep_wait();
   const int4 blk = blocks[blockIdx.x];
   if (blk.w > 2) return;  // a longer key range: attn_tc_long_kernel
   const int s = blk.x, i0 = blk.y, c0 = blk.z, nkt = blk.w;
@@ -283,6 +284,7 @@ __global__ void __launch_bounds__(kAtThreads, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  dep_trigger();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -459,6 +461,7 @@ __global__ void __launch_bounds__(kAtThreads, 2)
   using S = AttnLongSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  dep_wait();
   const int4 blk = blocks[blockIdx.x];
   if (blk.w <= 2) return;  // attn_tc_kernel's block
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem + S::kBar);
@@ -503,6 +506,7 @@ __global__ void __launch_bounds__(kAtThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  dep_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -758,14 +762,15 @@ int launch_attend_tc(const AttnArgs &a, const int4 *d_blocks, int nshort, int nl
       attr_long.ensure((const void *)attn_tc_long_kernel, AttnLongSmem::kTotal) != cudaSuccess)
     return IG_ERR_CUDA;
   if (nshort > 0) {
-    attn_tc_kernel<<<dim3(nshort, a.nh), kAtThreads, AttnTcSmem::kTotal, st>>>(
-        mq, mk, mv, d_blocks, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx);
-    if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+    if (launch_dep(attn_tc_kernel, dim3(nshort, a.nh), kAtThreads, AttnTcSmem::kTotal, st, mq, mk, mv, d_blocks,
+                   a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx) != cudaSuccess)
+      return IG_ERR_CUDA;
   }
   if (nlong > 0) {
-    attn_tc_long_kernel<<<dim3(nlong, a.nh), kAtThreads, AttnLongSmem::kTotal, st>>>(
-        mq, mk, mv, d_blocks + nshort, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx);
-    if (cudaGetLastError() != cudaSuccess) return IG_ERR_CUDA;
+    if (launch_dep(attn_tc_long_kernel, dim3(nlong, a.nh), kAtThreads, AttnLongSmem::kTotal, st, mq, mk, mv,
+                   d_blocks + nshort, a.offs, a.N, a.H, a.nh, a.window, a.V, a.sq, a.ks, a.kzc, a.vs, a.ctx) !=
+        cudaSuccess)
+      return IG_ERR_CUDA;
   }
   return 0;
 }

@@ -81,6 +81,7 @@ struct ProfRec {
 struct Profiler {
   std::mutex mu;
   bool on = false;
+  std::string only;  // when set, only launches recorded under this name get events
   std::vector<ProfRec> recs;
   std::vector<cudaEvent_t> pool;
   cudaEvent_t get() {
@@ -97,6 +98,8 @@ struct Profiler {
 };
 static Profiler g_prof;
 static std::atomic<long long> g_launches{0};
+static thread_local long long t_launches = 0;  // this thread's share of g_launches
+static std::atomic<long long> g_graph_runs{0}, g_graph_records{0};  // since the library loaded
 
 struct ProfScope {
   bool on = false;
@@ -104,7 +107,8 @@ struct ProfScope {
   cudaStream_t st = nullptr;
   ProfScope(const char *name, double bytes, double ops, int launches, cudaStream_t s, bool capturing = false) {
     g_launches += launches;
-    on = g_prof.on && !capturing;
+    t_launches += launches;
+    on = g_prof.on && !capturing && (g_prof.only.empty() || g_prof.only == name);
     if (!on) return;
     st = s;
     r = ProfRec{name, g_prof.get(), g_prof.get(), bytes, ops, launches};
@@ -180,12 +184,21 @@ struct Workspace {
   int32_t *ids, *offs, *row_seq, *pos;
   char *blocks;  // PlanDev lists
   PlanDev pd;
+  uint64_t gen = 0;  // bumped whenever the device buffers move
+  // A host call's kernels recorded as a CUDA graph (run_graphed): the call's
+  // key (offsets, mode, outputs), the model version and buffer generation it
+  // was recorded with, and its kernel count; `seen` is the previous call's key.
+  std::vector<int64_t> graph_key, seen;
+  uint64_t graph_ver = 0, graph_gen = 0;
+  long long graph_launches = 0;
+  cudaGraphExec_t graph = nullptr;
   float *x, *xn, *sa, *qkv, *ctx, *g, *sq, *ks, *kzc, *kmean, *vs, *vinv, *pooled;
   float *sg;  // row scales of the quantized GeGLU output (kEpiGegluQ; its bytes go over g)
   uint8_t *xq, *qa;
   int8_t *kq, *vq;
   double *logits, *tlogits;
   ~Workspace() {
+    if (graph) cudaGraphExecDestroy(graph);
     if (dev) cudaFree(dev);
     if (host) cudaFreeHost(host);
     if (ohost) cudaFreeHost(ohost);
@@ -248,6 +261,9 @@ struct ig_model {
   // owned; the group itself holds no device memory.
   std::vector<ig_model *> replicas;
   std::atomic<int> inflight{0};  // host calls running on this model (shard placement)
+  // Bumped by every change a recorded graph depends on (embedding table,
+  // heads, SetInt8, RoPE tables): graphs of an older version are re-recorded.
+  std::atomic<uint64_t> version{0};
   ~ig_model() {
     if (!replicas.empty()) {
       for (ig_model *r : replicas) delete r;
@@ -387,6 +403,7 @@ int ensure_rope(ig_model *m, int npos) {
     m->rope_sin[t] = ds;
   }
   m->rope_npos = n;
+  m->version++;
   return 0;
 }
 
@@ -564,6 +581,7 @@ int acquire_ws_sized(ig_model *m, size_t rows, size_t seqs, size_t blks, size_t 
     carve_ws(*w, m, nullptr, r2, s2, b2, t2, p2, f32, &total);
     IG_CU(cudaMalloc(&w->dev, total));
     carve_ws(*w, m, reinterpret_cast<char *>(w->dev), r2, s2, b2, t2, p2, f32, &total);
+    w->gen++;
     w->f32_cap = f32;
     w->rows_cap = r2;
     w->seq_cap = s2;
@@ -1185,6 +1203,9 @@ int run_tail_staged(ig_model *m, Workspace &w, const Plan &p, int mode, cudaStre
   }
   char *stage = static_cast<char *>(w.ohost);
   const int per = (int)align_up((size_t)(N + kTailChunks - 1) / kTailChunks, 32);
+  // Each chunk's kernels follow the event the previous chunk's copy waits
+  // for: plain stream order here, so that event completes with its chunk.
+  DepLaunchOff plain_order;
   struct Piece {
     void *dst;
     size_t at, bytes;
@@ -1248,6 +1269,84 @@ int run_tail_staged(ig_model *m, Workspace &w, const Plan &p, int mode, cudaStre
 int encode_group(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
                  size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len);
 
+// ---- repeated small host calls as CUDA graphs ------------------------------------
+// A host call of at most kGraphMaxRows tokens takes about as long to launch
+// its ~50 kernels as the GPU takes to run them (a 32 x 128 batch: about
+// 0.37 ms of launches). Its kernels (layers, final norm, pooling, heads) are
+// therefore recorded as a CUDA graph the second time a workspace sees the
+// same offsets, mode and outputs in a row, and replayed by one graph launch
+// after that. The same offsets give the same plan, grids and arguments; the
+// data the kernels read (ids, offsets, block lists) is uploaded into the
+// same workspace buffers before every call. A graph is re-recorded when the
+// model changes (model version) or the workspace's buffers move (generation).
+// IG_GRAPH=0 turns this off.
+constexpr int64_t kGraphMaxRows = 1 << 14;
+
+bool graphs_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_GRAPH");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
+int run_graphed(ig_model *m, Workspace &w, const Plan &p, const int64_t *offs, int enc_mode, bool want_logits,
+                bool want_tlog, cudaStream_t st) {
+  auto body = [&](bool capturing) -> int {
+    IG_TRY(run_encoder(m, w, w.ids, p, enc_mode, st, nullptr, capturing, true));
+    if (want_logits || want_tlog)
+      IG_TRY(run_heads(m, w, p, st, want_logits ? w.logits : nullptr, want_tlog ? w.tlogits : nullptr, capturing));
+    return 0;
+  };
+  std::vector<int64_t> key(offs, offs + p.nseq + 1);
+  key.push_back(enc_mode);
+  key.push_back((want_logits ? 1 : 0) | (want_tlog ? 2 : 0));
+  const uint64_t ver = m->version.load();
+  if (w.graph && w.graph_ver == ver && w.graph_gen == w.gen && w.graph_key == key) {
+    g_launches += w.graph_launches;
+    t_launches += w.graph_launches;
+    IG_CU(cudaGraphLaunch(w.graph, st));
+    g_graph_runs++;
+    return 0;
+  }
+  if (w.seen != key) {  // first sight of this key: run as usual
+    w.seen = std::move(key);
+    return body(false);
+  }
+  if (w.graph) {
+    cudaGraphExecDestroy(w.graph);
+    w.graph = nullptr;
+  }
+  const long long l0 = t_launches;
+  IG_CU(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  const int rc = body(true);
+  cudaGraph_t g = nullptr;
+  cudaError_t ce = cudaStreamEndCapture(st, &g);
+  const long long launches = t_launches - l0;
+  g_launches -= launches;  // counted when the graph runs
+  t_launches -= launches;
+  cudaGraphExec_t ex = nullptr;
+  if (!rc && ce == cudaSuccess && g) ce = cudaGraphInstantiate(&ex, g, 0);
+  if (g) cudaGraphDestroy(g);
+  if (rc || ce != cudaSuccess || !ex) {
+    // Not recordable: run it as usual (an error the capture hid shows here).
+    cudaGetLastError();
+    w.seen.clear();
+    return body(false);
+  }
+  w.graph = ex;
+  w.graph_key = std::move(key);
+  w.graph_ver = ver;
+  w.graph_gen = w.gen;
+  w.graph_launches = launches;
+  g_launches += launches;
+  t_launches += launches;
+  IG_CU(cudaGraphLaunch(ex, st));
+  g_graph_records++;
+  g_graph_runs++;
+  return 0;
+}
+
 int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
                 size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len) {
   t_last_error.clear();
@@ -1293,18 +1392,24 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   // Per-token logits for the host: the tail runs in chunks whose copies
   // overlap the kernels after them.
   const bool chunked_tail = tlog && tl && !out && !dump && p.N >= kTailMinRows && out_bytes >= kStageMinBytes;
-  if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump, false, !chunked_tail);
-  if (!rc && chunked_tail) {
-    rc = run_tail_staged(m, *w, p, enc_mode, st, logits, tlog, pl, tl);
-    if (w->copy_stream) cudaStreamSynchronize(w->copy_stream);  // also after an early error
-    cudaError_t se = cudaStreamSynchronize(st);
-    release_ws(m, w, st, false);
-    if (rc) return rc;
-    if (se != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(se));
-    return 0;
+  const bool graphed = !chunked_tail && !dump && !m->f32 && !g_prof.on && p.N > 0 && p.N <= kGraphMaxRows &&
+                       graphs_enabled();
+  if (!rc && graphed) {
+    rc = run_graphed(m, *w, p, offs, enc_mode, logits != nullptr, tlog != nullptr, st);
+  } else {
+    if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump, false, !chunked_tail);
+    if (!rc && chunked_tail) {
+      rc = run_tail_staged(m, *w, p, enc_mode, st, logits, tlog, pl, tl);
+      if (w->copy_stream) cudaStreamSynchronize(w->copy_stream);  // also after an early error
+      cudaError_t se = cudaStreamSynchronize(st);
+      release_ws(m, w, st, false);
+      if (rc) return rc;
+      if (se != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(se));
+      return 0;
+    }
+    if (!rc && (logits || tlog))
+      rc = run_heads(m, *w, p, st, logits ? w->logits : nullptr, tlog ? w->tlogits : nullptr, false);
   }
-  if (!rc && (logits || tlog))
-    rc = run_heads(m, *w, p, st, logits ? w->logits : nullptr, tlog ? w->tlogits : nullptr, false);
   std::vector<OutCopy> outs;
   if (logits && nseq && pl) outs.push_back({w->logits, logits, sizeof(double) * nseq * pl});
   if (tlog && p.N && tl) outs.push_back({w->tlogits, tlog, sizeof(double) * p.N * tl});
@@ -1524,6 +1629,7 @@ int ig_model_set_embeddings(ig_model *m, const ig_embedding_table *t) {
   for (void *p : m->emb_allocs) cudaFree(p);
   m->emb_allocs = std::move(allocs);
   m->emb = e;
+  m->version++;
   return 0;
 }
 
@@ -1552,6 +1658,7 @@ int ig_model_set_heads(ig_model *m, int32_t nheads, const ig_head *heads) {
     cudaFree(h.b);
   }
   m->heads = hs;
+  m->version++;
   return 0;
 }
 
@@ -1584,6 +1691,7 @@ int ig_model_set_int8(ig_model *m, int32_t on) {
     if (int rc = ig_model_set_int8(r, on)) return rc;
   std::lock_guard<std::mutex> lk(m->mu);
   m->f32 = on == 0;
+  m->version++;
   return 0;
 }
 
@@ -1687,6 +1795,13 @@ int ig_profile(int32_t enable) {
   return 0;
 }
 
+int ig_profile_only(const char *name) {
+  t_last_error.clear();
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  g_prof.only = name ? name : "";
+  return 0;
+}
+
 int64_t ig_profile_report(char *buf, size_t len) {
   cudaDeviceSynchronize();
   struct Agg {
@@ -1715,7 +1830,9 @@ int64_t ig_profile_report(char *buf, size_t len) {
       a->ops += r.ops;
     }
   }
-  std::string js = "{\"launches\": " + std::to_string((long long)g_launches) + ", \"kernels\": [";
+  std::string js = "{\"launches\": " + std::to_string((long long)g_launches) +
+                   ", \"graphs_recorded\": " + std::to_string((long long)g_graph_records) +
+                   ", \"graph_runs\": " + std::to_string((long long)g_graph_runs) + ", \"kernels\": [";
   char tmp[512];
   for (size_t i = 0; i < aggs.size(); i++) {
     snprintf(tmp, sizeof(tmp), "%s{\"name\": \"%s\", \"launches\": %lld, \"records\": %lld, \"ms\": %.6f, "

@@ -5,9 +5,11 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include <atomic>
 #include <mutex>
+#include <utility>
 
 namespace ig {
 
@@ -366,5 +368,65 @@ struct PerDevice {
     return x;
   }
 };
+
+// ---- programmatic dependent launch ----------------------------------------------
+// A kernel launched by launch_dep() may be scheduled while the kernel before it
+// in the stream is still running: its CTAs take their SM slots during that
+// kernel's last wave and run up to dep_wait(), which returns once that kernel
+// has completed and its writes are visible. So the launch latency and the
+// ramp of one kernel hide behind the tail of the previous one. Every kernel
+// launched this way calls dep_wait() before it reads anything an earlier
+// kernel of the stream wrote or writes anything one reads, and calls
+// dep_trigger() (after which the next kernel may be scheduled) only after its
+// dep_wait() and after it holds its tensor memory: a CTA of the next kernel
+// that allocates before its own dep_wait() can then only wait for columns this
+// kernel frees, never take ones a CTA of this kernel still has to allocate.
+// Without the launch attribute both are no-ops.
+__device__ __forceinline__ void dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// IG_PDL=0 launches every kernel with plain stream order (default: on).
+// DepLaunchOff turns it off for the launches of the current thread while it
+// lives (stretches that record events between kernels for another stream).
+inline thread_local int t_dep_off = 0;
+inline bool dep_launch_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_PDL");
+    return !(s && s[0] == '0');
+  }();
+  return on && t_dep_off == 0;
+}
+struct DepLaunchOff {
+  explicit DepLaunchOff(bool off = true) : on(off) { t_dep_off += on; }
+  ~DepLaunchOff() { t_dep_off -= on; }
+  DepLaunchOff(const DepLaunchOff &) = delete;
+  DepLaunchOff &operator=(const DepLaunchOff &) = delete;
+  int on;
+};
+
+// The launch attribute that lets the kernel start before its predecessor in
+// the stream completes (appended to a launch's attribute list).
+inline void add_dep_attr(cudaLaunchAttribute *attrs, unsigned &n) {
+  if (!dep_launch_enabled()) return;
+  attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[n].val.programmaticStreamSerializationAllowed = 1;
+  n++;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[1];
+  unsigned n = 0;
+  add_dep_attr(attrs, n);
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace ig

@@ -146,6 +146,8 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
   cluster_sync_all();  // barriers and TMEM of both CTAs exist before any remote use
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Everything above touches no global memory an earlier kernel writes.
+  dep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -254,6 +256,9 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // The next kernel is scheduled once every CTA is here: a persistent grid
+  // that let it in at its start would have it wait on the SMs all along.
+  dep_trigger();
   cluster_sync_all();  // no remote arrival or MMA write is still on its way
   if (warp == 1) {
     tc_fence_after();
@@ -300,7 +305,7 @@ static cudaError_t launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, con
   const int ntiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + S::kBN - 1) / S::kBN);
   const int npairs = ntiles < maxc ? ntiles : maxc;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -311,6 +316,7 @@ static cudaError_t launch_pair(const CUtensorMap &ma, const CUtensorMap &mb, con
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  add_dep_attr(attr, cfg.numAttrs);
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ma, mb, mc, M, N, K, ep);
   if (e == cudaSuccess) *launched = true;
   return e;

@@ -477,6 +477,8 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
   // The cluster's barriers are initialised before any CTA arrives on them.
   if constexpr (S::kQ) cluster_sync_all();
   const uint32_t tmem = *tmem_slot;
+  // Everything above touches no global memory an earlier kernel writes.
+  dep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -591,6 +593,9 @@ __global__ void __launch_bounds__(PEpi<EPI>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // The next kernel is scheduled once every CTA is here: a persistent grid
+  // that let it in at its start would have it wait on the SMs all along.
+  dep_trigger();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 2 * BN);
@@ -643,7 +648,7 @@ static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, 
     cfg.blockDim = dim3(PEpi<EPI>::kThreads);
     cfg.dynamicSmemBytes = S::kTotal;
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = tiles_n;
     at[0].val.clusterDim.y = 1;
@@ -664,11 +669,11 @@ static cudaError_t launch_persist(const CUtensorMap &ma, const CUtensorMap &mb, 
     int clusters = resident < mblocks ? resident : mblocks;
     if (clusters < 1) clusters = 1;
     cfg.gridDim = dim3(clusters * tiles_n);
+    add_dep_attr(at, cfg.numAttrs);
     return cudaLaunchKernelEx(&cfg, gemm_persist_kernel<BN, EPI>, ma, mb, mc, M, N, K, ep);
   }
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
-  gemm_persist_kernel<BN, EPI><<<grid, PEpi<EPI>::kThreads, S::kTotal, st>>>(ma, mb, mc, M, N, K, ep);
-  return cudaGetLastError();
+  return launch_dep(gemm_persist_kernel<BN, EPI>, grid, PEpi<EPI>::kThreads, S::kTotal, st, ma, mb, mc, M, N, K, ep);
 }
 
 // kEpiGegluQ needs whole 128-column GeGLU tiles (so each CTA's columns are

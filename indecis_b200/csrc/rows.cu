@@ -140,6 +140,8 @@ __global__ void quant_rows_kernel(const float *__restrict__ x, int ldx, int M, i
 __global__ void pool_kernel(const float *__restrict__ xn, const int32_t *__restrict__ offs, int H, int cls,
                             float *__restrict__ out) {
   const int s = blockIdx.x;
+  dep_wait();
+  dep_trigger();
   const int t0 = offs[s], t1 = offs[s + 1];
   const int n = t1 - t0;
   for (int d = threadIdx.x; d < H; d += blockDim.x) {
@@ -171,6 +173,7 @@ __global__ void __launch_bounds__(64) pool_long_kernel(const __grid_constant__ C
   uint64_t *full = reinterpret_cast<uint64_t *>(pl_smem + kPlStages * kPlRows * 128);
   uint64_t *empty = full + kPlStages;
   const int s = blockIdx.x, c0 = blockIdx.y * 32, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  dep_wait();
   const int t0 = offs[s], n = offs[s + 1] - t0;
   const int nchunks = (n + kPlRows - 1) / kPlRows;
   if (threadIdx.x == 32) {
@@ -191,7 +194,7 @@ __global__ void __launch_bounds__(64) pool_long_kernel(const __grid_constant__ C
         tma_load_2d(&mx, stages + k * kPlRows * 32, &full[k], c0, t0 + c * kPlRows);
       }
     }
-    return;
+    return;  // exits count as the trigger
   }
   double acc = 0.0;
   for (int c = 0; c < nchunks; c++) {
@@ -209,11 +212,14 @@ __global__ void __launch_bounds__(64) pool_long_kernel(const __grid_constant__ C
     if (lane == 0) mbar_arrive(&empty[k]);
   }
   out[(size_t)s * H + c0 + lane] = n > 0 ? __double2float_rn(__ddiv_rn(acc, (double)n)) : 0.0f;
+  dep_trigger();  // one wave of long-lived CTAs: the next kernel is let in at the end
 }
 
 __global__ void head_logits_kernel(const float *__restrict__ w, const float *__restrict__ b, int rows, int H,
                                    const float *__restrict__ x, int nx, double *__restrict__ z, int ldz) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  dep_wait();
+  dep_trigger();
   if (idx >= nx * rows) return;
   const int t = idx / rows, r = idx % rows;
   const float *wr = w + (size_t)r * H;
@@ -230,6 +236,8 @@ __global__ void head_logits_rows_kernel(const float *__restrict__ w, const float
                                         const float *__restrict__ x, int nx, double *__restrict__ z, int ldz) {
   constexpr int kMaxRows = 16;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  dep_wait();
+  dep_trigger();
   if (t >= nx) return;
   const float *xt = x + (size_t)t * H;
   double s[kMaxRows];
@@ -359,6 +367,8 @@ int launch_quant_rows(const float *x, int ldx, int M, int K, uint8_t *q, int ldq
 
 __global__ void fill_rows_kernel(const int32_t *__restrict__ offs, int32_t *__restrict__ row_seq,
                                  int32_t *__restrict__ pos) {
+  dep_wait();
+  dep_trigger();
   const int s = blockIdx.x, t0 = offs[s], n = offs[s + 1] - t0;
   for (int t = threadIdx.x; t < n; t += blockDim.x) {
     row_seq[t0 + t] = s;
@@ -368,7 +378,7 @@ __global__ void fill_rows_kernel(const int32_t *__restrict__ offs, int32_t *__re
 
 int launch_fill_rows(const int32_t *offs, int nseq, int32_t *row_seq, int32_t *pos, cudaStream_t st) {
   if (nseq <= 0) return 0;
-  fill_rows_kernel<<<nseq, 128, 0, st>>>(offs, row_seq, pos);
+  launch_dep(fill_rows_kernel, nseq, 128, 0, st, offs, row_seq, pos);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 
@@ -391,10 +401,10 @@ int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, 
     const int smem = kPlStages * kPlRows * 128 + 16 * kPlStages;
     static SmemOptIn attr;
     if (attr.ensure((const void *)pool_long_kernel, smem) != cudaSuccess) return IG_ERR_CUDA;
-    pool_long_kernel<<<dim3(nseq, H / 32), 64, smem, st>>>(map, offs, H, out);
+    launch_dep(pool_long_kernel, dim3(nseq, H / 32), 64, smem, st, map, offs, H, out);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
-  pool_kernel<<<nseq, 256, 0, st>>>(xn, offs, H, cls, out);
+  launch_dep(pool_kernel, nseq, 256, 0, st, xn, offs, H, cls, out);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 
@@ -406,11 +416,11 @@ int launch_head_logits(const float *w, const float *b, int rows, int H, const fl
     if (rc != -1) return rc;
   }
   if (rows <= 16 && nx >= 1024) {
-    head_logits_rows_kernel<<<(nx + 127) / 128, 128, 0, st>>>(w, b, rows, H, x, nx, z, ldz);
+    launch_dep(head_logits_rows_kernel, (nx + 127) / 128, 128, 0, st, w, b, rows, H, x, nx, z, ldz);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
   const int total = nx * rows;
-  head_logits_kernel<<<(total + 127) / 128, 128, 0, st>>>(w, b, rows, H, x, nx, z, ldz);
+  launch_dep(head_logits_kernel, (total + 127) / 128, 128, 0, st, w, b, rows, H, x, nx, z, ldz);
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
 }
 

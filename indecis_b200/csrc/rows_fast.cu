@@ -122,6 +122,8 @@ __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 3, k = lane & 7;
   const int row = (blockIdx.x * 8 + warp) * 4 + r;
   const bool rv = row < M;
+  dep_wait();
+  dep_trigger();
   float v[NB];
   if constexpr (EMBED) {
     int id = rv ? ids[row] : 0;
@@ -168,6 +170,8 @@ __global__ void __launch_bounds__(256) ln8h_kernel(const float *__restrict__ x, 
   const int row = (blockIdx.x * 8 + warp) * 2 + r;
   const bool rv = row < M;
   const int b0 = hf * NH;
+  dep_wait();
+  dep_trigger();
   float v[NH];
   {
     const float *src = x + (size_t)(rv ? row : 0) * H + k + 8 * b0;
@@ -314,6 +318,7 @@ __global__ void __launch_bounds__(256, 2) ln8_staged_kernel(const float *__restr
     fence_barrier_init();
   }
   __syncthreads();
+  dep_wait();
 
   // Warp 0 stages group grp into stage s: lane i copies row i.
   auto stage = [&](int grp, int s) {
@@ -349,6 +354,7 @@ __global__ void __launch_bounds__(256, 2) ln8_staged_kernel(const float *__restr
       if (nxt < ngroups) stage(nxt, s);
     }
   }
+  dep_trigger();  // a persistent grid: the next kernel is let in at its end
 }
 
 // One warp per row; lane takes float4 chunks lane, lane + 32, ... (K % 4 == 0).
@@ -356,6 +362,8 @@ template <int NJ>
 __global__ void __launch_bounds__(256) quant_rows4_kernel(const float *__restrict__ x, int ldx, int M, int K,
                                                           uint8_t *__restrict__ q, int ldq, float *__restrict__ sa) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  dep_wait();
+  dep_trigger();
   if (row >= M) return;
   const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)row * ldx);
   const int nq = K >> 2;
@@ -422,6 +430,8 @@ __global__ void __launch_bounds__(128) head_logits_tok_kernel(const float *__res
                                                               int H, const float *__restrict__ x, int nx,
                                                               double *__restrict__ z, int ldz) {
   extern __shared__ double s_w[];
+  dep_wait();
+  dep_trigger();
   for (int e = threadIdx.x; e < H * R; e += blockDim.x) {
     const int i = e / R, r = e - i * R;
     s_w[e] = (double)__ldg(w + (size_t)r * H + i);
@@ -457,7 +467,7 @@ static int launch_head_logits_tok(const float *w, const float *b, int rows, int 
   switch (rows) {
 #define IG_HT(R)                                                                                      \
   case R:                                                                                            \
-    head_logits_tok_kernel<R><<<blocks, 128, smem, st>>>(w, b, H, x, nx, z, ldz);                    \
+    launch_dep(head_logits_tok_kernel<R>, blocks, 128, smem, st, w, b, H, x, nx, z, ldz);            \
     break;
     IG_HT(1) IG_HT(2) IG_HT(3) IG_HT(4) IG_HT(5) IG_HT(6) IG_HT(7) IG_HT(8)
     IG_HT(9) IG_HT(10) IG_HT(11) IG_HT(12) IG_HT(13) IG_HT(14) IG_HT(15) IG_HT(16)
@@ -497,19 +507,20 @@ static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTa
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int groups = (M + S::kRows - 1) / S::kRows;
     const int grid = groups < 2 * sms ? groups : 2 * sms;
-    ln8_staged_kernel<32><<<grid, 256, S::kTotal, st>>>(x, gamma, beta, M, eps, xout, q, ldq, sa);
+    launch_dep(ln8_staged_kernel<32>, grid, 256, S::kTotal, st, x, gamma, beta, M, eps, xout, q, ldq, sa);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
   // Wide rows (H = 768, C4): the split-chain kernel (three times the warps
   // per SM of ln8_kernel<96>, whose 130 registers leave one block per SM).
   if (!EMBED && H == 768 && !beta && ln_split_enabled()) {
-    ln8h_kernel<96><<<(M + 15) / 16, 256, 0, st>>>(x, gamma, M, eps, xout, q, ldq, sa);
+    launch_dep(ln8h_kernel<96>, (M + 15) / 16, 256, 0, st, x, gamma, M, eps, xout, q, ldq, sa);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
   const int blocks = (M + 31) / 32;
 #define IG_LN8(NB)                                                                                                 \
   case 8 * NB:                                                                                                     \
-    ln8_kernel<NB, EMBED><<<blocks, 256, 0, st>>>(x, ids, vocab, emb, gamma, beta, M, eps, xout, q, ldq, sa);     \
+    launch_dep(ln8_kernel<NB, EMBED>, blocks, 256, 0, st, x, ids, vocab, emb, gamma, beta, M, eps, xout, q, ldq, \
+               sa);                                                                                                \
     break;
   switch (H) {
     IG_LN8(8)
@@ -530,21 +541,21 @@ static int launch_quant_rows4(const float *x, int ldx, int M, int K, uint8_t *q,
   const int nj = (K / 4 + 31) / 32;
   const int blocks = (M + 7) / 8;
   switch (nj) {
-    case 1: quant_rows4_kernel<1><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
-    case 2: quant_rows4_kernel<2><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
-    case 3: quant_rows4_kernel<3><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
-    case 4: quant_rows4_kernel<4><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    case 1: launch_dep(quant_rows4_kernel<1>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa); break;
+    case 2: launch_dep(quant_rows4_kernel<2>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa); break;
+    case 3: launch_dep(quant_rows4_kernel<3>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa); break;
+    case 4: launch_dep(quant_rows4_kernel<4>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa); break;
     case 5:
-    case 6: quant_rows4_kernel<6><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    case 6: launch_dep(quant_rows4_kernel<6>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa); break;
     case 7:
-    case 8: quant_rows4_kernel<8><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa); break;
+    case 8: launch_dep(quant_rows4_kernel<8>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa); break;
     default:
       if (nj <= 12)
-        quant_rows4_kernel<12><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa);
+        launch_dep(quant_rows4_kernel<12>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa);
       else if (nj <= 16)
-        quant_rows4_kernel<16><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa);
+        launch_dep(quant_rows4_kernel<16>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa);
       else
-        quant_rows4_kernel<24><<<blocks, 256, 0, st>>>(x, ldx, M, K, q, ldq, sa);
+        launch_dep(quant_rows4_kernel<24>, blocks, 256, 0, st, x, ldx, M, K, q, ldq, sa);
       break;
   }
   return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
