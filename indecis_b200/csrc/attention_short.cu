@@ -262,7 +262,8 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
   volatile int *s_vfast = reinterpret_cast<volatile int *>(smem + S::kTmem + 4);
 
   const int s = blockIdx.x, h = blockIdx.y;
-  dep_wait();
+  // The offsets are copied from the host ahead of every kernel of the
+  // stream, not written by one: they may be read before dep_wait().
   const int t0 = offs[s];
   const int n = offs[s + 1] - t0;
   if (n <= 0) return;
@@ -292,18 +293,19 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
       mbar_init(bar_m, 1);
       fence_barrier_init();
       // A: 128 rows from the sequence's first (rows past it are never used);
-      // B: the head's 64 Q weight rows.
+      // B: the head's 64 Q weight rows. The weights and the RoPE rows are
+      // fetched while the previous kernel finishes, A after dep_wait().
       mbar_arrive_expect_tx(bar_load, nkb * (16384 + 8192) + (rope ? 32768 : 0));
-      for (int kb = 0; kb < nkb; kb++) {
-        tma_load_2d(&mqkv, smem + S::kA + kb * 16384, bar_load, kb * 128, t0);
-        tma_load_2d(&mw, smem + S::kB + kb * 8192, bar_load, kb * 128, h * 64);
-      }
+      for (int kb = 0; kb < nkb; kb++) tma_load_2d(&mw, smem + S::kB + kb * 8192, bar_load, kb * 128, h * 64);
       if (rope) {
         tma_load_2d(&mcos, smem + S::kRope, bar_load, 0, 0);
         tma_load_2d(&msin, smem + S::kRope + 16384, bar_load, 0, 0);
       }
     }
     if (warp == 1) tmem_alloc(tmem_slot, 128);
+    dep_wait();
+    if (tid == 0)
+      for (int kb = 0; kb < nkb; kb++) tma_load_2d(&mqkv, smem + S::kA + kb * 16384, bar_load, kb * 128, t0);
     const int q4 = warp & 3, hq = warp >> 2, r = q4 * 32 + lane;
     qr = r;
     qh = hq;
@@ -474,6 +476,7 @@ __global__ void __launch_bounds__(kShortThreads, QKV ? kShortProjCtasPerSm : kSh
     tc_fence_before();
     __syncthreads();
   } else {
+    dep_wait();
     // 1. K and V by TMA; Q and the RoPE factors straight into registers.
     if (tid == 0) {
       *s_vfast = 1;

@@ -625,8 +625,14 @@ void release_ws(ig_model *m, Workspace *w, cudaStream_t st, bool capturing) {
 // row -> sequence and position tables on the device from the offsets.
 // memcpy(dst, src, n) split over the host copy pool's threads (CopyPool).
 void host_copy(char *dst, const char *src, size_t n);
+bool host_copy_ids(int32_t *dst, const int32_t *src, size_t n, uint32_t vocab);
+int check_ids(const ig_model *m, const int32_t *ids, int64_t N);
 
-int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream_t st, bool capturing = false) {
+// With host ids, `m` given: the ids are tested against the vocabulary while
+// they are staged (no separate pass over them); an id outside it fails the
+// call with the first such id, before anything is enqueued.
+int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream_t st, bool capturing = false,
+                const ig_model *m = nullptr) {
   char *h = reinterpret_cast<char *>(w.host);
   size_t off = 0;
   auto put = [&](const void *src, size_t bytes) {
@@ -640,7 +646,26 @@ int upload_plan(Workspace &w, const Plan &p, const int32_t *host_ids, cudaStream
   for (int k = 0; k < 2; k++) put(p.tc[k].data(), 16 * p.tc[k].size());
   for (int k = 0; k < 2; k++) put(p.v1[k].data(), 8 * p.v1[k].size());
   put(p.fb.data(), 8 * p.fb.size());
-  if (host_ids) put(host_ids, sizeof(int32_t) * p.N);
+  if (host_ids && m) {
+    bool bad;
+    if (p.N >= (128 << 10)) {
+      bad = host_copy_ids(reinterpret_cast<int32_t *>(h + off), host_ids, p.N, (uint32_t)m->cfg.vocab);
+    } else {
+      bad = false;
+      const uint32_t vocab = (uint32_t)m->cfg.vocab;
+      int32_t *dst = reinterpret_cast<int32_t *>(h + off);
+      uint32_t b = 0;
+      for (int64_t i = 0; i < p.N; i++) {
+        dst[i] = host_ids[i];
+        b |= (uint32_t)((uint32_t)host_ids[i] >= vocab);
+      }
+      bad = b != 0;
+    }
+    if (bad) return check_ids(m, host_ids, p.N);  // the first bad id's error
+    off += sizeof(int32_t) * p.N;
+  } else if (host_ids) {
+    put(host_ids, sizeof(int32_t) * p.N);
+  }
   // The device buffers are carved separately: issue one copy per region
   // from the pinned staging (small, contiguous on the host).
   size_t o = 0;
@@ -1047,24 +1072,46 @@ class CopyPool {
     return *pool;
   }
   // memcpy(dst, src, n), split across the pool's threads and the caller.
-  void copy(char *dst, const char *src, size_t n) {
+  void copy(char *dst, const char *src, size_t n) { run_split(dst, src, n, 0, nullptr); }
+  // The same for n int32 ids, returning whether any is outside [0, vocab).
+  bool copy_checked(int32_t *dst, const int32_t *src, size_t n, uint32_t vocab) {
+    std::atomic<uint32_t> bad{0};
+    run_split(reinterpret_cast<char *>(dst), reinterpret_cast<const char *>(src), 4 * n, vocab, &bad);
+    return bad.load() != 0;
+  }
+  // Copies ids, OR-ing the unsigned test id >= vocab (negative ids included)
+  // without a branch, so that the loop vectorizes.
+  static uint32_t copy_ids(int32_t *dst, const int32_t *src, size_t n, uint32_t vocab) {
+    uint32_t bad = 0;
+    for (size_t i = 0; i < n; i++) {
+      const int32_t v = src[i];
+      dst[i] = v;
+      bad |= (uint32_t)((uint32_t)v >= vocab);
+    }
+    return bad;
+  }
+
+ private:
+  void run_split(char *dst, const char *src, size_t n, uint32_t vocab, std::atomic<uint32_t> *bad) {
     const size_t parts = std::min<size_t>(nthreads_ + 1, std::max<size_t>(1, n / kMinPart));
     const size_t per = align_up((n + parts - 1) / parts, 64);
     Batch b;
     {
       std::lock_guard<std::mutex> lk(mu_);
       for (size_t o = per; o < n; o += per) {
-        jobs_.push_back({dst + o, src + o, std::min(per, n - o), &b});
+        jobs_.push_back({dst + o, src + o, std::min(per, n - o), &b, vocab, bad});
         b.left++;
       }
     }
     cv_.notify_all();
-    std::memcpy(dst, src, std::min(per, n));
+    const size_t n0 = std::min(per, n);
+    if (vocab)
+      bad->fetch_or(copy_ids(reinterpret_cast<int32_t *>(dst), reinterpret_cast<const int32_t *>(src), n0 / 4, vocab));
+    else
+      std::memcpy(dst, src, n0);
     std::unique_lock<std::mutex> lk(b.mu);
     b.cv.wait(lk, [&] { return b.left == 0; });
   }
-
- private:
   static constexpr size_t kMinPart = 256 << 10;
   struct Batch {
     std::mutex mu;
@@ -1076,6 +1123,8 @@ class CopyPool {
     const char *src;
     size_t n;
     Batch *b;
+    uint32_t vocab;         // nonzero: int32 ids, each tested against it while copied
+    std::atomic<uint32_t> *bad;
   };
   CopyPool() {
     const unsigned hc = std::thread::hardware_concurrency();
@@ -1091,7 +1140,11 @@ class CopyPool {
         j = jobs_.front();
         jobs_.pop_front();
       }
-      std::memcpy(j.dst, j.src, j.n);
+      if (j.vocab)
+        j.bad->fetch_or(copy_ids(reinterpret_cast<int32_t *>(j.dst), reinterpret_cast<const int32_t *>(j.src),
+                                 j.n / 4, j.vocab));
+      else
+        std::memcpy(j.dst, j.src, j.n);
       std::lock_guard<std::mutex> lk(j.b->mu);
       if (--j.b->left == 0) j.b->cv.notify_all();
     }
@@ -1103,6 +1156,9 @@ class CopyPool {
 };
 
 void host_copy(char *dst, const char *src, size_t n) { CopyPool::get().copy(dst, src, n); }
+bool host_copy_ids(int32_t *dst, const int32_t *src, size_t n, uint32_t vocab) {
+  return CopyPool::get().copy_checked(dst, src, n, vocab);
+}
 
 struct OutCopy {
   const void *src;  // device
@@ -1365,7 +1421,6 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   int max_len = 0;
   IG_TRY(scan_offsets(offs, nseq, &nrows, &max_len));
   if (nrows > 0 && !ids) return fail(IG_ERR_BAD_ARG, "null ids");
-  IG_TRY(check_ids(m, ids, nrows));
   const size_t H = m->H;
   const size_t need = mode == IG_MODE_POOLED ? (size_t)nseq * H : (size_t)nrows * H;
   if (out && out_len < need) return fail(IG_ERR_BAD_ARG, "output too short");
@@ -1387,7 +1442,7 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
   IG_TRY(acquire_ws(m, p, tl, pl, nullptr, false, &w));
   if (!w->own_stream) IG_CU(cudaStreamCreateWithFlags(&w->own_stream, cudaStreamNonBlocking));
   st = w->own_stream;
-  int rc = upload_plan(*w, p, ids, st);
+  int rc = upload_plan(*w, p, ids, st, false, m);  // also the id check (reference run's first check)
   const int enc_mode = (logits || tlog) ? (mode == kModeMeanRows ? kModeMeanRows : IG_MODE_POOLED) : mode;
   // Per-token logits for the host: the tail runs in chunks whose copies
   // overlap the kernels after them.

@@ -150,8 +150,17 @@ __global__ void pool_kernel(const float *__restrict__ xn, const int32_t *__restr
       if (cls) {
         v = xn[(size_t)t0 * H + d];
       } else {
+        // Token order; eight rows' loads are issued ahead of their additions.
         double acc = 0.0;
-        for (int t = t0; t < t1; t++) acc = __dadd_rn(acc, (double)xn[(size_t)t * H + d]);
+        int t = t0;
+        for (; t + 8 <= t1; t += 8) {
+          float f[8];
+#pragma unroll
+          for (int u = 0; u < 8; u++) f[u] = __ldg(xn + (size_t)(t + u) * H + d);
+#pragma unroll
+          for (int u = 0; u < 8; u++) acc = __dadd_rn(acc, (double)f[u]);
+        }
+        for (; t < t1; t++) acc = __dadd_rn(acc, (double)__ldg(xn + (size_t)t * H + d));
         v = __double2float_rn(__ddiv_rn(acc, (double)n));
       }
     }
@@ -411,7 +420,10 @@ int launch_pool(const float *xn, const int32_t *offs, int nseq, int H, int cls, 
 int launch_head_logits(const float *w, const float *b, int rows, int H, const float *x, int nx, double *z, int ldz,
                        cudaStream_t st) {
   if (nx <= 0 || rows <= 0) return 0;
-  if (nx >= 256) {
+  {
+    // Any token count: the weights staged in shared memory once per block
+    // beat per-thread global loads in the sequential chains even for the 32
+    // pooled vectors of one batch (18 us -> a few us per head).
     const int rc = launch_head_logits_tok(w, b, rows, H, x, nx, z, ldz, st);
     if (rc != -1) return rc;
   }

@@ -463,11 +463,15 @@ static int launch_head_logits_tok(const float *w, const float *b, int rows, int 
   if (rows < 1 || rows > 16 || (H & 3) || (reinterpret_cast<uintptr_t>(x) & 15)) return -1;
   const size_t smem = (size_t)H * rows * sizeof(double);
   if (smem > 48 * 1024) return -1;
-  const int blocks = (nx + 127) / 128;
+  // One token a thread, 128 a block (blocks of 32 for small batches, more
+  // SMs but four times the weight staging, measured slower: 21 against 17 us
+  // a head at 32 sequences).
+  const int tpb = 128;
+  const int blocks = (nx + tpb - 1) / tpb;
   switch (rows) {
 #define IG_HT(R)                                                                                      \
   case R:                                                                                            \
-    launch_dep(head_logits_tok_kernel<R>, blocks, 128, smem, st, w, b, H, x, nx, z, ldz);            \
+    launch_dep(head_logits_tok_kernel<R>, blocks, tpb, smem, st, w, b, H, x, nx, z, ldz);            \
     break;
     IG_HT(1) IG_HT(2) IG_HT(3) IG_HT(4) IG_HT(5) IG_HT(6) IG_HT(7) IG_HT(8)
     IG_HT(9) IG_HT(10) IG_HT(11) IG_HT(12) IG_HT(13) IG_HT(14) IG_HT(15) IG_HT(16)
