@@ -357,6 +357,56 @@ __global__ void __launch_bounds__(256, 2) ln8_staged_kernel(const float *__restr
   dep_trigger();  // a persistent grid: the next kernel is let in at its end
 }
 
+// ln8_kernel with each warp's four rows fetched by bulk copies (one 1 KB copy
+// a row into the warp's shared buffer, completing on the warp's mbarrier)
+// instead of the lanes' stride-8 loads: those move 32 bytes of a row per
+// instruction, four L1 wavefronts for 128 bytes, and kept the L1 at 81% of its
+// throughput; the chain reads from shared memory take one wavefront each (row
+// pitch H + 8 floats: the four rows' lanes hit distinct banks). The
+// arithmetic is ln8_kernel's (ln8_row_finish).
+template <int NB>
+__global__ void __launch_bounds__(256) ln8_bulk_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
+                                                       const float *__restrict__ beta, int M, double eps,
+                                                       float *__restrict__ xout, uint8_t *__restrict__ q, int ldq,
+                                                       float *__restrict__ sa) {
+  constexpr int H = 8 * NB;
+  constexpr int P = H + 8;   // float pitch of the staged rows
+  constexpr int QP = H + 8;  // byte pitch of the quantized rows
+  __shared__ __align__(16) float s_x[8][4][P];
+  __shared__ __align__(16) uint8_t s_q[8][4][QP];
+  __shared__ __align__(8) uint64_t s_bar[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 3, k = lane & 7;
+  const int row0 = (blockIdx.x * 8 + warp) * 4, row = row0 + r;
+  const int nr = min(4, M - row0);  // this warp's rows (<= 0 past the end)
+  const bool rv = row < M;
+  if (lane == 0) {
+    mbar_init(&s_bar[warp], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  dep_wait();
+  dep_trigger();
+  bool ok = true;
+  if (nr > 0) {
+    if (lane == 0) mbar_arrive_expect_tx(&s_bar[warp], (uint32_t)(nr * H * 4));
+    __syncwarp();
+    if (lane < nr) bulk_g2s(&s_x[warp][lane][0], x + (size_t)(row0 + lane) * H, H * 4, &s_bar[warp]);
+    ok = mbar_wait(&s_bar[warp], 0, kDevTimeoutFull);
+  }
+  float v[NB];
+#pragma unroll
+  for (int b = 0; b < NB; b++) v[b] = rv && ok ? s_x[warp][r][k + 8 * b] : 0.0f;
+  ln8_row_finish<NB>(v, GammaLdg{gamma + k}, beta, r, k, row, rv && ok, eps, xout, q, ldq, sa, s_q[warp][r]);
+}
+
+static bool ln_bulk_enabled() {
+  static const bool on = [] {
+    const char *s = getenv("IG_LN_BULK");
+    return !(s && s[0] == '0');
+  }();
+  return on;
+}
+
 // One warp per row; lane takes float4 chunks lane, lane + 32, ... (K % 4 == 0).
 template <int NJ>
 __global__ void __launch_bounds__(256) quant_rows4_kernel(const float *__restrict__ x, int ldx, int M, int K,
@@ -513,6 +563,14 @@ static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTa
     const int grid = groups < 2 * sms ? groups : 2 * sms;
     launch_dep(ln8_staged_kernel<32>, grid, 256, S::kTotal, st, x, gamma, beta, M, eps, xout, q, ldq, sa);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+  }
+  // The quantizing norms at H = 256 (attn_norm, mlp_norm): rows fetched by
+  // bulk copies.
+  if (!EMBED && H == 256 && q && ln_bulk_enabled() && !(reinterpret_cast<uintptr_t>(x) & 15)) {
+    return launch_dep(ln8_bulk_kernel<32>, (M + 31) / 32, 256, 0, st, x, gamma, beta, M, eps, xout, q, ldq, sa) ==
+                   cudaSuccess
+               ? 0
+               : IG_ERR_CUDA;
   }
   // Wide rows (H = 768, C4): the split-chain kernel (three times the warps
   // per SM of ln8_kernel<96>, whose 130 registers leave one block per SM).
