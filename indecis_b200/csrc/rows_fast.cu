@@ -25,6 +25,15 @@
 
 namespace ig {
 
+// 16-byte-granular bulk copy global -> this CTA's shared memory, completing
+// on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // gamma[k + 8b] read through the read-only cache.
 struct GammaLdg {
   const float *p;
@@ -156,24 +165,56 @@ __global__ void __launch_bounds__(256) ln8_kernel(const float *__restrict__ x, c
 // thread holds half as many values as in ln8_kernel: at H = 768 that is 48
 // registers of row data instead of 96, and three times the warps per SM.
 // The float64 combines, gamma, the maximum and the bytes follow
-// ln8_row_finish.
-template <int NB>
-__global__ void __launch_bounds__(256) ln8h_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
-                                                   int M, double eps, float *__restrict__ xout,
-                                                   uint8_t *__restrict__ q, int ldq, float *__restrict__ sa) {
+// ln8_row_finish. BULK: 4 warps a block, each warp's two rows fetched into
+// shared memory by bulk copies, half a row a copy (as ln8_bulk_kernel; the
+// halves sit 8 floats apart and the rows 16 floats off a bank multiple, so the
+// warp's 32 chain reads hit distinct banks), instead of stride-8 lane loads.
+template <int NB, bool BULK>
+__global__ void __launch_bounds__(BULK ? 128 : 256) ln8h_kernel(const float *__restrict__ x,
+                                                                const float *__restrict__ gamma, int M, double eps,
+                                                                float *__restrict__ xout, uint8_t *__restrict__ q,
+                                                                int ldq, float *__restrict__ sa) {
   static_assert(NB % 2 == 0, "even chain length");
   constexpr int H = 8 * NB, NH = NB / 2;
   constexpr int QP = H + 8;
-  __shared__ __align__(16) uint8_t s_q[8][2][QP];
+  constexpr int kWarps = BULK ? 4 : 8;
+  constexpr int HP = H / 2 + 8;  // BULK: float offset of a staged row's second half
+  constexpr int RP = 2 * HP;     // BULK: float pitch of the staged rows (16 mod 32)
+  static_assert(RP % 32 == 16 && (HP * 4) % 16 == 0, "bank layout, 16-byte copies");
+  __shared__ __align__(16) uint8_t s_q[kWarps][2][QP];
+  __shared__ __align__(16) float s_x[BULK ? kWarps : 1][BULK ? 2 * RP : 1];
+  __shared__ __align__(8) uint64_t s_bar[kWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 4, hf = (lane >> 3) & 1, k = lane & 7;
-  const int row = (blockIdx.x * 8 + warp) * 2 + r;
-  const bool rv = row < M;
+  const int row0 = (blockIdx.x * kWarps + warp) * 2, row = row0 + r;
+  bool rv = row < M;
   const int b0 = hf * NH;
+  if constexpr (BULK) {
+    if (lane == 0) {
+      mbar_init(&s_bar[warp], 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+  }
   dep_wait();
   dep_trigger();
   float v[NH];
-  {
+  if constexpr (BULK) {
+    const int nr = min(2, M - row0);
+    bool ok = true;
+    if (nr > 0) {
+      if (lane == 0) mbar_arrive_expect_tx(&s_bar[warp], (uint32_t)(nr * H * 4));
+      __syncwarp();
+      if (lane < 2 * nr)  // lane 2r' + h copies half h of row r'
+        bulk_g2s(&s_x[warp][(lane >> 1) * RP + (lane & 1) * HP], x + (size_t)(row0 + (lane >> 1)) * H + (lane & 1) * (H / 2),
+                 H * 2, &s_bar[warp]);
+      ok = mbar_wait(&s_bar[warp], 0, kDevTimeoutFull);
+    }
+    rv = rv && ok;
+    const float *src = &s_x[warp][r * RP + hf * HP + k];
+#pragma unroll
+    for (int b = 0; b < NH; b++) v[b] = rv ? src[8 * b] : 0.0f;
+  } else {
     const float *src = x + (size_t)(rv ? row : 0) * H + k + 8 * b0;
 #pragma unroll
     for (int b = 0; b < NH; b++) v[b] = rv ? __ldg(src + 8 * b) : 0.0f;
@@ -267,15 +308,6 @@ struct GammaRegs {
   __device__ __forceinline__ float operator()(int b) const { return g[b]; }
 };
 
-// 16-byte-granular bulk copy global -> this CTA's shared memory, completing
-// on `bar` (no multicast).
-__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes, uint64_t *bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(smem_dst)),
-               "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
 // ln8_kernel for row-contiguous f32 rows, persistent: groups of 32 rows are
 // staged in shared memory by bulk copies (one per row, a padded row pitch so
 // that the lanes' stride-8 chain reads hit distinct banks), three groups in
@@ -363,9 +395,13 @@ __global__ void __launch_bounds__(256, 2) ln8_staged_kernel(const float *__restr
 // instruction, four L1 wavefronts for 128 bytes, and kept the L1 at 81% of its
 // throughput; the chain reads from shared memory take one wavefront each (row
 // pitch H + 8 floats: the four rows' lanes hit distinct banks). The
-// arithmetic is ln8_kernel's (ln8_row_finish).
-template <int NB>
-__global__ void __launch_bounds__(256) ln8_bulk_kernel(const float *__restrict__ x, const float *__restrict__ gamma,
+// arithmetic is ln8_kernel's (ln8_row_finish). EMBED: the rows are float32
+// embedding rows gathered by id (an id outside the vocabulary is recorded in
+// g_device_error and reads row 0, as ln8_kernel does).
+template <int NB, bool EMBED>
+__global__ void __launch_bounds__(256) ln8_bulk_kernel(const float *__restrict__ x, const int32_t *__restrict__ ids,
+                                                       int vocab, const float *__restrict__ emb,
+                                                       const float *__restrict__ gamma,
                                                        const float *__restrict__ beta, int M, double eps,
                                                        float *__restrict__ xout, uint8_t *__restrict__ q, int ldq,
                                                        float *__restrict__ sa) {
@@ -390,7 +426,20 @@ __global__ void __launch_bounds__(256) ln8_bulk_kernel(const float *__restrict__
   if (nr > 0) {
     if (lane == 0) mbar_arrive_expect_tx(&s_bar[warp], (uint32_t)(nr * H * 4));
     __syncwarp();
-    if (lane < nr) bulk_g2s(&s_x[warp][lane][0], x + (size_t)(row0 + lane) * H, H * 4, &s_bar[warp]);
+    if (lane < nr) {
+      const float *src;
+      if constexpr (EMBED) {
+        int id = ids[row0 + lane];
+        if (id < 0 || id >= vocab) {
+          set_device_error(kDevBadId);
+          id = 0;
+        }
+        src = emb + (size_t)id * H;
+      } else {
+        src = x + (size_t)(row0 + lane) * H;
+      }
+      bulk_g2s(&s_x[warp][lane][0], src, H * 4, &s_bar[warp]);
+    }
     ok = mbar_wait(&s_bar[warp], 0, kDevTimeoutFull);
   }
   float v[NB];
@@ -564,18 +613,23 @@ static int launch_ln8(const float *x, const int32_t *ids, int vocab, const EmbTa
     launch_dep(ln8_staged_kernel<32>, grid, 256, S::kTotal, st, x, gamma, beta, M, eps, xout, q, ldq, sa);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
-  // The quantizing norms at H = 256 (attn_norm, mlp_norm): rows fetched by
-  // bulk copies.
-  if (!EMBED && H == 256 && q && ln_bulk_enabled() && !(reinterpret_cast<uintptr_t>(x) & 15)) {
-    return launch_dep(ln8_bulk_kernel<32>, (M + 31) / 32, 256, 0, st, x, gamma, beta, M, eps, xout, q, ldq, sa) ==
-                   cudaSuccess
+  // The quantizing norms at H = 256 (attn_norm, mlp_norm, and the embedding
+  // norm over a float32 table): rows fetched by bulk copies.
+  if (H == 256 && q && ln_bulk_enabled() &&
+      (EMBED ? emb.fmt == IG_EMB_F32 && !(reinterpret_cast<uintptr_t>(emb.f32) & 15)
+             : !(reinterpret_cast<uintptr_t>(x) & 15))) {
+    return launch_dep(ln8_bulk_kernel<32, EMBED>, (M + 31) / 32, 256, 0, st, x, ids, vocab, emb.f32, gamma, beta, M,
+                      eps, xout, q, ldq, sa) == cudaSuccess
                ? 0
                : IG_ERR_CUDA;
   }
   // Wide rows (H = 768, C4): the split-chain kernel (three times the warps
   // per SM of ln8_kernel<96>, whose 130 registers leave one block per SM).
   if (!EMBED && H == 768 && !beta && ln_split_enabled()) {
-    launch_dep(ln8h_kernel<96>, (M + 15) / 16, 256, 0, st, x, gamma, M, eps, xout, q, ldq, sa);
+    if (ln_bulk_enabled() && !(reinterpret_cast<uintptr_t>(x) & 15))
+      launch_dep(ln8h_kernel<96, true>, (M + 7) / 8, 128, 0, st, x, gamma, M, eps, xout, q, ldq, sa);
+    else
+      launch_dep(ln8h_kernel<96, false>, (M + 15) / 16, 256, 0, st, x, gamma, M, eps, xout, q, ldq, sa);
     return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
   }
   const int blocks = (M + 31) / 32;
