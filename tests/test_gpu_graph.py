@@ -96,3 +96,41 @@ def test_replay_reports_out_of_vocabulary(igdev, oracle_lib):
         gm.EncodeSeqs((bad, offs))
     assert np.array_equal(_bits(gm.EncodeSeqs((x, offs))), _bits(ref))
     gm.close()
+
+
+def test_concurrent_callers_record_and_replay(igdev, oracle_lib):
+    """Eight threads calling on one model with batches of one shape: each
+    call takes its own workspace, so the graphs are recorded concurrently on
+    several streams and replayed; every result bit for bit as the oracle's."""
+    import threading
+
+    import oracle
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Config, Model
+    cfg = S.tiny(layers=2, hidden=256, heads=4, intermediate=384, vocab=3000)
+    W = S.weights(cfg, seed=19)
+    om, gm = oracle.Model(cfg, W), Model.from_arrays(Config.from_dict(cfg), W)
+    _, offs = S.ids_fixed(6, 96, cfg["vocab"], seed=1)
+    rng = np.random.default_rng(9)
+    batches = [rng.integers(4, cfg["vocab"], int(offs[-1])).astype(np.int32) for _ in range(12)]
+    refs = [om.encode(x, offs, threads=4) for x in batches]
+    rec0, run0 = _graph_counts()
+    errors = []
+
+    def work(t):
+        try:
+            for i in range(6):
+                k = (t + i) % len(batches)
+                got = gm.EncodeSeqs((batches[k], offs))
+                if not np.array_equal(_bits(got), _bits(refs[k])):
+                    errors.append((t, i))
+        except Exception as e:  # reported below, in the main thread
+            errors.append((t, repr(e)))
+
+    ths = [threading.Thread(target=work, args=(t,)) for t in range(8)]
+    [t.start() for t in ths]
+    [t.join() for t in ths]
+    assert not errors, errors[:5]
+    rec1, run1 = _graph_counts()
+    assert rec1 > rec0 and run1 - run0 >= rec1 - rec0
+    gm.close()
