@@ -286,7 +286,10 @@ IG_API int ig_pack_b8(const float *w, int32_t n, int32_t k, int8_t *q, int32_t l
 /* attention8 (infer.go:484-518; linalg/attention8.go): qkv [N][3*hidden]
  * rows after RoPE, sequences at host offsets offs[nseq+1]; window < 0 for a
  * global layer, else the half-window; ctx [N][hidden]. Work buffers are
- * allocated for the call (a test entry point; ig_encode uses its workspace). */
+ * allocated for the call (a test entry point; ig_encode uses its workspace).
+ * A (sequence, head) whose Q or K values are NaN, infinite or large enough
+ * for a score to overflow is recomputed with the reference's float->int
+ * conversions and NaN flow, so it too gets the reference's bits. */
 IG_API int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t *offs, int32_t nseq,
                  int32_t window, int32_t simd_lanes, float *ctx, void *stream);
 

@@ -1176,6 +1176,229 @@ static int launch_quant64(const AttnArgs &a, cudaStream_t st) {
              : IG_ERR_CUDA;
 }
 
+// ---- exact recomputation for inputs outside the fast kernels' range ----------
+//
+// The tensor-core attend kernels assume what finite inputs of moderate size
+// guarantee: score corrections 128*sum(kq) below 2^22 (the TMEM preset
+// shortcut), finite scores, and no NaN reaching ExpShift. A NaN or an infinity
+// in a Q or K row, or values so large that a score overflows, breaks those,
+// and the reference then does things the fast kernels do not follow: its
+// float->int conversions (VCVTPS2DQ) turn NaN and out-of-range values into
+// INT_MIN, which enters the key's byte sum and the row's P sum; its clamps
+// (VMAXPS/VMINPS with the value second) let NaN through ExpShift; and the row
+// scale 1/qsum has no guard. ig_attention runs this kernel after the fast
+// ones: one CTA per (sequence, head) scans that head's Q and K values, and
+// only where they are outside the range recomputes the head's prepare
+// (attention8.go:203-294) and attend (attention8.go:298-376) row by row on the
+// CUDA cores with the reference's conversions and orders, overwriting its ctx
+// columns and quantized operands. Clean heads return after the scan.
+constexpr int kExThreads = 128;
+
+// x86 semantics of the steps that differ from CUDA's defaults: comparisons
+// as clamps (NaN passes through), conversions with NaN/out of range ->
+// INT_MIN, integer sums that wrap.
+__device__ __forceinline__ float x86_max(float a, float b) { return a < b ? b : a; }   // std::max(a, b)
+__device__ __forceinline__ float x86_min(float a, float b) { return b < a ? b : a; }   // std::min(a, b)
+__device__ __forceinline__ int32_t wrap_add(int32_t a, int32_t b) { return (int32_t)((uint32_t)a + (uint32_t)b); }
+
+// ExpShift's vector body (vec_simd.go:235-248) with the reference's NaN flow.
+__device__ __forceinline__ float exp_body_x86(float v) {
+  const bool under = v < -87.3f;
+  v = x86_min(x86_max(v, -87.3f), 88.7f);
+  const float n = __fsub_rn(__fmaf_rn(v, 1.44269504088896341f, 12582912.0f), 12582912.0f);
+  float r = __fmaf_rn(n, -0.693359375f, v);
+  r = __fmaf_rn(n, 2.12194440e-4f, r);
+  float p = __fmaf_rn(r, 1.9875691500e-4f, 1.3981999507e-3f);
+  p = __fmaf_rn(r, p, 8.3334519073e-3f);
+  p = __fmaf_rn(r, p, 4.1665795894e-2f);
+  p = __fmaf_rn(r, p, 1.6666665459e-1f);
+  p = __fmaf_rn(r, p, 5.0000001201e-1f);
+  const float y = __fadd_rn(__fmaf_rn(__fmul_rn(p, r), r, r), 1.0f);
+  const float pw = __uint_as_float((uint32_t)wrap_add(rne_int(n), 127) << 23);
+  return under ? 0.0f : __fmul_rn(y, pw);
+}
+
+// exp32 (fastmath.go:35-51) with the reference's NaN flow.
+__device__ __forceinline__ float exp32_x86(float x) {
+  if (x < -87.3f) return 0.0f;
+  x = x86_min(x, 88.7f);
+  const float n = __fsub_rn(__fadd_rn(__fmul_rn(x, 1.44269504088896341f), 12582912.0f), 12582912.0f);
+  float r = __fsub_rn(x, __fmul_rn(n, 0.693359375f));
+  r = __fsub_rn(r, __fmul_rn(n, -2.12194440e-4f));
+  float p = 1.9875691500e-4f;
+  p = __fadd_rn(__fmul_rn(p, r), 1.3981999507e-3f);
+  p = __fadd_rn(__fmul_rn(p, r), 8.3334519073e-3f);
+  p = __fadd_rn(__fmul_rn(p, r), 4.1665795894e-2f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.6666665459e-1f);
+  p = __fadd_rn(__fmul_rn(p, r), 5.0000001201e-1f);
+  const float y = __fadd_rn(__fadd_rn(__fmul_rn(__fmul_rn(p, r), r), r), 1.0f);
+  return __fmul_rn(y, __uint_as_float((uint32_t)wrap_add(rne_int(n), 127) << 23));
+}
+
+// The reference's row quantization (attention8.go:210-251 through
+// quantizeRow): maximum of |x - mean| skipping NaN, scale max/127, bytes
+// rne(c * inv) summed before the int8 clamp. Writes D bytes (q + 128 when
+// flip) unless the maximum is 0; returns the scale (0 for a zero row).
+__device__ float quant_row_x86(const float *x, const float *mean, int8_t *dst, bool flip, int32_t *sum) {
+  float mx = 0.0f;
+  for (int d = 0; d < 64; d++) mx = x86_max(mx, fabsf(mean ? __fsub_rn(x[d], mean[d]) : x[d]));
+  if (mx == 0.0f) {
+    *sum = 0;
+    return 0.0f;
+  }
+  const float scale = __fdiv_rn(mx, 127.0f), inv = __fdiv_rn(1.0f, scale);
+  int32_t s = 0;
+  for (int d = 0; d < 64; d++) {
+    const float c = mean ? __fsub_rn(x[d], mean[d]) : x[d];
+    const int32_t q = rne_int(__fmul_rn(c, inv));
+    s = wrap_add(s, q);
+    const int32_t qc = max(-128, min(127, q));
+    dst[d] = (int8_t)(flip ? (qc ^ 0x80) : qc);
+  }
+  *sum = s;
+  return scale;
+}
+
+__global__ void __launch_bounds__(kExThreads)
+    attn_exact_kernel(const float *__restrict__ qkv, const int32_t *__restrict__ offs, int N, int H, int nh,
+                      int window, int V, float scale, uint8_t *__restrict__ qa, float *__restrict__ sq,
+                      int8_t *__restrict__ kq, float *__restrict__ ks, float *__restrict__ kzc,
+                      int8_t *__restrict__ vq, float *__restrict__ ctx) {
+  __shared__ float s_mean[64], s_vs[64], s_vinv[64], s_qmax[kExThreads / 32], s_kmax[kExThreads / 32];
+  __shared__ int s_bad;
+  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = offs[s], n = offs[s + 1] - t0;
+  if (n <= 0) return;
+  const size_t ld = 3 * (size_t)H;
+  const float *qb = qkv + (size_t)t0 * ld + h * 64, *kb = qb + H, *vb = qb + 2 * H;
+  // 1. The scan: non-finite Q or K values, and the largest magnitudes.
+  bool bad = false;
+  float qm = 0.0f, km = 0.0f;
+  for (int e = tid; e < n * 64; e += kExThreads) {
+    const size_t o = (size_t)(e >> 6) * ld + (e & 63);
+    const float q = qb[o], k = kb[o];
+    bad |= !isfinite(q) || !isfinite(k);
+    qm = fmaxf(qm, fabsf(q));
+    km = fmaxf(km, fabsf(k));
+  }
+  for (int o = 16; o; o >>= 1) {
+    qm = fmaxf(qm, __shfl_xor_sync(0xffffffffu, qm, o));
+    km = fmaxf(km, __shfl_xor_sync(0xffffffffu, km, o));
+  }
+  bad = __any_sync(0xffffffffu, bad);
+  if (tid == 0) s_bad = 0;
+  __syncthreads();
+  if (lane == 0) {
+    s_qmax[warp] = qm;
+    s_kmax[warp] = km;
+    if (bad) s_bad = 1;
+  }
+  __syncthreads();
+  if (tid == 0 && !s_bad) {
+    float q = 0.0f, k = 0.0f;
+    for (int w = 0; w < kExThreads / 32; w++) {
+      q = fmaxf(q, s_qmax[w]);
+      k = fmaxf(k, s_kmax[w]);
+    }
+    // |score| <= 64*128*127 * (2k/127) * (q/127) * scale; the K sum <= n*k.
+    if ((double)q * (double)k * (double)scale * 130.0 >= 1e30 || (double)k * n >= 1e38) s_bad = 1;
+  }
+  __syncthreads();
+  if (!s_bad) return;
+
+  // 2. Prepare (attention8.go:203-294): K column means (AddTo in row order,
+  // then Scale by 1/n), V column scales.
+  if (tid < 64) {
+    float acc = 0.0f;
+    for (int r = 0; r < n; r++) acc = __fadd_rn(acc, kb[(size_t)r * ld + tid]);
+    s_mean[tid] = __fmul_rn(acc, __fdiv_rn(1.0f, (float)n));
+  } else {
+    const int d = tid - 64;
+    float m = 0.0f;
+    for (int r = 0; r < n; r++) m = x86_max(m, fabsf(vb[(size_t)r * ld + d]));
+    float sc = m, inv = 0.0f;
+    if (m > 0.0f) {
+      sc = __fdiv_rn(m, 127.0f);
+      inv = __fdiv_rn(1.0f, sc);
+    }
+    s_vs[d] = sc;
+    s_vinv[d] = inv;
+  }
+  __syncthreads();
+  for (int r = tid; r < n; r += kExThreads) {
+    const size_t plane = (size_t)h * N + t0 + r, o = (size_t)r * ld;
+    int32_t sum = 0;
+    int8_t *qd = reinterpret_cast<int8_t *>(qa + plane * 64);
+    const float qs = quant_row_x86(qb + o, nullptr, qd, true, &sum);
+    if (qs != 0.0f) {
+      sq[plane] = __fmul_rn(qs, scale);
+    } else {
+      sq[plane] = 0.0f;
+      for (int d = 0; d < 64; d++) qa[plane * 64 + d] = 128;
+    }
+    int8_t *kd = kq + plane * 64;
+    const float kss = quant_row_x86(kb + o, s_mean, kd, false, &sum);
+    if (kss != 0.0f) {
+      ks[plane] = kss;
+      kzc[plane] = __fmul_rn(128.0f, (float)sum);
+    } else {
+      ks[plane] = 0.0f;
+      kzc[plane] = 0.0f;
+      for (int d = 0; d < 64; d++) kd[d] = 0;
+    }
+    for (int d = 0; d < 64; d++)
+      vq[plane * 64 + d] = (int8_t)max(-128, min(127, rne_int(__fmul_rn(vb[o + d], s_vinv[d]))));
+  }
+  __syncthreads();
+
+  // 3. Attend (attention8.go:335-374), a row a thread: scores, their maximum,
+  // ExpShift (V-lane body, exp32 tail), P = rne(e * 255) with its int32 sum,
+  // O = P . V dequantized with 1 / qsum.
+  const size_t pl0 = (size_t)h * N + t0;
+  for (int i = tid; i < n; i += kExThreads) {
+    int js = 0, je = n;
+    if (window >= 0) {
+      js = max(0, i - window);
+      je = min(n, i + window + 1);
+    }
+    const int len = je - js, body = (len / V) * V;
+    const uint32_t *qrow = reinterpret_cast<const uint32_t *>(qa + (pl0 + i) * 64);
+    const float sqi = sq[pl0 + i];
+    auto score = [&](int j) {
+      const uint32_t *krow = reinterpret_cast<const uint32_t *>(kq + (pl0 + j) * 64);
+      int32_t acc = 0;
+      for (int w = 0; w < 16; w++) acc = dp4a_us(qrow[w], krow[w], acc);  // u8 x s8
+      return dequant1(acc, kzc[pl0 + j], ks[pl0 + j], sqi);
+    };
+    float mx = -INFINITY;
+    for (int j = js; j < je; j++) mx = x86_max(mx, score(j));
+    int32_t oacc[64];
+    for (int d = 0; d < 64; d++) oacc[d] = 0;
+    int32_t qsum = 0;
+    for (int j = js; j < je; j++) {
+      const float v = __fsub_rn(score(j), mx);
+      const float e = j - js < body ? exp_body_x86(v) : exp32_x86(v);
+      const int32_t pq = rne_int(__fsub_rn(__fadd_rn(__fmul_rn(e, 255.0f), 12582912.0f), 12582912.0f));
+      qsum = wrap_add(qsum, pq);
+      const int32_t pb = (int32_t)(uint8_t)pq;
+      const int8_t *vr = vq + (pl0 + j) * 64;
+      for (int d = 0; d < 64; d++) oacc[d] += pb * (int32_t)vr[d];
+    }
+    const float sp = __fdiv_rn(1.0f, (float)qsum);
+    float *out = ctx + (size_t)(t0 + i) * H + h * 64;
+    for (int d = 0; d < 64; d++) out[d] = dequant1(oacc[d], 0.0f, s_vs[d], sp);
+  }
+}
+
+int launch_attn_exact(const AttnArgs &a, cudaStream_t st) {
+  if (a.nseq <= 0 || a.N <= 0) return 0;
+  if (a.D != 64 || a.rope_cos || a.V < 1) return IG_ERR_UNSUPPORTED;
+  attn_exact_kernel<<<dim3(a.nseq, a.nh), kExThreads, 0, st>>>(a.qkv, a.offs, a.N, a.H, a.nh, a.window, a.V,
+                                                               a.scale, a.qa, a.sq, a.kq, a.ks, a.kzc, a.vq,
+                                                               a.ctx);
+  return cudaGetLastError() == cudaSuccess ? 0 : IG_ERR_CUDA;
+}
+
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
   if (a.rope_cos && a.D != 64) return IG_ERR_UNSUPPORTED;
   if (a.rope_cos && a.nseq > 0 && a.N > 0 && a.max_len <= kShortSeq && (a.H % 4) == 0) {

@@ -2046,6 +2046,9 @@ int ig_attention(const float *qkv, int32_t hidden, int32_t heads, const int64_t 
       if (!rc) rc = launch_attend_tc(a, d_tc, p.tc_short[0], (int)p.tc[0].size() - p.tc_short[0], st);
       if (!rc) rc = launch_attend(a, d_v1, (int)p.v1[0].size(), st);
     }
+    // Heads whose Q or K values are non-finite or overflow-sized: recomputed
+    // with the reference's conversions (the fast kernels' results replaced).
+    if (!rc && a.D == 64) rc = launch_attn_exact(a, st);
     if (rc) fail(rc, "ig_attention launch failed");
   }
   cudaStreamSynchronize(st);

@@ -158,6 +158,7 @@ struct AttnArgs {
 // Whether launch_attn_short can quantize ctx itself (AttnArgs::xq).
 bool attn_short_quantizes(const AttnArgs &a);
 int launch_attention(const AttnArgs &a, cudaStream_t st);
+int launch_attn_exact(const AttnArgs &a, cudaStream_t st);
 int launch_attend(const AttnArgs &a, const int2 *d_blocks, int nblocks, cudaStream_t st);
 int attn_query_block();
 // Tensor-core attention (attention_tc.cu): 128-query blocks whose keys span

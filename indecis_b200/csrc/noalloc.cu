@@ -172,6 +172,9 @@ extern "C" int ig_attention_noalloc(const float *qkv, int32_t hidden, int32_t he
   a.ctx = ctx;
   int rc = launch_attention(a, st);
   if (!rc) rc = launch_attend(a, reinterpret_cast<const int2 *>(b + o_blocks), (int)nblocks, st);
+  // As ig_attention: heads with non-finite or overflow-sized Q/K recomputed
+  // with the reference's conversions (in the same scratch, nothing allocated).
+  if (!rc && a.D == 64) rc = launch_attn_exact(a, st);
   if (rc) return fail(rc, "ig_attention_noalloc: launch failed");
   return 0;
 }

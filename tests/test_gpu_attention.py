@@ -84,6 +84,7 @@ def _special(qkv, offs, H, cases):
                                 qkv.__setitem__((b + 4, slice(H, 2 * H)), qkv[b + 4, H:2 * H] * 1e-40)),
         "k_nan": lambda: qkv.__setitem__((a + 7, H + 70), np.nan),
         "k_inf": lambda: qkv.__setitem__((a + 9, H + 130), np.inf),
+        "q_inf": lambda: qkv.__setitem__((a + 5, 200), -np.inf),
     }
     for c in cases:
         plant[c]()
@@ -112,18 +113,19 @@ def test_attention_special_values(igdev, oracle_lib, lens):
     _compare_special(oracle_lib, lens, ["q_nan", "v_inf", "v_nan", "zero_rows", "tiny_scales"])
 
 
-@pytest.mark.xfail(strict=True, reason="non-finite K values: the reference's NaN-keeping ExpShift clamp, INT_MIN "
-                                       "terms in the P sum and 128*sum corrections beyond 2^22 are not reproduced")
-@pytest.mark.parametrize("case", ["k_nan", "k_inf"])
-def test_attention_nonfinite_keys(igdev, oracle_lib, case):
-    """A NaN or an infinity in a K row makes the K column mean non-finite, so
-    every key of that (sequence, head) takes the clamped conversion with
-    INT_MIN in its sum (a 128*sum correction far beyond 2^22, which the
-    kernels' exact integer-to-float shortcut assumes) and the scores can be
-    NaN (which the reference's ExpShift keeps through its clamp and its P
-    quantization adds to the row sum as INT_MIN). The kernels differ from the
-    reference for that (sequence, head); every other output agrees."""
-    _compare_special(oracle_lib, [96, 128, 17], [case])
+@pytest.mark.parametrize("lens", [[96, 128, 17], [300, 129, 5]])
+@pytest.mark.parametrize("case", ["k_nan", "k_inf", "q_inf"])
+def test_attention_nonfinite_keys(igdev, oracle_lib, case, lens):
+    """A NaN or an infinity in a K row makes that head's K column mean
+    non-finite: every key of the (sequence, head) then converts with INT_MIN
+    in its byte sum (a 128*sum correction far beyond what the tensor-core
+    kernels' integer-to-float shortcut covers), and an infinite key makes the
+    scores NaN, which the reference carries through ExpShift's clamps into P
+    (as INT_MIN in the row's P sum, the row scale 1/qsum unguarded).
+    ig_attention recomputes such heads with the reference's conversions: every
+    output bit as the oracle's (NaN where it has NaN), short and long
+    sequences, a NaN and an infinity in a Q row too."""
+    _compare_special(oracle_lib, lens, [case])
 
 
 def test_attention_accuracy_vs_float(igdev):

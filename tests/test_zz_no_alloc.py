@@ -56,6 +56,23 @@ def test_noalloc_matches_allocating_entry_point(igdev):
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (lens, window)
 
 
+def test_noalloc_nonfinite_keys_match(igdev):
+    """Heads whose K rows hold a NaN or an infinity are recomputed with the
+    reference's conversions by both entry points (inside the fixed array for
+    the allocation-free one): the same bits, NaN where the other has NaN."""
+    from indecis_b200 import ops
+    H, nh = 256, 4
+    qkv_np, offs = _qkv([300, 129, 5], H, nh, 7)
+    qkv_np[offs[0] + 7, H + 70] = np.nan
+    qkv_np[offs[1] + 9, H + 130] = np.inf
+    qkv = torch.from_numpy(qkv_np).cuda()
+    want = ops.attention(qkv, H, nh, offs, -1).cpu().numpy()
+    got = _noalloc(qkv, H, nh, offs, -1)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    ok = ~np.isnan(want)
+    assert np.array_equal(got.view(np.uint32)[ok], want.view(np.uint32)[ok])
+
+
 def test_noalloc_rejects_oversize(igdev):
     from indecis_b200 import _capi
     H, nh = 256, 4
