@@ -233,9 +233,22 @@ IG_API int ig_profile_only(const char *name);
 /* Message of the calling thread's last failure ("" if none). */
 IG_API const char *ig_last_error(void);
 
-/* First error code a kernel recorded (bounded waits, out-of-vocabulary ids
- * in ig_encode_device); reset != 0 clears it. Synchronizes the device. */
+/* First error code a kernel recorded on the current device since the last
+ * reset (one value per device, shared by every model and call on it): 1, 2, 3
+ * a bounded wait gave up (a TMA stage, a stage release, an accumulator), 4 a
+ * bad shape, 5 an id outside the vocabulary in ig_encode_device; 0 none.
+ * reset != 0 clears it. Synchronizes the device. */
 IG_API int32_t ig_device_error(int32_t reset);
+
+/* Self-check of the bounded waits (no counterpart in the reference, which
+ * runs on the CPU). Every mbarrier wait in the kernels gives
+ * up after a limit (2 s), records its code (1-3) in ig_device_error() and
+ * lets the kernel wind down instead of hanging the GPU. This runs one such
+ * wait on a barrier that nothing completes, with a limit of limit_ns
+ * (0 < limit_ns <= 2 s): *timed_out = 1 when it gave up, *waited_ns
+ * (optional) = the time it waited. It leaves code 1 in ig_device_error();
+ * the device stays usable. Synchronizes the device. */
+IG_API int ig_check_wait_timeout(int64_t limit_ns, int32_t *timed_out, int64_t *waited_ns);
 
 /* Self-check of the GELU vector body's division shortcut (an FMA-refined
  * reciprocal in place of the IEEE division of geluMulAVX2's VDIVPS,

@@ -33,7 +33,7 @@ SYMBOLS = ["ig_model_create", "ig_model_destroy", "ig_model_set_heads", "ig_enco
            "ig_spans_tags_device", "ig_spans_tags", "ig_spans_from_tags", "ig_model_set_int8",
            "ig_check_gelu_division", "ig_model_create_multi", "ig_model_replica", "ig_model_device_count",
            "ig_model_create_stored", "ig_model_create_stored_multi", "ig_device_count", "ig_gemm_geglu_quant",
-           "ig_profile_only"]
+           "ig_profile_only", "ig_check_wait_timeout"]
 
 IG_EMB_F32 = 0
 IG_EMB_BF16 = 1
@@ -160,6 +160,7 @@ def load() -> C.CDLL:
     L.ig_logits_device.argtypes = [vp, vp, vp, i32, vp, vp, vp]
     L.ig_attention_noalloc.argtypes = [vp, i32, i32, vp, i32, i32, i32, vp, vp]
     L.ig_check_gelu_division.argtypes = [vp, vp, vp]
+    L.ig_check_wait_timeout.argtypes = [C.c_int64, vp, vp]
     L.ig_model_set_embeddings.argtypes = [vp, C.POINTER(IgEmbeddingTable)]
     f64 = C.c_double
     L.ig_plan_windows.argtypes = [i32, i32, i32, C.POINTER(IgWindow), i32, i32p]

@@ -120,9 +120,6 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete. Gives up after about
-// two seconds (a wait that long means a lost arrival): records `code` in
-// g_device_error and returns false so the caller can wind down.
 // try_wait that may suspend the thread for up to ns nanoseconds (or until
 // the phase completes) instead of returning at once.
 __device__ __forceinline__ bool mbar_try_wait_for(uint64_t *bar, uint32_t parity, uint32_t ns) {
@@ -137,16 +134,24 @@ __device__ __forceinline__ bool mbar_try_wait_for(uint64_t *bar, uint32_t parity
   return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {
+// Waits for the phase with the given parity to complete. Gives up after
+// limit_ns (a wait that long means a lost arrival): records `code` in
+// g_device_error and returns false so the caller can wind down.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (;;) {
     if (mbar_try_wait_for(bar, parity, 1000000u)) return true;
-    if (globaltimer() - t0 > 2000000000ull) {
+    if (globaltimer() - t0 > limit_ns) {
       set_device_error(code);
       return false;
     }
   }
+}
+
+// The kernels' waits: two seconds.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {
+  return mbar_wait_limit(bar, parity, code, 2000000000ull);
 }
 
 // mbar_wait for a barrier that other CTAs of the cluster arrive on.

@@ -47,7 +47,39 @@ __global__ void gelu_div_check_kernel(uint32_t npos) {
   }
 }
 
+// The bounded wait every kernel's mbarrier waits go through, made to run out:
+// one thread waits on a barrier that no thread and no copy will ever
+// complete, with a limit of limit_ns. The wait gives up, records
+// kDevTimeoutFull in g_device_error and returns false; the kernel then
+// stores the outcome and the time waited and exits, leaving the context
+// usable. out[0] = 1 if the wait returned false, out[1] = ns waited.
+__global__ void wait_timeout_check_kernel(uint64_t limit_ns, long long *out) {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  const uint64_t t0 = globaltimer();
+  const bool ok = mbar_wait_limit(&bar, 0, kDevTimeoutFull, limit_ns);
+  out[0] = ok ? 0 : 1;
+  out[1] = (long long)(globaltimer() - t0);
+}
+
 }  // namespace ig
+
+extern "C" int ig_check_wait_timeout(int64_t limit_ns, int32_t *timed_out, int64_t *waited_ns) {
+  using namespace ig;
+  if (!timed_out || limit_ns <= 0 || limit_ns > 2000000000ll) return IG_ERR_BAD_ARG;
+  long long *d = nullptr;
+  if (cudaMalloc(&d, 2 * sizeof(long long)) != cudaSuccess) return IG_ERR_CUDA;
+  wait_timeout_check_kernel<<<1, 1>>>((uint64_t)limit_ns, d);
+  long long h[2] = {0, 0};
+  const bool good = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+                    cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost) == cudaSuccess;
+  cudaFree(d);
+  if (!good) return IG_ERR_CUDA;
+  *timed_out = (int32_t)h[0];
+  if (waited_ns) *waited_ns = h[1];
+  return 0;
+}
 
 extern "C" int ig_check_gelu_division(int64_t *mismatches, uint32_t *first_bad_bits, int64_t *histogram) {
   using namespace ig;
