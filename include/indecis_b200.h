@@ -237,7 +237,8 @@ IG_API const char *ig_last_error(void);
  * reset (one value per device, shared by every model and call on it): 1, 2, 3
  * a bounded wait gave up (a TMA stage, a stage release, an accumulator), 4 a
  * bad shape, 5 an id outside the vocabulary in ig_encode_device; 0 none.
- * reset != 0 clears it. Synchronizes the device. */
+ * Host calls (ig_encode, ig_logits, ...) return IG_ERR_CUDA while it holds
+ * 1-3. reset != 0 clears it. Synchronizes the device. */
 IG_API int32_t ig_device_error(int32_t reset);
 
 /* Self-check of the bounded waits (no counterpart in the reference, which

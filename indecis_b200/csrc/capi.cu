@@ -185,6 +185,7 @@ struct Workspace {
   char *blocks;  // PlanDev lists
   PlanDev pd;
   uint64_t gen = 0;  // bumped whenever the device buffers move
+  int32_t *err_host = nullptr;  // pinned copy of the device error flag at the end of a host call
   // A host call's kernels recorded as a CUDA graph (run_graphed): the call's
   // key (offsets, mode, outputs), the model version and buffer generation it
   // was recorded with, and its kernel count; `seen` is the previous call's key.
@@ -198,6 +199,7 @@ struct Workspace {
   int8_t *kq, *vq;
   double *logits, *tlogits;
   ~Workspace() {
+    if (err_host) cudaFreeHost(err_host);
     if (graph) cudaGraphExecDestroy(graph);
     if (dev) cudaFree(dev);
     if (host) cudaFreeHost(host);
@@ -1403,6 +1405,29 @@ int run_graphed(ig_model *m, Workspace &w, const Plan &p, const int64_t *offs, i
   return 0;
 }
 
+// A host call's kernels that gave up a bounded wait leave a code in the
+// device error flag; the call copies the flag after its last kernel (one
+// 4-byte copy on its stream) and fails when it holds a wait code, since its
+// results are then not valid. The flag is not cleared (ig_device_error(1)
+// does): it is one per device, and a wait that ran out means something on it
+// is wrong.
+void watch_device_error(Workspace &w, cudaStream_t st) {
+  if (!w.err_host && cudaMallocHost(&w.err_host, sizeof(int32_t)) != cudaSuccess) {
+    w.err_host = nullptr;
+    cudaGetLastError();
+    return;
+  }
+  *w.err_host = 0;
+  cudaMemcpyFromSymbolAsync(w.err_host, g_device_error, sizeof(int32_t), 0, cudaMemcpyDeviceToHost, st);
+}
+
+int device_wait_failed(const Workspace &w) {
+  const int e = w.err_host ? *w.err_host : 0;
+  if (e < kDevTimeoutFull || e > kDevTimeoutAccum) return 0;
+  return fail(IG_ERR_CUDA, "encode: a kernel gave up a bounded wait (device error " + std::to_string(e) +
+                               "); the results of this call are not valid");
+}
+
 int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t nseq, int32_t mode, float *out,
                 size_t out_len, ig_dump *dump, double *logits, size_t logits_len, double *tlog, size_t tlog_len) {
   t_last_error.clear();
@@ -1455,8 +1480,10 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
     if (!rc) rc = run_encoder(m, *w, w->ids, p, enc_mode, st, dump, false, !chunked_tail);
     if (!rc && chunked_tail) {
       rc = run_tail_staged(m, *w, p, enc_mode, st, logits, tlog, pl, tl);
+      if (!rc) watch_device_error(*w, st);
       if (w->copy_stream) cudaStreamSynchronize(w->copy_stream);  // also after an early error
       cudaError_t se = cudaStreamSynchronize(st);
+      if (!rc && se == cudaSuccess) rc = device_wait_failed(*w);
       release_ws(m, w, st, false);
       if (rc) return rc;
       if (se != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(se));
@@ -1472,6 +1499,7 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
     if (mode == IG_MODE_POOLED && p.N == 0) std::memset(out, 0, need * sizeof(float));
     else outs.push_back({mode == IG_MODE_POOLED ? w->pooled : w->xn, out, need * sizeof(float)});
   }
+  if (!rc) watch_device_error(*w, st);
   if (!rc && out_bytes > 0) {
     rc = copy_out_staged(*w, st, outs);
   } else {
@@ -1480,6 +1508,7 @@ int encode_host(ig_model *m, const int32_t *ids, const int64_t *offs, int32_t ns
         rc = fail(IG_ERR_CUDA, "copy of the output");
   }
   cudaError_t se = cudaStreamSynchronize(st);
+  if (!rc && se == cudaSuccess) rc = device_wait_failed(*w);
   release_ws(m, w, st, false);
   if (rc) return rc;
   if (se != cudaSuccess) return fail(IG_ERR_CUDA, std::string("encode: ") + cudaGetErrorString(se));

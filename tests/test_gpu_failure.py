@@ -70,3 +70,29 @@ def test_out_of_vocabulary_id_on_device_is_reported(igdev):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
     assert L.ig_device_error(0) == 0
     gm.close()
+
+
+def test_host_call_fails_while_a_wait_code_is_set(igdev, oracle_lib):
+    """A host call copies the device error flag after its last kernel and
+    fails while the flag holds a wait code (its results would not be valid);
+    once the code is cleared, calls succeed with the oracle's bits."""
+    import oracle
+    from indecis_b200 import _capi
+    from indecis_b200 import synthetic as S
+    from indecis_b200.model import Config, Model
+    cfg = S.tiny(layers=2, hidden=128, heads=2, intermediate=256, vocab=500)
+    W = S.weights(cfg, seed=6)
+    om, gm = oracle.Model(cfg, W), Model.from_arrays(Config.from_dict(cfg), W)
+    ids, offs = S.ids_fixed(4, 30, cfg["vocab"], seed=5)
+    want = om.encode(ids, offs)
+    L = _capi.load()
+    L.ig_device_error(1)
+    assert np.array_equal(gm.EncodeSeqs((ids, offs)).view(np.uint32), want.view(np.uint32))
+    timed_out = C.c_int32(0)
+    _capi.check(L.ig_check_wait_timeout(20_000_000, C.byref(timed_out), None))
+    assert timed_out.value == 1
+    with pytest.raises(Exception, match="bounded wait"):
+        gm.EncodeSeqs((ids, offs))
+    assert L.ig_device_error(1) == 1
+    assert np.array_equal(gm.EncodeSeqs((ids, offs)).view(np.uint32), want.view(np.uint32))
+    gm.close()
