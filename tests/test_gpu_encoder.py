@@ -286,3 +286,29 @@ def test_window_logits_chunked_tail(igdev):
             else:
                 assert np.array_equal(np.asarray(x).view(np.uint64), np.asarray(y).view(np.uint64))
     gm.close()
+
+
+def test_nonfinite_embedding_rows(igdev, oracle_lib):
+    """An embedding table holding a NaN row and a row with an infinity: the
+    reference's row quantization sees no finite maximum in the normalized
+    NaN rows and turns them into zero rows with scale 0, so the attention and
+    MLP inputs stay finite while the residual stream of those tokens carries
+    NaN to the end. Every pooled and per-token output bit as the oracle's,
+    NaN where it has NaN."""
+    from indecis_b200 import synthetic as S
+    cfg = S.tiny(layers=3, hidden=256, heads=4, intermediate=384, vocab=800)
+    W = S.weights(cfg, seed=23, gamma_noise=0.1)
+    W["emb"][7, :] = np.nan
+    W["emb"][9, 40] = np.inf
+    import oracle
+    from indecis_b200.model import Config, Model
+    om, gm = oracle.Model(cfg, W), Model.from_arrays(Config.from_dict(cfg), W)
+    ids, offs = S.ids_varlen(6, 3, 140, cfg["vocab"], seed=31)
+    ids[2], ids[int(offs[3]) + 1], ids[-1] = 7, 9, 7
+    for mode, got in ((0, gm.EncodeSeqs((ids, offs))), (1, gm.EncodeTokens((ids, offs)))):
+        ref = om.encode(ids, offs, mode=mode, threads=8)
+        assert np.isnan(ref).any()
+        assert np.array_equal(np.isnan(got), np.isnan(ref)), mode
+        ok = ~np.isnan(ref)
+        assert np.array_equal(_bits(got)[ok], _bits(ref)[ok]), mode
+    gm.close()
